@@ -1,0 +1,16 @@
+"""AxiomLM-B200: the quantized decode hot path of AxiomLM on sm_100a.
+
+``ops``    -- the reference's ``_METAL_MOD`` op table on CUDA (libaxb.so)
+``cache``  -- ``StaticKVCache`` in HBM
+``model``  -- ``QuantizedDecoder`` (the CUDA-graph decode runner)
+``tree``   -- Medusa tree compilation and greedy accept (host logic)
+"""
+
+__version__ = "0.1.0"
+
+
+def load_library():
+    """Load libaxb.so (raises ImportError if it has not been built)."""
+    from . import _lib
+
+    return _lib.load()

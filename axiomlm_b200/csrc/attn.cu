@@ -1,0 +1,693 @@
+// KV-cache write (RoPE + FP8/INT4 quantization) and GQA attention for sm_100a.
+//
+// Replaces rope_kv_cache_write_quantized (axiomlm/kernels/quant.py:896-1008),
+// StaticKVCache.update (engine/paged_cache.py:218-361), gqa_flash_decode_mps
+// (kernels/ops.py:552-654), gqa_tree_verify_mps (ops.py:657-797) and
+// compact_tree_path (paged_cache.py:376-462); Metal counterparts
+// rope_kv_cache_write_{half,fp8,int4}_kernel, gqa_flash_decode_split_kv_*,
+// gqa_tree_verify_split_kv_*, compact_tree_kv_* (metal_kernels.metal).
+#include <algorithm>
+
+#include "axb_common.cuh"
+
+namespace axb {
+
+// ---------------------------------------------------------------- quantize
+// The reference's rule (quant.py:709-719, :788-797) for one group, evaluated
+// on fp32 inputs (the model path: K after RoPE and V are fp32 tensors there) or
+// on fp16 inputs (the op path).  Returns the fp16 scale and writes the ratio
+// x / scale, rounded to fp16 first on the fp16 path.
+__device__ __forceinline__ float kv_scale(float amax, float qmax, bool fp32_in) {
+  float r = __fdiv_rn(amax, qmax);
+  if (fp32_in) r = fmaxf(r, 1e-8f);  // the fp16 clamp at 1e-8 is a no-op
+  return __half2float(__float2half_rn(r));
+}
+__device__ __forceinline__ float kv_ratio(float x, float scale, bool fp32_in) {
+  float r = __fdiv_rn(x, scale);
+  if (!fp32_in) r = __half2float(__float2half_rn(r));
+  return r;
+}
+__device__ __forceinline__ uint8_t fp8_code(float x, float scale, bool fp32_in) {
+  // scale 0 (amax below fp16 range): the reference divides by zero and stores
+  // NaN codes; write zero codes instead so the cache stays finite.
+  if (scale == 0.f) return 0;
+  return float_to_e4m3(kv_ratio(x, scale, fp32_in));
+}
+__device__ __forceinline__ int int4_code(float x, float scale, bool fp32_in) {
+  if (scale == 0.f) return x > 0.f ? 7 : (x < 0.f ? -8 : 0);  // +-inf clamp, NaN -> 0 (as the reference)
+  float r = rintf(kv_ratio(x, scale, fp32_in));
+  return (int)fminf(fmaxf(r, -8.f), 7.f);
+}
+
+// lanes in the same scale group: group of G elements over EPL elements/lane
+__device__ __forceinline__ float group_max(float v, int lanes_per_group) {
+  for (int o = 1; o < lanes_per_group; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// one warp quantizes one hd-vector held EPL = hd/32 elements per lane
+template <int EPL>
+__device__ __forceinline__ void store_kv_row(const float (&v)[EPL], int lane, int kv_type, int G, bool fp32_in,
+                                             uint8_t* row, __half* srow) {
+  if (kv_type == AXB_KV_F16) {
+    __half* r = reinterpret_cast<__half*>(row);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) r[lane * EPL + e] = __float2half_rn(v[e]);
+    return;
+  }
+  float am = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) am = fmaxf(am, fabsf(v[e]));
+  const int lpg = G / EPL;  // lanes per scale group
+  am = group_max(am, lpg);
+  const float qmax = kv_type == AXB_KV_FP8 ? 448.f : 7.f;
+  const float sc = kv_scale(am, qmax, fp32_in);
+  if ((lane % lpg) == 0) srow[(lane * EPL) / G] = __float2half_rn(sc);
+  if (kv_type == AXB_KV_FP8) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) row[lane * EPL + e] = fp8_code(v[e], sc, fp32_in);
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; e += 2) {
+      int lo = int4_code(v[e], sc, fp32_in), hi = int4_code(v[e + 1], sc, fp32_in);
+      row[(lane * EPL + e) >> 1] = (uint8_t)((lo & 0xF) | ((hi & 0xF) << 4));
+    }
+  }
+}
+
+__device__ __forceinline__ int kv_row_bytes(int kv_type, int hd) {
+  return kv_type == AXB_KV_F16 ? hd * 2 : (kv_type == AXB_KV_FP8 ? hd : hd / 2);
+}
+
+// ---------------------------------------------------------------- rope + write
+template <int EPL>
+__global__ void rope_kv_write_kernel(const axb_kv_write_desc d) {
+  pdl_wait();  // qkv comes from the preceding GEMV
+  const int lane = threadIdx.x & 31;
+  const int heads = d.n_head + 2 * d.n_kv_head;
+  const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const long long rows = (long long)d.B * d.T;
+  if (item >= rows * heads) return;
+  const int row = (int)(item / heads), h = (int)(item % heads);
+  const int b = row / d.T, t = row % d.T;
+  const int hd = d.head_dim;
+  const __half* src = reinterpret_cast<const __half*>(d.qkv) + (size_t)row * heads * hd + (size_t)h * hd;
+  float v[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    float x = __half2float(src[lane * EPL + e]);
+    if (d.bias) x = __half2float(__float2half_rn(__fadd_rn(x, __half2float(reinterpret_cast<const __half*>(d.bias)[h * hd + lane * EPL + e]))));
+    v[e] = x;
+  }
+  const bool is_v = h >= d.n_head + d.n_kv_head;
+  if (!is_v) {
+    // RoPE on interleaved pairs: complex multiply as torch does on the CPU,
+    // (a + bi)(c + di) = (ac - bd) + (ad + bc)i, every product rounded.
+    const int off = d.depths ? d.depths[t] : t;
+    const int rp = d.dev_params ? d.dev_params[0] : d.rope_pos;
+    const int pos = (int)(((long long)rp + off) % d.rope_len);
+    const float* f = d.rope + (size_t)pos * hd;  // (hd/2, 2)
+#pragma unroll
+    for (int e = 0; e < EPL; e += 2) {
+      const int i = (lane * EPL + e) >> 1;
+      const float c = f[2 * i], s = f[2 * i + 1];
+      const float a = v[e], bb = v[e + 1];
+      v[e] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(bb, s));
+      v[e + 1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(bb, c));
+    }
+  }
+  if (h < d.n_head) {
+    float* q = d.q_out + (size_t)row * d.n_head * hd + (size_t)h * hd;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) q[lane * EPL + e] = v[e];
+    return;
+  }
+  const int kvh = is_v ? h - d.n_head - d.n_kv_head : h - d.n_head;
+  const int wp = d.dev_params ? d.dev_params[1] : d.write_pos;
+  const int slot = (int)(((long long)wp + t) % d.max_seq);
+  const size_t ridx = ((size_t)b * d.n_kv_head + kvh) * d.max_seq + slot;
+  const int rb = kv_row_bytes(d.kv_type, hd);
+  uint8_t* base = reinterpret_cast<uint8_t*>(is_v ? d.v_cache : d.k_cache) + ridx * rb;
+  __half* sbase = nullptr;
+  if (d.kv_type != AXB_KV_F16)
+    sbase = reinterpret_cast<__half*>(is_v ? d.v_scale : d.k_scale) + ridx * (hd / d.kv_group);
+  // K/V values are fp32 on the model path; on the fp16 op path round first
+  if (!d.k_is_fp32) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) v[e] = __half2float(__float2half_rn(v[e]));
+  }
+  store_kv_row<EPL>(v, lane, d.kv_type, d.kv_group, d.k_is_fp32 != 0, base, sbase);
+}
+
+// standalone quantize of (rows, hd) fp16/fp32 vectors
+template <int EPL>
+__global__ void kv_quantize_kernel(const void* x, int fp32_in, int rows, int hd, int kv_type, int G, uint8_t* q,
+                                   __half* sc) {
+  const int lane = threadIdx.x & 31;
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  float v[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    size_t i = (size_t)r * hd + lane * EPL + e;
+    v[e] = fp32_in ? reinterpret_cast<const float*>(x)[i] : __half2float(reinterpret_cast<const __half*>(x)[i]);
+  }
+  store_kv_row<EPL>(v, lane, kv_type, G, fp32_in != 0, q + (size_t)r * kv_row_bytes(kv_type, hd),
+                    sc + (size_t)r * (hd / G));
+}
+
+// dequant: fp16(decoded fp16 value * fp16 scale) (quant.py:764-767, :846-851)
+__global__ void kv_dequantize_kernel(const uint8_t* q, const __half* sc, long long n, int hd, int kv_type, int G,
+                                     __half* out) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    long long r = i / hd;
+    int e = (int)(i % hd);
+    float s = __half2float(sc[r * (hd / G) + e / G]);
+    float val;
+    if (kv_type == AXB_KV_FP8) {
+      uint8_t c = q[r * hd + e];
+      val = e4m3x2_to_float2((uint16_t)c).x;
+    } else {
+      uint8_t c = q[r * (hd / 2) + e / 2];
+      int nib = (e & 1) ? (c >> 4) : (c & 0xF);
+      val = (float)((nib ^ 8) - 8);
+    }
+    out[i] = __float2half_rn(__fmul_rn(val, s));
+  }
+}
+
+// ---------------------------------------------------------------- attention
+// K/V row loaders: element e of the row as fp32 *without* the group scale.
+struct KvRow {
+  const uint8_t* p;
+  int type;
+};
+
+__device__ __forceinline__ float kv_elem(const uint8_t* row, int type, int e) {
+  if (type == AXB_KV_F16) return __half2float(reinterpret_cast<const __half*>(row)[e]);
+  if (type == AXB_KV_FP8) return e4m3x2_to_float2((uint16_t)row[e]).x;
+  uint8_t c = row[e >> 1];
+  int nib = (e & 1) ? (c >> 4) : (c & 0xF);
+  return (float)((nib ^ 8) - 8);
+}
+
+// Load 16 consecutive elements [e0, e0+16) of a row as fp32 (16-byte aligned
+// chunks: 32 B fp16, 16 B fp8, 8 B int4).
+__device__ __forceinline__ void kv_load16(const uint8_t* row, int type, int e0, float (&o)[16]) {
+  if (type == AXB_KV_F16) {
+    const uint4* p = reinterpret_cast<const uint4*>(row + e0 * 2);
+    uint4 a = p[0], b = p[1];
+    const __half2* ha = reinterpret_cast<const __half2*>(&a);
+    const __half2* hb = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __half22float2(ha[i]);
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+      f = __half22float2(hb[i]);
+      o[8 + 2 * i] = f.x;
+      o[8 + 2 * i + 1] = f.y;
+    }
+  } else if (type == AXB_KV_FP8) {
+    uint4 a = *reinterpret_cast<const uint4*>(row + e0);
+    const uint16_t* u = reinterpret_cast<const uint16_t*>(&a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float2 f = e4m3x2_to_float2(u[i]);
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+  } else {
+    uint2 a = *reinterpret_cast<const uint2*>(row + e0 / 2);
+    const uint8_t* u = reinterpret_cast<const uint8_t*>(&a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o[2 * i] = (float)(((u[i] & 0xF) ^ 8) - 8);
+      o[2 * i + 1] = (float)(((u[i] >> 4) ^ 8) - 8);
+    }
+  }
+}
+
+constexpr int kMaxRep = 8;    // q heads per kv head
+constexpr int kDecTile = 64;  // tokens per online-softmax tile
+
+// Split-K flash decode, T = 1 per sequence.  grid (max_splits, Hkv, B), 128 threads.
+// Each CTA: one (b, kv head), a token range; all n_rep q heads share the K/V reads.
+template <int HD>
+__global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d, int max_splits, float* part_o,
+                                                          float* part_ml, int* counters) {
+  constexpr int EPT = HD / 16;  // lanes-groups: 16 elements per thread-chunk
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int n_rep = d.n_head / d.n_kv_head;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  pdl_wait();
+  const int active = d.dev_params ? d.dev_params[2] : d.active_len;
+  int nsplit = min(max_splits, max(1, (active + 63) / 64));
+  if (split >= nsplit) return;
+  const int chunk = (active + nsplit - 1) / nsplit;
+  const int t0 = split * chunk, t1 = min(active, t0 + chunk);
+  const int hq0 = kvh * n_rep;
+  const float sm_scale = 1.0f / sqrtf((float)HD);
+
+  __shared__ float q_s[kMaxRep][HD];
+  __shared__ float p_s[kMaxRep][kDecTile];
+  __shared__ float m_s[kMaxRep], l_s[kMaxRep], corr_s[kMaxRep];
+  __shared__ float o_red[4][kMaxRep][HD / 32 * 32];
+
+  for (int i = tid; i < n_rep * HD; i += 128) {
+    int r = i / HD, e = i % HD;
+    size_t qi = ((size_t)b * d.n_head + hq0 + r) * HD + e;
+    q_s[r][e] = d.q_is_fp32 ? reinterpret_cast<const float*>(d.q)[qi]
+                            : __half2float(reinterpret_cast<const __half*>(d.q)[qi]);
+  }
+  if (tid < kMaxRep) {
+    m_s[tid] = -INFINITY;
+    l_s[tid] = 0.f;
+  }
+  const int rb = kv_row_bytes(d.kv_type, HD);
+  const int G = d.kv_group, ng = HD / G;
+  const size_t head_base = ((size_t)b * d.n_kv_head + kvh) * d.max_seq;
+  const uint8_t* kc = reinterpret_cast<const uint8_t*>(d.k_cache) + head_base * rb;
+  const uint8_t* vc = reinterpret_cast<const uint8_t*>(d.v_cache) + head_base * rb;
+  const __half* ks = d.k_scale ? reinterpret_cast<const __half*>(d.k_scale) + head_base * ng : nullptr;
+  const __half* vs = d.v_scale ? reinterpret_cast<const __half*>(d.v_scale) + head_base * ng : nullptr;
+
+  // PV accumulators: lane owns dims [lane*HD/32, +HD/32) for every head
+  constexpr int DPL = HD / 32;
+  float acc[kMaxRep][DPL];
+#pragma unroll
+  for (int r = 0; r < kMaxRep; ++r)
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) acc[r][e] = 0.f;
+  __syncthreads();
+
+  for (int tt = t0; tt < t1; tt += kDecTile) {
+    const int nt = min(kDecTile, t1 - tt);
+    // scores: one (token, 16-element chunk) per thread pass; chunks of a token
+    // are reduced with shuffles (EPT threads per token)
+    for (int base = 0; base < kDecTile; base += 128 / EPT) {
+      const int tk = base + tid / EPT, ch = tid % EPT;
+      float part[kMaxRep];
+#pragma unroll
+      for (int r = 0; r < kMaxRep; ++r) part[r] = 0.f;
+      if (tk < nt) {
+        const int slot = tt + tk;
+        float kv[16];
+        kv_load16(kc + (size_t)slot * rb, d.kv_type, ch * 16, kv);
+        float s = ks ? __half2float(ks[(size_t)slot * ng + (ch * 16) / G]) : 1.f;
+#pragma unroll
+        for (int r = 0; r < kMaxRep; ++r) {
+          if (r < n_rep) {
+            float a = 0.f;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) a = __fmaf_rn(q_s[r][ch * 16 + e], kv[e], a);
+            part[r] = a * s;
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kMaxRep; ++r) {
+        float a = part[r];
+        for (int o = 1; o < EPT; o <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (ch == 0 && tk < kDecTile && r < n_rep) p_s[r][tk] = (tk < nt) ? a * sm_scale : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // online softmax update: warp w handles heads w, w+4
+    for (int r = wid; r < n_rep; r += 4) {
+      float v0 = p_s[r][lane], v1 = p_s[r][lane + 32];
+      float mx = warp_max(fmaxf(v0, v1));
+      float m_old = m_s[r];
+      float m_new = fmaxf(m_old, mx);
+      float e0 = (v0 == -INFINITY) ? 0.f : __expf(v0 - m_new);
+      float e1 = (v1 == -INFINITY) ? 0.f : __expf(v1 - m_new);
+      p_s[r][lane] = e0;
+      p_s[r][lane + 32] = e1;
+      float sum = warp_sum(e0 + e1);
+      if (lane == 0) {
+        float c = (m_old == -INFINITY) ? 0.f : __expf(m_old - m_new);
+        corr_s[r] = c;
+        l_s[r] = l_s[r] * c + sum;
+        m_s[r] = m_new;
+      }
+    }
+    __syncthreads();
+    // PV: warp w takes tokens w, w+4, ...; lane covers DPL dims
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) {
+      if (r < n_rep) {
+        float c = corr_s[r];
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[r][e] *= c;
+      }
+    }
+    for (int tk = wid; tk < nt; tk += 4) {
+      const int slot = tt + tk;
+      const uint8_t* vrow = vc + (size_t)slot * rb;
+      float vv[DPL];
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) vv[e] = kv_elem(vrow, d.kv_type, lane * DPL + e);
+      float s = vs ? __half2float(vs[(size_t)slot * ng + (lane * DPL) / G]) : 1.f;
+#pragma unroll
+      for (int r = 0; r < kMaxRep; ++r) {
+        if (r < n_rep) {
+          float p = p_s[r][tk] * s;
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) acc[r][e] = __fmaf_rn(p, vv[e], acc[r][e]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // cross-warp reduction of acc
+#pragma unroll
+  for (int r = 0; r < kMaxRep; ++r)
+    if (r < n_rep)
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) o_red[wid][r][lane * DPL + e] = acc[r][e];
+  __syncthreads();
+  const size_t pidx = ((size_t)b * d.n_head + hq0);
+  for (int i = tid; i < n_rep * HD; i += 128) {
+    int r = i / HD, e = i % HD;
+    float o = o_red[0][r][e] + o_red[1][r][e] + o_red[2][r][e] + o_red[3][r][e];
+    if (nsplit == 1) {
+      reinterpret_cast<__half*>(d.out)[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(o, l_s[r]));
+    } else {
+      part_o[((pidx + r) * max_splits + split) * HD + e] = o;
+    }
+  }
+  if (nsplit == 1) return;
+  if (tid < n_rep) {
+    part_ml[((pidx + tid) * max_splits + split) * 2 + 0] = m_s[tid];
+    part_ml[((pidx + tid) * max_splits + split) * 2 + 1] = l_s[tid];
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ int last;
+  if (tid == 0) last = (atomicAdd(counters + b * d.n_kv_head + kvh, 1) == nsplit - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // deterministic combine over splits in index order
+  for (int i = tid; i < n_rep * HD; i += 128) {
+    int r = i / HD, e = i % HD;
+    const size_t hb = (pidx + r) * max_splits;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(part_ml + (hb + sp) * 2));
+    float L = 0.f, O = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      float m = __ldcg(part_ml + (hb + sp) * 2), l = __ldcg(part_ml + (hb + sp) * 2 + 1);
+      float c = (m == -INFINITY) ? 0.f : __expf(m - M);
+      L += l * c;
+      O += __ldcg(part_o + (hb + sp) * HD + e) * c;
+    }
+    reinterpret_cast<__half*>(d.out)[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, L));
+  }
+  if (tid == 0) counters[b * d.n_kv_head + kvh] = 0;
+}
+
+// Tree / chunked-prefill attention: T query tokens per sequence, each sees the
+// prefix [0, prefix_len) and tree slot write_pos + j iff bit j of masks[t].
+// grid (ceil(T / TQ), Hkv, B); 128 threads; rows = TQ tokens x n_rep heads <= 16.
+constexpr int kTreeRows = 16;
+constexpr int kTreeKeys = 32;
+template <int HD>
+__global__ void __launch_bounds__(128) tree_attn_kernel(axb_attn_desc d) {
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int n_rep = d.n_head / d.n_kv_head;
+  const int TQ = max(1, kTreeRows / n_rep);
+  const int u0 = blockIdx.x * TQ;
+  const int nu = min(TQ, d.T - u0);
+  const int R = nu * n_rep;
+  const int tid = threadIdx.x;
+  const float sm_scale = 1.0f / sqrtf((float)HD);
+  __shared__ float q_s[kTreeRows][HD + 1];
+  __shared__ float k_s[kTreeKeys][HD + 1];
+  __shared__ float v_s[kTreeKeys][HD + 1];
+  __shared__ float p_s[kTreeRows][kTreeKeys + 1];
+  __shared__ float m_s[kTreeRows], l_s[kTreeRows], c_s[kTreeRows];
+  __shared__ unsigned long long mask_s[kTreeRows];
+  pdl_wait();
+  if (d.dev_params) {
+    d.write_pos = d.dev_params[1];
+    d.prefix_len = d.dev_params[3];
+  }
+  for (int i = tid; i < R * HD; i += 128) {
+    int r = i / HD, e = i % HD;
+    int u = u0 + r / n_rep, hq = kvh * n_rep + r % n_rep;
+    size_t qi = (((size_t)b * d.T + u) * d.n_head + hq) * HD + e;
+    q_s[r][e] = d.q_is_fp32 ? reinterpret_cast<const float*>(d.q)[qi]
+                            : __half2float(reinterpret_cast<const __half*>(d.q)[qi]);
+  }
+  if (tid < R) {
+    m_s[tid] = -INFINITY;
+    l_s[tid] = 0.f;
+    mask_s[tid] = d.masks[u0 + tid / n_rep];
+  }
+  const int rb = kv_row_bytes(d.kv_type, HD);
+  const int G = d.kv_group, ng = HD / G;
+  const size_t head_base = ((size_t)b * d.n_kv_head + kvh) * d.max_seq;
+  const uint8_t* kc = reinterpret_cast<const uint8_t*>(d.k_cache) + head_base * rb;
+  const uint8_t* vc = reinterpret_cast<const uint8_t*>(d.v_cache) + head_base * rb;
+  const __half* ks = d.k_scale ? reinterpret_cast<const __half*>(d.k_scale) + head_base * ng : nullptr;
+  const __half* vs = d.v_scale ? reinterpret_cast<const __half*>(d.v_scale) + head_base * ng : nullptr;
+  // thread -> (row, dims) for PV: 8 threads per row, HD/8 dims each
+  constexpr int DPT = HD / 8;
+  float acc[DPT];
+#pragma unroll
+  for (int e = 0; e < DPT; ++e) acc[e] = 0.f;
+  const int my_r = tid >> 3, my_d0 = (tid & 7) * DPT;
+  __syncthreads();
+  const int n_keys = d.prefix_len + d.T;
+  for (int kt = 0; kt < n_keys; kt += kTreeKeys) {
+    const int nk = min(kTreeKeys, n_keys - kt);
+    // stage dequantized K/V (scales applied) for the key tile
+    for (int i = tid; i < nk * HD; i += 128) {
+      int kk = i / HD, e = i % HD;
+      int key = kt + kk;
+      int slot = key < d.prefix_len ? key : (d.write_pos + key - d.prefix_len) % d.max_seq;
+      float sk = ks ? __half2float(ks[(size_t)slot * ng + e / G]) : 1.f;
+      float sv = vs ? __half2float(vs[(size_t)slot * ng + e / G]) : 1.f;
+      k_s[kk][e] = kv_elem(kc + (size_t)slot * rb, d.kv_type, e) * sk;
+      v_s[kk][e] = kv_elem(vc + (size_t)slot * rb, d.kv_type, e) * sv;
+    }
+    __syncthreads();
+    for (int i = tid; i < kTreeRows * kTreeKeys; i += 128) {
+      int r = i / kTreeKeys, kk = i % kTreeKeys;
+      float sc = -INFINITY;
+      if (r < R && kk < nk) {
+        int key = kt + kk;
+        bool vis = key < d.prefix_len || ((mask_s[r] >> (key - d.prefix_len)) & 1ull);
+        if (vis) {
+          float a = 0.f;
+#pragma unroll 8
+          for (int e = 0; e < HD; ++e) a = __fmaf_rn(q_s[r][e], k_s[kk][e], a);
+          sc = a * sm_scale;
+        }
+      }
+      p_s[r][kk] = sc;
+    }
+    __syncthreads();
+    // online softmax: warp w handles rows w, w+4, ...
+    {
+      const int lane = tid & 31, wid = tid >> 5;
+      for (int r = wid; r < R; r += 4) {
+        float v = p_s[r][lane];
+        float mx = warp_max(v);
+        float m_old = m_s[r], m_new = fmaxf(m_old, mx);
+        float e = (v == -INFINITY) ? 0.f : __expf(v - m_new);
+        p_s[r][lane] = e;
+        float sum = warp_sum(e);
+        if (lane == 0) {
+          float c = (m_old == -INFINITY) ? ((m_new == -INFINITY) ? 1.f : 0.f) : __expf(m_old - m_new);
+          c_s[r] = c;
+          l_s[r] = l_s[r] * c + sum;
+          m_s[r] = m_new;
+        }
+      }
+    }
+    __syncthreads();
+    if (my_r < R) {
+      float c = c_s[my_r];
+#pragma unroll
+      for (int e = 0; e < DPT; ++e) acc[e] *= c;
+      for (int kk = 0; kk < nk; ++kk) {
+        float p = p_s[my_r][kk];
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) acc[e] = __fmaf_rn(p, v_s[kk][my_d0 + e], acc[e]);
+      }
+    }
+    __syncthreads();
+  }
+  if (my_r < R) {
+    int u = u0 + my_r / n_rep, hq = kvh * n_rep + my_r % n_rep;
+    __half* o = reinterpret_cast<__half*>(d.out) + (((size_t)b * d.T + u) * d.n_head + hq) * HD + my_d0;
+    float l = l_s[my_r];
+#pragma unroll
+    for (int e = 0; e < DPT; ++e) o[e] = __float2half_rn(__fdiv_rn(acc[e], l));
+  }
+}
+
+// ---------------------------------------------------------------- compaction
+__global__ void compact_kv_kernel(uint8_t* cache, __half* scales, int max_batch, int n_kv_head, int max_seq,
+                                  int row_bytes, int n_groups, int write_pos, const int32_t* acc, int n_acc) {
+  // blockIdx.x = ((layer*2 + kv)*max_batch + b)*Hkv + h
+  extern __shared__ uint8_t stage[];
+  const size_t head = blockIdx.x;
+  uint8_t* rows = cache + head * max_seq * (size_t)row_bytes;
+  __half* srow = scales ? scales + head * max_seq * (size_t)n_groups : nullptr;
+  __half* sstage = reinterpret_cast<__half*>(stage + (size_t)n_acc * row_bytes);
+  for (int i = threadIdx.x; i < n_acc * row_bytes; i += blockDim.x) {
+    int m = i / row_bytes, e = i % row_bytes;
+    int src = (write_pos + acc[m]) % max_seq;
+    stage[i] = rows[(size_t)src * row_bytes + e];
+  }
+  if (srow)
+    for (int i = threadIdx.x; i < n_acc * n_groups; i += blockDim.x) {
+      int m = i / n_groups, e = i % n_groups;
+      sstage[i] = srow[(size_t)((write_pos + acc[m]) % max_seq) * n_groups + e];
+    }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_acc * row_bytes; i += blockDim.x) {
+    int m = i / row_bytes, e = i % row_bytes;
+    rows[(size_t)((write_pos + m) % max_seq) * row_bytes + e] = stage[i];
+  }
+  if (srow)
+    for (int i = threadIdx.x; i < n_acc * n_groups; i += blockDim.x) {
+      int m = i / n_groups, e = i % n_groups;
+      srow[(size_t)((write_pos + m) % max_seq) * n_groups + e] = sstage[i];
+    }
+}
+
+// ---------------------------------------------------------------- host
+static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int decode_max_splits(int B, int n_kv_head) {
+  int ctas = B * n_kv_head;
+  int want = (2 * num_sms() + ctas - 1) / ctas;
+  return std::max(1, std::min(64, want));
+}
+
+size_t attn_workspace(int B, int n_head, int head_dim, int max_splits) {
+  size_t o = (size_t)B * n_head * max_splits * head_dim * 4;
+  size_t ml = (size_t)B * n_head * max_splits * 2 * 4;
+  size_t cnt = (size_t)B * n_head * 4;
+  return round_up(o, 256) + round_up(ml, 256) + round_up(cnt, 256);
+}
+
+int rope_kv_write(const axb_kv_write_desc* d, cudaStream_t s, bool pdl) {
+  AXB_CHECK_ARG(d && d->qkv && d->rope && d->q_out && d->k_cache && d->v_cache, "rope_kv_write: null pointer");
+  AXB_CHECK_ARG(d->head_dim == 64 || d->head_dim == 128, "rope_kv_write: head_dim must be 64 or 128");
+  AXB_CHECK_ARG(d->n_kv_head > 0 && d->n_head % d->n_kv_head == 0, "rope_kv_write: bad head counts");
+  AXB_CHECK_ARG(d->kv_type == AXB_KV_F16 || (d->k_scale && d->v_scale), "rope_kv_write: quantized cache needs scales");
+  AXB_CHECK_ARG(d->kv_type == AXB_KV_F16 || (d->kv_group >= 32 && d->head_dim % d->kv_group == 0 &&
+                                              d->kv_group >= d->head_dim / 32),
+                "rope_kv_write: kv_group must divide head_dim and be >= 32");
+  AXB_CHECK_ARG(d->B >= 1 && d->B <= d->max_batch && d->T >= 1 && d->rope_len > 0, "rope_kv_write: bad B/T");
+  long long items = (long long)d->B * d->T * (d->n_head + 2 * d->n_kv_head);
+  int blocks = (int)((items + 3) / 4);
+  cudaError_t e;
+  if (d->head_dim == 128)
+    e = launch_pdl(rope_kv_write_kernel<4>, dim3(blocks), dim3(128), 0, s, pdl, *d);
+  else
+    e = launch_pdl(rope_kv_write_kernel<2>, dim3(blocks), dim3(128), 0, s, pdl, *d);
+  return cuda_status(e, "rope_kv_write launch");
+}
+
+int attention(const axb_attn_desc* d, cudaStream_t s) {
+  AXB_CHECK_ARG(d && d->q && d->k_cache && d->v_cache && d->out, "attention: null pointer");
+  AXB_CHECK_ARG(d->head_dim == 64 || d->head_dim == 128, "attention: head_dim must be 64 or 128");
+  AXB_CHECK_ARG(d->n_kv_head > 0 && d->n_head % d->n_kv_head == 0 && d->n_head / d->n_kv_head <= kMaxRep,
+                "attention: n_head / n_kv_head must be an integer <= %d", kMaxRep);
+  AXB_CHECK_ARG(d->kv_type == AXB_KV_F16 || (d->k_scale && d->v_scale && d->kv_group > 0 &&
+                                              d->head_dim % d->kv_group == 0 && d->kv_group % 16 == 0),
+                "attention: bad quantized-cache scales / group");
+  if (d->masks == nullptr) {
+    AXB_CHECK_ARG(d->active_len >= 1 && d->active_len <= d->max_seq, "attention: bad active_len %d", d->active_len);
+    int ms = d->num_splits > 0 ? std::min(64, d->num_splits) : decode_max_splits(d->B, d->n_kv_head);
+    AXB_CHECK_ARG(d->workspace && d->workspace_bytes >= attn_workspace(d->B, d->n_head, d->head_dim, ms),
+                  "attention: workspace too small");
+    char* ws = reinterpret_cast<char*>(d->workspace);
+    float* po = reinterpret_cast<float*>(ws);
+    size_t o_b = round_up((size_t)d->B * d->n_head * ms * d->head_dim * 4, 256);
+    float* pml = reinterpret_cast<float*>(ws + o_b);
+    size_t ml_b = round_up((size_t)d->B * d->n_head * ms * 2 * 4, 256);
+    int* cnt = reinterpret_cast<int*>(ws + o_b + ml_b);
+    dim3 grid(ms, d->n_kv_head, d->B);
+    cudaError_t e;
+    if (d->head_dim == 128)
+      e = launch_pdl(decode_attn_kernel<128>, grid, dim3(128), 0, s, d->pdl != 0, *d, ms, po, pml, cnt);
+    else
+      e = launch_pdl(decode_attn_kernel<64>, grid, dim3(128), 0, s, d->pdl != 0, *d, ms, po, pml, cnt);
+    return cuda_status(e, "decode attention launch");
+  }
+  AXB_CHECK_ARG(d->T >= 1 && d->T <= 64, "attention: tree mode needs 1 <= T <= 64");
+  AXB_CHECK_ARG(d->prefix_len >= 0 && d->prefix_len <= d->max_seq, "attention: bad prefix_len");
+  int n_rep = d->n_head / d->n_kv_head;
+  int TQ = std::max(1, kTreeRows / n_rep);
+  dim3 grid((d->T + TQ - 1) / TQ, d->n_kv_head, d->B);
+  cudaError_t e;
+  if (d->head_dim == 128)
+    e = launch_pdl(tree_attn_kernel<128>, grid, dim3(128), 0, s, d->pdl != 0, *d);
+  else
+    e = launch_pdl(tree_attn_kernel<64>, grid, dim3(128), 0, s, d->pdl != 0, *d);
+  return cuda_status(e, "tree attention launch");
+}
+
+}  // namespace axb
+
+using namespace axb;
+
+extern "C" {
+
+int axb_rope_kv_write(const axb_kv_write_desc* d, void* stream) { return rope_kv_write(d, (cudaStream_t)stream, false); }
+
+int axb_kv_quantize(const void* x, int x_is_fp32, int rows, int hd, int kv_type, int G, void* q, uint16_t* sc,
+                    void* stream) {
+  AXB_CHECK_ARG(x && q && sc && rows >= 0, "kv_quantize: null pointer");
+  AXB_CHECK_ARG(kv_type == AXB_KV_FP8 || kv_type == AXB_KV_INT4, "kv_quantize: kv_type must be FP8 or INT4");
+  AXB_CHECK_ARG((hd == 64 || hd == 128) && G >= 32 && hd % G == 0, "kv_quantize: bad head_dim/group");
+  if (rows == 0) return AXB_OK;
+  int blocks = (rows + 3) / 4;
+  if (hd == 128)
+    kv_quantize_kernel<4><<<blocks, 128, 0, (cudaStream_t)stream>>>(x, x_is_fp32, rows, hd, kv_type, G, (uint8_t*)q,
+                                                                    (__half*)sc);
+  else
+    kv_quantize_kernel<2><<<blocks, 128, 0, (cudaStream_t)stream>>>(x, x_is_fp32, rows, hd, kv_type, G, (uint8_t*)q,
+                                                                    (__half*)sc);
+  return launch_status("kv_quantize");
+}
+
+int axb_kv_dequantize(const void* q, const uint16_t* sc, int rows, int hd, int kv_type, int G, uint16_t* out,
+                      void* stream) {
+  AXB_CHECK_ARG(q && sc && out && rows >= 0 && hd > 0 && G > 0 && hd % G == 0, "kv_dequantize: bad args");
+  AXB_CHECK_ARG(kv_type == AXB_KV_FP8 || kv_type == AXB_KV_INT4, "kv_dequantize: kv_type must be FP8 or INT4");
+  long long n = (long long)rows * hd;
+  if (n == 0) return AXB_OK;
+  int blocks = (int)std::min<long long>((n + 255) / 256, 4096);
+  kv_dequantize_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>((const uint8_t*)q, (const __half*)sc, n, hd, kv_type,
+                                                                 G, (__half*)out);
+  return launch_status("kv_dequantize");
+}
+
+size_t axb_attn_workspace_bytes(int B, int n_head, int head_dim, int T, int max_splits) {
+  (void)T;
+  int ms = max_splits > 0 ? std::min(64, max_splits) : 64;
+  return attn_workspace(B, n_head, head_dim, ms);
+}
+
+int axb_attention(const axb_attn_desc* d, void* stream) { return attention(d, (cudaStream_t)stream); }
+
+int axb_compact_kv(void* cache, uint16_t* scales, int n_layer, int max_batch, int n_kv_head, int max_seq,
+                   int row_bytes, int n_groups, int write_pos, const int32_t* accepted, int n_acc, void* stream) {
+  AXB_CHECK_ARG(cache && accepted && n_acc >= 0 && n_acc <= 64 && row_bytes > 0, "compact_kv: bad args");
+  if (n_acc == 0) return AXB_OK;
+  size_t smem = (size_t)n_acc * row_bytes + (size_t)n_acc * n_groups * 2;
+  int heads = n_layer * 2 * max_batch * n_kv_head;
+  compact_kv_kernel<<<heads, 256, smem, (cudaStream_t)stream>>>((uint8_t*)cache, (__half*)scales, max_batch,
+                                                                n_kv_head, max_seq, row_bytes, n_groups, write_pos,
+                                                                accepted, n_acc);
+  return launch_status("compact_kv");
+}
+
+}  // extern "C"

@@ -1,0 +1,856 @@
+// Quantized weight formats and the W4A16 GEMV / small-M GEMM for sm_100a.
+//
+// Replaces qmv_q4_marlin / qmm_q4_marlin (axiomlm/kernels/quant.py:637-684)
+// and the Metal kernels qmv_q4_marlin_apple_kernel / qmm_q4_marlin_*
+// (metal_kernels.metal:2135, :2268, :2404).  The reference dequantizes into
+// fp16 and runs F.linear; here the 4-bit codes stream from HBM straight into
+// mma.sync A-fragments (q4t layout, one 128-bit load per lane per 16x64 block)
+// and the activations are the B operand, so M <= 64 tokens share one weight
+// pass.  Work is split "stream-K" at group granularity over every warp of a
+// persistent grid; tiles split between warps are reduced deterministically by
+// the last warp to arrive (fixed summation order, per-tile arrival counter).
+#include <algorithm>
+
+#include "axb_common.cuh"
+
+namespace axb {
+
+// ------------------------------------------------------------------ layout
+// q4t: tile t (16 rows) x k-block b (64 columns) = 512 B at ((t*KB)+b)*512.
+// Lane l = 4*g + t4 owns, in word j, rows {g, g+8} x columns
+// 64*b + 16*t4 + 4*j + {0..3}; nibble i = low half of fragment register a_i,
+// nibble i+4 = its high half (registers: a0 (g, +0/+1), a1 (g+8, +0/+1),
+// a2 (g, +2/+3), a3 (g+8, +2/+3)).
+// Scales per (tile, group): SYM 8 x half2 (s[g], s[g+8]); AFFINE 8 x
+// (s[g], b[g], s[g+8], b[g+8]).
+
+__host__ __device__ inline int gu_src_row(int p, int N, int gu) {
+  // packed row p -> source row; gate/up interleave by 8 for the SwiGLU epilogue
+  if (!gu) return p;
+  int F = N >> 1;
+  int tile = p >> 4, h = (p >> 3) & 1, i = p & 7;
+  int j = tile * 8 + i;
+  if (j >= F) return N;  // padding
+  return h ? F + j : j;
+}
+
+__device__ __forceinline__ void q4t_word_coords(int lane, int j, int nib, int& row, int& kk) {
+  int g = lane >> 2, t4 = lane & 3;
+  int reg = nib & 3, hi = nib >> 2;
+  row = g + ((reg & 1) ? 8 : 0);
+  kk = 16 * t4 + 4 * j + ((reg & 2) ? 2 : 0) + hi;
+}
+
+// ---- packing from fp32 weights (RTN) ---------------------------------------
+__global__ void q4t_pack_kernel(const float* __restrict__ w, int N, int K, int G, int sym, int gu,
+                                uint32_t* __restrict__ words, __half* __restrict__ scales) {
+  const int KB = K / 64, tile = blockIdx.y, kb = blockIdx.x;
+  const int grp = (kb * 64) / G;
+  __shared__ float s_sc[16], s_bi[16];
+  // stats: 16 rows x 16 threads each
+  {
+    int r = threadIdx.x >> 4, part = threadIdx.x & 15;
+    int src = gu_src_row(tile * 16 + r, N, gu);
+    float mn = INFINITY, mx = -INFINITY, am = 0.f;
+    if (src < N) {
+      const float* row = w + (size_t)src * K + (size_t)grp * G;
+      for (int e = part; e < G; e += 16) {
+        float v = row[e];
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+        am = fmaxf(am, fabsf(v));
+      }
+    } else {
+      mn = mx = am = 0.f;
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    }
+    if (part == 0) {
+      if (sym) {
+        __half s = __float2half_rn(__fdiv_rn(fmaxf(am, 1e-8f), 7.0f));
+        s_sc[r] = __half2float(s);
+        s_bi[r] = 0.f;
+      } else {
+        // quant.py:475-486
+        float denom = fmaxf(__fsub_rn(mx, mn), 1e-8f);
+        s_sc[r] = __half2float(__float2half_rn(__fdiv_rn(denom, 15.0f)));
+        s_bi[r] = __half2float(__float2half_rn(mn));
+      }
+    }
+  }
+  __syncthreads();
+  if (kb * 64 % G == 0 && threadIdx.x < 8) {
+    int g = threadIdx.x;
+    size_t base = ((size_t)tile * (K / G) + grp) * 8 + g;
+    if (sym) {
+      scales[base * 2 + 0] = __float2half_rn(s_sc[g]);
+      scales[base * 2 + 1] = __float2half_rn(s_sc[g + 8]);
+    } else {
+      scales[base * 4 + 0] = __float2half_rn(s_sc[g]);
+      scales[base * 4 + 1] = __float2half_rn(s_bi[g]);
+      scales[base * 4 + 2] = __float2half_rn(s_sc[g + 8]);
+      scales[base * 4 + 3] = __float2half_rn(s_bi[g + 8]);
+    }
+  }
+  if (threadIdx.x < 128) {
+    int lane = threadIdx.x >> 2, j = threadIdx.x & 3;
+    uint32_t word = 0;
+#pragma unroll
+    for (int nib = 0; nib < 8; ++nib) {
+      int row, kk;
+      q4t_word_coords(lane, j, nib, row, kk);
+      int src = gu_src_row(tile * 16 + row, N, gu);
+      int q;
+      float sc = s_sc[row];
+      if (src >= N) {
+        q = sym ? 8 : 0;
+      } else {
+        float v = w[(size_t)src * K + kb * 64 + kk];
+        if (sym) {
+          if (sc == 0.f) {
+            q = 8;
+          } else {
+            float r = rintf(__fdiv_rn(v, sc));
+            q = (int)fminf(fmaxf(r, -8.f), 7.f) + 8;
+          }
+        } else {
+          float r = rintf(__fdiv_rn(__fsub_rn(v, s_bi[row]), fmaxf(sc, 1e-8f)));
+          q = (int)fminf(fmaxf(r, 0.f), 15.f);
+        }
+      }
+      word |= (uint32_t)(q & 0xF) << (4 * nib);
+    }
+    words[((size_t)tile * KB + kb) * 128 + lane * 4 + j] = word;
+  }
+}
+
+// ---- relayout of the reference MARLIN-ladder format -----------------------
+__device__ __forceinline__ int ladder_code(const uint32_t* wm, int KG, int row, int k) {
+  int t8 = row >> 3, c = row & 7, kb = k >> 6, kk = k & 63;
+  int wsel = kk >> 5, s = (kk >> 3) & 3, r = kk & 7;
+  int c0 = c & 6;
+  int lane = (((r >> 2) & 1) << 4) | (((c0 >> 2) & 1) << 3) | (((r >> 1) & 1) << 2) | ((r & 1) << 1) |
+             ((c0 >> 1) & 1);
+  uint32_t word = wm[(((size_t)t8 * KG + kb) * 32 + lane) * 2 + wsel];
+  int shift = ((c & 1) ? 16 : 0) + 4 * s;
+  return (word >> shift) & 0xF;
+}
+
+__global__ void q4t_from_marlin_kernel(const uint32_t* __restrict__ wm, const __half* __restrict__ sb, int n_rows8,
+                                       int K, int n_out, int gu, uint32_t* __restrict__ words,
+                                       __half* __restrict__ scales) {
+  const int KB = K / 64, tile = blockIdx.y, kb = blockIdx.x;
+  int t = threadIdx.x;
+  if (t < 128) {
+    int lane = t >> 2, j = t & 3;
+    uint32_t word = 0;
+#pragma unroll
+    for (int nib = 0; nib < 8; ++nib) {
+      int row, kk;
+      q4t_word_coords(lane, j, nib, row, kk);
+      int src = gu_src_row(tile * 16 + row, n_out, gu);
+      int q = 0;
+      if (src < n_out && src < n_rows8) q = ladder_code(wm, KB, src, kb * 64 + kk);
+      word |= (uint32_t)q << (4 * nib);
+    }
+    words[((size_t)tile * KB + kb) * 128 + lane * 4 + j] = word;
+  } else if (t < 136) {
+    int g = t - 128;
+    size_t base = ((size_t)tile * KB + kb) * 8 + g;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int src = gu_src_row(tile * 16 + g + 8 * h, n_out, gu);
+      __half s = __float2half_rn(0.f), b = __float2half_rn(0.f);
+      if (src < n_out && src < n_rows8) {
+        int t8 = src >> 3, c = src & 7;
+        const __half* p = sb + (((size_t)t8 * KB + kb) * 8 + c) * 2;
+        s = p[0];
+        b = p[1];
+      }
+      scales[base * 4 + 2 * h + 0] = s;
+      scales[base * 4 + 2 * h + 1] = b;
+    }
+  }
+}
+
+// ---- dequant (bit-exact statements of the reference formulas) --------------
+__global__ void q4t_dequant_kernel(const uint32_t* __restrict__ words, const __half* __restrict__ scales, int N,
+                                   int K, int G, int sym, int gu, __half* __restrict__ out) {
+  const int KB = K / 64, tile = blockIdx.y, kb = blockIdx.x;
+  int t = threadIdx.x;  // 128 threads: one word each
+  int lane = t >> 2, j = t & 3;
+  uint32_t word = words[((size_t)tile * KB + kb) * 128 + lane * 4 + j];
+  int grp = kb * 64 / G;
+#pragma unroll
+  for (int nib = 0; nib < 8; ++nib) {
+    int row, kk;
+    q4t_word_coords(lane, j, nib, row, kk);
+    int p = tile * 16 + row;
+    int dst = gu_src_row(p, N, gu);
+    if (dst >= N) continue;
+    int q = (word >> (4 * nib)) & 0xF;
+    int g = row & 7, h = row >> 3;
+    size_t base = ((size_t)tile * (K / G) + grp) * 8 + g;
+    float v;
+    if (sym) {
+      float s = __half2float(scales[base * 2 + h]);
+      v = __fmul_rn((float)(q - 8), s);
+    } else {
+      float s = __half2float(scales[base * 4 + 2 * h]);
+      float b = __half2float(scales[base * 4 + 2 * h + 1]);
+      v = __fadd_rn(__fmul_rn((float)q, s), b);  // quant.py:627-631: two fp32 ops
+    }
+    out[(size_t)dst * K + kb * 64 + kk] = __float2half_rn(v);
+  }
+}
+
+__global__ void marlin_dequant_kernel(const uint32_t* __restrict__ wm, const __half* __restrict__ sb, int K,
+                                      int n_out, __half* __restrict__ out) {
+  int row = blockIdx.y, KG = K / 64;
+  for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < K; k += gridDim.x * blockDim.x) {
+    int q = ladder_code(wm, KG, row, k);
+    int t8 = row >> 3, c = row & 7, kb = k >> 6;
+    const __half* p = sb + (((size_t)t8 * KG + kb) * 8 + c) * 2;
+    float v = __fadd_rn(__fmul_rn((float)q, __half2float(p[0])), __half2float(p[1]));
+    out[(size_t)row * K + k] = __float2half_rn(v);
+  }
+}
+
+// quant.py:72-129: Q8_G64 RTN pack (one warp per (row, group))
+__global__ void q8_pack_kernel(const float* __restrict__ w, int N, int K, uint32_t* __restrict__ out,
+                               __half* __restrict__ sb) {
+  const int lane = threadIdx.x & 31;
+  const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int G = K / 64;
+  if (item >= (long long)N * G) return;
+  const int row = (int)(item / G), grp = (int)(item % G);
+  const float* src = w + (size_t)row * K + grp * 64;
+  float v0 = src[2 * lane], v1 = src[2 * lane + 1];
+  float mn = fminf(v0, v1), mx = fmaxf(v0, v1);
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  const float denom = fmaxf(__fsub_rn(mx, mn), 1e-8f);
+  const __half sc = __float2half_rn(__fdiv_rn(denom, 255.0f));
+  const __half bi = __float2half_rn(mn);
+  const float scf = fmaxf(__half2float(sc), 1e-8f), bif = __half2float(bi);
+  int q0 = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(v0, bif), scf)), 0.f), 255.f);
+  int q1 = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(v1, bif), scf)), 0.f), 255.f);
+  // two bytes per lane: lanes 2i, 2i+1 form word i
+  uint32_t part = (uint32_t)q0 | ((uint32_t)q1 << 8);
+  uint32_t other = __shfl_xor_sync(0xffffffffu, part, 1);
+  if ((lane & 1) == 0) out[(size_t)row * (K / 4) + grp * 16 + lane / 2] = part | (other << 16);
+  if (lane == 0) {
+    sb[((size_t)row * G + grp) * 2] = sc;
+    sb[((size_t)row * G + grp) * 2 + 1] = bi;
+  }
+}
+
+__global__ void q8_rows_kernel(const uint32_t* __restrict__ w, const __half* __restrict__ sb,
+                               const int32_t* __restrict__ idx, int K, __half* __restrict__ out) {
+  int i = blockIdx.x;
+  int r = idx[i];
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    uint32_t word = w[(size_t)r * (K / 4) + k / 4];
+    int q = (word >> (8 * (k & 3))) & 0xFF;
+    const __half* p = sb + ((size_t)r * (K / 64) + k / 64) * 2;
+    float v = __fadd_rn(__fmul_rn((float)q, __half2float(p[0])), __half2float(p[1]));
+    out[(size_t)i * K + k] = __float2half_rn(v);
+  }
+}
+
+__global__ void ternary_dequant_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ s, int K,
+                                       int per_tensor, __half* __restrict__ out) {
+  int row = blockIdx.y;
+  for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < K; k += gridDim.x * blockDim.x) {
+    int b = w[(size_t)row * (K / 4) + k / 4] >> (2 * (k & 3));
+    int q = (b & 1) - ((b >> 1) & 1);
+    float sc = __half2float(per_tensor ? s[0] : s[(size_t)row * (K / 64) + k / 64]);
+    out[(size_t)row * K + k] = __float2half_rn(__fmul_rn((float)q, sc));
+  }
+}
+
+__global__ void q2_dequant_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ sb, int K,
+                                  __half* __restrict__ out) {
+  int row = blockIdx.y;
+  for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < K; k += gridDim.x * blockDim.x) {
+    int q = (w[(size_t)row * (K / 4) + k / 4] >> (2 * (k & 3))) & 3;
+    const __half* p = sb + ((size_t)row * (K / 64) + k / 64) * 2;
+    // quant.py:399-401: q*scale and +bias are separate fp16 tensor ops
+    __half t = __float2half_rn(__fmul_rn((float)q, __half2float(p[0])));
+    out[(size_t)row * K + k] = __float2half_rn(__fadd_rn(__half2float(t), __half2float(p[1])));
+  }
+}
+
+// ------------------------------------------------------------------ GEMV
+struct GemmArgs {
+  const uint4* W;
+  const char* S;
+  int N, K, M, KB, GB, upt;
+  long long U;
+  long long Wt;
+  const __half* x;
+  int ldx;
+  const float* norm_w;
+  float eps;
+  void* y;
+  int ldy;
+  const __half* bias;
+  int epi, gu;
+  float* partials;
+  int* counters;
+  int* err;
+  int xs_stride;  // smem row stride (halves); 0 = read x from global
+  int xs_bytes;   // bytes of the staged-x region at the start of shared memory
+};
+
+constexpr int kWarpsPerCta = 8;
+constexpr int kCH = 4;             // k-blocks (512 B each) per pipeline stage
+constexpr int kStages = 4;         // stages per warp
+constexpr int kStageW = kCH * 512; // weight bytes per stage
+constexpr int kStageS = kCH * 64;  // scale bytes per stage (max: affine, one group per k-block)
+constexpr int kWarpRing = kStages * (kStageW + kStageS) + kStages * 8;
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+__device__ __forceinline__ long long warp_start(long long w, long long U, long long Wt) { return w * U / Wt; }
+__device__ __forceinline__ long long warp_of_unit(long long u, long long U, long long Wt) {
+  return ((u + 1) * Wt - 1) / U;
+}
+
+// nibble pairs of one word -> four A-fragment registers holding (q - Z)
+template <int Z>
+__device__ __forceinline__ void unpack_word(uint32_t w, uint32_t (&a)[4]) {
+  const uint32_t MAGIC = 0x64006400u;
+  uint32_t lo0 = lop3_and_or(w, 0x000F000Fu, MAGIC);
+  uint32_t hi0 = lop3_and_or(w, 0x00F000F0u, MAGIC);
+  uint32_t w8 = w >> 8;
+  uint32_t lo1 = lop3_and_or(w8, 0x000F000Fu, MAGIC);
+  uint32_t hi1 = lop3_and_or(w8, 0x00F000F0u, MAGIC);
+  // lo: 1024 + q ; hi: 1024 + 16 q  (exact fp16 values)
+  const __half2 sub = __halves2half2(__ushort_as_half(0x6400 + Z), __ushort_as_half(0x6400 + Z));  // 1024+Z
+  const __half2 mul = __float2half2_rn(1.0f / 16.0f);
+  const __half2 add = __float2half2_rn(-(64.0f + (float)Z));
+  a[0] = h2_as_u32(__hsub2(u32_as_h2(lo0), sub));
+  a[1] = h2_as_u32(__hfma2(u32_as_h2(hi0), mul, add));
+  a[2] = h2_as_u32(__hsub2(u32_as_h2(lo1), sub));
+  a[3] = h2_as_u32(__hfma2(u32_as_h2(hi1), mul, add));
+}
+
+template <int NT>
+__device__ __forceinline__ void epilogue(const GemmArgs& a, int tile, const float (&acc)[NT][4], int lane) {
+  const int g = lane >> 2, t4 = lane & 3;
+  const int r0 = tile * 16 + g, r1 = r0 + 8;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int n = nt * 8 + 2 * t4 + e;
+      if (n >= a.M) continue;
+      const float v0 = acc[nt][e], v1 = acc[nt][2 + e];
+      if (a.epi == AXB_EPI_SWIGLU) {
+        const int j = tile * 8 + g;
+        if (j < (a.N >> 1)) {
+          // gate and up are fp16-rounded GEMV outputs; silu(g) * u in fp32
+          float gg = __half2float(__float2half_rn(v0));
+          float uu = __half2float(__float2half_rn(v1));
+          float sw = __fmul_rn(silu_f(gg), uu);
+          reinterpret_cast<__half*>(a.y)[(size_t)n * a.ldy + j] = __float2half_rn(sw);
+        }
+        continue;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int p = h ? r1 : r0;
+        const int col = gu_src_row(p, a.N, a.gu);
+        if (col >= a.N) continue;
+        float v = h ? v1 : v0;
+        if (a.bias) v = __fadd_rn(v, __half2float(a.bias[col]));
+        __half vh = __float2half_rn(v);
+        if (a.epi == AXB_EPI_RESIDUAL) {
+          __half* yp = reinterpret_cast<__half*>(a.y) + (size_t)n * a.ldy + col;
+          *yp = __float2half_rn(__fadd_rn(__half2float(*yp), __half2float(vh)));
+        } else if (a.epi == AXB_EPI_F32) {
+          reinterpret_cast<float*>(a.y)[(size_t)n * a.ldy + col] = __half2float(vh);
+        } else {
+          reinterpret_cast<__half*>(a.y)[(size_t)n * a.ldy + col] = vh;
+        }
+      }
+    }
+  }
+}
+
+// Stage x (optionally RMS-normalized, modules.py:41-43 with fp32 weight) into smem.
+__device__ void stage_x(const GemmArgs& a, __half* xs) {
+  const int lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5, wid = threadIdx.x >> 5;
+  for (int m = wid; m < a.M; m += nw) {
+    const __half* xr = a.x + (size_t)m * a.ldx;
+    __half* sr = xs + (size_t)m * a.xs_stride;
+    if (a.norm_w) {
+      float ss = 0.f;
+      for (int k = lane * 8; k < a.K; k += 256) {
+        uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+        const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float2 f = __half22float2(h[q]);
+          ss = __fmaf_rn(f.x, f.x, ss);
+          ss = __fmaf_rn(f.y, f.y, ss);
+        }
+      }
+      ss = warp_sum(ss);
+      const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps)));
+      for (int k = lane * 8; k < a.K; k += 256) {
+        uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+        const __half2* h = reinterpret_cast<const __half2*>(&v);
+        uint4 o;
+        __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float2 f = __half22float2(h[q]);
+          float w0 = a.norm_w[k + 2 * q], w1 = a.norm_w[k + 2 * q + 1];
+          oh[q] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, rms), w0), __fmul_rn(__fmul_rn(f.y, rms), w1));
+        }
+        *reinterpret_cast<uint4*>(sr + k) = o;
+      }
+    } else {
+      for (int k = lane * 8; k < a.K; k += 256)
+        *reinterpret_cast<uint4*>(sr + k) = *reinterpret_cast<const uint4*>(xr + k);
+    }
+  }
+}
+
+template <int NT, bool SYM, int GB, bool XS>
+__global__ void __launch_bounds__(kWarpsPerCta * 32) qgemm_kernel(const GemmArgs a) {
+  extern __shared__ __align__(128) char smem[];
+  __half* xs = reinterpret_cast<__half*>(smem);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + wid;
+  const long long u0 = warp_start(w, a.U, a.Wt), u1 = warp_start(w + 1, a.U, a.Wt);
+  const long long kb0 = u0 * GB, kb1 = u1 * GB;
+  const int nst = (int)((kb1 - kb0 + kCH - 1) / kCH);
+  constexpr int UB = SYM ? 32 : 64;  // scale bytes per group
+
+  // per-warp ring of bulk-copied weight (and scale) stages
+  char* ring = smem + a.xs_bytes + (size_t)wid * kWarpRing;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kStages * (kStageW + kStageS));
+  if (lane == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(bars + s, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  auto issue = [&](int it) {
+    if (lane != 0 || it >= nst) return;
+    const int st = it % kStages;
+    const long long kbs = kb0 + (long long)it * kCH;
+    const int n = (int)((kb1 - kbs) < kCH ? (kb1 - kbs) : kCH);
+    const uint32_t bw = n * 512, bs = (n / GB) * UB;
+    fence_proxy_async();
+    mbar_expect_tx(bars + st, bw + bs);
+    bulk_g2s(ring + st * kStageW, a.W + kbs * 32, bw, bars + st);
+    bulk_g2s(ring + kStages * kStageW + st * kStageS, a.S + (kbs / GB) * UB, bs, bars + st);
+  };
+  // 1. weights do not depend on the producer kernel: start streaming them now
+  for (int it = 0; it < kStages; ++it) issue(it);
+
+  pdl_wait();
+  if (XS) {
+    stage_x(a, xs);
+    __syncthreads();
+  }
+  pdl_trigger();
+
+  float acc[NT][4];
+  float tmp[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[nt][i] = tmp[nt][i] = 0.f;
+
+  bool first_seg = true;
+  for (int it = 0; it < nst; ++it) {
+    const int st = it % kStages;
+    if (!mbar_wait(bars + st, (uint32_t)((it / kStages) & 1), kWaitLimit)) {
+      // record the failure, give the copies still in flight a bounded chance
+      // to land (so none writes into shared memory after exit), and leave
+      if (lane == 0) atomicExch(a.err, AXB_ETIMEOUT);
+      for (int j = it + 1; j < nst && j < it + kStages; ++j)
+        mbar_wait(bars + (j % kStages), (uint32_t)((j / kStages) & 1), kWaitLimit);
+      return;
+    }
+    const uint4* wst = reinterpret_cast<const uint4*>(ring + st * kStageW);
+    const char* sst = ring + kStages * kStageW + st * kStageS;
+    const long long kbs = kb0 + (long long)it * kCH;
+    const int n = (int)((kb1 - kbs) < kCH ? (kb1 - kbs) : kCH);
+    const long long unit0 = kbs / GB;
+    for (int kbo = 0; kbo < n; ++kbo) {
+      const long long kbi = kbs + kbo;
+      const int tile = (int)(kbi / a.KB);
+      const int kb = (int)(kbi - (long long)tile * a.KB);
+      const uint4 cur = wst[kbo * 32 + lane];
+      const int su = (int)(kbi / GB - unit0);
+      // B fragments (activations) for this k-block
+      uint32_t bf[NT][8];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int nn = nt * 8 + g;
+        if (nn < a.M) {
+          const __half* src = XS ? xs + (size_t)nn * a.xs_stride + kb * 64 + 16 * t4
+                                 : a.x + (size_t)nn * a.ldx + kb * 64 + 16 * t4;
+          uint4 v0 = *reinterpret_cast<const uint4*>(src);
+          uint4 v1 = *reinterpret_cast<const uint4*>(src + 8);
+          bf[nt][0] = v0.x; bf[nt][1] = v0.y; bf[nt][2] = v0.z; bf[nt][3] = v0.w;
+          bf[nt][4] = v1.x; bf[nt][5] = v1.y; bf[nt][6] = v1.z; bf[nt][7] = v1.w;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) bf[nt][q] = 0u;
+        }
+      }
+      const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
+      if (SYM) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t af[4];
+          unpack_word<8>(words[j], af);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma_16816(tmp[nt], af, bf[nt][2 * j], bf[nt][2 * j + 1], tmp[nt]);
+        }
+        if ((kb % GB) == GB - 1) {  // group complete: apply the per-row scales
+          const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[su * 8 + g];
+          const float2 sc = __half22float2(u32_as_h2(sp));
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            acc[nt][0] = __fmaf_rn(sc.x, tmp[nt][0], acc[nt][0]);
+            acc[nt][1] = __fmaf_rn(sc.x, tmp[nt][1], acc[nt][1]);
+            acc[nt][2] = __fmaf_rn(sc.y, tmp[nt][2], acc[nt][2]);
+            acc[nt][3] = __fmaf_rn(sc.y, tmp[nt][3], acc[nt][3]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) tmp[nt][q] = 0.f;
+          }
+        }
+      } else {
+        const uint2 sb = reinterpret_cast<const uint2*>(sst)[su * 8 + g];
+        const __half2 s01 = u32_as_h2(sb.x), s23 = u32_as_h2(sb.y);
+        const __half2 sg = __half2half2(__low2half(s01)), bg = __half2half2(__high2half(s01));
+        const __half2 sg8 = __half2half2(__low2half(s23)), bg8 = __half2half2(__high2half(s23));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t af[4];
+          unpack_word<0>(words[j], af);
+          // w = fp16(q * s + b): the reference's dequantized fp16 weight
+          af[0] = h2_as_u32(__hfma2(u32_as_h2(af[0]), sg, bg));
+          af[1] = h2_as_u32(__hfma2(u32_as_h2(af[1]), sg8, bg8));
+          af[2] = h2_as_u32(__hfma2(u32_as_h2(af[2]), sg, bg));
+          af[3] = h2_as_u32(__hfma2(u32_as_h2(af[3]), sg8, bg8));
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma_16816(acc[nt], af, bf[nt][2 * j], bf[nt][2 * j + 1], acc[nt]);
+        }
+      }
+      // segment end: end of the tile or of this warp's range
+      if (kb == a.KB - 1 || kbi == kb1 - 1) {
+        const bool complete = (kb == a.KB - 1) && (!first_seg || kb0 == (long long)tile * a.KB);
+        if (complete) {
+          epilogue<NT>(a, tile, acc, lane);
+        } else {
+          const int slot = first_seg ? 0 : 1;
+          float* p = a.partials + ((w * 2 + slot) * 32 + lane) * (4 * NT);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            *reinterpret_cast<float4*>(p + 4 * nt) = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+          __threadfence();
+          __syncwarp();
+          int old = 0;
+          if (lane == 0) old = atomicAdd(a.counters + tile, 1);
+          old = __shfl_sync(0xffffffffu, old, 0);
+          const long long tu0 = (long long)tile * a.upt, tu1 = tu0 + a.upt - 1;
+          const long long wf = warp_of_unit(tu0, a.U, a.Wt), wl = warp_of_unit(tu1, a.U, a.Wt);
+          if (old == (int)(wl - wf)) {  // last contributor: reduce in warp order
+            __threadfence();
+            float sum[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int q = 0; q < 4; ++q) sum[nt][q] = 0.f;
+            for (long long ww = wf; ww <= wl; ++ww) {
+              const int sl = (warp_start(ww, a.U, a.Wt) / a.upt == tile) ? 0 : 1;
+              const float* pp = a.partials + ((ww * 2 + sl) * 32 + lane) * (4 * NT);
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                float4 v = __ldcg(reinterpret_cast<const float4*>(pp + 4 * nt));
+                sum[nt][0] += v.x;
+                sum[nt][1] += v.y;
+                sum[nt][2] += v.z;
+                sum[nt][3] += v.w;
+              }
+            }
+            epilogue<NT>(a, tile, sum, lane);
+            if (lane == 0) a.counters[tile] = 0;
+          }
+        }
+        first_seg = false;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[nt][q] = 0.f;
+      }
+    }
+    __syncwarp();
+    issue(it + kStages);
+  }
+}
+
+// ------------------------------------------------------------------ host
+static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+static int nt_for(int M) { return M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; }
+static long long max_warps() { return (long long)num_sms() * 2 * kWarpsPerCta; }
+static constexpr size_t kSmemLimit = 227 * 1024;
+static constexpr size_t kXsLimit = kSmemLimit - kWarpsPerCta * kWarpRing - 1024;
+
+template <int NT, bool SYM, int GB, bool XS>
+static cudaError_t launch_one(const GemmArgs& ga, int ctas, int threads, size_t smem, cudaStream_t s, bool pdl) {
+  return launch_pdl(qgemm_kernel<NT, SYM, GB, XS>, dim3(ctas), dim3(threads), smem, s, pdl, ga);
+}
+
+template <int NT, bool XS>
+static cudaError_t dispatch_fmt(const GemmArgs& ga, bool sym, int GB, int ctas, int threads, size_t smem,
+                                cudaStream_t s, bool pdl) {
+  if (sym)
+    return GB == 2 ? launch_one<NT, true, 2, XS>(ga, ctas, threads, smem, s, pdl)
+                   : launch_one<NT, true, 1, XS>(ga, ctas, threads, smem, s, pdl);
+  return GB == 2 ? launch_one<NT, false, 2, XS>(ga, ctas, threads, smem, s, pdl)
+                 : launch_one<NT, false, 1, XS>(ga, ctas, threads, smem, s, pdl);
+}
+
+bool qgemm_can_fuse_norm(int M, int K) {
+  return nt_for(M) <= 4 && round_up((size_t)M * (K + 8) * sizeof(__half), 128) <= kXsLimit;
+}
+
+// Set the shared-memory attribute of every instantiation once per device,
+// outside any stream capture.
+int qgemm_prepare() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int done_dev = -1;
+  if (done_dev == dev) return AXB_OK;
+#define AXB_SET(NT, SYM, GB, XS)                                                                             \
+  {                                                                                                         \
+    cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<NT, SYM, GB, XS>,                                      \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);     \
+    if (e != cudaSuccess) return cuda_status(e, "qgemm attribute");                                         \
+  }
+#define AXB_SET4(NT, XS) AXB_SET(NT, true, 1, XS) AXB_SET(NT, true, 2, XS) AXB_SET(NT, false, 1, XS) AXB_SET(NT, false, 2, XS)
+  AXB_SET4(1, true) AXB_SET4(1, false) AXB_SET4(2, true) AXB_SET4(2, false) AXB_SET4(4, true) AXB_SET4(4, false)
+  AXB_SET4(8, false)
+#undef AXB_SET4
+#undef AXB_SET
+  done_dev = dev;
+  return AXB_OK;
+}
+
+size_t qgemm_workspace(int N, int M) {
+  int n_tiles = (N + 15) / 16;
+  size_t head = 256;  // error word
+  size_t counters = round_up((size_t)n_tiles * 4, 256);
+  size_t partials = (size_t)2 * max_warps() * 32 * 4 * nt_for(M) * sizeof(float);
+  return head + counters + partials;
+}
+
+int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
+  AXB_CHECK_ARG(d, "null descriptor");
+  AXB_CHECK_ARG(d->fmt == AXB_W_Q4T_SYM || d->fmt == AXB_W_Q4T_AFFINE, "qgemm: unsupported fmt %d", d->fmt);
+  AXB_CHECK_ARG(d->group == 64 || d->group == 128, "qgemm: group must be 64 or 128");
+  AXB_CHECK_ARG(d->N > 0 && d->K > 0 && d->K % d->group == 0, "qgemm: bad N/K (%d, %d)", d->N, d->K);
+  AXB_CHECK_ARG(d->M >= 1 && d->M <= 64, "qgemm: M must be in [1, 64], got %d", d->M);
+  AXB_CHECK_ARG(d->words && d->scales && d->x && d->y, "qgemm: null pointer");
+  AXB_CHECK_ARG((reinterpret_cast<uintptr_t>(d->words) & 15) == 0 && (reinterpret_cast<uintptr_t>(d->scales) & 15) == 0,
+                "qgemm: weights and scales must be 16-byte aligned");
+  AXB_CHECK_ARG(d->ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(d->x) & 15) == 0,
+                "qgemm: x must be 16-byte aligned with ldx %% 8 == 0");
+  AXB_CHECK_ARG(!d->gate_up_interleave || d->N % 16 == 0, "qgemm: gate/up interleave needs N %% 16 == 0");
+  AXB_CHECK_ARG(d->epilogue != AXB_EPI_SWIGLU || d->gate_up_interleave, "qgemm: SWIGLU needs interleaved rows");
+  AXB_CHECK_ARG(d->workspace && d->workspace_bytes >= qgemm_workspace(d->N, d->M),
+                "qgemm: workspace too small (%zu < %zu)", d->workspace_bytes, qgemm_workspace(d->N, d->M));
+  if (int rc = qgemm_prepare()) return rc;
+  GemmArgs ga = {};
+  ga.W = reinterpret_cast<const uint4*>(d->words);
+  ga.S = reinterpret_cast<const char*>(d->scales);
+  ga.N = d->N;
+  ga.K = d->K;
+  ga.M = d->M;
+  ga.KB = d->K / 64;
+  ga.GB = d->group / 64;
+  ga.upt = d->K / d->group;
+  const int n_tiles = (d->N + 15) / 16;
+  ga.U = (long long)n_tiles * ga.upt;
+  ga.x = reinterpret_cast<const __half*>(d->x);
+  ga.ldx = d->ldx;
+  ga.norm_w = d->norm_w;
+  ga.eps = d->eps;
+  ga.y = d->y;
+  ga.ldy = d->ldy;
+  ga.bias = reinterpret_cast<const __half*>(d->bias);
+  ga.epi = d->epilogue;
+  ga.gu = d->gate_up_interleave;
+  char* ws = reinterpret_cast<char*>(d->workspace);
+  ga.err = reinterpret_cast<int*>(ws);
+  ga.counters = reinterpret_cast<int*>(ws + 256);
+  ga.partials = reinterpret_cast<float*>(ws + 256 + round_up((size_t)n_tiles * 4, 256));
+  // grid: persistent, every warp owns >= 1 quantization group
+  long long wt = std::min<long long>(max_warps(), ga.U);
+  int threads = kWarpsPerCta * 32;
+  int ctas;
+  if (wt >= kWarpsPerCta) {
+    ctas = (int)(wt / kWarpsPerCta);
+    wt = (long long)ctas * kWarpsPerCta;
+  } else {
+    ctas = 1;
+    threads = (int)wt * 32;
+  }
+  ga.Wt = wt;
+  const int pad = 8;
+  size_t xsb = round_up((size_t)d->M * (d->K + pad) * sizeof(__half), 128);
+  const int nt = nt_for(d->M);
+  bool xs = nt <= 4 && xsb <= kXsLimit;
+  AXB_CHECK_ARG(xs || !d->norm_w, "qgemm: fused RMSNorm needs M <= 32 and M*K*2 <= %zu bytes", kXsLimit);
+  ga.xs_stride = xs ? d->K + pad : 0;
+  ga.xs_bytes = xs ? (int)xsb : 0;
+  size_t smem = (size_t)ga.xs_bytes + (size_t)(threads / 32) * kWarpRing;
+  const bool sym = d->fmt == AXB_W_Q4T_SYM;
+  cudaError_t e;
+  switch (nt) {
+    case 1:
+      e = xs ? dispatch_fmt<1, true>(ga, sym, ga.GB, ctas, threads, smem, stream, d->pdl)
+             : dispatch_fmt<1, false>(ga, sym, ga.GB, ctas, threads, smem, stream, d->pdl);
+      break;
+    case 2:
+      e = xs ? dispatch_fmt<2, true>(ga, sym, ga.GB, ctas, threads, smem, stream, d->pdl)
+             : dispatch_fmt<2, false>(ga, sym, ga.GB, ctas, threads, smem, stream, d->pdl);
+      break;
+    case 4:
+      e = xs ? dispatch_fmt<4, true>(ga, sym, ga.GB, ctas, threads, smem, stream, d->pdl)
+             : dispatch_fmt<4, false>(ga, sym, ga.GB, ctas, threads, smem, stream, d->pdl);
+      break;
+    default: e = dispatch_fmt<8, false>(ga, sym, ga.GB, ctas, threads, smem, stream, d->pdl); break;
+  }
+  return cuda_status(e, "qgemm launch");
+}
+
+int qgemm_status(void* workspace, cudaStream_t s) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(e, "qgemm status");
+  if (v != 0) {
+    set_error("qgemm: a weight-stream wait ran out (status %d)", v);
+    int z = 0;
+    cudaMemcpyAsync(workspace, &z, sizeof(int), cudaMemcpyHostToDevice, s);
+    cudaStreamSynchronize(s);
+    return v;
+  }
+  return AXB_OK;
+}
+
+}  // namespace axb
+
+using namespace axb;
+
+extern "C" {
+
+size_t axb_q4t_words_bytes(int N, int K) { return (size_t)((N + 15) / 16) * (K / 64) * 512; }
+size_t axb_q4t_scales_bytes(int N, int K, int group, int fmt) {
+  return (size_t)((N + 15) / 16) * (K / group) * 16 * (fmt == AXB_W_Q4T_AFFINE ? 2 : 1) * sizeof(uint16_t);
+}
+
+int axb_q4t_pack(const float* w, int N, int K, int group, int fmt, int gu, void* words, void* scales, void* stream) {
+  AXB_CHECK_ARG(w && words && scales, "q4t_pack: null pointer");
+  AXB_CHECK_ARG(K % 64 == 0 && (group == 64 || group == 128) && K % group == 0, "q4t_pack: bad K/group");
+  AXB_CHECK_ARG(fmt == AXB_W_Q4T_SYM || fmt == AXB_W_Q4T_AFFINE, "q4t_pack: bad fmt");
+  AXB_CHECK_ARG(!gu || N % 16 == 0, "q4t_pack: gate/up interleave needs N %% 16 == 0");
+  dim3 grid(K / 64, (N + 15) / 16);
+  q4t_pack_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(w, N, K, group, fmt == AXB_W_Q4T_SYM, gu,
+                                                          (uint32_t*)words, (__half*)scales);
+  return launch_status("q4t_pack");
+}
+
+int axb_q4t_from_marlin(const int32_t* wm, const uint16_t* sb, int n_tiles8, int K, int n_out, int gu, void* words,
+                        void* scales, void* stream) {
+  AXB_CHECK_ARG(wm && sb && words && scales, "q4t_from_marlin: null pointer");
+  AXB_CHECK_ARG(K % 64 == 0 && n_out > 0 && n_out <= n_tiles8 * 8, "q4t_from_marlin: bad shape");
+  AXB_CHECK_ARG(!gu || n_out % 16 == 0, "q4t_from_marlin: gate/up interleave needs N %% 16 == 0");
+  dim3 grid(K / 64, (n_out + 15) / 16);
+  q4t_from_marlin_kernel<<<grid, 160, 0, (cudaStream_t)stream>>>((const uint32_t*)wm, (const __half*)sb,
+                                                                 n_tiles8 * 8, K, n_out, gu, (uint32_t*)words,
+                                                                 (__half*)scales);
+  return launch_status("q4t_from_marlin");
+}
+
+int axb_q4t_dequant(const void* words, const void* scales, int N, int K, int group, int fmt, int gu, uint16_t* out,
+                    void* stream) {
+  AXB_CHECK_ARG(words && scales && out, "q4t_dequant: null pointer");
+  AXB_CHECK_ARG(K % 64 == 0 && (group == 64 || group == 128) && K % group == 0, "q4t_dequant: bad K/group");
+  dim3 grid(K / 64, (N + 15) / 16);
+  q4t_dequant_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>((const uint32_t*)words, (const __half*)scales, N, K,
+                                                             group, fmt == AXB_W_Q4T_SYM, gu, (__half*)out);
+  return launch_status("q4t_dequant");
+}
+
+int axb_q4_marlin_dequant(const int32_t* wm, const uint16_t* sb, int n_tiles8, int K, int n_out, uint16_t* out,
+                          void* stream) {
+  AXB_CHECK_ARG(wm && sb && out && K % 64 == 0 && n_out <= n_tiles8 * 8 && n_out > 0, "marlin_dequant: bad args");
+  dim3 grid((K + 255) / 256, n_out);
+  marlin_dequant_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint32_t*)wm, (const __half*)sb, K, n_out,
+                                                                (__half*)out);
+  return launch_status("marlin_dequant");
+}
+
+int axb_q8_pack(const float* w, int N, int K, int32_t* out, uint16_t* sb, void* stream) {
+  AXB_CHECK_ARG(w && out && sb && N > 0 && K % 64 == 0, "q8_pack: bad args");
+  long long items = (long long)N * (K / 64);
+  q8_pack_kernel<<<(unsigned)((items + 7) / 8), 256, 0, (cudaStream_t)stream>>>(w, N, K, (uint32_t*)out, (__half*)sb);
+  return launch_status("q8_pack");
+}
+
+int axb_q8_rows(const int32_t* w, const uint16_t* sb, const int32_t* idx, int n_idx, int K, uint16_t* out,
+                void* stream) {
+  AXB_CHECK_ARG(w && sb && idx && out && K % 64 == 0 && n_idx >= 0, "q8_rows: bad args");
+  if (n_idx == 0) return AXB_OK;
+  q8_rows_kernel<<<n_idx, 256, 0, (cudaStream_t)stream>>>((const uint32_t*)w, (const __half*)sb, idx, K,
+                                                          (__half*)out);
+  return launch_status("q8_rows");
+}
+
+int axb_ternary_dequant(const uint8_t* w, const uint16_t* s, int N, int K, int per_tensor, uint16_t* out,
+                        void* stream) {
+  AXB_CHECK_ARG(w && s && out && K % 64 == 0 && N > 0, "ternary_dequant: bad args");
+  dim3 grid((K + 255) / 256, N);
+  ternary_dequant_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(w, (const __half*)s, K, per_tensor, (__half*)out);
+  return launch_status("ternary_dequant");
+}
+
+int axb_q2_dequant(const uint8_t* w, const uint16_t* sb, int N, int K, uint16_t* out, void* stream) {
+  AXB_CHECK_ARG(w && sb && out && K % 64 == 0 && N > 0, "q2_dequant: bad args");
+  dim3 grid((K + 255) / 256, N);
+  q2_dequant_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(w, (const __half*)sb, K, (__half*)out);
+  return launch_status("q2_dequant");
+}
+
+size_t axb_qgemm_workspace_bytes(int N, int K, int M, int group) {
+  (void)K;
+  (void)group;
+  return qgemm_workspace(N, M);
+}
+
+int axb_qgemm(const axb_qgemm_desc* d, void* stream) { return qgemm(d, (cudaStream_t)stream); }
+
+int axb_qgemm_status(void* workspace, void* stream) {
+  AXB_CHECK_ARG(workspace, "qgemm_status: null workspace");
+  return qgemm_status(workspace, (cudaStream_t)stream);
+}
+
+}  // extern "C"

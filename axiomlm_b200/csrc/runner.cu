@@ -1,0 +1,424 @@
+// Whole-model quantized decode runner: one CUDA graph per (batch, tokens, mode).
+//
+// Replaces MPSQuantizedDecodeRunner / QuantizedDecodeGraphState
+// (axiomlm/kernels/mps_kernels.mm:2982-3737: step 3195, verify_tree_step 3265,
+// verify_step 3359, get_last_norm 3732), which encodes every layer into one
+// Metal command buffer per step.  Here the per-step kernel sequence
+//   embed -> L x [qkv GEMV(+RMSNorm) -> RoPE+KV write -> attention ->
+//   o GEMV(+residual) -> gate_up GEMV(+RMSNorm, SwiGLU) -> down GEMV(+residual)]
+//   -> lm_head GEMV(+final RMSNorm) -> argmax
+// is captured once into a CUDA graph (kernels chained with programmatic
+// dependent launch) and replayed; per-step positions live in a device buffer
+// written by one tiny kernel before each replay.
+#include <map>
+#include <tuple>
+#include <vector>
+
+#include "axb_common.cuh"
+
+namespace axb {
+
+int qgemm(const axb_qgemm_desc* d, cudaStream_t stream);
+int qgemm_prepare();
+bool qgemm_can_fuse_norm(int M, int K);
+size_t qgemm_workspace(int N, int M);
+int rope_kv_write(const axb_kv_write_desc* d, cudaStream_t s, bool pdl);
+int attention(const axb_attn_desc* d, cudaStream_t s);
+size_t attn_workspace(int B, int n_head, int head_dim, int max_splits);
+int decode_max_splits(int B, int n_kv_head);
+int rmsnorm(const __half* x, const float* w, int M, int K, float eps, __half* out, cudaStream_t s);
+int argmax(const __half* x, int rows, int n, int ld, int32_t* out, cudaStream_t s);
+
+struct StepParams {
+  int32_t p[4];  // rope_pos, write_pos, active_len, prefix_len
+  int32_t T;
+  uint64_t masks[64];
+  int32_t depths[64];
+};
+
+__global__ void set_params_kernel(StepParams sp, int32_t* params, uint64_t* masks, int32_t* depths) {
+  int t = threadIdx.x;
+  if (t < 4) params[t] = sp.p[t];
+  if (t < sp.T) {
+    masks[t] = sp.masks[t];
+    depths[t] = sp.depths[t];
+  }
+}
+
+__global__ void embed_q8_kernel(const uint32_t* __restrict__ w, const __half* __restrict__ sb,
+                                const int32_t* __restrict__ tok, int K, int V, __half* __restrict__ out,
+                                int* __restrict__ err) {
+  pdl_wait();
+  const int i = blockIdx.x;
+  const int r = tok[i];
+  if (r < 0 || r >= V) {  // out-of-vocabulary id: zero row, flag the error
+    for (int k = threadIdx.x; k < K; k += blockDim.x) out[(size_t)i * K + k] = __float2half_rn(0.f);
+    if (threadIdx.x == 0) atomicExch(err, AXB_EINVAL);
+    return;
+  }
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    uint32_t word = w[(size_t)r * (K / 4) + k / 4];
+    int q = (word >> (8 * (k & 3))) & 0xFF;
+    const __half* p = sb + ((size_t)r * (K / 64) + k / 64) * 2;
+    float v = __fadd_rn(__fmul_rn((float)q, __half2float(p[0])), __half2float(p[1]));
+    out[(size_t)i * K + k] = __float2half_rn(v);
+  }
+}
+
+// final-norm hidden state in fp32 (the reference's x_norm / get_last_norm)
+__global__ void rmsnorm_f32_kernel(const __half* __restrict__ x, const float* __restrict__ w, int K, float eps,
+                                   float* __restrict__ out) {
+  pdl_wait();
+  const int row = blockIdx.x;
+  const __half* xr = x + (size_t)row * K;
+  float ss = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    float v = __half2float(xr[k]);
+    ss = __fmaf_rn(v, v, ss);
+  }
+  __shared__ float red[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)K), eps)));
+  for (int k = threadIdx.x; k < K; k += blockDim.x)
+    out[(size_t)row * K + k] = __fmul_rn(__fmul_rn(__half2float(xr[k]), rms), w[k]);
+}
+
+static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+struct Layout {
+  size_t tokens, params, masks, depths, x, h, qkv, q, attn, sw, logits, amax, xnorm, gemm_ws, attn_ws, total;
+  size_t gemm_ws_bytes, attn_ws_bytes;
+};
+
+static Layout make_layout(const axb_model_cfg& c) {
+  Layout L = {};
+  const size_t rows = (size_t)c.max_batch * c.max_tokens;
+  const size_t qkv_dim = (size_t)(c.n_head + 2 * c.n_kv_head) * c.head_dim;
+  const size_t qd = (size_t)c.n_head * c.head_dim;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += align256(bytes);
+    return o;
+  };
+  L.tokens = take(rows * 4);
+  L.params = take(32);  // [rope_pos, write_pos, active_len, prefix_len, error]
+  L.masks = take(64 * 8);
+  L.depths = take(64 * 4);
+  L.x = take(rows * c.d_model * 2);
+  L.h = take(rows * c.d_model * 2);
+  L.qkv = take(rows * qkv_dim * 2);
+  L.q = take(rows * qd * 4);
+  L.attn = take(rows * qd * 2);
+  L.sw = take(rows * (size_t)c.ffn * 2);
+  L.logits = take(rows * (size_t)c.vocab * 2);
+  L.amax = take(rows * 4);
+  L.xnorm = take(rows * (size_t)c.d_model * 4);
+  int m = (int)std::min<size_t>(rows, 64);
+  size_t g = 0;
+  for (int n : {(int)qkv_dim, c.d_model, 2 * c.ffn, c.vocab}) g = std::max(g, qgemm_workspace(n, m));
+  L.gemm_ws_bytes = g;
+  L.gemm_ws = take(g);
+  size_t a = 0;
+  for (int b = 1; b <= c.max_batch; ++b)
+    a = std::max(a, attn_workspace(b, c.n_head, c.head_dim, decode_max_splits(b, c.n_kv_head)));
+  L.attn_ws_bytes = a;
+  L.attn_ws = take(a);
+  L.total = off;
+  return L;
+}
+
+struct Runner {
+  axb_model_cfg c;
+  Layout L;
+  char* ws;
+  const void *emb_w, *emb_s, *lm_w, *lm_s;
+  const float *ln_f, *rope;
+  std::vector<const void*> qkv_w, qkv_s, qkv_b, o_w, o_s, gu_w, gu_s, dn_w, dn_s;
+  std::vector<const float*> ln1, ln2;
+  std::vector<void*> kc, vc, ks, vs;
+  cudaStream_t cap = nullptr;
+  std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;
+
+  template <typename T>
+  T* buf(size_t off) const {
+    return reinterpret_cast<T*>(ws + off);
+  }
+
+  int gemv(const void* w, const void* s, int fmt, int group, int N, int K, int M, const __half* x, int ldx,
+           void* y, int ldy, const void* bias, const float* norm_w, int epi, int gu, cudaStream_t st) const {
+    // rows beyond 64 are processed in 64-row chunks (one weight pass each)
+    for (int m0 = 0; m0 < M; m0 += 64) {
+      axb_qgemm_desc d = {};
+      d.fmt = fmt;
+      d.group = group;
+      d.words = w;
+      d.scales = s;
+      d.N = N;
+      d.K = K;
+      d.M = std::min(64, M - m0);
+      d.x = x + (size_t)m0 * ldx;
+      d.ldx = ldx;
+      size_t esz = epi == AXB_EPI_F32 ? 4 : 2;
+      d.y = reinterpret_cast<char*>(y) + (size_t)m0 * ldy * esz;
+      d.ldy = ldy;
+      d.bias = bias;
+      d.norm_w = norm_w;
+      d.eps = c.eps;
+      d.epilogue = epi;
+      d.gate_up_interleave = gu;
+      d.workspace = buf<void>(L.gemm_ws);
+      d.workspace_bytes = L.gemm_ws_bytes;
+      d.pdl = 1;
+      int rc = qgemm(&d, st);
+      if (rc) return rc;
+    }
+    return AXB_OK;
+  }
+
+  // norm + GEMV: fused prologue when the normalized rows fit in shared memory
+  int norm_gemv(const float* nw, const void* w, const void* s, int N, int K, int M, void* y, int ldy,
+                const void* bias, int epi, int gu, int fmt, int group, cudaStream_t st) const {
+    const __half* x = buf<__half>(L.x);
+    if (qgemm_can_fuse_norm(M, K))
+      return gemv(w, s, fmt, group, N, K, M, x, K, y, ldy, bias, nw, epi, gu, st);
+    int rc = rmsnorm(x, nw, M, K, c.eps, buf<__half>(L.h), st);
+    if (rc) return rc;
+    return gemv(w, s, fmt, group, N, K, M, buf<__half>(L.h), K, y, ldy, bias, nullptr, epi, gu, st);
+  }
+
+  int forward(int B, int T, bool tree, bool want_norm, cudaStream_t st) const {
+    const int rows = B * T;
+    const int d = c.d_model, hd = c.head_dim, Hq = c.n_head, Hkv = c.n_kv_head;
+    const int qkv_dim = (Hq + 2 * Hkv) * hd, qd = Hq * hd;
+    cudaError_t e = launch_pdl(embed_q8_kernel, dim3(rows), dim3(256), 0, st, true, (const uint32_t*)emb_w,
+                               (const __half*)emb_s, (const int32_t*)buf<int32_t>(L.tokens), d, c.vocab,
+                               buf<__half>(L.x), buf<int>(L.params) + 4);
+    if (e != cudaSuccess) return cuda_status(e, "embed launch");
+    for (int l = 0; l < c.n_layer; ++l) {
+      int rc = norm_gemv(ln1[l], qkv_w[l], qkv_s[l], qkv_dim, d, rows, buf<void>(L.qkv), qkv_dim, qkv_b[l],
+                         AXB_EPI_STORE, 0, c.wfmt, c.group, st);
+      if (rc) return rc;
+      axb_kv_write_desc kw = {};
+      kw.kv_type = c.kv_type;
+      kw.kv_group = c.kv_group;
+      kw.B = B;
+      kw.T = T;
+      kw.n_head = Hq;
+      kw.n_kv_head = Hkv;
+      kw.head_dim = hd;
+      kw.max_seq = c.max_seq;
+      kw.max_batch = c.max_batch;
+      kw.qkv = buf<uint16_t>(L.qkv);
+      kw.rope = rope;
+      kw.rope_len = c.rope_len;
+      kw.depths = tree ? buf<int>(L.depths) : nullptr;
+      kw.q_out = buf<float>(L.q);
+      kw.dev_params = buf<int32_t>(L.params);
+      kw.k_cache = kc[l];
+      kw.v_cache = vc[l];
+      kw.k_scale = (uint16_t*)ks[l];
+      kw.v_scale = (uint16_t*)vs[l];
+      kw.k_is_fp32 = 1;
+      rc = rope_kv_write(&kw, st, true);
+      if (rc) return rc;
+      axb_attn_desc ad = {};
+      ad.kv_type = c.kv_type;
+      ad.kv_group = c.kv_group;
+      ad.B = B;
+      ad.n_head = Hq;
+      ad.n_kv_head = Hkv;
+      ad.head_dim = hd;
+      ad.max_seq = c.max_seq;
+      ad.max_batch = c.max_batch;
+      ad.q = buf<void>(L.q);
+      ad.q_is_fp32 = 1;
+      ad.k_cache = kc[l];
+      ad.v_cache = vc[l];
+      ad.k_scale = (const uint16_t*)ks[l];
+      ad.v_scale = (const uint16_t*)vs[l];
+      ad.out = buf<void>(L.attn);
+      ad.active_len = 1;  // overridden by dev_params
+      ad.T = T;
+      ad.prefix_len = 0;
+      ad.masks = tree ? buf<uint64_t>(L.masks) : nullptr;
+      ad.dev_params = buf<int32_t>(L.params);
+      ad.workspace = buf<void>(L.attn_ws);
+      ad.workspace_bytes = L.attn_ws_bytes;
+      ad.pdl = 1;
+      rc = attention(&ad, st);
+      if (rc) return rc;
+      rc = gemv(o_w[l], o_s[l], c.wfmt, c.group, d, qd, rows, buf<__half>(L.attn), qd, buf<void>(L.x), d, nullptr,
+                nullptr, AXB_EPI_RESIDUAL, 0, st);
+      if (rc) return rc;
+      rc = norm_gemv(ln2[l], gu_w[l], gu_s[l], 2 * c.ffn, d, rows, buf<void>(L.sw), c.ffn, nullptr, AXB_EPI_SWIGLU,
+                     1, c.wfmt, c.group, st);
+      if (rc) return rc;
+      rc = gemv(dn_w[l], dn_s[l], c.wfmt, c.group, d, c.ffn, rows, buf<__half>(L.sw), c.ffn, buf<void>(L.x), d,
+                nullptr, nullptr, AXB_EPI_RESIDUAL, 0, st);
+      if (rc) return rc;
+    }
+    int rc = norm_gemv(ln_f, lm_w, lm_s, c.vocab, d, rows, buf<void>(L.logits), c.vocab, nullptr, AXB_EPI_STORE, 0,
+                       c.lm_fmt, c.lm_group, st);
+    if (rc) return rc;
+    if (want_norm) {
+      e = launch_pdl(rmsnorm_f32_kernel, dim3(rows), dim3(256), 0, st, true, (const __half*)buf<__half>(L.x), ln_f,
+                     d, c.eps, buf<float>(L.xnorm));
+      if (e != cudaSuccess) return cuda_status(e, "final norm launch");
+    }
+    return argmax(buf<__half>(L.logits), rows, c.vocab, c.vocab, buf<int32_t>(L.amax), st);
+  }
+};
+
+}  // namespace axb
+
+using namespace axb;
+
+extern "C" {
+
+size_t axb_runner_workspace_bytes(const axb_model_cfg* cfg) {
+  if (!cfg) return 0;
+  return make_layout(*cfg).total;
+}
+
+int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* ws, size_t ws_bytes, void** out) {
+  AXB_CHECK_ARG(cfg && p && ws && out, "runner_create: null argument");
+  const axb_model_cfg& c = *cfg;
+  AXB_CHECK_ARG(c.n_layer > 0 && c.d_model % 64 == 0 && c.ffn % 64 == 0 && c.vocab > 0, "runner_create: bad dims");
+  AXB_CHECK_ARG(c.head_dim == 64 || c.head_dim == 128, "runner_create: head_dim must be 64 or 128");
+  AXB_CHECK_ARG(c.n_head * c.head_dim == c.d_model, "runner_create: n_head * head_dim must equal d_model");
+  AXB_CHECK_ARG(c.wfmt == AXB_W_Q4T_SYM || c.wfmt == AXB_W_Q4T_AFFINE, "runner_create: unsupported weight format");
+  AXB_CHECK_ARG(c.lm_fmt == AXB_W_Q4T_SYM || c.lm_fmt == AXB_W_Q4T_AFFINE,
+                "runner_create: lm_head format %d not supported by the runner", c.lm_fmt);
+  AXB_CHECK_ARG(c.max_tokens >= 1 && c.max_tokens <= 64 && c.max_batch >= 1, "runner_create: bad max_tokens/batch");
+  AXB_CHECK_ARG(c.ffn % 8 == 0, "runner_create: ffn must be a multiple of 8");
+  Layout L = make_layout(c);
+  AXB_CHECK_ARG(ws_bytes >= L.total, "runner_create: workspace %zu < %zu bytes", ws_bytes, L.total);
+  if (int rc = qgemm_prepare()) return rc;
+  Runner* r = new Runner();
+  r->c = c;
+  r->L = L;
+  r->ws = reinterpret_cast<char*>(ws);
+  r->emb_w = p->emb_w;
+  r->emb_s = p->emb_s;
+  r->lm_w = p->lm_w;
+  r->lm_s = p->lm_s;
+  r->ln_f = p->ln_f;
+  r->rope = p->rope;
+  for (int l = 0; l < c.n_layer; ++l) {
+    r->qkv_w.push_back(p->qkv_w[l]);
+    r->qkv_s.push_back(p->qkv_s[l]);
+    r->qkv_b.push_back(p->qkv_b ? p->qkv_b[l] : nullptr);
+    r->o_w.push_back(p->o_w[l]);
+    r->o_s.push_back(p->o_s[l]);
+    r->gu_w.push_back(p->gu_w[l]);
+    r->gu_s.push_back(p->gu_s[l]);
+    r->dn_w.push_back(p->dn_w[l]);
+    r->dn_s.push_back(p->dn_s[l]);
+    r->ln1.push_back(p->ln1[l]);
+    r->ln2.push_back(p->ln2[l]);
+    r->kc.push_back(p->k_cache[l]);
+    r->vc.push_back(p->v_cache[l]);
+    r->ks.push_back(p->k_scale ? p->k_scale[l] : nullptr);
+    r->vs.push_back(p->v_scale ? p->v_scale[l] : nullptr);
+  }
+  cudaError_t e = cudaStreamCreateWithFlags(&r->cap, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete r;
+    return cuda_status(e, "runner stream");
+  }
+  *out = r;
+  return AXB_OK;
+}
+
+int axb_runner_destroy(void* h) {
+  Runner* r = reinterpret_cast<Runner*>(h);
+  if (!r) return AXB_OK;
+  for (auto& kv : r->graphs) cudaGraphExecDestroy(kv.second);
+  if (r->cap) cudaStreamDestroy(r->cap);
+  delete r;
+  return AXB_OK;
+}
+
+int axb_runner_buffer(void* h, int which, size_t* off, size_t* bytes) {
+  Runner* r = reinterpret_cast<Runner*>(h);
+  AXB_CHECK_ARG(r && off && bytes, "runner_buffer: null argument");
+  const size_t rows = (size_t)r->c.max_batch * r->c.max_tokens;
+  switch (which) {
+    case 0: *off = r->L.tokens; *bytes = rows * 4; break;
+    case 1: *off = r->L.logits; *bytes = rows * r->c.vocab * 2; break;
+    case 2: *off = r->L.amax; *bytes = rows * 4; break;
+    case 3: *off = r->L.xnorm; *bytes = rows * r->c.d_model * 4; break;
+    case 4: *off = r->L.params + 16; *bytes = 4; break;
+    default: axb::set_error("runner_buffer: unknown buffer %d", which); return AXB_EINVAL;
+  }
+  return AXB_OK;
+}
+
+int axb_runner_step(void* h, int B, int T, int rope_pos, int write_pos, int active_len, int prefix_len,
+                    const uint64_t* masks, const int32_t* depths, int use_graph, void* stream) {
+  Runner* r = reinterpret_cast<Runner*>(h);
+  AXB_CHECK_ARG(r, "runner_step: null handle");
+  const axb_model_cfg& c = r->c;
+  AXB_CHECK_ARG(B >= 1 && B <= c.max_batch && T >= 1 && T <= c.max_tokens, "runner_step: bad B/T (%d, %d)", B, T);
+  const bool tree = masks != nullptr;
+  AXB_CHECK_ARG(tree || T == 1, "runner_step: T > 1 needs masks (tree / chunked-prefill mode)");
+  AXB_CHECK_ARG(!tree || (depths != nullptr), "runner_step: tree mode needs depths");
+  AXB_CHECK_ARG(tree || (active_len >= 1 && active_len <= c.max_seq), "runner_step: bad active_len %d", active_len);
+  AXB_CHECK_ARG(write_pos >= 0 && write_pos < c.max_seq, "runner_step: bad write_pos %d", write_pos);
+  AXB_CHECK_ARG(!tree || (prefix_len >= 0 && prefix_len + T <= c.max_seq && write_pos + T <= c.max_seq),
+                "runner_step: tree slots must fit in the cache");
+  if (tree)
+    for (int t = 0; t < T; ++t) {
+      AXB_CHECK_ARG((masks[t] >> t) & 1ull, "runner_step: masks[%d] must include the node itself", t);
+      AXB_CHECK_ARG(T == 64 || (masks[t] >> T) == 0, "runner_step: masks[%d] has bits beyond T", t);
+    }
+  cudaStream_t st = (cudaStream_t)stream;
+  StepParams sp = {};
+  sp.p[0] = rope_pos;
+  sp.p[1] = write_pos;
+  sp.p[2] = active_len;
+  sp.p[3] = prefix_len;
+  sp.T = tree ? T : 0;
+  if (tree)
+    for (int t = 0; t < T; ++t) {
+      sp.masks[t] = masks[t];
+      sp.depths[t] = depths[t];
+    }
+  set_params_kernel<<<1, 64, 0, st>>>(sp, r->buf<int32_t>(r->L.params), r->buf<uint64_t>(r->L.masks),
+                                      r->buf<int32_t>(r->L.depths));
+  int rc = launch_status("set_params");
+  if (rc) return rc;
+  const bool want_norm = tree;
+  if (!use_graph) return r->forward(B, T, tree, want_norm, st);
+  auto key = std::make_tuple(B, T, tree ? 1 : 0);
+  auto it = r->graphs.find(key);
+  if (it == r->graphs.end()) {
+    cudaError_t e = cudaStreamBeginCapture(r->cap, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return cuda_status(e, "begin capture");
+    rc = r->forward(B, T, tree, want_norm, r->cap);
+    cudaGraph_t g = nullptr;
+    e = cudaStreamEndCapture(r->cap, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return cuda_status(e, "end capture");
+    cudaGraphExec_t ex = nullptr;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_status(e, "graph instantiate");
+    it = r->graphs.emplace(key, ex).first;
+  }
+  return cuda_status(cudaGraphLaunch(it->second, st), "graph launch");
+}
+
+}  // extern "C"

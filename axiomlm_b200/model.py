@@ -1,0 +1,271 @@
+"""Quantized decoder on the CUDA-graph runner: the drop-in for the reference's
+quantized ``Transformer`` decode path.
+
+Mirrors ``Transformer.quantize`` / ``_ensure_quant_weights`` /
+``forward`` (T = 1 decode and T > 1 chunked prefill) /
+``forward_tree_verify`` / ``get_decode_runner`` (axiomlm/models/transformer.py
+276-352, 822-1008, 1415-1546, 581-784, 1202-1308), over ``libaxb.so``'s
+runner (replacing MPSQuantizedDecodeRunner, mps_kernels.mm:2982-3737).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from typing import Any
+
+import torch
+
+from . import _lib as L
+from . import ops
+from .cache import StaticKVCache
+
+WEIGHT_FORMATS = {
+    # reference q4_rtn: MARLIN RTN values, affine (scale, bias), group 64
+    "q4_rtn": (L.W_Q4T_AFFINE, 64),
+    # BASELINE config: symmetric, group 128, fp16 scales (4.125 bits/weight)
+    "q4_g128_sym": (L.W_Q4T_SYM, 128),
+}
+
+
+def _vp_array(items):
+    arr = (C.c_void_p * len(items))()
+    for i, t in enumerate(items):
+        arr[i] = None if t is None else t.data_ptr()
+    return arr
+
+
+class QuantizedDecoder:
+    """Packed weights + ``StaticKVCache`` + the CUDA-graph runner.
+
+    ``cfg`` keys: n_layer, d_model, n_head, n_kv_head, ffn, vocab, eps, theta,
+    rope_scaling (optional).  Build with ``from_weights`` (fp32 master
+    weights, packed on the GPU) or ``from_reference`` (a reference
+    ``Transformer`` after ``quantize()``: its own packed tensors are relaid
+    out, so MSE-clipped "q4" models are served exactly as packed).
+    """
+
+    def __init__(self, cfg: dict, packed: dict, *, kv_dtype: str = "fp16", kv_group: int = 64, max_batch: int = 1,
+                 max_seq: int = 1024, max_tokens: int = 64, ring_buffer: bool = False, rope_len: int | None = None,
+                 device: str | torch.device = "cuda", use_graph: bool = True):
+        self.cfg = dict(cfg)
+        self.device = torch.device(device)
+        d, H, Hkv = cfg["d_model"], cfg["n_head"], cfg["n_kv_head"]
+        self.head_dim = d // H
+        self.max_tokens = max_tokens
+        self.use_graph = use_graph
+        self.packed = packed
+        self.cache = StaticKVCache(max_batch, max_seq, cfg["n_layer"], Hkv, self.head_dim, device=self.device,
+                                   ring_buffer=ring_buffer, cache_dtype=kv_dtype, kv_group=kv_group)
+        self.rope_len = rope_len or max(max_seq, cfg.get("block_size", 0))
+        self.rope = ops.rope_table(self.head_dim, self.rope_len, cfg.get("theta", 10000.0),
+                                   cfg.get("rope_scaling")).to(self.device)
+        lay = packed["layers"]
+        wq = lay[0]["qkv"]
+        lm = packed["lm_head"]
+        c = L.ModelCfg(n_layer=cfg["n_layer"], d_model=d, n_head=H, n_kv_head=Hkv, head_dim=self.head_dim,
+                       ffn=cfg["ffn"], vocab=cfg["vocab"], eps=float(cfg["eps"]), wfmt=wq.fmt, group=wq.group,
+                       lm_fmt=lm.fmt, lm_group=lm.group, kv_type=L.KV_TYPES[self.cache.cache_dtype],
+                       kv_group=self.cache.kv_group, max_batch=max_batch, max_seq=max_seq, max_tokens=max_tokens,
+                       rope_len=self.rope_len, has_qkv_bias=int(lay[0].get("qkv_b") is not None))
+        self._cfg_c = c
+        lib = L.load()
+        nbytes = lib.axb_runner_workspace_bytes(C.byref(c))
+        self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        kc = self.cache.k_caches
+        vc = self.cache.v_caches
+        ks = self.cache.k_scales or [None] * cfg["n_layer"]
+        vs = self.cache.v_scales or [None] * cfg["n_layer"]
+        self._arrays = dict(
+            qkv_w=_vp_array([x["qkv"].words for x in lay]), qkv_s=_vp_array([x["qkv"].scales for x in lay]),
+            qkv_b=_vp_array([x.get("qkv_b") for x in lay]),
+            o_w=_vp_array([x["o"].words for x in lay]), o_s=_vp_array([x["o"].scales for x in lay]),
+            gu_w=_vp_array([x["gu"].words for x in lay]), gu_s=_vp_array([x["gu"].scales for x in lay]),
+            dn_w=_vp_array([x["down"].words for x in lay]), dn_s=_vp_array([x["down"].scales for x in lay]),
+            ln1=_vp_array([x["ln_1"] for x in lay]), ln2=_vp_array([x["ln_2"] for x in lay]),
+            k_cache=_vp_array(kc), v_cache=_vp_array(vc), k_scale=_vp_array(ks), v_scale=_vp_array(vs))
+        p = L.ModelPtrs(emb_w=packed["emb_w"].data_ptr(), emb_s=packed["emb_s"].data_ptr(), lm_w=lm.words.data_ptr(),
+                        lm_s=lm.scales.data_ptr(), ln_f=packed["ln_f"].data_ptr(), rope=self.rope.data_ptr(),
+                        **{k: C.cast(v, C.POINTER(C.c_void_p)) for k, v in self._arrays.items()})
+        h = C.c_void_p()
+        L.call("axb_runner_create", C.byref(c), C.byref(p), C.c_void_p(self.workspace.data_ptr()), nbytes, C.byref(h))
+        self._h = h
+
+        def view(which, dtype, shape):
+            off, nb = C.c_size_t(), C.c_size_t()
+            L.call("axb_runner_buffer", self._h, which, C.byref(off), C.byref(nb))
+            return self.workspace[off.value: off.value + nb.value].view(dtype).view(*shape)
+
+        rows = max_batch * max_tokens
+        self.tokens = view(0, torch.int32, (rows,))
+        self.logits_buf = view(1, torch.float16, (rows, cfg["vocab"]))
+        self.argmax_buf = view(2, torch.int32, (rows,))
+        self.norm_buf = view(3, torch.float32, (rows, d))
+        self._last_T = 1
+
+    # ------------------------------------------------------------ builders
+    @classmethod
+    def from_weights(cls, cfg: dict, weights: dict, weight_format: str = "q4_rtn", **kw) -> "QuantizedDecoder":
+        """Pack fp32 master weights (``tests/golden/model_weights.make_weights``
+        layout) on the GPU, following ``_ensure_quant_weights`` in q4_rtn
+        mode (transformer.py:822-1008): projections and an untied lm_head in
+        Q4, token embeddings in Q8_G64, RMSNorm weights kept fp32."""
+        dev = torch.device(kw.get("device", "cuda"))
+        fmt, group = WEIGHT_FORMATS[weight_format]
+        sym = fmt == L.W_Q4T_SYM
+        if weights.get("lm_head") is None:
+            raise NotImplementedError("tied embeddings need the Q8_G64 lm_head GEMV, which the runner lacks")
+
+        def g(t):
+            return t.to(dev, torch.float32)
+
+        layers = []
+        for lw in weights["layers"]:
+            gu = torch.cat([g(lw["w_gate"]), g(lw["w_up"])], 0)
+            layers.append(dict(
+                qkv=ops.pack_q4t(g(lw["c_attn"]), group, sym), o=ops.pack_q4t(g(lw["c_proj"]), group, sym),
+                gu=ops.pack_q4t(gu, group, sym, gate_up=True), down=ops.pack_q4t(g(lw["w_down"]), group, sym),
+                ln_1=g(lw["ln_1"]).contiguous(), ln_2=g(lw["ln_2"]).contiguous(), qkv_b=None))
+            del gu
+        emb_w, emb_s = ops.pack_q8_g64(g(weights["wte"]))
+        packed = dict(layers=layers, emb_w=emb_w, emb_s=emb_s, lm_head=ops.pack_q4t(g(weights["lm_head"]), group, sym),
+                      ln_f=g(weights["ln_f"]).contiguous())
+        return cls(cfg, packed, **kw)
+
+    @classmethod
+    def from_reference(cls, model: Any, **kw) -> "QuantizedDecoder":
+        """Serve a reference ``Transformer`` after ``model.quantize("q4" |
+        "q4_rtn")``: its packed MARLIN tensors are relaid out bit-exactly."""
+        dev = torch.device(kw.get("device", "cuda"))
+        mc = model.config
+        qw = model._ensure_quant_weights(torch.device("cpu"))
+        if qw["lmh_p"].ndim != 4:
+            raise NotImplementedError("Q8_G64 lm_head (tied / q4_k_m) is not supported by the runner")
+        H = mc.n_head
+        Hkv = mc.n_kv_head or H
+        hd = mc.n_embd // H
+        cfg = dict(n_layer=mc.n_layer, d_model=mc.n_embd, n_head=H, n_kv_head=Hkv, ffn=qw["hidden_dim"],
+                   vocab=mc.vocab_size, eps=mc.rms_norm_eps, theta=mc.rope_theta, rope_scaling=mc.rope_scaling,
+                   block_size=mc.block_size)
+        qkv_dim = (H + 2 * Hkv) * hd
+        layers = []
+        for i, b in enumerate(model.transformer.h):
+            def rl(p, s, n, gu=False):
+                return ops.q4t_from_marlin(p.to(dev), s.to(dev), n, gate_up=gu)
+            cb = qw["c_attn_b"][i]
+            layers.append(dict(
+                qkv=rl(qw["c_attn_p"][i], qw["c_attn_s"][i], qkv_dim), o=rl(qw["c_proj_p"][i], qw["c_proj_s"][i], mc.n_embd),
+                gu=rl(qw["gu_p"][i], qw["gu_s"][i], 2 * qw["hidden_dim"], True),
+                down=rl(qw["wd_p"][i], qw["wd_s"][i], mc.n_embd),
+                ln_1=b.ln_1.weight.detach().to(dev, torch.float32).contiguous(),
+                ln_2=b.ln_2.weight.detach().to(dev, torch.float32).contiguous(),
+                qkv_b=cb.to(dev, torch.float16) if cb.numel() > 0 else None))
+        packed = dict(layers=layers, emb_w=qw["wte_p"].to(dev), emb_s=qw["wte_sb"].to(dev),
+                      lm_head=ops.q4t_from_marlin(qw["lmh_p"].to(dev), qw["lmh_sb"].to(dev), mc.vocab_size),
+                      ln_f=model.transformer.ln_f.weight.detach().to(dev, torch.float32).contiguous())
+        return cls(cfg, packed, **kw)
+
+    # ------------------------------------------------------------ steps
+    @property
+    def weight_bytes(self) -> int:
+        p = self.packed
+        n = p["emb_w"].numel() * 0  # embedding rows are gathered, not streamed
+        n += p["lm_head"].nbytes
+        for x in p["layers"]:
+            n += x["qkv"].nbytes + x["o"].nbytes + x["gu"].nbytes + x["down"].nbytes
+        return n
+
+    def _step(self, B, T, rope_pos, write_pos, active_len, prefix_len, masks=None, depths=None):
+        st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        mp = dp = None
+        if masks is not None:
+            ma = (C.c_uint64 * T)(*[int(m) & 0xFFFFFFFFFFFFFFFF for m in masks])
+            da = (C.c_int32 * T)(*[int(x) for x in depths])
+            mp, dp = C.cast(ma, C.c_void_p), C.cast(da, C.c_void_p)
+        L.call("axb_runner_step", self._h, B, T, rope_pos, write_pos, active_len, prefix_len, mp, dp,
+               int(self.use_graph), st)
+        self._last_T = T
+
+    def _load_tokens(self, idx: torch.Tensor):
+        n = idx.numel()
+        self.tokens[:n].copy_(idx.reshape(-1).to(torch.int32), non_blocking=True)
+
+    def decode_step(self, idx: torch.Tensor) -> torch.Tensor:
+        """One T = 1 step for B sequences (idx (B, 1)); returns (B, 1, V) fp16
+        logits (a view of the runner's buffer, valid until the next step)."""
+        B = idx.shape[0]
+        seen = self.cache.total_seen_tokens[0]
+        wp, active, new_seen = self.cache.next_positions(1)
+        self._load_tokens(idx)
+        self._step(B, 1, seen % self.rope_len, wp, active, 0)
+        self.cache.advance(new_seen)
+        return self.logits_buf[:B].view(B, 1, -1)
+
+    def prefill(self, idx: torch.Tensor) -> torch.Tensor:
+        """T > 1 tokens per sequence, in chunks of max_tokens, each chunk a
+        causal chain over the cached prefix; returns last-token logits."""
+        B, T = idx.shape
+        seen = self.cache.total_seen_tokens[0]
+        if seen + T > self.cache.max_seq_len:
+            raise RuntimeError("prefill beyond the cache capacity (ring wrap during prefill is not supported)")
+        for t0 in range(0, T, self.max_tokens):
+            n = min(self.max_tokens, T - t0)
+            seen = self.cache.total_seen_tokens[0]
+            masks = [(1 << (u + 1)) - 1 for u in range(n)]
+            self._load_tokens(idx[:, t0:t0 + n].contiguous())
+            self._step(B, n, seen % self.rope_len, seen, seen + n, seen, masks, list(range(n)))
+            self.cache.advance(seen + n)
+        last = self.logits_buf[: B * n].view(B, n, -1)[:, -1:, :]
+        return last
+
+    def forward(self, idx: torch.Tensor, return_all_logits: bool = False) -> torch.Tensor:
+        idx = idx if idx.dim() == 2 else idx.view(1, -1)
+        if idx.shape[1] == 1:
+            return self.decode_step(idx)
+        out = self.prefill(idx)
+        return out
+
+    def forward_tree_verify(self, idx: torch.Tensor, tree_depths: list[int], tree_mask: list[int]) -> torch.Tensor:
+        """transformer.py:581-784 with uint64 masks (up to 64 nodes); K/V of the
+        nodes land at [seen, seen + T); the caller commits with
+        ``cache.compact_tree_path``.  Returns (B, T, V) fp16 logits."""
+        idx = idx if idx.dim() == 2 else idx.view(1, -1)
+        B, T = idx.shape
+        seen = self.cache.total_seen_tokens[0]
+        wp = (seen % self.cache.max_seq_len) if (self.cache.ring_buffer or seen >= self.cache.max_seq_len) else seen
+        if wp + T > self.cache.max_seq_len or seen != wp:
+            raise RuntimeError(f"tree verification needs contiguous tail capacity: write_pos={wp}, T={T}")
+        self._load_tokens(idx)
+        self._step(B, T, seen % self.rope_len, wp, seen + T, seen, tree_mask, tree_depths)
+        return self.logits_buf[: B * T].view(B, T, -1)
+
+    def get_last_norm(self, T: int | None = None) -> torch.Tensor:
+        """Final-norm hidden states (fp32) of the last tree/prefill step."""
+        T = T or self._last_T
+        return self.norm_buf[:T].view(1, T, -1)
+
+    def argmax(self, rows: int) -> torch.Tensor:
+        return self.argmax_buf[:rows]
+
+    @torch.no_grad()
+    def generate_greedy(self, prompt: torch.Tensor, n_new: int) -> list[int]:
+        prompt = prompt.to(self.device).view(1, -1)
+        logits = self.prefill(prompt)
+        T = prompt.shape[1] - (prompt.shape[1] - 1) // self.max_tokens * self.max_tokens
+        tok = self.argmax_buf[T - 1: T].clone()
+        out = [tok]
+        for _ in range(n_new - 1):
+            self.decode_step(tok.view(1, 1))
+            tok = self.argmax_buf[:1].clone()
+            out.append(tok)
+        return [int(t) for t in torch.cat(out).tolist()]
+
+    def close(self):
+        if getattr(self, "_h", None):
+            L.call("axb_runner_destroy", self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

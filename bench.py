@@ -1,0 +1,449 @@
+"""Decode throughput of the quantized hot path (BASELINE.json metric).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+                    [--batch B] [--ctx C] [--layers L]
+
+Workload (one GPU): Llama-3-8B-shaped decoder (32 layers,
+d 4096, 32/8 heads, head_dim 128, FFN 14336, vocab 128256), random N(0, 0.02)
+weights quantized Q4 group-128 symmetric (4.125 bits/weight), FP8-e4m3 KV
+cache with one fp16 scale per (token, head), a 4096-token context of random
+token ids prefilled through the same runner, batch 1 per GPU.  A step is one
+greedy decode step (embed -> 32 layers -> lm_head -> argmax) for every
+sequence.  Under torchrun each rank runs its own batch (replicas, weak
+scaling); the time is the max over ranks.
+
+``--impl reference`` times the reference algorithm's CPU path (the oracle
+restatement of ``_forward_quantized_sequence``: per-call dequant + F.linear,
+SDPA over the dequantized FP8 cache) on the host cores, on a bounded sample of
+the same step (one layer and 1/32 of the lm_head rows, scaled by 32).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG_8B = dict(n_layer=32, d_model=4096, n_head=32, n_kv_head=8, ffn=14336, vocab=128256, eps=1e-5, theta=10000.0,
+              block_size=8192)
+METRIC = "decode tokens/s (Q4 8B-shape, FP8 KV, ctx 4096)"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ------------------------------------------------------------------ distributed
+
+def dist_setup(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (the recipe's clocks line)."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 4:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+                bits = int(parts[3], 16)
+            except ValueError:
+                continue
+            for b, name in self.REASONS.items():
+                if bits & b and name != "gpu_idle":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ our arm
+
+def build_decoder(cfg, batch, ctx, kv, seed=0):
+    from axiomlm_b200 import ops
+    from axiomlm_b200.model import QuantizedDecoder
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    dev = torch.device("cuda")
+
+    def rn(*shape):
+        return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * 0.02
+
+    d, H, Hkv, F, V = cfg["d_model"], cfg["n_head"], cfg["n_kv_head"], cfg["ffn"], cfg["vocab"]
+    hd = d // H
+    layers = []
+    for _ in range(cfg["n_layer"]):
+        layers.append(dict(
+            qkv=ops.pack_q4t(rn((H + 2 * Hkv) * hd, d), 128, True), o=ops.pack_q4t(rn(d, H * hd), 128, True),
+            gu=ops.pack_q4t(rn(2 * F, d), 128, True, gate_up=True), down=ops.pack_q4t(rn(d, F), 128, True),
+            ln_1=torch.ones(d, device=dev), ln_2=torch.ones(d, device=dev), qkv_b=None))
+        torch.cuda.synchronize()
+    wte = rn(V, d)
+    emb_w, emb_s = ops.pack_q8_g64(wte)
+    del wte
+    lm = ops.pack_q4t(rn(V, d), 128, True)
+    packed = dict(layers=layers, emb_w=emb_w, emb_s=emb_s, lm_head=lm, ln_f=torch.ones(d, device=dev))
+    torch.cuda.synchronize()
+    kv_dtype, kv_group = kv
+    dec = QuantizedDecoder(cfg, packed, kv_dtype=kv_dtype, kv_group=kv_group, max_batch=batch,
+                           max_seq=ctx + 1024, max_tokens=1, rope_len=cfg["block_size"])
+    return dec
+
+
+def fill_context(dec, batch, ctx, seed=1):
+    """ctx random token ids per sequence, run through the decode graph."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    toks = torch.randint(0, dec.cfg["vocab"], (batch, ctx), generator=g, device="cuda")
+    for t in range(ctx):
+        dec.decode_step(toks[:, t:t + 1])
+    torch.cuda.synchronize()
+
+
+def step_bytes(dec, batch):
+    """Algorithmic HBM bytes of one decode step: every packed projection and
+    the lm_head once, the KV cache of every sequence over the active window
+    (codes + scales), the new K/V rows, embeddings rows; activations are
+    negligible and excluded."""
+    c = dec.cache
+    active = c.layer_seq_lens[0]
+    row = c.cache.shape[-1] * c.cache.element_size()
+    kv = c.n_layer * 2 * batch * c.n_kv_head * active * row
+    if c.scales is not None:
+        kv += c.n_layer * 2 * batch * c.n_kv_head * active * c.scales.shape[-1] * 2
+    emb = batch * dec.cfg["d_model"] * (1 + 2 / 64 * 2)
+    return dec.weight_bytes + kv + emb
+
+
+def gemv_roofline(dec, batch, reps=3):
+    """Time every projection GEMV of one step eagerly (same kernel, same
+    launch shape as in the graph) with CUDA events on the launching stream;
+    report algorithmic bytes per launch / mean launch time."""
+    from axiomlm_b200 import _lib as L
+    from axiomlm_b200 import ops
+
+    d, F = dec.cfg["d_model"], dec.cfg["ffn"]
+    st = torch.cuda.current_stream()
+    x_d = torch.randn(batch, d, device="cuda").half()
+    x_f = torch.randn(batch, F, device="cuda").half()
+    launches = []
+    for lay in dec.packed["layers"]:
+        launches += [(lay["qkv"], x_d, L.EPI_STORE), (lay["o"], x_d, L.EPI_STORE),
+                     (lay["gu"], x_d, L.EPI_SWIGLU), (lay["down"], x_f, L.EPI_STORE)]
+    launches.append((dec.packed["lm_head"], x_d, L.EPI_STORE))
+    tot_bytes = sum(W.nbytes + batch * W.K * 2 + batch * W.N * 2 for W, _, _ in launches)
+    for W, x, e in launches[:8]:  # warm-up
+        ops.qgemm(x, W, epilogue=e)
+    times = []
+    for _ in range(reps):
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record(st)
+        for W, x, e in launches:
+            ops.qgemm(x, W, epilogue=e)
+        ev1.record(st)
+        ev1.synchronize()
+        times.append(ev0.elapsed_time(ev1) / 1e3)
+    t = min(times)
+    per_launch_s = t / len(launches)
+    per_launch_bytes = tot_bytes / len(launches)
+    return per_launch_bytes, per_launch_s, len(launches)
+
+
+def run_ours(args, rank, world):
+    from axiomlm_b200 import _lib as L
+
+    L.load()
+    if L.load().axb_check_device() != 0:
+        raise SystemExit(L.load().axb_last_error().decode())
+    cfg = dict(CFG_8B)
+    if args.layers:
+        cfg["n_layer"] = args.layers
+    kv = {"fp8_head": ("fp8", 128), "fp8_g64": ("fp8", 64), "fp16": ("fp16", 64), "int4_g32": ("int4", 32)}[args.kv]
+    B = args.batch
+    dec = build_decoder(cfg, B, args.ctx, kv, seed=1000 + rank)
+    fill_context(dec, B, args.ctx, seed=2000 + rank)
+    st = torch.cuda.current_stream()
+    tok = dec.argmax(B).view(B, 1).long()
+    for _ in range(args.warmup):
+        dec.decode_step(tok)
+        tok = dec.argmax(B).view(B, 1).long()
+    torch.cuda.synchronize()
+    # ---- device-timed region: K greedy steps, inputs resident in HBM
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        ev0.record(st)
+        for _ in range(args.steps):
+            dec.decode_step(tok)
+            tok = dec.argmax(B).view(B, 1).long()  # next input stays on the device
+        ev1.record(st)
+        torch.cuda.synchronize()
+        barrier(world)
+    t = max_over_ranks(ev0.elapsed_time(ev1) / 1e3, world)
+    value = world * B * args.steps / t
+    sbytes = step_bytes(dec, B)
+    # ---- end to end through the public API, host buffers
+    host_in = torch.zeros((B, 1), dtype=torch.int64).pin_memory()
+    host_out = torch.zeros((B,), dtype=torch.int32).pin_memory()
+    host_in.copy_(tok.cpu())
+    dev_in = torch.empty((B, 1), dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        dev_in.copy_(host_in, non_blocking=True)
+        dec.decode_step(dev_in)
+        host_out.copy_(dec.argmax(B), non_blocking=True)
+        st.synchronize()
+        host_in[:, 0].copy_(host_out)
+    e1.record(st)
+    e1.synchronize()
+    barrier(world)
+    te = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
+    e2e = {"value": world * B * args.steps / te, "unit": "tokens/s", "h2d_bytes_per_step": B * 8,
+           "d2h_bytes_per_step": B * 4}
+    # ---- roofline of the dominant kernel (the Q4 GEMV)
+    pk, pk_kind = peaks()
+    bpl, spl, nl = gemv_roofline(dec, B)
+    achieved = bpl / spl / 1e9
+    out = None
+    if rank == 0:
+        launches_per_step = 2 + cfg["n_layer"] * 6 + 2 + 1  # set_params, embed, 6/layer, lm_head, argmax
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "w4a16 (fp32 accumulate)",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform-random token ids)",
+            "config": {"workload": f"Llama-3-8B-shape decode ({cfg['n_layer']} layers), Q4 G128 sym, "
+                                   f"KV {args.kv}, ctx {args.ctx}, batch {B}/GPU",
+                       "global_batch": B * world, "seq_len": args.ctx, "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (weights %.2f GB per step)" % (dec.weight_bytes / 1e9)},
+            "achieved_hbm_gbs": round(sbytes * B * args.steps / B / t / 1e9 / 1, 1) if world == 1 else None,
+            "step_bytes": int(sbytes),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                         "kernel": "qgemm_kernel<1,SYM,2,*> (Q4 G128 GEMV)", "launches_timed": nl,
+                         "bytes_per_launch": int(bpl), "peak_kind": f"{pk_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+            "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},
+            "clocks": clk.summary(), "gpu_launches": launches_per_step * args.steps,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline(cfg, B, args.ctx, kv, reps=1)
+    dec.close()
+    return out
+
+
+# ------------------------------------------------------------------ CPU (oracle) arm
+
+def _cpu_sample_fns(cfg, B, ctx, kv):
+    """Build the bounded CPU sample: one decoder layer of the step and 1/32 of
+    the lm_head rows, packed in the reference's MARLIN layout (random codes;
+    the dequant + F.linear cost does not depend on values)."""
+    import numpy as np
+
+    import oracle as O
+
+    d, H, Hkv, F, V = cfg["d_model"], cfg["n_head"], cfg["n_kv_head"], cfg["ffn"], cfg["vocab"]
+    hd = d // H
+    rng = np.random.default_rng(0)
+
+    def ladder(N, K):
+        nt = (N + 7) // 8
+        w = rng.integers(-2 ** 31, 2 ** 31 - 1, size=(nt, K // 64, 32, 2), dtype=np.int64).astype(np.int32)
+        sb = (rng.standard_normal((nt, K // 64, 8, 2)) * 0.01).astype(np.float16)
+        return torch.from_numpy(w), torch.from_numpy(sb)
+
+    mats = {"qkv": ladder((H + 2 * Hkv) * hd, d), "o": ladder(d, H * hd), "gu": ladder(2 * F, d),
+            "down": ladder(d, F), "lm": ladder(V // cfg["n_layer"], d)}
+    kvq = torch.from_numpy(rng.integers(0, 120, size=(B, Hkv, ctx, hd), dtype=np.uint8))
+    kvs = torch.from_numpy((rng.random((B, Hkv, ctx, hd // kv[1])) * 0.01).astype(np.float16))
+    x = torch.randn(B, 1, d).half()
+
+    def linear(name, inp, K, n):
+        w, sb = mats[name]
+        W = torch.from_numpy(O.dequant_q4_marlin(w.numpy(), sb.numpy(), K, n))  # quant.py:656-661, every call
+        return torch.nn.functional.linear(inp.half(), W)
+
+    def sample():
+        qkv = linear("qkv", x, d, (H + 2 * Hkv) * hd).float()
+        q = qkv[..., : H * hd].view(B, 1, H, hd).transpose(1, 2)
+        kd = torch.from_numpy(O.dequant_kv_fp8(kvq.numpy(), kvs.numpy(), kv[1])).float()
+        vd = torch.from_numpy(O.dequant_kv_fp8(kvq.numpy(), kvs.numpy(), kv[1])).float()
+        y = O.attention_decode(q, kd, vd, ctx).transpose(1, 2).reshape(B, 1, H * hd)
+        o = linear("o", y, H * hd, d)
+        gu = linear("gu", o, d, 2 * F).float()
+        sw = torch.nn.functional.silu(gu[..., :F]) * gu[..., F:]
+        linear("down", sw, F, d)
+        linear("lm", o, d, V // cfg["n_layer"])
+
+    return sample
+
+
+def cpu_baseline(cfg, B, ctx, kv, reps=1):
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample = _cpu_sample_fns(cfg, B, ctx, kv)
+    sample()  # warm
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        sample()
+        ts.append(time.perf_counter() - t0)
+    tok_s = B / (min(ts) * cfg["n_layer"])
+    return {"value": round(tok_s, 4), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"1 of {cfg['n_layer']} layers + 1/{cfg['n_layer']} of lm_head rows per step "
+                      f"(per-call dequant + F.linear, SDPA over the dequantized FP8 cache, ctx {ctx}), x{cfg['n_layer']}"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    cfg = dict(CFG_8B)
+    kv = {"fp8_head": ("fp8", 128), "fp8_g64": ("fp8", 64), "fp16": ("fp16", 64), "int4_g32": ("int4", 32)}[args.kv]
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample = _cpu_sample_fns(cfg, args.batch, args.ctx, kv)
+    for _ in range(args.warmup):
+        sample()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        sample()
+    t = (time.perf_counter() - t0) * cfg["n_layer"]
+    v = args.batch * args.steps / t
+    cb = {"value": round(v, 4), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+          "sample": f"per step: 1 of {cfg['n_layer']} layers + 1/{cfg['n_layer']} of lm_head rows, x{cfg['n_layer']}"}
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (CPU)",
+            "data": "synthetic", "config": {"workload": f"Llama-3-8B-shape decode, Q4 (reference MARLIN layout), "
+                                                        f"KV {args.kv}, ctx {args.ctx}, batch {args.batch}",
+                                            "global_batch": args.batch, "seq_len": args.ctx,
+                                            "parallelism": "CPU, rank 0 only"},
+            "cpu_baseline": cb, "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--kv", default="fp8_head", choices=["fp8_head", "fp8_g64", "fp16", "int4_g32"])
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (debug only)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 200 if args.impl == "ours" else 5
+    if args.warmup is None:
+        args.warmup = 10 if args.impl == "ours" else 3
+    args.warmup = max(args.warmup, 3)
+    rank, world = dist_setup(args.gpus)
+    if args.impl == "reference":
+        out = run_reference(args, rank, world)
+    else:
+        out = run_ours(args, rank, world)
+    if rank == 0 and out is not None:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

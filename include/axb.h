@@ -1,0 +1,262 @@
+/*
+ * AxiomLM-B200: C ABI of the quantized decode hot path (libaxb.so).
+ *
+ * Plain pointers and sizes only.  Every pointer argument named *_dev is CUDA
+ * device memory on the current device; `stream` is a cudaStream_t passed as
+ * void*.  Every entry point returns an int status (AXB_OK == 0, negative on
+ * error; axb_last_error() has the message) and never allocates device memory
+ * in a steady-state call: scratch space ("workspace") is passed in by the
+ * caller, sized by the matching *_workspace_bytes() function and zero-filled
+ * once before first use (the kernels leave it zeroed again).
+ *
+ * Each entry point names the reference interface it replaces (paths inside
+ * the AxiomLM project).  Those reference functions are PyTorch/Metal; the host
+ * mirror in axiomlm_b200/ops.py keeps their Python names and argument meaning
+ * and calls these.
+ */
+#ifndef AXB_H
+#define AXB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status ---------------------------------------------------------------- */
+#define AXB_OK 0
+#define AXB_EINVAL (-1)       /* bad argument / shape / unsupported combination */
+#define AXB_ECUDA (-2)        /* a CUDA runtime call or launch failed */
+#define AXB_EUNSUPPORTED (-3) /* device is not sm_100 */
+#define AXB_ETIMEOUT (-4)     /* a bounded device-side wait ran out */
+
+/* ---- formats ----------------------------------------------------------------- */
+/* Projection weights: q4t = 16-row tiles of mma A-fragments, 64207531 nibble
+ * interleave.  SYM: w = (q - 8) * s; AFFINE: w = q * s + b. */
+#define AXB_W_Q4T_SYM 1
+#define AXB_W_Q4T_AFFINE 2
+#define AXB_W_Q8_G64 3 /* reference Q8_G64 row-major (quant.py:72) */
+
+/* KV cache element types (StaticKVCache cache_dtype, paged_cache.py:122) */
+#define AXB_KV_F16 0
+#define AXB_KV_FP8 1  /* e4m3fn + one fp16 scale per kv_group elements */
+#define AXB_KV_INT4 2 /* symmetric int4, 2 per byte, low nibble = even element */
+
+/* GEMV epilogues */
+#define AXB_EPI_STORE 0    /* y = fp16(acc [+ bias]) */
+#define AXB_EPI_RESIDUAL 1 /* y = fp16(y + fp16(acc)) in place (x = x + proj(..)) */
+#define AXB_EPI_SWIGLU 2   /* rows interleaved gate/up by 8: y[j] = fp16(silu(g) * u) */
+#define AXB_EPI_F32 3      /* y (fp32) = fp16-rounded acc, stored as fp32 */
+
+const char* axb_last_error(void);
+int axb_version(void);
+/* 0 when the current device is sm_100 (B200), AXB_EUNSUPPORTED otherwise */
+int axb_check_device(void);
+
+/* ---- weight packing / relayout / dequant -------------------------------- */
+
+/* Bytes of the q4t words / scales arrays for an (N, K) matrix. */
+size_t axb_q4t_words_bytes(int N, int K);
+size_t axb_q4t_scales_bytes(int N, int K, int group, int fmt);
+
+/* Round-to-nearest pack of fp32 (N, K) row-major weights into q4t.
+ * fmt AXB_W_Q4T_AFFINE reproduces pack_linear_q4_marlin(clip_search=False)
+ * values (quant.py:475-486) at any group; AXB_W_Q4T_SYM is the BASELINE
+ * group-128 symmetric form.  `gate_up_interleave`: rows are [gate(F); up(F)]
+ * and are stored interleaved by 8 for the SwiGLU epilogue. */
+int axb_q4t_pack(const float* w_dev, int N, int K, int group, int fmt, int gate_up_interleave,
+                 void* words_dev, void* scales_dev, void* stream);
+
+/* Relayout reference MARLIN-ladder Q4 (w_marlin int32 (Nt8, K/64, 32, 2),
+ * sb_marlin fp16 (Nt8, K/64, 8, 2); quant.py:447-594) into q4t affine G64.
+ * Bit-exact on codes, scales and biases. */
+int axb_q4t_from_marlin(const int32_t* w_marlin_dev, const uint16_t* sb_marlin_dev, int n_tiles8, int K,
+                        int n_out, int gate_up_interleave, void* words_dev, void* scales_dev, void* stream);
+
+/* fp16 (N, K) dequant of q4t (replaces dequantize_q4_marlin, quant.py:597,
+ * on the relaid-out form: identical values). */
+int axb_q4t_dequant(const void* words_dev, const void* scales_dev, int N, int K, int group, int fmt,
+                    int gate_up_interleave, uint16_t* out_dev, void* stream);
+
+/* Direct dequant of the reference ladder layout (quant.py:597-634). */
+int axb_q4_marlin_dequant(const int32_t* w_marlin_dev, const uint16_t* sb_marlin_dev, int n_tiles8, int K,
+                          int n_out, uint16_t* out_dev, void* stream);
+
+/* pack_linear_q8_g64 (quant.py:72-129): RTN Q8 G64 of fp32 (N, K) weights into
+ * (N, K/4) int32 + (N, K/64, 2) fp16 (scale, bias) */
+int axb_q8_pack(const float* w_dev, int N, int K, int32_t* out_dev, uint16_t* sb_dev, void* stream);
+
+/* dequant_q8_rows (quant.py:132-163): out[i] = fp16(q * s + b) of row idx[i] */
+int axb_q8_rows(const int32_t* w_dev, const uint16_t* sb_dev, const int32_t* idx_dev, int n_idx, int K,
+                uint16_t* out_dev, void* stream);
+
+/* dequantize_ternary (quant.py:277-295) and dequantize_q2_k (quant.py:383-403) */
+int axb_ternary_dequant(const uint8_t* w_dev, const uint16_t* s_dev, int N, int K, int per_tensor,
+                        uint16_t* out_dev, void* stream);
+int axb_q2_dequant(const uint8_t* w_dev, const uint16_t* sb_dev, int N, int K, uint16_t* out_dev, void* stream);
+
+/* ---- quantized GEMV / small-M GEMM (qmv_q4_marlin / qmm_q4_marlin,
+ *      quant.py:637-684; Metal qmv_q4_marlin_apple_kernel) ------------------- */
+typedef struct {
+  int fmt;            /* AXB_W_Q4T_SYM | AXB_W_Q4T_AFFINE */
+  int group;          /* 64 | 128 */
+  const void* words;  /* q4t words */
+  const void* scales; /* q4t scales */
+  int N, K, M;        /* y[M, N] = x[M, K] W^T ; M <= 64 */
+  const void* x;      /* fp16 (M, ldx) */
+  int ldx;
+  void* y; /* fp16 (M, ldy) or fp32 for AXB_EPI_F32 */
+  int ldy;
+  const void* bias;     /* fp16 (N) or NULL */
+  const float* norm_w;  /* if non-NULL: B operand = fp16(rmsnorm(x) * norm_w) (fp32 math) */
+  float eps;
+  int epilogue;         /* AXB_EPI_* */
+  int gate_up_interleave;
+  void* workspace; /* >= axb_qgemm_workspace_bytes(...), zeroed once */
+  size_t workspace_bytes;
+  int pdl; /* launch with programmatic dependent launch */
+} axb_qgemm_desc;
+
+size_t axb_qgemm_workspace_bytes(int N, int K, int M, int group);
+int axb_qgemm(const axb_qgemm_desc* d, void* stream);
+/* Synchronizes `stream`; returns AXB_ETIMEOUT (and clears the flag) if a
+ * bounded weight-stream wait in an earlier axb_qgemm on this workspace ran out. */
+int axb_qgemm_status(void* workspace, void* stream);
+
+/* ---- RMSNorm (modules.py:30-43) ---------------------------------------- */
+/* out fp16 (M, K) = fp16(fp32(x) * rsqrt(mean(x^2) + eps) * w) */
+int axb_rmsnorm(const uint16_t* x_dev, const float* w_dev, int M, int K, float eps, uint16_t* out_dev,
+                void* stream);
+
+/* ---- KV write with RoPE (rope_kv_cache_write_quantized, quant.py:896-1008;
+ *      StaticKVCache.update, paged_cache.py:218-361) --------------------------- */
+typedef struct {
+  int kv_type;  /* AXB_KV_* */
+  int kv_group; /* elements per fp16 scale (64 ref, head_dim, 32) */
+  int B, T;     /* sequences, new tokens per sequence */
+  int n_head, n_kv_head, head_dim;
+  int max_seq;           /* cache S */
+  int max_batch;         /* cache batch capacity (stride) */
+  const uint16_t* qkv;   /* fp16 (B*T, (Hq + 2*Hkv) * hd) GEMV output */
+  const uint16_t* bias;  /* optional fp16 qkv bias or NULL */
+  const float* rope;     /* (rope_len, hd/2, 2) fp32 = view_as_real(freqs_cis) */
+  int rope_len;
+  int rope_pos;          /* position of token 0 */
+  const int* depths;     /* optional per-token offsets (tree verify) or NULL: offset = t */
+  int write_pos;         /* slot of token 0 (slot t = (write_pos + t) % S) */
+  float* q_out;          /* fp32 (B*T, Hq*hd): rotated queries (kept fp32, as the reference) */
+  const int32_t* dev_params; /* optional device [rope_pos, write_pos, active_len, prefix_len]
+                                overriding the scalar fields (CUDA-graph replay) */
+  void* k_cache;         /* (max_batch, Hkv, S, row) */
+  void* v_cache;
+  uint16_t* k_scale;     /* (max_batch, Hkv, S, hd/kv_group) fp16, or NULL for F16 */
+  uint16_t* v_scale;
+  int k_is_fp32;         /* quantize K from fp32 (model path) instead of fp16 (op path) */
+} axb_kv_write_desc;
+int axb_rope_kv_write(const axb_kv_write_desc* d, void* stream);
+
+/* Quantize fp16/fp32 (rows, hd) into the cache formats (quantize_kv_fp8 /
+ * quantize_kv_int4, quant.py:692-807). */
+int axb_kv_quantize(const void* x_dev, int x_is_fp32, int rows, int head_dim, int kv_type, int kv_group,
+                    void* q_dev, uint16_t* scale_dev, void* stream);
+/* dequantize_kv_fp8 / dequantize_kv_int4 (quant.py:727-852) */
+int axb_kv_dequantize(const void* q_dev, const uint16_t* scale_dev, int rows, int head_dim, int kv_type,
+                      int kv_group, uint16_t* out_dev, void* stream);
+
+/* ---- attention (gqa_flash_decode_mps ops.py:552, gqa_tree_verify_mps
+ *      ops.py:657; Metal gqa_flash_decode_split_kv_*_kernel) -------------- */
+typedef struct {
+  int kv_type, kv_group;
+  int B, n_head, n_kv_head, head_dim, max_seq, max_batch;
+  const void* q; /* fp32 or fp16 (B*T, Hq*hd) */
+  int q_is_fp32;
+  const void* k_cache;
+  const void* v_cache;
+  const uint16_t* k_scale;
+  const uint16_t* v_scale;
+  void* out; /* fp16 (B*T, Hq*hd) */
+  /* decode (T == 1): all slots [0, active_len) are visible */
+  int active_len;
+  int num_splits; /* 0 = auto */
+  /* tree (T >= 1): slots [0, prefix_len) plus tree slot write_pos + j when
+   * bit j of masks[t] is set */
+  int T;
+  int prefix_len;
+  int write_pos;
+  const uint64_t* masks; /* device, T entries; NULL = decode mode */
+  const int32_t* dev_params; /* optional device [rope_pos, write_pos, active_len, prefix_len] */
+  void* workspace;
+  size_t workspace_bytes;
+  int pdl;
+} axb_attn_desc;
+size_t axb_attn_workspace_bytes(int B, int n_head, int head_dim, int T, int max_splits);
+int axb_attention(const axb_attn_desc* d, void* stream);
+
+/* compact_tree_path (paged_cache.py:376-462): move accepted tree slots
+ * (write_pos + acc[m]) % S -> (write_pos + m) % S across all layers. */
+int axb_compact_kv(void* cache_dev, uint16_t* scales_dev, int n_layer, int max_batch, int n_kv_head,
+                   int max_seq, int row_bytes, int n_groups, int write_pos, const int32_t* accepted_dev,
+                   int n_accepted, void* stream);
+
+/* Greedy argmax over rows (ties -> lowest index, torch.argmax). */
+int axb_argmax(const uint16_t* x_dev, int rows, int n, int ld, int32_t* out_dev, void* stream);
+
+/* ---- whole-model decode runner (replaces MPSQuantizedDecodeRunner,
+ *      mps_kernels.mm:2982-3737; Transformer.forward T=1 fast path,
+ *      transformer.py:1438-1473, forward_tree_verify transformer.py:581) ---- */
+typedef struct {
+  int n_layer, d_model, n_head, n_kv_head, head_dim, ffn, vocab;
+  float eps;
+  int wfmt, group;       /* projection format (AXB_W_Q4T_*) */
+  int lm_fmt, lm_group;  /* lm_head: AXB_W_Q4T_* or AXB_W_Q8_G64 (tied) */
+  int kv_type, kv_group; /* cache format */
+  int max_batch, max_seq, max_tokens; /* max_tokens = tokens per sequence per step (<= 64) */
+  int rope_len;
+  int has_qkv_bias;
+} axb_model_cfg;
+
+typedef struct {
+  const void* emb_w;  /* Q8_G64 (V, d/4) int32 */
+  const void* emb_s;  /* (V, d/64, 2) fp16 */
+  const void* lm_w;
+  const void* lm_s;
+  const float* ln_f;
+  const float* rope; /* (rope_len, hd/2, 2) fp32 */
+  const void* const* qkv_w;
+  const void* const* qkv_s;
+  const void* const* qkv_b; /* may be NULL or entries NULL */
+  const void* const* o_w;
+  const void* const* o_s;
+  const void* const* gu_w; /* gate/up interleaved by 8 */
+  const void* const* gu_s;
+  const void* const* dn_w;
+  const void* const* dn_s;
+  const float* const* ln1;
+  const float* const* ln2;
+  void* const* k_cache; /* per layer (max_batch, Hkv, S, row) */
+  void* const* v_cache;
+  void* const* k_scale; /* per layer fp16 or NULL */
+  void* const* v_scale;
+} axb_model_ptrs;
+
+size_t axb_runner_workspace_bytes(const axb_model_cfg* cfg);
+/* workspace: zeroed device memory of the size above, owned by the caller */
+int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* ptrs, void* workspace_dev,
+                      size_t workspace_bytes, void** handle_out);
+int axb_runner_destroy(void* handle);
+/* Offsets (bytes, into the workspace) of the runner's I/O buffers:
+ * which = 0 tokens int32 (max_batch*max_tokens), 1 logits fp16 (rows, vocab),
+ * 2 argmax int32 (rows), 3 final-norm hidden fp32 (rows, d), 4 error word int32
+ * (non-zero after a step that met an out-of-vocabulary token id) */
+int axb_runner_buffer(void* handle, int which, size_t* offset_out, size_t* bytes_out);
+/* One forward step over B sequences x T new tokens already placed in the
+ * token buffer.  T == 1 and masks == NULL: decode (all active slots visible).
+ * Otherwise tree/chunk mode: masks[t] / depths[t] host arrays of length T. */
+int axb_runner_step(void* handle, int B, int T, int rope_pos, int write_pos, int active_len, int prefix_len,
+                    const uint64_t* masks_host, const int32_t* depths_host, int use_graph, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AXB_H */

@@ -503,54 +503,76 @@ def _q4t_unpack_codes(words: np.ndarray) -> np.ndarray:
     return qb.transpose(0, 2, 1, 3).reshape(nt * 16, kb * 64)
 
 
-def q4t_pack(w, group: int = 128, symmetric: bool = True):
-    """Quantize (N, K) fp32 weights into the q4t layout.
+def _gu_rows(npad: int, N: int, gu: bool) -> np.ndarray:
+    """packed row -> source row (N = padding) for the gate/up interleave:
+    tile t holds gate rows 8t..8t+7 then up rows F+8t..F+8t+7."""
+    p = np.arange(npad)
+    if not gu:
+        return np.where(p < N, p, N)
+    F = N // 2
+    j = (p >> 4) * 8 + (p & 7)
+    src = np.where((p >> 3) & 1, F + j, j)
+    return np.where(j < F, src, N)
 
-    symmetric: ``s = fp16(absmax / 7)`` (clamped at 1e-8 before the cast),
-    ``q = clip(rint(w / s), -8, 7) + 8``; dequant ``fp16((q - 8) * s)``.
+
+def q4t_pack(w, group: int = 128, symmetric: bool = True, gate_up: bool = False):
+    """Quantize (N, K) fp32 weights into the q4t layout (RTN).
+
+    symmetric: ``s = fp16(max(absmax, 1e-8) / 7)``, ``q = clip(rint(w / s),
+    -8, 7) + 8`` (q = 8 where s rounds to 0); dequant ``fp16((q - 8) * s)``.
     affine: the reference's RTN min/max rule (quant.py:475-486) at ``group``.
+    Scales: symmetric (tiles, K/G, 8, 2) = (s[g], s[g+8]); affine
+    (tiles, K/G, 8, 4) = (s[g], b[g], s[g+8], b[g+8]).
     """
     w = _f32(_to_np(w))
     N, K = w.shape
     assert K % 64 == 0 and K % group == 0
     nt = (N + 15) // 16
-    wp = np.zeros((nt * 16, K), np.float32)
-    wp[:N] = w
+    src = _gu_rows(nt * 16, N, gate_up)
+    wp = np.concatenate([w, np.zeros((1, K), np.float32)], 0)[src]
     wg = wp.reshape(nt * 16, K // group, group)
     if symmetric:
         amax = np.abs(wg).max(-1)
         s = (np.maximum(amax, np.float32(1e-8)) / np.float32(7.0)).astype(np.float16)
-        q = np.clip(np.rint(wg / s[..., None].astype(np.float32)), -8, 7).astype(np.int32) + 8
-        sc = s.reshape(nt, 16, K // group).transpose(0, 2, 1)
+        sf = s[..., None].astype(np.float32)
+        with np.errstate(divide="ignore", invalid="ignore"):
+            q = np.clip(np.rint(wg / sf), -8, 7)
+        q = np.where(sf == 0, 0, q).astype(np.int32) + 8
+        sc = s.reshape(nt, 2, 8, K // group).transpose(0, 3, 2, 1)  # (nt, grp, 8, [g, g+8])
     else:
         q, s, b = _rtn_affine(wg, 15.0)
-        sc = np.stack([s, b], -1).reshape(nt, 16, K // group, 2).transpose(0, 2, 1, 3)
+        sb = np.stack([s, b], -1).reshape(nt, 2, 8, K // group, 2)  # (nt, h, g, grp, 2)
+        sc = sb.transpose(0, 3, 2, 1, 4).reshape(nt, K // group, 8, 4)
     words = _q4t_pack_codes(q.reshape(nt * 16, K))
     return words.view(np.int32), np.ascontiguousarray(sc.astype(np.float16))
 
 
-def q4t_dequant(words, scales, K: int, group: int, symmetric: bool, out_features: int | None = None):
+def q4t_dequant(words, scales, K: int, group: int, symmetric: bool, out_features: int | None = None,
+                gate_up: bool = False):
+    """Inverse of ``q4t_pack``: fp16 (N, K) in the source row order."""
     q = _q4t_unpack_codes(words).astype(np.float32)
     npad = q.shape[0]
-    s = _to_np(scales).astype(np.float32)
     nt = npad // 16
+    s = _to_np(scales).astype(np.float32)
     qg = q.reshape(npad, K // group, group)
     if symmetric:
-        sc = s.transpose(0, 2, 1).reshape(npad, K // group)
+        sc = s.transpose(0, 3, 2, 1).reshape(npad, K // group)  # (nt, h, g, grp)
         w = ((qg - 8.0) * sc[..., None]).astype(np.float16).reshape(npad, K)
     else:
-        sc = s.transpose(0, 2, 1, 3).reshape(npad, K // group, 2)
-        w = (qg * sc[..., 0:1] + sc[..., 1:2]).astype(np.float16).reshape(npad, K)
-    return w[:out_features] if out_features is not None else w
+        sb = s.reshape(nt, K // group, 8, 2, 2).transpose(0, 3, 2, 1, 4).reshape(npad, K // group, 2)
+        w = (qg * sb[..., 0:1] + sb[..., 1:2]).astype(np.float16).reshape(npad, K)
+    N = out_features if out_features is not None else npad
+    src = _gu_rows(npad, N, gate_up)
+    out = np.zeros((N, K), np.float16)
+    ok = src < N
+    out[src[ok]] = w[ok]
+    return out
 
 
-def q4t_from_marlin(w_marlin, sb_marlin, n_out: int | None = None):
+def q4t_from_marlin(w_marlin, sb_marlin, n_out: int | None = None, gate_up: bool = False):
     """Relayout reference ladder Q4 (G64 affine) into q4t affine G64.
 
-    Bit-exact on values: the same codes, scales and biases, only moved.
-    Rows beyond the 8-row padding of the ladder format are zero codes with
-    zero scale/bias.
-    """
+    Bit-exact on values: the same codes, scales and biases, only moved."""
     q = _marlin_unlayout(w_marlin)  # (nt8*8, kg, 64)
     sb = _to_np(sb_marlin)
     nt8, kg = sb.shape[:2]
@@ -558,13 +580,13 @@ def q4t_from_marlin(w_marlin, sb_marlin, n_out: int | None = None):
     sbr = sb.transpose(0, 2, 1, 3).reshape(n8, kg, 2)
     N = n_out if n_out is not None else n8
     nt = (N + 15) // 16
-    qq = np.zeros((nt * 16, kg * 64), np.int32)
-    ss = np.zeros((nt * 16, kg, 2), np.float16)
-    m = min(N, n8)
-    qq[:m] = q.reshape(n8, kg * 64)[:m]
-    ss[:m] = sbr[:m]
+    src = _gu_rows(nt * 16, N, gate_up)
+    qz = np.concatenate([q.reshape(n8, kg * 64)[:N], np.zeros((1, kg * 64), np.int32)], 0)
+    sz = np.concatenate([sbr[:N], np.zeros((1, kg, 2), np.float16)], 0)
+    qq = qz[np.minimum(src, N)]
+    ss = sz[np.minimum(src, N)]
     words = _q4t_pack_codes(qq)
-    sc = ss.reshape(nt, 16, kg, 2).transpose(0, 2, 1, 3)
+    sc = ss.reshape(nt, 2, 8, kg, 2).transpose(0, 3, 2, 1, 4).reshape(nt, kg, 8, 4)
     return words.view(np.int32), np.ascontiguousarray(sc)
 
 

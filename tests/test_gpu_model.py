@@ -1,0 +1,83 @@
+"""Whole-model parity: the CUDA-graph runner against the reference's own
+greedy decode (fixtures from tests/golden/make_golden.py).
+
+Greedy token ids must be identical step for step; logits within rel 2e-3 of
+the reference's (fp16-valued) logits.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from model_weights import SMALL, TINY, make_weights
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 2e-3
+
+
+def _fx(name):
+    return np.load(os.path.join(GOLDEN, f"{name}.npz"))
+
+
+def _rel(a, b):
+    a = torch.as_tensor(a).float().cpu()
+    b = torch.as_tensor(b).float().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp(min=1e-6))
+
+
+def _decoder(cfg, fx, kv, **kw):
+    from axiomlm_b200.model import QuantizedDecoder
+
+    W = make_weights(cfg, int(fx["seed"]), ln_random=bool(fx["ln_random"]), tied=bool(fx["tied"]))
+    return QuantizedDecoder.from_weights(cfg, W, "q4_rtn", kv_dtype=kv, max_seq=int(fx["max_seq"]),
+                                         ring_buffer=bool(fx["ring"]), rope_len=cfg["block_size"], **kw)
+
+
+def _greedy_with_logits(dec, prompt, n):
+    logits = dec.prefill(torch.as_tensor(prompt).cuda())
+    steps = [logits[0, -1].float().cpu()]
+    toks = [int(torch.argmax(steps[-1]))]
+    for _ in range(n - 1):
+        lg = dec.decode_step(torch.tensor([[toks[-1]]], device="cuda"))
+        steps.append(lg[0, -1].float().cpu())
+        toks.append(int(torch.argmax(steps[-1])))
+    return toks, torch.stack(steps)
+
+
+@pytest.mark.parametrize("name,kv", [("small_fp16", "fp16"), ("small_fp8", "fp8"), ("small_int4", "int4"),
+                                     ("small_fp8_ring", "fp8")])
+@pytest.mark.parametrize("graph", [True, False])
+def test_small_model_greedy_parity(name, kv, graph):
+    fx = _fx(name)
+    dec = _decoder(SMALL, fx, kv, use_graph=graph)
+    toks, logits = _greedy_with_logits(dec, fx["prompt"], len(fx["tokens"]))
+    assert toks == fx["tokens"].tolist()
+    for i in range(len(toks)):
+        assert _rel(logits[i], fx["logits"][i]) < REL_TOL, i
+    # the runner's in-graph argmax agrees with the host argmax
+    assert int(dec.argmax(1)[0]) == toks[-1]
+    if "tree_logits" in fx.files:
+        tl = dec.forward_tree_verify(torch.as_tensor(fx["tree_tokens"]).cuda(), fx["tree_depths"].tolist(),
+                                     fx["tree_mask"].tolist())
+        assert _rel(tl[0], fx["tree_logits"]) < REL_TOL
+        ref_pred = torch.as_tensor(fx["tree_logits"]).argmax(-1)
+        assert torch.equal(tl[0].float().cpu().argmax(-1), ref_pred)
+    dec.close()
+
+
+@pytest.mark.parametrize("kv", ["fp16", "fp8"])
+def test_tiny_config_128_greedy_tokens(kv):
+    """12L/768d/12H, vocab 32000, prompt 128, 128 greedy tokens."""
+    fx = _fx(f"tiny_{kv}")
+    dec = _decoder(TINY, fx, kv)
+    toks, _ = _greedy_with_logits(dec, fx["prompt"], len(fx["tokens"]))
+    ref = fx["tokens"].tolist()
+    if toks != ref:
+        i = next(j for j in range(len(ref)) if toks[j] != ref[j])
+        pytest.fail(f"first divergence at step {i}: ours {toks[i]} ref {ref[i]}; reference top-2 margin "
+                    f"there {fx['margin'][i]:.2e}")
+    dec.close()
