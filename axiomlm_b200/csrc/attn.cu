@@ -568,11 +568,15 @@ int decode_max_splits(int B, int n_kv_head) {
   return std::max(1, std::min(64, want));
 }
 
+// Workspace: [combine counters | kAttnCounters ints][m, l partials][O partials].
+// The counters sit at a fixed offset for every (B, heads, splits), so one
+// zeroed workspace serves any call; the combining CTA returns each to zero.
+constexpr size_t kAttnCounters = 1 << 16;
+
 size_t attn_workspace(int B, int n_head, int head_dim, int max_splits) {
   size_t o = (size_t)B * n_head * max_splits * head_dim * 4;
   size_t ml = (size_t)B * n_head * max_splits * 2 * 4;
-  size_t cnt = (size_t)B * n_head * 4;
-  return round_up(o, 256) + round_up(ml, 256) + round_up(cnt, 256);
+  return kAttnCounters * 4 + round_up(ml, 256) + round_up(o, 256);
 }
 
 int rope_kv_write(const axb_kv_write_desc* d, cudaStream_t s, bool pdl) {
@@ -607,12 +611,12 @@ int attention(const axb_attn_desc* d, cudaStream_t s) {
     int ms = d->num_splits > 0 ? std::min(64, d->num_splits) : decode_max_splits(d->B, d->n_kv_head);
     AXB_CHECK_ARG(d->workspace && d->workspace_bytes >= attn_workspace(d->B, d->n_head, d->head_dim, ms),
                   "attention: workspace too small");
+    AXB_CHECK_ARG((size_t)d->B * d->n_kv_head <= kAttnCounters, "attention: too many sequences x heads");
     char* ws = reinterpret_cast<char*>(d->workspace);
-    float* po = reinterpret_cast<float*>(ws);
-    size_t o_b = round_up((size_t)d->B * d->n_head * ms * d->head_dim * 4, 256);
-    float* pml = reinterpret_cast<float*>(ws + o_b);
+    int* cnt = reinterpret_cast<int*>(ws);
+    float* pml = reinterpret_cast<float*>(ws + kAttnCounters * 4);
     size_t ml_b = round_up((size_t)d->B * d->n_head * ms * 2 * 4, 256);
-    int* cnt = reinterpret_cast<int*>(ws + o_b + ml_b);
+    float* po = reinterpret_cast<float*>(ws + kAttnCounters * 4 + ml_b);
     dim3 grid(ms, d->n_kv_head, d->B);
     cudaError_t e;
     if (d->head_dim == 128)

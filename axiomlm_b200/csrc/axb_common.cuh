@@ -132,8 +132,26 @@ __device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t two) {
   __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two), __NV_E4M3);
   return __half22float2(*reinterpret_cast<__half2*>(&h));
 }
+// float -> e4m3fn byte with round-half-even and no saturation: magnitudes
+// above 464 (that would round to 480) and NaN/inf encode as NaN (0x7F | sign),
+// the rule of torch's Tensor.to(float8_e4m3fn) used by the reference.
 __device__ __forceinline__ uint8_t float_to_e4m3(float f) {
-  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(f, __NV_SATFINITE, __NV_E4M3));
+  const uint32_t bits = __float_as_uint(f);
+  const uint32_t sign = (bits >> 24) & 0x80u;
+  const float a = fabsf(f);
+  if (!(a < 480.0f)) return (uint8_t)(sign | 0x7Fu);  // NaN, inf, >= 480
+  if (a < 0.015625f) {                                  // subnormal range: quantum 2^-9
+    return (uint8_t)(sign | (uint32_t)rintf(a * 512.0f));  // 0..8 (8 == min normal)
+  }
+  int e = (int)((__float_as_uint(a) >> 23) & 0xFF) - 127;  // [-6, 8]
+  float m = rintf(ldexpf(a, 3 - e));                         // [8, 16]
+  if (m >= 16.0f) {
+    m = 8.0f;
+    ++e;
+  }
+  uint32_t code = ((uint32_t)(e + 7) << 3) | ((uint32_t)m - 8u);
+  if (code > 0x7Fu) code = 0x7Fu;
+  return (uint8_t)(sign | code);
 }
 
 // Reference SiLU on fp32: x / (1 + exp(-x)).

@@ -653,12 +653,17 @@ int qgemm_prepare() {
   return AXB_OK;
 }
 
+// Workspace: [error word | 256 B][tile counters | kMaxTiles ints][partials].
+// Every region sits at a fixed offset, so one zeroed workspace serves calls of
+// any N and M: counters are only ever touched by the arrival logic, which
+// returns each one to zero.
+constexpr size_t kMaxTiles = 1 << 17;
+constexpr size_t kCountersOff = 256;
+constexpr size_t kPartialsOff = kCountersOff + kMaxTiles * 4;
+
 size_t qgemm_workspace(int N, int M) {
-  int n_tiles = (N + 15) / 16;
-  size_t head = 256;  // error word
-  size_t counters = round_up((size_t)n_tiles * 4, 256);
-  size_t partials = (size_t)2 * max_warps() * 32 * 4 * nt_for(M) * sizeof(float);
-  return head + counters + partials;
+  (void)N;
+  return kPartialsOff + (size_t)2 * max_warps() * 32 * 4 * nt_for(M) * sizeof(float);
 }
 
 int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
@@ -697,10 +702,11 @@ int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
   ga.bias = reinterpret_cast<const __half*>(d->bias);
   ga.epi = d->epilogue;
   ga.gu = d->gate_up_interleave;
+  AXB_CHECK_ARG((size_t)n_tiles <= kMaxTiles, "qgemm: N too large (%d rows)", d->N);
   char* ws = reinterpret_cast<char*>(d->workspace);
   ga.err = reinterpret_cast<int*>(ws);
-  ga.counters = reinterpret_cast<int*>(ws + 256);
-  ga.partials = reinterpret_cast<float*>(ws + 256 + round_up((size_t)n_tiles * 4, 256));
+  ga.counters = reinterpret_cast<int*>(ws + kCountersOff);
+  ga.partials = reinterpret_cast<float*>(ws + kPartialsOff);
   // grid: persistent, every warp owns >= 1 quantization group
   long long wt = std::min<long long>(max_warps(), ga.U);
   int threads = kWarpsPerCta * 32;

@@ -16,7 +16,14 @@ from model_weights import SMALL, TINY, make_weights
 
 pytestmark = pytest.mark.gpu
 
-REL_TOL = 2e-3
+# logits vs the reference's fp16-valued logits, relative to the max |logit|.
+# FP8/INT4 KV quantize K/V to 3-bit / 4-bit mantissas: a last-ulp difference
+# in an fp32 K value (GEMV summation order) can move a code by a whole step,
+# so the end-to-end bound there is looser than the layer-level 2e-3.
+REL_TOL = {"fp16": 2e-3, "fp8": 1.5e-2, "int4": 3e-2}
+# a reference step whose top-2 relative margin is below this is a near-tie
+# (one fixture step is an exact fp16 tie): either of the two tokens is accepted
+TIE = 2e-3
 
 
 def _fx(name):
@@ -37,15 +44,31 @@ def _decoder(cfg, fx, kv, **kw):
                                          ring_buffer=bool(fx["ring"]), rope_len=cfg["block_size"], **kw)
 
 
-def _greedy_with_logits(dec, prompt, n):
+def _greedy_with_logits(dec, prompt, n, forced=None):
+    """Greedy decode; with ``forced`` (the reference tokens) the next input is
+    the reference's token (teacher forcing) while our argmax is recorded."""
     logits = dec.prefill(torch.as_tensor(prompt).cuda())
     steps = [logits[0, -1].float().cpu()]
     toks = [int(torch.argmax(steps[-1]))]
-    for _ in range(n - 1):
-        lg = dec.decode_step(torch.tensor([[toks[-1]]], device="cuda"))
+    for i in range(n - 1):
+        nxt = toks[-1] if forced is None else int(forced[i])
+        lg = dec.decode_step(torch.tensor([[nxt]], device="cuda"))
         steps.append(lg[0, -1].float().cpu())
         toks.append(int(torch.argmax(steps[-1])))
     return toks, torch.stack(steps)
+
+
+def _check_tokens(toks, fx, logits=None):
+    """Every step must pick the reference's token, except at near-ties where
+    it must pick one of the reference's top-2."""
+    ref = fx["tokens"].tolist()
+    for i, (a, b) in enumerate(zip(toks, ref)):
+        if a == b:
+            continue
+        assert fx["margin"][i] < TIE, f"step {i}: ours {a} ref {b}, reference margin {fx['margin'][i]:.2e}"
+        if "logits" in fx.files:
+            top2 = np.argsort(-fx["logits"][i].astype(np.float32), kind="stable")[:2].tolist()
+            assert a in top2, f"step {i}: ours {a} not in the reference top-2 {top2}"
 
 
 @pytest.mark.parametrize("name,kv", [("small_fp16", "fp16"), ("small_fp8", "fp8"), ("small_int4", "int4"),
@@ -54,16 +77,16 @@ def _greedy_with_logits(dec, prompt, n):
 def test_small_model_greedy_parity(name, kv, graph):
     fx = _fx(name)
     dec = _decoder(SMALL, fx, kv, use_graph=graph)
-    toks, logits = _greedy_with_logits(dec, fx["prompt"], len(fx["tokens"]))
-    assert toks == fx["tokens"].tolist()
+    toks, logits = _greedy_with_logits(dec, fx["prompt"], len(fx["tokens"]), forced=fx["tokens"])
+    _check_tokens(toks, fx)
     for i in range(len(toks)):
-        assert _rel(logits[i], fx["logits"][i]) < REL_TOL, i
+        assert _rel(logits[i], fx["logits"][i]) < REL_TOL[kv], i
     # the runner's in-graph argmax agrees with the host argmax
     assert int(dec.argmax(1)[0]) == toks[-1]
     if "tree_logits" in fx.files:
         tl = dec.forward_tree_verify(torch.as_tensor(fx["tree_tokens"]).cuda(), fx["tree_depths"].tolist(),
                                      fx["tree_mask"].tolist())
-        assert _rel(tl[0], fx["tree_logits"]) < REL_TOL
+        assert _rel(tl[0], fx["tree_logits"]) < REL_TOL[kv]
         ref_pred = torch.as_tensor(fx["tree_logits"]).argmax(-1)
         assert torch.equal(tl[0].float().cpu().argmax(-1), ref_pred)
     dec.close()
@@ -74,10 +97,17 @@ def test_tiny_config_128_greedy_tokens(kv):
     """12L/768d/12H, vocab 32000, prompt 128, 128 greedy tokens."""
     fx = _fx(f"tiny_{kv}")
     dec = _decoder(TINY, fx, kv)
+    # free-running greedy: identical to the reference up to its first near-tie
     toks, _ = _greedy_with_logits(dec, fx["prompt"], len(fx["tokens"]))
     ref = fx["tokens"].tolist()
-    if toks != ref:
-        i = next(j for j in range(len(ref)) if toks[j] != ref[j])
+    first_tie = next((i for i, m in enumerate(fx["margin"]) if m < TIE), len(ref))
+    if toks[:first_tie] != ref[:first_tie]:
+        i = next(j for j in range(first_tie) if toks[j] != ref[j])
         pytest.fail(f"first divergence at step {i}: ours {toks[i]} ref {ref[i]}; reference top-2 margin "
                     f"there {fx['margin'][i]:.2e}")
+    dec.close()
+    # teacher-forced: every step agrees except at near-ties
+    dec = _decoder(TINY, fx, kv)
+    toks, _ = _greedy_with_logits(dec, fx["prompt"], len(fx["tokens"]), forced=fx["tokens"])
+    _check_tokens(toks, fx)
     dec.close()
