@@ -62,7 +62,7 @@ __device__ __forceinline__ void store_kv_row(const float (&v)[EPL], int lane, in
   am = group_max(am, lpg);
   const float qmax = kv_type == AXB_KV_FP8 ? 448.f : 7.f;
   const float sc = kv_scale(am, qmax, fp32_in);
-  if ((lane % lpg) == 0) srow[(lane * EPL) / G] = __float2half_rn(sc);
+  if (srow && (lane % lpg) == 0) srow[(lane * EPL) / G] = __float2half_rn(sc);
   if (kv_type == AXB_KV_FP8) {
 #pragma unroll
     for (int e = 0; e < EPL; ++e) row[lane * EPL + e] = fp8_code(v[e], sc, fp32_in);
@@ -229,51 +229,131 @@ __device__ __forceinline__ void kv_load16(const uint8_t* row, int type, int e0, 
 }
 
 constexpr int kMaxRep = 8;    // q heads per kv head
-constexpr int kDecTile = 64;  // tokens per online-softmax tile
+constexpr int kDecTile = 64;  // tokens per K/V stage (and online-softmax tile)
+constexpr uint32_t kAttnWaitLimit = 1u << 22;
 
-// Split-K flash decode, T = 1 per sequence.  grid (max_splits, Hkv, B), 128 threads.
-// Each CTA: one (b, kv head), a token range; all n_rep q heads share the K/V reads.
+// Optional fusion of RoPE + KV write into decode attention (T = 1): q and the
+// new token's K/V come straight from the QKV GEMV output.
+struct DecodeFuse {
+  const __half* qkv;  // (B, (Hq + 2 Hkv) hd) fp16, or nullptr: q in d.q, cache already written
+  const float* rope;  // (rope_len, hd/2, 2)
+  int rope_len;
+};
+
+// Split-K flash decode, T = 1 per sequence.  grid (max_splits, Hkv, B), 128
+// threads.  A CTA owns one (sequence, kv head) and a token range; its K/V rows
+// (contiguous per head) are bulk-copied into shared memory in 64-token stages
+// -- issued before the PDL wait, since cached rows do not depend on the
+// preceding kernel -- and the n_rep q heads of the group share every tile.
+// With fusion, the CTA whose range holds the new slot rotates and quantizes
+// the new K/V row, writes it to the cache and patches its staged copy.
 template <int HD>
 __global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d, int max_splits, float* part_o,
-                                                          float* part_ml, int* counters) {
-  constexpr int EPT = HD / 16;  // lanes-groups: 16 elements per thread-chunk
+                                                          float* part_ml, int* counters, int* err,
+                                                          const DecodeFuse f) {
+  constexpr int DPL = HD / 32;  // dims per lane in PV
+  constexpr int EPT = HD / 16;  // threads per token in the score pass (16 elements each)
+  extern __shared__ __align__(128) char sm[];
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int n_rep = d.n_head / d.n_kv_head;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  pdl_wait();
   const int active = d.dev_params ? d.dev_params[2] : d.active_len;
-  int nsplit = min(max_splits, max(1, (active + 63) / 64));
+  const int wpos = d.dev_params ? d.dev_params[1] : d.write_pos;
+  const int nsplit = min(max_splits, max(1, (active + kDecTile - 1) / kDecTile));
   if (split >= nsplit) return;
   const int chunk = (active + nsplit - 1) / nsplit;
   const int t0 = split * chunk, t1 = min(active, t0 + chunk);
+  const int ntiles = (t1 - t0 + kDecTile - 1) / kDecTile;
   const int hq0 = kvh * n_rep;
-  const float sm_scale = 1.0f / sqrtf((float)HD);
-
-  __shared__ float q_s[kMaxRep][HD];
-  __shared__ float p_s[kMaxRep][kDecTile];
-  __shared__ float m_s[kMaxRep], l_s[kMaxRep], corr_s[kMaxRep];
-  __shared__ float o_red[4][kMaxRep][HD / 32 * 32];
-
-  for (int i = tid; i < n_rep * HD; i += 128) {
-    int r = i / HD, e = i % HD;
-    size_t qi = ((size_t)b * d.n_head + hq0 + r) * HD + e;
-    q_s[r][e] = d.q_is_fp32 ? reinterpret_cast<const float*>(d.q)[qi]
-                            : __half2float(reinterpret_cast<const __half*>(d.q)[qi]);
-  }
-  if (tid < kMaxRep) {
-    m_s[tid] = -INFINITY;
-    l_s[tid] = 0.f;
-  }
   const int rb = kv_row_bytes(d.kv_type, HD);
   const int G = d.kv_group, ng = HD / G;
+  const bool quant = d.kv_type != AXB_KV_F16;
+
+  // shared memory carve-up
+  char* kst = sm;                              // [2][64][rb]
+  char* vst = kst + 2 * kDecTile * rb;         // [2][64][rb]
+  float* q_s = reinterpret_cast<float*>(sm + max(4 * kDecTile * rb, 4 * kMaxRep * HD * 4));  // [8][HD]
+  float* p_s = q_s + kMaxRep * HD;             // [8][64]
+  float* ks_s = p_s + kMaxRep * kDecTile;      // [64][ng <= 4] K scales of the current tile
+  float* vs_s = ks_s + kDecTile * 4;           // [64][ng]
+  float* ml_s = vs_s + kDecTile * 4;           // m[8], l[8], corr[8]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ml_s + 3 * kMaxRep + 8);
+  float* o_red = reinterpret_cast<float*>(sm);  // [4][8][HD], reuses the K/V stages at the end
+
   const size_t head_base = ((size_t)b * d.n_kv_head + kvh) * d.max_seq;
   const uint8_t* kc = reinterpret_cast<const uint8_t*>(d.k_cache) + head_base * rb;
   const uint8_t* vc = reinterpret_cast<const uint8_t*>(d.v_cache) + head_base * rb;
-  const __half* ks = d.k_scale ? reinterpret_cast<const __half*>(d.k_scale) + head_base * ng : nullptr;
-  const __half* vs = d.v_scale ? reinterpret_cast<const __half*>(d.v_scale) + head_base * ng : nullptr;
+  const __half* ksc = quant ? reinterpret_cast<const __half*>(d.k_scale) + head_base * ng : nullptr;
+  const __half* vsc = quant ? reinterpret_cast<const __half*>(d.v_scale) + head_base * ng : nullptr;
 
-  // PV accumulators: lane owns dims [lane*HD/32, +HD/32) for every head
-  constexpr int DPL = HD / 32;
+  if (tid == 0) {
+    mbar_init(bars, 1);
+    mbar_init(bars + 1, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i) {  // thread 0: stage i % 2 <- tokens [t0 + 64 i, ...)
+    if (tid != 0 || i >= ntiles) return;
+    const int ts = t0 + i * kDecTile, n = min(kDecTile, t1 - ts), st = i & 1;
+    fence_proxy_async();
+    mbar_expect_tx(bars + st, 2u * n * rb);
+    bulk_g2s(kst + st * kDecTile * rb, kc + (size_t)ts * rb, n * rb, bars + st);
+    bulk_g2s(vst + st * kDecTile * rb, vc + (size_t)ts * rb, n * rb, bars + st);
+  };
+  issue(0);
+  issue(1);
+
+  pdl_wait();  // q / the new K,V row come from the preceding GEMV
+
+  // ---- q (rotated in fp32 when fused) and the new K/V row
+  const int qkv_dim = (d.n_head + 2 * d.n_kv_head) * HD;
+  float nk[DPL], nv[DPL];  // new K/V row (warp 0 / warp 1 of the covering CTA), lane-owned dims
+  const bool covers_new = f.qkv != nullptr && wpos >= t0 && wpos < t1;
+  if (f.qkv) {
+    const __half* row = f.qkv + (size_t)b * qkv_dim;
+    const int rp = d.dev_params ? d.dev_params[0] : 0;
+    const float* fr = f.rope + (size_t)(rp % f.rope_len) * HD;
+    for (int i = tid; i < n_rep * HD / 2; i += 128) {
+      const int r = i / (HD / 2), pr = i % (HD / 2);
+      const __half2 x2 = reinterpret_cast<const __half2*>(row + (hq0 + r) * HD)[pr];
+      const float a0 = __low2float(x2), a1 = __high2float(x2);
+      const float c = fr[2 * pr], sn = fr[2 * pr + 1];
+      q_s[r * HD + 2 * pr] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, sn));
+      q_s[r * HD + 2 * pr + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, c));
+    }
+    if (covers_new && wid < 2) {
+      const __half* src = row + (size_t)(d.n_head + (wid == 0 ? 0 : d.n_kv_head) + kvh) * HD;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) nk[e] = __half2float(src[lane * DPL + e]);
+      if (wid == 0) {
+#pragma unroll
+        for (int e = 0; e < DPL; e += 2) {
+          const int pr = (lane * DPL + e) >> 1;
+          const float c = fr[2 * pr], sn = fr[2 * pr + 1], a0 = nk[e], a1 = nk[e + 1];
+          nk[e] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, sn));
+          nk[e + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, c));
+        }
+      }
+      // quantize (fp32 rule) and write the cache row
+      uint8_t* crow = const_cast<uint8_t*>((wid == 0 ? kc : vc) + (size_t)wpos * rb);
+      __half* srow = quant ? const_cast<__half*>((wid == 0 ? ksc : vsc) + (size_t)wpos * ng) : nullptr;
+      store_kv_row<DPL>(nk, lane, d.kv_type, G, true, crow, srow);
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) nv[e] = nk[e];
+    }
+  } else {
+    for (int i = tid; i < n_rep * HD; i += 128) {
+      const int r = i / HD, e = i % HD;
+      const size_t qi = ((size_t)b * d.n_head + hq0 + r) * HD + e;
+      q_s[i] = d.q_is_fp32 ? reinterpret_cast<const float*>(d.q)[qi]
+                           : __half2float(reinterpret_cast<const __half*>(d.q)[qi]);
+    }
+  }
+  if (tid < kMaxRep) {
+    ml_s[tid] = -INFINITY;
+    ml_s[kMaxRep + tid] = 0.f;
+  }
+  const float sm_scale = 1.0f / sqrtf((float)HD);
   float acc[kMaxRep][DPL];
 #pragma unroll
   for (int r = 0; r < kMaxRep; ++r)
@@ -281,26 +361,51 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d,
     for (int e = 0; e < DPL; ++e) acc[r][e] = 0.f;
   __syncthreads();
 
-  for (int tt = t0; tt < t1; tt += kDecTile) {
-    const int nt = min(kDecTile, t1 - tt);
-    // scores: one (token, 16-element chunk) per thread pass; chunks of a token
-    // are reduced with shuffles (EPT threads per token)
+  bool failed = false;
+  for (int i = 0; i < ntiles; ++i) {
+    const int st = i & 1, ts = t0 + i * kDecTile, nt = min(kDecTile, t1 - ts);
+    // scales of this tile (plain loads; tiny)
+    if (quant)
+      for (int j = tid; j < nt * ng; j += 128) {
+        ks_s[j] = __half2float(ksc[(size_t)ts * ng + j]);
+        vs_s[j] = __half2float(vsc[(size_t)ts * ng + j]);
+      }
+    if (!mbar_wait(bars + st, (uint32_t)((i >> 1) & 1), kAttnWaitLimit)) {
+      if (tid == 0) atomicExch(err, AXB_ETIMEOUT);
+      if (i + 1 < ntiles) mbar_wait(bars + (st ^ 1), (uint32_t)(((i + 1) >> 1) & 1), kAttnWaitLimit);
+      failed = true;
+    }
+    if (__syncthreads_or(failed)) return;
+    uint8_t* kt = reinterpret_cast<uint8_t*>(kst + st * kDecTile * rb);
+    uint8_t* vt = reinterpret_cast<uint8_t*>(vst + st * kDecTile * rb);
+    if (covers_new && wid < 2 && wpos >= ts && wpos < ts + nt) {
+      // patch the staged copy with the row written this step (the prefetch saw the old one)
+      uint8_t* row = (wid == 0 ? kt : vt) + (size_t)(wpos - ts) * rb;
+      store_kv_row<DPL>(nv, lane, d.kv_type, G, true, row, nullptr);
+    }
+    __syncthreads();
+    if (covers_new && quant && wpos >= ts && wpos < ts + nt && tid < 2 * ng) {
+      const int which = tid / ng, gi = tid % ng;
+      (which == 0 ? ks_s : vs_s)[(wpos - ts) * ng + gi] =
+          __half2float((which == 0 ? ksc : vsc)[(size_t)wpos * ng + gi]);
+    }
+    __syncthreads();
+    // scores: EPT threads per token, 16 elements each (128 / EPT tokens per pass)
     for (int base = 0; base < kDecTile; base += 128 / EPT) {
       const int tk = base + tid / EPT, ch = tid % EPT;
       float part[kMaxRep];
 #pragma unroll
       for (int r = 0; r < kMaxRep; ++r) part[r] = 0.f;
       if (tk < nt) {
-        const int slot = tt + tk;
         float kv[16];
-        kv_load16(kc + (size_t)slot * rb, d.kv_type, ch * 16, kv);
-        float s = ks ? __half2float(ks[(size_t)slot * ng + (ch * 16) / G]) : 1.f;
+        kv_load16(kt + (size_t)tk * rb, d.kv_type, ch * 16, kv);
+        const float s = quant ? ks_s[tk * ng + (ch * 16) / G] : 1.f;
 #pragma unroll
         for (int r = 0; r < kMaxRep; ++r) {
           if (r < n_rep) {
             float a = 0.f;
 #pragma unroll
-            for (int e = 0; e < 16; ++e) a = __fmaf_rn(q_s[r][ch * 16 + e], kv[e], a);
+            for (int e = 0; e < 16; ++e) a = __fmaf_rn(q_s[r * HD + ch * 16 + e], kv[e], a);
             part[r] = a * s;
           }
         }
@@ -309,77 +414,77 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d,
       for (int r = 0; r < kMaxRep; ++r) {
         float a = part[r];
         for (int o = 1; o < EPT; o <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (ch == 0 && tk < kDecTile && r < n_rep) p_s[r][tk] = (tk < nt) ? a * sm_scale : -INFINITY;
+        if (ch == 0 && r < n_rep) p_s[r * kDecTile + tk] = (tk < nt) ? a * sm_scale : -INFINITY;
       }
     }
     __syncthreads();
-    // online softmax update: warp w handles heads w, w+4
+    // online softmax: warp w handles heads w, w+4
     for (int r = wid; r < n_rep; r += 4) {
-      float v0 = p_s[r][lane], v1 = p_s[r][lane + 32];
-      float mx = warp_max(fmaxf(v0, v1));
-      float m_old = m_s[r];
-      float m_new = fmaxf(m_old, mx);
-      float e0 = (v0 == -INFINITY) ? 0.f : __expf(v0 - m_new);
-      float e1 = (v1 == -INFINITY) ? 0.f : __expf(v1 - m_new);
-      p_s[r][lane] = e0;
-      p_s[r][lane + 32] = e1;
-      float sum = warp_sum(e0 + e1);
+      const float v0 = p_s[r * kDecTile + lane], v1 = p_s[r * kDecTile + lane + 32];
+      const float mx = warp_max(fmaxf(v0, v1));
+      const float m_old = ml_s[r], m_new = fmaxf(m_old, mx);
+      const float e0 = (v0 == -INFINITY) ? 0.f : __expf(v0 - m_new);
+      const float e1 = (v1 == -INFINITY) ? 0.f : __expf(v1 - m_new);
+      p_s[r * kDecTile + lane] = e0;
+      p_s[r * kDecTile + lane + 32] = e1;
+      const float sum = warp_sum(e0 + e1);
       if (lane == 0) {
-        float c = (m_old == -INFINITY) ? 0.f : __expf(m_old - m_new);
-        corr_s[r] = c;
-        l_s[r] = l_s[r] * c + sum;
-        m_s[r] = m_new;
+        const float c = (m_old == -INFINITY) ? 0.f : __expf(m_old - m_new);
+        ml_s[2 * kMaxRep + r] = c;
+        ml_s[kMaxRep + r] = ml_s[kMaxRep + r] * c + sum;
+        ml_s[r] = m_new;
       }
     }
     __syncthreads();
-    // PV: warp w takes tokens w, w+4, ...; lane covers DPL dims
 #pragma unroll
     for (int r = 0; r < kMaxRep; ++r) {
       if (r < n_rep) {
-        float c = corr_s[r];
+        const float c = ml_s[2 * kMaxRep + r];
 #pragma unroll
         for (int e = 0; e < DPL; ++e) acc[r][e] *= c;
       }
     }
+    // PV: warp w takes tokens w, w+4, ...; lane covers DPL consecutive dims
     for (int tk = wid; tk < nt; tk += 4) {
-      const int slot = tt + tk;
-      const uint8_t* vrow = vc + (size_t)slot * rb;
+      const uint8_t* vrow = vt + (size_t)tk * rb;
       float vv[DPL];
 #pragma unroll
       for (int e = 0; e < DPL; ++e) vv[e] = kv_elem(vrow, d.kv_type, lane * DPL + e);
-      float s = vs ? __half2float(vs[(size_t)slot * ng + (lane * DPL) / G]) : 1.f;
+      const float s = quant ? vs_s[tk * ng + (lane * DPL) / G] : 1.f;
 #pragma unroll
       for (int r = 0; r < kMaxRep; ++r) {
         if (r < n_rep) {
-          float p = p_s[r][tk] * s;
+          const float pw = p_s[r * kDecTile + tk] * s;
 #pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[r][e] = __fmaf_rn(p, vv[e], acc[r][e]);
+          for (int e = 0; e < DPL; ++e) acc[r][e] = __fmaf_rn(pw, vv[e], acc[r][e]);
         }
       }
     }
-    __syncthreads();
+    __syncthreads();  // stage st and p_s are free again
+    issue(i + 2);
   }
-  // cross-warp reduction of acc
+  // cross-warp reduction of acc (o_red aliases the K/V stages, all consumed)
 #pragma unroll
   for (int r = 0; r < kMaxRep; ++r)
     if (r < n_rep)
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) o_red[wid][r][lane * DPL + e] = acc[r][e];
+      for (int e = 0; e < DPL; ++e) o_red[(wid * kMaxRep + r) * HD + lane * DPL + e] = acc[r][e];
   __syncthreads();
   const size_t pidx = ((size_t)b * d.n_head + hq0);
   for (int i = tid; i < n_rep * HD; i += 128) {
-    int r = i / HD, e = i % HD;
-    float o = o_red[0][r][e] + o_red[1][r][e] + o_red[2][r][e] + o_red[3][r][e];
+    const int r = i / HD, e = i % HD;
+    const float o = o_red[(0 * kMaxRep + r) * HD + e] + o_red[(1 * kMaxRep + r) * HD + e] +
+                    o_red[(2 * kMaxRep + r) * HD + e] + o_red[(3 * kMaxRep + r) * HD + e];
     if (nsplit == 1) {
-      reinterpret_cast<__half*>(d.out)[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(o, l_s[r]));
+      reinterpret_cast<__half*>(d.out)[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(o, ml_s[kMaxRep + r]));
     } else {
       part_o[((pidx + r) * max_splits + split) * HD + e] = o;
     }
   }
   if (nsplit == 1) return;
   if (tid < n_rep) {
-    part_ml[((pidx + tid) * max_splits + split) * 2 + 0] = m_s[tid];
-    part_ml[((pidx + tid) * max_splits + split) * 2 + 1] = l_s[tid];
+    part_ml[((pidx + tid) * max_splits + split) * 2 + 0] = ml_s[tid];
+    part_ml[((pidx + tid) * max_splits + split) * 2 + 1] = ml_s[kMaxRep + tid];
   }
   __threadfence();
   __syncthreads();
@@ -390,20 +495,28 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d,
   __threadfence();
   // deterministic combine over splits in index order
   for (int i = tid; i < n_rep * HD; i += 128) {
-    int r = i / HD, e = i % HD;
+    const int r = i / HD, e = i % HD;
     const size_t hb = (pidx + r) * max_splits;
     float M = -INFINITY;
     for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(part_ml + (hb + sp) * 2));
     float L = 0.f, O = 0.f;
     for (int sp = 0; sp < nsplit; ++sp) {
-      float m = __ldcg(part_ml + (hb + sp) * 2), l = __ldcg(part_ml + (hb + sp) * 2 + 1);
-      float c = (m == -INFINITY) ? 0.f : __expf(m - M);
+      const float m = __ldcg(part_ml + (hb + sp) * 2), l = __ldcg(part_ml + (hb + sp) * 2 + 1);
+      const float c = (m == -INFINITY) ? 0.f : __expf(m - M);
       L += l * c;
       O += __ldcg(part_o + (hb + sp) * HD + e) * c;
     }
     reinterpret_cast<__half*>(d.out)[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, L));
   }
   if (tid == 0) counters[b * d.n_kv_head + kvh] = 0;
+}
+
+size_t decode_smem(int kv_type, int hd) {
+  int rb = kv_type == AXB_KV_F16 ? hd * 2 : (kv_type == AXB_KV_FP8 ? hd : hd / 2);
+  size_t stages = (size_t)4 * kDecTile * rb;
+  size_t ored = (size_t)4 * kMaxRep * hd * 4;
+  size_t rest = (size_t)(kMaxRep * hd + kMaxRep * kDecTile + 8 * kDecTile + 3 * kMaxRep + 8) * 4 + 2 * 8 + 16;
+  return std::max(stages, ored) + rest;
 }
 
 // Tree / chunked-prefill attention: T query tokens per sequence, each sees the
@@ -572,11 +685,12 @@ int decode_max_splits(int B, int n_kv_head) {
 // The counters sit at a fixed offset for every (B, heads, splits), so one
 // zeroed workspace serves any call; the combining CTA returns each to zero.
 constexpr size_t kAttnCounters = 1 << 16;
+constexpr size_t kAttnHead = 256;  // error word
 
 size_t attn_workspace(int B, int n_head, int head_dim, int max_splits) {
   size_t o = (size_t)B * n_head * max_splits * head_dim * 4;
   size_t ml = (size_t)B * n_head * max_splits * 2 * 4;
-  return kAttnCounters * 4 + round_up(ml, 256) + round_up(o, 256);
+  return kAttnHead + kAttnCounters * 4 + round_up(ml, 256) + round_up(o, 256);
 }
 
 int rope_kv_write(const axb_kv_write_desc* d, cudaStream_t s, bool pdl) {
@@ -598,14 +712,36 @@ int rope_kv_write(const axb_kv_write_desc* d, cudaStream_t s, bool pdl) {
   return cuda_status(e, "rope_kv_write launch");
 }
 
+int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s);
+
+// Raise the dynamic shared-memory limit of the decode kernels once per device
+// (outside any stream capture).
+int attn_prepare() {
+  static int done_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (done_dev == dev) return AXB_OK;
+  cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  if (e != cudaSuccess) return cuda_status(e, "attention attribute");
+  done_dev = dev;
+  return AXB_OK;
+}
+
 int attention(const axb_attn_desc* d, cudaStream_t s) {
+  DecodeFuse f = {};
+  return attention_fused(d, f, s);
+}
+
+int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s) {
   AXB_CHECK_ARG(d && d->q && d->k_cache && d->v_cache && d->out, "attention: null pointer");
   AXB_CHECK_ARG(d->head_dim == 64 || d->head_dim == 128, "attention: head_dim must be 64 or 128");
   AXB_CHECK_ARG(d->n_kv_head > 0 && d->n_head % d->n_kv_head == 0 && d->n_head / d->n_kv_head <= kMaxRep,
                 "attention: n_head / n_kv_head must be an integer <= %d", kMaxRep);
-  AXB_CHECK_ARG(d->kv_type == AXB_KV_F16 || (d->k_scale && d->v_scale && d->kv_group > 0 &&
-                                              d->head_dim % d->kv_group == 0 && d->kv_group % 16 == 0),
-                "attention: bad quantized-cache scales / group");
+  AXB_CHECK_ARG(d->kv_type == AXB_KV_F16 || (d->k_scale && d->v_scale && d->kv_group >= 32 &&
+                                              d->head_dim % d->kv_group == 0),
+                "attention: bad quantized-cache scales / group (kv_group must divide head_dim, >= 32)");
   if (d->masks == nullptr) {
     AXB_CHECK_ARG(d->active_len >= 1 && d->active_len <= d->max_seq, "attention: bad active_len %d", d->active_len);
     int ms = d->num_splits > 0 ? std::min(64, d->num_splits) : decode_max_splits(d->B, d->n_kv_head);
@@ -613,16 +749,21 @@ int attention(const axb_attn_desc* d, cudaStream_t s) {
                   "attention: workspace too small");
     AXB_CHECK_ARG((size_t)d->B * d->n_kv_head <= kAttnCounters, "attention: too many sequences x heads");
     char* ws = reinterpret_cast<char*>(d->workspace);
-    int* cnt = reinterpret_cast<int*>(ws);
-    float* pml = reinterpret_cast<float*>(ws + kAttnCounters * 4);
+    int* err = reinterpret_cast<int*>(ws);
+    int* cnt = reinterpret_cast<int*>(ws + kAttnHead);
+    float* pml = reinterpret_cast<float*>(ws + kAttnHead + kAttnCounters * 4);
     size_t ml_b = round_up((size_t)d->B * d->n_head * ms * 2 * 4, 256);
-    float* po = reinterpret_cast<float*>(ws + kAttnCounters * 4 + ml_b);
+    float* po = reinterpret_cast<float*>(ws + kAttnHead + kAttnCounters * 4 + ml_b);
+    AXB_CHECK_ARG((reinterpret_cast<uintptr_t>(d->k_cache) & 15) == 0 && (reinterpret_cast<uintptr_t>(d->v_cache) & 15) == 0,
+                  "attention: caches must be 16-byte aligned");
     dim3 grid(ms, d->n_kv_head, d->B);
+    const size_t smem = decode_smem(d->kv_type, d->head_dim);
+    if (int rc = attn_prepare()) return rc;
     cudaError_t e;
     if (d->head_dim == 128)
-      e = launch_pdl(decode_attn_kernel<128>, grid, dim3(128), 0, s, d->pdl != 0, *d, ms, po, pml, cnt);
+      e = launch_pdl(decode_attn_kernel<128>, grid, dim3(128), smem, s, d->pdl != 0, *d, ms, po, pml, cnt, err, f);
     else
-      e = launch_pdl(decode_attn_kernel<64>, grid, dim3(128), 0, s, d->pdl != 0, *d, ms, po, pml, cnt);
+      e = launch_pdl(decode_attn_kernel<64>, grid, dim3(128), smem, s, d->pdl != 0, *d, ms, po, pml, cnt, err, f);
     return cuda_status(e, "decode attention launch");
   }
   AXB_CHECK_ARG(d->T >= 1 && d->T <= 64, "attention: tree mode needs 1 <= T <= 64");

@@ -288,12 +288,19 @@ __global__ void q2_dequant_kernel(const uint8_t* __restrict__ w, const __half* _
 }
 
 // ------------------------------------------------------------------ GEMV
+// Work split: "stream-K" over quantization groups ("units") at CTA level.
+// CTA c owns units [c*U/C, (c+1)*U/C) of the tile-major unit sequence; inside
+// the CTA the 4 warps split every tile segment's K range into 4 contiguous
+// chunks, stream them through per-warp bulk-copy rings, and reduce the 4
+// partial fragments in shared memory in warp order.  A tile whose units span
+// several CTAs is finished by the last CTA to arrive (per-tile counter), which
+// sums the CTA partials in CTA order: the result is deterministic.
 struct GemmArgs {
   const uint4* W;
   const char* S;
   int N, K, M, KB, GB, upt;
   long long U;
-  long long Wt;
+  long long C;  // CTAs
   const __half* x;
   int ldx;
   const float* norm_w;
@@ -309,17 +316,18 @@ struct GemmArgs {
   int xs_bytes;   // bytes of the staged-x region at the start of shared memory
 };
 
-constexpr int kWarpsPerCta = 8;
-constexpr int kCH = 4;             // k-blocks (512 B each) per pipeline stage
-constexpr int kStages = 4;         // stages per warp
-constexpr int kStageW = kCH * 512; // weight bytes per stage
-constexpr int kStageS = kCH * 64;  // scale bytes per stage (max: affine, one group per k-block)
+constexpr int kWarps = 4;           // warps per CTA (K-split of each tile)
+constexpr int kCtasPerSm = 4;       // resident CTAs per SM the grid is sized for
+constexpr int kCH = 4;              // k-blocks (512 B each) per pipeline stage
+constexpr int kStages = 2;          // stages per warp
+constexpr int kStageW = kCH * 512;  // weight bytes per stage
+constexpr int kStageS = kCH * 64;   // scale bytes per stage (max: affine, one group per k-block)
 constexpr int kWarpRing = kStages * (kStageW + kStageS) + kStages * 8;
 constexpr uint32_t kWaitLimit = 1u << 22;
 
-__device__ __forceinline__ long long warp_start(long long w, long long U, long long Wt) { return w * U / Wt; }
-__device__ __forceinline__ long long warp_of_unit(long long u, long long U, long long Wt) {
-  return ((u + 1) * Wt - 1) / U;
+__device__ __forceinline__ int cta_start(long long c, long long U, long long C) { return (int)(c * U / C); }
+__device__ __forceinline__ int cta_of_unit(long long u, long long U, long long C) {
+  return (int)(((u + 1) * C - 1) / U);
 }
 
 // nibble pairs of one word -> four A-fragment registers holding (q - Z)
@@ -384,233 +392,306 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, int tile, const floa
   }
 }
 
-// Stage x (optionally RMS-normalized, modules.py:41-43 with fp32 weight) into smem.
-__device__ void stage_x(const GemmArgs& a, __half* xs) {
-  const int lane = threadIdx.x & 31;
-  const int nw = blockDim.x >> 5, wid = threadIdx.x >> 5;
-  for (int m = wid; m < a.M; m += nw) {
-    const __half* xr = a.x + (size_t)m * a.ldx;
-    __half* sr = xs + (size_t)m * a.xs_stride;
-    if (a.norm_w) {
-      float ss = 0.f;
-      for (int k = lane * 8; k < a.K; k += 256) {
-        uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-        const __half2* h = reinterpret_cast<const __half2*>(&v);
+// Stage x (optionally RMS-normalized: modules.py:41-43 with an fp32 weight,
+// rms = 1/sqrt(mean(x^2) + eps), h = fp16((x * rms) * w)) into shared memory.
+// All threads of the CTA share each row so the row's loads are all in flight.
+__device__ void stage_x(const GemmArgs& a, __half* xs, float* red) {
+  const int tid = threadIdx.x, nth = blockDim.x;
+  const int lane = tid & 31, wid = tid >> 5, nw = nth >> 5;
+  const int K8 = a.K >> 3;  // uint4 chunks per row
+  for (int m = 0; m < a.M; ++m) {
+    const uint4* xr = reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx);
+    uint4* sr = reinterpret_cast<uint4*>(xs + (size_t)m * a.xs_stride);
+    if (!a.norm_w) {
+      for (int c = tid; c < K8; c += nth) sr[c] = xr[c];
+      continue;
+    }
+    float ss = 0.f;
+    for (int c0 = tid; c0 < K8; c0 += nth * 4) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (c0 + u * nth < K8) v[u] = xr[c0 + u * nth];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (c0 + u * nth >= K8) continue;
+        const __half2* h = reinterpret_cast<const __half2*>(&v[u]);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           float2 f = __half22float2(h[q]);
           ss = __fmaf_rn(f.x, f.x, ss);
           ss = __fmaf_rn(f.y, f.y, ss);
         }
+        sr[c0 + u * nth] = v[u];  // raw x, scaled below
       }
-      ss = warp_sum(ss);
-      const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps)));
-      for (int k = lane * 8; k < a.K; k += 256) {
-        uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-        const __half2* h = reinterpret_cast<const __half2*>(&v);
-        uint4 o;
-        __half2* oh = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float2 f = __half22float2(h[q]);
-          float w0 = a.norm_w[k + 2 * q], w1 = a.norm_w[k + 2 * q + 1];
-          oh[q] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, rms), w0), __fmul_rn(__fmul_rn(f.y, rms), w1));
-        }
-        *reinterpret_cast<uint4*>(sr + k) = o;
-      }
-    } else {
-      for (int k = lane * 8; k < a.K; k += 256)
-        *reinterpret_cast<uint4*>(sr + k) = *reinterpret_cast<const uint4*>(xr + k);
     }
+    ss = warp_sum(ss);
+    if (lane == 0) red[wid] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < nw; ++w) tot += red[w];
+    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.K), a.eps)));
+    for (int c = tid; c < K8; c += nth) {
+      uint4 v = sr[c];
+      const __half2* h = reinterpret_cast<const __half2*>(&v);
+      uint4 o;
+      __half2* oh = reinterpret_cast<__half2*>(&o);
+      const float4 w0 = reinterpret_cast<const float4*>(a.norm_w)[2 * c];
+      const float4 w1 = reinterpret_cast<const float4*>(a.norm_w)[2 * c + 1];
+      const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = __half22float2(h[q]);
+        oh[q] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, rms), ws[2 * q]),
+                                  __fmul_rn(__fmul_rn(f.y, rms), ws[2 * q + 1]));
+      }
+      sr[c] = o;
+    }
+    __syncthreads();  // red[] reuse
   }
 }
 
+// chunk of tile t handled by warp w: global k-block range [lo, hi)
+__device__ __forceinline__ void warp_chunk(int upt, int GB, int U0, int U1, int t, int w, int& lo, int& hi) {
+  const int s0 = max(U0, t * upt), s1 = min(U1, (t + 1) * upt);
+  const int ns = s1 - s0;
+  lo = (s0 + ns * w / kWarps) * GB;
+  hi = (s0 + ns * (w + 1) / kWarps) * GB;
+}
+
 template <int NT, bool SYM, int GB, bool XS>
-__global__ void __launch_bounds__(kWarpsPerCta * 32) qgemm_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 8 : (NT == 2 ? 5 : 3)) qgemm_kernel(const GemmArgs a) {
   extern __shared__ __align__(128) char smem[];
   __half* xs = reinterpret_cast<__half*>(smem);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int g = lane >> 2, t4 = lane & 3;
-  const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + wid;
-  const long long u0 = warp_start(w, a.U, a.Wt), u1 = warp_start(w + 1, a.U, a.Wt);
-  const long long kb0 = u0 * GB, kb1 = u1 * GB;
-  const int nst = (int)((kb1 - kb0 + kCH - 1) / kCH);
+  const int c = blockIdx.x;
+  const int U0 = cta_start(c, a.U, a.C), U1 = cta_start(c + 1, a.U, a.C);
+  const int t_first = U0 / a.upt, t_last = (U1 - 1) / a.upt;
   constexpr int UB = SYM ? 32 : 64;  // scale bytes per group
 
-  // per-warp ring of bulk-copied weight (and scale) stages
   char* ring = smem + a.xs_bytes + (size_t)wid * kWarpRing;
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kStages * (kStageW + kStageS));
+  float* red = reinterpret_cast<float*>(smem + a.xs_bytes + kWarps * kWarpRing);  // [kWarps][32][4*NT]
+  float* nred = red + kWarps * 32 * 4 * NT;                                       // [kWarps] norm partials
   if (lane == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(bars + s, 1);
+    for (int st = 0; st < kStages; ++st) mbar_init(bars + st, 1);
     fence_mbar_init();
   }
   __syncwarp();
-  auto issue = [&](int it) {
-    if (lane != 0 || it >= nst) return;
-    const int st = it % kStages;
-    const long long kbs = kb0 + (long long)it * kCH;
-    const int n = (int)((kb1 - kbs) < kCH ? (kb1 - kbs) : kCH);
+
+  // producer state (lane 0): next stage to issue
+  int p_t = t_first, p_kb = 0, p_end = 0, p_i = 0;
+  if (lane == 0) warp_chunk(a.upt, GB, U0, U1, p_t, wid, p_kb, p_end);
+  auto issue = [&]() {
+    if (lane != 0) return;
+    while (p_kb >= p_end && p_t < t_last) {
+      ++p_t;
+      warp_chunk(a.upt, GB, U0, U1, p_t, wid, p_kb, p_end);
+    }
+    if (p_kb >= p_end) return;
+    const int st = p_i % kStages;
+    const int n = min(kCH, p_end - p_kb);
     const uint32_t bw = n * 512, bs = (n / GB) * UB;
     fence_proxy_async();
     mbar_expect_tx(bars + st, bw + bs);
-    bulk_g2s(ring + st * kStageW, a.W + kbs * 32, bw, bars + st);
-    bulk_g2s(ring + kStages * kStageW + st * kStageS, a.S + (kbs / GB) * UB, bs, bars + st);
+    bulk_g2s(ring + st * kStageW, a.W + (size_t)p_kb * 32, bw, bars + st);
+    bulk_g2s(ring + kStages * kStageW + st * kStageS, a.S + (size_t)(p_kb / GB) * UB, bs, bars + st);
+    p_kb += n;
+    ++p_i;
   };
-  // 1. weights do not depend on the producer kernel: start streaming them now
-  for (int it = 0; it < kStages; ++it) issue(it);
+  // weights do not depend on the producer kernel: start streaming now
+  for (int i = 0; i < kStages; ++i) issue();
 
   pdl_wait();
   if (XS) {
-    stage_x(a, xs);
+    stage_x(a, xs, nred);
     __syncthreads();
   }
   pdl_trigger();
 
-  float acc[NT][4];
-  float tmp[NT][4];
+  int ci = 0;  // stages consumed by this warp
+  bool failed = false;
+  for (int t = t_first; t <= t_last; ++t) {
+    int kb_lo, kb_hi;
+    warp_chunk(a.upt, GB, U0, U1, t, wid, kb_lo, kb_hi);
+    float acc[NT][4];
+    float tmp[NT][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[nt][i] = tmp[nt][i] = 0.f;
-
-  bool first_seg = true;
-  for (int it = 0; it < nst; ++it) {
-    const int st = it % kStages;
-    if (!mbar_wait(bars + st, (uint32_t)((it / kStages) & 1), kWaitLimit)) {
-      // record the failure, give the copies still in flight a bounded chance
-      // to land (so none writes into shared memory after exit), and leave
-      if (lane == 0) atomicExch(a.err, AXB_ETIMEOUT);
-      for (int j = it + 1; j < nst && j < it + kStages; ++j)
-        mbar_wait(bars + (j % kStages), (uint32_t)((j / kStages) & 1), kWaitLimit);
-      return;
-    }
-    const uint4* wst = reinterpret_cast<const uint4*>(ring + st * kStageW);
-    const char* sst = ring + kStages * kStageW + st * kStageS;
-    const long long kbs = kb0 + (long long)it * kCH;
-    const int n = (int)((kb1 - kbs) < kCH ? (kb1 - kbs) : kCH);
-    const long long unit0 = kbs / GB;
-    for (int kbo = 0; kbo < n; ++kbo) {
-      const long long kbi = kbs + kbo;
-      const int tile = (int)(kbi / a.KB);
-      const int kb = (int)(kbi - (long long)tile * a.KB);
-      const uint4 cur = wst[kbo * 32 + lane];
-      const int su = (int)(kbi / GB - unit0);
-      // B fragments (activations) for this k-block
-      uint32_t bf[NT][8];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int nn = nt * 8 + g;
-        if (nn < a.M) {
-          const __half* src = XS ? xs + (size_t)nn * a.xs_stride + kb * 64 + 16 * t4
-                                 : a.x + (size_t)nn * a.ldx + kb * 64 + 16 * t4;
-          uint4 v0 = *reinterpret_cast<const uint4*>(src);
-          uint4 v1 = *reinterpret_cast<const uint4*>(src + 8);
-          bf[nt][0] = v0.x; bf[nt][1] = v0.y; bf[nt][2] = v0.z; bf[nt][3] = v0.w;
-          bf[nt][4] = v1.x; bf[nt][5] = v1.y; bf[nt][6] = v1.z; bf[nt][7] = v1.w;
-        } else {
-#pragma unroll
-          for (int q = 0; q < 8; ++q) bf[nt][q] = 0u;
-        }
+      for (int q = 0; q < 4; ++q) acc[nt][q] = tmp[nt][q] = 0.f;
+    for (int kb0 = kb_lo; kb0 < kb_hi && !failed;) {
+      const int st = ci % kStages;
+      if (!mbar_wait(bars + st, (uint32_t)((ci / kStages) & 1), kWaitLimit)) {
+        // record the failure; the remaining copy (if any) gets a bounded wait
+        if (lane == 0) atomicExch(a.err, AXB_ETIMEOUT);
+        mbar_wait(bars + ((ci + 1) % kStages), (uint32_t)(((ci + 1) / kStages) & 1), kWaitLimit);
+        failed = true;
+        break;
       }
-      const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
-      if (SYM) {
+      const int n = min(kCH, kb_hi - kb0);
+      const uint4* wst = reinterpret_cast<const uint4*>(ring + st * kStageW);
+      const char* sst = ring + kStages * kStageW + st * kStageS;
+      const int unit0 = kb0 / GB;
+      for (int j = 0; j < n; ++j) {
+        const int kbi = kb0 + j;
+        const int kb = kbi - t * a.KB;
+        const uint4 cur = wst[j * 32 + lane];
+        const int su = kbi / GB - unit0;
+        uint32_t bf[NT][8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t af[4];
-          unpack_word<8>(words[j], af);
+        for (int nt = 0; nt < NT; ++nt) {
+          const int nn = nt * 8 + g;
+          if (nn < a.M) {
+            const __half* src = XS ? xs + (size_t)nn * a.xs_stride + kb * 64 + 16 * t4
+                                   : a.x + (size_t)nn * a.ldx + kb * 64 + 16 * t4;
+            uint4 v0 = *reinterpret_cast<const uint4*>(src);
+            uint4 v1 = *reinterpret_cast<const uint4*>(src + 8);
+            bf[nt][0] = v0.x; bf[nt][1] = v0.y; bf[nt][2] = v0.z; bf[nt][3] = v0.w;
+            bf[nt][4] = v1.x; bf[nt][5] = v1.y; bf[nt][6] = v1.z; bf[nt][7] = v1.w;
+          } else {
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma_16816(tmp[nt], af, bf[nt][2 * j], bf[nt][2 * j + 1], tmp[nt]);
-        }
-        if ((kb % GB) == GB - 1) {  // group complete: apply the per-row scales
-          const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[su * 8 + g];
-          const float2 sc = __half22float2(u32_as_h2(sp));
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            acc[nt][0] = __fmaf_rn(sc.x, tmp[nt][0], acc[nt][0]);
-            acc[nt][1] = __fmaf_rn(sc.x, tmp[nt][1], acc[nt][1]);
-            acc[nt][2] = __fmaf_rn(sc.y, tmp[nt][2], acc[nt][2]);
-            acc[nt][3] = __fmaf_rn(sc.y, tmp[nt][3], acc[nt][3]);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) tmp[nt][q] = 0.f;
+            for (int q = 0; q < 8; ++q) bf[nt][q] = 0u;
           }
         }
-      } else {
-        const uint2 sb = reinterpret_cast<const uint2*>(sst)[su * 8 + g];
-        const __half2 s01 = u32_as_h2(sb.x), s23 = u32_as_h2(sb.y);
-        const __half2 sg = __half2half2(__low2half(s01)), bg = __half2half2(__high2half(s01));
-        const __half2 sg8 = __half2half2(__low2half(s23)), bg8 = __half2half2(__high2half(s23));
+        const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
+        if (SYM) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t af[4];
-          unpack_word<0>(words[j], af);
-          // w = fp16(q * s + b): the reference's dequantized fp16 weight
-          af[0] = h2_as_u32(__hfma2(u32_as_h2(af[0]), sg, bg));
-          af[1] = h2_as_u32(__hfma2(u32_as_h2(af[1]), sg8, bg8));
-          af[2] = h2_as_u32(__hfma2(u32_as_h2(af[2]), sg, bg));
-          af[3] = h2_as_u32(__hfma2(u32_as_h2(af[3]), sg8, bg8));
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma_16816(acc[nt], af, bf[nt][2 * j], bf[nt][2 * j + 1], acc[nt]);
-        }
-      }
-      // segment end: end of the tile or of this warp's range
-      if (kb == a.KB - 1 || kbi == kb1 - 1) {
-        const bool complete = (kb == a.KB - 1) && (!first_seg || kb0 == (long long)tile * a.KB);
-        if (complete) {
-          epilogue<NT>(a, tile, acc, lane);
-        } else {
-          const int slot = first_seg ? 0 : 1;
-          float* p = a.partials + ((w * 2 + slot) * 32 + lane) * (4 * NT);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-            *reinterpret_cast<float4*>(p + 4 * nt) = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-          __threadfence();
-          __syncwarp();
-          int old = 0;
-          if (lane == 0) old = atomicAdd(a.counters + tile, 1);
-          old = __shfl_sync(0xffffffffu, old, 0);
-          const long long tu0 = (long long)tile * a.upt, tu1 = tu0 + a.upt - 1;
-          const long long wf = warp_of_unit(tu0, a.U, a.Wt), wl = warp_of_unit(tu1, a.U, a.Wt);
-          if (old == (int)(wl - wf)) {  // last contributor: reduce in warp order
-            __threadfence();
-            float sum[NT][4];
+          for (int jj = 0; jj < 4; ++jj) {
+            uint32_t af[4];
+            unpack_word<8>(words[jj], af);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
+              mma_16816(tmp[nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], tmp[nt]);
+          }
+          if ((kb % GB) == GB - 1) {  // group complete: apply the per-row scales
+            const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[su * 8 + g];
+            const float2 sc = __half22float2(u32_as_h2(sp));
 #pragma unroll
-              for (int q = 0; q < 4; ++q) sum[nt][q] = 0.f;
-            for (long long ww = wf; ww <= wl; ++ww) {
-              const int sl = (warp_start(ww, a.U, a.Wt) / a.upt == tile) ? 0 : 1;
-              const float* pp = a.partials + ((ww * 2 + sl) * 32 + lane) * (4 * NT);
+            for (int nt = 0; nt < NT; ++nt) {
+              acc[nt][0] = __fmaf_rn(sc.x, tmp[nt][0], acc[nt][0]);
+              acc[nt][1] = __fmaf_rn(sc.x, tmp[nt][1], acc[nt][1]);
+              acc[nt][2] = __fmaf_rn(sc.y, tmp[nt][2], acc[nt][2]);
+              acc[nt][3] = __fmaf_rn(sc.y, tmp[nt][3], acc[nt][3]);
 #pragma unroll
-              for (int nt = 0; nt < NT; ++nt) {
-                float4 v = __ldcg(reinterpret_cast<const float4*>(pp + 4 * nt));
-                sum[nt][0] += v.x;
-                sum[nt][1] += v.y;
-                sum[nt][2] += v.z;
-                sum[nt][3] += v.w;
-              }
+              for (int q = 0; q < 4; ++q) tmp[nt][q] = 0.f;
             }
-            epilogue<NT>(a, tile, sum, lane);
-            if (lane == 0) a.counters[tile] = 0;
+          }
+        } else {
+          const uint2 sb = reinterpret_cast<const uint2*>(sst)[su * 8 + g];
+          const __half2 s01 = u32_as_h2(sb.x), s23 = u32_as_h2(sb.y);
+          const __half2 sg = __half2half2(__low2half(s01)), bg = __half2half2(__high2half(s01));
+          const __half2 sg8 = __half2half2(__low2half(s23)), bg8 = __half2half2(__high2half(s23));
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            uint32_t af[4];
+            unpack_word<0>(words[jj], af);
+            // w = fp16(q * s + b): the reference's dequantized fp16 weight
+            af[0] = h2_as_u32(__hfma2(u32_as_h2(af[0]), sg, bg));
+            af[1] = h2_as_u32(__hfma2(u32_as_h2(af[1]), sg8, bg8));
+            af[2] = h2_as_u32(__hfma2(u32_as_h2(af[2]), sg, bg));
+            af[3] = h2_as_u32(__hfma2(u32_as_h2(af[3]), sg8, bg8));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+              mma_16816(acc[nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], acc[nt]);
           }
         }
-        first_seg = false;
+      }
+      __syncwarp();
+      issue();
+      ++ci;
+      kb0 += n;
+    }
+    // CTA reduction of the 4 warps' fragments, in warp order
+    float* my = red + ((size_t)wid * 32 + lane) * (4 * NT);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      *reinterpret_cast<float4*>(my + 4 * nt) = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+    __syncthreads();
+    if (wid == 0) {
+      float sum[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sum[nt][q] = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float* pw = red + ((size_t)w * 32 + lane) * (4 * NT);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float4 v = *reinterpret_cast<const float4*>(pw + 4 * nt);
+          sum[nt][0] += v.x;
+          sum[nt][1] += v.y;
+          sum[nt][2] += v.z;
+          sum[nt][3] += v.w;
+        }
+      }
+      const bool complete = t * a.upt >= U0 && (t + 1) * a.upt <= U1;
+      if (complete) {
+        epilogue<NT>(a, t, sum, lane);
+      } else {
+        const int slot = (t == t_first) ? 0 : 1;
+        float* p = a.partials + ((size_t)(c * 2 + slot) * 32 + lane) * (4 * NT);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
+          *reinterpret_cast<float4*>(p + 4 * nt) = make_float4(sum[nt][0], sum[nt][1], sum[nt][2], sum[nt][3]);
+        __threadfence();
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(a.counters + t, 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        const int cf = cta_of_unit((long long)t * a.upt, a.U, a.C);
+        const int cl = cta_of_unit((long long)(t + 1) * a.upt - 1, a.U, a.C);
+        if (old == (int)(cl - cf)) {  // last contributor: reduce in CTA order
+          __threadfence();
+          float tot[NT][4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) acc[nt][q] = 0.f;
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) tot[nt][q] = 0.f;
+          for (int cc0 = cf; cc0 <= cl; cc0 += 4) {
+            float4 v[4][NT];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {  // independent loads, all in flight
+              const int cc = cc0 + u;
+              if (cc > cl) continue;
+              const int sl = (cta_start(cc, a.U, a.C) / a.upt == t) ? 0 : 1;
+              const float* pp = a.partials + ((size_t)(cc * 2 + sl) * 32 + lane) * (4 * NT);
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) v[u][nt] = __ldcg(reinterpret_cast<const float4*>(pp + 4 * nt));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              if (cc0 + u > cl) continue;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                tot[nt][0] += v[u][nt].x;
+                tot[nt][1] += v[u][nt].y;
+                tot[nt][2] += v[u][nt].z;
+                tot[nt][3] += v[u][nt].w;
+              }
+            }
+          }
+          epilogue<NT>(a, t, tot, lane);
+          if (lane == 0) a.counters[t] = 0;
+        }
       }
     }
-    __syncwarp();
-    issue(it + kStages);
+    __syncthreads();  // red[] reuse
   }
 }
 
 // ------------------------------------------------------------------ host
 static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 static int nt_for(int M) { return M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; }
-static long long max_warps() { return (long long)num_sms() * 2 * kWarpsPerCta; }
+static long long max_ctas() { return (long long)num_sms() * kCtasPerSm; }
 static constexpr size_t kSmemLimit = 227 * 1024;
-static constexpr size_t kXsLimit = kSmemLimit - kWarpsPerCta * kWarpRing - 1024;
+static constexpr size_t kRingBytes = (size_t)kWarps * kWarpRing;
+static size_t red_bytes(int NT) { return (size_t)kWarps * 32 * 4 * NT * 4 + 64; }
+// staged x is kept small so that two GEMV grids fit on an SM at once (the
+// next kernel prefetches its weights under PDL while this one finishes)
+static constexpr size_t kXsLimit = 64 * 1024;
 
 template <int NT, bool SYM, int GB, bool XS>
 static cudaError_t launch_one(const GemmArgs& ga, int ctas, int threads, size_t smem, cudaStream_t s, bool pdl) {
@@ -663,7 +744,7 @@ constexpr size_t kPartialsOff = kCountersOff + kMaxTiles * 4;
 
 size_t qgemm_workspace(int N, int M) {
   (void)N;
-  return kPartialsOff + (size_t)2 * max_warps() * 32 * 4 * nt_for(M) * sizeof(float);
+  return kPartialsOff + (size_t)2 * max_ctas() * 32 * 4 * nt_for(M) * sizeof(float);
 }
 
 int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
@@ -677,6 +758,8 @@ int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
                 "qgemm: weights and scales must be 16-byte aligned");
   AXB_CHECK_ARG(d->ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(d->x) & 15) == 0,
                 "qgemm: x must be 16-byte aligned with ldx %% 8 == 0");
+  AXB_CHECK_ARG(!d->norm_w || (reinterpret_cast<uintptr_t>(d->norm_w) & 15) == 0,
+                "qgemm: norm weight must be 16-byte aligned");
   AXB_CHECK_ARG(!d->gate_up_interleave || d->N % 16 == 0, "qgemm: gate/up interleave needs N %% 16 == 0");
   AXB_CHECK_ARG(d->epilogue != AXB_EPI_SWIGLU || d->gate_up_interleave, "qgemm: SWIGLU needs interleaved rows");
   AXB_CHECK_ARG(d->workspace && d->workspace_bytes >= qgemm_workspace(d->N, d->M),
@@ -692,6 +775,8 @@ int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
   ga.GB = d->group / 64;
   ga.upt = d->K / d->group;
   const int n_tiles = (d->N + 15) / 16;
+  AXB_CHECK_ARG((size_t)n_tiles <= kMaxTiles && (long long)n_tiles * (d->K / 64) < (1ll << 30),
+                "qgemm: matrix too large (%d x %d)", d->N, d->K);
   ga.U = (long long)n_tiles * ga.upt;
   ga.x = reinterpret_cast<const __half*>(d->x);
   ga.ldx = d->ldx;
@@ -702,31 +787,20 @@ int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
   ga.bias = reinterpret_cast<const __half*>(d->bias);
   ga.epi = d->epilogue;
   ga.gu = d->gate_up_interleave;
-  AXB_CHECK_ARG((size_t)n_tiles <= kMaxTiles, "qgemm: N too large (%d rows)", d->N);
   char* ws = reinterpret_cast<char*>(d->workspace);
   ga.err = reinterpret_cast<int*>(ws);
   ga.counters = reinterpret_cast<int*>(ws + kCountersOff);
   ga.partials = reinterpret_cast<float*>(ws + kPartialsOff);
-  // grid: persistent, every warp owns >= 1 quantization group
-  long long wt = std::min<long long>(max_warps(), ga.U);
-  int threads = kWarpsPerCta * 32;
-  int ctas;
-  if (wt >= kWarpsPerCta) {
-    ctas = (int)(wt / kWarpsPerCta);
-    wt = (long long)ctas * kWarpsPerCta;
-  } else {
-    ctas = 1;
-    threads = (int)wt * 32;
-  }
-  ga.Wt = wt;
-  const int pad = 8;
-  size_t xsb = round_up((size_t)d->M * (d->K + pad) * sizeof(__half), 128);
+  // persistent grid: kCtasPerSm CTAs per SM, every CTA owns >= 1 group
+  ga.C = std::min<long long>(max_ctas(), ga.U);
   const int nt = nt_for(d->M);
-  bool xs = nt <= 4 && xsb <= kXsLimit;
+  const size_t xsb = round_up((size_t)d->M * (d->K + 8) * sizeof(__half), 128);
+  const bool xs = nt <= 4 && (d->norm_w != nullptr || xsb <= 16 * 1024) && xsb <= kXsLimit;
   AXB_CHECK_ARG(xs || !d->norm_w, "qgemm: fused RMSNorm needs M <= 32 and M*K*2 <= %zu bytes", kXsLimit);
-  ga.xs_stride = xs ? d->K + pad : 0;
+  ga.xs_stride = xs ? d->K + 8 : 0;
   ga.xs_bytes = xs ? (int)xsb : 0;
-  size_t smem = (size_t)ga.xs_bytes + (size_t)(threads / 32) * kWarpRing;
+  const size_t smem = (size_t)ga.xs_bytes + kRingBytes + red_bytes(nt);
+  const int ctas = (int)ga.C, threads = kWarps * 32;
   const bool sym = d->fmt == AXB_W_Q4T_SYM;
   cudaError_t e;
   switch (nt) {

@@ -24,6 +24,13 @@ bool qgemm_can_fuse_norm(int M, int K);
 size_t qgemm_workspace(int N, int M);
 int rope_kv_write(const axb_kv_write_desc* d, cudaStream_t s, bool pdl);
 int attention(const axb_attn_desc* d, cudaStream_t s);
+struct DecodeFuse {
+  const __half* qkv;
+  const float* rope;
+  int rope_len;
+};
+int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s);
+int attn_prepare();
 size_t attn_workspace(int B, int n_head, int head_dim, int max_splits);
 int decode_max_splits(int B, int n_kv_head);
 int rmsnorm(const __half* x, const float* w, int M, int K, float eps, __half* out, cudaStream_t s);
@@ -45,24 +52,104 @@ __global__ void set_params_kernel(StepParams sp, int32_t* params, uint64_t* mask
   }
 }
 
+// dequant_q8_rows (quant.py:132-163) for the step's tokens; grid (rows, K/256):
+// each thread produces 4 consecutive dims from one 32-bit word.
 __global__ void embed_q8_kernel(const uint32_t* __restrict__ w, const __half* __restrict__ sb,
                                 const int32_t* __restrict__ tok, int K, int V, __half* __restrict__ out,
                                 int* __restrict__ err) {
   pdl_wait();
   const int i = blockIdx.x;
   const int r = tok[i];
+  const int k = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
+  if (k >= K) return;
+  __half* o = out + (size_t)i * K + k;
   if (r < 0 || r >= V) {  // out-of-vocabulary id: zero row, flag the error
-    for (int k = threadIdx.x; k < K; k += blockDim.x) out[(size_t)i * K + k] = __float2half_rn(0.f);
-    if (threadIdx.x == 0) atomicExch(err, AXB_EINVAL);
+    o[0] = o[1] = o[2] = o[3] = __float2half_rn(0.f);
+    if (k == 0) atomicExch(err, AXB_EINVAL);
     return;
   }
-  for (int k = threadIdx.x; k < K; k += blockDim.x) {
-    uint32_t word = w[(size_t)r * (K / 4) + k / 4];
-    int q = (word >> (8 * (k & 3))) & 0xFF;
-    const __half* p = sb + ((size_t)r * (K / 64) + k / 64) * 2;
-    float v = __fadd_rn(__fmul_rn((float)q, __half2float(p[0])), __half2float(p[1]));
-    out[(size_t)i * K + k] = __float2half_rn(v);
+  const uint32_t word = w[(size_t)r * (K / 4) + k / 4];
+  const __half2 p = reinterpret_cast<const __half2*>(sb)[(size_t)r * (K / 64) + k / 64];
+  const float s = __low2float(p), bi = __high2float(p);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    o[j] = __float2half_rn(__fadd_rn(__fmul_rn((float)((word >> (8 * j)) & 0xFF), s), bi));
+}
+
+// Greedy argmax over the vocabulary (torch.argmax: first index of the max),
+// split over many CTAs; the last CTA of a row combines the partials in order.
+__global__ void argmax_part_kernel(const __half* __restrict__ x, int n, int ld, int chunk, float* __restrict__ pv,
+                                   int* __restrict__ pi, int* __restrict__ cnt, int32_t* __restrict__ out) {
+  pdl_wait();
+  const int part = blockIdx.x, row = blockIdx.y, nparts = gridDim.x;
+  const __half* xr = x + (size_t)row * ld;
+  const int k0 = part * chunk, k1 = min(n, k0 + chunk);
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int k = k0 + threadIdx.x * 8; k < k1; k += blockDim.x * 8) {
+    if (k + 8 <= k1 && ((((uintptr_t)(xr + k)) & 15) == 0)) {
+      uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+      const __half* h = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float f = __half2float(h[j]);
+        if (f > best) {
+          best = f;
+          bi = k + j;
+        }
+      }
+    } else {
+      for (int j = k; j < min(k + 8, k1); ++j) {
+        float f = __half2float(xr[j]);
+        if (f > best) {
+          best = f;
+          bi = j;
+        }
+      }
+    }
   }
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ int last;
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
+        best = sv[w];
+        bi = si[w];
+      }
+    pv[row * nparts + part] = best;
+    pi[row * nparts + part] = bi;
+    __threadfence();
+    last = atomicAdd(cnt + row, 1) == nparts - 1;
+  }
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  float b = -INFINITY;
+  int id = 0x7fffffff;
+  for (int p = 0; p < nparts; ++p) {  // parts in index order: strict > keeps the lowest index
+    float v = __ldcg(pv + row * nparts + p);
+    int ii = __ldcg(pi + row * nparts + p);
+    if (v > b || (v == b && ii < id)) {
+      b = v;
+      id = ii;
+    }
+  }
+  out[row] = id == 0x7fffffff ? 0 : id;
+  cnt[row] = 0;
 }
 
 // final-norm hidden state in fp32 (the reference's x_norm / get_last_norm)
@@ -93,8 +180,11 @@ __global__ void rmsnorm_f32_kernel(const __half* __restrict__ x, const float* __
 
 static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
+constexpr int kArgmaxParts = 256;
+
 struct Layout {
   size_t tokens, params, masks, depths, x, h, qkv, q, attn, sw, logits, amax, xnorm, gemm_ws, attn_ws, total;
+  size_t am_v, am_i, am_cnt;
   size_t gemm_ws_bytes, attn_ws_bytes;
 };
 
@@ -122,6 +212,9 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.logits = take(rows * (size_t)c.vocab * 2);
   L.amax = take(rows * 4);
   L.xnorm = take(rows * (size_t)c.d_model * 4);
+  L.am_v = take(rows * kArgmaxParts * 4);
+  L.am_i = take(rows * kArgmaxParts * 4);
+  L.am_cnt = take(rows * 4);
   int m = (int)std::min<size_t>(rows, 64);
   size_t g = 0;
   for (int n : {(int)qkv_dim, c.d_model, 2 * c.ffn, c.vocab}) g = std::max(g, qgemm_workspace(n, m));
@@ -199,7 +292,8 @@ struct Runner {
     const int rows = B * T;
     const int d = c.d_model, hd = c.head_dim, Hq = c.n_head, Hkv = c.n_kv_head;
     const int qkv_dim = (Hq + 2 * Hkv) * hd, qd = Hq * hd;
-    cudaError_t e = launch_pdl(embed_q8_kernel, dim3(rows), dim3(256), 0, st, true, (const uint32_t*)emb_w,
+    cudaError_t e = launch_pdl(embed_q8_kernel, dim3(rows, (d / 4 + 127) / 128), dim3(128), 0, st, true,
+                               (const uint32_t*)emb_w,
                                (const __half*)emb_s, (const int32_t*)buf<int32_t>(L.tokens), d, c.vocab,
                                buf<__half>(L.x), buf<int>(L.params) + 4);
     if (e != cudaSuccess) return cuda_status(e, "embed launch");
@@ -228,8 +322,10 @@ struct Runner {
       kw.k_scale = (uint16_t*)ks[l];
       kw.v_scale = (uint16_t*)vs[l];
       kw.k_is_fp32 = 1;
-      rc = rope_kv_write(&kw, st, true);
-      if (rc) return rc;
+      if (tree) {  // decode (T = 1) fuses RoPE + KV write into the attention kernel
+        rc = rope_kv_write(&kw, st, true);
+        if (rc) return rc;
+      }
       axb_attn_desc ad = {};
       ad.kv_type = c.kv_type;
       ad.kv_group = c.kv_group;
@@ -254,7 +350,12 @@ struct Runner {
       ad.workspace = buf<void>(L.attn_ws);
       ad.workspace_bytes = L.attn_ws_bytes;
       ad.pdl = 1;
-      rc = attention(&ad, st);
+      if (tree) {
+        rc = attention(&ad, st);
+      } else {
+        DecodeFuse f = {buf<__half>(L.qkv), rope, c.rope_len};
+        rc = attention_fused(&ad, f, st);
+      }
       if (rc) return rc;
       rc = gemv(o_w[l], o_s[l], c.wfmt, c.group, d, qd, rows, buf<__half>(L.attn), qd, buf<void>(L.x), d, nullptr,
                 nullptr, AXB_EPI_RESIDUAL, 0, st);
@@ -274,7 +375,12 @@ struct Runner {
                      d, c.eps, buf<float>(L.xnorm));
       if (e != cudaSuccess) return cuda_status(e, "final norm launch");
     }
-    return argmax(buf<__half>(L.logits), rows, c.vocab, c.vocab, buf<int32_t>(L.amax), st);
+    const int chunk = ((c.vocab + kArgmaxParts - 1) / kArgmaxParts + 7) / 8 * 8;
+    const int parts = (c.vocab + chunk - 1) / chunk;
+    e = launch_pdl(argmax_part_kernel, dim3(parts, rows), dim3(128), 0, st, true, (const __half*)buf<__half>(L.logits),
+                   c.vocab, c.vocab, chunk, buf<float>(L.am_v), buf<int>(L.am_i), buf<int>(L.am_cnt),
+                   buf<int32_t>(L.amax));
+    return cuda_status(e, "argmax launch");
   }
 };
 
@@ -303,6 +409,7 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   Layout L = make_layout(c);
   AXB_CHECK_ARG(ws_bytes >= L.total, "runner_create: workspace %zu < %zu bytes", ws_bytes, L.total);
   if (int rc = qgemm_prepare()) return rc;
+  if (int rc = attn_prepare()) return rc;
   Runner* r = new Runner();
   r->c = c;
   r->L = L;
