@@ -319,7 +319,7 @@ struct GemmArgs {
 constexpr int kWarps = 4;           // warps per CTA (K-split of each tile)
 constexpr int kCtasPerSm = 4;       // resident CTAs per SM the grid is sized for
 constexpr int kCH = 4;              // k-blocks (512 B each) per pipeline stage
-constexpr int kStages = 2;          // stages per warp
+constexpr int kStages = 3;          // stages per warp
 constexpr int kStageW = kCH * 512;  // weight bytes per stage
 constexpr int kStageS = kCH * 64;   // scale bytes per stage (max: affine, one group per k-block)
 constexpr int kWarpRing = kStages * (kStageW + kStageS) + kStages * 8;
@@ -512,6 +512,14 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 8 : (NT == 2 ? 5 : 3)) 
 
   int ci = 0;  // stages consumed by this warp
   bool failed = false;
+  // B-fragment rows: token nt*8 + g, clamped to a valid row (columns >= M are
+  // computed but never stored, so no per-lane branch is needed)
+  const __half* xrow[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int nn = min(nt * 8 + g, a.M - 1);
+    xrow[nt] = (XS ? xs + (size_t)nn * a.xs_stride : a.x + (size_t)nn * a.ldx) + 16 * t4;
+  }
   for (int t = t_first; t <= t_last; ++t) {
     int kb_lo, kb_hi;
     warp_chunk(a.upt, GB, U0, U1, t, wid, kb_lo, kb_hi);
@@ -524,77 +532,70 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 8 : (NT == 2 ? 5 : 3)) 
     for (int kb0 = kb_lo; kb0 < kb_hi && !failed;) {
       const int st = ci % kStages;
       if (!mbar_wait(bars + st, (uint32_t)((ci / kStages) & 1), kWaitLimit)) {
-        // record the failure; the remaining copy (if any) gets a bounded wait
+        // record the failure; copies still in flight get a bounded wait
         if (lane == 0) atomicExch(a.err, AXB_ETIMEOUT);
-        mbar_wait(bars + ((ci + 1) % kStages), (uint32_t)(((ci + 1) / kStages) & 1), kWaitLimit);
+        for (int k2 = 1; k2 < kStages; ++k2)
+          mbar_wait(bars + ((ci + k2) % kStages), (uint32_t)(((ci + k2) / kStages) & 1), kWaitLimit);
         failed = true;
         break;
       }
       const int n = min(kCH, kb_hi - kb0);
-      const uint4* wst = reinterpret_cast<const uint4*>(ring + st * kStageW);
+      const uint4* wst = reinterpret_cast<const uint4*>(ring + st * kStageW) + lane;
       const char* sst = ring + kStages * kStageW + st * kStageS;
-      const int unit0 = kb0 / GB;
-      for (int j = 0; j < n; ++j) {
-        const int kbi = kb0 + j;
-        const int kb = kbi - t * a.KB;
-        const uint4 cur = wst[j * 32 + lane];
-        const int su = kbi / GB - unit0;
-        uint32_t bf[NT][8];
+      const int kbt = kb0 - t * a.KB;  // k-block of the stage within the tile
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const int nn = nt * 8 + g;
-          if (nn < a.M) {
-            const __half* src = XS ? xs + (size_t)nn * a.xs_stride + kb * 64 + 16 * t4
-                                   : a.x + (size_t)nn * a.ldx + kb * 64 + 16 * t4;
-            uint4 v0 = *reinterpret_cast<const uint4*>(src);
-            uint4 v1 = *reinterpret_cast<const uint4*>(src + 8);
+      for (int j = 0; j < kCH; ++j) {
+        if (j < n) {
+          const uint4 cur = wst[j * 32];
+          uint32_t bf[NT][8];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint4* xp = reinterpret_cast<const uint4*>(xrow[nt] + (kbt + j) * 64);
+            const uint4 v0 = xp[0], v1 = xp[1];
             bf[nt][0] = v0.x; bf[nt][1] = v0.y; bf[nt][2] = v0.z; bf[nt][3] = v0.w;
             bf[nt][4] = v1.x; bf[nt][5] = v1.y; bf[nt][6] = v1.z; bf[nt][7] = v1.w;
-          } else {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) bf[nt][q] = 0u;
           }
-        }
-        const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
-        if (SYM) {
+          const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
+          if (SYM) {
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            uint32_t af[4];
-            unpack_word<8>(words[jj], af);
+            for (int jj = 0; jj < 4; ++jj) {
+              uint32_t af[4];
+              unpack_word<8>(words[jj], af);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-              mma_16816(tmp[nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], tmp[nt]);
-          }
-          if ((kb % GB) == GB - 1) {  // group complete: apply the per-row scales
-            const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[su * 8 + g];
-            const float2 sc = __half22float2(u32_as_h2(sp));
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              acc[nt][0] = __fmaf_rn(sc.x, tmp[nt][0], acc[nt][0]);
-              acc[nt][1] = __fmaf_rn(sc.x, tmp[nt][1], acc[nt][1]);
-              acc[nt][2] = __fmaf_rn(sc.y, tmp[nt][2], acc[nt][2]);
-              acc[nt][3] = __fmaf_rn(sc.y, tmp[nt][3], acc[nt][3]);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) tmp[nt][q] = 0.f;
+              for (int nt = 0; nt < NT; ++nt)
+                mma_16816(tmp[nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], tmp[nt]);
             }
-          }
-        } else {
-          const uint2 sb = reinterpret_cast<const uint2*>(sst)[su * 8 + g];
-          const __half2 s01 = u32_as_h2(sb.x), s23 = u32_as_h2(sb.y);
-          const __half2 sg = __half2half2(__low2half(s01)), bg = __half2half2(__high2half(s01));
-          const __half2 sg8 = __half2half2(__low2half(s23)), bg8 = __half2half2(__high2half(s23));
+            if (GB == 1 || (j & 1)) {  // group complete (stages start on a group boundary)
+              const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[(j / GB) * 8 + g];
+              const float2 sc = __half22float2(u32_as_h2(sp));
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            uint32_t af[4];
-            unpack_word<0>(words[jj], af);
-            // w = fp16(q * s + b): the reference's dequantized fp16 weight
-            af[0] = h2_as_u32(__hfma2(u32_as_h2(af[0]), sg, bg));
-            af[1] = h2_as_u32(__hfma2(u32_as_h2(af[1]), sg8, bg8));
-            af[2] = h2_as_u32(__hfma2(u32_as_h2(af[2]), sg, bg));
-            af[3] = h2_as_u32(__hfma2(u32_as_h2(af[3]), sg8, bg8));
+              for (int nt = 0; nt < NT; ++nt) {
+                acc[nt][0] = __fmaf_rn(sc.x, tmp[nt][0], acc[nt][0]);
+                acc[nt][1] = __fmaf_rn(sc.x, tmp[nt][1], acc[nt][1]);
+                acc[nt][2] = __fmaf_rn(sc.y, tmp[nt][2], acc[nt][2]);
+                acc[nt][3] = __fmaf_rn(sc.y, tmp[nt][3], acc[nt][3]);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-              mma_16816(acc[nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], acc[nt]);
+                for (int q = 0; q < 4; ++q) tmp[nt][q] = 0.f;
+              }
+            }
+          } else {
+            const uint2 sb = reinterpret_cast<const uint2*>(sst)[(j / GB) * 8 + g];
+            const __half2 s01 = u32_as_h2(sb.x), s23 = u32_as_h2(sb.y);
+            const __half2 sg = __half2half2(__low2half(s01)), bg = __half2half2(__high2half(s01));
+            const __half2 sg8 = __half2half2(__low2half(s23)), bg8 = __half2half2(__high2half(s23));
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              uint32_t af[4];
+              unpack_word<0>(words[jj], af);
+              // w = fp16(q * s + b): the reference's dequantized fp16 weight
+              af[0] = h2_as_u32(__hfma2(u32_as_h2(af[0]), sg, bg));
+              af[1] = h2_as_u32(__hfma2(u32_as_h2(af[1]), sg8, bg8));
+              af[2] = h2_as_u32(__hfma2(u32_as_h2(af[2]), sg, bg));
+              af[3] = h2_as_u32(__hfma2(u32_as_h2(af[3]), sg8, bg8));
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+                mma_16816(acc[nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], acc[nt]);
+            }
           }
         }
       }

@@ -10,6 +10,7 @@
 // is captured once into a CUDA graph (kernels chained with programmatic
 // dependent launch) and replayed; per-step positions live in a device buffer
 // written by one tiny kernel before each replay.
+#include <cstdlib>
 #include <map>
 #include <tuple>
 #include <vector>
@@ -231,6 +232,7 @@ static Layout make_layout(const axb_model_cfg& c) {
 
 struct Runner {
   axb_model_cfg c;
+  bool pdl = true;  // chain kernels with programmatic dependent launch (env AXB_PDL=0 disables)
   Layout L;
   char* ws;
   const void *emb_w, *emb_s, *lm_w, *lm_s;
@@ -270,7 +272,7 @@ struct Runner {
       d.gate_up_interleave = gu;
       d.workspace = buf<void>(L.gemm_ws);
       d.workspace_bytes = L.gemm_ws_bytes;
-      d.pdl = 1;
+      d.pdl = pdl ? 1 : 0;
       int rc = qgemm(&d, st);
       if (rc) return rc;
     }
@@ -292,7 +294,7 @@ struct Runner {
     const int rows = B * T;
     const int d = c.d_model, hd = c.head_dim, Hq = c.n_head, Hkv = c.n_kv_head;
     const int qkv_dim = (Hq + 2 * Hkv) * hd, qd = Hq * hd;
-    cudaError_t e = launch_pdl(embed_q8_kernel, dim3(rows, (d / 4 + 127) / 128), dim3(128), 0, st, true,
+    cudaError_t e = launch_pdl(embed_q8_kernel, dim3(rows, (d / 4 + 127) / 128), dim3(128), 0, st, pdl,
                                (const uint32_t*)emb_w,
                                (const __half*)emb_s, (const int32_t*)buf<int32_t>(L.tokens), d, c.vocab,
                                buf<__half>(L.x), buf<int>(L.params) + 4);
@@ -323,7 +325,7 @@ struct Runner {
       kw.v_scale = (uint16_t*)vs[l];
       kw.k_is_fp32 = 1;
       if (tree) {  // decode (T = 1) fuses RoPE + KV write into the attention kernel
-        rc = rope_kv_write(&kw, st, true);
+        rc = rope_kv_write(&kw, st, pdl);
         if (rc) return rc;
       }
       axb_attn_desc ad = {};
@@ -349,7 +351,7 @@ struct Runner {
       ad.dev_params = buf<int32_t>(L.params);
       ad.workspace = buf<void>(L.attn_ws);
       ad.workspace_bytes = L.attn_ws_bytes;
-      ad.pdl = 1;
+      ad.pdl = pdl ? 1 : 0;
       if (tree) {
         rc = attention(&ad, st);
       } else {
@@ -371,13 +373,13 @@ struct Runner {
                        c.lm_fmt, c.lm_group, st);
     if (rc) return rc;
     if (want_norm) {
-      e = launch_pdl(rmsnorm_f32_kernel, dim3(rows), dim3(256), 0, st, true, (const __half*)buf<__half>(L.x), ln_f,
+      e = launch_pdl(rmsnorm_f32_kernel, dim3(rows), dim3(256), 0, st, pdl, (const __half*)buf<__half>(L.x), ln_f,
                      d, c.eps, buf<float>(L.xnorm));
       if (e != cudaSuccess) return cuda_status(e, "final norm launch");
     }
     const int chunk = ((c.vocab + kArgmaxParts - 1) / kArgmaxParts + 7) / 8 * 8;
     const int parts = (c.vocab + chunk - 1) / chunk;
-    e = launch_pdl(argmax_part_kernel, dim3(parts, rows), dim3(128), 0, st, true, (const __half*)buf<__half>(L.logits),
+    e = launch_pdl(argmax_part_kernel, dim3(parts, rows), dim3(128), 0, st, pdl, (const __half*)buf<__half>(L.logits),
                    c.vocab, c.vocab, chunk, buf<float>(L.am_v), buf<int>(L.am_i), buf<int>(L.am_cnt),
                    buf<int32_t>(L.amax));
     return cuda_status(e, "argmax launch");
@@ -412,6 +414,7 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   if (int rc = attn_prepare()) return rc;
   Runner* r = new Runner();
   r->c = c;
+  if (const char* ev = getenv("AXB_PDL")) r->pdl = atoi(ev) != 0;
   r->L = L;
   r->ws = reinterpret_cast<char*>(ws);
   r->emb_w = p->emb_w;
