@@ -322,7 +322,11 @@ constexpr int kCH = 4;              // k-blocks (512 B each) per pipeline stage
 constexpr int kStages = 3;          // stages per warp
 constexpr int kStageW = kCH * 512;  // weight bytes per stage
 constexpr int kStageS = kCH * 64;   // scale bytes per stage (max: affine, one group per k-block)
-constexpr int kWarpRing = kStages * (kStageW + kStageS) + kStages * 8;
+// per-warp ring: stages of weights, stages of scales, mbarriers; the stride is
+// rounded to 128 B so every warp's bulk-copy destinations stay 16-B aligned
+constexpr int kWarpRing = (kStages * (kStageW + kStageS) + kStages * 8 + 127) / 128 * 128;
+static_assert(kStageW % 16 == 0 && kStageS % 16 == 0 && kWarpRing % 128 == 0, "bulk-copy alignment");
+static_assert((kStages * (kStageW + kStageS)) % 8 == 0, "mbarrier alignment");
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 __device__ __forceinline__ int cta_start(long long c, long long U, long long C) { return (int)(c * U / C); }
