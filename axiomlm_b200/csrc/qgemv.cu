@@ -314,6 +314,7 @@ struct GemmArgs {
   int* err;
   int xs_stride;  // smem row stride (halves); 0 = read x from global
   int xs_bytes;   // bytes of the staged-x region at the start of shared memory
+  int early_trigger;  // release the dependent launch right after staging x
 };
 
 constexpr int kWarps = 4;           // warps per CTA (K-split of each tile)
@@ -464,7 +465,7 @@ __device__ __forceinline__ void warp_chunk(int upt, int GB, int U0, int U1, int 
 }
 
 template <int NT, bool SYM, int GB, bool XS>
-__global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 8 : (NT == 2 ? 5 : 3)) qgemm_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 7 : (NT == 2 ? 5 : 3)) qgemm_kernel(const GemmArgs a) {
   extern __shared__ __align__(128) char smem[];
   __half* xs = reinterpret_cast<__half*>(smem);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -512,27 +513,45 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 8 : (NT == 2 ? 5 : 3)) 
     stage_x(a, xs, nred);
     __syncthreads();
   }
-  pdl_trigger();
+  if (a.early_trigger) pdl_trigger();
 
   int ci = 0;  // stages consumed by this warp
   bool failed = false;
   // B-fragment rows: token nt*8 + g, clamped to a valid row (columns >= M are
   // computed but never stored, so no per-lane branch is needed)
-  const __half* xrow[NT];
+  const uint4* xrow[NT];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int nn = min(nt * 8 + g, a.M - 1);
-    xrow[nt] = (XS ? xs + (size_t)nn * a.xs_stride : a.x + (size_t)nn * a.ldx) + 16 * t4;
+    xrow[nt] = reinterpret_cast<const uint4*>((XS ? xs + (size_t)nn * a.xs_stride : a.x + (size_t)nn * a.ldx) +
+                                              16 * t4);
   }
+  // independent accumulation chains per group (the mma results of one
+  // k-block's 4 words go to different registers, so consecutive HMMAs do not
+  // wait on each other); summed when the group's scale is applied
+  constexpr int CH = NT == 1 ? 4 : (NT == 2 ? 2 : 1);
   for (int t = t_first; t <= t_last; ++t) {
     int kb_lo, kb_hi;
     warp_chunk(a.upt, GB, U0, U1, t, wid, kb_lo, kb_hi);
     float acc[NT][4];
-    float tmp[NT][4];
+    float tmp[CH][NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[nt][q] = tmp[nt][q] = 0.f;
+      for (int q = 0; q < 4; ++q) {
+        acc[nt][q] = 0.f;
+#pragma unroll
+        for (int c2 = 0; c2 < CH; ++c2) tmp[c2][nt][q] = 0.f;
+      }
+    // activation fragments of the next k-block, loaded one k-block ahead
+    uint4 xn[NT][2];
+    if (kb_lo < kb_hi) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        xn[nt][0] = xrow[nt][(kb_lo - t * a.KB) * 8];
+        xn[nt][1] = xrow[nt][(kb_lo - t * a.KB) * 8 + 1];
+      }
+    }
     for (int kb0 = kb_lo; kb0 < kb_hi && !failed;) {
       const int st = ci % kStages;
       if (!mbar_wait(bars + st, (uint32_t)((ci / kStages) & 1), kWaitLimit)) {
@@ -554,10 +573,15 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 8 : (NT == 2 ? 5 : 3)) 
           uint32_t bf[NT][8];
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            const uint4* xp = reinterpret_cast<const uint4*>(xrow[nt] + (kbt + j) * 64);
-            const uint4 v0 = xp[0], v1 = xp[1];
-            bf[nt][0] = v0.x; bf[nt][1] = v0.y; bf[nt][2] = v0.z; bf[nt][3] = v0.w;
-            bf[nt][4] = v1.x; bf[nt][5] = v1.y; bf[nt][6] = v1.z; bf[nt][7] = v1.w;
+            bf[nt][0] = xn[nt][0].x; bf[nt][1] = xn[nt][0].y; bf[nt][2] = xn[nt][0].z; bf[nt][3] = xn[nt][0].w;
+            bf[nt][4] = xn[nt][1].x; bf[nt][5] = xn[nt][1].y; bf[nt][6] = xn[nt][1].z; bf[nt][7] = xn[nt][1].w;
+          }
+          if (kb0 + j + 1 < kb_hi) {  // prefetch the next k-block's fragments
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              xn[nt][0] = xrow[nt][(kbt + j + 1) * 8];
+              xn[nt][1] = xrow[nt][(kbt + j + 1) * 8 + 1];
+            }
           }
           const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
           if (SYM) {
@@ -567,19 +591,27 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 8 : (NT == 2 ? 5 : 3)) 
               unpack_word<8>(words[jj], af);
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt)
-                mma_16816(tmp[nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], tmp[nt]);
+                mma_16816(tmp[jj % CH][nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], tmp[jj % CH][nt]);
             }
             if (GB == 1 || (j & 1)) {  // group complete (stages start on a group boundary)
               const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[(j / GB) * 8 + g];
               const float2 sc = __half22float2(u32_as_h2(sp));
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt) {
-                acc[nt][0] = __fmaf_rn(sc.x, tmp[nt][0], acc[nt][0]);
-                acc[nt][1] = __fmaf_rn(sc.x, tmp[nt][1], acc[nt][1]);
-                acc[nt][2] = __fmaf_rn(sc.y, tmp[nt][2], acc[nt][2]);
-                acc[nt][3] = __fmaf_rn(sc.y, tmp[nt][3], acc[nt][3]);
+                float s4[4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) tmp[nt][q] = 0.f;
+                for (int q = 0; q < 4; ++q) {
+                  float v = tmp[0][nt][q];
+#pragma unroll
+                  for (int c2 = 1; c2 < CH; ++c2) v += tmp[c2][nt][q];
+                  s4[q] = v;
+#pragma unroll
+                  for (int c2 = 0; c2 < CH; ++c2) tmp[c2][nt][q] = 0.f;
+                }
+                acc[nt][0] = __fmaf_rn(sc.x, s4[0], acc[nt][0]);
+                acc[nt][1] = __fmaf_rn(sc.x, s4[1], acc[nt][1]);
+                acc[nt][2] = __fmaf_rn(sc.y, s4[2], acc[nt][2]);
+                acc[nt][3] = __fmaf_rn(sc.y, s4[3], acc[nt][3]);
               }
             }
           } else {
@@ -598,7 +630,7 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 8 : (NT == 2 ? 5 : 3)) 
               af[3] = h2_as_u32(__hfma2(u32_as_h2(af[3]), sg8, bg8));
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt)
-                mma_16816(acc[nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], acc[nt]);
+                mma_16816(tmp[jj % CH][nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], tmp[jj % CH][nt]);
             }
           }
         }
@@ -607,6 +639,17 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 8 : (NT == 2 ? 5 : 3)) 
       issue();
       ++ci;
       kb0 += n;
+    }
+    if (!SYM) {  // affine: the chains carry scaled values already
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float v = tmp[0][nt][q];
+#pragma unroll
+          for (int c2 = 1; c2 < CH; ++c2) v += tmp[c2][nt][q];
+          acc[nt][q] = v;
+        }
     }
     // CTA reduction of the 4 warps' fragments, in warp order
     float* my = red + ((size_t)wid * 32 + lane) * (4 * NT);
@@ -792,6 +835,7 @@ int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
   ga.bias = reinterpret_cast<const __half*>(d->bias);
   ga.epi = d->epilogue;
   ga.gu = d->gate_up_interleave;
+  ga.early_trigger = d->pdl >= 2 ? 0 : 1;  // pdl == 2: dependent launch at exit only
   char* ws = reinterpret_cast<char*>(d->workspace);
   ga.err = reinterpret_cast<int*>(ws);
   ga.counters = reinterpret_cast<int*>(ws + kCountersOff);

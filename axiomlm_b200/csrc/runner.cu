@@ -233,6 +233,7 @@ static Layout make_layout(const axb_model_cfg& c) {
 struct Runner {
   axb_model_cfg c;
   bool pdl = true;  // chain kernels with programmatic dependent launch (env AXB_PDL=0 disables)
+  int pdl_mode = 1;  // AXB_PDL=2: programmatic edges, GEMVs release dependents only at exit
   Layout L;
   char* ws;
   const void *emb_w, *emb_s, *lm_w, *lm_s;
@@ -272,7 +273,7 @@ struct Runner {
       d.gate_up_interleave = gu;
       d.workspace = buf<void>(L.gemm_ws);
       d.workspace_bytes = L.gemm_ws_bytes;
-      d.pdl = pdl ? 1 : 0;
+      d.pdl = pdl ? pdl_mode : 0;
       int rc = qgemm(&d, st);
       if (rc) return rc;
     }
@@ -414,7 +415,10 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   if (int rc = attn_prepare()) return rc;
   Runner* r = new Runner();
   r->c = c;
-  if (const char* ev = getenv("AXB_PDL")) r->pdl = atoi(ev) != 0;
+  if (const char* ev = getenv("AXB_PDL")) {
+    r->pdl = atoi(ev) != 0;
+    r->pdl_mode = atoi(ev) == 2 ? 2 : 1;
+  }
   r->L = L;
   r->ws = reinterpret_cast<char*>(ws);
   r->emb_w = p->emb_w;

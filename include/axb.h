@@ -115,7 +115,8 @@ typedef struct {
   int gate_up_interleave;
   void* workspace; /* >= axb_qgemm_workspace_bytes(...), zeroed once */
   size_t workspace_bytes;
-  int pdl; /* launch with programmatic dependent launch */
+  int pdl; /* 1: programmatic dependent launch, dependents released after the
+              x staging; 2: dependents released at exit; 0: plain launch */
 } axb_qgemm_desc;
 
 size_t axb_qgemm_workspace_bytes(int N, int K, int M, int group);
