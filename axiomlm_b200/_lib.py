@@ -118,7 +118,7 @@ _SIGS = {
     "axb_rope_kv_write": (i32, [C.POINTER(KvWriteDesc), vp]),
     "axb_kv_quantize": (i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp]),
     "axb_kv_dequantize": (i32, [vp, vp, i32, i32, i32, i32, vp, vp]),
-    "axb_attn_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
+    "axb_attn_workspace_bytes": (sz, [i32, i32, i32, i32, i32, i32, i32]),
     "axb_attention": (i32, [C.POINTER(AttnDesc), vp]),
     "axb_compact_kv": (i32, [vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, i32, vp]),
     "axb_argmax": (i32, [vp, i32, i32, i32, vp, vp]),

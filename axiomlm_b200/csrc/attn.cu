@@ -241,15 +241,38 @@ struct DecodeFuse {
 };
 
 // Split-K flash decode, T = 1 per sequence.  grid (max_splits, Hkv, B), 128
-// threads.  A CTA owns one (sequence, kv head) and a token range; its K/V rows
-// (contiguous per head) are bulk-copied into shared memory in 64-token stages
-// -- issued before the PDL wait, since cached rows do not depend on the
-// preceding kernel -- and the n_rep q heads of the group share every tile.
-// With fusion, the CTA whose range holds the new slot rotates and quantizes
-// the new K/V row, writes it to the cache and patches its staged copy.
+// threads.  A CTA owns one (sequence, kv head) and a chunk of <= kMaxChunk
+// tokens.  Its K/V rows (contiguous per head) are bulk-copied into shared
+// memory in one go -- issued before the PDL wait, since cached rows do not
+// depend on the preceding kernel -- and the chunk is processed in a single
+// pass (scores, softmax, PV) by all n_rep q heads of the group.  With fusion,
+// the CTA whose chunk holds the new slot rotates and quantizes the new K/V
+// row, writes it to the cache and patches its staged copy.  Split partials
+// (O, m, l) are combined by the last CTA of the (sequence, head) in split
+// order, all splits loaded in parallel.
+constexpr int kMaxChunk = 256;
+
+__host__ __device__ inline int decode_chunk_cap(int kv_type, int hd) {
+  const int rb = kv_type == AXB_KV_F16 ? hd * 2 : (kv_type == AXB_KV_FP8 ? hd : hd / 2);
+  const int cap = 32768 / rb;  // K and V stages together <= 64 KB
+  return cap < kMaxChunk ? cap : kMaxChunk;
+}
+
+__host__ __device__ inline void decode_split(int active, int max_splits, int cap, int& nsplit, int& chunk) {
+  int ns = (active + cap - 1) / cap;
+  if (ns < max_splits) ns = max_splits;
+  chunk = (active + ns - 1) / ns;
+  chunk = (chunk + 15) / 16 * 16;
+  if (chunk > cap) chunk = cap;
+  ns = (active + chunk - 1) / chunk;
+  nsplit = ns;
+}
+
+constexpr int kMaxSplits = 256;
+
 template <int HD>
-__global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d, int max_splits, float* part_o,
-                                                          float* part_ml, int* counters, int* err,
+__global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d, int target_splits, int max_splits,
+                                                          float* part_o, float* part_ml, int* counters, int* err,
                                                           const DecodeFuse f) {
   constexpr int DPL = HD / 32;  // dims per lane in PV
   constexpr int EPT = HD / 16;  // threads per token in the score pass (16 elements each)
@@ -259,26 +282,27 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d,
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int active = d.dev_params ? d.dev_params[2] : d.active_len;
   const int wpos = d.dev_params ? d.dev_params[1] : d.write_pos;
-  const int nsplit = min(max_splits, max(1, (active + kDecTile - 1) / kDecTile));
+  const int cap = decode_chunk_cap(d.kv_type, HD);
+  int nsplit, chunk;
+  decode_split(active, target_splits, cap, nsplit, chunk);
   if (split >= nsplit) return;
-  const int chunk = (active + nsplit - 1) / nsplit;
-  const int t0 = split * chunk, t1 = min(active, t0 + chunk);
-  const int ntiles = (t1 - t0 + kDecTile - 1) / kDecTile;
+  const int t0 = split * chunk, t1 = min(active, t0 + chunk), nt = t1 - t0;
   const int hq0 = kvh * n_rep;
   const int rb = kv_row_bytes(d.kv_type, HD);
   const int G = d.kv_group, ng = HD / G;
   const bool quant = d.kv_type != AXB_KV_F16;
 
-  // shared memory carve-up
-  char* kst = sm;                              // [2][64][rb]
-  char* vst = kst + 2 * kDecTile * rb;         // [2][64][rb]
-  float* q_s = reinterpret_cast<float*>(sm + max(4 * kDecTile * rb, 4 * kMaxRep * HD * 4));  // [8][HD]
-  float* p_s = q_s + kMaxRep * HD;             // [8][64]
-  float* ks_s = p_s + kMaxRep * kDecTile;      // [64][ng <= 4] K scales of the current tile
-  float* vs_s = ks_s + kDecTile * 4;           // [64][ng]
-  float* ml_s = vs_s + kDecTile * 4;           // m[8], l[8], corr[8]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ml_s + 3 * kMaxRep + 8);
-  float* o_red = reinterpret_cast<float*>(sm);  // [4][8][HD], reuses the K/V stages at the end
+  // shared memory: K rows, V rows, q, probabilities, scales, softmax stats
+  char* kst = sm;                                   // [cap][rb]
+  char* vst = kst + (size_t)cap * rb;               // [cap][rb]
+  float* q_s = reinterpret_cast<float*>(vst + (size_t)cap * rb);  // [8][HD]
+  float* p_s = q_s + kMaxRep * HD;                  // [8][cap]
+  float* ks_s = p_s + kMaxRep * cap;                // [cap][ng]
+  float* vs_s = ks_s + cap * 4;                     // [cap][ng]
+  float* ml_s = vs_s + cap * 4;                     // m[8], l[8], scratch
+  float* coef = ml_s + 4 * kMaxRep;                 // [8][kMaxSplits] combine weights
+  uint64_t* bar = reinterpret_cast<uint64_t*>(coef + kMaxRep * kMaxSplits);
+  float* o_red = reinterpret_cast<float*>(sm);      // [4][8][HD], reuses the K/V rows at the end
 
   const size_t head_base = ((size_t)b * d.n_kv_head + kvh) * d.max_seq;
   const uint8_t* kc = reinterpret_cast<const uint8_t*>(d.k_cache) + head_base * rb;
@@ -287,27 +311,25 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d,
   const __half* vsc = quant ? reinterpret_cast<const __half*>(d.v_scale) + head_base * ng : nullptr;
 
   if (tid == 0) {
-    mbar_init(bars, 1);
-    mbar_init(bars + 1, 1);
+    mbar_init(bar, 1);
     fence_mbar_init();
-  }
-  __syncthreads();
-  auto issue = [&](int i) {  // thread 0: stage i % 2 <- tokens [t0 + 64 i, ...)
-    if (tid != 0 || i >= ntiles) return;
-    const int ts = t0 + i * kDecTile, n = min(kDecTile, t1 - ts), st = i & 1;
     fence_proxy_async();
-    mbar_expect_tx(bars + st, 2u * n * rb);
-    bulk_g2s(kst + st * kDecTile * rb, kc + (size_t)ts * rb, n * rb, bars + st);
-    bulk_g2s(vst + st * kDecTile * rb, vc + (size_t)ts * rb, n * rb, bars + st);
-  };
-  issue(0);
-  issue(1);
+    mbar_expect_tx(bar, 2u * nt * rb);
+    bulk_g2s(kst, kc + (size_t)t0 * rb, nt * rb, bar);
+    bulk_g2s(vst, vc + (size_t)t0 * rb, nt * rb, bar);
+  }
+  // scales of the chunk (plain loads; the new slot's is patched below)
+  if (quant)
+    for (int j = tid; j < nt * ng; j += 128) {
+      ks_s[j] = __half2float(ksc[(size_t)t0 * ng + j]);
+      vs_s[j] = __half2float(vsc[(size_t)t0 * ng + j]);
+    }
 
   pdl_wait();  // q / the new K,V row come from the preceding GEMV
 
   // ---- q (rotated in fp32 when fused) and the new K/V row
   const int qkv_dim = (d.n_head + 2 * d.n_kv_head) * HD;
-  float nk[DPL], nv[DPL];  // new K/V row (warp 0 / warp 1 of the covering CTA), lane-owned dims
+  float nkv[DPL];
   const bool covers_new = f.qkv != nullptr && wpos >= t0 && wpos < t1;
   if (f.qkv) {
     const __half* row = f.qkv + (size_t)b * qkv_dim;
@@ -324,22 +346,20 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d,
     if (covers_new && wid < 2) {
       const __half* src = row + (size_t)(d.n_head + (wid == 0 ? 0 : d.n_kv_head) + kvh) * HD;
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) nk[e] = __half2float(src[lane * DPL + e]);
-      if (wid == 0) {
+      for (int e = 0; e < DPL; ++e) nkv[e] = __half2float(src[lane * DPL + e]);
+      if (wid == 0) {  // RoPE on K (transformer.py:1105-1127 rounding)
 #pragma unroll
         for (int e = 0; e < DPL; e += 2) {
           const int pr = (lane * DPL + e) >> 1;
-          const float c = fr[2 * pr], sn = fr[2 * pr + 1], a0 = nk[e], a1 = nk[e + 1];
-          nk[e] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, sn));
-          nk[e + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, c));
+          const float c = fr[2 * pr], sn = fr[2 * pr + 1], a0 = nkv[e], a1 = nkv[e + 1];
+          nkv[e] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, sn));
+          nkv[e + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, c));
         }
       }
-      // quantize (fp32 rule) and write the cache row
+      // quantize (fp32 rule) and write the cache row + scale
       uint8_t* crow = const_cast<uint8_t*>((wid == 0 ? kc : vc) + (size_t)wpos * rb);
       __half* srow = quant ? const_cast<__half*>((wid == 0 ? ksc : vsc) + (size_t)wpos * ng) : nullptr;
-      store_kv_row<DPL>(nk, lane, d.kv_type, G, true, crow, srow);
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) nv[e] = nk[e];
+      store_kv_row<DPL>(nkv, lane, d.kv_type, G, true, crow, srow);
     }
   } else {
     for (int i = tid; i < n_rep * HD; i += 128) {
@@ -349,121 +369,91 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d,
                            : __half2float(reinterpret_cast<const __half*>(d.q)[qi]);
     }
   }
-  if (tid < kMaxRep) {
-    ml_s[tid] = -INFINITY;
-    ml_s[kMaxRep + tid] = 0.f;
+  if (!mbar_wait(bar, 0, kAttnWaitLimit)) {
+    if (tid == 0) atomicExch(err, AXB_ETIMEOUT);
+    return;  // the only copy in flight is the one that timed out
   }
+  if (covers_new && wid < 2) {
+    // patch the staged copy (the prefetch read the slot before this step wrote it)
+    uint8_t* rowp = reinterpret_cast<uint8_t*>(wid == 0 ? kst : vst) + (size_t)(wpos - t0) * rb;
+    store_kv_row<DPL>(nkv, lane, d.kv_type, G, true, rowp, nullptr);
+  }
+  __syncthreads();  // global scale writes of the new slot are visible inside the CTA
+  if (covers_new && quant && tid < 2 * ng) {
+    const int which = tid / ng, gi = tid % ng;
+    (which == 0 ? ks_s : vs_s)[(wpos - t0) * ng + gi] = __half2float((which == 0 ? ksc : vsc)[(size_t)wpos * ng + gi]);
+  }
+  __syncthreads();
+
   const float sm_scale = 1.0f / sqrtf((float)HD);
+  // ---- scores for the whole chunk: EPT threads per token, 16 elements each
+  for (int base = 0; base < nt; base += 128 / EPT) {
+    const int tk = base + tid / EPT, ch = tid % EPT;
+    float part[kMaxRep];
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) part[r] = 0.f;
+    if (tk < nt) {
+      float kv[16];
+      kv_load16(reinterpret_cast<const uint8_t*>(kst) + (size_t)tk * rb, d.kv_type, ch * 16, kv);
+      const float s = quant ? ks_s[tk * ng + (ch * 16) / G] : 1.f;
+#pragma unroll
+      for (int r = 0; r < kMaxRep; ++r) {
+        if (r < n_rep) {
+          float acc = 0.f;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) acc = __fmaf_rn(q_s[r * HD + ch * 16 + e], kv[e], acc);
+          part[r] = acc * s;
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) {
+      float v = part[r];
+      for (int o = 1; o < EPT; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (ch == 0 && tk < nt && r < n_rep) p_s[r * cap + tk] = v * sm_scale;
+    }
+  }
+  __syncthreads();
+  // ---- softmax over the chunk: warp w handles heads w, w+4
+  for (int r = wid; r < n_rep; r += 4) {
+    float mx = -INFINITY;
+    for (int tk = lane; tk < nt; tk += 32) mx = fmaxf(mx, p_s[r * cap + tk]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int tk = lane; tk < nt; tk += 32) {
+      const float e = __expf(p_s[r * cap + tk] - mx);
+      p_s[r * cap + tk] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) {
+      ml_s[r] = mx;
+      ml_s[kMaxRep + r] = sum;
+    }
+  }
+  __syncthreads();
+  // ---- PV: warp w takes tokens w, w+4, ...; lane covers DPL consecutive dims
   float acc[kMaxRep][DPL];
 #pragma unroll
   for (int r = 0; r < kMaxRep; ++r)
 #pragma unroll
     for (int e = 0; e < DPL; ++e) acc[r][e] = 0.f;
-  __syncthreads();
-
-  bool failed = false;
-  for (int i = 0; i < ntiles; ++i) {
-    const int st = i & 1, ts = t0 + i * kDecTile, nt = min(kDecTile, t1 - ts);
-    // scales of this tile (plain loads; tiny)
-    if (quant)
-      for (int j = tid; j < nt * ng; j += 128) {
-        ks_s[j] = __half2float(ksc[(size_t)ts * ng + j]);
-        vs_s[j] = __half2float(vsc[(size_t)ts * ng + j]);
-      }
-    if (!mbar_wait(bars + st, (uint32_t)((i >> 1) & 1), kAttnWaitLimit)) {
-      if (tid == 0) atomicExch(err, AXB_ETIMEOUT);
-      if (i + 1 < ntiles) mbar_wait(bars + (st ^ 1), (uint32_t)(((i + 1) >> 1) & 1), kAttnWaitLimit);
-      failed = true;
-    }
-    if (__syncthreads_or(failed)) return;
-    uint8_t* kt = reinterpret_cast<uint8_t*>(kst + st * kDecTile * rb);
-    uint8_t* vt = reinterpret_cast<uint8_t*>(vst + st * kDecTile * rb);
-    if (covers_new && wid < 2 && wpos >= ts && wpos < ts + nt) {
-      // patch the staged copy with the row written this step (the prefetch saw the old one)
-      uint8_t* row = (wid == 0 ? kt : vt) + (size_t)(wpos - ts) * rb;
-      store_kv_row<DPL>(nv, lane, d.kv_type, G, true, row, nullptr);
-    }
-    __syncthreads();
-    if (covers_new && quant && wpos >= ts && wpos < ts + nt && tid < 2 * ng) {
-      const int which = tid / ng, gi = tid % ng;
-      (which == 0 ? ks_s : vs_s)[(wpos - ts) * ng + gi] =
-          __half2float((which == 0 ? ksc : vsc)[(size_t)wpos * ng + gi]);
-    }
-    __syncthreads();
-    // scores: EPT threads per token, 16 elements each (128 / EPT tokens per pass)
-    for (int base = 0; base < kDecTile; base += 128 / EPT) {
-      const int tk = base + tid / EPT, ch = tid % EPT;
-      float part[kMaxRep];
+  for (int tk = wid; tk < nt; tk += 4) {
+    const uint8_t* vrow = reinterpret_cast<const uint8_t*>(vst) + (size_t)tk * rb;
+    float vv[DPL];
 #pragma unroll
-      for (int r = 0; r < kMaxRep; ++r) part[r] = 0.f;
-      if (tk < nt) {
-        float kv[16];
-        kv_load16(kt + (size_t)tk * rb, d.kv_type, ch * 16, kv);
-        const float s = quant ? ks_s[tk * ng + (ch * 16) / G] : 1.f;
-#pragma unroll
-        for (int r = 0; r < kMaxRep; ++r) {
-          if (r < n_rep) {
-            float a = 0.f;
-#pragma unroll
-            for (int e = 0; e < 16; ++e) a = __fmaf_rn(q_s[r * HD + ch * 16 + e], kv[e], a);
-            part[r] = a * s;
-          }
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < kMaxRep; ++r) {
-        float a = part[r];
-        for (int o = 1; o < EPT; o <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (ch == 0 && r < n_rep) p_s[r * kDecTile + tk] = (tk < nt) ? a * sm_scale : -INFINITY;
-      }
-    }
-    __syncthreads();
-    // online softmax: warp w handles heads w, w+4
-    for (int r = wid; r < n_rep; r += 4) {
-      const float v0 = p_s[r * kDecTile + lane], v1 = p_s[r * kDecTile + lane + 32];
-      const float mx = warp_max(fmaxf(v0, v1));
-      const float m_old = ml_s[r], m_new = fmaxf(m_old, mx);
-      const float e0 = (v0 == -INFINITY) ? 0.f : __expf(v0 - m_new);
-      const float e1 = (v1 == -INFINITY) ? 0.f : __expf(v1 - m_new);
-      p_s[r * kDecTile + lane] = e0;
-      p_s[r * kDecTile + lane + 32] = e1;
-      const float sum = warp_sum(e0 + e1);
-      if (lane == 0) {
-        const float c = (m_old == -INFINITY) ? 0.f : __expf(m_old - m_new);
-        ml_s[2 * kMaxRep + r] = c;
-        ml_s[kMaxRep + r] = ml_s[kMaxRep + r] * c + sum;
-        ml_s[r] = m_new;
-      }
-    }
-    __syncthreads();
+    for (int e = 0; e < DPL; ++e) vv[e] = kv_elem(vrow, d.kv_type, lane * DPL + e);
+    const float s = quant ? vs_s[tk * ng + (lane * DPL) / G] : 1.f;
 #pragma unroll
     for (int r = 0; r < kMaxRep; ++r) {
       if (r < n_rep) {
-        const float c = ml_s[2 * kMaxRep + r];
+        const float pw = p_s[r * cap + tk] * s;
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) acc[r][e] *= c;
+        for (int e = 0; e < DPL; ++e) acc[r][e] = __fmaf_rn(pw, vv[e], acc[r][e]);
       }
     }
-    // PV: warp w takes tokens w, w+4, ...; lane covers DPL consecutive dims
-    for (int tk = wid; tk < nt; tk += 4) {
-      const uint8_t* vrow = vt + (size_t)tk * rb;
-      float vv[DPL];
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) vv[e] = kv_elem(vrow, d.kv_type, lane * DPL + e);
-      const float s = quant ? vs_s[tk * ng + (lane * DPL) / G] : 1.f;
-#pragma unroll
-      for (int r = 0; r < kMaxRep; ++r) {
-        if (r < n_rep) {
-          const float pw = p_s[r * kDecTile + tk] * s;
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[r][e] = __fmaf_rn(pw, vv[e], acc[r][e]);
-        }
-      }
-    }
-    __syncthreads();  // stage st and p_s are free again
-    issue(i + 2);
   }
-  // cross-warp reduction of acc (o_red aliases the K/V stages, all consumed)
+  __syncthreads();  // K/V rows are dead: o_red may reuse them
 #pragma unroll
   for (int r = 0; r < kMaxRep; ++r)
     if (r < n_rep)
@@ -475,11 +465,10 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d,
     const int r = i / HD, e = i % HD;
     const float o = o_red[(0 * kMaxRep + r) * HD + e] + o_red[(1 * kMaxRep + r) * HD + e] +
                     o_red[(2 * kMaxRep + r) * HD + e] + o_red[(3 * kMaxRep + r) * HD + e];
-    if (nsplit == 1) {
+    if (nsplit == 1)
       reinterpret_cast<__half*>(d.out)[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(o, ml_s[kMaxRep + r]));
-    } else {
+    else
       part_o[((pidx + r) * max_splits + split) * HD + e] = o;
-    }
   }
   if (nsplit == 1) return;
   if (tid < n_rep) {
@@ -493,30 +482,46 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const axb_attn_desc d,
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // deterministic combine over splits in index order
+  // ---- combine, split order fixed: per-head weights first (warp per head)
+  for (int r = wid; r < n_rep; r += 4) {
+    const size_t hb = (pidx + r) * max_splits;
+    float M = -INFINITY;
+    for (int sp = lane; sp < nsplit; sp += 32) M = fmaxf(M, __ldcg(part_ml + (hb + sp) * 2));
+    M = warp_max(M);
+    float L = 0.f;
+    for (int sp = lane; sp < nsplit; sp += 32) {
+      const float m = __ldcg(part_ml + (hb + sp) * 2), l = __ldcg(part_ml + (hb + sp) * 2 + 1);
+      const float cwt = (m == -INFINITY) ? 0.f : __expf(m - M);
+      coef[r * kMaxSplits + sp] = cwt;
+      L += l * cwt;
+    }
+    L = warp_sum(L);
+    if (lane == 0) ml_s[kMaxRep + r] = L;
+  }
+  __syncthreads();
   for (int i = tid; i < n_rep * HD; i += 128) {
     const int r = i / HD, e = i % HD;
     const size_t hb = (pidx + r) * max_splits;
-    float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(part_ml + (hb + sp) * 2));
-    float L = 0.f, O = 0.f;
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float m = __ldcg(part_ml + (hb + sp) * 2), l = __ldcg(part_ml + (hb + sp) * 2 + 1);
-      const float c = (m == -INFINITY) ? 0.f : __expf(m - M);
-      L += l * c;
-      O += __ldcg(part_o + (hb + sp) * HD + e) * c;
+    float O = 0.f;
+    for (int sp0 = 0; sp0 < nsplit; sp0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = (sp0 + u < nsplit) ? __ldcg(part_o + (hb + sp0 + u) * HD + e) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (sp0 + u < nsplit) O += v[u] * coef[r * kMaxSplits + sp0 + u];
     }
-    reinterpret_cast<__half*>(d.out)[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, L));
+    reinterpret_cast<__half*>(d.out)[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, ml_s[kMaxRep + r]));
   }
   if (tid == 0) counters[b * d.n_kv_head + kvh] = 0;
 }
 
 size_t decode_smem(int kv_type, int hd) {
-  int rb = kv_type == AXB_KV_F16 ? hd * 2 : (kv_type == AXB_KV_FP8 ? hd : hd / 2);
-  size_t stages = (size_t)4 * kDecTile * rb;
-  size_t ored = (size_t)4 * kMaxRep * hd * 4;
-  size_t rest = (size_t)(kMaxRep * hd + kMaxRep * kDecTile + 8 * kDecTile + 3 * kMaxRep + 8) * 4 + 2 * 8 + 16;
-  return std::max(stages, ored) + rest;
+  const int rb = kv_type == AXB_KV_F16 ? hd * 2 : (kv_type == AXB_KV_FP8 ? hd : hd / 2);
+  const int cap = decode_chunk_cap(kv_type, hd);
+  size_t rows = std::max((size_t)2 * cap * rb, (size_t)4 * kMaxRep * hd * 4);
+  size_t rest = (size_t)(kMaxRep * hd + kMaxRep * cap + 8 * cap + 4 * kMaxRep + kMaxRep * kMaxSplits) * 4 + 16;
+  return rows + rest;
 }
 
 // Tree / chunked-prefill attention: T query tokens per sequence, each sees the
@@ -675,10 +680,17 @@ __global__ void compact_kv_kernel(uint8_t* cache, __half* scales, int max_batch,
 // ---------------------------------------------------------------- host
 static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// CTAs of one (sequence, kv head) the split count aims for: ~2 CTAs per SM
 int decode_max_splits(int B, int n_kv_head) {
   int ctas = B * n_kv_head;
   int want = (2 * num_sms() + ctas - 1) / ctas;
   return std::max(1, std::min(64, want));
+}
+
+// grid width (and partial-buffer stride) covering every active length <= max_seq
+int decode_grid_splits(int target, int max_seq, int kv_type, int hd) {
+  const int cap = decode_chunk_cap(kv_type, hd);
+  return std::max(target, (max_seq + cap - 1) / cap);
 }
 
 // Workspace: [combine counters | kAttnCounters ints][m, l partials][O partials].
@@ -744,7 +756,9 @@ int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s)
                 "attention: bad quantized-cache scales / group (kv_group must divide head_dim, >= 32)");
   if (d->masks == nullptr) {
     AXB_CHECK_ARG(d->active_len >= 1 && d->active_len <= d->max_seq, "attention: bad active_len %d", d->active_len);
-    int ms = d->num_splits > 0 ? std::min(64, d->num_splits) : decode_max_splits(d->B, d->n_kv_head);
+    const int target = d->num_splits > 0 ? std::min(64, d->num_splits) : decode_max_splits(d->B, d->n_kv_head);
+    const int ms = decode_grid_splits(target, d->max_seq, d->kv_type, d->head_dim);
+    AXB_CHECK_ARG(ms <= kMaxSplits, "attention: max_seq %d needs %d splits (> %d)", d->max_seq, ms, kMaxSplits);
     AXB_CHECK_ARG(d->workspace && d->workspace_bytes >= attn_workspace(d->B, d->n_head, d->head_dim, ms),
                   "attention: workspace too small");
     AXB_CHECK_ARG((size_t)d->B * d->n_kv_head <= kAttnCounters, "attention: too many sequences x heads");
@@ -761,9 +775,11 @@ int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s)
     if (int rc = attn_prepare()) return rc;
     cudaError_t e;
     if (d->head_dim == 128)
-      e = launch_pdl(decode_attn_kernel<128>, grid, dim3(128), smem, s, d->pdl != 0, *d, ms, po, pml, cnt, err, f);
+      e = launch_pdl(decode_attn_kernel<128>, grid, dim3(128), smem, s, d->pdl != 0, *d, target, ms, po, pml, cnt, err,
+                     f);
     else
-      e = launch_pdl(decode_attn_kernel<64>, grid, dim3(128), smem, s, d->pdl != 0, *d, ms, po, pml, cnt, err, f);
+      e = launch_pdl(decode_attn_kernel<64>, grid, dim3(128), smem, s, d->pdl != 0, *d, target, ms, po, pml, cnt, err,
+                     f);
     return cuda_status(e, "decode attention launch");
   }
   AXB_CHECK_ARG(d->T >= 1 && d->T <= 64, "attention: tree mode needs 1 <= T <= 64");
@@ -815,10 +831,10 @@ int axb_kv_dequantize(const void* q, const uint16_t* sc, int rows, int hd, int k
   return launch_status("kv_dequantize");
 }
 
-size_t axb_attn_workspace_bytes(int B, int n_head, int head_dim, int T, int max_splits) {
-  (void)T;
-  int ms = max_splits > 0 ? std::min(64, max_splits) : 64;
-  return attn_workspace(B, n_head, head_dim, ms);
+size_t axb_attn_workspace_bytes(int B, int n_head, int n_kv_head, int head_dim, int max_seq, int kv_type,
+                                int num_splits) {
+  const int target = num_splits > 0 ? std::min(64, num_splits) : decode_max_splits(B, n_kv_head);
+  return attn_workspace(B, n_head, head_dim, decode_grid_splits(target, max_seq, kv_type, head_dim));
 }
 
 int axb_attention(const axb_attn_desc* d, void* stream) { return attention(d, (cudaStream_t)stream); }

@@ -566,9 +566,7 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 7 : (NT == 2 ? 5 : 3)) 
       const uint4* wst = reinterpret_cast<const uint4*>(ring + st * kStageW) + lane;
       const char* sst = ring + kStages * kStageW + st * kStageS;
       const int kbt = kb0 - t * a.KB;  // k-block of the stage within the tile
-#pragma unroll
-      for (int j = 0; j < kCH; ++j) {
-        if (j < n) {
+      auto kblock = [&](const int j) {
           const uint4 cur = wst[j * 32];
           uint32_t bf[NT][8];
 #pragma unroll
@@ -633,7 +631,14 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 7 : (NT == 2 ? 5 : 3)) 
                 mma_16816(tmp[jj % CH][nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], tmp[jj % CH][nt]);
             }
           }
-        }
+      };
+      if (n == kCH) {  // full stage: no guards, the 4 k-blocks interleave freely
+#pragma unroll
+        for (int j = 0; j < kCH; ++j) kblock(j);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kCH; ++j)
+          if (j < n) kblock(j);
       }
       __syncwarp();
       issue();
@@ -840,15 +845,17 @@ int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
   ga.err = reinterpret_cast<int*>(ws);
   ga.counters = reinterpret_cast<int*>(ws + kCountersOff);
   ga.partials = reinterpret_cast<float*>(ws + kPartialsOff);
-  // persistent grid: kCtasPerSm CTAs per SM, every CTA owns >= 1 group
-  ga.C = std::min<long long>(max_ctas(), ga.U);
   const int nt = nt_for(d->M);
   const size_t xsb = round_up((size_t)d->M * (d->K + 8) * sizeof(__half), 128);
-  const bool xs = nt <= 4 && (d->norm_w != nullptr || xsb <= 16 * 1024) && xsb <= kXsLimit;
+  const bool xs = nt <= 4 && (d->norm_w != nullptr || xsb <= 32 * 1024) && xsb <= kXsLimit;
   AXB_CHECK_ARG(xs || !d->norm_w, "qgemm: fused RMSNorm needs M <= 32 and M*K*2 <= %zu bytes", kXsLimit);
   ga.xs_stride = xs ? d->K + 8 : 0;
   ga.xs_bytes = xs ? (int)xsb : 0;
   const size_t smem = (size_t)ga.xs_bytes + kRingBytes + red_bytes(nt);
+  // persistent grid: every CTA resident at once (up to kCtasPerSm per SM, fewer
+  // when the staged activations make CTAs larger) and owning >= 1 group
+  const int fit = (int)std::min<size_t>(kCtasPerSm, (kSmemLimit - 1024) / smem);
+  ga.C = std::min<long long>((long long)num_sms() * std::max(1, fit), ga.U);
   const int ctas = (int)ga.C, threads = kWarps * 32;
   const bool sym = d->fmt == AXB_W_Q4T_SYM;
   cudaError_t e;

@@ -34,6 +34,7 @@ int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s)
 int attn_prepare();
 size_t attn_workspace(int B, int n_head, int head_dim, int max_splits);
 int decode_max_splits(int B, int n_kv_head);
+int decode_grid_splits(int target, int max_seq, int kv_type, int hd);
 int rmsnorm(const __half* x, const float* w, int M, int K, float eps, __half* out, cudaStream_t s);
 int argmax(const __half* x, int rows, int n, int ld, int32_t* out, cudaStream_t s);
 
@@ -223,7 +224,9 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.gemm_ws = take(g);
   size_t a = 0;
   for (int b = 1; b <= c.max_batch; ++b)
-    a = std::max(a, attn_workspace(b, c.n_head, c.head_dim, decode_max_splits(b, c.n_kv_head)));
+    a = std::max(a, attn_workspace(b, c.n_head, c.head_dim,
+                                   decode_grid_splits(decode_max_splits(b, c.n_kv_head), c.max_seq, c.kv_type,
+                                                      c.head_dim)));
   L.attn_ws_bytes = a;
   L.attn_ws = take(a);
   L.total = off;

@@ -339,7 +339,7 @@ def _attention(q, k_cache, v_cache, k_scales, v_scales, kv_dtype, *, active_len=
     qf = q.contiguous()
     out = torch.empty((Bc * (T if masks is not None else 1), Hq * hd), dtype=torch.float16, device=q.device)
     lib = L.load()
-    ws = _ATTN_WS.get(lib.axb_attn_workspace_bytes(Bc, Hq, hd, T, num_splits), q.device)
+    ws = _ATTN_WS.get(lib.axb_attn_workspace_bytes(Bc, Hq, Hkv, hd, S, kt, num_splits), q.device)
     mask_t = None
     if masks is not None:
         mask_t = torch.tensor([int(m) & 0xFFFFFFFFFFFFFFFF for m in masks], dtype=torch.uint64, device=q.device)

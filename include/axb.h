@@ -191,7 +191,8 @@ typedef struct {
   size_t workspace_bytes;
   int pdl;
 } axb_attn_desc;
-size_t axb_attn_workspace_bytes(int B, int n_head, int head_dim, int T, int max_splits);
+size_t axb_attn_workspace_bytes(int B, int n_head, int n_kv_head, int head_dim, int max_seq, int kv_type,
+                                int num_splits);
 int axb_attention(const axb_attn_desc* d, void* stream);
 
 /* compact_tree_path (paged_cache.py:376-462): move accepted tree slots
