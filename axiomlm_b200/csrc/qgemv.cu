@@ -315,12 +315,26 @@ struct GemmArgs {
   int xs_stride;  // smem row stride (halves); 0 = read x from global
   int xs_bytes;   // bytes of the staged-x region at the start of shared memory
   int early_trigger;  // release the dependent launch right after staging x
+  int xsum_off;       // byte offset of the per-(group, token) x sums in shared memory (SYM + XS)
+  int xsum_ld;        // tokens per group row of the x sums (>= M rounded to 8)
 };
 
-constexpr int kWarps = 4;           // warps per CTA (K-split of each tile)
-constexpr int kCtasPerSm = 4;       // resident CTAs per SM the grid is sized for
-constexpr int kCH = 4;              // k-blocks (512 B each) per pipeline stage
-constexpr int kStages = 3;          // stages per warp
+#ifndef AXB_GEMV_WARPS
+#define AXB_GEMV_WARPS 4
+#endif
+#ifndef AXB_GEMV_CTAS_PER_SM
+#define AXB_GEMV_CTAS_PER_SM 4
+#endif
+#ifndef AXB_GEMV_CH
+#define AXB_GEMV_CH 4
+#endif
+#ifndef AXB_GEMV_STAGES
+#define AXB_GEMV_STAGES 3
+#endif
+constexpr int kWarps = AXB_GEMV_WARPS;            // warps per CTA (K-split of each tile)
+constexpr int kCtasPerSm = AXB_GEMV_CTAS_PER_SM;  // resident CTAs per SM the grid is sized for
+constexpr int kCH = AXB_GEMV_CH;                  // k-blocks (512 B each) per pipeline stage
+constexpr int kStages = AXB_GEMV_STAGES;          // stages per warp
 constexpr int kStageW = kCH * 512;  // weight bytes per stage
 constexpr int kStageS = kCH * 64;   // scale bytes per stage (max: affine, one group per k-block)
 // per-warp ring: stages of weights, stages of scales, mbarriers; the stride is
@@ -352,6 +366,19 @@ __device__ __forceinline__ void unpack_word(uint32_t w, uint32_t (&a)[4]) {
   a[1] = h2_as_u32(__hfma2(u32_as_h2(hi0), mul, add));
   a[2] = h2_as_u32(__hsub2(u32_as_h2(lo1), sub));
   a[3] = h2_as_u32(__hfma2(u32_as_h2(hi1), mul, add));
+}
+
+// nibble pairs of one word -> four A-fragment registers holding fp16
+// (1024 + q) for rows g (registers 0, 2) and (1024 + 16 q) for rows g + 8
+// (registers 1, 3); the offsets are removed per group with the group sums of
+// x: sum (q - 8) x = C_lo - 1032 X  and  C_hi / 16 - 72 X.
+__device__ __forceinline__ void unpack_word_raw(uint32_t w, uint32_t (&a)[4]) {
+  const uint32_t MAGIC = 0x64006400u;
+  a[0] = lop3_and_or(w, 0x000F000Fu, MAGIC);
+  a[1] = lop3_and_or(w, 0x00F000F0u, MAGIC);
+  const uint32_t w8 = w >> 8;
+  a[2] = lop3_and_or(w8, 0x000F000Fu, MAGIC);
+  a[3] = lop3_and_or(w8, 0x00F000F0u, MAGIC);
 }
 
 template <int NT>
@@ -456,6 +483,23 @@ __device__ void stage_x(const GemmArgs& a, __half* xs, float* red) {
   }
 }
 
+// Per-(group, token) sums of the staged fp16 x, in fp32: X[g][m].
+__device__ void stage_xsum(const GemmArgs& a, const __half* xs, float* X, int G) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int ngr = a.K / G;
+  for (int item = wid; item < ngr * a.M; item += nw) {
+    const int grp = item % ngr, m = item / ngr;
+    const __half* src = xs + (size_t)m * a.xs_stride + grp * G;
+    float v = 0.f;
+    for (int k = lane * 2; k < G; k += 64) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(src + k));
+      v += f.x + f.y;
+    }
+    v = warp_sum(v);
+    if (lane == 0) X[grp * a.xsum_ld + m] = v;
+  }
+}
+
 // chunk of tile t handled by warp w: global k-block range [lo, hi)
 __device__ __forceinline__ void warp_chunk(int upt, int GB, int U0, int U1, int t, int w, int& lo, int& hi) {
   const int s0 = max(U0, t * upt), s1 = min(U1, (t + 1) * upt);
@@ -465,7 +509,7 @@ __device__ __forceinline__ void warp_chunk(int upt, int GB, int U0, int U1, int 
 }
 
 template <int NT, bool SYM, int GB, bool XS>
-__global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 7 : (NT == 2 ? 5 : 3)) qgemm_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, (NT == 1 ? 28 : (NT == 2 ? 20 : 12)) / kWarps) qgemm_kernel(const GemmArgs a) {
   extern __shared__ __align__(128) char smem[];
   __half* xs = reinterpret_cast<__half*>(smem);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -512,6 +556,10 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 7 : (NT == 2 ? 5 : 3)) 
   if (XS) {
     stage_x(a, xs, nred);
     __syncthreads();
+    if (SYM) {
+      stage_xsum(a, xs, reinterpret_cast<float*>(smem + a.xsum_off), GB * 64);
+      __syncthreads();
+    }
   }
   if (a.early_trigger) pdl_trigger();
 
@@ -529,7 +577,7 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 7 : (NT == 2 ? 5 : 3)) 
   // independent accumulation chains per group (the mma results of one
   // k-block's 4 words go to different registers, so consecutive HMMAs do not
   // wait on each other); summed when the group's scale is applied
-  constexpr int CH = NT == 1 ? 4 : (NT == 2 ? 2 : 1);
+  constexpr int CH = NT == 1 ? 2 : 1;
   for (int t = t_first; t <= t_last; ++t) {
     int kb_lo, kb_hi;
     warp_chunk(a.upt, GB, U0, U1, t, wid, kb_lo, kb_hi);
@@ -545,7 +593,7 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 7 : (NT == 2 ? 5 : 3)) 
       }
     // activation fragments of the next k-block, loaded one k-block ahead
     uint4 xn[NT][2];
-    if (kb_lo < kb_hi) {
+    if (!XS && kb_lo < kb_hi) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         xn[nt][0] = xrow[nt][(kb_lo - t * a.KB) * 8];
@@ -569,12 +617,21 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 7 : (NT == 2 ? 5 : 3)) 
       auto kblock = [&](const int j) {
           const uint4 cur = wst[j * 32];
           uint32_t bf[NT][8];
+          if (XS) {  // staged activations: shared-memory loads, scheduled freely in the unrolled stage
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            bf[nt][0] = xn[nt][0].x; bf[nt][1] = xn[nt][0].y; bf[nt][2] = xn[nt][0].z; bf[nt][3] = xn[nt][0].w;
-            bf[nt][4] = xn[nt][1].x; bf[nt][5] = xn[nt][1].y; bf[nt][6] = xn[nt][1].z; bf[nt][7] = xn[nt][1].w;
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint4 v0 = xrow[nt][(kbt + j) * 8], v1 = xrow[nt][(kbt + j) * 8 + 1];
+              bf[nt][0] = v0.x; bf[nt][1] = v0.y; bf[nt][2] = v0.z; bf[nt][3] = v0.w;
+              bf[nt][4] = v1.x; bf[nt][5] = v1.y; bf[nt][6] = v1.z; bf[nt][7] = v1.w;
+            }
+          } else {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              bf[nt][0] = xn[nt][0].x; bf[nt][1] = xn[nt][0].y; bf[nt][2] = xn[nt][0].z; bf[nt][3] = xn[nt][0].w;
+              bf[nt][4] = xn[nt][1].x; bf[nt][5] = xn[nt][1].y; bf[nt][6] = xn[nt][1].z; bf[nt][7] = xn[nt][1].w;
+            }
           }
-          if (kb0 + j + 1 < kb_hi) {  // prefetch the next k-block's fragments
+          if (!XS && kb0 + j + 1 < kb_hi) {  // prefetch the next k-block's fragments
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
               xn[nt][0] = xrow[nt][(kbt + j + 1) * 8];
@@ -582,7 +639,40 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 7 : (NT == 2 ? 5 : 3)) 
             }
           }
           const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
-          if (SYM) {
+          if (SYM && XS) {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              uint32_t af[4];
+              unpack_word_raw(words[jj], af);
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+                mma_16816(tmp[jj % CH][nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], tmp[jj % CH][nt]);
+            }
+            if (GB == 1 || (j & 1)) {  // group complete: remove the offsets, apply the scales
+              const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[(j / GB) * 8 + g];
+              const float2 sc = __half22float2(u32_as_h2(sp));
+              const int grp = (kbt + j) / GB;
+              const float* Xg = reinterpret_cast<const float*>(smem + a.xsum_off) + grp * a.xsum_ld;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                const float2 xg = *reinterpret_cast<const float2*>(Xg + nt * 8 + 2 * t4);
+                float s4[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  float v = tmp[0][nt][q];
+#pragma unroll
+                  for (int c2 = 1; c2 < CH; ++c2) v += tmp[c2][nt][q];
+                  s4[q] = v;
+#pragma unroll
+                  for (int c2 = 0; c2 < CH; ++c2) tmp[c2][nt][q] = 0.f;
+                }
+                acc[nt][0] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg.x, s4[0]), acc[nt][0]);
+                acc[nt][1] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg.y, s4[1]), acc[nt][1]);
+                acc[nt][2] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[2], -72.f * xg.x), acc[nt][2]);
+                acc[nt][3] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[3], -72.f * xg.y), acc[nt][3]);
+              }
+            }
+          } else if (SYM) {
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
               uint32_t af[4];
@@ -850,7 +940,11 @@ int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
   const bool xs = nt <= 4 && (d->norm_w != nullptr || xsb <= 32 * 1024) && xsb <= kXsLimit;
   AXB_CHECK_ARG(xs || !d->norm_w, "qgemm: fused RMSNorm needs M <= 32 and M*K*2 <= %zu bytes", kXsLimit);
   ga.xs_stride = xs ? d->K + 8 : 0;
-  ga.xs_bytes = xs ? (int)xsb : 0;
+  ga.xsum_ld = (d->M + 7) / 8 * 8 + 8;
+  size_t xsum_b = 0;
+  if (xs && d->fmt == AXB_W_Q4T_SYM) xsum_b = round_up((size_t)(d->K / d->group) * ga.xsum_ld * 4, 128);
+  ga.xs_bytes = xs ? (int)(xsb + xsum_b) : 0;
+  ga.xsum_off = (int)xsb;
   const size_t smem = (size_t)ga.xs_bytes + kRingBytes + red_bytes(nt);
   // persistent grid: every CTA resident at once (up to kCtasPerSm per SM, fewer
   // when the staged activations make CTAs larger) and owning >= 1 group
