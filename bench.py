@@ -364,7 +364,7 @@ def _cpu_sample_fns(cfg, B, ctx, kv):
 
     def linear(name, inp, K, n):
         w, sb = mats[name]
-        W = torch.from_numpy(O.dequant_q4_marlin(w.numpy(), sb.numpy(), K, n))  # quant.py:656-661, every call
+        W = O.dequant_q4_marlin_torch(w, sb, K, n)  # quant.py:656-661: dequantized on every call
         return torch.nn.functional.linear(inp.half(), W)
 
     def sample():

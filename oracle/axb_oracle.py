@@ -43,6 +43,7 @@ __all__ = [
     "marlin_lane_maps",
     "pack_q4_marlin_rtn",
     "dequant_q4_marlin",
+    "dequant_q4_marlin_torch",
     "pack_q4_g64",
     "dequant_q4_g64",
     "pack_q8_g64",
@@ -182,6 +183,27 @@ def dequant_q4_marlin(w_marlin, sb_marlin, K: int, out_features: int | None = No
     if out_features is not None and out_features < w.shape[0]:
         w = w[:out_features]
     return w
+
+
+def dequant_q4_marlin_torch(w_marlin: torch.Tensor, sb_marlin: torch.Tensor, K: int, out_features: int | None = None):
+    """quant.py:597-634 with the reference's own torch ops (multi-threaded on
+    the CPU); used to time the reference's per-call dequant fairly.  Equal to
+    ``dequant_q4_marlin`` value for value."""
+    nt, kg = w_marlin.shape[:2]
+    lanes = torch.arange(32)
+    r_idx = ((lanes & 16) >> 2) | ((lanes & 6) >> 1)
+    c0 = ((lanes & 8) >> 1) | ((lanes & 1) << 1)
+    c1 = c0 + 1
+    w = w_marlin.unsqueeze(-1)
+    q0 = ((w >> torch.tensor([0, 4, 8, 12], dtype=torch.int32)) & 0xF).float()
+    q1 = ((w >> torch.tensor([16, 20, 24, 28], dtype=torch.int32)) & 0xF).float()
+    q = torch.empty((nt, kg, 8, 8, 2, 4), dtype=torch.float32)
+    q[:, :, c0, r_idx, :, :] = q0
+    q[:, :, c1, r_idx, :, :] = q1
+    q = q.permute(0, 2, 1, 4, 5, 3).reshape(nt * 8, kg, 64)
+    sb = sb_marlin.permute(0, 2, 1, 3).reshape(nt * 8, kg, 2)
+    out = (q * sb[:, :, 0:1].float() + sb[:, :, 1:2].float()).reshape(nt * 8, K).to(torch.float16)
+    return out[:out_features] if out_features is not None and out_features < out.shape[0] else out
 
 
 # ---------------------------------------------------------------------------

@@ -30,6 +30,12 @@ def test_q4_marlin_dequant_bit_exact(pfx):
     assert np.array_equal(dq.view(np.uint16), g[f"{pfx}_dq"].view(np.uint16))
 
 
+def test_torch_restatement_of_marlin_dequant_matches():
+    g = _load("quant.npz")
+    dq = O.dequant_q4_marlin_torch(torch.from_numpy(g["q4m_clip_w"]), torch.from_numpy(g["q4m_clip_sb"]), 256, 40)
+    assert np.array_equal(dq.numpy().view(np.uint16), g["q4m_clip_dq"].view(np.uint16))
+
+
 def test_q4_g64_and_marlin_rtn_identical_values():
     # test_phase0_research.py:56-95: MARLIN RTN == Q4_G64 value for value
     g = _load("quant.npz")
