@@ -114,6 +114,8 @@ _SIGS = {
     "axb_qgemm_workspace_bytes": (sz, [i32, i32, i32, i32]),
     "axb_qgemm": (i32, [C.POINTER(QGemmDesc), vp]),
     "axb_qgemm_status": (i32, [vp, vp]),
+    "axb_qgemm_noalloc": (i32, [C.POINTER(QGemmDesc), vp]),
+    "axb_qgemm_noalloc_scratch_bytes": (sz, []),
     "axb_rmsnorm": (i32, [vp, vp, i32, i32, f32, vp, vp]),
     "axb_rope_kv_write": (i32, [C.POINTER(KvWriteDesc), vp]),
     "axb_kv_quantize": (i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp]),

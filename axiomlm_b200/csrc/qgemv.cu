@@ -986,6 +986,60 @@ int qgemm_status(void* workspace, cudaStream_t s) {
   return AXB_OK;
 }
 
+// ---------------------------------------------------------------- no-alloc GEMV
+// Scratch of axb_qgemm_noalloc: the same layout axb_qgemm expects in a caller
+// workspace (error word, tile counters, CTA partials for M <= 8), held in a
+// file-scope device array.  Every GPU that loads this library keeps one copy
+// (kNoAllocBytes) until the process exits.
+constexpr int kNoAllocMaxM = 8;
+constexpr size_t kNoAllocMaxCtas = 1024;
+constexpr size_t kNoAllocBytes = kPartialsOff + 2 * kNoAllocMaxCtas * 32 * 4 * sizeof(float);
+static __device__ __align__(256) char g_noalloc_scratch[kNoAllocBytes];
+
+// Device address of g_noalloc_scratch, looked up once per device with that
+// device current (a host-side symbol is not a device address).
+static void* noalloc_scratch(int* status) {
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = e != cudaSuccess ? cuda_status(e, "qgemm_noalloc: cudaGetDevice") : AXB_EINVAL;
+    if (*status == AXB_EINVAL) set_error("qgemm_noalloc: device index %d out of range", dev);
+    return nullptr;
+  }
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      *status = cuda_status(e, "qgemm_noalloc: cudaGetSymbolAddress");
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  *status = AXB_OK;
+  return addr[dev];
+}
+
+int qgemm_noalloc(const axb_qgemm_desc* d, cudaStream_t stream) {
+  AXB_CHECK_ARG(d, "null descriptor");
+  AXB_CHECK_ARG(d->M >= 1 && d->M <= kNoAllocMaxM, "qgemm_noalloc: M must be in [1, %d] (got %d); use axb_qgemm",
+                kNoAllocMaxM, d->M);
+  AXB_CHECK_ARG(max_ctas() <= (long long)kNoAllocMaxCtas, "qgemm_noalloc: device has too many SMs for the scratch");
+  AXB_CHECK_ARG(d->N > 0 && (size_t)((d->N + 15) / 16) <= kMaxTiles, "qgemm_noalloc: N out of range (%d)", d->N);
+  int rc = AXB_OK;
+  char* ws = reinterpret_cast<char*>(noalloc_scratch(&rc));
+  if (rc) return rc;
+  // the array keeps the previous call's contents: clear the error word and the
+  // tile counters this call uses (a call that ended early may leave them set)
+  cudaError_t e = cudaMemsetAsync(ws, 0, 4, stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(ws + kCountersOff, 0, (size_t)((d->N + 15) / 16) * 4, stream);
+  if (e != cudaSuccess) return cuda_status(e, "qgemm_noalloc: clear scratch");
+  axb_qgemm_desc dd = *d;
+  dd.workspace = ws;
+  dd.workspace_bytes = kNoAllocBytes;
+  return qgemm(&dd, stream);
+}
+
 }  // namespace axb
 
 using namespace axb;
@@ -1077,6 +1131,10 @@ size_t axb_qgemm_workspace_bytes(int N, int K, int M, int group) {
 }
 
 int axb_qgemm(const axb_qgemm_desc* d, void* stream) { return qgemm(d, (cudaStream_t)stream); }
+
+int axb_qgemm_noalloc(const axb_qgemm_desc* d, void* stream) { return qgemm_noalloc(d, (cudaStream_t)stream); }
+
+size_t axb_qgemm_noalloc_scratch_bytes(void) { return kNoAllocBytes; }
 
 int axb_qgemm_status(void* workspace, void* stream) {
   AXB_CHECK_ARG(workspace, "qgemm_status: null workspace");

@@ -121,6 +121,21 @@ typedef struct {
 
 size_t axb_qgemm_workspace_bytes(int N, int K, int M, int group);
 int axb_qgemm(const axb_qgemm_desc* d, void* stream);
+/* GEMV that allocates nothing, for callers that cannot hand over device
+ * memory: hosts that reserve the whole device in their own pool up front,
+ * plugin or FFI hosts with no allocator of their own, and latency-critical
+ * paths where an allocation's implicit synchronization is not acceptable.
+ * Same arguments and results as axb_qgemm, but d->workspace is ignored: the
+ * scratch (error word, tile counters, partial sums) is a fixed array of
+ * axb_qgemm_noalloc_scratch_bytes() (about 1.5 MiB) inside the library, one
+ * per GPU, held until the process exits.  Limits: M <= 8 tokens.  The first
+ * call on a device looks the array's device address up (make that call before
+ * any stream capture).  All calls share the array: two calls that may run at
+ * the same time on the GPU (different streams without ordering) race.  Each
+ * call clears the parts of the array that must start at zero.  This entry
+ * point has no counterpart in the reference. */
+int axb_qgemm_noalloc(const axb_qgemm_desc* d, void* stream);
+size_t axb_qgemm_noalloc_scratch_bytes(void);
 /* Synchronizes `stream`; returns AXB_ETIMEOUT (and clears the flag) if a
  * bounded weight-stream wait in an earlier axb_qgemm on this workspace ran out. */
 int axb_qgemm_status(void* workspace, void* stream);
