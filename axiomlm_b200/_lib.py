@@ -129,6 +129,7 @@ _SIGS = {
     "axb_runner_destroy": (i32, [vp]),
     "axb_runner_buffer": (i32, [vp, i32, C.POINTER(sz), C.POINTER(sz)]),
     "axb_runner_step": (i32, [vp, i32, i32, i32, i32, i32, i32, vp, vp, i32, vp]),
+    "axb_runner_uses_step_kernel": (i32, [vp]),
 }
 
 _lib = None

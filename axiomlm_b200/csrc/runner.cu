@@ -15,7 +15,7 @@
 #include <tuple>
 #include <vector>
 
-#include "axb_common.cuh"
+#include "step.cuh"
 
 namespace axb {
 
@@ -188,6 +188,9 @@ struct Layout {
   size_t tokens, params, masks, depths, x, h, qkv, q, attn, sw, logits, amax, xnorm, gemm_ws, attn_ws, total;
   size_t am_v, am_i, am_cnt;
   size_t gemm_ws_bytes, attn_ws_bytes;
+  // persistent step kernel (decode, B <= 8)
+  size_t st_layers, st_done, st_tiles, st_part, st_po, st_pml, st_acnt, st_keys, st_exit;
+  int st_max_tiles;
 };
 
 static Layout make_layout(const axb_model_cfg& c) {
@@ -229,6 +232,18 @@ static Layout make_layout(const axb_model_cfg& c) {
                                                       c.head_dim)));
   L.attn_ws_bytes = a;
   L.attn_ws = take(a);
+  const int sb = std::min(c.max_batch, kStepMaxM);
+  L.st_max_tiles = 0;
+  for (int n : {(int)qkv_dim, c.d_model, 2 * c.ffn, c.vocab}) L.st_max_tiles = std::max(L.st_max_tiles, (n + 15) / 16);
+  L.st_layers = take((size_t)c.n_layer * sizeof(StepLayer));
+  L.st_done = take((size_t)(2 + 5 * c.n_layer) * 4);
+  L.st_tiles = take((size_t)L.st_max_tiles * 4);
+  L.st_part = take((size_t)num_sms() * step_num_warps() * 2 * 32 * 4 * sizeof(float));
+  L.st_po = take((size_t)sb * c.n_head * kStepMaxSplits * c.head_dim * sizeof(float));
+  L.st_pml = take((size_t)sb * c.n_head * kStepMaxSplits * 2 * sizeof(float));
+  L.st_acnt = take((size_t)sb * c.n_kv_head * 4);
+  L.st_keys = take((size_t)kStepMaxM * 8);
+  L.st_exit = take(16);
   L.total = off;
   return L;
 }
@@ -246,6 +261,10 @@ struct Runner {
   std::vector<void*> kc, vc, ks, vs;
   cudaStream_t cap = nullptr;
   std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;
+  // persistent step kernel: decode steps of B <= 8 sequences run as one launch
+  bool step_ok = false;
+  bool step_graph_ok = true;  // cleared if the cooperative launch cannot be captured
+  StepArgs sa = {};
 
   template <typename T>
   T* buf(size_t off) const {
@@ -292,6 +311,12 @@ struct Runner {
     int rc = rmsnorm(x, nw, M, K, c.eps, buf<__half>(L.h), st);
     if (rc) return rc;
     return gemv(w, s, fmt, group, N, K, M, buf<__half>(L.h), K, y, ldy, bias, nullptr, epi, gu, st);
+  }
+
+  int step_forward(int B, cudaStream_t st) const {
+    StepArgs a = sa;
+    a.B = B;
+    return step_launch(a, st);
   }
 
   int forward(int B, int T, bool tree, bool want_norm, cudaStream_t st) const {
@@ -452,6 +477,86 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
     delete r;
     return cuda_status(e, "runner stream");
   }
+  // persistent step kernel (env AXB_STEP=0 keeps decode on the per-kernel graph)
+  const char* sv = getenv("AXB_STEP");
+  const int cap_tok = step_attn_cap(c.kv_type, c.head_dim, c.kv_group);
+  r->step_ok = !(sv && atoi(sv) == 0) &&
+               step_supported(c.wfmt, c.group, c.lm_fmt, c.lm_group, c.head_dim, c.n_head, c.n_kv_head, c.d_model,
+                              c.kv_type, c.kv_group) &&
+               c.ffn % 64 == 0;
+  if (r->step_ok) {
+    if (int rc = step_prepare()) {
+      axb_runner_destroy(r);
+      return rc;
+    }
+    std::vector<StepLayer> tab(c.n_layer);
+    for (int l = 0; l < c.n_layer; ++l) {
+      StepLayer& t = tab[l];
+      t.w[0] = (const char*)p->qkv_w[l];
+      t.s[0] = (const char*)p->qkv_s[l];
+      t.w[1] = (const char*)p->o_w[l];
+      t.s[1] = (const char*)p->o_s[l];
+      t.w[2] = (const char*)p->gu_w[l];
+      t.s[2] = (const char*)p->gu_s[l];
+      t.w[3] = (const char*)p->dn_w[l];
+      t.s[3] = (const char*)p->dn_s[l];
+      t.qkv_b = p->qkv_b ? (const __half*)p->qkv_b[l] : nullptr;
+      t.ln1 = p->ln1[l];
+      t.ln2 = p->ln2[l];
+      t.kc = (uint8_t*)p->k_cache[l];
+      t.vc = (uint8_t*)p->v_cache[l];
+      t.ks = p->k_scale ? (__half*)p->k_scale[l] : nullptr;
+      t.vs = p->v_scale ? (__half*)p->v_scale[l] : nullptr;
+    }
+    e = cudaMemcpy(r->buf<void>(L.st_layers), tab.data(), tab.size() * sizeof(StepLayer), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      axb_runner_destroy(r);
+      return cuda_status(e, "step layer table");
+    }
+    StepArgs& a = r->sa;
+    a.layers = r->buf<StepLayer>(L.st_layers);
+    a.L = c.n_layer;
+    a.d = c.d_model;
+    a.Hq = c.n_head;
+    a.Hkv = c.n_kv_head;
+    a.hd = c.head_dim;
+    a.F = c.ffn;
+    a.V = c.vocab;
+    a.S = c.max_seq;
+    a.kv_type = c.kv_type;
+    a.kv_group = c.kv_type == AXB_KV_F16 ? c.head_dim : c.kv_group;
+    a.group = c.group;
+    a.sym = c.wfmt == AXB_W_Q4T_SYM ? 1 : 0;
+    a.eps = c.eps;
+    a.emb_w = (const uint32_t*)p->emb_w;
+    a.emb_s = (const __half*)p->emb_s;
+    a.lm_w = (const char*)p->lm_w;
+    a.lm_s = (const char*)p->lm_s;
+    a.ln_f = p->ln_f;
+    a.rope = p->rope;
+    a.rope_len = c.rope_len;
+    a.tokens = r->buf<int32_t>(L.tokens);
+    a.params = r->buf<int32_t>(L.params);
+    a.err = r->buf<int>(L.params) + 4;
+    a.h = r->buf<__half>(L.x);
+    a.qkv = r->buf<__half>(L.qkv);
+    a.attn = r->buf<__half>(L.attn);
+    a.sw = r->buf<__half>(L.sw);
+    a.logits = r->buf<__half>(L.logits);
+    a.amax = r->buf<int32_t>(L.amax);
+    a.done = r->buf<int>(L.st_done);
+    a.tile_cnt = r->buf<int>(L.st_tiles);
+    a.partials = r->buf<float>(L.st_part);
+    a.part_o = r->buf<float>(L.st_po);
+    a.part_ml = r->buf<float>(L.st_pml);
+    a.attn_cnt = r->buf<int>(L.st_acnt);
+    a.keys = r->buf<unsigned long long>(L.st_keys);
+    a.exit_cnt = r->buf<int>(L.st_exit);
+    a.max_tiles = L.st_max_tiles;
+    a.attn_cap = cap_tok;
+    const char* l2 = getenv("AXB_STEP_L2");
+    a.l2_ahead = l2 ? atoi(l2) : 8;
+  }
   *out = r;
   return AXB_OK;
 }
@@ -478,6 +583,11 @@ int axb_runner_buffer(void* h, int which, size_t* off, size_t* bytes) {
     default: axb::set_error("runner_buffer: unknown buffer %d", which); return AXB_EINVAL;
   }
   return AXB_OK;
+}
+
+int axb_runner_uses_step_kernel(void* h) {
+  Runner* r = reinterpret_cast<Runner*>(h);
+  return r && r->step_ok ? 1 : 0;
 }
 
 int axb_runner_step(void* h, int B, int T, int rope_pos, int write_pos, int active_len, int prefix_len,
@@ -515,24 +625,28 @@ int axb_runner_step(void* h, int B, int T, int rope_pos, int write_pos, int acti
   int rc = launch_status("set_params");
   if (rc) return rc;
   const bool want_norm = tree;
+  const bool step_mode = !tree && T == 1 && B <= kStepMaxM && r->step_ok;
+  if (step_mode && (!use_graph || !r->step_graph_ok)) return r->step_forward(B, st);
   if (!use_graph) return r->forward(B, T, tree, want_norm, st);
-  auto key = std::make_tuple(B, T, tree ? 1 : 0);
+  auto key = std::make_tuple(B, T, step_mode ? 2 : (tree ? 1 : 0));
   auto it = r->graphs.find(key);
   if (it == r->graphs.end()) {
     cudaError_t e = cudaStreamBeginCapture(r->cap, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) return cuda_status(e, "begin capture");
-    rc = r->forward(B, T, tree, want_norm, r->cap);
+    rc = step_mode ? r->step_forward(B, r->cap) : r->forward(B, T, tree, want_norm, r->cap);
     cudaGraph_t g = nullptr;
     e = cudaStreamEndCapture(r->cap, &g);
-    if (rc) {
-      if (g) cudaGraphDestroy(g);
-      return rc;
-    }
-    if (e != cudaSuccess) return cuda_status(e, "end capture");
     cudaGraphExec_t ex = nullptr;
-    e = cudaGraphInstantiate(&ex, g, 0);
-    cudaGraphDestroy(g);
-    if (e != cudaSuccess) return cuda_status(e, "graph instantiate");
+    if (!rc && e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (step_mode && (rc || e != cudaSuccess)) {
+      // the cooperative step launch could not go into a graph: launch it directly from now on
+      cudaGetLastError();
+      r->step_graph_ok = false;
+      return r->step_forward(B, st);
+    }
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_status(e, "graph capture");
     it = r->graphs.emplace(key, ex).first;
   }
   return cuda_status(cudaGraphLaunch(it->second, st), "graph launch");

@@ -1,0 +1,1105 @@
+// Persistent decode step for sm_100a: one cooperative launch (one CTA per SM)
+// runs a whole T = 1 forward pass -- embedding, every layer, lm_head, argmax.
+//
+// Replaces the decode step of MPSQuantizedDecodeRunner / QuantizedDecodeGraphState
+// (axiomlm/kernels/mps_kernels.mm:2982-3737, step at :3195), i.e. the T = 1 path of
+// Transformer._forward_quantized_sequence (axiomlm/models/transformer.py:1036-1200)
+// with StaticKVCache.update (engine/paged_cache.py:250-361) and
+// gqa_flash_decode_mps (kernels/ops.py:552-654) inside it.  Numerics are those of
+// the per-kernel runner (runner.cu): fp16 activations, fp32 accumulation, the
+// reference's RMSNorm / RoPE / KV-quantization rounding points.
+//
+// Design.
+//  * Every GEMV of the step is split "stream-K" over quantization groups with one
+//    rule: warp i of the grid owns units [i*U/W, (i+1)*U/W).  A warp's weight
+//    stream for the whole step is therefore known at launch.  Lane 0 streams it
+//    through a private ring of bulk copies (TMA, non-tensor form) and runs ahead
+//    across phase boundaries -- weights never depend on activations -- with an
+//    L2 prefetch further ahead, so HBM keeps streaming while the warp waits for
+//    the previous phase's activations.
+//  * Phases are ordered by completion counters in global memory (tiles finished,
+//    attention heads finished) instead of kernel boundaries.  Every wait is
+//    bounded; one that runs out records AXB_ETIMEOUT and the grid winds down.
+//  * A tile split between warps is finished by the last warp to arrive, which
+//    sums the partials in warp order: results are deterministic.
+//  * Attention runs on two groups of four warps per CTA over (sequence, kv head,
+//    split) items; the cached rows of an item are bulk-copied before the QKV
+//    phase has finished; RoPE and the new K/V row's quantized write are fused.
+#include <algorithm>
+
+#include "kv.cuh"
+#include "q4t.cuh"
+#include "step.cuh"
+
+namespace axb {
+
+constexpr int kSW = 8;  // warps per CTA
+constexpr int kSThreads = kSW * 32;
+constexpr int kSCH = 4;      // k-blocks (512 B of weights each) per ring stage
+constexpr int kSStages = 7;  // ring stages per warp
+constexpr int kSStageW = kSCH * 512;
+constexpr int kSStageS = kSCH * 64;  // scale bytes per stage (max: affine, one group per k-block)
+constexpr int kSRing = (kSStages * (kSStageW + kSStageS) + kSStages * 8 + 127) / 128 * 128;
+constexpr int kSUnion = 96 * 1024;  // staged activations, or the two attention groups' working sets
+constexpr int kSMisc = 512;         // reduction scratch + attention mbarriers
+constexpr size_t kSSmem = (size_t)kSW * kSRing + kSUnion + kSMisc;
+constexpr int kSGroups = 2;  // attention groups (4 warps each) per CTA
+constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint32_t kSMbarLimit = 1u << 22;
+constexpr int kMaxRepS = 8;  // q heads per kv head
+static_assert(kSSmem <= 227 * 1024, "step kernel shared memory");
+static_assert(kSStageW % 16 == 0 && kSStageS % 16 == 0 && kSRing % 128 == 0, "bulk-copy alignment");
+static_assert((kSStages * (kSStageW + kSStageS)) % 8 == 0, "mbarrier alignment");
+static_assert(kSW == 4 * kSGroups, "attention groups are 4 warps");
+
+// ------------------------------------------------------------------ helpers
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void group_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+// barrier of one attention group that also ORs a predicate over its 128 threads
+__device__ __forceinline__ bool group_bar_or(int id, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred q, o;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred o, %2, 128, q;\n selp.u32 %0, 1, 0, o;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)p), "r"(id)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ int tiles_of(int n) { return (n + 15) >> 4; }
+
+// Bounded wait for *ctr >= target.  Gives up early when another CTA has already
+// raised the abort flag; on running out it raises the flag and records
+// AXB_ETIMEOUT in the error word.
+__device__ bool wait_ge(const int* ctr, int target, const StepArgs& a) {
+  int* abort_flag = a.exit_cnt + 1;
+  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+    if (ld_acquire(ctr) >= target) return true;
+    if ((it & 15) == 15 && *reinterpret_cast<volatile int*>(abort_flag) != 0) return false;
+    __nanosleep(it < 32 ? 20 : 200);
+  }
+  atomicExch(abort_flag, 1);
+  atomicExch(a.err, AXB_ETIMEOUT);
+  return false;
+}
+
+__device__ void raise_abort(const StepArgs& a) {
+  atomicExch(a.exit_cnt + 1, 1);
+  atomicExch(a.err, AXB_ETIMEOUT);
+}
+
+// CTA-wide wait: thread 0 polls, the barrier publishes the outcome.
+__device__ bool cta_wait(const int* ctr, int target, const StepArgs& a, bool ok) {
+  int good = 0;
+  if (threadIdx.x == 0 && ok) {
+    good = wait_ge(ctr, target, a) ? 1 : 0;
+    __threadfence();
+  }
+  return __syncthreads_or(good) != 0;
+}
+
+// ------------------------------------------------------------------ GEMV phases
+// phase p: 4*l + {0 QKV, 1 o, 2 gate_up, 3 down}; 4*L = lm_head
+struct GPh {
+  const char* W;
+  const char* S;
+  int N, K, upt, kind;
+  long long U;
+};
+
+// Warps that share a GEMV: min(warps, units), so every participating warp
+// owns at least one unit (the arrival count of a split tile relies on it).
+// Virtual warp v owns units [v*U/We, (v+1)*U/We); v = wid * C + cta spreads a
+// small GEMV over all CTAs.
+__device__ __forceinline__ long long eff_warps(long long U, int Wt) { return U < Wt ? U : (long long)Wt; }
+
+__device__ __forceinline__ GPh gph(const StepArgs& a, int ph) {
+  GPh g;
+  if (ph >= 4 * a.L) {
+    g.W = a.lm_w;
+    g.S = a.lm_s;
+    g.N = a.V;
+    g.K = a.d;
+    g.kind = 4;
+  } else {
+    const StepLayer* ly = a.layers + (ph >> 2);
+    const int k = ph & 3;
+    g.W = ly->w[k];
+    g.S = ly->s[k];
+    g.kind = k;
+    switch (k) {
+      case 0: g.N = (a.Hq + 2 * a.Hkv) * a.hd; g.K = a.d; break;
+      case 1: g.N = a.d; g.K = a.Hq * a.hd; break;
+      case 2: g.N = 2 * a.F; g.K = a.d; break;
+      default: g.N = a.d; g.K = a.F; break;
+    }
+  }
+  g.upt = g.K / a.group;
+  g.U = (long long)tiles_of(g.N) * g.upt;
+  return g;
+}
+
+// Producer cursor over a warp's weight stream (lane 0 only).
+struct Cur {
+  int ph, t, t_last, kb, kb_end, upt;
+  long long u0, u1;
+  const char* W;
+  const char* S;
+};
+
+template <int GB>
+__device__ __forceinline__ void cur_tile(Cur& c) {
+  c.kb = (int)max(c.u0, (long long)c.t * c.upt) * GB;
+  c.kb_end = (int)min(c.u1, (long long)(c.t + 1) * c.upt) * GB;
+}
+
+template <int GB>
+__device__ void cur_load(Cur& c, const StepArgs& a, int gw, int Wt) {
+  const GPh g = gph(a, c.ph);
+  c.W = g.W;
+  c.S = g.S;
+  c.upt = g.upt;
+  const long long We = eff_warps(g.U, Wt);
+  c.u0 = gw < We ? (long long)gw * g.U / We : 0;
+  c.u1 = gw < We ? (long long)(gw + 1) * g.U / We : 0;
+  if (c.u0 >= c.u1) {
+    c.t = 0;
+    c.t_last = -1;
+    c.kb = c.kb_end = 0;
+    return;
+  }
+  c.t = (int)(c.u0 / c.upt);
+  c.t_last = (int)((c.u1 - 1) / c.upt);
+  cur_tile<GB>(c);
+}
+
+// advance past exhausted tiles / phases; false at the end of the step
+template <int GB>
+__device__ bool cur_fix(Cur& c, const StepArgs& a, int gw, int Wt) {
+  while (c.kb >= c.kb_end) {
+    if (c.t < c.t_last) {
+      ++c.t;
+      cur_tile<GB>(c);
+      continue;
+    }
+    if (c.ph >= 4 * a.L) return false;
+    ++c.ph;
+    cur_load<GB>(c, a, gw, Wt);
+  }
+  return true;
+}
+
+struct Ring {
+  char* buf;
+  uint64_t* bars;
+  int ci, pi;  // stages consumed / issued
+};
+
+template <bool SYM, int GB>
+__device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, Cur& pf, const StepArgs& a, int gw, int Wt, int lane) {
+  if (lane != 0) return;
+  constexpr int UB = SYM ? 32 : 64;  // scale bytes per group
+  if (!cur_fix<GB>(pc, a, gw, Wt)) return;
+  const int st = r.pi % kSStages;
+  const int n = min(kSCH, pc.kb_end - pc.kb);
+  const uint32_t bw = n * 512, bs = (n / GB) * UB;
+  fence_proxy_async();
+  mbar_expect_tx(r.bars + st, bw + bs);
+  bulk_g2s(r.buf + st * kSStageW, pc.W + (size_t)pc.kb * 512, bw, r.bars + st);
+  bulk_g2s(r.buf + kSStages * kSStageW + st * kSStageS, pc.S + (size_t)(pc.kb / GB) * UB, bs, r.bars + st);
+  pc.kb += n;
+  ++r.pi;
+  // keep the L2 prefetch cursor l2_ahead stages beyond the ring's leading edge
+  if (a.l2_ahead > 0 && cur_fix<GB>(pf, a, gw, Wt)) {
+    const int n2 = min(kSCH, pf.kb_end - pf.kb);
+    prefetch_l2(pf.W + (size_t)pf.kb * 512, n2 * 512);
+    prefetch_l2(pf.S + (size_t)(pf.kb / GB) * UB, (n2 / GB) * UB);
+    pf.kb += n2;
+  }
+}
+
+__device__ __forceinline__ int warp_of_unit(long long u, long long U, long long Wt) {
+  return (int)(((u + 1) * Wt - 1) / U);
+}
+
+// Tile epilogue: token n = 2*t4 + e, rows tile*16 + g (+8).
+__device__ void step_epilogue(const StepArgs& a, const GPh& g, int tile, const float (&acc)[4], int lane) {
+  const int gg = lane >> 2, t4 = lane & 3;
+  const int r0 = tile * 16 + gg, r1 = r0 + 8;
+  const int M = a.B;
+  unsigned long long best[2] = {0ull, 0ull};
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int n = 2 * t4 + e;
+    if (n >= M) continue;
+    const float v0 = acc[e], v1 = acc[2 + e];
+    if (g.kind == 2) {  // SwiGLU: rows g (gate) and g + 8 (up) of the interleaved tile
+      const int j = tile * 8 + gg;
+      if (j < a.F) {
+        const float gv = __half2float(__float2half_rn(v0));
+        const float uv = __half2float(__float2half_rn(v1));
+        a.sw[(size_t)n * a.F + j] = __float2half_rn(__fmul_rn(silu_f(gv), uv));
+      }
+      continue;
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = h ? r1 : r0;
+      if (row >= g.N) continue;
+      float v = h ? v1 : v0;
+      if (g.kind == 0) {
+        a.qkv[(size_t)n * g.N + row] = __float2half_rn(v);
+      } else if (g.kind == 4) {
+        const __half vh = __float2half_rn(v);
+        a.logits[(size_t)n * a.V + row] = vh;
+        // argmax key: ordered value bits, then the lowest row wins ties
+        uint32_t bits = __float_as_uint(__half2float(vh));
+        bits = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+        const unsigned long long key = ((unsigned long long)bits << 32) | (0xFFFFFFFFu - (uint32_t)row);
+        best[e] = key > best[e] ? key : best[e];
+      } else {  // residual add into h (fp16 GEMV output, fp16 sum)
+        __half* hp = a.h + (size_t)n * a.d + row;
+        const float old = __half2float(__ldcg(hp));
+        *hp = __float2half_rn(__fadd_rn(old, __half2float(__float2half_rn(v))));
+      }
+    }
+  }
+  if (g.kind == 4) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      unsigned long long k = best[e];
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
+        k = ok > k ? ok : k;
+      }
+      const int n = 2 * t4 + e;
+      if (gg == 0 && n < M && k) atomicMax(a.keys + n, k);
+    }
+  }
+}
+
+// QKV bias (c_attn_bs) is folded in by the QKV tile finisher
+__device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const StepLayer* ly, const GPh& g, int tile,
+                                             float (&acc)[4], int lane) {
+  if (g.kind != 0 || ly == nullptr || ly->qkv_b == nullptr) return;
+  const int gg = lane >> 2;
+  const int r0 = tile * 16 + gg, r1 = r0 + 8;
+  if (r0 < g.N) {
+    const float b0 = __half2float(ly->qkv_b[r0]);
+    acc[0] = __fadd_rn(acc[0], b0);
+    acc[1] = __fadd_rn(acc[1], b0);
+  }
+  if (r1 < g.N) {
+    const float b1 = __half2float(ly->qkv_b[r1]);
+    acc[2] = __fadd_rn(acc[2], b1);
+    acc[3] = __fadd_rn(acc[3], b1);
+  }
+}
+
+// One GEMV phase for this warp.  x is staged in shared memory (XS: normalized
+// rows + per-group sums) or read from global memory (L2) one k-block ahead.
+template <bool SYM, int GB, bool XS>
+__device__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf, const __half* xs, int xs_stride,
+                           const float* xsum, int xsum_ld, const __half* xg, int ldx, int gw, int Wt, int lane,
+                           bool ok, int* done_ctr) {
+  const GPh g = gph(a, ph);
+  const long long We = eff_warps(g.U, Wt);
+  if (gw >= We || !ok) return ok;
+  const long long u0 = (long long)gw * g.U / We, u1 = (long long)(gw + 1) * g.U / We;
+  const StepLayer* ly = ph < 4 * a.L ? a.layers + (ph >> 2) : nullptr;
+  const int gq = lane >> 2, t4 = lane & 3;
+  const int KB = g.K / 64;
+  const int t_first = (int)(u0 / g.upt), t_last = (int)((u1 - 1) / g.upt);
+  const int nn = min(gq, a.B - 1);
+  const uint4* xrow = reinterpret_cast<const uint4*>((XS ? xs + (size_t)nn * xs_stride : xg + (size_t)nn * ldx) +
+                                                     16 * t4);
+  int finished = 0;
+  constexpr int CH = 2;
+  for (int t = t_first; t <= t_last && ok; ++t) {
+    const int kb_lo = (int)max(u0, (long long)t * g.upt) * GB;
+    const int kb_hi = (int)min(u1, (long long)(t + 1) * g.upt) * GB;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float tmp[CH][4];
+#pragma unroll
+    for (int c2 = 0; c2 < CH; ++c2)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tmp[c2][q] = 0.f;
+    uint4 xn0 = make_uint4(0, 0, 0, 0), xn1 = xn0;
+    if (!XS) {
+      xn0 = __ldcg(xrow + (kb_lo - t * KB) * 8);
+      xn1 = __ldcg(xrow + (kb_lo - t * KB) * 8 + 1);
+    }
+    for (int kb0 = kb_lo; kb0 < kb_hi;) {
+      const int st = r.ci % kSStages;
+      const bool got = mbar_wait(r.bars + st, (uint32_t)((r.ci / kSStages) & 1), kSMbarLimit);
+      if (!__all_sync(0xffffffffu, got)) {  // one decision for the whole warp
+        if (lane == 0) raise_abort(a);
+        ok = false;
+        break;
+      }
+      const int n = min(kSCH, kb_hi - kb0);
+      const uint4* wst = reinterpret_cast<const uint4*>(r.buf + st * kSStageW) + lane;
+      const char* sst = r.buf + kSStages * kSStageW + st * kSStageS;
+      const int kbt = kb0 - t * KB;
+      auto kblock = [&](const int j) {
+        const uint4 cur = wst[j * 32];
+        uint32_t bf[8];
+        if (XS) {
+          const uint4 v0 = xrow[(kbt + j) * 8], v1 = xrow[(kbt + j) * 8 + 1];
+          bf[0] = v0.x; bf[1] = v0.y; bf[2] = v0.z; bf[3] = v0.w;
+          bf[4] = v1.x; bf[5] = v1.y; bf[6] = v1.z; bf[7] = v1.w;
+        } else {
+          bf[0] = xn0.x; bf[1] = xn0.y; bf[2] = xn0.z; bf[3] = xn0.w;
+          bf[4] = xn1.x; bf[5] = xn1.y; bf[6] = xn1.z; bf[7] = xn1.w;
+          if (kb0 + j + 1 < kb_hi) {
+            xn0 = __ldcg(xrow + (kbt + j + 1) * 8);
+            xn1 = __ldcg(xrow + (kbt + j + 1) * 8 + 1);
+          }
+        }
+        const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
+        if (SYM && XS) {
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            uint32_t af[4];
+            unpack_word_raw(words[jj], af);
+            mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
+          }
+          if (GB == 1 || (j & 1)) {  // group complete: remove the offsets, apply the scales
+            const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[(j / GB) * 8 + gq];
+            const float2 sc = __half22float2(u32_as_h2(sp));
+            const int grp = (kbt + j) / GB;
+            const float2 xg2 = *reinterpret_cast<const float2*>(xsum + grp * xsum_ld + 2 * t4);
+            float s4[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              s4[q] = tmp[0][q] + tmp[1][q];
+              tmp[0][q] = tmp[1][q] = 0.f;
+            }
+            acc[0] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.x, s4[0]), acc[0]);
+            acc[1] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.y, s4[1]), acc[1]);
+            acc[2] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[2], -72.f * xg2.x), acc[2]);
+            acc[3] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[3], -72.f * xg2.y), acc[3]);
+          }
+        } else if (SYM) {
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            uint32_t af[4];
+            unpack_word<8>(words[jj], af);
+            mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
+          }
+          if (GB == 1 || (j & 1)) {
+            const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[(j / GB) * 8 + gq];
+            const float2 sc = __half22float2(u32_as_h2(sp));
+            float s4[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              s4[q] = tmp[0][q] + tmp[1][q];
+              tmp[0][q] = tmp[1][q] = 0.f;
+            }
+            acc[0] = __fmaf_rn(sc.x, s4[0], acc[0]);
+            acc[1] = __fmaf_rn(sc.x, s4[1], acc[1]);
+            acc[2] = __fmaf_rn(sc.y, s4[2], acc[2]);
+            acc[3] = __fmaf_rn(sc.y, s4[3], acc[3]);
+          }
+        } else {
+          const uint2 sb = reinterpret_cast<const uint2*>(sst)[(j / GB) * 8 + gq];
+          const __half2 s01 = u32_as_h2(sb.x), s23 = u32_as_h2(sb.y);
+          const __half2 sg = __half2half2(__low2half(s01)), bg = __half2half2(__high2half(s01));
+          const __half2 sg8 = __half2half2(__low2half(s23)), bg8 = __half2half2(__high2half(s23));
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            uint32_t af[4];
+            unpack_word<0>(words[jj], af);
+            af[0] = h2_as_u32(__hfma2(u32_as_h2(af[0]), sg, bg));
+            af[1] = h2_as_u32(__hfma2(u32_as_h2(af[1]), sg8, bg8));
+            af[2] = h2_as_u32(__hfma2(u32_as_h2(af[2]), sg, bg));
+            af[3] = h2_as_u32(__hfma2(u32_as_h2(af[3]), sg8, bg8));
+            mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
+          }
+        }
+      };
+      if (n == kSCH) {
+#pragma unroll
+        for (int j = 0; j < kSCH; ++j) kblock(j);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kSCH; ++j)
+          if (j < n) kblock(j);
+      }
+      __syncwarp();
+      ring_issue<SYM, GB>(r, pc, pf, a, gw, Wt, lane);
+      ++r.ci;
+      kb0 += n;
+    }
+    if (!ok) break;
+    if (!SYM) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] = tmp[0][q] + tmp[1][q];
+    }
+    const bool complete = (long long)t * g.upt >= u0 && (long long)(t + 1) * g.upt <= u1;
+    if (complete) {
+      qkv_bias_fix(a, ly, g, t, acc, lane);
+      step_epilogue(a, g, t, acc, lane);
+      ++finished;
+      continue;
+    }
+    const int slot = (t == t_first) ? 0 : 1;
+    float* p = a.partials + ((size_t)(gw * 2 + slot) * 32 + lane) * 4;
+    *reinterpret_cast<float4*>(p) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    __threadfence();
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atomicAdd(a.tile_cnt + t, 1);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    const int wf = warp_of_unit((long long)t * g.upt, g.U, We);
+    const int wl = warp_of_unit((long long)(t + 1) * g.upt - 1, g.U, We);
+    if (old != wl - wf) continue;
+    __threadfence();
+    float tot[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int w0 = wf; w0 <= wl; w0 += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {  // independent loads, all in flight
+        const int w = w0 + u;
+        if (w > wl) continue;
+        const int sl = ((long long)w * g.U / We) / g.upt == t ? 0 : 1;
+        v[u] = __ldcg(reinterpret_cast<const float4*>(a.partials + ((size_t)(w * 2 + sl) * 32 + lane) * 4));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (w0 + u > wl) continue;
+        tot[0] += v[u].x;
+        tot[1] += v[u].y;
+        tot[2] += v[u].z;
+        tot[3] += v[u].w;
+      }
+    }
+    qkv_bias_fix(a, ly, g, t, tot, lane);
+    step_epilogue(a, g, t, tot, lane);
+    if (lane == 0) atomicExch(a.tile_cnt + t, 0);
+    ++finished;
+  }
+  if (finished) {
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) atomicAdd(done_ctr, finished);
+  }
+  return ok;
+}
+
+// ------------------------------------------------------------------ staging
+// Embedding rows (dequant_q8_rows, quant.py:132-163) into xs; CTA 0 also
+// stores them into h (the residual stream).
+__device__ void stage_embed(const StepArgs& a, __half* xs, int stride) {
+  const int K4 = a.d / 4;
+  for (int i = threadIdx.x; i < a.B * K4; i += blockDim.x) {
+    const int m = i / K4, k4 = i % K4;
+    const int r = a.tokens[m];
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (r >= 0 && r < a.V) {
+      const uint32_t word = a.emb_w[(size_t)r * K4 + k4];
+      const __half2 p = reinterpret_cast<const __half2*>(a.emb_s)[(size_t)r * (a.d / 64) + k4 / 16];
+      const float s = __low2float(p), bi = __high2float(p);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = __fadd_rn(__fmul_rn((float)((word >> (8 * j)) & 0xFF), s), bi);
+    } else if (blockIdx.x == 0 && k4 == 0) {
+      atomicExch(a.err, AXB_EINVAL);  // out-of-vocabulary id: zero row
+    }
+    __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
+    uint2 pk = make_uint2(h2_as_u32(h01), h2_as_u32(h23));
+    *reinterpret_cast<uint2*>(xs + (size_t)m * stride + 4 * k4) = pk;
+    if (blockIdx.x == 0) *reinterpret_cast<uint2*>(a.h + (size_t)m * a.d + 4 * k4) = pk;
+  }
+}
+
+// RMSNorm (modules.py:30-43: rms = 1/sqrt(mean(x^2) + eps), fp16((x * rms) * w))
+// of M rows of h (or of the raw rows already in xs when src is null) into xs,
+// then (SYM) the fp32 per-group sums of the normalized rows.
+__device__ void stage_norm(const StepArgs& a, const __half* src, const float* w, __half* xs, int stride, float* xsum,
+                           int xsum_ld, bool sums, float* red) {
+  const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, wid = tid >> 5;
+  const int K = a.d, K8 = K / 8;
+  for (int m = 0; m < a.B; ++m) {
+    float ss = 0.f;
+    for (int c = tid; c < K8; c += nth) {
+      uint4 v;
+      if (src) {
+        v = __ldcg(reinterpret_cast<const uint4*>(src + (size_t)m * K) + c);
+        reinterpret_cast<uint4*>(xs + (size_t)m * stride)[c] = v;
+      } else {
+        v = reinterpret_cast<const uint4*>(xs + (size_t)m * stride)[c];
+      }
+      const __half2* hh = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __half22float2(hh[q]);
+        ss = __fmaf_rn(f.x, f.x, ss);
+        ss = __fmaf_rn(f.y, f.y, ss);
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[wid * kStepMaxM + m] = ss;
+  }
+  __syncthreads();
+  for (int i = tid; i < a.B * K8; i += nth) {
+    const int m = i / K8, c = i % K8;
+    float tot = 0.f;
+    for (int ww = 0; ww < (nth >> 5); ++ww) tot += red[ww * kStepMaxM + m];
+    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+    uint4* sp = reinterpret_cast<uint4*>(xs + (size_t)m * stride) + c;
+    const uint4 v = *sp;
+    const __half2* hh = reinterpret_cast<const __half2*>(&v);
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c);
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c + 1);
+    const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    uint4 o;
+    __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __half22float2(hh[q]);
+      oh[q] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, rms), ws[2 * q]),
+                                __fmul_rn(__fmul_rn(f.y, rms), ws[2 * q + 1]));
+    }
+    *sp = o;
+  }
+  __syncthreads();
+  if (sums) {
+    const int G = a.group, ngr = K / G, nw = nth >> 5;
+    for (int item = wid; item < ngr * a.B; item += nw) {
+      const int grp = item % ngr, m = item / ngr;
+      const __half* s = xs + (size_t)m * stride + grp * G;
+      float v = 0.f;
+      for (int k = lane * 2; k < G; k += 64) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(s + k));
+        v += f.x + f.y;
+      }
+      v = warp_sum(v);
+      if (lane == 0) xsum[grp * xsum_ld + m] = v;
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ attention
+struct AttnLayout {
+  int rb, ng, kv, q, p, ks, vs, ml, coef, bytes;
+};
+
+__host__ __device__ inline AttnLayout attn_layout(int kv_type, int hd, int kv_group, int cap) {
+  AttnLayout L;
+  L.rb = kv_row_bytes(kv_type, hd);
+  L.ng = kv_type == AXB_KV_F16 ? 1 : hd / kv_group;
+  int off = 0;
+  L.kv = off;
+  off += 2 * cap * L.rb;
+  off = (off + 15) / 16 * 16;
+  L.q = off;
+  off += 8 * hd * 4;
+  L.p = off;
+  off += 8 * cap * 4;
+  L.ks = off;
+  off += cap * L.ng * 4;
+  L.vs = off;
+  off += cap * L.ng * 4;
+  L.ml = off;
+  off += 32 * 4;  // m[8], l[8], alpha[8], flags
+  L.coef = off;
+  off += 8 * kStepMaxSplits * 4;
+  L.bytes = (off + 127) / 128 * 128;
+  return L;
+}
+
+__device__ __forceinline__ void attn_split_plan(int active, int units, int cap, int& nsplit, int& chunk) {
+  int target = units;
+  if (target > kStepMaxSplits) target = kStepMaxSplits;
+  if (target < 1) target = 1;
+  chunk = (active + target - 1) / target;
+  chunk = (chunk + 15) / 16 * 16;
+  if (chunk < 16) chunk = 16;
+  nsplit = (active + chunk - 1) / chunk;
+  (void)cap;
+}
+
+// Issue the bulk copy of cached K/V rows [c0, c0 + nt) of one head (group thread 0).
+__device__ __forceinline__ void attn_copy(const StepLayer* ly, size_t head_base, int rb, int c0, int nt, char* gsm,
+                                          const AttnLayout& Lo, int cap, uint64_t* bar) {
+  fence_proxy_async();
+  mbar_expect_tx(bar, 2u * nt * rb);
+  bulk_g2s(gsm + Lo.kv, ly->kc + (head_base + c0) * rb, nt * rb, bar);
+  bulk_g2s(gsm + Lo.kv + (size_t)cap * rb, ly->vc + (head_base + c0) * rb, nt * rb, bar);
+}
+
+struct AttnItem {
+  int b, kvh, split, t0, t1;
+};
+
+__device__ __forceinline__ AttnItem attn_item_of(int item, int nsplit, int chunk, int Hkv, int active) {
+  AttnItem it;
+  it.split = item % nsplit;
+  const int r2 = item / nsplit;
+  it.kvh = r2 % Hkv;
+  it.b = r2 / Hkv;
+  it.t0 = it.split * chunk;
+  it.t1 = min(active, it.t0 + chunk);
+  return it;
+}
+
+// One attention item (sequence b, kv head, split) on a group of 4 warps.
+// gt = thread index in the group, gwarp = warp index in the group.
+template <int HD>
+__device__ bool attn_item(const StepArgs& a, const StepLayer* ly, const AttnItem& it, int nsplit, bool prefetched,
+                          char* gsm, uint64_t* bar, uint32_t& uses, int bar_id, int gt, int* done_ctr, bool ok) {
+  constexpr int DPL = HD / 32, EPT = HD / 16;
+  const int lane = gt & 31, gwarp = gt >> 5;
+  const int cap = a.attn_cap;
+  const AttnLayout Lo = attn_layout(a.kv_type, HD, a.kv_group, cap);
+  const int rb = Lo.rb, ng = Lo.ng, G = a.kv_group;
+  const bool quant = a.kv_type != AXB_KV_F16;
+  const int n_rep = a.Hq / a.Hkv, hq0 = it.kvh * n_rep;
+  const int rpos = a.params[0], wpos = a.params[1];
+  const size_t head_base = ((size_t)it.b * a.Hkv + it.kvh) * a.S;
+  char* kst = gsm + Lo.kv;
+  char* vst = kst + (size_t)cap * rb;
+  float* q_s = reinterpret_cast<float*>(gsm + Lo.q);
+  float* p_s = reinterpret_cast<float*>(gsm + Lo.p);
+  float* ks_s = reinterpret_cast<float*>(gsm + Lo.ks);
+  float* vs_s = reinterpret_cast<float*>(gsm + Lo.vs);
+  float* ml_s = reinterpret_cast<float*>(gsm + Lo.ml);  // m[8] l[8] alpha[8] flag
+  float* coef = reinterpret_cast<float*>(gsm + Lo.coef);
+  float* o_red = reinterpret_cast<float*>(kst);
+  const __half* ksc = quant ? ly->ks + head_base * ng : nullptr;
+  const __half* vsc = quant ? ly->vs + head_base * ng : nullptr;
+
+  // ---- q with RoPE (fp32), the new K/V row rotated, quantized and written
+  const int qkv_dim = (a.Hq + 2 * a.Hkv) * HD;
+  const __half* row = a.qkv + (size_t)it.b * qkv_dim;
+  const float* fr = a.rope + (size_t)(rpos % a.rope_len) * HD;
+  for (int i = gt; i < n_rep * HD / 2; i += 128) {
+    const int rr = i / (HD / 2), pr = i % (HD / 2);
+    const __half2 x2 = __ldcg(reinterpret_cast<const __half2*>(row + (hq0 + rr) * HD) + pr);
+    const float a0 = __low2float(x2), a1 = __high2float(x2);
+    const float c = fr[2 * pr], sn = fr[2 * pr + 1];
+    q_s[rr * HD + 2 * pr] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, sn));
+    q_s[rr * HD + 2 * pr + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, c));
+  }
+  if (gt < 8) {
+    ml_s[gt] = -INFINITY;
+    ml_s[8 + gt] = 0.f;
+  }
+  float nkv[DPL];
+  const bool covers = wpos >= it.t0 && wpos < it.t1;
+  if (covers && gwarp < 2) {
+    const __half* src = row + (size_t)(a.Hq + (gwarp == 0 ? 0 : a.Hkv) + it.kvh) * HD;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) nkv[e] = __half2float(__ldcg(src + lane * DPL + e));
+    if (gwarp == 0) {  // RoPE on K, every product rounded (transformer.py:1105-1127)
+#pragma unroll
+      for (int e = 0; e < DPL; e += 2) {
+        const int pr = (lane * DPL + e) >> 1;
+        const float c = fr[2 * pr], sn = fr[2 * pr + 1], a0 = nkv[e], a1 = nkv[e + 1];
+        nkv[e] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, sn));
+        nkv[e + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, c));
+      }
+    }
+    uint8_t* crow = (gwarp == 0 ? ly->kc : ly->vc) + (head_base + wpos) * rb;
+    __half* srow = quant ? (gwarp == 0 ? ly->ks : ly->vs) + (head_base + wpos) * ng : nullptr;
+    store_kv_row<DPL>(nkv, lane, a.kv_type, G, true, crow, srow);
+  }
+  group_bar(bar_id);
+
+  float acc[kMaxRepS][DPL];
+#pragma unroll
+  for (int r = 0; r < kMaxRepS; ++r)
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) acc[r][e] = 0.f;
+  const float sm_scale = 1.0f / sqrtf((float)HD);
+  bool first = true;
+  for (int c0 = it.t0; c0 < it.t1 && ok; c0 += cap) {
+    const int nt = min(cap, it.t1 - c0);
+    if (!(first && prefetched) && gt == 0) attn_copy(ly, head_base, rb, c0, nt, gsm, Lo, cap, bar);
+    first = false;
+    if (quant)
+      for (int j = gt; j < nt * ng; j += 128) {
+        ks_s[j] = __half2float(ksc[(size_t)c0 * ng + j]);
+        vs_s[j] = __half2float(vsc[(size_t)c0 * ng + j]);
+      }
+    const bool got = mbar_wait(bar, uses & 1, kSMbarLimit);
+    ++uses;
+    if (group_bar_or(bar_id, !got)) {  // one decision for the whole group
+      if (gt == 0) raise_abort(a);
+      ok = false;
+      break;
+    }
+    if (covers && gwarp < 2 && wpos >= c0 && wpos < c0 + nt) {
+      // the copy may have read the slot before this step wrote it
+      uint8_t* rowp = reinterpret_cast<uint8_t*>(gwarp == 0 ? kst : vst) + (size_t)(wpos - c0) * rb;
+      store_kv_row<DPL>(nkv, lane, a.kv_type, G, true, rowp, nullptr);
+    }
+    group_bar(bar_id);
+    // scores: EPT threads per token, 16 elements each
+    for (int base = 0; base < nt; base += 128 / EPT) {
+      const int tk = base + gt / EPT, ch = gt % EPT;
+      float part[kMaxRepS];
+#pragma unroll
+      for (int r = 0; r < kMaxRepS; ++r) part[r] = 0.f;
+      if (tk < nt) {
+        float kv[16];
+        kv_load16(reinterpret_cast<const uint8_t*>(kst) + (size_t)tk * rb, a.kv_type, ch * 16, kv);
+        const float s = quant ? ks_s[tk * ng + (ch * 16) / G] : 1.f;
+#pragma unroll
+        for (int r = 0; r < kMaxRepS; ++r) {
+          if (r < n_rep) {
+            float d = 0.f;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) d = __fmaf_rn(q_s[r * HD + ch * 16 + e], kv[e], d);
+            part[r] = d * s;
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kMaxRepS; ++r) {
+        float v = part[r];
+        for (int o = 1; o < EPT; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (ch == 0 && tk < nt && r < n_rep) p_s[r * cap + tk] = v * sm_scale;
+      }
+    }
+    group_bar(bar_id);
+    // online softmax over the sub-chunk: warp w handles heads w, w + 4
+    for (int r = gwarp; r < n_rep; r += 4) {
+      float mx = -INFINITY;
+      for (int tk = lane; tk < nt; tk += 32) mx = fmaxf(mx, p_s[r * cap + tk]);
+      mx = warp_max(mx);
+      const float m_old = ml_s[r];
+      const float m_new = fmaxf(m_old, mx);
+      float sum = 0.f;
+      for (int tk = lane; tk < nt; tk += 32) {
+        const float e = __expf(p_s[r * cap + tk] - m_new);
+        p_s[r * cap + tk] = e;
+        sum += e;
+      }
+      sum = warp_sum(sum);
+      __syncwarp();
+      if (lane == 0) {
+        const float alpha = m_old == -INFINITY ? 0.f : __expf(m_old - m_new);
+        ml_s[r] = m_new;
+        ml_s[8 + r] = ml_s[8 + r] * alpha + sum;
+        ml_s[16 + r] = alpha;
+      }
+    }
+    group_bar(bar_id);
+    // PV: warp w takes tokens w, w + 4, ...; lane covers DPL consecutive dims
+#pragma unroll
+    for (int r = 0; r < kMaxRepS; ++r) {
+      if (r < n_rep) {
+        const float al = ml_s[16 + r];
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[r][e] *= al;
+      }
+    }
+    for (int tk = gwarp; tk < nt; tk += 4) {
+      const uint8_t* vrow = reinterpret_cast<const uint8_t*>(vst) + (size_t)tk * rb;
+      float vv[DPL];
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) vv[e] = kv_elem(vrow, a.kv_type, lane * DPL + e);
+      const float s = quant ? vs_s[tk * ng + (lane * DPL) / G] : 1.f;
+#pragma unroll
+      for (int r = 0; r < kMaxRepS; ++r) {
+        if (r < n_rep) {
+          const float pw = p_s[r * cap + tk] * s;
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) acc[r][e] = __fmaf_rn(pw, vv[e], acc[r][e]);
+        }
+      }
+    }
+    group_bar(bar_id);  // staged rows and p_s are free for the next sub-chunk
+  }
+  if (!ok) return false;
+  // ---- reduce the 4 warps' accumulators (o_red reuses the staged rows)
+#pragma unroll
+  for (int r = 0; r < kMaxRepS; ++r)
+    if (r < n_rep)
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) o_red[(gwarp * kMaxRepS + r) * HD + lane * DPL + e] = acc[r][e];
+  group_bar(bar_id);
+  const size_t pidx = (size_t)it.b * a.Hq + hq0;
+  for (int i = gt; i < n_rep * HD; i += 128) {
+    const int r = i / HD, e = i % HD;
+    const float o = o_red[(0 * kMaxRepS + r) * HD + e] + o_red[(1 * kMaxRepS + r) * HD + e] +
+                    o_red[(2 * kMaxRepS + r) * HD + e] + o_red[(3 * kMaxRepS + r) * HD + e];
+    if (nsplit == 1)
+      a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(o, ml_s[8 + r]));
+    else
+      a.part_o[((pidx + r) * kStepMaxSplits + it.split) * HD + e] = o;
+  }
+  int* flag = reinterpret_cast<int*>(ml_s + 24);
+  if (nsplit == 1) {
+    __threadfence();
+    group_bar(bar_id);
+    if (gt == 0) atomicAdd(done_ctr, 1);
+    return true;
+  }
+  if (gt < n_rep) {
+    a.part_ml[((pidx + gt) * kStepMaxSplits + it.split) * 2 + 0] = ml_s[gt];
+    a.part_ml[((pidx + gt) * kStepMaxSplits + it.split) * 2 + 1] = ml_s[8 + gt];
+  }
+  __threadfence();
+  group_bar(bar_id);
+  int* cnt = a.attn_cnt + it.b * a.Hkv + it.kvh;
+  if (gt == 0) *flag = (atomicAdd(cnt, 1) == nsplit - 1) ? 1 : 0;
+  group_bar(bar_id);
+  if (!*flag) return true;
+  __threadfence();
+  // ---- combine the splits in split order: per-head weights first
+  for (int r = gwarp; r < n_rep; r += 4) {
+    const size_t hb = (pidx + r) * kStepMaxSplits;
+    float Mx = -INFINITY;
+    for (int sp = lane; sp < nsplit; sp += 32) Mx = fmaxf(Mx, __ldcg(a.part_ml + (hb + sp) * 2));
+    Mx = warp_max(Mx);
+    float Ls = 0.f;
+    for (int sp = lane; sp < nsplit; sp += 32) {
+      const float m = __ldcg(a.part_ml + (hb + sp) * 2), l = __ldcg(a.part_ml + (hb + sp) * 2 + 1);
+      const float cw = (m == -INFINITY) ? 0.f : __expf(m - Mx);
+      coef[r * kStepMaxSplits + sp] = cw;
+      Ls += l * cw;
+    }
+    Ls = warp_sum(Ls);
+    if (lane == 0) ml_s[8 + r] = Ls;
+  }
+  group_bar(bar_id);
+  for (int i = gt; i < n_rep * HD; i += 128) {
+    const int r = i / HD, e = i % HD;
+    const size_t hb = (pidx + r) * kStepMaxSplits;
+    float O = 0.f;
+    for (int sp0 = 0; sp0 < nsplit; sp0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = (sp0 + u < nsplit) ? __ldcg(a.part_o + (hb + sp0 + u) * HD + e) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (sp0 + u < nsplit) O += v[u] * coef[r * kStepMaxSplits + sp0 + u];
+    }
+    a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, ml_s[8 + r]));
+  }
+  __threadfence();
+  group_bar(bar_id);
+  if (gt == 0) {
+    atomicExch(cnt, 0);
+    atomicAdd(done_ctr, 1);
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ kernel
+template <bool SYM, int GB, int HD>
+__global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
+  extern __shared__ __align__(128) char smem[];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int C = gridDim.x, Wt = C * kSW, gw = wid * C + blockIdx.x;  // virtual warp id
+  char* uni = smem + kSW * kSRing;
+  float* red = reinterpret_cast<float*>(uni + kSUnion);  // [kSW][kStepMaxM]
+  uint64_t* abar = reinterpret_cast<uint64_t*>(uni + kSUnion + 256);  // one per attention group
+  int* s_last = reinterpret_cast<int*>(uni + kSUnion + 256 + 64);
+
+  // staged activations: M rows of K + 8 halves, then per-(group, token) sums
+  const int xs_stride = a.d + 8;
+  __half* xs = reinterpret_cast<__half*>(uni);
+  const int xsum_ld = 16;
+  float* xsum = reinterpret_cast<float*>(uni + ((size_t)kStepMaxM * xs_stride * 2 + 127) / 128 * 128);
+
+  Ring ring;
+  ring.buf = smem + wid * kSRing;
+  ring.bars = reinterpret_cast<uint64_t*>(ring.buf + kSStages * (kSStageW + kSStageS));
+  ring.ci = 0;
+  ring.pi = 0;
+  Cur pc, pf;
+  if (lane == 0) {
+    for (int s = 0; s < kSStages; ++s) mbar_init(ring.bars + s, 1);
+    if (wid < kSGroups) mbar_init(abar + wid, 1);
+    fence_mbar_init();
+    pc.ph = 0;
+    cur_load<GB>(pc, a, gw, Wt);
+    pf = pc;
+    // the L2 prefetch cursor starts at the end of the first ring fill
+    for (int s = 0; s < kSStages && cur_fix<GB>(pf, a, gw, Wt); ++s) pf.kb += min(kSCH, pf.kb_end - pf.kb);
+    constexpr int UB = SYM ? 32 : 64;
+    for (int s = 0; s < a.l2_ahead && cur_fix<GB>(pf, a, gw, Wt); ++s) {
+      const int n2 = min(kSCH, pf.kb_end - pf.kb);
+      prefetch_l2(pf.W + (size_t)pf.kb * 512, n2 * 512);
+      prefetch_l2(pf.S + (size_t)(pf.kb / GB) * UB, (n2 / GB) * UB);
+      pf.kb += n2;
+    }
+    for (int s = 0; s < kSStages; ++s) ring_issue<SYM, GB>(ring, pc, pf, a, gw, Wt, lane);
+  }
+  __syncthreads();
+
+  bool ok = true;
+  const int qkv_dim = (a.Hq + 2 * a.Hkv) * a.hd;
+  const int t_d = tiles_of(a.d);
+  const int grp = wid >> 2, gt = tid & 127;
+  uint32_t abar_uses = 0;
+
+  // embedding rows for the first layer's QKV (every CTA stages its own copy)
+  stage_embed(a, xs, xs_stride);
+  __threadfence();
+  __syncthreads();
+  if (blockIdx.x == 0 && tid == 0) atomicAdd(a.done, 1);
+
+  for (int l = 0; l < a.L; ++l) {
+    const StepLayer* ly = a.layers + l;
+    int* dn = a.done + 1 + 5 * l;  // QKV, attention, o, gate_up, down
+    // ---- QKV (RMSNorm fused)
+    if (l > 0) ok = cta_wait(dn - 1, t_d, a, ok);
+    if (ok) stage_norm(a, l > 0 ? a.h : nullptr, ly->ln1, xs, xs_stride, xsum, xsum_ld, SYM, red);
+    ok = gemv_phase<SYM, GB, true>(a, 4 * l + 0, ring, pc, pf, xs, xs_stride, xsum, xsum_ld, nullptr, 0, gw, Wt,
+                                   lane, ok, dn + 0);
+    ok = __syncthreads_and(ok) != 0;  // the staged rows are dead: the union holds attention next
+    // ---- attention (RoPE + KV write fused)
+    {
+      const int active = a.params[2];
+      int nsplit, chunk;
+      attn_split_plan(active, (kSGroups * C) / (a.B * a.Hkv), a.attn_cap, nsplit, chunk);
+      const int n_items = a.B * a.Hkv * nsplit;
+      char* gsm = uni + grp * (kSUnion / kSGroups);
+      const AttnLayout Lo = attn_layout(a.kv_type, HD, a.kv_group, a.attn_cap);
+      int item = blockIdx.x * kSGroups + grp;
+      if (ok && item < n_items && gt == 0) {  // cached rows do not depend on this step's QKV
+        const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
+        const size_t hb = ((size_t)it.b * a.Hkv + it.kvh) * a.S;
+        attn_copy(ly, hb, Lo.rb, it.t0, min(a.attn_cap, it.t1 - it.t0), gsm, Lo, a.attn_cap, abar + grp);
+      }
+      const bool pre_ok = ok;
+      ok = cta_wait(dn + 0, tiles_of(qkv_dim), a, ok);
+      bool first = true;
+      for (; item < n_items; item += kSGroups * C) {
+        if (!ok) {
+          // a copy issued above is still owed to this group's mbarrier
+          if (first && pre_ok) mbar_wait(abar + grp, abar_uses & 1, kSMbarLimit);
+          break;
+        }
+        const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
+        ok = attn_item<HD>(a, ly, it, nsplit, first, gsm, abar + grp, abar_uses, 1 + grp, gt, dn + 1, ok);
+        first = false;
+      }
+    }
+    // ---- o projection (+ residual)
+    ok = cta_wait(dn + 1, a.B * a.Hkv, a, ok);
+    if (l == 0) ok = cta_wait(a.done, 1, a, ok);  // h holds the embedding rows
+    ok = gemv_phase<SYM, GB, false>(a, 4 * l + 1, ring, pc, pf, nullptr, 0, nullptr, 0, a.attn, a.Hq * a.hd, gw,
+                                    Wt, lane, ok, dn + 2);
+    // ---- gate_up (RMSNorm fused, SwiGLU epilogue)
+    ok = cta_wait(dn + 2, t_d, a, ok);
+    if (ok) stage_norm(a, a.h, ly->ln2, xs, xs_stride, xsum, xsum_ld, SYM, red);
+    ok = gemv_phase<SYM, GB, true>(a, 4 * l + 2, ring, pc, pf, xs, xs_stride, xsum, xsum_ld, nullptr, 0, gw, Wt,
+                                   lane, ok, dn + 3);
+    // ---- down projection (+ residual)
+    ok = cta_wait(dn + 3, tiles_of(2 * a.F), a, ok);
+    ok = gemv_phase<SYM, GB, false>(a, 4 * l + 3, ring, pc, pf, nullptr, 0, nullptr, 0, a.sw, a.F, gw, Wt, lane,
+                                    ok, dn + 4);
+  }
+  // ---- lm_head (final RMSNorm fused) + argmax keys
+  ok = cta_wait(a.done + 5 * a.L, t_d, a, ok);
+  if (ok) stage_norm(a, a.h, a.ln_f, xs, xs_stride, xsum, xsum_ld, SYM, red);
+  ok = gemv_phase<SYM, GB, true>(a, 4 * a.L, ring, pc, pf, xs, xs_stride, xsum, xsum_ld, nullptr, 0, gw, Wt, lane,
+                                 ok, a.done + 1 + 5 * a.L);
+
+  // ---- wind down: copies still in flight (only after an abort) get a bounded wait
+  for (int i = ring.ci; i < ring.pi; ++i) mbar_wait(ring.bars + (i % kSStages), (uint32_t)((i / kSStages) & 1), kSMbarLimit);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) *s_last = (atomicAdd(a.exit_cnt, 1) == C - 1) ? 1 : 0;
+  __syncthreads();
+  if (!*s_last) return;
+  __threadfence();
+  // last CTA: publish the argmax, return every counter to zero
+  if (tid < a.B) {
+    const unsigned long long k = __ldcg(a.keys + tid);
+    a.amax[tid] = k ? (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
+    a.keys[tid] = 0ull;
+  }
+  for (int i = tid; i < 2 + 5 * a.L; i += blockDim.x) a.done[i] = 0;
+  if (*reinterpret_cast<volatile int*>(a.exit_cnt + 1) != 0) {  // an aborted step may leave arrivals behind
+    for (int i = tid; i < a.max_tiles; i += blockDim.x) a.tile_cnt[i] = 0;
+    for (int i = tid; i < a.B * a.Hkv; i += blockDim.x) a.attn_cnt[i] = 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    a.exit_cnt[1] = 0;
+    a.exit_cnt[0] = 0;
+  }
+}
+
+// ------------------------------------------------------------------ host
+int step_num_warps() { return kSW; }
+
+int step_attn_cap(int kv_type, int hd, int kv_group) {
+  for (int cap = 256; cap >= 16; cap -= 16) {
+    const AttnLayout L = attn_layout(kv_type, hd, kv_group, cap);
+    if (L.bytes <= kSUnion / kSGroups && 2 * cap * L.rb >= 4 * 8 * hd * 4) return cap;
+  }
+  return 0;
+}
+
+bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n_head, int n_kv_head, int d_model,
+                    int kv_type, int kv_group) {
+  if (wfmt != lm_fmt || group != lm_group) return false;
+  if (wfmt != AXB_W_Q4T_SYM && wfmt != AXB_W_Q4T_AFFINE) return false;
+  if (group != 64 && group != 128) return false;
+  if (hd != 64 && hd != 128) return false;
+  if (n_kv_head <= 0 || n_head % n_kv_head != 0 || n_head / n_kv_head > 8) return false;
+  if (d_model % 128 != 0) return false;
+  const size_t xsb = ((size_t)kStepMaxM * (d_model + 8) * 2 + 127) / 128 * 128;
+  if (xsb + (size_t)(d_model / 64) * 16 * 4 > (size_t)kSUnion) return false;
+  if (kv_type != AXB_KV_F16 && (kv_group < 16 || hd % kv_group != 0)) return false;  // 16 elements share a scale in the score loads
+  return step_attn_cap(kv_type, hd, kv_group) > 0;
+}
+
+#define AXB_STEP_KERNELS(X) \
+  X(true, 2, 128) X(true, 1, 128) X(false, 2, 128) X(false, 1, 128) X(true, 2, 64) X(true, 1, 64) X(false, 2, 64) X(false, 1, 64)
+
+int step_prepare() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int done_dev = -1;
+  if (done_dev == dev) return AXB_OK;
+#define AXB_SET(SYM, GB, HD)                                                                                 \
+  {                                                                                                         \
+    cudaError_t e = cudaFuncSetAttribute(step_kernel<SYM, GB, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                         (int)kSSmem);                                                      \
+    if (e != cudaSuccess) return cuda_status(e, "step kernel attribute");                                   \
+  }
+  AXB_STEP_KERNELS(AXB_SET)
+#undef AXB_SET
+  done_dev = dev;
+  return AXB_OK;
+}
+
+int step_launch(const StepArgs& a, cudaStream_t s) {
+  AXB_CHECK_ARG(a.B >= 1 && a.B <= kStepMaxM, "step: batch %d out of range", a.B);
+  if (int rc = step_prepare()) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms());
+  cfg.blockDim = dim3(kSThreads);
+  cfg.dynamicSmemBytes = kSSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the phases wait on one another
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaErrorInvalidValue;
+  const int GB = a.group / 64;
+#define AXB_LAUNCH(SYM, GBv, HD) \
+  if (a.sym == (SYM ? 1 : 0) && GB == GBv && a.hd == HD) e = cudaLaunchKernelEx(&cfg, step_kernel<SYM, GBv, HD>, a); else
+  AXB_STEP_KERNELS(AXB_LAUNCH) { set_error("step: unsupported format"); return AXB_EINVAL; }
+#undef AXB_LAUNCH
+  return cuda_status(e, "step kernel launch");
+}
+
+}  // namespace axb

@@ -1,0 +1,73 @@
+// Arguments of the persistent decode-step kernel (step.cu), filled by the
+// runner (runner.cu).
+#pragma once
+
+#include "axb_common.cuh"
+
+namespace axb {
+
+// Per-layer weights and cache, one entry per layer in device memory.
+struct StepLayer {
+  const char* w[4];  // q4t words: QKV, o, gate_up (interleaved by 8), down
+  const char* s[4];  // matching scales
+  const __half* qkv_b;
+  const float* ln1;
+  const float* ln2;
+  uint8_t* kc;
+  uint8_t* vc;
+  __half* ks;
+  __half* vs;
+};
+
+struct StepArgs {
+  const StepLayer* layers;
+  int L;
+  int d, Hq, Hkv, hd, F, V, S, kv_type, kv_group, group;
+  int sym;  // 1: AXB_W_Q4T_SYM, 0: AXB_W_Q4T_AFFINE (all projections and the lm_head)
+  float eps;
+  int B;  // sequences this step (one token each), <= 8
+  const uint32_t* emb_w;
+  const __half* emb_s;
+  const char* lm_w;
+  const char* lm_s;
+  const float* ln_f;
+  const float* rope;
+  int rope_len;
+  const int32_t* tokens;
+  const int32_t* params;  // rope_pos, write_pos, active_len, prefix_len
+  int* err;
+  // activations
+  __half* h;       // (B, d) residual stream
+  __half* qkv;     // (B, (Hq + 2 Hkv) hd)
+  __half* attn;    // (B, Hq hd)
+  __half* sw;      // (B, F)
+  __half* logits;  // (B, V)
+  int32_t* amax;   // (B,)
+  // scratch (zeroed once; every counter returns to zero by the end of a step)
+  int* done;          // per-phase completion counters
+  int* tile_cnt;      // per-tile arrival counters
+  float* partials;    // per warp: 2 x 32 lanes x 4 floats
+  float* part_o;      // attention split partials (B, Hq, kStepMaxSplits, hd)
+  float* part_ml;     // (B, Hq, kStepMaxSplits, 2)
+  int* attn_cnt;      // (B, Hkv)
+  unsigned long long* keys;  // per-token argmax keys
+  int* exit_cnt;
+  int max_tiles;      // size of tile_cnt
+  int attn_cap;       // tokens per attention sub-chunk
+  int l2_ahead;       // weight stages prefetched into L2 ahead of the shared-memory ring (per warp)
+};
+
+constexpr int kStepMaxSplits = 64;
+constexpr int kStepMaxM = 8;
+
+// host side
+int step_prepare();
+// Tokens per attention sub-chunk for this cache format, or 0 when the
+// attention working set does not fit the kernel's shared memory.
+int step_attn_cap(int kv_type, int hd, int kv_group);
+bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n_head, int n_kv_head, int d_model,
+                    int kv_type, int kv_group);
+int step_num_warps();  // warps per CTA of the step kernel (partials are sized per warp)
+int step_launch(const StepArgs& a, cudaStream_t s);
+
+}  // namespace axb

@@ -100,6 +100,7 @@ class QuantizedDecoder:
         self.logits_buf = view(1, torch.float16, (rows, cfg["vocab"]))
         self.argmax_buf = view(2, torch.int32, (rows,))
         self.norm_buf = view(3, torch.float32, (rows, d))
+        self.error_buf = view(4, torch.int32, (1,))
         self._last_T = 1
 
     # ------------------------------------------------------------ builders
@@ -242,6 +243,17 @@ class QuantizedDecoder:
         """Final-norm hidden states (fp32) of the last tree/prefill step."""
         T = T or self._last_T
         return self.norm_buf[:T].view(1, T, -1)
+
+    def status(self) -> int:
+        """The runner's error word (synchronizes): 0, or the status of the first
+        problem a step met (AXB_EINVAL: an out-of-vocabulary token id,
+        AXB_ETIMEOUT: a bounded device-side wait ran out)."""
+        return int(self.error_buf.item())
+
+    @property
+    def uses_step_kernel(self) -> bool:
+        """True when decode steps run as one persistent kernel launch."""
+        return bool(L.load().axb_runner_uses_step_kernel(self._h))
 
     def argmax(self, rows: int) -> torch.Tensor:
         return self.argmax_buf[:rows]

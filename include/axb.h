@@ -272,6 +272,10 @@ int axb_runner_buffer(void* handle, int which, size_t* offset_out, size_t* bytes
  * Otherwise tree/chunk mode: masks[t] / depths[t] host arrays of length T. */
 int axb_runner_step(void* handle, int B, int T, int rope_pos, int write_pos, int active_len, int prefix_len,
                     const uint64_t* masks_host, const int32_t* depths_host, int use_graph, void* stream);
+/* 1 when decode steps (T == 1, B <= 8) of this runner run as one persistent
+ * kernel launch, 0 when they run as the per-kernel CUDA graph (unsupported
+ * format, or AXB_STEP=0 in the environment at creation). */
+int axb_runner_uses_step_kernel(void* handle);
 
 #ifdef __cplusplus
 }
