@@ -189,7 +189,8 @@ struct Layout {
   size_t am_v, am_i, am_cnt;
   size_t gemm_ws_bytes, attn_ws_bytes;
   // persistent step kernel (decode, B <= 8)
-  size_t st_layers, st_done, st_tiles, st_part, st_po, st_pml, st_acnt, st_keys, st_exit;
+  size_t st_layers, st_done, st_tiles, st_part, st_po, st_pml, st_acnt, st_keys, st_exit, st_trace;
+  size_t st_trace_bytes;
   int st_max_tiles;
 };
 
@@ -244,6 +245,8 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.st_acnt = take((size_t)sb * c.n_kv_head * 4);
   L.st_keys = take((size_t)kStepMaxM * 8);
   L.st_exit = take(16);
+  L.st_trace_bytes = (size_t)num_sms() * step_trace_slots(c.n_layer) * 8;
+  L.st_trace = take(L.st_trace_bytes);
   L.total = off;
   return L;
 }
@@ -439,6 +442,14 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   AXB_CHECK_ARG(c.ffn % 8 == 0, "runner_create: ffn must be a multiple of 8");
   Layout L = make_layout(c);
   AXB_CHECK_ARG(ws_bytes >= L.total, "runner_create: workspace %zu < %zu bytes", ws_bytes, L.total);
+  AXB_CHECK_ARG(p->emb_w && p->emb_s && p->lm_w && p->lm_s && p->ln_f && p->rope, "runner_create: null model pointer");
+  for (int l = 0; l < c.n_layer; ++l) {
+    AXB_CHECK_ARG(p->qkv_w[l] && p->qkv_s[l] && p->o_w[l] && p->o_s[l] && p->gu_w[l] && p->gu_s[l] && p->dn_w[l] &&
+                      p->dn_s[l] && p->ln1[l] && p->ln2[l] && p->k_cache[l] && p->v_cache[l],
+                  "runner_create: null pointer for layer %d", l);
+    AXB_CHECK_ARG(c.kv_type == AXB_KV_F16 || (p->k_scale && p->v_scale && p->k_scale[l] && p->v_scale[l]),
+                  "runner_create: quantized KV cache needs scales (layer %d)", l);
+  }
   if (int rc = qgemm_prepare()) return rc;
   if (int rc = attn_prepare()) return rc;
   Runner* r = new Runner();
@@ -555,7 +566,9 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
     a.max_tiles = L.st_max_tiles;
     a.attn_cap = cap_tok;
     const char* l2 = getenv("AXB_STEP_L2");
-    a.l2_ahead = l2 ? atoi(l2) : 8;
+    a.l2_ahead = l2 ? atoi(l2) : 2;
+    const char* tr = getenv("AXB_STEP_TRACE");  // phase timeline into runner buffer 5
+    a.trace = (tr && atoi(tr) != 0) ? r->buf<unsigned long long>(L.st_trace) : nullptr;
   }
   *out = r;
   return AXB_OK;
@@ -580,6 +593,7 @@ int axb_runner_buffer(void* h, int which, size_t* off, size_t* bytes) {
     case 2: *off = r->L.amax; *bytes = rows * 4; break;
     case 3: *off = r->L.xnorm; *bytes = rows * r->c.d_model * 4; break;
     case 4: *off = r->L.params + 16; *bytes = 4; break;
+    case 5: *off = r->L.st_trace; *bytes = r->L.st_trace_bytes; break;
     default: axb::set_error("runner_buffer: unknown buffer %d", which); return AXB_EINVAL;
   }
   return AXB_OK;

@@ -33,10 +33,33 @@
 
 namespace axb {
 
+#ifndef AXB_STEP_CH
+#define AXB_STEP_CH 8
+#endif
+#ifndef AXB_STEP_STAGES
+#define AXB_STEP_STAGES 3
+#endif
+#ifndef AXB_STEP_CHAINS
+#define AXB_STEP_CHAINS 2
+#endif
+// 1: the GEMV / attention / norm bodies are separate functions (smaller code, own register budgets)
+#ifndef AXB_STEP_OUTLINE
+#define AXB_STEP_OUTLINE 0
+#endif
+// 1: a stage is copied to registers and its ring slot re-armed before the math
+#ifndef AXB_STEP_REGSTAGE
+#define AXB_STEP_REGSTAGE 0
+#endif
+#if AXB_STEP_OUTLINE
+#define AXB_STEP_FN __noinline__
+#else
+#define AXB_STEP_FN __forceinline__
+#endif
 constexpr int kSW = 8;  // warps per CTA
 constexpr int kSThreads = kSW * 32;
-constexpr int kSCH = 4;      // k-blocks (512 B of weights each) per ring stage
-constexpr int kSStages = 7;  // ring stages per warp
+constexpr int kSCH = AXB_STEP_CH;          // k-blocks (512 B of weights each) per ring stage
+constexpr int kSStages = AXB_STEP_STAGES;  // ring stages per warp
+constexpr int kSChains = AXB_STEP_CHAINS;  // independent MMA accumulator chains per warp
 constexpr int kSStageW = kSCH * 512;
 constexpr int kSStageS = kSCH * 64;  // scale bytes per stage (max: affine, one group per k-block)
 constexpr int kSRing = (kSStages * (kSStageW + kSStageS) + kSStages * 8 + 127) / 128 * 128;
@@ -58,6 +81,18 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Hand-offs between CTAs: the writers of a block of results meet at a warp /
+// group / CTA barrier, then one thread publishes with a release (or acq_rel)
+// atomic; the reader polls with an acquire load and meets its peers at a
+// barrier before they read.  No full fences.
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int atom_acq_rel_add(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -73,6 +108,14 @@ __device__ __forceinline__ bool group_bar_or(int id, bool p) {
   return r != 0;
 }
 __device__ __forceinline__ int tiles_of(int n) { return (n + 15) >> 4; }
+
+// phase timeline stamp (thread 0 of each CTA), only when a trace buffer is set
+__device__ __forceinline__ void trace_mark(const StepArgs& a, int slot) {
+  if (a.trace == nullptr || threadIdx.x != 0) return;
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  a.trace[(size_t)blockIdx.x * step_trace_slots(a.L) + slot] = t;
+}
 
 // Bounded wait for *ctr >= target.  Gives up early when another CTA has already
 // raised the abort flag; on running out it raises the flag and records
@@ -97,10 +140,7 @@ __device__ void raise_abort(const StepArgs& a) {
 // CTA-wide wait: thread 0 polls, the barrier publishes the outcome.
 __device__ bool cta_wait(const int* ctr, int target, const StepArgs& a, bool ok) {
   int good = 0;
-  if (threadIdx.x == 0 && ok) {
-    good = wait_ge(ctr, target, a) ? 1 : 0;
-    __threadfence();
-  }
+  if (threadIdx.x == 0 && ok) good = wait_ge(ctr, target, a) ? 1 : 0;
   return __syncthreads_or(good) != 0;
 }
 
@@ -215,13 +255,28 @@ __device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, Cur& pf, const Step
   bulk_g2s(r.buf + kSStages * kSStageW + st * kSStageS, pc.S + (size_t)(pc.kb / GB) * UB, bs, r.bars + st);
   pc.kb += n;
   ++r.pi;
-  // keep the L2 prefetch cursor l2_ahead stages beyond the ring's leading edge
-  if (a.l2_ahead > 0 && cur_fix<GB>(pf, a, gw, Wt)) {
-    const int n2 = min(kSCH, pf.kb_end - pf.kb);
-    prefetch_l2(pf.W + (size_t)pf.kb * 512, n2 * 512);
-    prefetch_l2(pf.S + (size_t)(pf.kb / GB) * UB, (n2 / GB) * UB);
-    pf.kb += n2;
+  (void)pf;
+}
+
+// L2 prefetch of this warp's whole slice (words and scales) of GEMV phase ph,
+// in bulk requests of at most 64 KB (lane 0).  Issued a few phases ahead, it
+// keeps HBM streaming through the latency-bound stretches of a layer (waits,
+// attention, split-tile reductions) that the shared-memory ring alone cannot
+// cover.
+template <bool SYM, int GB>
+__device__ void prefetch_phase(const StepArgs& a, int ph, int gw, int Wt, int lane) {
+  if (lane != 0 || ph > 4 * a.L) return;
+  constexpr int UB = SYM ? 32 : 64;
+  const GPh g = gph(a, ph);
+  const long long We = eff_warps(g.U, Wt);
+  if (gw >= We) return;
+  const long long u0 = (long long)gw * g.U / We, u1 = (long long)(gw + 1) * g.U / We;
+  const size_t ub = (size_t)GB * 512, end = (size_t)u1 * ub;
+  for (size_t o = (size_t)u0 * ub; o < end; o += 65536) {
+    const size_t len = end - o < 65536 ? end - o : 65536;
+    prefetch_l2(g.W + o, (uint32_t)len);
   }
+  prefetch_l2(g.S + u0 * UB, (uint32_t)((u1 - u0) * UB));
 }
 
 __device__ __forceinline__ int warp_of_unit(long long u, long long U, long long Wt) {
@@ -306,9 +361,10 @@ __device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const StepLayer*
 // One GEMV phase for this warp.  x is staged in shared memory (XS: normalized
 // rows + per-group sums) or read from global memory (L2) one k-block ahead.
 template <bool SYM, int GB, bool XS>
-__device__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf, const __half* xs, int xs_stride,
+__device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf, const __half* xs, int xs_stride,
                            const float* xsum, int xsum_ld, const __half* xg, int ldx, int gw, int Wt, int lane,
                            bool ok, int* done_ctr) {
+  if (a.l2_ahead > 0) prefetch_phase<SYM, GB>(a, ph + a.l2_ahead, gw, Wt, lane);
   const GPh g = gph(a, ph);
   const long long We = eff_warps(g.U, Wt);
   if (gw >= We || !ok) return ok;
@@ -321,16 +377,20 @@ __device__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf,
   const uint4* xrow = reinterpret_cast<const uint4*>((XS ? xs + (size_t)nn * xs_stride : xg + (size_t)nn * ldx) +
                                                      16 * t4);
   int finished = 0;
-  constexpr int CH = 2;
+  constexpr int CH = kSChains;
   for (int t = t_first; t <= t_last && ok; ++t) {
     const int kb_lo = (int)max(u0, (long long)t * g.upt) * GB;
     const int kb_hi = (int)min(u1, (long long)(t + 1) * g.upt) * GB;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    float tmp[CH][4];
+    // accumulators per MMA chain, in two sets used by alternate groups: the
+    // scale fold of one group overlaps the MMAs of the next
+    float tmp2[2][CH][4];
 #pragma unroll
-    for (int c2 = 0; c2 < CH; ++c2)
+    for (int p2 = 0; p2 < 2; ++p2)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) tmp[c2][q] = 0.f;
+      for (int c2 = 0; c2 < CH; ++c2)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmp2[p2][c2][q] = 0.f;
     uint4 xn0 = make_uint4(0, 0, 0, 0), xn1 = xn0;
     if (!XS) {
       xn0 = __ldcg(xrow + (kb_lo - t * KB) * 8);
@@ -348,8 +408,33 @@ __device__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf,
       const uint4* wst = reinterpret_cast<const uint4*>(r.buf + st * kSStageW) + lane;
       const char* sst = r.buf + kSStages * kSStageW + st * kSStageS;
       const int kbt = kb0 - t * KB;
+      // copy the stage (this lane's words, the scales of its rows) into
+      // registers and hand the slot back at once: the next copy is in flight
+      // while this stage is computed
+      uint4 wreg[AXB_STEP_REGSTAGE ? kSCH : 1];
+      uint2 sreg[AXB_STEP_REGSTAGE ? kSCH : 1];  // SYM: .x = (s[g], s[g+8]); AFFINE: (s, b) pairs
+      if (AXB_STEP_REGSTAGE) {
+#pragma unroll
+        for (int j = 0; j < (AXB_STEP_REGSTAGE ? kSCH : 1); ++j) {
+          if (j < n) wreg[j] = wst[j * 32];
+          if (j < n / GB) {
+            if (SYM) sreg[j].x = reinterpret_cast<const uint32_t*>(sst)[j * 8 + gq];
+            else sreg[j] = reinterpret_cast<const uint2*>(sst)[j * 8 + gq];
+          }
+        }
+        __syncwarp();
+        ring_issue<SYM, GB>(r, pc, pf, a, gw, Wt, lane);
+        ++r.ci;
+      }
+      auto wword = [&](const int j) -> uint4 { return AXB_STEP_REGSTAGE ? wreg[AXB_STEP_REGSTAGE ? j : 0] : wst[j * 32]; };
+      auto sword = [&](const int gi) -> uint2 {
+        if (AXB_STEP_REGSTAGE) return sreg[AXB_STEP_REGSTAGE ? gi : 0];
+        return SYM ? make_uint2(reinterpret_cast<const uint32_t*>(sst)[gi * 8 + gq], 0u)
+                   : reinterpret_cast<const uint2*>(sst)[gi * 8 + gq];
+      };
       auto kblock = [&](const int j) {
-        const uint4 cur = wst[j * 32];
+        float(&tmp)[CH][4] = tmp2[SYM ? ((j / GB) & 1) : 0];
+        const uint4 cur = wword(j);
         uint32_t bf[8];
         if (XS) {
           const uint4 v0 = xrow[(kbt + j) * 8], v1 = xrow[(kbt + j) * 8 + 1];
@@ -372,15 +457,19 @@ __device__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf,
             mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
           }
           if (GB == 1 || (j & 1)) {  // group complete: remove the offsets, apply the scales
-            const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[(j / GB) * 8 + gq];
+            const uint32_t sp = sword(j / GB).x;
             const float2 sc = __half22float2(u32_as_h2(sp));
             const int grp = (kbt + j) / GB;
             const float2 xg2 = *reinterpret_cast<const float2*>(xsum + grp * xsum_ld + 2 * t4);
             float s4[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              s4[q] = tmp[0][q] + tmp[1][q];
-              tmp[0][q] = tmp[1][q] = 0.f;
+              float v = tmp[0][q];
+#pragma unroll
+              for (int c2 = 1; c2 < CH; ++c2) v += tmp[c2][q];
+              s4[q] = v;
+#pragma unroll
+              for (int c2 = 0; c2 < CH; ++c2) tmp[c2][q] = 0.f;
             }
             acc[0] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.x, s4[0]), acc[0]);
             acc[1] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.y, s4[1]), acc[1]);
@@ -395,13 +484,17 @@ __device__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf,
             mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
           }
           if (GB == 1 || (j & 1)) {
-            const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[(j / GB) * 8 + gq];
+            const uint32_t sp = sword(j / GB).x;
             const float2 sc = __half22float2(u32_as_h2(sp));
             float s4[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              s4[q] = tmp[0][q] + tmp[1][q];
-              tmp[0][q] = tmp[1][q] = 0.f;
+              float v = tmp[0][q];
+#pragma unroll
+              for (int c2 = 1; c2 < CH; ++c2) v += tmp[c2][q];
+              s4[q] = v;
+#pragma unroll
+              for (int c2 = 0; c2 < CH; ++c2) tmp[c2][q] = 0.f;
             }
             acc[0] = __fmaf_rn(sc.x, s4[0], acc[0]);
             acc[1] = __fmaf_rn(sc.x, s4[1], acc[1]);
@@ -409,7 +502,7 @@ __device__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf,
             acc[3] = __fmaf_rn(sc.y, s4[3], acc[3]);
           }
         } else {
-          const uint2 sb = reinterpret_cast<const uint2*>(sst)[(j / GB) * 8 + gq];
+          const uint2 sb = sword(j / GB);
           const __half2 s01 = u32_as_h2(sb.x), s23 = u32_as_h2(sb.y);
           const __half2 sg = __half2half2(__low2half(s01)), bg = __half2half2(__high2half(s01));
           const __half2 sg8 = __half2half2(__low2half(s23)), bg8 = __half2half2(__high2half(s23));
@@ -433,15 +526,22 @@ __device__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf,
         for (int j = 0; j < kSCH; ++j)
           if (j < n) kblock(j);
       }
-      __syncwarp();
-      ring_issue<SYM, GB>(r, pc, pf, a, gw, Wt, lane);
-      ++r.ci;
+      if (!AXB_STEP_REGSTAGE) {
+        __syncwarp();
+        ring_issue<SYM, GB>(r, pc, pf, a, gw, Wt, lane);
+        ++r.ci;
+      }
       kb0 += n;
     }
     if (!ok) break;
     if (!SYM) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[q] = tmp[0][q] + tmp[1][q];
+      for (int q = 0; q < 4; ++q) {
+        float v = tmp2[0][0][q];
+#pragma unroll
+        for (int c2 = 1; c2 < CH; ++c2) v += tmp2[0][c2][q];
+        acc[q] = v;
+      }
     }
     const bool complete = (long long)t * g.upt >= u0 && (long long)(t + 1) * g.upt <= u1;
     if (complete) {
@@ -453,15 +553,14 @@ __device__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf,
     const int slot = (t == t_first) ? 0 : 1;
     float* p = a.partials + ((size_t)(gw * 2 + slot) * 32 + lane) * 4;
     *reinterpret_cast<float4*>(p) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    __threadfence();
     __syncwarp();
     int old = 0;
-    if (lane == 0) old = atomicAdd(a.tile_cnt + t, 1);
+    if (lane == 0) old = atom_acq_rel_add(a.tile_cnt + t, 1);
     old = __shfl_sync(0xffffffffu, old, 0);
     const int wf = warp_of_unit((long long)t * g.upt, g.U, We);
     const int wl = warp_of_unit((long long)(t + 1) * g.upt - 1, g.U, We);
     if (old != wl - wf) continue;
-    __threadfence();
+    __syncwarp();  // the other lanes' loads follow lane 0's acquire
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
     for (int w0 = wf; w0 <= wl; w0 += 4) {
       float4 v[4];
@@ -487,9 +586,8 @@ __device__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf,
     ++finished;
   }
   if (finished) {
-    __threadfence();
     __syncwarp();
-    if (lane == 0) atomicAdd(done_ctr, finished);
+    if (lane == 0) red_release_add(done_ctr, finished);
   }
   return ok;
 }
@@ -522,7 +620,7 @@ __device__ void stage_embed(const StepArgs& a, __half* xs, int stride) {
 // RMSNorm (modules.py:30-43: rms = 1/sqrt(mean(x^2) + eps), fp16((x * rms) * w))
 // of M rows of h (or of the raw rows already in xs when src is null) into xs,
 // then (SYM) the fp32 per-group sums of the normalized rows.
-__device__ void stage_norm(const StepArgs& a, const __half* src, const float* w, __half* xs, int stride, float* xsum,
+__device__ AXB_STEP_FN void stage_norm(const StepArgs& a, const __half* src, const float* w, __half* xs, int stride, float* xsum,
                            int xsum_ld, bool sums, float* red) {
   const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, wid = tid >> 5;
   const int K = a.d, K8 = K / 8;
@@ -654,7 +752,7 @@ __device__ __forceinline__ AttnItem attn_item_of(int item, int nsplit, int chunk
 // One attention item (sequence b, kv head, split) on a group of 4 warps.
 // gt = thread index in the group, gwarp = warp index in the group.
 template <int HD>
-__device__ bool attn_item(const StepArgs& a, const StepLayer* ly, const AttnItem& it, int nsplit, bool prefetched,
+__device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, const AttnItem& it, int nsplit, bool prefetched,
                           char* gsm, uint64_t* bar, uint32_t& uses, int bar_id, int gt, int* done_ctr, bool ok) {
   constexpr int DPL = HD / 32, EPT = HD / 16;
   const int lane = gt & 31, gwarp = gt >> 5;
@@ -840,22 +938,19 @@ __device__ bool attn_item(const StepArgs& a, const StepLayer* ly, const AttnItem
   }
   int* flag = reinterpret_cast<int*>(ml_s + 24);
   if (nsplit == 1) {
-    __threadfence();
     group_bar(bar_id);
-    if (gt == 0) atomicAdd(done_ctr, 1);
+    if (gt == 0) red_release_add(done_ctr, 1);
     return true;
   }
   if (gt < n_rep) {
     a.part_ml[((pidx + gt) * kStepMaxSplits + it.split) * 2 + 0] = ml_s[gt];
     a.part_ml[((pidx + gt) * kStepMaxSplits + it.split) * 2 + 1] = ml_s[8 + gt];
   }
-  __threadfence();
   group_bar(bar_id);
   int* cnt = a.attn_cnt + it.b * a.Hkv + it.kvh;
-  if (gt == 0) *flag = (atomicAdd(cnt, 1) == nsplit - 1) ? 1 : 0;
+  if (gt == 0) *flag = (atom_acq_rel_add(cnt, 1) == nsplit - 1) ? 1 : 0;
   group_bar(bar_id);
   if (!*flag) return true;
-  __threadfence();
   // ---- combine the splits in split order: per-head weights first
   for (int r = gwarp; r < n_rep; r += 4) {
     const size_t hb = (pidx + r) * kStepMaxSplits;
@@ -887,11 +982,10 @@ __device__ bool attn_item(const StepArgs& a, const StepLayer* ly, const AttnItem
     }
     a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, ml_s[8 + r]));
   }
-  __threadfence();
   group_bar(bar_id);
   if (gt == 0) {
     atomicExch(cnt, 0);
-    atomicAdd(done_ctr, 1);
+    red_release_add(done_ctr, 1);
   }
   return true;
 }
@@ -926,16 +1020,9 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     pc.ph = 0;
     cur_load<GB>(pc, a, gw, Wt);
     pf = pc;
-    // the L2 prefetch cursor starts at the end of the first ring fill
-    for (int s = 0; s < kSStages && cur_fix<GB>(pf, a, gw, Wt); ++s) pf.kb += min(kSCH, pf.kb_end - pf.kb);
-    constexpr int UB = SYM ? 32 : 64;
-    for (int s = 0; s < a.l2_ahead && cur_fix<GB>(pf, a, gw, Wt); ++s) {
-      const int n2 = min(kSCH, pf.kb_end - pf.kb);
-      prefetch_l2(pf.W + (size_t)pf.kb * 512, n2 * 512);
-      prefetch_l2(pf.S + (size_t)(pf.kb / GB) * UB, (n2 / GB) * UB);
-      pf.kb += n2;
-    }
     for (int s = 0; s < kSStages; ++s) ring_issue<SYM, GB>(ring, pc, pf, a, gw, Wt, lane);
+    // phases 0 .. l2_ahead - 1 now; each later one when its predecessor l2_ahead back starts
+    for (int p = 0; p < a.l2_ahead; ++p) prefetch_phase<SYM, GB>(a, p, gw, Wt, lane);
   }
   __syncthreads();
 
@@ -945,21 +1032,24 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   const int grp = wid >> 2, gt = tid & 127;
   uint32_t abar_uses = 0;
 
+  trace_mark(a, 0);
   // embedding rows for the first layer's QKV (every CTA stages its own copy)
   stage_embed(a, xs, xs_stride);
-  __threadfence();
   __syncthreads();
-  if (blockIdx.x == 0 && tid == 0) atomicAdd(a.done, 1);
+  if (blockIdx.x == 0 && tid == 0) red_release_add(a.done, 1);
 
   for (int l = 0; l < a.L; ++l) {
     const StepLayer* ly = a.layers + l;
     int* dn = a.done + 1 + 5 * l;  // QKV, attention, o, gate_up, down
     // ---- QKV (RMSNorm fused)
+    const int ts = 1 + 10 * l;
     if (l > 0) ok = cta_wait(dn - 1, t_d, a, ok);
+    trace_mark(a, ts + 0);
     if (ok) stage_norm(a, l > 0 ? a.h : nullptr, ly->ln1, xs, xs_stride, xsum, xsum_ld, SYM, red);
     ok = gemv_phase<SYM, GB, true>(a, 4 * l + 0, ring, pc, pf, xs, xs_stride, xsum, xsum_ld, nullptr, 0, gw, Wt,
                                    lane, ok, dn + 0);
     ok = __syncthreads_and(ok) != 0;  // the staged rows are dead: the union holds attention next
+    trace_mark(a, ts + 1);
     // ---- attention (RoPE + KV write fused)
     {
       const int active = a.params[2];
@@ -976,6 +1066,7 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
       }
       const bool pre_ok = ok;
       ok = cta_wait(dn + 0, tiles_of(qkv_dim), a, ok);
+      trace_mark(a, ts + 2);
       bool first = true;
       for (; item < n_items; item += kSGroups * C) {
         if (!ok) {
@@ -988,35 +1079,44 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
         first = false;
       }
     }
+    trace_mark(a, ts + 3);
     // ---- o projection (+ residual)
     ok = cta_wait(dn + 1, a.B * a.Hkv, a, ok);
     if (l == 0) ok = cta_wait(a.done, 1, a, ok);  // h holds the embedding rows
+    trace_mark(a, ts + 4);
     ok = gemv_phase<SYM, GB, false>(a, 4 * l + 1, ring, pc, pf, nullptr, 0, nullptr, 0, a.attn, a.Hq * a.hd, gw,
                                     Wt, lane, ok, dn + 2);
+    trace_mark(a, ts + 5);
     // ---- gate_up (RMSNorm fused, SwiGLU epilogue)
     ok = cta_wait(dn + 2, t_d, a, ok);
+    trace_mark(a, ts + 6);
     if (ok) stage_norm(a, a.h, ly->ln2, xs, xs_stride, xsum, xsum_ld, SYM, red);
     ok = gemv_phase<SYM, GB, true>(a, 4 * l + 2, ring, pc, pf, xs, xs_stride, xsum, xsum_ld, nullptr, 0, gw, Wt,
                                    lane, ok, dn + 3);
+    trace_mark(a, ts + 7);
     // ---- down projection (+ residual)
     ok = cta_wait(dn + 3, tiles_of(2 * a.F), a, ok);
+    trace_mark(a, ts + 8);
     ok = gemv_phase<SYM, GB, false>(a, 4 * l + 3, ring, pc, pf, nullptr, 0, nullptr, 0, a.sw, a.F, gw, Wt, lane,
                                     ok, dn + 4);
+    trace_mark(a, ts + 9);
   }
   // ---- lm_head (final RMSNorm fused) + argmax keys
-  ok = cta_wait(a.done + 5 * a.L, t_d, a, ok);
+  // (with no layers the lm_head reads the embedding rows: wait for CTA 0's copy in h)
+  ok = a.L > 0 ? cta_wait(a.done + 5 * a.L, t_d, a, ok) : cta_wait(a.done, 1, a, ok);
+  trace_mark(a, 1 + 10 * a.L);
   if (ok) stage_norm(a, a.h, a.ln_f, xs, xs_stride, xsum, xsum_ld, SYM, red);
   ok = gemv_phase<SYM, GB, true>(a, 4 * a.L, ring, pc, pf, xs, xs_stride, xsum, xsum_ld, nullptr, 0, gw, Wt, lane,
                                  ok, a.done + 1 + 5 * a.L);
+  trace_mark(a, 2 + 10 * a.L);
 
   // ---- wind down: copies still in flight (only after an abort) get a bounded wait
   for (int i = ring.ci; i < ring.pi; ++i) mbar_wait(ring.bars + (i % kSStages), (uint32_t)((i / kSStages) & 1), kSMbarLimit);
-  __threadfence();
   __syncthreads();
-  if (tid == 0) *s_last = (atomicAdd(a.exit_cnt, 1) == C - 1) ? 1 : 0;
+  trace_mark(a, 3 + 10 * a.L);
+  if (tid == 0) *s_last = (atom_acq_rel_add(a.exit_cnt, 1) == C - 1) ? 1 : 0;
   __syncthreads();
   if (!*s_last) return;
-  __threadfence();
   // last CTA: publish the argmax, return every counter to zero
   if (tid < a.B) {
     const unsigned long long k = __ldcg(a.keys + tid);
@@ -1082,6 +1182,22 @@ int step_prepare() {
 
 int step_launch(const StepArgs& a, cudaStream_t s) {
   AXB_CHECK_ARG(a.B >= 1 && a.B <= kStepMaxM, "step: batch %d out of range", a.B);
+  // the shapes the kernel's fixed shared-memory layout is sized for
+  AXB_CHECK_ARG(a.group == 64 || a.group == 128, "step: group %d", a.group);
+  AXB_CHECK_ARG(a.d > 0 && a.d % 128 == 0 && a.F % 64 == 0 && a.V > 0, "step: bad dims (%d, %d, %d)", a.d, a.F, a.V);
+  AXB_CHECK_ARG((a.hd == 64 || a.hd == 128) && a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kMaxRepS,
+                "step: bad heads (%d, %d, %d)", a.Hq, a.Hkv, a.hd);
+  AXB_CHECK_ARG(((size_t)kStepMaxM * (a.d + 8) * 2 + 127) / 128 * 128 + (size_t)(a.d / 64) * 16 * 4 <=
+                    (size_t)kSUnion,
+                "step: d_model %d too large for the staged activations", a.d);
+  AXB_CHECK_ARG(a.attn_cap >= 16 && attn_layout(a.kv_type, a.hd, a.kv_group, a.attn_cap).bytes <= kSUnion / kSGroups,
+                "step: attention chunk %d does not fit", a.attn_cap);
+  AXB_CHECK_ARG(a.lm_w && a.lm_s && a.ln_f && a.emb_w && a.emb_s && a.rope && a.tokens && a.params && a.err && a.h &&
+                    a.logits && a.amax && a.done && a.tile_cnt && a.partials && a.keys && a.exit_cnt &&
+                    (a.L == 0 || (a.layers && a.qkv && a.attn && a.sw && a.part_o && a.part_ml && a.attn_cnt)),
+                "step: null pointer in the step arguments");
+  AXB_CHECK_ARG((reinterpret_cast<uintptr_t>(a.lm_w) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.lm_s) & 15) == 0,
+                "step: lm_head words and scales must be 16-byte aligned");
   if (int rc = step_prepare()) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_sms());

@@ -54,8 +54,12 @@ struct StepArgs {
   int* exit_cnt;
   int max_tiles;      // size of tile_cnt
   int attn_cap;       // tokens per attention sub-chunk
-  int l2_ahead;       // weight stages prefetched into L2 ahead of the shared-memory ring (per warp)
+  int l2_ahead;       // GEMV phases ahead whose weights are prefetched into L2 (0: none)
+  unsigned long long* trace;  // optional phase timeline: [CTA][step_trace_slots(L)] globaltimer stamps
 };
+
+// Phase timeline slots per CTA: start, 10 per layer, then lm_head wait, lm_head done, exit.
+__host__ __device__ inline int step_trace_slots(int L) { return 4 + 10 * L; }
 
 constexpr int kStepMaxSplits = 64;
 constexpr int kStepMaxM = 8;

@@ -265,7 +265,10 @@ int axb_runner_destroy(void* handle);
 /* Offsets (bytes, into the workspace) of the runner's I/O buffers:
  * which = 0 tokens int32 (max_batch*max_tokens), 1 logits fp16 (rows, vocab),
  * 2 argmax int32 (rows), 3 final-norm hidden fp32 (rows, d), 4 error word int32
- * (non-zero after a step that met an out-of-vocabulary token id) */
+ * (non-zero after a step that met an out-of-vocabulary token id or a bounded
+ * device wait that ran out), 5 step-kernel phase timeline uint64 (SMs,
+ * 4 + 10 * n_layer) globaltimer stamps, written when AXB_STEP_TRACE=1 was set
+ * at creation */
 int axb_runner_buffer(void* handle, int which, size_t* offset_out, size_t* bytes_out);
 /* One forward step over B sequences x T new tokens already placed in the
  * token buffer.  T == 1 and masks == NULL: decode (all active slots visible).
