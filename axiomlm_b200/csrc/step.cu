@@ -70,6 +70,20 @@ constexpr int kSGroups = 2;  // attention groups (4 warps each) per CTA
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kSMbarLimit = 1u << 22;
 constexpr int kMaxRepS = 8;  // q heads per kv head
+constexpr int kXsumLd = 16;  // tokens per group row of the staged-x sums
+// the staged-x sums of a K-wide activation sit at the end of the union, the rows from its start
+__host__ __device__ constexpr int xsum_bytes(int K, int G) { return ((K / G) * kXsumLd * 4 + 127) / 128 * 128; }
+__host__ __device__ constexpr bool xs_fits(int M, int K, int G) {
+  return (long long)M * (K + 8) * 2 <= (long long)(kSUnion - xsum_bytes(K, G));
+}
+// D = A * B with a zero accumulator (the first MMA of a chain)
+__device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
 static_assert(kSSmem <= 227 * 1024, "step kernel shared memory");
 static_assert(kSStageW % 16 == 0 && kSStageS % 16 == 0 && kSRing % 128 == 0, "bulk-copy alignment");
 static_assert((kSStages * (kSStageW + kSStageS)) % 8 == 0, "mbarrier alignment");
@@ -235,26 +249,40 @@ __device__ bool cur_fix(Cur& c, const StepArgs& a, int gw, int Wt) {
   return true;
 }
 
+// Per-warp ring of kSStages slots.  Slot indices and mbarrier parities are
+// advanced incrementally (no divisions on the per-stage path).  A slot is
+// re-armed by the same warp after its stage has been computed: the generic
+// loads of the stage have returned by then, so no proxy fence is needed.
 struct Ring {
   char* buf;
   uint64_t* bars;
-  int ci, pi;  // stages consumed / issued
+  int cs, cpar;     // consumer: next slot and the parity its mbarrier completes with
+  int ps;           // producer (lane 0): next slot to fill
+  int inflight;     // producer (lane 0): stages issued and not yet consumed
 };
+
+__device__ __forceinline__ void ring_consumed(Ring& r) {
+  if (++r.cs == kSStages) {
+    r.cs = 0;
+    r.cpar ^= 1;
+  }
+  --r.inflight;
+}
 
 template <bool SYM, int GB>
 __device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, Cur& pf, const StepArgs& a, int gw, int Wt, int lane) {
   if (lane != 0) return;
   constexpr int UB = SYM ? 32 : 64;  // scale bytes per group
-  if (!cur_fix<GB>(pc, a, gw, Wt)) return;
-  const int st = r.pi % kSStages;
+  if (pc.kb >= pc.kb_end && !cur_fix<GB>(pc, a, gw, Wt)) return;
+  const int st = r.ps;
+  r.ps = st + 1 == kSStages ? 0 : st + 1;
   const int n = min(kSCH, pc.kb_end - pc.kb);
   const uint32_t bw = n * 512, bs = (n / GB) * UB;
-  fence_proxy_async();
   mbar_expect_tx(r.bars + st, bw + bs);
   bulk_g2s(r.buf + st * kSStageW, pc.W + (size_t)pc.kb * 512, bw, r.bars + st);
   bulk_g2s(r.buf + kSStages * kSStageW + st * kSStageS, pc.S + (size_t)(pc.kb / GB) * UB, bs, r.bars + st);
   pc.kb += n;
-  ++r.pi;
+  ++r.inflight;
   (void)pf;
 }
 
@@ -362,7 +390,7 @@ __device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const StepLayer*
 // rows + per-group sums) or read from global memory (L2) one k-block ahead.
 template <bool SYM, int GB, bool XS>
 __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf, const __half* xs, int xs_stride,
-                           const float* xsum, int xsum_ld, const __half* xg, int ldx, int gw, int Wt, int lane,
+                           const float* xsum, const __half* xg, int ldx, int gw, int Wt, int lane,
                            bool ok, int* done_ctr) {
   if (a.l2_ahead > 0) prefetch_phase<SYM, GB>(a, ph + a.l2_ahead, gw, Wt, lane);
   const GPh g = gph(a, ph);
@@ -397,8 +425,8 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
       xn1 = __ldcg(xrow + (kb_lo - t * KB) * 8 + 1);
     }
     for (int kb0 = kb_lo; kb0 < kb_hi;) {
-      const int st = r.ci % kSStages;
-      const bool got = mbar_wait(r.bars + st, (uint32_t)((r.ci / kSStages) & 1), kSMbarLimit);
+      const int st = r.cs;
+      const bool got = mbar_wait(r.bars + st, (uint32_t)r.cpar, kSMbarLimit);
       if (!__all_sync(0xffffffffu, got)) {  // one decision for the whole warp
         if (lane == 0) raise_abort(a);
         ok = false;
@@ -423,8 +451,8 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
           }
         }
         __syncwarp();
+        ring_consumed(r);
         ring_issue<SYM, GB>(r, pc, pf, a, gw, Wt, lane);
-        ++r.ci;
       }
       auto wword = [&](const int j) -> uint4 { return AXB_STEP_REGSTAGE ? wreg[AXB_STEP_REGSTAGE ? j : 0] : wst[j * 32]; };
       auto sword = [&](const int gi) -> uint2 {
@@ -454,13 +482,18 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
           for (int jj = 0; jj < 4; ++jj) {
             uint32_t af[4];
             unpack_word_raw(words[jj], af);
-            mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
+            // the first MMA of each chain in a group starts from zero
+            const bool fresh = (j % GB) == 0 && jj < CH;
+            if (fresh)
+              mma_16816_z(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1]);
+            else
+              mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
           }
           if (GB == 1 || (j & 1)) {  // group complete: remove the offsets, apply the scales
             const uint32_t sp = sword(j / GB).x;
             const float2 sc = __half22float2(u32_as_h2(sp));
             const int grp = (kbt + j) / GB;
-            const float2 xg2 = *reinterpret_cast<const float2*>(xsum + grp * xsum_ld + 2 * t4);
+            const float2 xg2 = *reinterpret_cast<const float2*>(xsum + grp * kXsumLd + 2 * t4);
             float s4[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -468,8 +501,6 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
 #pragma unroll
               for (int c2 = 1; c2 < CH; ++c2) v += tmp[c2][q];
               s4[q] = v;
-#pragma unroll
-              for (int c2 = 0; c2 < CH; ++c2) tmp[c2][q] = 0.f;
             }
             acc[0] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.x, s4[0]), acc[0]);
             acc[1] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.y, s4[1]), acc[1]);
@@ -481,7 +512,11 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
           for (int jj = 0; jj < 4; ++jj) {
             uint32_t af[4];
             unpack_word<8>(words[jj], af);
-            mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
+            const bool fresh = (j % GB) == 0 && jj < CH;
+            if (fresh)
+              mma_16816_z(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1]);
+            else
+              mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
           }
           if (GB == 1 || (j & 1)) {
             const uint32_t sp = sword(j / GB).x;
@@ -493,8 +528,6 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
 #pragma unroll
               for (int c2 = 1; c2 < CH; ++c2) v += tmp[c2][q];
               s4[q] = v;
-#pragma unroll
-              for (int c2 = 0; c2 < CH; ++c2) tmp[c2][q] = 0.f;
             }
             acc[0] = __fmaf_rn(sc.x, s4[0], acc[0]);
             acc[1] = __fmaf_rn(sc.x, s4[1], acc[1]);
@@ -528,8 +561,8 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
       }
       if (!AXB_STEP_REGSTAGE) {
         __syncwarp();
+        ring_consumed(r);
         ring_issue<SYM, GB>(r, pc, pf, a, gw, Wt, lane);
-        ++r.ci;
       }
       kb0 += n;
     }
@@ -617,69 +650,81 @@ __device__ void stage_embed(const StepArgs& a, __half* xs, int stride) {
   }
 }
 
-// RMSNorm (modules.py:30-43: rms = 1/sqrt(mean(x^2) + eps), fp16((x * rms) * w))
-// of M rows of h (or of the raw rows already in xs when src is null) into xs,
-// then (SYM) the fp32 per-group sums of the normalized rows.
-__device__ AXB_STEP_FN void stage_norm(const StepArgs& a, const __half* src, const float* w, __half* xs, int stride, float* xsum,
-                           int xsum_ld, bool sums, float* red) {
+// Stage M rows of K activations into shared memory (row stride K + 8 halves):
+// from global memory (src), or the raw rows already in xs (src null).  With
+// an RMSNorm weight w (modules.py:30-43: rms = 1/sqrt(mean(x^2) + eps),
+// fp16((x * rms) * w)) the rows are normalized in place.  With sums (SYM
+// weights) the fp32 per-group sums of the staged rows follow.
+__device__ __noinline__ void stage_x(int B, int G, float eps, const __half* src, int K, const float* w, __half* xs,
+                                     int stride, float* xsum, bool sums, float* red) {
   const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, wid = tid >> 5;
-  const int K = a.d, K8 = K / 8;
-  for (int m = 0; m < a.B; ++m) {
+  const int K8 = K / 8;
+  for (int m = 0; m < B; ++m) {
     float ss = 0.f;
-    for (int c = tid; c < K8; c += nth) {
-      uint4 v;
-      if (src) {
-        v = __ldcg(reinterpret_cast<const uint4*>(src + (size_t)m * K) + c);
-        reinterpret_cast<uint4*>(xs + (size_t)m * stride)[c] = v;
-      } else {
-        v = reinterpret_cast<const uint4*>(xs + (size_t)m * stride)[c];
+    const uint4* srow = src ? reinterpret_cast<const uint4*>(src + (size_t)m * K) : nullptr;
+    uint4* drow = reinterpret_cast<uint4*>(xs + (size_t)m * stride);
+    for (int c0 = tid; c0 < K8; c0 += 4 * nth) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)  // all loads of the round in flight together
+        if (c0 + u * nth < K8) v[u] = srow ? __ldcg(srow + c0 + u * nth) : drow[c0 + u * nth];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (c0 + u * nth >= K8) continue;
+        if (srow) drow[c0 + u * nth] = v[u];
+        if (w) {
+          const __half2* hh = reinterpret_cast<const __half2*>(&v[u]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __half22float2(hh[q]);
+            ss = __fmaf_rn(f.x, f.x, ss);
+            ss = __fmaf_rn(f.y, f.y, ss);
+          }
+        }
       }
+    }
+    if (w) {
+      ss = warp_sum(ss);
+      if (lane == 0) red[wid * kStepMaxM + m] = ss;
+    }
+  }
+  __syncthreads();
+  if (w) {
+    for (int i = tid; i < B * K8; i += nth) {
+      const int m = i / K8, c = i % K8;
+      float tot = 0.f;
+      for (int ww = 0; ww < (nth >> 5); ++ww) tot += red[ww * kStepMaxM + m];
+      const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), eps)));
+      uint4* sp = reinterpret_cast<uint4*>(xs + (size_t)m * stride) + c;
+      const uint4 v = *sp;
       const __half2* hh = reinterpret_cast<const __half2*>(&v);
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c);
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c + 1);
+      const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      uint4 o;
+      __half2* oh = reinterpret_cast<__half2*>(&o);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const float2 f = __half22float2(hh[q]);
-        ss = __fmaf_rn(f.x, f.x, ss);
-        ss = __fmaf_rn(f.y, f.y, ss);
+        oh[q] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, rms), ws[2 * q]),
+                                  __fmul_rn(__fmul_rn(f.y, rms), ws[2 * q + 1]));
       }
+      *sp = o;
     }
-    ss = warp_sum(ss);
-    if (lane == 0) red[wid * kStepMaxM + m] = ss;
+    __syncthreads();
   }
-  __syncthreads();
-  for (int i = tid; i < a.B * K8; i += nth) {
-    const int m = i / K8, c = i % K8;
-    float tot = 0.f;
-    for (int ww = 0; ww < (nth >> 5); ++ww) tot += red[ww * kStepMaxM + m];
-    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
-    uint4* sp = reinterpret_cast<uint4*>(xs + (size_t)m * stride) + c;
-    const uint4 v = *sp;
-    const __half2* hh = reinterpret_cast<const __half2*>(&v);
-    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c);
-    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c + 1);
-    const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-    uint4 o;
-    __half2* oh = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 f = __half22float2(hh[q]);
-      oh[q] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, rms), ws[2 * q]),
-                                __fmul_rn(__fmul_rn(f.y, rms), ws[2 * q + 1]));
-    }
-    *sp = o;
-  }
-  __syncthreads();
   if (sums) {
-    const int G = a.group, ngr = K / G, nw = nth >> 5;
-    for (int item = wid; item < ngr * a.B; item += nw) {
+    const int ngr = K / G, nw = nth >> 5;
+    for (int item = wid; item < ngr * B; item += nw) {
       const int grp = item % ngr, m = item / ngr;
-      const __half* s = xs + (size_t)m * stride + grp * G;
+      const __half* sx = xs + (size_t)m * stride + grp * G;
       float v = 0.f;
       for (int k = lane * 2; k < G; k += 64) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(s + k));
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(sx + k));
         v += f.x + f.y;
       }
       v = warp_sum(v);
-      if (lane == 0) xsum[grp * xsum_ld + m] = v;
+      if (lane == 0) xsum[grp * kXsumLd + m] = v;
     }
     __syncthreads();
   }
@@ -1001,17 +1046,19 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   uint64_t* abar = reinterpret_cast<uint64_t*>(uni + kSUnion + 256);  // one per attention group
   int* s_last = reinterpret_cast<int*>(uni + kSUnion + 256 + 64);
 
-  // staged activations: M rows of K + 8 halves, then per-(group, token) sums
-  const int xs_stride = a.d + 8;
+  // staged activations: M rows of K + 8 halves from the union's start, their
+  // per-(group, token) sums at its end
   __half* xs = reinterpret_cast<__half*>(uni);
-  const int xsum_ld = 16;
-  float* xsum = reinterpret_cast<float*>(uni + ((size_t)kStepMaxM * xs_stride * 2 + 127) / 128 * 128);
+  auto xsum_of = [&](int K) { return reinterpret_cast<float*>(uni + kSUnion - xsum_bytes(K, a.group)); };
+  const int xs_stride = a.d + 8;
 
   Ring ring;
   ring.buf = smem + wid * kSRing;
   ring.bars = reinterpret_cast<uint64_t*>(ring.buf + kSStages * (kSStageW + kSStageS));
-  ring.ci = 0;
-  ring.pi = 0;
+  ring.cs = 0;
+  ring.cpar = 0;
+  ring.ps = 0;
+  ring.inflight = 0;
   Cur pc, pf;
   if (lane == 0) {
     for (int s = 0; s < kSStages; ++s) mbar_init(ring.bars + s, 1);
@@ -1038,19 +1085,66 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   __syncthreads();
   if (blockIdx.x == 0 && tid == 0) red_release_add(a.done, 1);
 
-  for (int l = 0; l < a.L; ++l) {
-    const StepLayer* ly = a.layers + l;
-    int* dn = a.done + 1 + 5 * l;  // QKV, attention, o, gate_up, down
-    // ---- QKV (RMSNorm fused)
+  // GEMV phases in order: p = 4 l + {0 QKV, 1 o, 2 gate_up, 3 down}, 4 L = lm_head;
+  // attention runs between a layer's QKV and o phases.  One loop, so every
+  // GEMV variant is emitted once.
+  for (int ph = 0; ph <= 4 * a.L; ++ph) {
+    const int l = ph >> 2, kind = ph < 4 * a.L ? (ph & 3) : 4;
+    const StepLayer* ly = a.layers + (kind == 4 ? 0 : l);
+    int* dn = a.done + 1 + 5 * l;  // QKV, attention, o, gate_up, down counters of layer l
     const int ts = 1 + 10 * l;
-    if (l > 0) ok = cta_wait(dn - 1, t_d, a, ok);
-    trace_mark(a, ts + 0);
-    if (ok) stage_norm(a, l > 0 ? a.h : nullptr, ly->ln1, xs, xs_stride, xsum, xsum_ld, SYM, red);
-    ok = gemv_phase<SYM, GB, true>(a, 4 * l + 0, ring, pc, pf, xs, xs_stride, xsum, xsum_ld, nullptr, 0, gw, Wt,
-                                   lane, ok, dn + 0);
+    // ---- wait for the phase's input; its source, width and RMSNorm weight
+    const __half* src;
+    const float* nw = nullptr;
+    int K, *done_ctr;
+    if (kind == 0) {  // QKV: RMSNorm(h) (the embedding rows already in xs for layer 0)
+      if (l > 0) ok = cta_wait(dn - 1, t_d, a, ok);
+      trace_mark(a, ts + 0);
+      src = l > 0 ? a.h : nullptr;
+      K = a.d;
+      nw = ly->ln1;
+      done_ctr = dn;
+    } else if (kind == 1) {  // o: attention output (+ residual)
+      ok = cta_wait(dn + 1, a.B * a.Hkv, a, ok);
+      if (l == 0) ok = cta_wait(a.done, 1, a, ok);  // h holds the embedding rows
+      trace_mark(a, ts + 4);
+      src = a.attn;
+      K = a.Hq * a.hd;
+      done_ctr = dn + 2;
+    } else if (kind == 2) {  // gate_up: RMSNorm(h), SwiGLU epilogue
+      ok = cta_wait(dn + 2, t_d, a, ok);
+      trace_mark(a, ts + 6);
+      src = a.h;
+      K = a.d;
+      nw = ly->ln2;
+      done_ctr = dn + 3;
+    } else if (kind == 3) {  // down: SwiGLU output (+ residual)
+      ok = cta_wait(dn + 3, tiles_of(2 * a.F), a, ok);
+      trace_mark(a, ts + 8);
+      src = a.sw;
+      K = a.F;
+      done_ctr = dn + 4;
+    } else {  // lm_head: final RMSNorm(h); with no layers h holds CTA 0's embedding rows
+      ok = a.L > 0 ? cta_wait(a.done + 5 * a.L, t_d, a, ok) : cta_wait(a.done, 1, a, ok);
+      trace_mark(a, 1 + 10 * a.L);
+      src = a.h;
+      K = a.d;
+      nw = a.ln_f;
+      done_ctr = a.done + 1 + 5 * a.L;
+    }
+    // ---- the GEMV: activations staged in shared memory when they fit (always
+    // for the normalized inputs), else read from L2 one k-block ahead
+    if (xs_fits(a.B, K, a.group)) {
+      if (ok) stage_x(a.B, a.group, a.eps, src, K, nw, xs, K + 8, xsum_of(K), SYM, red);
+      ok = gemv_phase<SYM, GB, true>(a, ph, ring, pc, pf, xs, K + 8, xsum_of(K), nullptr, 0, gw, Wt, lane, ok,
+                                     done_ctr);
+    } else {
+      ok = gemv_phase<SYM, GB, false>(a, ph, ring, pc, pf, nullptr, 0, nullptr, src, K, gw, Wt, lane, ok, done_ctr);
+    }
+    trace_mark(a, kind == 4 ? 2 + 10 * a.L : ts + (kind == 0 ? 1 : 2 * kind + 3));  // QKV, o, gate_up, down done
+    if (kind != 0) continue;
+    // ---- attention of layer l (RoPE + KV write fused)
     ok = __syncthreads_and(ok) != 0;  // the staged rows are dead: the union holds attention next
-    trace_mark(a, ts + 1);
-    // ---- attention (RoPE + KV write fused)
     {
       const int active = a.params[2];
       int nsplit, chunk;
@@ -1080,38 +1174,17 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
       }
     }
     trace_mark(a, ts + 3);
-    // ---- o projection (+ residual)
-    ok = cta_wait(dn + 1, a.B * a.Hkv, a, ok);
-    if (l == 0) ok = cta_wait(a.done, 1, a, ok);  // h holds the embedding rows
-    trace_mark(a, ts + 4);
-    ok = gemv_phase<SYM, GB, false>(a, 4 * l + 1, ring, pc, pf, nullptr, 0, nullptr, 0, a.attn, a.Hq * a.hd, gw,
-                                    Wt, lane, ok, dn + 2);
-    trace_mark(a, ts + 5);
-    // ---- gate_up (RMSNorm fused, SwiGLU epilogue)
-    ok = cta_wait(dn + 2, t_d, a, ok);
-    trace_mark(a, ts + 6);
-    if (ok) stage_norm(a, a.h, ly->ln2, xs, xs_stride, xsum, xsum_ld, SYM, red);
-    ok = gemv_phase<SYM, GB, true>(a, 4 * l + 2, ring, pc, pf, xs, xs_stride, xsum, xsum_ld, nullptr, 0, gw, Wt,
-                                   lane, ok, dn + 3);
-    trace_mark(a, ts + 7);
-    // ---- down projection (+ residual)
-    ok = cta_wait(dn + 3, tiles_of(2 * a.F), a, ok);
-    trace_mark(a, ts + 8);
-    ok = gemv_phase<SYM, GB, false>(a, 4 * l + 3, ring, pc, pf, nullptr, 0, nullptr, 0, a.sw, a.F, gw, Wt, lane,
-                                    ok, dn + 4);
-    trace_mark(a, ts + 9);
   }
-  // ---- lm_head (final RMSNorm fused) + argmax keys
-  // (with no layers the lm_head reads the embedding rows: wait for CTA 0's copy in h)
-  ok = a.L > 0 ? cta_wait(a.done + 5 * a.L, t_d, a, ok) : cta_wait(a.done, 1, a, ok);
-  trace_mark(a, 1 + 10 * a.L);
-  if (ok) stage_norm(a, a.h, a.ln_f, xs, xs_stride, xsum, xsum_ld, SYM, red);
-  ok = gemv_phase<SYM, GB, true>(a, 4 * a.L, ring, pc, pf, xs, xs_stride, xsum, xsum_ld, nullptr, 0, gw, Wt, lane,
-                                 ok, a.done + 1 + 5 * a.L);
-  trace_mark(a, 2 + 10 * a.L);
 
   // ---- wind down: copies still in flight (only after an abort) get a bounded wait
-  for (int i = ring.ci; i < ring.pi; ++i) mbar_wait(ring.bars + (i % kSStages), (uint32_t)((i / kSStages) & 1), kSMbarLimit);
+  if (lane == 0)
+    for (int i = 0; i < ring.inflight; ++i) {
+      mbar_wait(ring.bars + ring.cs, (uint32_t)ring.cpar, kSMbarLimit);
+      if (++ring.cs == kSStages) {
+        ring.cs = 0;
+        ring.cpar ^= 1;
+      }
+    }
   __syncthreads();
   trace_mark(a, 3 + 10 * a.L);
   if (tid == 0) *s_last = (atom_acq_rel_add(a.exit_cnt, 1) == C - 1) ? 1 : 0;
@@ -1154,8 +1227,7 @@ bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n
   if (hd != 64 && hd != 128) return false;
   if (n_kv_head <= 0 || n_head % n_kv_head != 0 || n_head / n_kv_head > 8) return false;
   if (d_model % 128 != 0) return false;
-  const size_t xsb = ((size_t)kStepMaxM * (d_model + 8) * 2 + 127) / 128 * 128;
-  if (xsb + (size_t)(d_model / 64) * 16 * 4 > (size_t)kSUnion) return false;
+  if (!xs_fits(kStepMaxM, d_model, group)) return false;
   if (kv_type != AXB_KV_F16 && (kv_group < 16 || hd % kv_group != 0)) return false;  // 16 elements share a scale in the score loads
   return step_attn_cap(kv_type, hd, kv_group) > 0;
 }
@@ -1187,9 +1259,7 @@ int step_launch(const StepArgs& a, cudaStream_t s) {
   AXB_CHECK_ARG(a.d > 0 && a.d % 128 == 0 && a.F % 64 == 0 && a.V > 0, "step: bad dims (%d, %d, %d)", a.d, a.F, a.V);
   AXB_CHECK_ARG((a.hd == 64 || a.hd == 128) && a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kMaxRepS,
                 "step: bad heads (%d, %d, %d)", a.Hq, a.Hkv, a.hd);
-  AXB_CHECK_ARG(((size_t)kStepMaxM * (a.d + 8) * 2 + 127) / 128 * 128 + (size_t)(a.d / 64) * 16 * 4 <=
-                    (size_t)kSUnion,
-                "step: d_model %d too large for the staged activations", a.d);
+  AXB_CHECK_ARG(xs_fits(kStepMaxM, a.d, a.group), "step: d_model %d too large for the staged activations", a.d);
   AXB_CHECK_ARG(a.attn_cap >= 16 && attn_layout(a.kv_type, a.hd, a.kv_group, a.attn_cap).bytes <= kSUnion / kSGroups,
                 "step: attention chunk %d does not fit", a.attn_cap);
   AXB_CHECK_ARG(a.lm_w && a.lm_s && a.ln_f && a.emb_w && a.emb_s && a.rope && a.tokens && a.params && a.err && a.h &&
