@@ -36,8 +36,11 @@ namespace axb {
 #ifndef AXB_STEP_CH
 #define AXB_STEP_CH 8
 #endif
+#ifndef AXB_STEP_WARPS
+#define AXB_STEP_WARPS 8
+#endif
 #ifndef AXB_STEP_STAGES
-#define AXB_STEP_STAGES 3
+#define AXB_STEP_STAGES (AXB_STEP_WARPS >= 16 ? 2 : 3)
 #endif
 #ifndef AXB_STEP_CHAINS
 #define AXB_STEP_CHAINS 2
@@ -48,14 +51,14 @@ namespace axb {
 #endif
 // 1: a stage is copied to registers and its ring slot re-armed before the math
 #ifndef AXB_STEP_REGSTAGE
-#define AXB_STEP_REGSTAGE 0
+#define AXB_STEP_REGSTAGE 1
 #endif
 #if AXB_STEP_OUTLINE
 #define AXB_STEP_FN __noinline__
 #else
 #define AXB_STEP_FN __forceinline__
 #endif
-constexpr int kSW = 8;  // warps per CTA
+constexpr int kSW = AXB_STEP_WARPS;  // warps per CTA (one CTA per SM)
 constexpr int kSThreads = kSW * 32;
 constexpr int kSCH = AXB_STEP_CH;          // k-blocks (512 B of weights each) per ring stage
 constexpr int kSStages = AXB_STEP_STAGES;  // ring stages per warp
@@ -63,10 +66,11 @@ constexpr int kSChains = AXB_STEP_CHAINS;  // independent MMA accumulator chains
 constexpr int kSStageW = kSCH * 512;
 constexpr int kSStageS = kSCH * 64;  // scale bytes per stage (max: affine, one group per k-block)
 constexpr int kSRing = (kSStages * (kSStageW + kSStageS) + kSStages * 8 + 127) / 128 * 128;
-constexpr int kSUnion = 96 * 1024;  // staged activations, or the two attention groups' working sets
-constexpr int kSMisc = 512;         // reduction scratch + attention mbarriers
+// staged activations, or the two attention groups' working sets
+constexpr int kSUnion = (kSW >= 16 ? 72 : 96) * 1024;
+constexpr int kSMisc = 1024;  // reduction scratch [kSW][kStepMaxM] + attention mbarriers + flags
 constexpr size_t kSSmem = (size_t)kSW * kSRing + kSUnion + kSMisc;
-constexpr int kSGroups = 2;  // attention groups (4 warps each) per CTA
+constexpr int kSGroups = 2;  // attention groups (4 warps each, warps 0-7) per CTA
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kSMbarLimit = 1u << 22;
 constexpr int kMaxRepS = 8;  // q heads per kv head
@@ -87,7 +91,9 @@ __device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t (&a)[4
 static_assert(kSSmem <= 227 * 1024, "step kernel shared memory");
 static_assert(kSStageW % 16 == 0 && kSStageS % 16 == 0 && kSRing % 128 == 0, "bulk-copy alignment");
 static_assert((kSStages * (kSStageW + kSStageS)) % 8 == 0, "mbarrier alignment");
-static_assert(kSW == 4 * kSGroups, "attention groups are 4 warps");
+static_assert(kSW >= 4 * kSGroups, "attention groups are 4 warps");
+static_assert(kSW * kStepMaxM * 4 <= 512, "reduction scratch");
+static_assert(kSW <= kStepTraceW, "trace slots per phase");
 
 // ------------------------------------------------------------------ helpers
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -123,12 +129,16 @@ __device__ __forceinline__ bool group_bar_or(int id, bool p) {
 }
 __device__ __forceinline__ int tiles_of(int n) { return (n + 15) >> 4; }
 
-// phase timeline stamp (thread 0 of each CTA), only when a trace buffer is set
-__device__ __forceinline__ void trace_mark(const StepArgs& a, int slot) {
-  if (a.trace == nullptr || threadIdx.x != 0) return;
+// phase timeline stamp, only when a trace buffer is set: thread 0 of each CTA
+// (trace_mark), or the calling thread (trace_at)
+__device__ __forceinline__ void trace_at(const StepArgs& a, int slot) {
+  if (a.trace == nullptr) return;
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   a.trace[(size_t)blockIdx.x * step_trace_slots(a.L) + slot] = t;
+}
+__device__ __forceinline__ void trace_mark(const StepArgs& a, int slot) {
+  if (threadIdx.x == 0) trace_at(a, slot);
 }
 
 // Bounded wait for *ctr >= target.  Gives up early when another CTA has already
@@ -269,8 +279,76 @@ __device__ __forceinline__ void ring_consumed(Ring& r) {
   --r.inflight;
 }
 
+// L2 prefetch cursor (lane 0).  It runs a fixed number of weight bytes
+// (StepArgs::l2_ahead) in front of the ring's producer, over the same stream
+// in the same order -- this warp's slice of every GEMV phase in turn -- so
+// HBM keeps streaming, in the order the data is needed, while the warp waits
+// for activations; the ring's copies then find their data in L2.  A warp's
+// slice of a phase is one contiguous byte range of the words array (units
+// are (tile, group) pairs stored tile-major), and its scales one range too.
+struct Pf {
+  int ph;               // phase being prefetched; > 4 L when the step's stream is exhausted
+  long long off, end;   // words bytes [off, end) of this warp's slice still to prefetch
+  const char* W;
+  long long issued;     // words bytes prefetched so far this step
+  long long ringpos;    // words bytes handed to the ring so far this step
+};
+constexpr int kPfChunk = 16384;  // bytes per prefetch request
+
 template <bool SYM, int GB>
-__device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, Cur& pf, const StepArgs& a, int gw, int Wt, int lane) {
+__device__ void pf_load(Pf& f, const StepArgs& a, int gw, int Wt) {
+  constexpr int UB = SYM ? 32 : 64;
+  for (; f.ph <= 4 * a.L; ++f.ph) {
+    const GPh g = gph(a, f.ph);
+    const long long We = eff_warps(g.U, Wt);
+    if (gw >= We) continue;
+    const long long u0 = (long long)gw * g.U / We, u1 = (long long)(gw + 1) * g.U / We;
+    if (u0 >= u1) continue;
+    f.W = g.W;
+    f.off = u0 * GB * 512;
+    f.end = u1 * GB * 512;
+    prefetch_l2(g.S + u0 * UB, (uint32_t)((u1 - u0) * UB));  // the slice's scales in one request
+    return;
+  }
+  f.off = f.end = 0;
+}
+
+template <bool SYM, int GB>
+__device__ void pf_run(Pf& f, const StepArgs& a, int gw, int Wt) {
+  const long long target = f.ringpos + a.l2_ahead;
+  while (f.issued < target && f.ph <= 4 * a.L) {
+    if (f.off >= f.end) {
+      ++f.ph;
+      pf_load<SYM, GB>(f, a, gw, Wt);
+      continue;
+    }
+    const long long n = min(f.end - f.off, (long long)kPfChunk);
+    prefetch_l2(f.W + f.off, (uint32_t)n);
+    f.off += n;
+    f.issued += n;
+  }
+}
+
+// L2 prefetch of this warp's whole slice (words and scales) of GEMV phase ph
+// (lane 0), in requests of at most 64 KB.  Issued when the warp enters a
+// latency-bound stretch (attention), so HBM streams the next phases' weights
+// into L2 while the critical path does not need HBM.
+template <bool SYM, int GB>
+__device__ void prefetch_slice(const StepArgs& a, int ph, int gw, int Wt, int lane) {
+  if (lane != 0 || ph > 4 * a.L) return;
+  constexpr int UB = SYM ? 32 : 64;
+  const GPh g = gph(a, ph);
+  const long long We = eff_warps(g.U, Wt);
+  if (gw >= We) return;
+  const long long u0 = (long long)gw * g.U / We, u1 = (long long)(gw + 1) * g.U / We;
+  if (u0 >= u1) return;
+  const long long ub = (long long)GB * 512, end = u1 * ub;
+  for (long long o = u0 * ub; o < end; o += 65536) prefetch_l2(g.W + o, (uint32_t)min(end - o, 65536ll));
+  prefetch_l2(g.S + u0 * UB, (uint32_t)((u1 - u0) * UB));
+}
+
+template <bool SYM, int GB>
+__device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, Pf& pf, const StepArgs& a, int gw, int Wt, int lane) {
   if (lane != 0) return;
   constexpr int UB = SYM ? 32 : 64;  // scale bytes per group
   if (pc.kb >= pc.kb_end && !cur_fix<GB>(pc, a, gw, Wt)) return;
@@ -283,28 +361,10 @@ __device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, Cur& pf, const Step
   bulk_g2s(r.buf + kSStages * kSStageW + st * kSStageS, pc.S + (size_t)(pc.kb / GB) * UB, bs, r.bars + st);
   pc.kb += n;
   ++r.inflight;
-  (void)pf;
-}
-
-// L2 prefetch of this warp's whole slice (words and scales) of GEMV phase ph,
-// in bulk requests of at most 64 KB (lane 0).  Issued a few phases ahead, it
-// keeps HBM streaming through the latency-bound stretches of a layer (waits,
-// attention, split-tile reductions) that the shared-memory ring alone cannot
-// cover.
-template <bool SYM, int GB>
-__device__ void prefetch_phase(const StepArgs& a, int ph, int gw, int Wt, int lane) {
-  if (lane != 0 || ph > 4 * a.L) return;
-  constexpr int UB = SYM ? 32 : 64;
-  const GPh g = gph(a, ph);
-  const long long We = eff_warps(g.U, Wt);
-  if (gw >= We) return;
-  const long long u0 = (long long)gw * g.U / We, u1 = (long long)(gw + 1) * g.U / We;
-  const size_t ub = (size_t)GB * 512, end = (size_t)u1 * ub;
-  for (size_t o = (size_t)u0 * ub; o < end; o += 65536) {
-    const size_t len = end - o < 65536 ? end - o : 65536;
-    prefetch_l2(g.W + o, (uint32_t)len);
+  if (a.l2_ahead > 0) {
+    pf.ringpos += bw;
+    pf_run<SYM, GB>(pf, a, gw, Wt);
   }
-  prefetch_l2(g.S + u0 * UB, (uint32_t)((u1 - u0) * UB));
 }
 
 __device__ __forceinline__ int warp_of_unit(long long u, long long U, long long Wt) {
@@ -389,10 +449,9 @@ __device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const StepLayer*
 // One GEMV phase for this warp.  x is staged in shared memory (XS: normalized
 // rows + per-group sums) or read from global memory (L2) one k-block ahead.
 template <bool SYM, int GB, bool XS>
-__device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Cur& pf, const __half* xs, int xs_stride,
+__device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Pf& pf, const __half* xs, int xs_stride,
                            const float* xsum, const __half* xg, int ldx, int gw, int Wt, int lane,
                            bool ok, int* done_ctr) {
-  if (a.l2_ahead > 0) prefetch_phase<SYM, GB>(a, ph + a.l2_ahead, gw, Wt, lane);
   const GPh g = gph(a, ph);
   const long long We = eff_warps(g.U, Wt);
   if (gw >= We || !ok) return ok;
@@ -797,7 +856,7 @@ __device__ __forceinline__ AttnItem attn_item_of(int item, int nsplit, int chunk
 // One attention item (sequence b, kv head, split) on a group of 4 warps.
 // gt = thread index in the group, gwarp = warp index in the group.
 template <int HD>
-__device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, const AttnItem& it, int nsplit, bool prefetched,
+__device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, int layer, const AttnItem& it, int nsplit, bool prefetched,
                           char* gsm, uint64_t* bar, uint32_t& uses, int bar_id, int gt, int* done_ctr, bool ok) {
   constexpr int DPL = HD / 32, EPT = HD / 16;
   const int lane = gt & 31, gwarp = gt >> 5;
@@ -981,7 +1040,6 @@ __device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, co
     else
       a.part_o[((pidx + r) * kStepMaxSplits + it.split) * HD + e] = o;
   }
-  int* flag = reinterpret_cast<int*>(ml_s + 24);
   if (nsplit == 1) {
     group_bar(bar_id);
     if (gt == 0) red_release_add(done_ctr, 1);
@@ -992,46 +1050,75 @@ __device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, co
     a.part_ml[((pidx + gt) * kStepMaxSplits + it.split) * 2 + 1] = ml_s[8 + gt];
   }
   group_bar(bar_id);
+  // ---- combine, shared by all the head's split groups.  Every split of the
+  // head runs at once (n_items <= attention groups in the grid), so each group
+  // waits for all of them and then combines its own slice of the head's
+  // n_rep * HD outputs.  The per-head counter only grows during a step (layer l
+  // completes at (l + 1) * nsplit arrivals); the step's last CTA clears it.
   int* cnt = a.attn_cnt + it.b * a.Hkv + it.kvh;
-  if (gt == 0) *flag = (atom_acq_rel_add(cnt, 1) == nsplit - 1) ? 1 : 0;
+  int* flag = reinterpret_cast<int*>(ml_s + 24);
+  if (gt == 0) {
+    red_release_add(cnt, 1);
+    *flag = wait_ge(cnt, (layer + 1) * nsplit, a) ? 1 : 0;
+  }
   group_bar(bar_id);
-  if (!*flag) return true;
-  // ---- combine the splits in split order: per-head weights first
-  for (int r = gwarp; r < n_rep; r += 4) {
+  if (!*flag) return false;
+  const int nout = n_rep * HD;
+  const int i0 = it.split * nout / nsplit, i1 = (it.split + 1) * nout / nsplit;
+  const int r_lo = i0 / HD, r_hi = (i1 - 1) / HD;  // heads touched by the slice
+  // per-head split weights: each lane loads the (m, l) of splits lane and lane + 32
+  static_assert(kStepMaxSplits <= 64, "two splits per lane");
+  for (int r = r_lo + gwarp; r <= r_hi; r += 4) {
     const size_t hb = (pidx + r) * kStepMaxSplits;
-    float Mx = -INFINITY;
-    for (int sp = lane; sp < nsplit; sp += 32) Mx = fmaxf(Mx, __ldcg(a.part_ml + (hb + sp) * 2));
-    Mx = warp_max(Mx);
+    float2 ml[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int sp = lane + 32 * q;
+      ml[q] = sp < nsplit ? __ldcg(reinterpret_cast<const float2*>(a.part_ml) + hb + sp) : make_float2(-INFINITY, 0.f);
+    }
+    const float Mx = warp_max(fmaxf(ml[0].x, ml[1].x));
     float Ls = 0.f;
-    for (int sp = lane; sp < nsplit; sp += 32) {
-      const float m = __ldcg(a.part_ml + (hb + sp) * 2), l = __ldcg(a.part_ml + (hb + sp) * 2 + 1);
-      const float cw = (m == -INFINITY) ? 0.f : __expf(m - Mx);
-      coef[r * kStepMaxSplits + sp] = cw;
-      Ls += l * cw;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int sp = lane + 32 * q;
+      if (sp < nsplit) {
+        const float cw = (ml[q].x == -INFINITY) ? 0.f : __expf(ml[q].x - Mx);
+        coef[(r - r_lo) * kStepMaxSplits + sp] = cw;
+        Ls += ml[q].y * cw;
+      }
     }
     Ls = warp_sum(Ls);
-    if (lane == 0) ml_s[8 + r] = Ls;
+    if (lane == 0) ml_s[8 + (r - r_lo)] = Ls;
   }
   group_bar(bar_id);
-  for (int i = gt; i < n_rep * HD; i += 128) {
-    const int r = i / HD, e = i % HD;
+  // 8 lanes per output (splits j, j + 8, ...), 16 outputs per pass; the
+  // lanes' partial sums meet in a fixed shuffle order
+  const int j8 = gt & 7, npass = (i1 - i0 + 15) / 16;  // the same trip count in every lane
+  for (int pass = 0; pass < npass; ++pass) {
+    const int i = i0 + 16 * pass + (gt >> 3);
+    const bool act = i < i1;
+    const int ii = act ? i : i0;
+    const int r = ii / HD, e = ii % HD;
     const size_t hb = (pidx + r) * kStepMaxSplits;
-    float O = 0.f;
-    for (int sp0 = 0; sp0 < nsplit; sp0 += 8) {
-      float v[8];
+    float v[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = (sp0 + u < nsplit) ? __ldcg(a.part_o + (hb + sp0 + u) * HD + e) : 0.f;
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (sp0 + u < nsplit) O += v[u] * coef[r * kStepMaxSplits + sp0 + u];
+    for (int u = 0; u < 8; ++u) {
+      const int sp = j8 + 8 * u;
+      v[u] = (act && sp < nsplit) ? __ldcg(a.part_o + (hb + sp) * HD + e) : 0.f;
     }
-    a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, ml_s[8 + r]));
+    float O = 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int sp = j8 + 8 * u;
+      if (act && sp < nsplit) O = __fmaf_rn(v[u], coef[(r - r_lo) * kStepMaxSplits + sp], O);
+    }
+    O += __shfl_xor_sync(0xffffffffu, O, 1);
+    O += __shfl_xor_sync(0xffffffffu, O, 2);
+    O += __shfl_xor_sync(0xffffffffu, O, 4);
+    if (act && j8 == 0) a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, ml_s[8 + (r - r_lo)]));
   }
   group_bar(bar_id);
-  if (gt == 0) {
-    atomicExch(cnt, 0);
-    red_release_add(done_ctr, 1);
-  }
+  if (gt == 0) red_release_add(done_ctr, 1);
   return true;
 }
 
@@ -1043,8 +1130,8 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   const int C = gridDim.x, Wt = C * kSW, gw = wid * C + blockIdx.x;  // virtual warp id
   char* uni = smem + kSW * kSRing;
   float* red = reinterpret_cast<float*>(uni + kSUnion);  // [kSW][kStepMaxM]
-  uint64_t* abar = reinterpret_cast<uint64_t*>(uni + kSUnion + 256);  // one per attention group
-  int* s_last = reinterpret_cast<int*>(uni + kSUnion + 256 + 64);
+  uint64_t* abar = reinterpret_cast<uint64_t*>(uni + kSUnion + 512);  // one per attention group
+  int* s_last = reinterpret_cast<int*>(uni + kSUnion + 512 + 64);
 
   // staged activations: M rows of K + 8 halves from the union's start, their
   // per-(group, token) sums at its end
@@ -1059,17 +1146,19 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   ring.cpar = 0;
   ring.ps = 0;
   ring.inflight = 0;
-  Cur pc, pf;
+  Cur pc;
+  Pf pf;
   if (lane == 0) {
     for (int s = 0; s < kSStages; ++s) mbar_init(ring.bars + s, 1);
     if (wid < kSGroups) mbar_init(abar + wid, 1);
     fence_mbar_init();
     pc.ph = 0;
     cur_load<GB>(pc, a, gw, Wt);
-    pf = pc;
+    pf.ph = 0;
+    pf.issued = pf.ringpos = 0;
+    pf.W = nullptr;
+    pf_load<SYM, GB>(pf, a, gw, Wt);
     for (int s = 0; s < kSStages; ++s) ring_issue<SYM, GB>(ring, pc, pf, a, gw, Wt, lane);
-    // phases 0 .. l2_ahead - 1 now; each later one when its predecessor l2_ahead back starts
-    for (int p = 0; p < a.l2_ahead; ++p) prefetch_phase<SYM, GB>(a, p, gw, Wt, lane);
   }
   __syncthreads();
 
@@ -1105,7 +1194,11 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
       nw = ly->ln1;
       done_ctr = dn;
     } else if (kind == 1) {  // o: attention output (+ residual)
-      ok = cta_wait(dn + 1, a.B * a.Hkv, a, ok);
+      {
+        int nsplit, chunk;
+        attn_split_plan(a.params[2], (kSGroups * C) / (a.B * a.Hkv), a.attn_cap, nsplit, chunk);
+        ok = cta_wait(dn + 1, a.B * a.Hkv * nsplit, a, ok);  // every attention item (and its combine slice)
+      }
       if (l == 0) ok = cta_wait(a.done, 1, a, ok);  // h holds the embedding rows
       trace_mark(a, ts + 4);
       src = a.attn;
@@ -1141,18 +1234,23 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     } else {
       ok = gemv_phase<SYM, GB, false>(a, ph, ring, pc, pf, nullptr, 0, nullptr, src, K, gw, Wt, lane, ok, done_ctr);
     }
+    if (lane == 0) trace_at(a, 4 + 10 * a.L + ph * kStepTraceW + wid);  // this warp's share done
     trace_mark(a, kind == 4 ? 2 + 10 * a.L : ts + (kind == 0 ? 1 : 2 * kind + 3));  // QKV, o, gate_up, down done
     if (kind != 0) continue;
     // ---- attention of layer l (RoPE + KV write fused)
+    if (a.pf_mask & 1) prefetch_slice<SYM, GB>(a, ph + 2, gw, Wt, lane);  // gate_up
+    if (a.pf_mask & 2) prefetch_slice<SYM, GB>(a, ph + 3, gw, Wt, lane);  // down
+    if (a.pf_mask & 4) prefetch_slice<SYM, GB>(a, ph + 1, gw, Wt, lane);  // o
     ok = __syncthreads_and(ok) != 0;  // the staged rows are dead: the union holds attention next
     {
       const int active = a.params[2];
       int nsplit, chunk;
       attn_split_plan(active, (kSGroups * C) / (a.B * a.Hkv), a.attn_cap, nsplit, chunk);
       const int n_items = a.B * a.Hkv * nsplit;
-      char* gsm = uni + grp * (kSUnion / kSGroups);
+      char* gsm = uni + (grp < kSGroups ? grp : 0) * (kSUnion / kSGroups);
       const AttnLayout Lo = attn_layout(a.kv_type, HD, a.kv_group, a.attn_cap);
-      int item = blockIdx.x * kSGroups + grp;
+      // warps beyond the attention groups take no items
+      int item = grp < kSGroups ? blockIdx.x * kSGroups + grp : n_items;
       if (ok && item < n_items && gt == 0) {  // cached rows do not depend on this step's QKV
         const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
         const size_t hb = ((size_t)it.b * a.Hkv + it.kvh) * a.S;
@@ -1169,9 +1267,10 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
           break;
         }
         const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
-        ok = attn_item<HD>(a, ly, it, nsplit, first, gsm, abar + grp, abar_uses, 1 + grp, gt, dn + 1, ok);
+        ok = attn_item<HD>(a, ly, l, it, nsplit, first, gsm, abar + grp, abar_uses, 1 + grp, gt, dn + 1, ok);
         first = false;
       }
+      if (gt == 0 && grp < kSGroups) trace_at(a, 4 + 10 * a.L + (4 * a.L + 1) * kStepTraceW + 2 * l + grp);
     }
     trace_mark(a, ts + 3);
   }
@@ -1197,9 +1296,9 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     a.keys[tid] = 0ull;
   }
   for (int i = tid; i < 2 + 5 * a.L; i += blockDim.x) a.done[i] = 0;
+  for (int i = tid; i < a.B * a.Hkv; i += blockDim.x) a.attn_cnt[i] = 0;  // grow through the step
   if (*reinterpret_cast<volatile int*>(a.exit_cnt + 1) != 0) {  // an aborted step may leave arrivals behind
     for (int i = tid; i < a.max_tiles; i += blockDim.x) a.tile_cnt[i] = 0;
-    for (int i = tid; i < a.B * a.Hkv; i += blockDim.x) a.attn_cnt[i] = 0;
   }
   __syncthreads();
   if (tid == 0) {

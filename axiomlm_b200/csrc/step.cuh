@@ -54,12 +54,17 @@ struct StepArgs {
   int* exit_cnt;
   int max_tiles;      // size of tile_cnt
   int attn_cap;       // tokens per attention sub-chunk
-  int l2_ahead;       // GEMV phases ahead whose weights are prefetched into L2 (0: none)
+  int l2_ahead;       // weight bytes each warp keeps prefetched into L2 ahead of its ring (0: none)
+  int pf_mask;        // whole-slice L2 prefetch at attention start: 1 gate_up, 2 down, 4 o
   unsigned long long* trace;  // optional phase timeline: [CTA][step_trace_slots(L)] globaltimer stamps
 };
 
-// Phase timeline slots per CTA: start, 10 per layer, then lm_head wait, lm_head done, exit.
-__host__ __device__ inline int step_trace_slots(int L) { return 4 + 10 * L; }
+// Phase timeline slots per CTA: start, 10 per layer, then lm_head wait,
+// lm_head done, exit (thread 0); then, per GEMV phase, the time each of the
+// CTA's warps finished its share; then, per layer, the time each of the two
+// attention groups finished its items.
+constexpr int kStepTraceW = 16;  // warp slots per GEMV phase (at least the warps per CTA)
+__host__ __device__ inline int step_trace_slots(int L) { return 4 + 10 * L + (4 * L + 1) * kStepTraceW + 2 * L; }
 
 constexpr int kStepMaxSplits = 64;
 constexpr int kStepMaxM = 8;
