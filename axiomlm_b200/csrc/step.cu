@@ -642,27 +642,32 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
       ++finished;
       continue;
     }
-    const int slot = (t == t_first) ? 0 : 1;
-    float* p = a.partials + ((size_t)(gw * 2 + slot) * 32 + lane) * 4;
-    *reinterpret_cast<float4*>(p) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    __syncwarp();
-    int old = 0;
-    if (lane == 0) old = atom_acq_rel_add(a.tile_cnt + t, 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
+    // A split tile is finished by the warp that owns its first unit: the tile
+    // is always that warp's last one (had its range run past the tile, it
+    // would own the whole tile).  Every other warp of the tile has it as its
+    // first tile: it publishes a partial and moves on without waiting.
     const int wf = warp_of_unit((long long)t * g.upt, g.U, We);
     const int wl = warp_of_unit((long long)(t + 1) * g.upt - 1, g.U, We);
-    if (old != wl - wf) continue;
-    __syncwarp();  // the other lanes' loads follow lane 0's acquire
-    float tot[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int w0 = wf; w0 <= wl; w0 += 4) {
+    if (gw != wf) {
+      float* p = a.partials + ((size_t)(gw * 2) * 32 + lane) * 4;
+      *reinterpret_cast<float4*>(p) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      __syncwarp();
+      if (lane == 0) red_release_add(a.tile_cnt + t, 1);
+      continue;
+    }
+    int arrived = 1;
+    if (lane == 0) arrived = wait_ge(a.tile_cnt + t, wl - wf, a) ? 1 : 0;
+    if (__shfl_sync(0xffffffffu, arrived, 0) == 0) {
+      ok = false;
+      break;
+    }
+    // the partials in warp order, this warp's own first
+    float tot[4] = {acc[0], acc[1], acc[2], acc[3]};
+    for (int w0 = wf + 1; w0 <= wl; w0 += 4) {
       float4 v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {  // independent loads, all in flight
-        const int w = w0 + u;
-        if (w > wl) continue;
-        const int sl = ((long long)w * g.U / We) / g.upt == t ? 0 : 1;
-        v[u] = __ldcg(reinterpret_cast<const float4*>(a.partials + ((size_t)(w * 2 + sl) * 32 + lane) * 4));
-      }
+      for (int u = 0; u < 4; ++u)  // independent loads, all in flight
+        if (w0 + u <= wl) v[u] = __ldcg(reinterpret_cast<const float4*>(a.partials + ((size_t)((w0 + u) * 2) * 32 + lane) * 4));
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         if (w0 + u > wl) continue;
@@ -674,7 +679,7 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
     }
     qkv_bias_fix(a, ly, g, t, tot, lane);
     step_epilogue(a, g, t, tot, lane);
-    if (lane == 0) atomicExch(a.tile_cnt + t, 0);
+    if (lane == 0) a.tile_cnt[t] = 0;  // published by the done counter's release below
     ++finished;
   }
   if (finished) {
