@@ -565,10 +565,6 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
     a.exit_cnt = r->buf<int>(L.st_exit);
     a.max_tiles = L.st_max_tiles;
     a.attn_cap = cap_tok;
-    const char* l2 = getenv("AXB_STEP_L2");
-    a.l2_ahead = (l2 ? atoi(l2) : 0) * 1024;  // KB per warp
-    const char* pm = getenv("AXB_STEP_PF");
-    a.pf_mask = pm ? atoi(pm) : 0;
     const char* tr = getenv("AXB_STEP_TRACE");  // phase timeline into runner buffer 5
     a.trace = (tr && atoi(tr) != 0) ? r->buf<unsigned long long>(L.st_trace) : nullptr;
   }

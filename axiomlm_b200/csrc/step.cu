@@ -73,7 +73,7 @@ constexpr size_t kSSmem = (size_t)kSW * kSRing + kSUnion + kSMisc;
 constexpr int kSGroups = 2;  // attention groups (4 warps each, warps 0-7) per CTA
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kSMbarLimit = 1u << 22;
-constexpr int kMaxRepS = 8;  // q heads per kv head
+constexpr int kMaxRepS = 4;  // q heads per kv head (GQA up to 4:1; larger ratios use the per-kernel runner)
 constexpr int kXsumLd = 16;  // tokens per group row of the staged-x sums
 // the staged-x sums of a K-wide activation sit at the end of the union, the rows from its start
 __host__ __device__ constexpr int xsum_bytes(int K, int G) { return ((K / G) * kXsumLd * 4 + 127) / 128 * 128; }
@@ -112,9 +112,6 @@ __device__ __forceinline__ int atom_acq_rel_add(int* p, int v) {
   int old;
   asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
-}
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void group_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
 // barrier of one attention group that also ORs a predicate over its 128 threads
@@ -279,76 +276,8 @@ __device__ __forceinline__ void ring_consumed(Ring& r) {
   --r.inflight;
 }
 
-// L2 prefetch cursor (lane 0).  It runs a fixed number of weight bytes
-// (StepArgs::l2_ahead) in front of the ring's producer, over the same stream
-// in the same order -- this warp's slice of every GEMV phase in turn -- so
-// HBM keeps streaming, in the order the data is needed, while the warp waits
-// for activations; the ring's copies then find their data in L2.  A warp's
-// slice of a phase is one contiguous byte range of the words array (units
-// are (tile, group) pairs stored tile-major), and its scales one range too.
-struct Pf {
-  int ph;               // phase being prefetched; > 4 L when the step's stream is exhausted
-  long long off, end;   // words bytes [off, end) of this warp's slice still to prefetch
-  const char* W;
-  long long issued;     // words bytes prefetched so far this step
-  long long ringpos;    // words bytes handed to the ring so far this step
-};
-constexpr int kPfChunk = 16384;  // bytes per prefetch request
-
 template <bool SYM, int GB>
-__device__ void pf_load(Pf& f, const StepArgs& a, int gw, int Wt) {
-  constexpr int UB = SYM ? 32 : 64;
-  for (; f.ph <= 4 * a.L; ++f.ph) {
-    const GPh g = gph(a, f.ph);
-    const long long We = eff_warps(g.U, Wt);
-    if (gw >= We) continue;
-    const long long u0 = (long long)gw * g.U / We, u1 = (long long)(gw + 1) * g.U / We;
-    if (u0 >= u1) continue;
-    f.W = g.W;
-    f.off = u0 * GB * 512;
-    f.end = u1 * GB * 512;
-    prefetch_l2(g.S + u0 * UB, (uint32_t)((u1 - u0) * UB));  // the slice's scales in one request
-    return;
-  }
-  f.off = f.end = 0;
-}
-
-template <bool SYM, int GB>
-__device__ void pf_run(Pf& f, const StepArgs& a, int gw, int Wt) {
-  const long long target = f.ringpos + a.l2_ahead;
-  while (f.issued < target && f.ph <= 4 * a.L) {
-    if (f.off >= f.end) {
-      ++f.ph;
-      pf_load<SYM, GB>(f, a, gw, Wt);
-      continue;
-    }
-    const long long n = min(f.end - f.off, (long long)kPfChunk);
-    prefetch_l2(f.W + f.off, (uint32_t)n);
-    f.off += n;
-    f.issued += n;
-  }
-}
-
-// L2 prefetch of this warp's whole slice (words and scales) of GEMV phase ph
-// (lane 0), in requests of at most 64 KB.  Issued when the warp enters a
-// latency-bound stretch (attention), so HBM streams the next phases' weights
-// into L2 while the critical path does not need HBM.
-template <bool SYM, int GB>
-__device__ void prefetch_slice(const StepArgs& a, int ph, int gw, int Wt, int lane) {
-  if (lane != 0 || ph > 4 * a.L) return;
-  constexpr int UB = SYM ? 32 : 64;
-  const GPh g = gph(a, ph);
-  const long long We = eff_warps(g.U, Wt);
-  if (gw >= We) return;
-  const long long u0 = (long long)gw * g.U / We, u1 = (long long)(gw + 1) * g.U / We;
-  if (u0 >= u1) return;
-  const long long ub = (long long)GB * 512, end = u1 * ub;
-  for (long long o = u0 * ub; o < end; o += 65536) prefetch_l2(g.W + o, (uint32_t)min(end - o, 65536ll));
-  prefetch_l2(g.S + u0 * UB, (uint32_t)((u1 - u0) * UB));
-}
-
-template <bool SYM, int GB>
-__device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, Pf& pf, const StepArgs& a, int gw, int Wt, int lane) {
+__device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, const StepArgs& a, int gw, int Wt, int lane) {
   if (lane != 0) return;
   constexpr int UB = SYM ? 32 : 64;  // scale bytes per group
   if (pc.kb >= pc.kb_end && !cur_fix<GB>(pc, a, gw, Wt)) return;
@@ -361,10 +290,6 @@ __device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, Pf& pf, const StepA
   bulk_g2s(r.buf + kSStages * kSStageW + st * kSStageS, pc.S + (size_t)(pc.kb / GB) * UB, bs, r.bars + st);
   pc.kb += n;
   ++r.inflight;
-  if (a.l2_ahead > 0) {
-    pf.ringpos += bw;
-    pf_run<SYM, GB>(pf, a, gw, Wt);
-  }
 }
 
 __device__ __forceinline__ int warp_of_unit(long long u, long long U, long long Wt) {
@@ -449,7 +374,7 @@ __device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const StepLayer*
 // One GEMV phase for this warp.  x is staged in shared memory (XS: normalized
 // rows + per-group sums) or read from global memory (L2) one k-block ahead.
 template <bool SYM, int GB, bool XS>
-__device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, Pf& pf, const __half* xs, int xs_stride,
+__device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, const __half* xs, int xs_stride,
                            const float* xsum, const __half* xg, int ldx, int gw, int Wt, int lane,
                            bool ok, int* done_ctr) {
   const GPh g = gph(a, ph);
@@ -511,7 +436,7 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
         }
         __syncwarp();
         ring_consumed(r);
-        ring_issue<SYM, GB>(r, pc, pf, a, gw, Wt, lane);
+        ring_issue<SYM, GB>(r, pc, a, gw, Wt, lane);
       }
       auto wword = [&](const int j) -> uint4 { return AXB_STEP_REGSTAGE ? wreg[AXB_STEP_REGSTAGE ? j : 0] : wst[j * 32]; };
       auto sword = [&](const int gi) -> uint2 {
@@ -621,7 +546,7 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
       if (!AXB_STEP_REGSTAGE) {
         __syncwarp();
         ring_consumed(r);
-        ring_issue<SYM, GB>(r, pc, pf, a, gw, Wt, lane);
+        ring_issue<SYM, GB>(r, pc, a, gw, Wt, lane);
       }
       kb0 += n;
     }
@@ -1152,18 +1077,13 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   ring.ps = 0;
   ring.inflight = 0;
   Cur pc;
-  Pf pf;
   if (lane == 0) {
     for (int s = 0; s < kSStages; ++s) mbar_init(ring.bars + s, 1);
     if (wid < kSGroups) mbar_init(abar + wid, 1);
     fence_mbar_init();
     pc.ph = 0;
     cur_load<GB>(pc, a, gw, Wt);
-    pf.ph = 0;
-    pf.issued = pf.ringpos = 0;
-    pf.W = nullptr;
-    pf_load<SYM, GB>(pf, a, gw, Wt);
-    for (int s = 0; s < kSStages; ++s) ring_issue<SYM, GB>(ring, pc, pf, a, gw, Wt, lane);
+    for (int s = 0; s < kSStages; ++s) ring_issue<SYM, GB>(ring, pc, a, gw, Wt, lane);
   }
   __syncthreads();
 
@@ -1234,18 +1154,15 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     // for the normalized inputs), else read from L2 one k-block ahead
     if (xs_fits(a.B, K, a.group)) {
       if (ok) stage_x(a.B, a.group, a.eps, src, K, nw, xs, K + 8, xsum_of(K), SYM, red);
-      ok = gemv_phase<SYM, GB, true>(a, ph, ring, pc, pf, xs, K + 8, xsum_of(K), nullptr, 0, gw, Wt, lane, ok,
+      ok = gemv_phase<SYM, GB, true>(a, ph, ring, pc, xs, K + 8, xsum_of(K), nullptr, 0, gw, Wt, lane, ok,
                                      done_ctr);
     } else {
-      ok = gemv_phase<SYM, GB, false>(a, ph, ring, pc, pf, nullptr, 0, nullptr, src, K, gw, Wt, lane, ok, done_ctr);
+      ok = gemv_phase<SYM, GB, false>(a, ph, ring, pc, nullptr, 0, nullptr, src, K, gw, Wt, lane, ok, done_ctr);
     }
     if (lane == 0) trace_at(a, 4 + 10 * a.L + ph * kStepTraceW + wid);  // this warp's share done
     trace_mark(a, kind == 4 ? 2 + 10 * a.L : ts + (kind == 0 ? 1 : 2 * kind + 3));  // QKV, o, gate_up, down done
     if (kind != 0) continue;
     // ---- attention of layer l (RoPE + KV write fused)
-    if (a.pf_mask & 1) prefetch_slice<SYM, GB>(a, ph + 2, gw, Wt, lane);  // gate_up
-    if (a.pf_mask & 2) prefetch_slice<SYM, GB>(a, ph + 3, gw, Wt, lane);  // down
-    if (a.pf_mask & 4) prefetch_slice<SYM, GB>(a, ph + 1, gw, Wt, lane);  // o
     ok = __syncthreads_and(ok) != 0;  // the staged rows are dead: the union holds attention next
     {
       const int active = a.params[2];
@@ -1318,7 +1235,7 @@ int step_num_warps() { return kSW; }
 int step_attn_cap(int kv_type, int hd, int kv_group) {
   for (int cap = 256; cap >= 16; cap -= 16) {
     const AttnLayout L = attn_layout(kv_type, hd, kv_group, cap);
-    if (L.bytes <= kSUnion / kSGroups && 2 * cap * L.rb >= 4 * 8 * hd * 4) return cap;
+    if (L.bytes <= kSUnion / kSGroups && 2 * cap * L.rb >= 4 * kMaxRepS * hd * 4) return cap;
   }
   return 0;
 }
@@ -1329,7 +1246,7 @@ bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n
   if (wfmt != AXB_W_Q4T_SYM && wfmt != AXB_W_Q4T_AFFINE) return false;
   if (group != 64 && group != 128) return false;
   if (hd != 64 && hd != 128) return false;
-  if (n_kv_head <= 0 || n_head % n_kv_head != 0 || n_head / n_kv_head > 8) return false;
+  if (n_kv_head <= 0 || n_head % n_kv_head != 0 || n_head / n_kv_head > kMaxRepS) return false;
   if (d_model % 128 != 0) return false;
   if (!xs_fits(kStepMaxM, d_model, group)) return false;
   if (kv_type != AXB_KV_F16 && (kv_group < 16 || hd % kv_group != 0)) return false;  // 16 elements share a scale in the score loads

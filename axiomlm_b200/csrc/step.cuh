@@ -54,8 +54,6 @@ struct StepArgs {
   int* exit_cnt;
   int max_tiles;      // size of tile_cnt
   int attn_cap;       // tokens per attention sub-chunk
-  int l2_ahead;       // weight bytes each warp keeps prefetched into L2 ahead of its ring (0: none)
-  int pf_mask;        // whole-slice L2 prefetch at attention start: 1 gate_up, 2 down, 4 o
   unsigned long long* trace;  // optional phase timeline: [CTA][step_trace_slots(L)] globaltimer stamps
 };
 

@@ -38,6 +38,10 @@ CFG_8B = dict(n_layer=32, d_model=4096, n_head=32, n_kv_head=8, ffn=14336, vocab
               block_size=8192)
 METRIC = "decode tokens/s (Q4 8B-shape, FP8 KV, ctx 4096)"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+# DRAM bytes (read + write) per algorithmic byte of the step kernel, from one
+# ncu capture of a smaller case (profiles/step_kernel_8b_q4g128_fp8.md); the
+# traffic of a full launch is this ratio times its algorithmic bytes.
+STEP_TRAFFIC_RATIO = 1.015
 
 
 def peaks():
@@ -248,6 +252,29 @@ def gemv_roofline(dec, batch, reps=3):
     return per_launch_bytes, per_launch_s, len(launches)
 
 
+def step_roofline(dec, batch, reps=20):
+    """Time the decode-step kernel itself: the runner's step (one CUDA-graph
+    replay: a tiny parameter kernel and the persistent step kernel) launched
+    back to back at fixed positions, CUDA events on the launching stream.
+    Algorithmic bytes per launch = step_bytes (weights, the KV window, the new
+    K/V rows and embedding rows)."""
+    c = dec.cache
+    seen = c.total_seen_tokens[0]
+    wp, active, _ = c.next_positions(1)
+    st = torch.cuda.current_stream()
+    for _ in range(3):
+        dec._step(batch, 1, seen % dec.rope_len, wp, active, 0)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        dec._step(batch, 1, seen % dec.rope_len, wp, active, 0)
+    e1.record(st)
+    e1.synchronize()
+    return step_bytes(dec, batch), e0.elapsed_time(e1) / 1e3 / reps, reps
+
+
 def run_ours(args, rank, world):
     from axiomlm_b200 import _lib as L
 
@@ -305,13 +332,21 @@ def run_ours(args, rank, world):
     te = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
     e2e = {"value": world * B * args.steps / te, "unit": "tokens/s", "h2d_bytes_per_step": B * 8,
            "d2h_bytes_per_step": B * 4}
-    # ---- roofline of the dominant kernel (the Q4 GEMV)
+    # ---- roofline of the dominant kernel: the persistent step kernel (one
+    # launch per step), or the Q4 GEMV when the per-kernel graph runs the step
     pk, pk_kind = peaks()
-    bpl, spl, nl = gemv_roofline(dec, B)
+    step_kernel = dec.uses_step_kernel
+    if step_kernel:
+        bpl, spl, nl = step_roofline(dec, B)
+        kname = "step_kernel<SYM, GB=2, HD=128> (whole decode step, one persistent launch)"
+    else:
+        bpl, spl, nl = gemv_roofline(dec, B)
+        kname = "qgemm_kernel<1,SYM,2,*> (Q4 G128 GEMV)"
     achieved = bpl / spl / 1e9
     out = None
     if rank == 0:
-        launches_per_step = 2 + cfg["n_layer"] * 5 + 2  # set_params, embed, 5/layer, lm_head, argmax
+        # set_params + the step kernel; per-kernel graph: set_params, embed, 5/layer, lm_head, argmax
+        launches_per_step = 2 if step_kernel else 2 + cfg["n_layer"] * 5 + 2
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
@@ -324,8 +359,9 @@ def run_ours(args, rank, world):
             "achieved_hbm_gbs": round(sbytes * B * args.steps / B / t / 1e9 / 1, 1) if world == 1 else None,
             "step_bytes": int(sbytes),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
-                         "kernel": "qgemm_kernel<1,SYM,2,*> (Q4 G128 GEMV)", "launches_timed": nl,
+                         "frac": round(achieved / pk["hbm_gbs"], 4),
+                         "traffic": int(bpl * STEP_TRAFFIC_RATIO) if step_kernel else None,
+                         "kernel": kname, "launches_timed": nl, "us_per_launch": round(spl * 1e6, 1),
                          "bytes_per_launch": int(bpl), "peak_kind": f"{pk_kind} (MEASURED_PEAKS.json hbm_gbs)"},
             "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},
             "clocks": clk.summary(), "gpu_launches": launches_per_step * args.steps,
