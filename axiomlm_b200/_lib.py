@@ -23,6 +23,10 @@ AXB_ETIMEOUT = -4
 W_Q4T_SYM = 1
 W_Q4T_AFFINE = 2
 W_Q8_G64 = 3
+W_TERNARY_G64 = 4
+W_TERNARY_PT = 5
+W_Q2_G64 = 6
+W_Q2K_SB256 = 7
 
 KV_F16 = 0
 KV_FP8 = 1
@@ -63,6 +67,14 @@ class KvWriteDesc(C.Structure):
         ("qkv", vp), ("bias", vp), ("rope", vp), ("rope_len", i32), ("rope_pos", i32), ("depths", vp),
         ("write_pos", i32), ("q_out", vp), ("dev_params", vp), ("k_cache", vp), ("v_cache", vp),
         ("k_scale", vp), ("v_scale", vp), ("k_is_fp32", i32),
+    ]
+
+
+class LbGemvDesc(C.Structure):
+    _fields_ = [
+        ("fmt", i32), ("words", vp), ("meta", vp), ("meta2", vp), ("pt_scale", vp),
+        ("N", i32), ("K", i32), ("M", i32), ("x", vp), ("ldx", i32), ("y", vp), ("ldy", i32),
+        ("bias", vp), ("workspace", vp), ("workspace_bytes", sz),
     ]
 
 
@@ -111,6 +123,13 @@ _SIGS = {
     "axb_q8_rows": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "axb_ternary_dequant": (i32, [vp, vp, i32, i32, i32, vp, vp]),
     "axb_q2_dequant": (i32, [vp, vp, i32, i32, vp, vp]),
+    "axb_q2t_words_bytes": (sz, [i32, i32]),
+    "axb_q2t_meta_bytes": (sz, [i32, i32, i32]),
+    "axb_q2t_meta2_bytes": (sz, [i32, i32, i32]),
+    "axb_q2t_from_ref": (i32, [i32, vp, vp, vp, i32, i32, vp, vp, vp, vp]),
+    "axb_q2t_dequant": (i32, [i32, vp, vp, vp, vp, i32, i32, vp, vp]),
+    "axb_lbgemv_workspace_bytes": (sz, [i32, i32, i32]),
+    "axb_lbgemv": (i32, [C.POINTER(LbGemvDesc), vp]),
     "axb_qgemm_workspace_bytes": (sz, [i32, i32, i32, i32]),
     "axb_qgemm": (i32, [C.POINTER(QGemmDesc), vp]),
     "axb_qgemm_status": (i32, [vp, vp]),

@@ -170,6 +170,136 @@ def dequantize_q2_k(w_packed, scales_biases, K: int | None = None) -> torch.Tens
     return out
 
 
+# ---------------------------------------------------------------- 2-bit weights
+
+
+@dataclass
+class Q2TWeight:
+    """A 2-bit projection in the q2t layout (16-row tiles of mma fragments,
+    128-wide k-blocks), relaid out from a reference packing: BitNet ternary
+    with group-64 or per-tensor scales, 2-bit affine group 64 ("Q2_K" in the
+    reference) or K-quant-style 256-element super-blocks."""
+
+    words: torch.Tensor  # uint8 q2t codes
+    meta: torch.Tensor | None  # per-group metadata (None for per-tensor ternary)
+    meta2: torch.Tensor | None  # K-quant (d, dmin) per super-block
+    pt_scale: torch.Tensor | None  # per-tensor ternary fp16 scale (1,)
+    N: int
+    K: int
+    fmt: int
+
+    @property
+    def nbytes(self) -> int:
+        n = self.words.numel()
+        for t in (self.meta, self.meta2, self.pt_scale):
+            if t is not None:
+                n += t.numel() * t.element_size()
+        return n
+
+    def dequant(self) -> torch.Tensor:
+        out = torch.empty((self.N, self.K), dtype=torch.float16, device=self.words.device)
+        L.call("axb_q2t_dequant", self.fmt, _p(self.words), _p(self.meta), _p(self.meta2), _p(self.pt_scale),
+               self.N, self.K, _p(out), _stream())
+        return out
+
+
+def q2t_from_ref(fmt: int, codes: torch.Tensor, s1: torch.Tensor | None = None, s2: torch.Tensor | None = None,
+                 K: int | None = None) -> Q2TWeight:
+    """Relayout a reference 2-bit packing (``L.W_TERNARY_G64``: codes +
+    group scales, quant.py:236-274; ``L.W_TERNARY_PT``: codes + one scale;
+    ``L.W_Q2_G64``: codes + (scale, bias), quant.py:339-381;
+    ``L.W_Q2K_SB256``: codes + sub bytes + (d, dmin)) into q2t."""
+    c = _cuda(codes, "codes")
+    if c.dtype != torch.uint8:
+        raise RuntimeError("codes must be uint8 (4 codes per byte)")
+    N = c.shape[0]
+    K = K or c.shape[1] * 4
+    lib = L.load()
+    dev = c.device
+    words = torch.empty(lib.axb_q2t_words_bytes(N, K), dtype=torch.uint8, device=dev)
+    mb, m2b = lib.axb_q2t_meta_bytes(fmt, N, K), lib.axb_q2t_meta2_bytes(fmt, N, K)
+    meta = torch.zeros(mb, dtype=torch.uint8, device=dev) if mb else None
+    meta2 = torch.zeros(m2b, dtype=torch.uint8, device=dev) if m2b else None
+    a = None if s1 is None else _cuda(s1, "s1")
+    b = None if s2 is None else _cuda(s2, "s2")
+    if words.numel() == 0:
+        raise RuntimeError(f"q2t: K={K} must be a multiple of 128")
+    L.call("axb_q2t_from_ref", fmt, _p(c), _p(a), _p(b), N, K, _p(words), _p(meta), _p(meta2), _stream())
+    pt = a.to(torch.float16).reshape(1).contiguous() if fmt == L.W_TERNARY_PT else None
+    return Q2TWeight(words, meta, meta2, pt, N, K, fmt)
+
+
+def lbgemm(x: torch.Tensor, W: Q2TWeight, bias: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[M, N] = x[M, K] W^T (+ bias) on the 2-bit tensor-core kernel (M <= 8
+    per launch; larger M is chunked)."""
+    x = _cuda(x, "x")
+    if x.dtype != torch.float16:
+        x = x.to(torch.float16)
+    lead = x.shape[:-1]
+    K = x.shape[-1]
+    if K != W.K:
+        raise RuntimeError(f"x has K={K}, weight has K={W.K}")
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty((M, W.N), dtype=torch.float16, device=x.device)
+    o2 = out.view(M, W.N)
+    lib = L.load()
+    ws = _WS.get(lib.axb_lbgemv_workspace_bytes(W.fmt, K, 8), x.device)
+    b = None if bias is None else _cuda(bias, "bias").to(torch.float16)
+    for m0 in range(0, M, 8):
+        m = min(8, M - m0)
+        d = L.LbGemvDesc(fmt=W.fmt, words=W.words.data_ptr(),
+                         meta=None if W.meta is None else W.meta.data_ptr(),
+                         meta2=None if W.meta2 is None else W.meta2.data_ptr(),
+                         pt_scale=None if W.pt_scale is None else W.pt_scale.data_ptr(),
+                         N=W.N, K=K, M=m, x=x2.data_ptr() + m0 * K * 2, ldx=K, y=o2.data_ptr() + m0 * W.N * 2,
+                         ldy=W.N, bias=None if b is None else b.data_ptr(), workspace=ws.data_ptr(),
+                         workspace_bytes=ws.numel())
+        L.call("axb_lbgemv", C.byref(d), _stream())
+    return out.view(*lead, W.N)
+
+
+_Q2T_CACHE: dict = {}
+
+
+def _cached_q2t(fmt: int, codes: torch.Tensor, s1: torch.Tensor, s2: torch.Tensor | None = None) -> Q2TWeight:
+    # relayout once per (tensor storage, version): weights are constant in decode
+    key = (fmt, codes.data_ptr(), codes._version, s1.data_ptr(), s1._version,
+           None if s2 is None else (s2.data_ptr(), s2._version), tuple(codes.shape))
+    hit = _Q2T_CACHE.get(key)
+    if hit is None:
+        if len(_Q2T_CACHE) > 256:
+            _Q2T_CACHE.clear()
+        hit = q2t_from_ref(fmt, codes, s1, s2)
+        _Q2T_CACHE[key] = hit
+    return hit
+
+
+def qmv_ternary_mps(x, w_packed, scales, bias=None) -> torch.Tensor:
+    """``_METAL_MOD.qmv_ternary_mps`` (quant.py:298-317): y = x W^T (+ bias)
+    for BitNet ternary; ``scales`` (N, K/64) per group, or one element for
+    the per-tensor form."""
+    w = _cuda(w_packed, "w_packed")
+    s = _cuda(scales, "scales")
+    fmt = L.W_TERNARY_PT if s.numel() == 1 else L.W_TERNARY_G64
+    return lbgemm(x, _cached_q2t(fmt, w, s), bias=bias)
+
+
+qmm_ternary_mps = qmv_ternary_mps
+
+
+def qmv_q2_k_mps(x, w_packed, scales_biases, bias=None) -> torch.Tensor:
+    """``_METAL_MOD.qmv_q2_k_mps`` (quant.py:406-425): y = x W^T (+ bias) for
+    the reference's group-64 affine 2-bit format."""
+    return lbgemm(x, _cached_q2t(L.W_Q2_G64, _cuda(w_packed, "w_packed"), _cuda(scales_biases, "scales_biases")),
+                  bias=bias)
+
+
+qmm_q2_k_mps = qmv_q2_k_mps
+
+
 # ---------------------------------------------------------------- GEMV
 
 

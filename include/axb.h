@@ -37,6 +37,19 @@ extern "C" {
 #define AXB_W_Q4T_SYM 1
 #define AXB_W_Q4T_AFFINE 2
 #define AXB_W_Q8_G64 3 /* reference Q8_G64 row-major (quant.py:72) */
+/* 2-bit formats (q2t layout on the device, relaid out from these reference packings):
+ * TERNARY_G64: pack_linear_ternary (quant.py:236-274): codes (N, K/4) u8 (0 -> 0,
+ *   1 -> +1, 2 -> -1), scales (N, K/64) fp16, w = q * s.
+ * TERNARY_PT:  same codes, one per-tensor fp16 absmean scale.
+ * Q2_G64:      pack_linear_q2_k (quant.py:339-381): codes (N, K/4) u8 (u in 0..3),
+ *   (scale, bias) (N, K/64, 2) fp16, w = fp16(fp16(u * s) + b).
+ * Q2K_SB256:   K-quant-style super-blocks: codes (N, K/4) u8,
+ *   sub (N, K/16) u8 = sc | mn << 4, (d, dmin) (N, K/256, 2) fp16,
+ *   w = d * sc * u - dmin * mn. */
+#define AXB_W_TERNARY_G64 4
+#define AXB_W_TERNARY_PT 5
+#define AXB_W_Q2_G64 6
+#define AXB_W_Q2K_SB256 7
 
 /* KV cache element types (StaticKVCache cache_dtype, paged_cache.py:122) */
 #define AXB_KV_F16 0
@@ -95,6 +108,41 @@ int axb_q8_rows(const int32_t* w_dev, const uint16_t* sb_dev, const int32_t* idx
 int axb_ternary_dequant(const uint8_t* w_dev, const uint16_t* s_dev, int N, int K, int per_tensor,
                         uint16_t* out_dev, void* stream);
 int axb_q2_dequant(const uint8_t* w_dev, const uint16_t* sb_dev, int N, int K, uint16_t* out_dev, void* stream);
+
+/* ---- 2-bit weights: relayout, dequant, GEMV (qmv_ternary / qmm_ternary,
+ *      quant.py:298-336; qmv_q2_k / qmm_q2_k, quant.py:406-444) ----------- */
+/* Device bytes of the q2t words / per-group metadata / K-quant super-block
+ * metadata for an (N, K) matrix (K a multiple of 128; 256 for Q2K_SB256). */
+size_t axb_q2t_words_bytes(int N, int K);
+size_t axb_q2t_meta_bytes(int fmt, int N, int K);
+size_t axb_q2t_meta2_bytes(int fmt, int N, int K);
+/* Relayout a reference packing (see the AXB_W_* 2-bit formats) into q2t.
+ * s1: scales (TERNARY_G64), (scale, bias) (Q2_G64), sub bytes (Q2K_SB256),
+ * unused for TERNARY_PT; s2: (d, dmin) for Q2K_SB256.  Codes, scales and biases
+ * are moved, never recomputed. */
+int axb_q2t_from_ref(int fmt, const uint8_t* codes_dev, const void* s1_dev, const void* s2_dev, int N, int K,
+                     void* words_dev, void* meta_dev, void* meta2_dev, void* stream);
+/* fp16 (N, K) dequant of q2t with the reference's value rule (dequantize_ternary,
+ * quant.py:277-295; dequantize_q2_k, quant.py:383-403). */
+int axb_q2t_dequant(int fmt, const void* words_dev, const void* meta_dev, const void* meta2_dev,
+                    const uint16_t* pt_scale_dev, int N, int K, uint16_t* out_dev, void* stream);
+typedef struct {
+  int fmt;               /* AXB_W_TERNARY_G64 | TERNARY_PT | Q2_G64 | Q2K_SB256 */
+  const void* words;     /* q2t words */
+  const void* meta;      /* q2t per-group metadata (NULL for TERNARY_PT) */
+  const void* meta2;     /* Q2K_SB256 (d, dmin), else NULL */
+  const uint16_t* pt_scale; /* TERNARY_PT fp16 scale, else NULL */
+  int N, K, M;           /* y[M, N] = x[M, K] W^T (+ bias); M <= 8 */
+  const void* x;         /* fp16 (M, ldx), 16-byte aligned, ldx % 8 == 0 */
+  int ldx;
+  void* y;               /* fp16 (M, ldy) */
+  int ldy;
+  const void* bias;      /* fp16 (N) or NULL */
+  void* workspace;       /* >= axb_lbgemv_workspace_bytes(fmt, K, M) (group sums of x) */
+  size_t workspace_bytes;
+} axb_lbgemv_desc;
+size_t axb_lbgemv_workspace_bytes(int fmt, int K, int M);
+int axb_lbgemv(const axb_lbgemv_desc* d, void* stream);
 
 /* ---- quantized GEMV / small-M GEMM (qmv_q4_marlin / qmm_q4_marlin,
  *      quant.py:637-684; Metal qmv_q4_marlin_apple_kernel) ------------------- */
