@@ -130,6 +130,9 @@ _SIGS = {
     "axb_q2t_dequant": (i32, [i32, vp, vp, vp, vp, i32, i32, vp, vp]),
     "axb_lbgemv_workspace_bytes": (sz, [i32, i32, i32]),
     "axb_lbgemv": (i32, [C.POINTER(LbGemvDesc), vp]),
+    "axb_qgemm_tc_workspace_bytes": (sz, [i32, i32, i32]),
+    "axb_qgemm_tc": (i32, [C.POINTER(QGemmDesc), vp]),
+    "axb_qgemm_tc_status": (i32, [vp, vp]),
     "axb_qgemm_workspace_bytes": (sz, [i32, i32, i32, i32]),
     "axb_qgemm": (i32, [C.POINTER(QGemmDesc), vp]),
     "axb_qgemm_status": (i32, [vp, vp]),

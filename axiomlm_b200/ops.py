@@ -340,6 +340,52 @@ def qgemm(x: torch.Tensor, W: Q4TWeight, bias: torch.Tensor | None = None, norm_
     return out.view(*lead, n_out)
 
 
+_TC_WS = _Workspace()
+
+
+def qgemm_tc(x: torch.Tensor, W: Q4TWeight, bias: torch.Tensor | None = None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[M, N] = x[M, K] W^T (+ bias) on the tcgen05 tensor-core kernel: the
+    dense-contraction path for many tokens (tree verification, prefill
+    chunks, large decode batches).  M <= 64 per launch; larger M is chunked.
+    Weights are dequantized to the reference's fp16 values and accumulated in
+    fp32."""
+    x = _cuda(x, "x")
+    if x.dtype != torch.float16:
+        x = x.to(torch.float16)
+    lead = x.shape[:-1]
+    K = x.shape[-1]
+    if K != W.K:
+        raise RuntimeError(f"x has K={K}, weight has K={W.K}")
+    if W.gate_up:
+        raise RuntimeError("qgemm_tc stores rows in order: pass a weight packed without the gate/up interleave")
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty((M, W.N), dtype=torch.float16, device=x.device)
+    o2 = out.view(M, W.N)
+    lib = L.load()
+    ws = _TC_WS.get(lib.axb_qgemm_tc_workspace_bytes(W.N, K, 64), x.device)
+    b = None if bias is None else _cuda(bias, "bias").to(torch.float16)
+    for m0 in range(0, M, 64):
+        m = min(64, M - m0)
+        d = L.QGemmDesc(fmt=W.fmt, group=W.group, words=W.words.data_ptr(), scales=W.scales.data_ptr(),
+                        N=W.N, K=K, M=m, x=x2.data_ptr() + m0 * K * 2, ldx=K, y=o2.data_ptr() + m0 * W.N * 2,
+                        ldy=W.N, bias=None if b is None else b.data_ptr(), norm_w=None, eps=0.0,
+                        epilogue=L.EPI_STORE, gate_up_interleave=0, workspace=ws.data_ptr(),
+                        workspace_bytes=ws.numel(), pdl=0)
+        L.call("axb_qgemm_tc", C.byref(d), _stream())
+    return out.view(*lead, W.N)
+
+
+def qgemm_tc_status() -> int:
+    """Synchronizes; AXB_ETIMEOUT if a bounded tensor-core wait ran out."""
+    b = _TC_WS.bufs.get(torch.cuda.current_device())
+    if b is None:
+        return 0
+    return L.load().axb_qgemm_tc_status(C.c_void_p(b.data_ptr()), _stream())
+
+
 _MARLIN_CACHE: dict = {}
 
 

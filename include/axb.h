@@ -188,6 +188,16 @@ size_t axb_qgemm_noalloc_scratch_bytes(void);
  * bounded weight-stream wait in an earlier axb_qgemm on this workspace ran out. */
 int axb_qgemm_status(void* workspace, void* stream);
 
+/* The same product on the tcgen05 tensor cores for large M (qmm_q4_marlin,
+ * quant.py:664-684, Metal qmm_q4_marlin_apple_kernel :2404): 1 <= M <= 64,
+ * fmt SYM group 128 or AFFINE group 64, plain store epilogue (+ bias).  Weights
+ * are dequantized to the reference's fp16 values, products accumulate in fp32
+ * tensor memory.  The workspace (error word, split-K partials) is
+ * zero-filled once; axb_qgemm_tc_status reports a bounded wait that ran out. */
+size_t axb_qgemm_tc_workspace_bytes(int N, int K, int M);
+int axb_qgemm_tc(const axb_qgemm_desc* d, void* stream);
+int axb_qgemm_tc_status(void* workspace, void* stream);
+
 /* ---- RMSNorm (modules.py:30-43) ---------------------------------------- */
 /* out fp16 (M, K) = fp16(fp32(x) * rsqrt(mean(x^2) + eps) * w) */
 int axb_rmsnorm(const uint16_t* x_dev, const float* w_dev, int M, int K, float eps, uint16_t* out_dev,
