@@ -37,6 +37,11 @@ EPI_STORE = 0
 EPI_RESIDUAL = 1
 EPI_SWIGLU = 2
 EPI_F32 = 3
+EPI_F32_ACC = 4
+
+TP_SUM_F32 = 0
+TP_SUM_F16 = 1
+TP_MAX_U64 = 2
 
 
 class AxbError(RuntimeError):
@@ -93,7 +98,7 @@ class ModelCfg(C.Structure):
         ("n_layer", i32), ("d_model", i32), ("n_head", i32), ("n_kv_head", i32), ("head_dim", i32),
         ("ffn", i32), ("vocab", i32), ("eps", f32), ("wfmt", i32), ("group", i32), ("lm_fmt", i32),
         ("lm_group", i32), ("kv_type", i32), ("kv_group", i32), ("max_batch", i32), ("max_seq", i32),
-        ("max_tokens", i32), ("rope_len", i32), ("has_qkv_bias", i32),
+        ("max_tokens", i32), ("rope_len", i32), ("has_qkv_bias", i32), ("tp_world", i32), ("tp_rank", i32),
     ]
 
 
@@ -104,7 +109,7 @@ class ModelPtrs(C.Structure):
         ("o_w", C.POINTER(vp)), ("o_s", C.POINTER(vp)), ("gu_w", C.POINTER(vp)), ("gu_s", C.POINTER(vp)),
         ("dn_w", C.POINTER(vp)), ("dn_s", C.POINTER(vp)), ("ln1", C.POINTER(vp)), ("ln2", C.POINTER(vp)),
         ("k_cache", C.POINTER(vp)), ("v_cache", C.POINTER(vp)), ("k_scale", C.POINTER(vp)),
-        ("v_scale", C.POINTER(vp)),
+        ("v_scale", C.POINTER(vp)), ("tp_comm", vp),
     ]
 
 
@@ -152,6 +157,11 @@ _SIGS = {
     "axb_runner_buffer": (i32, [vp, i32, C.POINTER(sz), C.POINTER(sz)]),
     "axb_runner_step": (i32, [vp, i32, i32, i32, i32, i32, i32, vp, vp, i32, vp]),
     "axb_runner_uses_step_kernel": (i32, [vp]),
+    "axb_tp_unique_id": (i32, [vp]),
+    "axb_tp_comm_create": (i32, [vp, i32, i32, C.POINTER(vp)]),
+    "axb_tp_comm_destroy": (i32, [vp]),
+    "axb_tp_comm_abort": (i32, [vp]),
+    "axb_tp_allreduce": (i32, [vp, vp, sz, i32, vp]),
 }
 
 _lib = None

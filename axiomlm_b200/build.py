@@ -58,7 +58,7 @@ def build(force: bool = False, verbose: bool = True) -> str:
         objs = list(ex.map(lambda s: _compile(s, force, hmt), srcs))
     newest = max(os.path.getmtime(o) for o in objs)
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < newest:
-        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr[-4000:]}")

@@ -374,6 +374,8 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, int tile, const floa
           *yp = __float2half_rn(__fadd_rn(__half2float(*yp), __half2float(vh)));
         } else if (a.epi == AXB_EPI_F32) {
           reinterpret_cast<float*>(a.y)[(size_t)n * a.ldy + col] = __half2float(vh);
+        } else if (a.epi == AXB_EPI_F32_ACC) {
+          reinterpret_cast<float*>(a.y)[(size_t)n * a.ldy + col] = v;
         } else {
           reinterpret_cast<__half*>(a.y)[(size_t)n * a.ldy + col] = vh;
         }

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "step.cuh"
+#include "tp.cuh"
 
 namespace axb {
 
@@ -187,6 +188,7 @@ constexpr int kArgmaxParts = 256;
 struct Layout {
   size_t tokens, params, masks, depths, x, h, qkv, q, attn, sw, logits, amax, xnorm, gemm_ws, attn_ws, total;
   size_t am_v, am_i, am_cnt;
+  size_t tp_part, tp_keys;  // tensor parallel: row-parallel partial sums (fp32), argmax keys
   size_t gemm_ws_bytes, attn_ws_bytes;
   // persistent step kernel (decode, B <= 8)
   size_t st_layers, st_done, st_tiles, st_part, st_po, st_pml, st_acnt, st_keys, st_exit, st_trace;
@@ -221,6 +223,8 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.am_v = take(rows * kArgmaxParts * 4);
   L.am_i = take(rows * kArgmaxParts * 4);
   L.am_cnt = take(rows * 4);
+  L.tp_part = take(c.tp_world > 1 ? rows * c.d_model * 4 : 0);
+  L.tp_keys = take(c.tp_world > 1 ? rows * 8 : 0);
   int m = (int)std::min<size_t>(rows, 64);
   size_t g = 0;
   for (int n : {(int)qkv_dim, c.d_model, 2 * c.ffn, c.vocab}) g = std::max(g, qgemm_workspace(n, m));
@@ -262,6 +266,7 @@ struct Runner {
   std::vector<const void*> qkv_w, qkv_s, qkv_b, o_w, o_s, gu_w, gu_s, dn_w, dn_s;
   std::vector<const float*> ln1, ln2;
   std::vector<void*> kc, vc, ks, vs;
+  void* tp_comm = nullptr;  // tensor parallel communicator (tp_world > 1)
   cudaStream_t cap = nullptr;
   std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;
   // persistent step kernel: decode steps of B <= 8 sequences run as one launch
@@ -288,7 +293,7 @@ struct Runner {
       d.M = std::min(64, M - m0);
       d.x = x + (size_t)m0 * ldx;
       d.ldx = ldx;
-      size_t esz = epi == AXB_EPI_F32 ? 4 : 2;
+      size_t esz = (epi == AXB_EPI_F32 || epi == AXB_EPI_F32_ACC) ? 4 : 2;
       d.y = reinterpret_cast<char*>(y) + (size_t)m0 * ldy * esz;
       d.ldy = ldy;
       d.bias = bias;
@@ -316,6 +321,22 @@ struct Runner {
     return gemv(w, s, fmt, group, N, K, M, buf<__half>(L.h), K, y, ldy, bias, nullptr, epi, gu, st);
   }
 
+  // x += W a for the o / down projections.  Tensor parallel: this rank's
+  // K-slice gives an fp32 partial, the ranks' partials meet in one allreduce,
+  // then the residual add rounds as the single-GPU path does.
+  int row_parallel(const void* w, const void* s, int K, int rows, const __half* act, cudaStream_t st) const {
+    const int d = c.d_model;
+    if (c.tp_world <= 1)
+      return gemv(w, s, c.wfmt, c.group, d, K, rows, act, K, buf<void>(L.x), d, nullptr, nullptr, AXB_EPI_RESIDUAL, 0,
+                  st);
+    int rc = gemv(w, s, c.wfmt, c.group, d, K, rows, act, K, buf<void>(L.tp_part), d, nullptr, nullptr,
+                  AXB_EPI_F32_ACC, 0, st);
+    if (rc) return rc;
+    rc = tp_allreduce(tp_comm, buf<void>(L.tp_part), (size_t)rows * d, AXB_TP_SUM_F32, st);
+    if (rc) return rc;
+    return tp_residual(buf<__half>(L.x), buf<float>(L.tp_part), rows * d, st);
+  }
+
   int step_forward(int B, cudaStream_t st) const {
     StepArgs a = sa;
     a.B = B;
@@ -328,7 +349,8 @@ struct Runner {
     const int qkv_dim = (Hq + 2 * Hkv) * hd, qd = Hq * hd;
     cudaError_t e = launch_pdl(embed_q8_kernel, dim3(rows, (d / 4 + 127) / 128), dim3(128), 0, st, pdl,
                                (const uint32_t*)emb_w,
-                               (const __half*)emb_s, (const int32_t*)buf<int32_t>(L.tokens), d, c.vocab,
+                               (const __half*)emb_s, (const int32_t*)buf<int32_t>(L.tokens), d,
+                               c.vocab * c.tp_world,  // the embedding table is whole on every rank
                                buf<__half>(L.x), buf<int>(L.params) + 4);
     if (e != cudaSuccess) return cuda_status(e, "embed launch");
     for (int l = 0; l < c.n_layer; ++l) {
@@ -391,14 +413,12 @@ struct Runner {
         rc = attention_fused(&ad, f, st);
       }
       if (rc) return rc;
-      rc = gemv(o_w[l], o_s[l], c.wfmt, c.group, d, qd, rows, buf<__half>(L.attn), qd, buf<void>(L.x), d, nullptr,
-                nullptr, AXB_EPI_RESIDUAL, 0, st);
+      rc = row_parallel(o_w[l], o_s[l], qd, rows, buf<__half>(L.attn), st);
       if (rc) return rc;
       rc = norm_gemv(ln2[l], gu_w[l], gu_s[l], 2 * c.ffn, d, rows, buf<void>(L.sw), c.ffn, nullptr, AXB_EPI_SWIGLU,
                      1, c.wfmt, c.group, st);
       if (rc) return rc;
-      rc = gemv(dn_w[l], dn_s[l], c.wfmt, c.group, d, c.ffn, rows, buf<__half>(L.sw), c.ffn, buf<void>(L.x), d,
-                nullptr, nullptr, AXB_EPI_RESIDUAL, 0, st);
+      rc = row_parallel(dn_w[l], dn_s[l], c.ffn, rows, buf<__half>(L.sw), st);
       if (rc) return rc;
     }
     int rc = norm_gemv(ln_f, lm_w, lm_s, c.vocab, d, rows, buf<void>(L.logits), c.vocab, nullptr, AXB_EPI_STORE, 0,
@@ -414,7 +434,11 @@ struct Runner {
     e = launch_pdl(argmax_part_kernel, dim3(parts, rows), dim3(128), 0, st, pdl, (const __half*)buf<__half>(L.logits),
                    c.vocab, c.vocab, chunk, buf<float>(L.am_v), buf<int>(L.am_i), buf<int>(L.am_cnt),
                    buf<int32_t>(L.amax));
-    return cuda_status(e, "argmax launch");
+    if (e != cudaSuccess) return cuda_status(e, "argmax launch");
+    if (c.tp_world > 1)  // vocab-parallel lm_head: the ranks' winners meet in a max of (value, -index) keys
+      return tp_argmax(buf<__half>(L.logits), c.vocab, buf<int32_t>(L.amax), rows, c.tp_rank * c.vocab,
+                       buf<unsigned long long>(L.tp_keys), tp_comm, st);
+    return AXB_OK;
   }
 };
 
@@ -434,7 +458,11 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   const axb_model_cfg& c = *cfg;
   AXB_CHECK_ARG(c.n_layer > 0 && c.d_model % 64 == 0 && c.ffn % 64 == 0 && c.vocab > 0, "runner_create: bad dims");
   AXB_CHECK_ARG(c.head_dim == 64 || c.head_dim == 128, "runner_create: head_dim must be 64 or 128");
-  AXB_CHECK_ARG(c.n_head * c.head_dim == c.d_model, "runner_create: n_head * head_dim must equal d_model");
+  const int tpw = c.tp_world > 1 ? c.tp_world : 1;
+  AXB_CHECK_ARG(c.tp_world <= 1 || (c.tp_rank >= 0 && c.tp_rank < c.tp_world && p && p->tp_comm),
+                "runner_create: tensor parallel needs a rank in [0, tp_world) and a communicator");
+  AXB_CHECK_ARG(c.n_head * c.head_dim * tpw == c.d_model,
+                "runner_create: n_head * head_dim * tp_world must equal d_model");
   AXB_CHECK_ARG(c.wfmt == AXB_W_Q4T_SYM || c.wfmt == AXB_W_Q4T_AFFINE, "runner_create: unsupported weight format");
   AXB_CHECK_ARG(c.lm_fmt == AXB_W_Q4T_SYM || c.lm_fmt == AXB_W_Q4T_AFFINE,
                 "runner_create: lm_head format %d not supported by the runner", c.lm_fmt);
@@ -454,6 +482,11 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   if (int rc = attn_prepare()) return rc;
   Runner* r = new Runner();
   r->c = c;
+  if (c.tp_world <= 1) {
+    r->c.tp_world = 1;
+    r->c.tp_rank = 0;
+  }
+  r->tp_comm = c.tp_world > 1 ? p->tp_comm : nullptr;
   if (const char* ev = getenv("AXB_PDL")) {
     r->pdl = atoi(ev) != 0;
     r->pdl_mode = atoi(ev) == 2 ? 2 : 1;
@@ -491,7 +524,7 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   // persistent step kernel (env AXB_STEP=0 keeps decode on the per-kernel graph)
   const char* sv = getenv("AXB_STEP");
   const int cap_tok = step_attn_cap(c.kv_type, c.head_dim, c.kv_group);
-  r->step_ok = !(sv && atoi(sv) == 0) &&
+  r->step_ok = !(sv && atoi(sv) == 0) && c.tp_world <= 1 &&
                step_supported(c.wfmt, c.group, c.lm_fmt, c.lm_group, c.head_dim, c.n_head, c.n_kv_head, c.d_model,
                               c.kv_type, c.kv_group) &&
                c.ffn % 64 == 0;

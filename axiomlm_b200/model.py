@@ -46,11 +46,15 @@ class QuantizedDecoder:
 
     def __init__(self, cfg: dict, packed: dict, *, kv_dtype: str = "fp16", kv_group: int = 64, max_batch: int = 1,
                  max_seq: int = 1024, max_tokens: int = 64, ring_buffer: bool = False, rope_len: int | None = None,
-                 device: str | torch.device = "cuda", use_graph: bool = True):
+                 device: str | torch.device = "cuda", use_graph: bool = True, tp=None):
+        # tensor parallel (``tp``: an axiomlm_b200.tp.TensorParallel): ``cfg`` is
+        # the whole model's; ``packed`` holds this rank's shards
+        self.tp = tp
+        world = tp.world if tp is not None else 1
         self.cfg = dict(cfg)
         self.device = torch.device(device)
-        d, H, Hkv = cfg["d_model"], cfg["n_head"], cfg["n_kv_head"]
-        self.head_dim = d // H
+        d, H, Hkv = cfg["d_model"], cfg["n_head"] // world, cfg["n_kv_head"] // world
+        self.head_dim = d // cfg["n_head"]
         self.max_tokens = max_tokens
         self.use_graph = use_graph
         self.packed = packed
@@ -62,8 +66,10 @@ class QuantizedDecoder:
         lay = packed["layers"]
         wq = lay[0]["qkv"]
         lm = packed["lm_head"]
+        self.vocab_local = cfg["vocab"] // world
         c = L.ModelCfg(n_layer=cfg["n_layer"], d_model=d, n_head=H, n_kv_head=Hkv, head_dim=self.head_dim,
-                       ffn=cfg["ffn"], vocab=cfg["vocab"], eps=float(cfg["eps"]), wfmt=wq.fmt, group=wq.group,
+                       ffn=cfg["ffn"] // world, vocab=self.vocab_local, eps=float(cfg["eps"]), wfmt=wq.fmt,
+                       group=wq.group, tp_world=world, tp_rank=tp.rank if tp is not None else 0,
                        lm_fmt=lm.fmt, lm_group=lm.group, kv_type=L.KV_TYPES[self.cache.cache_dtype],
                        kv_group=self.cache.kv_group, max_batch=max_batch, max_seq=max_seq, max_tokens=max_tokens,
                        rope_len=self.rope_len, has_qkv_bias=int(lay[0].get("qkv_b") is not None))
@@ -85,6 +91,7 @@ class QuantizedDecoder:
             k_cache=_vp_array(kc), v_cache=_vp_array(vc), k_scale=_vp_array(ks), v_scale=_vp_array(vs))
         p = L.ModelPtrs(emb_w=packed["emb_w"].data_ptr(), emb_s=packed["emb_s"].data_ptr(), lm_w=lm.words.data_ptr(),
                         lm_s=lm.scales.data_ptr(), ln_f=packed["ln_f"].data_ptr(), rope=self.rope.data_ptr(),
+                        tp_comm=tp.comm if tp is not None else None,
                         **{k: C.cast(v, C.POINTER(C.c_void_p)) for k, v in self._arrays.items()})
         h = C.c_void_p()
         L.call("axb_runner_create", C.byref(c), C.byref(p), C.c_void_p(self.workspace.data_ptr()), nbytes, C.byref(h))
@@ -97,7 +104,7 @@ class QuantizedDecoder:
 
         rows = max_batch * max_tokens
         self.tokens = view(0, torch.int32, (rows,))
-        self.logits_buf = view(1, torch.float16, (rows, cfg["vocab"]))
+        self.logits_buf = view(1, torch.float16, (rows, self.vocab_local))  # this rank's vocab rows under tp
         self.argmax_buf = view(2, torch.int32, (rows,))
         self.norm_buf = view(3, torch.float32, (rows, d))
         self.error_buf = view(4, torch.int32, (1,))
@@ -106,6 +113,16 @@ class QuantizedDecoder:
     # ------------------------------------------------------------ builders
     @classmethod
     def from_weights(cls, cfg: dict, weights: dict, weight_format: str = "q4_rtn", **kw) -> "QuantizedDecoder":
+        tp = kw.get("tp")
+        if tp is not None and tp.world > 1:
+            from .tp import local_dims, shard_weights
+
+            local_dims(cfg, tp.world)  # divisibility checks
+            weights = shard_weights(cfg, weights, tp.rank, tp.world)
+        return cls._from_weights(cfg, weights, weight_format, **kw)
+
+    @classmethod
+    def _from_weights(cls, cfg: dict, weights: dict, weight_format: str = "q4_rtn", **kw) -> "QuantizedDecoder":
         """Pack fp32 master weights (``tests/golden/model_weights.make_weights``
         layout) on the GPU, following ``_ensure_quant_weights`` in q4_rtn
         mode (transformer.py:822-1008): projections and an untied lm_head in

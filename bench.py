@@ -151,11 +151,16 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ our arm
 
-def build_decoder(cfg, batch, ctx, kv, seed=0):
+def build_decoder(cfg, batch, ctx, kv, seed=0, tp=None):
+    """Random N(0, 0.02) weights packed on the GPU.  With ``tp`` (tensor
+    parallel) this rank packs only its shard: H / N query heads, Hkv / N KV
+    heads, F / N FFN rows, V / N vocab rows; the embedding and the norms,
+    replicated, come from the same seed on every rank."""
     from axiomlm_b200 import ops
     from axiomlm_b200.model import QuantizedDecoder
 
-    g = torch.Generator(device="cuda").manual_seed(seed)
+    world = tp.world if tp is not None else 1
+    g = torch.Generator(device="cuda").manual_seed(seed + (tp.rank if tp is not None else 0))
     dev = torch.device("cuda")
 
     def rn(*shape):
@@ -163,6 +168,7 @@ def build_decoder(cfg, batch, ctx, kv, seed=0):
 
     d, H, Hkv, F, V = cfg["d_model"], cfg["n_head"], cfg["n_kv_head"], cfg["ffn"], cfg["vocab"]
     hd = d // H
+    H, Hkv, F, V_l = H // world, Hkv // world, F // world, V // world
     layers = []
     for _ in range(cfg["n_layer"]):
         layers.append(dict(
@@ -170,15 +176,16 @@ def build_decoder(cfg, batch, ctx, kv, seed=0):
             gu=ops.pack_q4t(rn(2 * F, d), 128, True, gate_up=True), down=ops.pack_q4t(rn(d, F), 128, True),
             ln_1=torch.ones(d, device=dev), ln_2=torch.ones(d, device=dev), qkv_b=None))
         torch.cuda.synchronize()
-    wte = rn(V, d)
+    gr = torch.Generator(device="cuda").manual_seed(seed + 7919)  # replicated tensors: same on every rank
+    wte = torch.randn(V, d, generator=gr, device=dev, dtype=torch.float32) * 0.02
     emb_w, emb_s = ops.pack_q8_g64(wte)
     del wte
-    lm = ops.pack_q4t(rn(V, d), 128, True)
+    lm = ops.pack_q4t(rn(V_l, d), 128, True)
     packed = dict(layers=layers, emb_w=emb_w, emb_s=emb_s, lm_head=lm, ln_f=torch.ones(d, device=dev))
     torch.cuda.synchronize()
     kv_dtype, kv_group = kv
     dec = QuantizedDecoder(cfg, packed, kv_dtype=kv_dtype, kv_group=kv_group, max_batch=batch,
-                           max_seq=ctx + 1024, max_tokens=1, rope_len=cfg["block_size"])
+                           max_seq=ctx + 1024, max_tokens=1, rope_len=cfg["block_size"], tp=tp)
     return dec
 
 
@@ -213,15 +220,19 @@ def gemv_roofline(dec, batch, reps=3):
     from axiomlm_b200 import _lib as L
     from axiomlm_b200 import ops
 
-    d, F = dec.cfg["d_model"], dec.cfg["ffn"]
     st = torch.cuda.current_stream()
-    x_d = torch.randn(batch, d, device="cuda").half()
-    x_f = torch.randn(batch, F, device="cuda").half()
+    xs = {}
+
+    def act(K):  # activations of the launch's width (tensor parallel: o and down take a shard)
+        if K not in xs:
+            xs[K] = torch.randn(batch, K, device="cuda").half()
+        return xs[K]
+
     launches = []
     for lay in dec.packed["layers"]:
-        launches += [(lay["qkv"], x_d, L.EPI_STORE), (lay["o"], x_d, L.EPI_STORE),
-                     (lay["gu"], x_d, L.EPI_SWIGLU), (lay["down"], x_f, L.EPI_STORE)]
-    launches.append((dec.packed["lm_head"], x_d, L.EPI_STORE))
+        launches += [(lay["qkv"], act(lay["qkv"].K), L.EPI_STORE), (lay["o"], act(lay["o"].K), L.EPI_STORE),
+                     (lay["gu"], act(lay["gu"].K), L.EPI_SWIGLU), (lay["down"], act(lay["down"].K), L.EPI_STORE)]
+    launches.append((dec.packed["lm_head"], act(dec.packed["lm_head"].K), L.EPI_STORE))
     tot_bytes = sum(W.nbytes + batch * W.K * 2 + batch * W.N * 2 for W, _, _ in launches)
     outs = [torch.empty(batch, W.N // 2 if e == L.EPI_SWIGLU else W.N, dtype=torch.float16, device="cuda")
             for W, _, e in launches]
@@ -286,8 +297,15 @@ def run_ours(args, rank, world):
         cfg["n_layer"] = args.layers
     kv = {"fp8_head": ("fp8", 128), "fp8_g64": ("fp8", 64), "fp16": ("fp16", 64), "int4_g32": ("int4", 32)}[args.kv]
     B = args.batch
-    dec = build_decoder(cfg, B, args.ctx, kv, seed=1000 + rank)
-    fill_context(dec, B, args.ctx, seed=2000 + rank)
+    tp = None
+    if args.tp > 1:  # every rank works on the same sequences: ids and positions must agree
+        from axiomlm_b200.tp import TensorParallel
+
+        if args.tp != world:
+            raise SystemExit(f"--tp {args.tp} needs {args.tp} ranks under torchrun (got {world})")
+        tp = TensorParallel.from_process_group()
+    dec = build_decoder(cfg, B, args.ctx, kv, seed=1000 + (0 if tp else rank), tp=tp)
+    fill_context(dec, B, args.ctx, seed=2000 + (0 if tp else rank))
     st = torch.cuda.current_stream()
     tok = dec.argmax(B).view(B, 1).long()
     for _ in range(args.warmup):
@@ -308,7 +326,8 @@ def run_ours(args, rank, world):
         torch.cuda.synchronize()
         barrier(world)
     t = max_over_ranks(ev0.elapsed_time(ev1) / 1e3, world)
-    value = world * B * args.steps / t
+    seqs = B if tp else world * B  # tensor parallel: the ranks share the same B sequences
+    value = seqs * args.steps / t
     sbytes = step_bytes(dec, B)
     # ---- end to end through the public API, host buffers
     host_in = torch.zeros((B, 1), dtype=torch.int64).pin_memory()
@@ -330,7 +349,7 @@ def run_ours(args, rank, world):
     e1.synchronize()
     barrier(world)
     te = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
-    e2e = {"value": world * B * args.steps / te, "unit": "tokens/s", "h2d_bytes_per_step": B * 8,
+    e2e = {"value": seqs * args.steps / te, "unit": "tokens/s", "h2d_bytes_per_step": B * 8,
            "d2h_bytes_per_step": B * 4}
     # ---- roofline of the dominant kernel: the persistent step kernel (one
     # launch per step), or the Q4 GEMV when the per-kernel graph runs the step
@@ -350,11 +369,14 @@ def run_ours(args, rank, world):
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "w4a16 (fp32 accumulate)",
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "dtype": "w4a16 (fp32 accumulate)",
             "data": "synthetic (seeded N(0,0.02) weights, uniform-random token ids)",
             "config": {"workload": f"Llama-3-8B-shape decode ({cfg['n_layer']} layers), Q4 G128 sym, "
-                                   f"KV {args.kv}, ctx {args.ctx}, batch {B}/GPU",
-                       "global_batch": B * world, "seq_len": args.ctx, "parallelism": f"replicas x{world}",
+                                   f"KV {args.kv}, ctx {args.ctx}, batch {B}" + (f" tensor-parallel x{world}" if tp
+                                                                                 else "/GPU"),
+                       "global_batch": seqs, "seq_len": args.ctx,
+                       "parallelism": f"tp{world}" if tp else f"replicas x{world}",
                        "l2": "inputs larger than L2 (weights %.2f GB per step)" % (dec.weight_bytes / 1e9)},
             "achieved_hbm_gbs": round(sbytes * B * args.steps / B / t / 1e9 / 1, 1) if world == 1 else None,
             "step_bytes": int(sbytes),
@@ -369,6 +391,8 @@ def run_ours(args, rank, world):
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline(cfg, B, args.ctx, kv, reps=1)
     dec.close()
+    if tp is not None:
+        tp.close()
     return out
 
 
@@ -471,6 +495,7 @@ def main():
     ap.add_argument("--kv", default="fp8_head", choices=["fp8_head", "fp8_g64", "fp16", "int4_g32"])
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (debug only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (all ranks share one batch)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 200 if args.impl == "ours" else 5

@@ -61,6 +61,7 @@ extern "C" {
 #define AXB_EPI_RESIDUAL 1 /* y = fp16(y + fp16(acc)) in place (x = x + proj(..)) */
 #define AXB_EPI_SWIGLU 2   /* rows interleaved gate/up by 8: y[j] = fp16(silu(g) * u) */
 #define AXB_EPI_F32 3      /* y (fp32) = fp16-rounded acc, stored as fp32 */
+#define AXB_EPI_F32_ACC 4  /* y (fp32) = acc (+ bias), unrounded: a row-parallel partial sum */
 
 const char* axb_last_error(void);
 int axb_version(void);
@@ -289,6 +290,10 @@ typedef struct {
   int max_batch, max_seq, max_tokens; /* max_tokens = tokens per sequence per step (<= 64) */
   int rope_len;
   int has_qkv_bias;
+  /* tensor parallelism (0 or 1: off).  With tp_world > 1, n_head, n_kv_head,
+   * ffn and vocab are this rank's shard (heads tp_rank * n_head .., FFN rows
+   * tp_rank * ffn .., vocab rows tp_rank * vocab ..); d_model is replicated. */
+  int tp_world, tp_rank;
 } axb_model_cfg;
 
 typedef struct {
@@ -313,6 +318,7 @@ typedef struct {
   void* const* v_cache;
   void* const* k_scale; /* per layer fp16 or NULL */
   void* const* v_scale;
+  void* tp_comm; /* from axb_tp_comm_create when tp_world > 1, else NULL */
 } axb_model_ptrs;
 
 size_t axb_runner_workspace_bytes(const axb_model_cfg* cfg);
@@ -337,6 +343,22 @@ int axb_runner_step(void* handle, int B, int T, int rope_pos, int write_pos, int
  * kernel launch, 0 when they run as the per-kernel CUDA graph (unsupported
  * format, or AXB_STEP=0 in the environment at creation). */
 int axb_runner_uses_step_kernel(void* handle);
+
+/* ---- tensor parallelism over NVLink (no counterpart in the reference, whose
+ *      only collective is a training all_reduce, train.py:296) ------------- */
+#define AXB_TP_SUM_F32 0
+#define AXB_TP_SUM_F16 1
+#define AXB_TP_MAX_U64 2
+/* NCCL unique id (128 bytes) made on one rank and shared with the others by
+ * the host (torch.distributed, a store, ...). */
+int axb_tp_unique_id(void* id_out);
+/* Communicator of `world` ranks on the current device; one per rank. */
+int axb_tp_comm_create(const void* id, int world, int rank, void** comm_out);
+int axb_tp_comm_destroy(void* comm);
+/* Abandon a communicator whose peers may be gone (pending collectives end). */
+int axb_tp_comm_abort(void* comm);
+/* In-place allreduce of `count` elements on `stream` (AXB_TP_*). */
+int axb_tp_allreduce(void* comm, void* buf_dev, size_t count, int op, void* stream);
 
 #ifdef __cplusplus
 }
