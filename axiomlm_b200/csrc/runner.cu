@@ -526,7 +526,7 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   const int cap_tok = step_attn_cap(c.kv_type, c.head_dim, c.kv_group);
   r->step_ok = !(sv && atoi(sv) == 0) && c.tp_world <= 1 &&
                step_supported(c.wfmt, c.group, c.lm_fmt, c.lm_group, c.head_dim, c.n_head, c.n_kv_head, c.d_model,
-                              c.kv_type, c.kv_group) &&
+                              c.kv_type, c.kv_group, c.max_seq) &&
                c.ffn % 64 == 0;
   if (r->step_ok) {
     if (int rc = step_prepare()) {

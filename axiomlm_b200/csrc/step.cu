@@ -721,9 +721,13 @@ __device__ __noinline__ void stage_x(int B, int G, float eps, const __half* src,
 
 // ------------------------------------------------------------------ attention
 struct AttnLayout {
-  int rb, ng, kv, q, p, ks, vs, ml, coef, bytes;
+  int rb, ng, kv, ksc, vsc, qh, p, ml, coef, bytes;
 };
 
+// Working set of one attention group: staged K and V rows, their fp16 scales
+// (bulk-copied with the rows), q as fp16 hi / lo parts (8 rows, the ones past
+// n_rep zero), the probabilities, the online-softmax state and the split
+// combine weights.
 __host__ __device__ inline AttnLayout attn_layout(int kv_type, int hd, int kv_group, int cap) {
   AttnLayout L;
   L.rb = kv_row_bytes(kv_type, hd);
@@ -732,18 +736,19 @@ __host__ __device__ inline AttnLayout attn_layout(int kv_type, int hd, int kv_gr
   L.kv = off;
   off += 2 * cap * L.rb;
   off = (off + 15) / 16 * 16;
-  L.q = off;
-  off += 8 * hd * 4;
+  const int sb = (cap * L.ng * 2 + 15) / 16 * 16;
+  L.ksc = off;
+  off += sb;
+  L.vsc = off;
+  off += sb;
+  L.qh = off;
+  off += 2 * 8 * hd * 2;
   L.p = off;
-  off += 8 * cap * 4;
-  L.ks = off;
-  off += cap * L.ng * 4;
-  L.vs = off;
-  off += cap * L.ng * 4;
+  off += kMaxRepS * cap * 4;
   L.ml = off;
   off += 32 * 4;  // m[8], l[8], alpha[8], flags
   L.coef = off;
-  off += 8 * kStepMaxSplits * 4;
+  off += kMaxRepS * kStepMaxSplits * 4;
   L.bytes = (off + 127) / 128 * 128;
   return L;
 }
@@ -759,13 +764,20 @@ __device__ __forceinline__ void attn_split_plan(int active, int units, int cap, 
   (void)cap;
 }
 
-// Issue the bulk copy of cached K/V rows [c0, c0 + nt) of one head (group thread 0).
-__device__ __forceinline__ void attn_copy(const StepLayer* ly, size_t head_base, int rb, int c0, int nt, char* gsm,
-                                          const AttnLayout& Lo, int cap, uint64_t* bar) {
+// Issue the bulk copy of cached K/V rows [c0, c0 + nt) of one head and, for
+// quantized caches, their scales (rounded up to 8 tokens: 16-byte copies;
+// the cache length is a multiple of 8) (group thread 0).
+__device__ __forceinline__ void attn_copy(const StepLayer* ly, size_t head_base, int rb, int ng, bool quant, int c0,
+                                          int nt, char* gsm, const AttnLayout& Lo, int cap, uint64_t* bar) {
+  const int nt8 = (nt + 7) & ~7;
   fence_proxy_async();
-  mbar_expect_tx(bar, 2u * nt * rb);
+  mbar_expect_tx(bar, 2u * nt * rb + (quant ? 2u * nt8 * ng * 2 : 0u));
   bulk_g2s(gsm + Lo.kv, ly->kc + (head_base + c0) * rb, nt * rb, bar);
   bulk_g2s(gsm + Lo.kv + (size_t)cap * rb, ly->vc + (head_base + c0) * rb, nt * rb, bar);
+  if (quant) {
+    bulk_g2s(gsm + Lo.ksc, ly->ks + (head_base + c0) * ng, nt8 * ng * 2, bar);
+    bulk_g2s(gsm + Lo.vsc, ly->vs + (head_base + c0) * ng, nt8 * ng * 2, bar);
+  }
 }
 
 struct AttnItem {
@@ -783,43 +795,89 @@ __device__ __forceinline__ AttnItem attn_item_of(int item, int nsplit, int chunk
   return it;
 }
 
-// One attention item (sequence b, kv head, split) on a group of 4 warps.
+// fp16 pair (elements e, e + 1) of a staged K/V row: an MMA fragment register
+// holding the cache's exact values (fp16, e4m3 codes, or int4 codes)
+__device__ __forceinline__ uint32_t kv_pair_h2(const uint8_t* row, int type, int e) {
+  if (type == AXB_KV_F16) return *reinterpret_cast<const uint32_t*>(row + e * 2);
+  if (type == AXB_KV_FP8) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(*reinterpret_cast<const uint16_t*>(row + e), __NV_E4M3);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
+  }
+  const uint32_t cb = row[e >> 1];  // low nibble = element e, high = e + 1; value (n ^ 8) - 8
+  const uint32_t t = (((cb & 0xFu) | ((cb & 0xF0u) << 12)) ^ 0x00080008u) | 0x64006400u;
+  return h2_as_u32(__hsub2(u32_as_h2(t), __float2half2_rn(1032.f)));
+}
+// element e of two staged rows as an fp16 pair (row0, row1); an absent row is 0
+__device__ __forceinline__ uint32_t kv_col_pair_h2(const uint8_t* r0, const uint8_t* r1, int type, int e) {
+  if (type == AXB_KV_F16) {
+    const uint32_t lo = r0 ? reinterpret_cast<const uint16_t*>(r0)[e] : 0u;
+    const uint32_t hi = r1 ? reinterpret_cast<const uint16_t*>(r1)[e] : 0u;
+    return lo | (hi << 16);
+  }
+  if (type == AXB_KV_FP8) {
+    const uint16_t two = (uint16_t)((r0 ? r0[e] : 0u) | ((r1 ? r1[e] : 0u) << 8));
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(two, __NV_E4M3);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
+  }
+  const uint32_t sh = (e & 1) * 4;
+  const uint32_t n0 = r0 ? ((r0[e >> 1] >> sh) & 0xFu) ^ 8u : 8u;  // 8 encodes 0 after the offset
+  const uint32_t n1 = r1 ? ((r1[e >> 1] >> sh) & 0xFu) ^ 8u : 8u;
+  return h2_as_u32(__hsub2(u32_as_h2((n0 | (n1 << 16)) | 0x64006400u), __float2half2_rn(1032.f)));
+}
+// fp32 pair -> fp16 (hi, lo) pairs with hi + lo = the value to about 22 bits
+__device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 hf = __half22float2(h);
+  hi = h2_as_u32(h);
+  lo = h2_as_u32(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
+}
+
+// One attention item (sequence b, kv head, split) on a group of 4 warps, on
+// the tensor cores: S = q K^T with q as fp16 hi + lo (K codes are exact in
+// fp16; the per-token scales apply to the fp32 result), then O += P V with the
+// per-token V scale folded into P (normalized by the chunk's largest scale)
+// and P as hi + lo.  Warp w owns output dims [w HD / 4, (w + 1) HD / 4).
 // gt = thread index in the group, gwarp = warp index in the group.
 template <int HD>
-__device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, int layer, const AttnItem& it, int nsplit, bool prefetched,
-                          char* gsm, uint64_t* bar, uint32_t& uses, int bar_id, int gt, int* done_ctr, bool ok) {
-  constexpr int DPL = HD / 32, EPT = HD / 16;
-  const int lane = gt & 31, gwarp = gt >> 5;
+__device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, int layer, const AttnItem& it,
+                                      int nsplit, bool prefetched, char* gsm, uint64_t* bar, uint32_t& uses, int bar_id,
+                                      int gt, int* done_ctr, bool ok) {
+  constexpr int DPL = HD / 32, KS = HD / 16, NB = HD / 32;  // NB: n8 output blocks per warp
+  const int lane = gt & 31, gwarp = gt >> 5, g = lane >> 2, c = lane & 3;
   const int cap = a.attn_cap;
   const AttnLayout Lo = attn_layout(a.kv_type, HD, a.kv_group, cap);
-  const int rb = Lo.rb, ng = Lo.ng, G = a.kv_group;
+  const int rb = Lo.rb, ng = Lo.ng, G = a.kv_type == AXB_KV_F16 ? HD : a.kv_group;
   const bool quant = a.kv_type != AXB_KV_F16;
   const int n_rep = a.Hq / a.Hkv, hq0 = it.kvh * n_rep;
   const int rpos = a.params[0], wpos = a.params[1];
   const size_t head_base = ((size_t)it.b * a.Hkv + it.kvh) * a.S;
   char* kst = gsm + Lo.kv;
   char* vst = kst + (size_t)cap * rb;
-  float* q_s = reinterpret_cast<float*>(gsm + Lo.q);
+  __half* ksc_s = reinterpret_cast<__half*>(gsm + Lo.ksc);
+  __half* vsc_s = reinterpret_cast<__half*>(gsm + Lo.vsc);
+  __half* qh_s = reinterpret_cast<__half*>(gsm + Lo.qh);  // [hi / lo][8 rows][HD]
   float* p_s = reinterpret_cast<float*>(gsm + Lo.p);
-  float* ks_s = reinterpret_cast<float*>(gsm + Lo.ks);
-  float* vs_s = reinterpret_cast<float*>(gsm + Lo.vs);
   float* ml_s = reinterpret_cast<float*>(gsm + Lo.ml);  // m[8] l[8] alpha[8] flag
   float* coef = reinterpret_cast<float*>(gsm + Lo.coef);
-  float* o_red = reinterpret_cast<float*>(kst);
-  const __half* ksc = quant ? ly->ks + head_base * ng : nullptr;
-  const __half* vsc = quant ? ly->vs + head_base * ng : nullptr;
 
-  // ---- q with RoPE (fp32), the new K/V row rotated, quantized and written
+  // ---- q with RoPE (fp32), as fp16 hi / lo rows; the new K/V row rotated, quantized and written
   const int qkv_dim = (a.Hq + 2 * a.Hkv) * HD;
   const __half* row = a.qkv + (size_t)it.b * qkv_dim;
   const float* fr = a.rope + (size_t)(rpos % a.rope_len) * HD;
-  for (int i = gt; i < n_rep * HD / 2; i += 128) {
+  for (int i = gt; i < 8 * HD / 2; i += 128) {
     const int rr = i / (HD / 2), pr = i % (HD / 2);
-    const __half2 x2 = __ldcg(reinterpret_cast<const __half2*>(row + (hq0 + rr) * HD) + pr);
-    const float a0 = __low2float(x2), a1 = __high2float(x2);
-    const float c = fr[2 * pr], sn = fr[2 * pr + 1];
-    q_s[rr * HD + 2 * pr] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, sn));
-    q_s[rr * HD + 2 * pr + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, c));
+    float q0 = 0.f, q1 = 0.f;
+    if (rr < n_rep) {
+      const __half2 x2 = __ldcg(reinterpret_cast<const __half2*>(row + (hq0 + rr) * HD) + pr);
+      const float a0 = __low2float(x2), a1 = __high2float(x2);
+      const float cs = fr[2 * pr], sn = fr[2 * pr + 1];
+      q0 = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
+      q1 = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
+    }
+    uint32_t hi, lo;
+    split_h2(q0, q1, hi, lo);
+    reinterpret_cast<uint32_t*>(qh_s)[(rr * HD) / 2 + pr] = hi;
+    reinterpret_cast<uint32_t*>(qh_s)[(8 * HD + rr * HD) / 2 + pr] = lo;
   }
   if (gt < 8) {
     ml_s[gt] = -INFINITY;
@@ -835,9 +893,9 @@ __device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, in
 #pragma unroll
       for (int e = 0; e < DPL; e += 2) {
         const int pr = (lane * DPL + e) >> 1;
-        const float c = fr[2 * pr], sn = fr[2 * pr + 1], a0 = nkv[e], a1 = nkv[e + 1];
-        nkv[e] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, sn));
-        nkv[e + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, c));
+        const float cs = fr[2 * pr], sn = fr[2 * pr + 1], a0 = nkv[e], a1 = nkv[e + 1];
+        nkv[e] = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
+        nkv[e + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
       }
     }
     uint8_t* crow = (gwarp == 0 ? ly->kc : ly->vc) + (head_base + wpos) * rb;
@@ -846,22 +904,19 @@ __device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, in
   }
   group_bar(bar_id);
 
-  float acc[kMaxRepS][DPL];
-#pragma unroll
-  for (int r = 0; r < kMaxRepS; ++r)
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) acc[r][e] = 0.f;
   const float sm_scale = 1.0f / sqrtf((float)HD);
+  const int d0 = gwarp * (HD / 4);  // this warp's output dims (one V scale group: kv_group >= HD / 4)
+  const int vgrp = quant ? d0 / G : 0;
+  float oacc[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) oacc[nb][q] = 0.f;
   bool first = true;
   for (int c0 = it.t0; c0 < it.t1 && ok; c0 += cap) {
     const int nt = min(cap, it.t1 - c0);
-    if (!(first && prefetched) && gt == 0) attn_copy(ly, head_base, rb, c0, nt, gsm, Lo, cap, bar);
+    if (!(first && prefetched) && gt == 0) attn_copy(ly, head_base, rb, ng, quant, c0, nt, gsm, Lo, cap, bar);
     first = false;
-    if (quant)
-      for (int j = gt; j < nt * ng; j += 128) {
-        ks_s[j] = __half2float(ksc[(size_t)c0 * ng + j]);
-        vs_s[j] = __half2float(vsc[(size_t)c0 * ng + j]);
-      }
     const bool got = mbar_wait(bar, uses & 1, kSMbarLimit);
     ++uses;
     if (group_bar_or(bar_id, !got)) {  // one decision for the whole group
@@ -870,40 +925,45 @@ __device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, in
       break;
     }
     if (covers && gwarp < 2 && wpos >= c0 && wpos < c0 + nt) {
-      // the copy may have read the slot before this step wrote it
+      // the copy may have read the slot (codes and scale) before this step wrote it
       uint8_t* rowp = reinterpret_cast<uint8_t*>(gwarp == 0 ? kst : vst) + (size_t)(wpos - c0) * rb;
-      store_kv_row<DPL>(nkv, lane, a.kv_type, G, true, rowp, nullptr);
+      __half* sp = quant ? (gwarp == 0 ? ksc_s : vsc_s) + (size_t)(wpos - c0) * ng : nullptr;
+      store_kv_row<DPL>(nkv, lane, a.kv_type, G, true, rowp, sp);
     }
     group_bar(bar_id);
-    // scores: EPT threads per token, 16 elements each
-    for (int base = 0; base < nt; base += 128 / EPT) {
-      const int tk = base + gt / EPT, ch = gt % EPT;
-      float part[kMaxRepS];
+    // ---- scores: warp w takes 8-token blocks w, w + 4, ...; the fp32 result
+    // of each scale group is scaled by the token's K scale when the group ends
+    const uint32_t* qh32 = reinterpret_cast<const uint32_t*>(qh_s);
+    for (int blk = gwarp; blk * 8 < nt; blk += 4) {
+      const int tok = min(blk * 8 + g, nt - 1);  // B-fragment column; columns past nt are discarded
+      const uint8_t* krow = reinterpret_cast<const uint8_t*>(kst) + (size_t)tok * rb;
+      const int t_a = blk * 8 + 2 * c, t_b = t_a + 1;  // this thread's C-fragment columns
+      float sc0 = 0.f, sc1 = 0.f, gacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int r = 0; r < kMaxRepS; ++r) part[r] = 0.f;
-      if (tk < nt) {
-        float kv[16];
-        kv_load16(reinterpret_cast<const uint8_t*>(kst) + (size_t)tk * rb, a.kv_type, ch * 16, kv);
-        const float s = quant ? ks_s[tk * ng + (ch * 16) / G] : 1.f;
-#pragma unroll
-        for (int r = 0; r < kMaxRepS; ++r) {
-          if (r < n_rep) {
-            float d = 0.f;
-#pragma unroll
-            for (int e = 0; e < 16; ++e) d = __fmaf_rn(q_s[r * HD + ch * 16 + e], kv[e], d);
-            part[r] = d * s;
-          }
+      for (int s = 0; s < KS; ++s) {
+        const uint32_t b0 = kv_pair_h2(krow, a.kv_type, 16 * s + 2 * c);
+        const uint32_t b1 = kv_pair_h2(krow, a.kv_type, 16 * s + 2 * c + 8);
+        const uint32_t ahi[4] = {qh32[(g * HD + 16 * s + 2 * c) / 2], 0u, qh32[(g * HD + 16 * s + 2 * c + 8) / 2], 0u};
+        const uint32_t alo[4] = {qh32[(8 * HD + g * HD + 16 * s + 2 * c) / 2], 0u,
+                                 qh32[(8 * HD + g * HD + 16 * s + 2 * c + 8) / 2], 0u};
+        mma_16816(gacc, ahi, b0, b1, gacc);
+        mma_16816(gacc, alo, b0, b1, gacc);
+        if ((16 * (s + 1)) % G == 0) {  // a K scale group is complete
+          const int grp = (16 * s) / G;
+          const float s0 = quant && t_a < nt ? __half2float(ksc_s[t_a * ng + grp]) : 1.f;
+          const float s1 = quant && t_b < nt ? __half2float(ksc_s[t_b * ng + grp]) : 1.f;
+          sc0 = __fmaf_rn(gacc[0], s0, sc0);
+          sc1 = __fmaf_rn(gacc[1], s1, sc1);
+          gacc[0] = gacc[1] = gacc[2] = gacc[3] = 0.f;
         }
       }
-#pragma unroll
-      for (int r = 0; r < kMaxRepS; ++r) {
-        float v = part[r];
-        for (int o = 1; o < EPT; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (ch == 0 && tk < nt && r < n_rep) p_s[r * cap + tk] = v * sm_scale;
+      if (g < n_rep) {
+        if (t_a < nt) p_s[g * cap + t_a] = sc0 * sm_scale;
+        if (t_b < nt) p_s[g * cap + t_b] = sc1 * sm_scale;
       }
     }
     group_bar(bar_id);
-    // online softmax over the sub-chunk: warp w handles heads w, w + 4
+    // ---- online softmax over the chunk: warp w handles heads w, w + 4
     for (int r = gwarp; r < n_rep; r += 4) {
       float mx = -INFINITY;
       for (int tk = lane; tk < nt; tk += 32) mx = fmaxf(mx, p_s[r * cap + tk]);
@@ -926,49 +986,74 @@ __device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, in
       }
     }
     group_bar(bar_id);
-    // PV: warp w takes tokens w, w + 4, ...; lane covers DPL consecutive dims
-#pragma unroll
-    for (int r = 0; r < kMaxRepS; ++r) {
-      if (r < n_rep) {
-        const float al = ml_s[16 + r];
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) acc[r][e] *= al;
-      }
+    // ---- O = alpha O + vmax * (P' V), P' = p * vscale / vmax (vmax: the
+    // chunk's largest V scale of this warp's group, keeps P' in fp16 range)
+    float vmax = 1.f;
+    if (quant) {
+      float m = 0.f;
+      for (int tk = lane; tk < nt; tk += 32) m = fmaxf(m, __half2float(vsc_s[tk * ng + vgrp]));
+      m = warp_max(m);
+      vmax = m > 0.f ? m : 1.f;
     }
-    for (int tk = gwarp; tk < nt; tk += 4) {
-      const uint8_t* vrow = reinterpret_cast<const uint8_t*>(vst) + (size_t)tk * rb;
-      float vv[DPL];
+    const float inv_vmax = 1.f / vmax;
+    const float alpha = g < n_rep ? ml_s[16 + g] : 0.f;
+    float tacc[NB][4];
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) vv[e] = kv_elem(vrow, a.kv_type, lane * DPL + e);
-      const float s = quant ? vs_s[tk * ng + (lane * DPL) / G] : 1.f;
+    for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-      for (int r = 0; r < kMaxRepS; ++r) {
-        if (r < n_rep) {
-          const float pw = p_s[r * cap + tk] * s;
+      for (int q = 0; q < 4; ++q) tacc[nb][q] = 0.f;
+    for (int t0 = 0; t0 < nt; t0 += 16) {
+      float pv[4];
 #pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[r][e] = __fmaf_rn(pw, vv[e], acc[r][e]);
+      for (int q = 0; q < 4; ++q) {
+        const int t = t0 + 2 * c + (q & 1) + 8 * (q >> 1);
+        float v = 0.f;
+        if (g < n_rep && t < nt) {
+          v = p_s[g * cap + t];
+          if (quant) v *= __half2float(vsc_s[t * ng + vgrp]) * inv_vmax;
         }
+        pv[q] = v;
+      }
+      uint32_t h01, l01, h23, l23;
+      split_h2(pv[0], pv[1], h01, l01);
+      split_h2(pv[2], pv[3], h23, l23);
+      const uint32_t ahi[4] = {h01, 0u, h23, 0u}, alo[4] = {l01, 0u, l23, 0u};
+      const int ta = t0 + 2 * c, tb = ta + 8;
+      const uint8_t* r0 = ta < nt ? reinterpret_cast<const uint8_t*>(vst) + (size_t)ta * rb : nullptr;
+      const uint8_t* r1 = ta + 1 < nt ? reinterpret_cast<const uint8_t*>(vst) + (size_t)(ta + 1) * rb : nullptr;
+      const uint8_t* r2 = tb < nt ? reinterpret_cast<const uint8_t*>(vst) + (size_t)tb * rb : nullptr;
+      const uint8_t* r3 = tb + 1 < nt ? reinterpret_cast<const uint8_t*>(vst) + (size_t)(tb + 1) * rb : nullptr;
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        const int d = d0 + nb * 8 + g;  // B-fragment column
+        const uint32_t b0 = kv_col_pair_h2(r0, r1, a.kv_type, d);
+        const uint32_t b1 = kv_col_pair_h2(r2, r3, a.kv_type, d);
+        mma_16816(tacc[nb], ahi, b0, b1, tacc[nb]);
+        mma_16816(tacc[nb], alo, b0, b1, tacc[nb]);
       }
     }
-    group_bar(bar_id);  // staged rows and p_s are free for the next sub-chunk
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      oacc[nb][0] = __fmaf_rn(vmax, tacc[nb][0], oacc[nb][0] * alpha);
+      oacc[nb][1] = __fmaf_rn(vmax, tacc[nb][1], oacc[nb][1] * alpha);
+    }
+    group_bar(bar_id);  // staged rows and p_s are free for the next chunk
   }
   if (!ok) return false;
-  // ---- reduce the 4 warps' accumulators (o_red reuses the staged rows)
-#pragma unroll
-  for (int r = 0; r < kMaxRepS; ++r)
-    if (r < n_rep)
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) o_red[(gwarp * kMaxRepS + r) * HD + lane * DPL + e] = acc[r][e];
-  group_bar(bar_id);
+  // ---- this thread's outputs: head g, dims d0 + 8 nb + 2c + {0, 1}
   const size_t pidx = (size_t)it.b * a.Hq + hq0;
-  for (int i = gt; i < n_rep * HD; i += 128) {
-    const int r = i / HD, e = i % HD;
-    const float o = o_red[(0 * kMaxRepS + r) * HD + e] + o_red[(1 * kMaxRepS + r) * HD + e] +
-                    o_red[(2 * kMaxRepS + r) * HD + e] + o_red[(3 * kMaxRepS + r) * HD + e];
-    if (nsplit == 1)
-      a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(o, ml_s[8 + r]));
-    else
-      a.part_o[((pidx + r) * kStepMaxSplits + it.split) * HD + e] = o;
+  if (g < n_rep) {
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const int d = d0 + nb * 8 + 2 * c;
+      if (nsplit == 1) {
+        a.attn[(pidx + g) * HD + d] = __float2half_rn(__fdiv_rn(oacc[nb][0], ml_s[8 + g]));
+        a.attn[(pidx + g) * HD + d + 1] = __float2half_rn(__fdiv_rn(oacc[nb][1], ml_s[8 + g]));
+      } else {
+        *reinterpret_cast<float2*>(a.part_o + ((pidx + g) * kStepMaxSplits + it.split) * HD + d) =
+            make_float2(oacc[nb][0], oacc[nb][1]);
+      }
+    }
   }
   if (nsplit == 1) {
     group_bar(bar_id);
@@ -1152,7 +1237,15 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     }
     // ---- the GEMV: activations staged in shared memory when they fit (always
     // for the normalized inputs), else read from L2 one k-block ahead
-    if (xs_fits(a.B, K, a.group)) {
+    const bool staged = xs_fits(a.B, K, a.group);
+    if (!staged && (nw != nullptr || src == nullptr)) {
+      // normalized inputs (and layer 0's embedding rows) exist only as staged
+      // rows; the host guarantees they fit (xs_fits for d_model), so this is a
+      // contract violation: report it rather than read an absent source
+      if (tid == 0) atomicExch(a.err, AXB_EINVAL);
+      ok = false;
+    }
+    if (staged) {
       if (ok) stage_x(a.B, a.group, a.eps, src, K, nw, xs, K + 8, xsum_of(K), SYM, red);
       ok = gemv_phase<SYM, GB, true>(a, ph, ring, pc, xs, K + 8, xsum_of(K), nullptr, 0, gw, Wt, lane, ok,
                                      done_ctr);
@@ -1176,7 +1269,8 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
       if (ok && item < n_items && gt == 0) {  // cached rows do not depend on this step's QKV
         const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
         const size_t hb = ((size_t)it.b * a.Hkv + it.kvh) * a.S;
-        attn_copy(ly, hb, Lo.rb, it.t0, min(a.attn_cap, it.t1 - it.t0), gsm, Lo, a.attn_cap, abar + grp);
+        attn_copy(ly, hb, Lo.rb, Lo.ng, a.kv_type != AXB_KV_F16, it.t0, min(a.attn_cap, it.t1 - it.t0), gsm, Lo,
+                  a.attn_cap, abar + grp);
       }
       const bool pre_ok = ok;
       ok = cta_wait(dn + 0, tiles_of(qkv_dim), a, ok);
@@ -1235,13 +1329,13 @@ int step_num_warps() { return kSW; }
 int step_attn_cap(int kv_type, int hd, int kv_group) {
   for (int cap = 256; cap >= 16; cap -= 16) {
     const AttnLayout L = attn_layout(kv_type, hd, kv_group, cap);
-    if (L.bytes <= kSUnion / kSGroups && 2 * cap * L.rb >= 4 * kMaxRepS * hd * 4) return cap;
+    if (L.bytes <= kSUnion / kSGroups) return cap;
   }
   return 0;
 }
 
 bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n_head, int n_kv_head, int d_model,
-                    int kv_type, int kv_group) {
+                    int kv_type, int kv_group, int max_seq) {
   if (wfmt != lm_fmt || group != lm_group) return false;
   if (wfmt != AXB_W_Q4T_SYM && wfmt != AXB_W_Q4T_AFFINE) return false;
   if (group != 64 && group != 128) return false;
@@ -1249,7 +1343,9 @@ bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n
   if (n_kv_head <= 0 || n_head % n_kv_head != 0 || n_head / n_kv_head > kMaxRepS) return false;
   if (d_model % 128 != 0) return false;
   if (!xs_fits(kStepMaxM, d_model, group)) return false;
-  if (kv_type != AXB_KV_F16 && (kv_group < 16 || hd % kv_group != 0)) return false;  // 16 elements share a scale in the score loads
+  // a K scale group spans whole 16-wide MMA steps, a V scale group a warp's output dims
+  if (kv_type != AXB_KV_F16 && (kv_group < 16 || kv_group < hd / 4 || hd % kv_group != 0)) return false;
+  if (max_seq % 8) return false;  // scales are bulk-copied in 8-token (16-byte) runs
   return step_attn_cap(kv_type, hd, kv_group) > 0;
 }
 

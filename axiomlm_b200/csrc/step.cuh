@@ -73,7 +73,7 @@ int step_prepare();
 // attention working set does not fit the kernel's shared memory.
 int step_attn_cap(int kv_type, int hd, int kv_group);
 bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n_head, int n_kv_head, int d_model,
-                    int kv_type, int kv_group);
+                    int kv_type, int kv_group, int max_seq);
 int step_num_warps();  // warps per CTA of the step kernel (partials are sized per warp)
 int step_launch(const StepArgs& a, cudaStream_t s);
 
