@@ -133,7 +133,7 @@ _SIGS = {
     "axb_q2t_meta2_bytes": (sz, [i32, i32, i32]),
     "axb_q2t_from_ref": (i32, [i32, vp, vp, vp, i32, i32, vp, vp, vp, vp]),
     "axb_q2t_dequant": (i32, [i32, vp, vp, vp, vp, i32, i32, vp, vp]),
-    "axb_lbgemv_workspace_bytes": (sz, [i32, i32, i32]),
+    "axb_lbgemv_workspace_bytes": (sz, [i32, i32, i32, i32]),
     "axb_lbgemv": (i32, [C.POINTER(LbGemvDesc), vp]),
     "axb_qgemm_tc_workspace_bytes": (sz, [i32, i32, i32]),
     "axb_qgemm_tc": (i32, [C.POINTER(QGemmDesc), vp]),

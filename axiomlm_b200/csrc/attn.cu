@@ -411,12 +411,17 @@ size_t decode_smem(int kv_type, int hd) {
 // grid (ceil(T / TQ), Hkv, B); 128 threads; rows = TQ tokens x n_rep heads <= 16.
 constexpr int kTreeRows = 16;
 constexpr int kTreeKeys = 32;
+// Split-K over the keys: with nsplit > 1, CTA (tile, split) covers keys
+// [split * chunk, ...) and writes its unnormalized (O, m, l) to po / pml
+// (tree_combine_kernel merges the splits in order); with nsplit == 1 it
+// writes the output directly.
 template <int HD>
-__global__ void __launch_bounds__(128) tree_attn_kernel(axb_attn_desc d) {
+__global__ void __launch_bounds__(128) tree_attn_kernel(axb_attn_desc d, int nsplit, int chunk, float* po, float* pml) {
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int n_rep = d.n_head / d.n_kv_head;
   const int TQ = max(1, kTreeRows / n_rep);
-  const int u0 = blockIdx.x * TQ;
+  const int split = blockIdx.x % nsplit;
+  const int u0 = (blockIdx.x / nsplit) * TQ;
   const int nu = min(TQ, d.T - u0);
   const int R = nu * n_rep;
   const int tid = threadIdx.x;
@@ -458,8 +463,9 @@ __global__ void __launch_bounds__(128) tree_attn_kernel(axb_attn_desc d) {
   for (int e = 0; e < DPT; ++e) acc[e] = 0.f;
   const int my_r = tid >> 3, my_d0 = (tid & 7) * DPT;
   __syncthreads();
-  const int n_keys = d.prefix_len + d.T;
-  for (int kt = 0; kt < n_keys; kt += kTreeKeys) {
+  const int n_keys_all = d.prefix_len + d.T;
+  const int k_begin = split * chunk, n_keys = min(n_keys_all, k_begin + chunk);
+  for (int kt = k_begin; kt < n_keys; kt += kTreeKeys) {
     const int nk = min(kTreeKeys, n_keys - kt);
     // stage dequantized K/V (scales applied) for the key tile
     for (int i = tid; i < nk * HD; i += 128) {
@@ -521,11 +527,39 @@ __global__ void __launch_bounds__(128) tree_attn_kernel(axb_attn_desc d) {
   }
   if (my_r < R) {
     int u = u0 + my_r / n_rep, hq = kvh * n_rep + my_r % n_rep;
-    __half* o = reinterpret_cast<__half*>(d.out) + (((size_t)b * d.T + u) * d.n_head + hq) * HD + my_d0;
-    float l = l_s[my_r];
+    const size_t row = ((size_t)b * d.T + u) * d.n_head + hq;
+    if (nsplit == 1) {
+      __half* o = reinterpret_cast<__half*>(d.out) + row * HD + my_d0;
+      float l = l_s[my_r];
 #pragma unroll
-    for (int e = 0; e < DPT; ++e) o[e] = __float2half_rn(__fdiv_rn(acc[e], l));
+      for (int e = 0; e < DPT; ++e) o[e] = __float2half_rn(__fdiv_rn(acc[e], l));
+    } else {
+      float* o = po + (row * nsplit + split) * HD + my_d0;
+#pragma unroll
+      for (int e = 0; e < DPT; ++e) o[e] = acc[e];
+      if ((tid & 7) == 0) {
+        pml[(row * nsplit + split) * 2 + 0] = m_s[my_r];
+        pml[(row * nsplit + split) * 2 + 1] = l_s[my_r];
+      }
+    }
   }
+}
+
+// out[row] = sum_s w_s O_s / sum_s w_s l_s, w_s = exp(m_s - max m), in split order
+__global__ void tree_combine_kernel(const float* __restrict__ po, const float* __restrict__ pml, int nsplit, int hd,
+                                    __half* __restrict__ out) {
+  const size_t row = blockIdx.x;
+  const int e = threadIdx.x;
+  float M = -INFINITY;
+  for (int q = 0; q < nsplit; ++q) M = fmaxf(M, pml[(row * nsplit + q) * 2]);
+  float L = 0.f, O = 0.f;
+  for (int q = 0; q < nsplit; ++q) {
+    const float m = pml[(row * nsplit + q) * 2], l = pml[(row * nsplit + q) * 2 + 1];
+    const float w = m == -INFINITY ? 0.f : __expf(m - M);
+    L += l * w;
+    if (e < hd) O += po[(row * nsplit + q) * hd + e] * w;
+  }
+  if (e < hd) out[row * hd + e] = __float2half_rn(__fdiv_rn(O, L));
 }
 
 // ---------------------------------------------------------------- compaction
@@ -580,6 +614,24 @@ int decode_grid_splits(int target, int max_seq, int kv_type, int hd) {
 // zeroed workspace serves any call; the combining CTA returns each to zero.
 constexpr size_t kAttnCounters = 1 << 16;
 constexpr size_t kAttnHead = 256;  // error word
+
+// tree / chunked-prefill mode: splits of the key range and their partials
+int tree_splits(int B, int T, int n_head, int n_kv_head, int n_keys) {
+  const int n_rep = n_head / n_kv_head, TQ = std::max(1, kTreeRows / n_rep);
+  const int base = ((T + TQ - 1) / TQ) * n_kv_head * B;
+  int S = (5 * num_sms() + base - 1) / base;  // about five 43 KB CTAs per SM
+  S = std::min(S, std::max(1, n_keys / 128));
+  return std::max(1, std::min(S, 64));
+}
+// The partials follow the workspace's fixed header (error word and the decode
+// path's arrival counters, which must stay zero); they may reuse the decode
+// partial regions, which every decode launch rewrites before reading.
+size_t tree_partials_offset() { return round_up(kAttnHead + kAttnCounters * 4, 256); }
+size_t tree_workspace(int B, int T, int n_head, int head_dim, int nsplit) {
+  if (nsplit <= 1) return 0;
+  const size_t rows = (size_t)B * T * n_head;
+  return tree_partials_offset() + round_up(rows * nsplit * head_dim * 4, 256) + round_up(rows * nsplit * 2 * 4, 256);
+}
 
 size_t attn_workspace(int B, int n_head, int head_dim, int max_splits) {
   size_t o = (size_t)B * n_head * max_splits * head_dim * 4;
@@ -668,13 +720,27 @@ int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s)
   AXB_CHECK_ARG(d->prefix_len >= 0 && d->prefix_len <= d->max_seq, "attention: bad prefix_len");
   int n_rep = d->n_head / d->n_kv_head;
   int TQ = std::max(1, kTreeRows / n_rep);
-  dim3 grid((d->T + TQ - 1) / TQ, d->n_kv_head, d->B);
+  // split the keys across CTAs when the workspace holds the partials; the
+  // prefix length is read on the device, so the split plan uses its maximum
+  int S = tree_splits(d->B, d->T, d->n_head, d->n_kv_head, d->max_seq);
+  if (!d->workspace || d->workspace_bytes < tree_workspace(d->B, d->T, d->n_head, d->head_dim, S)) S = 1;
+  const int chunk = S > 1 ? ((d->max_seq + S - 1) / S + kTreeKeys - 1) / kTreeKeys * kTreeKeys : 1 << 30;
+  char* tws = reinterpret_cast<char*>(d->workspace) + tree_partials_offset();
+  float* po = S > 1 ? reinterpret_cast<float*>(tws) : nullptr;
+  const size_t rows = (size_t)d->B * d->T * d->n_head;
+  float* pml = S > 1 ? reinterpret_cast<float*>(tws + round_up(rows * S * d->head_dim * 4, 256)) : nullptr;
+  dim3 grid(((d->T + TQ - 1) / TQ) * S, d->n_kv_head, d->B);
   cudaError_t e;
   if (d->head_dim == 128)
-    e = launch_pdl(tree_attn_kernel<128>, grid, dim3(128), 0, s, d->pdl != 0, *d);
+    e = launch_pdl(tree_attn_kernel<128>, grid, dim3(128), 0, s, d->pdl != 0, *d, S, chunk, po, pml);
   else
-    e = launch_pdl(tree_attn_kernel<64>, grid, dim3(128), 0, s, d->pdl != 0, *d);
-  return cuda_status(e, "tree attention launch");
+    e = launch_pdl(tree_attn_kernel<64>, grid, dim3(128), 0, s, d->pdl != 0, *d, S, chunk, po, pml);
+  if (e != cudaSuccess) return cuda_status(e, "tree attention launch");
+  if (S > 1) {
+    tree_combine_kernel<<<(unsigned)rows, 128, 0, s>>>(po, pml, S, d->head_dim, reinterpret_cast<__half*>(d->out));
+    return launch_status("tree combine");
+  }
+  return AXB_OK;
 }
 
 }  // namespace axb

@@ -220,17 +220,19 @@ __global__ void __launch_bounds__(kLbWarps * 32) lbgemv_kernel(const uint4* __re
                                                                const __half* __restrict__ x, int ldx,
                                                                const float* __restrict__ xsum, int N, int K, int M,
                                                                __half* __restrict__ y, int ldy,
-                                                               const __half* __restrict__ bias) {
+                                                               const __half* __restrict__ bias, int nsplit,
+                                                               float* __restrict__ part) {
   __shared__ float4 red[kLbWarps][32];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
   const int t = blockIdx.x, KB = K / kQ2KB;
+  const int sp = blockIdx.y, kb0 = (int)((long long)sp * KB / nsplit), kb1 = (int)((long long)(sp + 1) * KB / nsplit);
   constexpr bool TER = FMT == AXB_W_TERNARY_G64 || FMT == AXB_W_TERNARY_PT;
   const __half2 off = TER ? __float2half2_rn(1025.f) : __float2half2_rn(1024.f);  // exact: raw - off = q or u
   const bool tok = g < M;  // B-fragment token of this lane
   const __half* xr = x + (size_t)(tok ? g : 0) * ldx + 8 * c;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int kb = wid; kb < KB; kb += kLbWarps) {
+  for (int kb = kb0 + wid; kb < kb1; kb += kLbWarps) {
     const size_t tb = (size_t)t * KB + kb;
     const uint4 wv = ldg_nc_v4(words + tb * 32 + lane);
     const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
@@ -312,10 +314,35 @@ __global__ void __launch_bounds__(kLbWarps * 32) lbgemv_kernel(const uint4* __re
   for (int q = 0; q < 4; ++q) {
     const int n = 2 * c + (q & 1), row = t * 16 + g + 8 * (q >> 1);
     if (n >= M || row >= N) continue;
+    if (nsplit > 1) {  // this split's fp32 partial; lb_reduce_kernel finishes the row
+      part[((size_t)sp * M + n) * N + row] = v[q];
+      continue;
+    }
     float o = FMT == AXB_W_TERNARY_PT ? v[q] * pts : v[q];
     if (bias) o += __half2float(bias[row]);
     y[(size_t)n * ldy + row] = __float2half_rn(o);
   }
+}
+
+// split-K: y[n][row] = fp16(sum of the splits in order (x the per-tensor scale) + bias)
+__global__ void lb_reduce_kernel(const float* __restrict__ part, int S, int M, int N, const __half* __restrict__ pt,
+                                 const __half* __restrict__ bias, __half* __restrict__ y, int ldy) {
+  const size_t total = (size_t)M * N;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int n = (int)(i / N), row = (int)(i % N);
+    float o = 0.f;
+    for (int q = 0; q < S; ++q) o += part[(size_t)q * total + i];
+    if (pt) o *= __half2float(pt[0]);
+    if (bias) o += __half2float(bias[row]);
+    y[(size_t)n * ldy + row] = __float2half_rn(o);
+  }
+}
+
+// k splits: enough CTAs (8 warps each) to fill the GPU when the tiles alone do not
+int lb_splits(int N, int K) {
+  const int tiles = (N + 15) / 16, KB = K / kQ2KB;
+  int S = (4 * num_sms() + tiles - 1) / tiles;
+  return std::max(1, std::min(S, std::max(1, KB / kLbWarps)));
 }
 
 }  // namespace axb
@@ -376,10 +403,14 @@ int axb_q2t_dequant(int fmt, const void* words, const void* meta, const void* me
   return launch_status("q2t_dequant");
 }
 
-size_t axb_lbgemv_workspace_bytes(int fmt, int K, int M) {
-  (void)M;
-  if (fmt != AXB_W_Q2_G64 || K <= 0) return 0;
-  return (size_t)(K / 64) * kLbMaxM * sizeof(float);
+static size_t lb_xsum_bytes(int fmt, int K) {
+  return fmt == AXB_W_Q2_G64 ? ((size_t)(K / 64) * kLbMaxM * sizeof(float) + 255) / 256 * 256 : 0;
+}
+
+size_t axb_lbgemv_workspace_bytes(int fmt, int N, int K, int M) {
+  if (N <= 0 || K <= 0 || K % kQ2KB || M < 1) return 0;
+  const int S = lb_splits(N, K);
+  return lb_xsum_bytes(fmt, K) + (S > 1 ? (size_t)S * kLbMaxM * N * sizeof(float) : 0);
 }
 
 int axb_lbgemv(const axb_lbgemv_desc* d, void* stream) {
@@ -394,21 +425,24 @@ int axb_lbgemv(const axb_lbgemv_desc* d, void* stream) {
   AXB_CHECK_ARG(d->fmt == AXB_W_TERNARY_PT || d->meta, "lbgemv: meta is required");
   AXB_CHECK_ARG(d->fmt != AXB_W_TERNARY_PT || d->pt_scale, "lbgemv: per-tensor ternary needs its scale");
   AXB_CHECK_ARG(d->fmt != AXB_W_Q2K_SB256 || (d->meta2 && d->K % 256 == 0), "lbgemv: K-quant needs meta2");
-  const size_t need = axb_lbgemv_workspace_bytes(d->fmt, d->K, d->M);
+  const size_t need = axb_lbgemv_workspace_bytes(d->fmt, d->N, d->K, d->M);
   AXB_CHECK_ARG(need == 0 || (d->workspace && d->workspace_bytes >= need), "lbgemv: workspace %zu < %zu bytes",
                 d->workspace_bytes, need);
   cudaStream_t st = (cudaStream_t)stream;
   float* xsum = (float*)d->workspace;
-  if (need) {
+  const int S = lb_splits(d->N, d->K);
+  float* part = S > 1 ? (float*)((char*)d->workspace + lb_xsum_bytes(d->fmt, d->K)) : nullptr;
+  if (lb_xsum_bytes(d->fmt, d->K)) {
     const int n = d->K / 64 * kLbMaxM;
     lb_xsum_kernel<<<(n + 127) / 128, 128, 0, st>>>((const __half*)d->x, d->ldx, d->M, d->K, xsum);
   }
   const int tiles = (d->N + 15) / 16;
 #define AXB_LB(F)                                                                                              \
   case F:                                                                                                      \
-    lbgemv_kernel<F><<<tiles, kLbWarps * 32, 0, st>>>(                                                        \
+    lbgemv_kernel<F><<<dim3(tiles, S), kLbWarps * 32, 0, st>>>(                                               \
         (const uint4*)d->words, (const uint8_t*)d->meta, (const __half2*)d->meta2, (const __half*)d->pt_scale, \
-        (const __half*)d->x, d->ldx, xsum, d->N, d->K, d->M, (__half*)d->y, d->ldy, (const __half*)d->bias);  \
+        (const __half*)d->x, d->ldx, xsum, d->N, d->K, d->M, (__half*)d->y, d->ldy, (const __half*)d->bias, S,   \
+        part);                                                                                                 \
     break;
   switch (d->fmt) {
     AXB_LB(AXB_W_TERNARY_G64)
@@ -417,7 +451,16 @@ int axb_lbgemv(const axb_lbgemv_desc* d, void* stream) {
     AXB_LB(AXB_W_Q2K_SB256)
   }
 #undef AXB_LB
-  return launch_status("lbgemv");
+  if (int rc = launch_status("lbgemv")) return rc;
+  if (S > 1) {
+    const size_t total = (size_t)d->M * d->N;
+    const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)num_sms() * 4);
+    lb_reduce_kernel<<<blocks, 256, 0, st>>>(part, S, d->M, d->N,
+                                             d->fmt == AXB_W_TERNARY_PT ? (const __half*)d->pt_scale : nullptr,
+                                             (const __half*)d->bias, (__half*)d->y, d->ldy);
+    return launch_status("lbgemv reduce");
+  }
+  return AXB_OK;
 }
 
 }  // extern "C"

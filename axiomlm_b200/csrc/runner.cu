@@ -34,9 +34,28 @@ struct DecodeFuse {
 int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s);
 int attn_prepare();
 size_t attn_workspace(int B, int n_head, int head_dim, int max_splits);
+int tree_splits(int B, int T, int n_head, int n_kv_head, int n_keys);
+size_t tree_workspace(int B, int T, int n_head, int head_dim, int nsplit);
 int decode_max_splits(int B, int n_kv_head);
 int decode_grid_splits(int target, int max_seq, int kv_type, int hd);
 int rmsnorm(const __half* x, const float* w, int M, int K, float eps, __half* out, cudaStream_t s);
+
+// many-token projections on the tcgen05 tensor cores (qgemm_tc.cu); their
+// residual / SwiGLU epilogues, with the GEMV's rounding points
+__global__ void residual_add_kernel(__half* __restrict__ x, const __half* __restrict__ y, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    x[i] = __float2half_rn(__fadd_rn(__half2float(x[i]), __half2float(y[i])));
+}
+// gate / up rows interleaved by 8 (tile = 8 gate + 8 up rows): sw[m][j] = fp16(silu(g) * u)
+__global__ void swiglu_packed_kernel(const __half* __restrict__ gu, int ld, int F, int rows, __half* __restrict__ sw) {
+  const size_t total = (size_t)rows * F;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / F), j = (int)(i % F);
+    const int p = (j >> 3) * 16 + (j & 7);
+    const float g = __half2float(gu[(size_t)m * ld + p]), u = __half2float(gu[(size_t)m * ld + p + 8]);
+    sw[(size_t)m * F + j] = __float2half_rn(__fmul_rn(silu_f(g), u));
+  }
+}
 int argmax(const __half* x, int rows, int n, int ld, int32_t* out, cudaStream_t s);
 
 struct StepParams {
@@ -184,11 +203,13 @@ __global__ void rmsnorm_f32_kernel(const __half* __restrict__ x, const float* __
 static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 constexpr int kArgmaxParts = 256;
+constexpr int kTcMinRows = 16;  // tree / prefill steps above this many rows use the tcgen05 GEMM
 
 struct Layout {
   size_t tokens, params, masks, depths, x, h, qkv, q, attn, sw, logits, amax, xnorm, gemm_ws, attn_ws, total;
   size_t am_v, am_i, am_cnt;
   size_t tp_part, tp_keys;  // tensor parallel: row-parallel partial sums (fp32), argmax keys
+  size_t gu_tmp, tc_ws, tc_ws_bytes;  // tensor-core projections for many-token steps
   size_t gemm_ws_bytes, attn_ws_bytes;
   // persistent step kernel (decode, B <= 8)
   size_t st_layers, st_done, st_tiles, st_part, st_po, st_pml, st_acnt, st_keys, st_exit, st_trace;
@@ -224,6 +245,18 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.am_i = take(rows * kArgmaxParts * 4);
   L.am_cnt = take(rows * 4);
   L.tp_part = take(c.tp_world > 1 ? rows * c.d_model * 4 : 0);
+  // tensor-core path (rows > 16): gate_up output in packed order, tcgen05 workspace
+  const bool tc = rows > kTcMinRows && c.tp_world <= 1;
+  L.gu_tmp = take(tc ? rows * 2 * (size_t)c.ffn * 2 : 0);
+  size_t tcw = 0;
+  if (tc) {
+    const int qd_ = c.n_head * c.head_dim;
+    const int NK[5][2] = {{(int)qkv_dim, c.d_model}, {c.d_model, qd_}, {2 * c.ffn, c.d_model}, {c.d_model, c.ffn},
+                          {c.vocab, c.d_model}};
+    for (auto& nk : NK) tcw = std::max(tcw, axb_qgemm_tc_workspace_bytes(nk[0], nk[1], 64));
+  }
+  L.tc_ws_bytes = tcw;
+  L.tc_ws = take(tcw);
   L.tp_keys = take(c.tp_world > 1 ? rows * 8 : 0);
   int m = (int)std::min<size_t>(rows, 64);
   size_t g = 0;
@@ -235,6 +268,12 @@ static Layout make_layout(const axb_model_cfg& c) {
     a = std::max(a, attn_workspace(b, c.n_head, c.head_dim,
                                    decode_grid_splits(decode_max_splits(b, c.n_kv_head), c.max_seq, c.kv_type,
                                                       c.head_dim)));
+  // tree / prefill steps split their keys across CTAs: room for the partials
+  if (c.max_tokens > 1)
+    for (int b = 1; b <= c.max_batch; ++b)
+      for (int t = 1; t <= c.max_tokens; ++t)
+        a = std::max(a, tree_workspace(b, t, c.n_head, c.head_dim,
+                                       tree_splits(b, t, c.n_head, c.n_kv_head, c.max_seq)));
   L.attn_ws_bytes = a;
   L.attn_ws = take(a);
   const int sb = std::min(c.max_batch, kStepMaxM);
@@ -321,11 +360,62 @@ struct Runner {
     return gemv(w, s, fmt, group, N, K, M, buf<__half>(L.h), K, y, ldy, bias, nullptr, epi, gu, st);
   }
 
+  // the tcgen05 kernel is built for Q4 symmetric group 128 and affine group 64
+  static bool tc_fmt(int fmt, int group) {
+    return (fmt == AXB_W_Q4T_SYM && group == 128) || (fmt == AXB_W_Q4T_AFFINE && group == 64);
+  }
+  bool tc_ok = true;  // env AXB_TC=0 keeps many-token steps on the warp-level GEMV
+  bool use_tc(int rows) const {
+    return tc_ok && rows > kTcMinRows && c.tp_world <= 1 && L.tc_ws_bytes > 0 && tc_fmt(c.wfmt, c.group) &&
+           tc_fmt(c.lm_fmt, c.lm_group);
+  }
+
+  // y = x W^T (+ bias) for many rows on the tcgen05 kernel (64 rows per launch)
+  int tc_gemm(const void* w, const void* s, int fmt, int group, int N, int K, int M, const __half* x, int ldx,
+              __half* y, int ldy, const void* bias, cudaStream_t st) const {
+    for (int m0 = 0; m0 < M; m0 += 64) {
+      axb_qgemm_desc d = {};
+      d.fmt = fmt;
+      d.group = group;
+      d.words = w;
+      d.scales = s;
+      d.N = N;
+      d.K = K;
+      d.M = std::min(64, M - m0);
+      d.x = x + (size_t)m0 * ldx;
+      d.ldx = ldx;
+      d.y = y + (size_t)m0 * ldy;
+      d.ldy = ldy;
+      d.bias = bias;
+      d.epilogue = AXB_EPI_STORE;
+      d.workspace = buf<void>(L.tc_ws);
+      d.workspace_bytes = L.tc_ws_bytes;
+      if (int rc = axb_qgemm_tc(&d, st)) return rc;
+    }
+    return AXB_OK;
+  }
+
+  // RMSNorm (fp16 rows into h) then the tensor-core GEMM
+  int norm_tc(const float* nw, const void* w, const void* s, int fmt, int group, int N, int K, int M, __half* y,
+              int ldy, const void* bias, cudaStream_t st) const {
+    int rc = rmsnorm(buf<__half>(L.x), nw, M, K, c.eps, buf<__half>(L.h), st);
+    if (rc) return rc;
+    return tc_gemm(w, s, fmt, group, N, K, M, buf<__half>(L.h), K, y, ldy, bias, st);
+  }
+
   // x += W a for the o / down projections.  Tensor parallel: this rank's
   // K-slice gives an fp32 partial, the ranks' partials meet in one allreduce,
   // then the residual add rounds as the single-GPU path does.
   int row_parallel(const void* w, const void* s, int K, int rows, const __half* act, cudaStream_t st) const {
     const int d = c.d_model;
+    if (use_tc(rows)) {  // h is free here: the product lands there, then the residual add
+      int rc = tc_gemm(w, s, c.wfmt, c.group, d, K, rows, act, K, buf<__half>(L.h), d, nullptr, st);
+      if (rc) return rc;
+      const int n = rows * d;
+      residual_add_kernel<<<std::min((n + 255) / 256, 4 * num_sms()), 256, 0, st>>>(buf<__half>(L.x),
+                                                                                   buf<__half>(L.h), n);
+      return launch_status("residual add");
+    }
     if (c.tp_world <= 1)
       return gemv(w, s, c.wfmt, c.group, d, K, rows, act, K, buf<void>(L.x), d, nullptr, nullptr, AXB_EPI_RESIDUAL, 0,
                   st);
@@ -354,8 +444,10 @@ struct Runner {
                                buf<__half>(L.x), buf<int>(L.params) + 4);
     if (e != cudaSuccess) return cuda_status(e, "embed launch");
     for (int l = 0; l < c.n_layer; ++l) {
-      int rc = norm_gemv(ln1[l], qkv_w[l], qkv_s[l], qkv_dim, d, rows, buf<void>(L.qkv), qkv_dim, qkv_b[l],
-                         AXB_EPI_STORE, 0, c.wfmt, c.group, st);
+      int rc = use_tc(rows) ? norm_tc(ln1[l], qkv_w[l], qkv_s[l], c.wfmt, c.group, qkv_dim, d, rows,
+                                      buf<__half>(L.qkv), qkv_dim, qkv_b[l], st)
+                            : norm_gemv(ln1[l], qkv_w[l], qkv_s[l], qkv_dim, d, rows, buf<void>(L.qkv), qkv_dim,
+                                        qkv_b[l], AXB_EPI_STORE, 0, c.wfmt, c.group, st);
       if (rc) return rc;
       axb_kv_write_desc kw = {};
       kw.kv_type = c.kv_type;
@@ -415,14 +507,26 @@ struct Runner {
       if (rc) return rc;
       rc = row_parallel(o_w[l], o_s[l], qd, rows, buf<__half>(L.attn), st);
       if (rc) return rc;
-      rc = norm_gemv(ln2[l], gu_w[l], gu_s[l], 2 * c.ffn, d, rows, buf<void>(L.sw), c.ffn, nullptr, AXB_EPI_SWIGLU,
-                     1, c.wfmt, c.group, st);
+      if (use_tc(rows)) {
+        rc = norm_tc(ln2[l], gu_w[l], gu_s[l], c.wfmt, c.group, 2 * c.ffn, d, rows, buf<__half>(L.gu_tmp), 2 * c.ffn,
+                     nullptr, st);
+        if (rc) return rc;
+        const size_t n = (size_t)rows * c.ffn;
+        swiglu_packed_kernel<<<(int)std::min<size_t>((n + 255) / 256, 4 * num_sms()), 256, 0, st>>>(
+            buf<__half>(L.gu_tmp), 2 * c.ffn, c.ffn, rows, buf<__half>(L.sw));
+        rc = launch_status("swiglu");
+      } else {
+        rc = norm_gemv(ln2[l], gu_w[l], gu_s[l], 2 * c.ffn, d, rows, buf<void>(L.sw), c.ffn, nullptr, AXB_EPI_SWIGLU,
+                       1, c.wfmt, c.group, st);
+      }
       if (rc) return rc;
       rc = row_parallel(dn_w[l], dn_s[l], c.ffn, rows, buf<__half>(L.sw), st);
       if (rc) return rc;
     }
-    int rc = norm_gemv(ln_f, lm_w, lm_s, c.vocab, d, rows, buf<void>(L.logits), c.vocab, nullptr, AXB_EPI_STORE, 0,
-                       c.lm_fmt, c.lm_group, st);
+    int rc = use_tc(rows) ? norm_tc(ln_f, lm_w, lm_s, c.lm_fmt, c.lm_group, c.vocab, d, rows, buf<__half>(L.logits),
+                                    c.vocab, nullptr, st)
+                          : norm_gemv(ln_f, lm_w, lm_s, c.vocab, d, rows, buf<void>(L.logits), c.vocab, nullptr,
+                                      AXB_EPI_STORE, 0, c.lm_fmt, c.lm_group, st);
     if (rc) return rc;
     if (want_norm) {
       e = launch_pdl(rmsnorm_f32_kernel, dim3(rows), dim3(256), 0, st, pdl, (const __half*)buf<__half>(L.x), ln_f,
@@ -487,6 +591,7 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
     r->c.tp_rank = 0;
   }
   r->tp_comm = c.tp_world > 1 ? p->tp_comm : nullptr;
+  if (const char* tv = getenv("AXB_TC")) r->tc_ok = atoi(tv) != 0;
   if (const char* ev = getenv("AXB_PDL")) {
     r->pdl = atoi(ev) != 0;
     r->pdl_mode = atoi(ev) == 2 ? 2 : 1;

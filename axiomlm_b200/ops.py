@@ -246,7 +246,7 @@ def lbgemm(x: torch.Tensor, W: Q2TWeight, bias: torch.Tensor | None = None,
         out = torch.empty((M, W.N), dtype=torch.float16, device=x.device)
     o2 = out.view(M, W.N)
     lib = L.load()
-    ws = _WS.get(lib.axb_lbgemv_workspace_bytes(W.fmt, K, 8), x.device)
+    ws = _WS.get(lib.axb_lbgemv_workspace_bytes(W.fmt, W.N, K, 8), x.device)
     b = None if bias is None else _cuda(bias, "bias").to(torch.float16)
     for m0 in range(0, M, 8):
         m = min(8, M - m0)

@@ -139,10 +139,10 @@ typedef struct {
   void* y;               /* fp16 (M, ldy) */
   int ldy;
   const void* bias;      /* fp16 (N) or NULL */
-  void* workspace;       /* >= axb_lbgemv_workspace_bytes(fmt, K, M) (group sums of x) */
+  void* workspace;       /* >= axb_lbgemv_workspace_bytes(fmt, N, K, M): group sums of x, split-K partials */
   size_t workspace_bytes;
 } axb_lbgemv_desc;
-size_t axb_lbgemv_workspace_bytes(int fmt, int K, int M);
+size_t axb_lbgemv_workspace_bytes(int fmt, int N, int K, int M);
 int axb_lbgemv(const axb_lbgemv_desc* d, void* stream);
 
 /* ---- quantized GEMV / small-M GEMM (qmv_q4_marlin / qmm_q4_marlin,
