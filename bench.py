@@ -354,10 +354,13 @@ def run_ours(args, rank, world):
     # ---- roofline of the dominant kernel: the persistent step kernel (one
     # launch per step), or the Q4 GEMV when the per-kernel graph runs the step
     pk, pk_kind = peaks()
-    step_kernel = dec.uses_step_kernel
+    step_kernel = dec.uses_step_kernel and B <= 8  # the persistent kernel takes decode batches of up to 8
     if step_kernel:
         bpl, spl, nl = step_roofline(dec, B)
         kname = "step_kernel<SYM, GB=2, HD=128> (whole decode step, one persistent launch)"
+    elif B > 16:  # many-token decode: the graph path with the tcgen05 projections; whole step timed
+        bpl, spl, nl = step_roofline(dec, B)
+        kname = "per-op CUDA graph step (qgemm_tc_kernel projections, split decode attention)"
     else:
         bpl, spl, nl = gemv_roofline(dec, B)
         kname = "qgemm_kernel<1,SYM,2,*> (Q4 G128 GEMV)"
