@@ -3,7 +3,7 @@
 ``ops``    -- the reference's ``_METAL_MOD`` op table on CUDA (libaxb.so)
 ``cache``  -- ``StaticKVCache`` in HBM
 ``model``  -- ``QuantizedDecoder`` (the CUDA-graph decode runner)
-``tree``   -- Medusa tree compilation and greedy accept (host logic)
+``medusa`` -- Medusa heads, tree compilation and speculative decoding (greedy on the device)
 """
 
 __version__ = "0.1.0"

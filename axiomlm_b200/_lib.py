@@ -38,6 +38,10 @@ EPI_RESIDUAL = 1
 EPI_SWIGLU = 2
 EPI_F32 = 3
 EPI_F32_ACC = 4
+TREE_MAX_NODES = 64
+TREE_RESULT_HDR = 4
+TREE_RESULT_WORDS = TREE_RESULT_HDR + 2 * TREE_MAX_NODES
+TOPK_MAX = 64
 
 TP_SUM_F32 = 0
 TP_SUM_F16 = 1
@@ -151,6 +155,12 @@ _SIGS = {
     "axb_attention": (i32, [C.POINTER(AttnDesc), vp]),
     "axb_compact_kv": (i32, [vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, i32, vp]),
     "axb_argmax": (i32, [vp, i32, i32, i32, vp, vp]),
+    "axb_compact_kv_dev": (i32, [vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, i32, vp]),
+    "axb_tree_accept": (i32, [i32, vp, vp, vp, i32, vp, vp]),
+    "axb_medusa_leaf": (i32, [vp, i32, vp, i32, vp, vp, vp]),
+    "axb_medusa_silu_add": (i32, [i32, i32, vp, vp, vp, vp]),
+    "axb_topk_rows": (i32, [vp, i32, i32, i32, i32, vp, vp]),
+    "axb_draft_tokens": (i32, [i32, vp, vp, vp, i32, vp, vp, vp]),
     "axb_runner_workspace_bytes": (sz, [C.POINTER(ModelCfg)]),
     "axb_runner_create": (i32, [C.POINTER(ModelCfg), C.POINTER(ModelPtrs), vp, sz, C.POINTER(vp)]),
     "axb_runner_destroy": (i32, [vp]),

@@ -564,9 +564,16 @@ __global__ void tree_combine_kernel(const float* __restrict__ po, const float* _
 
 // ---------------------------------------------------------------- compaction
 __global__ void compact_kv_kernel(uint8_t* cache, __half* scales, int max_batch, int n_kv_head, int max_seq,
-                                  int row_bytes, int n_groups, int write_pos, const int32_t* acc, int n_acc) {
+                                  int row_bytes, int n_groups, int write_pos, const int32_t* acc, int n_acc,
+                                  const int32_t* n_dev) {
   // blockIdx.x = ((layer*2 + kv)*max_batch + b)*Hkv + h
   extern __shared__ uint8_t stage[];
+  if (n_dev) {  // count from the device-side tree walk; an identity path moves nothing
+    n_acc = min(max(n_dev[0], 0), n_acc);
+    bool same = true;
+    for (int m = 0; m < n_acc; ++m) same &= acc[m] == m;
+    if (same) return;
+  }
   const size_t head = blockIdx.x;
   uint8_t* rows = cache + head * max_seq * (size_t)row_bytes;
   __half* srow = scales ? scales + head * max_seq * (size_t)n_groups : nullptr;
@@ -795,8 +802,22 @@ int axb_compact_kv(void* cache, uint16_t* scales, int n_layer, int max_batch, in
   int heads = n_layer * 2 * max_batch * n_kv_head;
   compact_kv_kernel<<<heads, 256, smem, (cudaStream_t)stream>>>((uint8_t*)cache, (__half*)scales, max_batch,
                                                                 n_kv_head, max_seq, row_bytes, n_groups, write_pos,
-                                                                accepted, n_acc);
+                                                                accepted, n_acc, nullptr);
   return launch_status("compact_kv");
+}
+
+int axb_compact_kv_dev(void* cache, uint16_t* scales, int n_layer, int max_batch, int n_kv_head, int max_seq,
+                       int row_bytes, int n_groups, int write_pos, const int32_t* accepted, const int32_t* n_acc_dev,
+                       int max_acc, void* stream) {
+  AXB_CHECK_ARG(cache && accepted && n_acc_dev && row_bytes > 0, "compact_kv_dev: null pointer");
+  AXB_CHECK_ARG(max_acc >= 1 && max_acc <= 64 && max_acc <= max_seq, "compact_kv_dev: max_accepted must be 1..64");
+  size_t smem = (size_t)max_acc * row_bytes + (size_t)max_acc * n_groups * 2;
+  AXB_CHECK_ARG(smem <= 48 * 1024, "compact_kv_dev: %d rows of %d bytes exceed the staging", max_acc, row_bytes);
+  int heads = n_layer * 2 * max_batch * n_kv_head;
+  compact_kv_kernel<<<heads, 256, smem, (cudaStream_t)stream>>>((uint8_t*)cache, (__half*)scales, max_batch,
+                                                                n_kv_head, max_seq, row_bytes, n_groups, write_pos,
+                                                                accepted, max_acc, n_acc_dev);
+  return launch_status("compact_kv_dev");
 }
 
 }  // extern "C"

@@ -109,6 +109,7 @@ class QuantizedDecoder:
         self.norm_buf = view(3, torch.float32, (rows, d))
         self.error_buf = view(4, torch.int32, (1,))
         self._last_T = 1
+        self.medusa_heads = None
 
     # ------------------------------------------------------------ builders
     @classmethod
@@ -147,7 +148,12 @@ class QuantizedDecoder:
         emb_w, emb_s = ops.pack_q8_g64(g(weights["wte"]))
         packed = dict(layers=layers, emb_w=emb_w, emb_s=emb_s, lm_head=ops.pack_q4t(g(weights["lm_head"]), group, sym),
                       ln_f=g(weights["ln_f"]).contiguous())
-        return cls(cfg, packed, **kw)
+        dec = cls(cfg, packed, **kw)
+        if weights.get("medusa"):
+            from .medusa import MedusaHeads
+
+            dec.add_medusa_heads(MedusaHeads.from_weights(weights["medusa"], weight_format, device=dev))
+        return dec
 
     @classmethod
     def from_reference(cls, model: Any, **kw) -> "QuantizedDecoder":
@@ -180,7 +186,12 @@ class QuantizedDecoder:
         packed = dict(layers=layers, emb_w=qw["wte_p"].to(dev), emb_s=qw["wte_sb"].to(dev),
                       lm_head=ops.q4t_from_marlin(qw["lmh_p"].to(dev), qw["lmh_sb"].to(dev), mc.vocab_size),
                       ln_f=model.transformer.ln_f.weight.detach().to(dev, torch.float32).contiguous())
-        return cls(cfg, packed, **kw)
+        dec = cls(cfg, packed, **kw)
+        if qw.get("medusa_packs"):
+            from .medusa import MedusaHeads
+
+            dec.add_medusa_heads(MedusaHeads.from_packs(qw["medusa_packs"], mc.n_embd, mc.vocab_size, device=dev))
+        return dec
 
     # ------------------------------------------------------------ steps
     @property
@@ -255,6 +266,44 @@ class QuantizedDecoder:
         self._load_tokens(idx)
         self._step(B, T, seen % self.rope_len, wp, seen + T, seen, tree_mask, tree_depths)
         return self.logits_buf[: B * T].view(B, T, -1)
+
+    def forward_tree_verify_device(self, T: int, tree_depths: list[int], tree_mask: list[int]) -> torch.Tensor:
+        """forward_tree_verify over the T tokens already in the runner's token
+        buffer (``self.tokens``, written on the device by the Medusa draft)."""
+        seen = self.cache.total_seen_tokens[0]
+        wp = (seen % self.cache.max_seq_len) if (self.cache.ring_buffer or seen >= self.cache.max_seq_len) else seen
+        if wp + T > self.cache.max_seq_len or seen != wp:
+            raise RuntimeError(f"tree verification needs contiguous tail capacity: write_pos={wp}, T={T}")
+        self._step(1, T, seen % self.rope_len, wp, seen + T, seen, tree_mask, tree_depths)
+        return self.logits_buf[:T].view(1, T, -1)
+
+    def compact_device(self, write_pos: int, result: torch.Tensor):
+        """compact_tree_path with the accepted nodes and their count taken from
+        a device tree-walk result block (no host round trip)."""
+        c = self.cache
+        cache = c.cache
+        L_, two, Bm, H, S, W = cache.shape
+        ng = 0 if c.scales is None else c.scales.shape[-1]
+        L.call("axb_compact_kv_dev", C.c_void_p(cache.data_ptr()), ops._p(c.scales), L_, Bm, H, S,
+               W * cache.element_size(), ng, int(write_pos), C.c_void_p(result.data_ptr() + 4 * L.TREE_RESULT_HDR),
+               C.c_void_p(result.data_ptr()), min(L.TREE_MAX_NODES, S), ops._stream())
+
+    # ------------------------------------------------------------ Medusa
+    def add_medusa_heads(self, heads):
+        """Attach quantized Medusa heads (an ``axiomlm_b200.medusa.MedusaHeads``),
+        as Transformer.add_medusa_heads + quantize do (transformer.py:386-412)."""
+        if heads.d != self.cfg["d_model"] or heads.vocab != self.vocab_local:
+            raise ValueError("Medusa heads must map d_model -> vocab")
+        if self.tp is not None and self.tp.world > 1:
+            raise NotImplementedError("Medusa heads under tensor parallelism")
+        self.medusa_heads = heads
+        return self
+
+    def eval_medusa_heads(self, x_norm: torch.Tensor) -> list[torch.Tensor]:
+        """transformer.py:414-445: the heads' logits on final-norm rows."""
+        if self.medusa_heads is None:
+            return []
+        return self.medusa_heads(x_norm)
 
     def get_last_norm(self, T: int | None = None) -> torch.Tensor:
         """Final-norm hidden states (fp32) of the last tree/prefill step."""

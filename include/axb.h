@@ -275,6 +275,15 @@ int axb_compact_kv(void* cache_dev, uint16_t* scales_dev, int n_layer, int max_b
                    int max_seq, int row_bytes, int n_groups, int write_pos, const int32_t* accepted_dev,
                    int n_accepted, void* stream);
 
+/* compact_tree_path with the accepted list and its length in device memory
+ * (written by axb_tree_accept: accepted = result + AXB_TREE_RESULT_HDR,
+ * n_accepted_dev = result), so no host round trip sits between the walk and
+ * the compaction.  max_accepted (<= 64) bounds the count and sizes the
+ * staging; an identity path (acc[m] == m) moves nothing. */
+int axb_compact_kv_dev(void* cache_dev, uint16_t* scales_dev, int n_layer, int max_batch, int n_kv_head,
+                       int max_seq, int row_bytes, int n_groups, int write_pos, const int32_t* accepted_dev,
+                       const int32_t* n_accepted_dev, int max_accepted, void* stream);
+
 /* Greedy argmax over rows (ties -> lowest index, torch.argmax). */
 int axb_argmax(const uint16_t* x_dev, int rows, int n, int ld, int32_t* out_dev, void* stream);
 
@@ -343,6 +352,42 @@ int axb_runner_step(void* handle, int B, int T, int rope_pos, int write_pos, int
  * kernel launch, 0 when they run as the per-kernel CUDA graph (unsupported
  * format, or AXB_STEP=0 in the environment at creation). */
 int axb_runner_uses_step_kernel(void* handle);
+
+/* ---- Medusa speculative decoding on the device (engine/medusa.py:48-116,
+ *      :231-330, models/medusa.py:20-54, transformer.py:414-445) ----------- */
+#define AXB_TREE_MAX_NODES 64 /* uint64 ancestor masks */
+#define AXB_TREE_RESULT_HDR 4
+/* result block of axb_tree_accept (int32): [0] accepted node count n (>= 1),
+ * [1] last accepted node (the next draft's leaf), [2] emitted token count
+ * (== n), [3] last emitted token, then AXB_TREE_MAX_NODES accepted node ids
+ * (node 0 first) and AXB_TREE_MAX_NODES emitted tokens. */
+#define AXB_TREE_RESULT_WORDS (AXB_TREE_RESULT_HDR + 2 * AXB_TREE_MAX_NODES)
+#define AXB_TOPK_MAX 64
+/* Greedy walk of engine/medusa.py:312-330 over a tree of T nodes: at node
+ * cur emit preds[cur]; descend to the first child c (children = nodes with
+ * parent[c] == cur, in increasing index order, as compile_medusa_tree lists
+ * them) whose draft token verif[c] equals it; stop when none does or after
+ * `budget` (>= 1) emitted tokens.  parent[0] = -1 and parent[u] < u.  All
+ * arrays are device int32 (preds: the runner's per-node argmax). */
+int axb_tree_accept(int T, const int32_t* parent, const int32_t* verif, const int32_t* preds, int budget,
+                    int32_t* result, void* stream);
+/* Head input of the next draft: x32 = norm[leaf] (fp32 final-norm rows of
+ * width d), x16 = fp16(x32).  leaf_dev (device int32, e.g. result + 1) wins
+ * over the host index `leaf` when non-NULL. */
+int axb_medusa_leaf(const float* norm, int d, const int32_t* leaf_dev, int leaf, float* x32, uint16_t* x16,
+                    void* stream);
+/* Residual Medusa heads (MedusaHead.forward with use_residual): for each of
+ * the K heads, h16[k] = fp16(x32 + silu(r16[k])) with r16[k] = the fp16
+ * output of that head's residual GEMV on x16 (all fp32 math). */
+int axb_medusa_silu_add(int K, int d, const float* x32, const uint16_t* r16, uint16_t* h16, void* stream);
+/* Top-k indices of each fp16 row (k <= AXB_TOPK_MAX), by value descending,
+ * equal values by lower index (torch.topk leaves tie order open): out_idx is
+ * (rows, k) int32. */
+int axb_topk_rows(const uint16_t* x, int rows, int n, int ld, int k, int32_t* out_idx, void* stream);
+/* Next draft (engine/medusa.py:290-298): tokens[0] = *root (the last emitted
+ * token), tokens[u] = topk[head_idx[u] * kmax + rank[u]] for u >= 1. */
+int axb_draft_tokens(int T, const int32_t* head_idx, const int32_t* rank, const int32_t* topk, int kmax,
+                     const int32_t* root, int32_t* tokens, void* stream);
 
 /* ---- tensor parallelism over NVLink (no counterpart in the reference, whose
  *      only collective is a training all_reduce, train.py:296) ------------- */
