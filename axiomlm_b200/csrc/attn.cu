@@ -406,140 +406,350 @@ size_t decode_smem(int kv_type, int hd) {
   return rows + rest;
 }
 
-// Tree / chunked-prefill attention: T query tokens per sequence, each sees the
-// prefix [0, prefix_len) and tree slot write_pos + j iff bit j of masks[t].
-// grid (ceil(T / TQ), Hkv, B); 128 threads; rows = TQ tokens x n_rep heads <= 16.
-constexpr int kTreeRows = 16;
-constexpr int kTreeKeys = 32;
-// Split-K over the keys: with nsplit > 1, CTA (tile, split) covers keys
+// Tree / chunked-prefill attention on the tensor cores: T query tokens per
+// sequence, each sees the prefix [0, prefix_len) and tree slot write_pos + j
+// iff bit j of masks[t].  Query rows are (token, head) pairs of one KV head,
+// token-major; a CTA of 4 warps takes 64 rows (16 per warp) against 64-key
+// tiles, flash-attention style:
+//  * K and V tiles are staged as exact fp16 codes (fp16 values, e4m3 codes, or
+//    int4 codes (n ^ 8) - 8) with their per-(token, group) scales;
+//  * S = q K^T with q as fp16 hi + lo (m16n8k16, fp32 accumulate), each K
+//    scale group's partial sum multiplied by the token's scale;
+//  * online softmax in registers (the C fragment of S is the A fragment of P);
+//  * O += P V with the V scale folded into P (normalized by the tile's largest
+//    scale of the group, so P' stays in [0, 1]) and P' as hi + lo.
+// Split-K over the keys: with nsplit > 1, CTA (rows, split) covers keys
 // [split * chunk, ...) and writes its unnormalized (O, m, l) to po / pml
 // (tree_combine_kernel merges the splits in order); with nsplit == 1 it
 // writes the output directly.
+constexpr int kTreeRows = 64;  // query rows per CTA (4 warps x 16)
+constexpr int kTreeKeys = 64;  // keys per tile
+
+template <int HD>
+struct TreeSmem {
+  static constexpr int LD = HD + 8;  // fp16 row pitch: conflict-free ldmatrix / fragment loads
+  static constexpr int kQ = 0;                                  // [hi, lo][64 rows][LD] fp16
+  static constexpr int kK = kQ + 2 * kTreeRows * LD * 2;        // [64 keys][LD] fp16 codes
+  static constexpr int kV = kK + kTreeKeys * LD * 2;            // [64 keys][LD]
+  static constexpr int kKs = kV + kTreeKeys * LD * 2;           // [64 keys][8 groups] fp32 K scales
+  static constexpr int kVs = kKs + kTreeKeys * 8 * 4;           // [64 keys][8 groups] fp32 V scales
+  static constexpr int kVmax = kVs + kTreeKeys * 8 * 4;         // [8 groups] fp32
+  static constexpr int kMask = kVmax + 8 * 4;                   // [64 rows] uint64
+  static constexpr int kBytes = kMask + kTreeRows * 8;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// fp32 pair -> fp16 (hi, lo) pairs with hi + lo = the value to about 22 bits
+__device__ __forceinline__ void tree_split_h2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 hf = __half22float2(h);
+  hi = h2_as_u32(h);
+  lo = h2_as_u32(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
+}
+// 16 exact fp16 codes of a staged row piece: fp16 copy, e4m3 -> fp16, int4 (n ^ 8) - 8
+__device__ __forceinline__ void tree_codes16(const uint8_t* src, int type, uint4 (&o)[2]) {
+  if (type == AXB_KV_F16) {
+    o[0] = reinterpret_cast<const uint4*>(src)[0];
+    o[1] = reinterpret_cast<const uint4*>(src)[1];
+  } else if (type == AXB_KV_FP8) {
+    const uint4 a = *reinterpret_cast<const uint4*>(src);
+    const uint16_t* u = reinterpret_cast<const uint16_t*>(&a);
+    uint32_t* w = reinterpret_cast<uint32_t*>(o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(u[i], __NV_E4M3);
+      w[i] = (uint32_t)h.x | ((uint32_t)h.y << 16);
+    }
+  } else {
+    const uint2 a = *reinterpret_cast<const uint2*>(src);
+    const uint8_t* cb = reinterpret_cast<const uint8_t*>(&a);
+    uint32_t* w = reinterpret_cast<uint32_t*>(o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {  // low nibble = element 2i, high = 2i + 1
+      const uint32_t c = cb[i];
+      const uint32_t t = (((c & 0xFu) | ((c & 0xF0u) << 12)) ^ 0x00080008u) | 0x64006400u;
+      w[i] = h2_as_u32(__hsub2(u32_as_h2(t), __float2half2_rn(1032.f)));
+    }
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(128) tree_attn_kernel(axb_attn_desc d, int nsplit, int chunk, float* po, float* pml) {
+  using SM = TreeSmem<HD>;
+  constexpr int LD = SM::LD, KS = HD / 16, NBO = HD / 8;
+  extern __shared__ __align__(16) char tsm[];
+  __half* q_s = reinterpret_cast<__half*>(tsm + SM::kQ);
+  __half* k_s = reinterpret_cast<__half*>(tsm + SM::kK);
+  __half* v_s = reinterpret_cast<__half*>(tsm + SM::kV);
+  float* ks_s = reinterpret_cast<float*>(tsm + SM::kKs);
+  float* vs_s = reinterpret_cast<float*>(tsm + SM::kVs);
+  float* vmax_s = reinterpret_cast<float*>(tsm + SM::kVmax);
+  unsigned long long* mask_s = reinterpret_cast<unsigned long long*>(tsm + SM::kMask);
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int n_rep = d.n_head / d.n_kv_head;
-  const int TQ = max(1, kTreeRows / n_rep);
   const int split = blockIdx.x % nsplit;
-  const int u0 = (blockIdx.x / nsplit) * TQ;
-  const int nu = min(TQ, d.T - u0);
-  const int R = nu * n_rep;
-  const int tid = threadIdx.x;
+  const int r0 = (blockIdx.x / nsplit) * kTreeRows;  // first (token, head) row of the CTA
+  const int R = min(kTreeRows, d.T * n_rep - r0);
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, c = lane & 3;
+  const bool quant = d.kv_type != AXB_KV_F16;
+  const int G = quant ? d.kv_group : HD, ng = HD / G;
   const float sm_scale = 1.0f / sqrtf((float)HD);
-  __shared__ float q_s[kTreeRows][HD + 1];
-  __shared__ float k_s[kTreeKeys][HD + 1];
-  __shared__ float v_s[kTreeKeys][HD + 1];
-  __shared__ float p_s[kTreeRows][kTreeKeys + 1];
-  __shared__ float m_s[kTreeRows], l_s[kTreeRows], c_s[kTreeRows];
-  __shared__ unsigned long long mask_s[kTreeRows];
   pdl_wait();
   if (d.dev_params) {
     d.write_pos = d.dev_params[1];
     d.prefix_len = d.dev_params[3];
   }
-  for (int i = tid; i < R * HD; i += 128) {
-    int r = i / HD, e = i % HD;
-    int u = u0 + r / n_rep, hq = kvh * n_rep + r % n_rep;
-    size_t qi = (((size_t)b * d.T + u) * d.n_head + hq) * HD + e;
-    q_s[r][e] = d.q_is_fp32 ? reinterpret_cast<const float*>(d.q)[qi]
-                            : __half2float(reinterpret_cast<const __half*>(d.q)[qi]);
+  // ---- q rows as fp16 hi / lo (rows past R zero), masks
+  for (int i = tid; i < kTreeRows * (HD / 2); i += 128) {
+    const int r = i / (HD / 2), e = 2 * (i % (HD / 2));
+    float x0 = 0.f, x1 = 0.f;
+    if (r < R) {
+      const int u = (r0 + r) / n_rep, hq = kvh * n_rep + (r0 + r) % n_rep;
+      const size_t qi = (((size_t)b * d.T + u) * d.n_head + hq) * HD + e;
+      if (d.q_is_fp32) {
+        const float2 f = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(d.q) + qi);
+        x0 = f.x;
+        x1 = f.y;
+      } else {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(d.q) + qi));
+        x0 = f.x;
+        x1 = f.y;
+      }
+    }
+    uint32_t hi, lo;
+    tree_split_h2(x0, x1, hi, lo);
+    *reinterpret_cast<uint32_t*>(q_s + r * LD + e) = hi;
+    *reinterpret_cast<uint32_t*>(q_s + (kTreeRows + r) * LD + e) = lo;
   }
-  if (tid < R) {
-    m_s[tid] = -INFINITY;
-    l_s[tid] = 0.f;
-    mask_s[tid] = d.masks[u0 + tid / n_rep];
-  }
+  for (int r = tid; r < kTreeRows; r += 128) mask_s[r] = r < R ? d.masks[(r0 + r) / n_rep] : 0ull;
+
   const int rb = kv_row_bytes(d.kv_type, HD);
-  const int G = d.kv_group, ng = HD / G;
   const size_t head_base = ((size_t)b * d.n_kv_head + kvh) * d.max_seq;
   const uint8_t* kc = reinterpret_cast<const uint8_t*>(d.k_cache) + head_base * rb;
   const uint8_t* vc = reinterpret_cast<const uint8_t*>(d.v_cache) + head_base * rb;
-  const __half* ks = d.k_scale ? reinterpret_cast<const __half*>(d.k_scale) + head_base * ng : nullptr;
-  const __half* vs = d.v_scale ? reinterpret_cast<const __half*>(d.v_scale) + head_base * ng : nullptr;
-  // thread -> (row, dims) for PV: 8 threads per row, HD/8 dims each
-  constexpr int DPT = HD / 8;
-  float acc[DPT];
+  const __half* ksg = quant ? reinterpret_cast<const __half*>(d.k_scale) + head_base * ng : nullptr;
+  const __half* vsg = quant ? reinterpret_cast<const __half*>(d.v_scale) + head_base * ng : nullptr;
+  // code bytes of 16 elements, and pieces of 16 elements per row
+  constexpr int PPR = HD / 16;
+  const int piece_bytes = d.kv_type == AXB_KV_F16 ? 32 : (d.kv_type == AXB_KV_FP8 ? 16 : 8);
+
+  // this thread's rows g and g + 8 of the warp's 16: online-softmax state
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  float oacc[NBO][4];
 #pragma unroll
-  for (int e = 0; e < DPT; ++e) acc[e] = 0.f;
-  const int my_r = tid >> 3, my_d0 = (tid & 7) * DPT;
-  __syncthreads();
+  for (int nb = 0; nb < NBO; ++nb)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) oacc[nb][q] = 0.f;
+  const uint32_t q_base = smem_u32(q_s), k_base = smem_u32(k_s), v_base = smem_u32(v_s);
+  const int mrow = lane & 7, msel = lane >> 3;  // ldmatrix: this lane's row within matrix msel
+
   const int n_keys_all = d.prefix_len + d.T;
   const int k_begin = split * chunk, n_keys = min(n_keys_all, k_begin + chunk);
   for (int kt = k_begin; kt < n_keys; kt += kTreeKeys) {
     const int nk = min(kTreeKeys, n_keys - kt);
-    // stage dequantized K/V (scales applied) for the key tile
-    for (int i = tid; i < nk * HD; i += 128) {
-      int kk = i / HD, e = i % HD;
-      int key = kt + kk;
-      int slot = key < d.prefix_len ? key : (d.write_pos + key - d.prefix_len) % d.max_seq;
-      float sk = ks ? __half2float(ks[(size_t)slot * ng + e / G]) : 1.f;
-      float sv = vs ? __half2float(vs[(size_t)slot * ng + e / G]) : 1.f;
-      k_s[kk][e] = kv_elem(kc + (size_t)slot * rb, d.kv_type, e) * sk;
-      v_s[kk][e] = kv_elem(vc + (size_t)slot * rb, d.kv_type, e) * sv;
-    }
-    __syncthreads();
-    for (int i = tid; i < kTreeRows * kTreeKeys; i += 128) {
-      int r = i / kTreeKeys, kk = i % kTreeKeys;
-      float sc = -INFINITY;
-      if (r < R && kk < nk) {
-        int key = kt + kk;
-        bool vis = key < d.prefix_len || ((mask_s[r] >> (key - d.prefix_len)) & 1ull);
-        if (vis) {
-          float a = 0.f;
-#pragma unroll 8
-          for (int e = 0; e < HD; ++e) a = __fmaf_rn(q_s[r][e], k_s[kk][e], a);
-          sc = a * sm_scale;
-        }
+    __syncthreads();  // the previous tile's K / V are no longer read
+    // ---- stage the tile: codes as fp16, scales as fp32 (keys past nk: zeros)
+    for (int i = tid; i < 2 * kTreeKeys * PPR; i += 128) {
+      const int isv = i / (kTreeKeys * PPR), j = (i / PPR) % kTreeKeys, p = i % PPR;
+      uint4 o[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+      if (j < nk) {
+        const int key = kt + j;
+        const int slot = key < d.prefix_len ? key : (d.write_pos + key - d.prefix_len) % d.max_seq;
+        tree_codes16((isv ? vc : kc) + (size_t)slot * rb + p * piece_bytes, d.kv_type, o);
       }
-      p_s[r][kk] = sc;
+      __half* dst = (isv ? v_s : k_s) + j * LD + 16 * p;
+      reinterpret_cast<uint4*>(dst)[0] = o[0];
+      reinterpret_cast<uint4*>(dst)[1] = o[1];
+    }
+    if (quant) {
+      for (int i = tid; i < 2 * kTreeKeys * ng; i += 128) {
+        const int isv = i / (kTreeKeys * ng), j = (i / ng) % kTreeKeys, gi = i % ng;
+        float sc = 0.f;
+        if (j < nk) {
+          const int key = kt + j;
+          const int slot = key < d.prefix_len ? key : (d.write_pos + key - d.prefix_len) % d.max_seq;
+          sc = __half2float((isv ? vsg : ksg)[(size_t)slot * ng + gi]);
+        }
+        (isv ? vs_s : ks_s)[j * 8 + gi] = sc;
+      }
     }
     __syncthreads();
-    // online softmax: warp w handles rows w, w+4, ...
+    if (quant && w == 0) {  // the tile's largest V scale per group
+      for (int gi = 0; gi < ng; ++gi) {
+        float mx = fmaxf(vs_s[lane * 8 + gi], vs_s[(lane + 32) * 8 + gi]);
+        mx = warp_max(mx);
+        if (lane == 0) vmax_s[gi] = mx > 0.f ? mx : 1.f;
+      }
+    }
+    // ---- S = q K^T (16 rows x 64 keys per warp)
+    float s[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) s[nb][q] = 0.f;
     {
-      const int lane = tid & 31, wid = tid >> 5;
-      for (int r = wid; r < R; r += 4) {
-        float v = p_s[r][lane];
-        float mx = warp_max(v);
-        float m_old = m_s[r], m_new = fmaxf(m_old, mx);
-        float e = (v == -INFINITY) ? 0.f : __expf(v - m_new);
-        p_s[r][lane] = e;
-        float sum = warp_sum(e);
-        if (lane == 0) {
-          float c = (m_old == -INFINITY) ? ((m_new == -INFINITY) ? 1.f : 0.f) : __expf(m_old - m_new);
-          c_s[r] = c;
-          l_s[r] = l_s[r] * c + sum;
-          m_s[r] = m_new;
+      float gacc[8][4];
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) gacc[nb][q] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t ahi[4], alo[4];
+        {
+          // A: m0 rows 0-7 / k 0-7, m1 rows 8-15 / k 0-7, m2 rows 0-7 / k 8-15, m3 rows 8-15 / k 8-15
+          const int row = w * 16 + 8 * (msel & 1) + mrow, col = 16 * ks + 8 * (msel >> 1);
+          ldsm_x4(ahi, q_base + (uint32_t)(row * LD + col) * 2);
+          ldsm_x4(alo, q_base + (uint32_t)((kTreeRows + row) * LD + col) * 2);
+        }
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          // B (K^T): m0 keys 0-7 / k 0-7, m1 keys 0-7 / k 8-15, m2 keys 8-15 / k 0-7, m3 keys 8-15 / k 8-15
+          uint32_t kb[4];
+          const int key = 16 * np + 8 * (msel >> 1) + mrow, col = 16 * ks + 8 * (msel & 1);
+          ldsm_x4(kb, k_base + (uint32_t)(key * LD + col) * 2);
+          mma_16816(gacc[2 * np], ahi, kb[0], kb[1], gacc[2 * np]);
+          mma_16816(gacc[2 * np], alo, kb[0], kb[1], gacc[2 * np]);
+          mma_16816(gacc[2 * np + 1], ahi, kb[2], kb[3], gacc[2 * np + 1]);
+          mma_16816(gacc[2 * np + 1], alo, kb[2], kb[3], gacc[2 * np + 1]);
+        }
+        if ((16 * (ks + 1)) % G == 0) {  // a K scale group is complete: fold it in with each key's scale
+          const int gi = (16 * ks) / G;
+#pragma unroll
+          for (int nb = 0; nb < 8; ++nb) {
+            const int j0 = 8 * nb + 2 * c;
+            const float s0 = quant ? ks_s[j0 * 8 + gi] : 1.f, s1 = quant ? ks_s[(j0 + 1) * 8 + gi] : 1.f;
+            s[nb][0] = __fmaf_rn(gacc[nb][0], s0, s[nb][0]);
+            s[nb][1] = __fmaf_rn(gacc[nb][1], s1, s[nb][1]);
+            s[nb][2] = __fmaf_rn(gacc[nb][2], s0, s[nb][2]);
+            s[nb][3] = __fmaf_rn(gacc[nb][3], s1, s[nb][3]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) gacc[nb][q] = 0.f;
+          }
         }
       }
     }
-    __syncthreads();
-    if (my_r < R) {
-      float c = c_s[my_r];
+    // ---- visibility, scale, online softmax (rows g: q 0/1, g + 8: q 2/3)
+    const unsigned long long mk[2] = {mask_s[w * 16 + g], mask_s[w * 16 + g + 8]};
+    float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-      for (int e = 0; e < DPT; ++e) acc[e] *= c;
-      for (int kk = 0; kk < nk; ++kk) {
-        float p = p_s[my_r][kk];
+    for (int nb = 0; nb < 8; ++nb)
 #pragma unroll
-        for (int e = 0; e < DPT; ++e) acc[e] = __fmaf_rn(p, v_s[kk][my_d0 + e], acc[e]);
+      for (int q = 0; q < 4; ++q) {
+        const int j = 8 * nb + 2 * c + (q & 1), key = kt + j;
+        const int hr = q >> 1;
+        const bool vis = j < nk && (key < d.prefix_len || ((mk[hr] >> (key - d.prefix_len)) & 1ull));
+        s[nb][q] = vis ? s[nb][q] * sm_scale : -INFINITY;
+        mx[hr] = fmaxf(mx[hr], s[nb][q]);
       }
+    float alpha[2];
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
+      mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
+      const float m_new = fmaxf(m_r[hr], mx[hr]);
+      alpha[hr] = m_new == -INFINITY ? 1.f : (m_r[hr] == -INFINITY ? 0.f : __expf(m_r[hr] - m_new));
+      m_r[hr] = m_new;
     }
-    __syncthreads();
+    float lsum[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int hr = q >> 1;
+        const float p = s[nb][q] == -INFINITY ? 0.f : __expf(s[nb][q] - m_r[hr]);
+        s[nb][q] = p;
+        lsum[hr] += p;
+      }
+    l_r[0] = l_r[0] * alpha[0] + lsum[0];
+    l_r[1] = l_r[1] * alpha[1] + lsum[1];
+    if (quant) __syncthreads();  // vmax_s
+    // ---- O = alpha O + vmax (P' V), P' = p vscale / vmax, per V scale group
+#pragma unroll
+    for (int gi = 0; gi < HD / 16; ++gi) {  // at most ng groups; G >= 16
+      if (gi >= ng) break;
+      const float vm = quant ? vmax_s[gi] : 1.f, inv = 1.f / vm;
+      const int nb0 = gi * (G / 8), nb1 = nb0 + G / 8;
+      // rescale this group's accumulators into units of vm
+#pragma unroll
+      for (int nb = 0; nb < NBO; ++nb)
+        if (nb >= nb0 && nb < nb1) {
+          oacc[nb][0] *= alpha[0] * inv;
+          oacc[nb][1] *= alpha[0] * inv;
+          oacc[nb][2] *= alpha[1] * inv;
+          oacc[nb][3] *= alpha[1] * inv;
+        }
+#pragma unroll
+      for (int kq = 0; kq < 4; ++kq) {  // 16 keys per k-step
+        float pv[2][4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int j = 16 * kq + 8 * h + 2 * c + (q & 1);
+            pv[h][q] = quant ? s[2 * kq + h][q] * (vs_s[j * 8 + gi] * inv) : s[2 * kq + h][q];
+          }
+        uint32_t phi[4], plo[4];
+        tree_split_h2(pv[0][0], pv[0][1], phi[0], plo[0]);  // row g, keys 2c, 2c + 1
+        tree_split_h2(pv[0][2], pv[0][3], phi[1], plo[1]);  // row g + 8
+        tree_split_h2(pv[1][0], pv[1][1], phi[2], plo[2]);  // row g, keys 8 + 2c
+        tree_split_h2(pv[1][2], pv[1][3], phi[3], plo[3]);  // row g + 8, keys 8 + 2c
+#pragma unroll
+        for (int nb = 0; nb < NBO; nb += 2)
+          if (nb >= nb0 && nb < nb1) {
+            // V (transposed): m0 keys 0-7 / dims nb, m1 keys 8-15 / dims nb, m2 / m3 the same for dims nb + 1
+            uint32_t vb[4];
+            const int key = 16 * kq + 8 * (msel & 1) + mrow, col = 8 * (nb + (msel >> 1));
+            ldsm_x4_t(vb, v_base + (uint32_t)(key * LD + col) * 2);
+            mma_16816(oacc[nb], phi, vb[0], vb[1], oacc[nb]);
+            mma_16816(oacc[nb], plo, vb[0], vb[1], oacc[nb]);
+            mma_16816(oacc[nb + 1], phi, vb[2], vb[3], oacc[nb + 1]);
+            mma_16816(oacc[nb + 1], plo, vb[2], vb[3], oacc[nb + 1]);
+          }
+      }
+#pragma unroll
+      for (int nb = 0; nb < NBO; ++nb)
+        if (nb >= nb0 && nb < nb1)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) oacc[nb][q] *= vm;
+    }
   }
-  if (my_r < R) {
-    int u = u0 + my_r / n_rep, hq = kvh * n_rep + my_r % n_rep;
+  // ---- row sums across the quad; outputs
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 1);
+    l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 2);
+  }
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int r = w * 16 + g + 8 * hr;
+    if (r >= R) continue;
+    const int u = (r0 + r) / n_rep, hq = kvh * n_rep + (r0 + r) % n_rep;
     const size_t row = ((size_t)b * d.T + u) * d.n_head + hq;
     if (nsplit == 1) {
-      __half* o = reinterpret_cast<__half*>(d.out) + row * HD + my_d0;
-      float l = l_s[my_r];
+      __half* o = reinterpret_cast<__half*>(d.out) + row * HD;
+      const float l = l_r[hr];
 #pragma unroll
-      for (int e = 0; e < DPT; ++e) o[e] = __float2half_rn(__fdiv_rn(acc[e], l));
+      for (int nb = 0; nb < NBO; ++nb)
+        *reinterpret_cast<__half2*>(o + 8 * nb + 2 * c) =
+            __floats2half2_rn(__fdiv_rn(oacc[nb][2 * hr], l), __fdiv_rn(oacc[nb][2 * hr + 1], l));
     } else {
-      float* o = po + (row * nsplit + split) * HD + my_d0;
+      float* o = po + (row * nsplit + split) * HD;
 #pragma unroll
-      for (int e = 0; e < DPT; ++e) o[e] = acc[e];
-      if ((tid & 7) == 0) {
-        pml[(row * nsplit + split) * 2 + 0] = m_s[my_r];
-        pml[(row * nsplit + split) * 2 + 1] = l_s[my_r];
+      for (int nb = 0; nb < NBO; ++nb)
+        *reinterpret_cast<float2*>(o + 8 * nb + 2 * c) = make_float2(oacc[nb][2 * hr], oacc[nb][2 * hr + 1]);
+      if (c == 0) {
+        pml[(row * nsplit + split) * 2 + 0] = m_r[hr];
+        pml[(row * nsplit + split) * 2 + 1] = l_r[hr];
       }
     }
   }
@@ -624,10 +834,10 @@ constexpr size_t kAttnHead = 256;  // error word
 
 // tree / chunked-prefill mode: splits of the key range and their partials
 int tree_splits(int B, int T, int n_head, int n_kv_head, int n_keys) {
-  const int n_rep = n_head / n_kv_head, TQ = std::max(1, kTreeRows / n_rep);
-  const int base = ((T + TQ - 1) / TQ) * n_kv_head * B;
-  int S = (5 * num_sms() + base - 1) / base;  // about five 43 KB CTAs per SM
-  S = std::min(S, std::max(1, n_keys / 128));
+  const int n_rep = n_head / n_kv_head;
+  const int base = ((T * n_rep + kTreeRows - 1) / kTreeRows) * n_kv_head * B;
+  int S = (3 * num_sms() + base - 1) / base;  // about three 73 KB CTAs per SM
+  S = std::min(S, std::max(1, n_keys / (2 * kTreeKeys)));
   return std::max(1, std::min(S, 64));
 }
 // The partials follow the workspace's fixed header (error word and the decode
@@ -677,6 +887,11 @@ int attn_prepare() {
   cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tree_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             TreeSmem<128>::kBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tree_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, TreeSmem<64>::kBytes);
   if (e != cudaSuccess) return cuda_status(e, "attention attribute");
   done_dev = dev;
   return AXB_OK;
@@ -725,8 +940,12 @@ int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s)
   }
   AXB_CHECK_ARG(d->T >= 1 && d->T <= 64, "attention: tree mode needs 1 <= T <= 64");
   AXB_CHECK_ARG(d->prefix_len >= 0 && d->prefix_len <= d->max_seq, "attention: bad prefix_len");
-  int n_rep = d->n_head / d->n_kv_head;
-  int TQ = std::max(1, kTreeRows / n_rep);
+  AXB_CHECK_ARG(d->kv_type == AXB_KV_F16 || (d->kv_group >= 16 && d->head_dim % d->kv_group == 0),
+                "attention: tree mode needs kv_group >= 16 dividing head_dim");
+  AXB_CHECK_ARG((reinterpret_cast<uintptr_t>(d->k_cache) & 15) == 0 && (reinterpret_cast<uintptr_t>(d->v_cache) & 15) == 0,
+                "attention: caches must be 16-byte aligned");
+  if (int rc = attn_prepare()) return rc;
+  const int n_rep = d->n_head / d->n_kv_head;
   // split the keys across CTAs when the workspace holds the partials; the
   // prefix length is read on the device, so the split plan uses its maximum
   int S = tree_splits(d->B, d->T, d->n_head, d->n_kv_head, d->max_seq);
@@ -736,12 +955,14 @@ int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s)
   float* po = S > 1 ? reinterpret_cast<float*>(tws) : nullptr;
   const size_t rows = (size_t)d->B * d->T * d->n_head;
   float* pml = S > 1 ? reinterpret_cast<float*>(tws + round_up(rows * S * d->head_dim * 4, 256)) : nullptr;
-  dim3 grid(((d->T + TQ - 1) / TQ) * S, d->n_kv_head, d->B);
+  dim3 grid(((d->T * n_rep + kTreeRows - 1) / kTreeRows) * S, d->n_kv_head, d->B);
   cudaError_t e;
   if (d->head_dim == 128)
-    e = launch_pdl(tree_attn_kernel<128>, grid, dim3(128), 0, s, d->pdl != 0, *d, S, chunk, po, pml);
+    e = launch_pdl(tree_attn_kernel<128>, grid, dim3(128), TreeSmem<128>::kBytes, s, d->pdl != 0, *d, S, chunk, po,
+                   pml);
   else
-    e = launch_pdl(tree_attn_kernel<64>, grid, dim3(128), 0, s, d->pdl != 0, *d, S, chunk, po, pml);
+    e = launch_pdl(tree_attn_kernel<64>, grid, dim3(128), TreeSmem<64>::kBytes, s, d->pdl != 0, *d, S, chunk, po,
+                   pml);
   if (e != cudaSuccess) return cuda_status(e, "tree attention launch");
   if (S > 1) {
     tree_combine_kernel<<<(unsigned)rows, 128, 0, s>>>(po, pml, S, d->head_dim, reinterpret_cast<__half*>(d->out));

@@ -295,6 +295,37 @@ def test_tree_attention_uint64_masks_vs_oracle(ax, T, kv):
     assert _rel(out.view(T, Hq * hd).cpu(), ref.transpose(1, 2).reshape(T, -1)) < REL_TOL
 
 
+@pytest.mark.parametrize("hd,kv,group,Hq,Hkv,T,write_pos", [
+    (64, "fp8", 64, 8, 8, 33, 150),      # MHA, head_dim 64
+    (128, "fp8", 128, 32, 8, 64, 150),   # one scale per (token, head)
+    (128, "int4", 32, 16, 2, 20, 200),   # 8:1 GQA, G32, tree slots apart from the prefix
+    (128, "int4", 64, 16, 4, 5, 150),
+    (64, "fp16", 64, 4, 1, 64, 180),     # 4:1 GQA over one KV head
+])
+def test_tree_attention_formats_vs_oracle(ax, hd, kv, group, Hq, Hkv, T, write_pos):
+    """Tensor-core tree attention over every cache format, group size, GQA
+    ratio and head size, with the tree's slots elsewhere in the cache."""
+    rng = np.random.default_rng(T + hd)
+    S, prefix = 256, 150
+    masks = [1]
+    for u in range(1, T):
+        masks.append(masks[int(rng.integers(0, u))] | (1 << u))
+    g = torch.Generator(device="cuda").manual_seed(T)
+    k = torch.randn(1, Hkv, S, hd, device="cuda", generator=g).half()
+    v = (torch.randn(1, Hkv, S, hd, device="cuda", generator=g) * 3).half()
+    q = torch.randn(1, T, Hq * hd, device="cuda", generator=g)
+    if kv == "fp16":
+        kc, vc, ks, vs, kd, vd = k, v, None, None, k, v
+    else:
+        kc, ks = ax.quantize_kv(k, kv, group)
+        vc, vs = ax.quantize_kv(v, kv, group)
+        kd, vd = ax.dequantize_kv(kc, ks, kv, hd), ax.dequantize_kv(vc, vs, kv, hd)
+    out = ax.gqa_tree_verify_mps(q, kc, vc, masks, prefix, write_pos, Hq, k_scales=ks, v_scales=vs, kv_dtype=kv)
+    q4 = q.view(1, T, Hq, hd).transpose(1, 2).cpu()
+    ref = O.attention_tree(q4, kd.float().cpu(), vd.float().cpu(), masks, prefix, write_pos)
+    assert _rel(out.view(T, Hq * hd).cpu(), ref.transpose(1, 2).reshape(T, -1)) < REL_TOL
+
+
 # ------------------------------------------------------------------ KV write / compaction
 
 @pytest.mark.parametrize("kv,group", [("fp16", 64), ("fp8", 64), ("int4", 64), ("fp8", 128), ("int4", 32)])
