@@ -7,22 +7,40 @@
 // M > 16.  At 64 tokens a Q4 weight byte feeds 256 flops, the B200's ridge:
 // the legacy warp-level mma path cannot keep up with HBM there.
 //
-// One CTA computes a 128-row x 64-token tile of y over a K range (split-K
-// across CTAs when the rows alone do not fill the GPU):
-//  * 4 warps dequantize the q4t weights of the CTA's 8 row tiles (one
-//    64-wide k-block per stage, loaded straight from HBM with 128-bit loads)
-//    into fp16 in shared memory -- the dequantized value is the reference's
-//    (fp16((q - 8) s) symmetric, fp16(q s + b) affine) -- and stage the
-//    activations; both in the canonical K-major no-swizzle layout (8-row x
-//    16-byte core matrices).
-//  * one thread issues tcgen05.mma (M = 128, N = 64, K = 16, fp16 in, fp32
-//    accumulate in tensor memory) and commits each stage to an mbarrier, so
-//    the warps fill the other stage while the tensor core works.
-//  * the epilogue reads the accumulator with tcgen05.ld (warp w: lanes 32w..),
-//    adds the bias and stores fp16 (or, split-K, fp32 partials that the last
-//    CTA of the row block sums in split order).
+// One CTA computes a 128-row x NT-token tile of y (NT = 32 or 64: the token
+// count rounded up) over a K range (split-K across CTAs when the rows alone
+// do not fill the GPU), with its warps specialized and linked by mbarriers --
+// no CTA-wide barrier in the k loop:
+//  * warp 8 streams the weights, two 64-wide k-blocks per slot, into a
+//    4-slot ring with one bulk copy per row tile (a q4t tile's k range is
+//    contiguous); a slot is released as soon as the dequantizing warps have
+//    read it;
+//  * warp 10 streams the NT-token activation blocks into a 3-slot ring (one
+//    copy per k-block), which a small pre-pass (tc_xlayout_kernel) has laid
+//    out in the tensor core's canonical K-major order, zero rows past M (a
+//    32-token width for M <= 32 halves this L2 traffic);
+//  * warps 0-7 (one row tile each; scales read from global memory a chunk
+//    ahead) dequantize the slot's weights to fp16 (the reference's values:
+//    fp16((q - 8) s) symmetric, fp16(q s + b) affine) into one of two operand
+//    stages, in the canonical no-swizzle layout with a 144-byte core-matrix
+//    pitch along K (16-byte rows of 8 lanes land in distinct banks), then
+//    signal the stage full;
+//  * warp 9 owns the tensor memory; its lane 0 issues tcgen05.mma (M = 128,
+//    N = NT, K = 16, fp32 accumulate) per stage and commits the stage's
+//    completion to the operand stage and the activation slot;
+//  * warps 0-7 finally read the accumulator with tcgen05.ld (warp w: lanes
+//    32 (w % 4).., tokens (NT / 2) (w / 4)..) and store fp16 (+ bias), or
+//    fp32 partials that tc_reduce_kernel sums in split order.
+// Measured limits (B200): with the dequantization and the MMAs both removed,
+// this copy-and-barrier skeleton alone streams about 2.4 TB/s; more
+// dequantizing warps, deeper rings, larger copies, three operand stages and
+// 256-row CTAs (halving the activation traffic) each left the time within a
+// few percent, so the ceiling is the per-SM handling of the bulk copies and
+// barrier hand-offs, not HBM.
 // Every mbarrier wait is bounded; a wait that runs out records AXB_ETIMEOUT,
-// waits (bounded) for the tensor core, frees the tensor memory and returns.
+// raises the CTA's abort flag (the other roles stop at their next stage),
+// waits (bounded) for the tensor core and the copies in flight, frees the
+// tensor memory and returns.
 #include <algorithm>
 
 #include "axb_common.cuh"
@@ -30,55 +48,69 @@
 
 namespace axb {
 
-constexpr int kTcRows = 128;  // weight rows per CTA (MMA M)
-constexpr int kTcTok = 64;    // tokens per CTA (MMA N)
-constexpr int kTcKC = 64;     // k per stage (one q4t k-block)
-constexpr int kTcStages = 2;  // dequantized weight (A) stages
-constexpr int kTcAhead = 3;   // chunks whose raw weights and activations are in flight ahead
-constexpr int kTcSlots = kTcAhead + kTcStages;  // raw / activation slots (a slot is held until its MMA is done)
-constexpr int kTcThreads = 256;  // 8 warps: warp w dequantizes row tile w of the CTA
-constexpr int kTcA = kTcRows * kTcKC * 2;  // 16 KB of fp16 weights per stage
-constexpr int kTcB = kTcTok * kTcKC * 2;   // 8 KB of fp16 activations per slot
-constexpr int kTcRawW = 8 * 512;           // q4t words of the CTA's 8 tiles per chunk
-constexpr int kTcRawS = 8 * 8 * 8;         // their scales (affine: 8 x (s, b, s, b) per tile)
-constexpr int kTcRaw = kTcRawW + kTcRawS;
-constexpr int kTcSmem = kTcStages * kTcA + kTcSlots * (kTcB + kTcRaw) + 128;
-constexpr int kTcCols = 64;  // tensor-memory columns: 64 fp32 tokens x 128 lanes
+constexpr int kTcHalf = 128;              // MMA M: rows per accumulator
+constexpr int kTcHalves = 1;              // 128-row accumulators per CTA
+constexpr int kTcRows = kTcHalves * kTcHalf;  // weight rows per CTA
+constexpr int kTcTiles = kTcRows / 16;    // q4t row tiles per CTA
+constexpr int kTcTok = 64;                // largest MMA N (tokens per CTA)
+constexpr int kTcKC = 64;                 // k per chunk (one q4t k-block; one operand stage)
+constexpr int kTcSlotK = 2;               // k-blocks per weight slot
+constexpr int kTcWSlots = 4;              // weight ring slots (released once dequantized)
+constexpr int kTcXSlots = 3;              // activation ring slots, one k-block each (released when its MMAs are done)
+constexpr int kTcStages = 2;              // dequantized operand stages
+constexpr int kTcDqWarps = kTcTiles;      // dequantize / epilogue warps
+constexpr int kTcWarpW = kTcDqWarps, kTcWarpMma = kTcDqWarps + 1, kTcWarpX = kTcDqWarps + 2;
+constexpr int kTcThreads = 32 * (kTcDqWarps + 3);
+constexpr int kTcX = kTcTok * kTcKC * 2;          // 8 KB activation block per k-block (64 token rows)
+constexpr int kTcWSlot = kTcTiles * kTcSlotK * 512;  // q4t words of the CTA's tiles per slot
+constexpr int kTcXSlot = kTcX;
+constexpr int kTcAK = 144;                // operand stage: core-matrix pitch along K (bytes)
+constexpr int kTcAM = 8 * kTcAK;          // ... and along M (8-row groups)
+constexpr int kTcAHalf = (kTcHalf / 8) * kTcAM;   // 18 KB per 128-row half
+constexpr int kTcA = kTcHalves * kTcAHalf;
+constexpr int kTcSmem = kTcWSlots * kTcWSlot + kTcXSlots * kTcXSlot + kTcStages * kTcA + 256;
 constexpr uint32_t kTcWaitLimit = 1u << 24;
 // instruction descriptor (kind::f16): D fp32, A and B fp16, both K-major,
-// N = 64 (bits 17-22: N / 8), M = 128 (bits 24-28: M / 16)
-constexpr uint32_t kTcIdesc = (1u << 4) | ((uint32_t)(kTcTok >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+// N (bits 17-22: N / 8), M = 128 (bits 24-28: M / 16)
+__host__ __device__ constexpr uint32_t tc_idesc(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcHalf >> 4) << 24);
+}
 
 struct TcArgs {
   const uint32_t* words;
   const __half* scales;
-  const __half* x;
+  const __half* xl;  // activations in the canonical layout: [K / 64][8 KB]
   const __half* bias;
   __half* y;
   float* part;  // split-K partials [S][M][N] (summed by tc_reduce_kernel), or null
   int* err;
-  int N, K, M, ldx, ldy, G;
+  int N, K, M, ldy, G;
 };
 
-// byte offset of element (r, k) of a stage tile: core matrices of 8 rows x
-// 16 bytes; the two core matrices of one 16-wide k step are 128 B apart
-// (leading byte offset), 8-row groups 1024 B apart (stride byte offset)
+// byte offset of element (n, k) of an activation block: core matrices of 8
+// rows x 16 bytes, 128 B apart along K (leading byte offset), 1024 B apart
+// along N (stride byte offset); the first NT rows are the first NT * 128 bytes
 __device__ __forceinline__ uint32_t tc_off(int r, int k) {
   return (uint32_t)((r >> 3) * 1024 + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
 }
+// byte offset of 16-byte row piece (r, k .. k + 7) of a 128-row operand half
+__device__ __forceinline__ uint32_t tc_aoff(int r, int k) {
+  return (uint32_t)((r >> 3) * kTcAM + (k >> 3) * kTcAK + (r & 7) * 16);
+}
 
-// shared-memory matrix descriptor: start >> 4, LBO 128 B, SBO 1024 B,
-// descriptor version 1 (bits 46-47), no swizzle
-__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+// shared-memory matrix descriptor: start >> 4, leading (K) and stride (M/N)
+// byte offsets >> 4, descriptor version 1 (bits 46-47), no swizzle
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
          ((uint64_t)1 << 46);
 }
 
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                       uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(kTcIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -86,197 +118,283 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-// 16-byte asynchronous copy global -> shared; src_bytes 0 writes zeros
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+// 16 consecutive fp32 accumulator columns of this warp's 32 lanes
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 
-template <bool SYM, int GB>
+// activations x (M x K, row pitch ldx) -> [K / 64] blocks of 64 tokens x 64 k
+// in the canonical K-major layout, zero rows past M
+__global__ void tc_xlayout_kernel(const __half* __restrict__ x, int M, int K, int ldx, __half* __restrict__ xl) {
+  const int KB = K / kTcKC;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < KB * kTcTok * 8; i += gridDim.x * blockDim.x) {
+    const int kb = i / (kTcTok * 8), n = (i / 8) % kTcTok, kc = i % 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (n < M) v = *reinterpret_cast<const uint4*>(x + (size_t)n * ldx + kb * kTcKC + kc * 8);
+    *reinterpret_cast<uint4*>(reinterpret_cast<char*>(xl) + (size_t)kb * kTcX + tc_off(n, kc * 8)) = v;
+  }
+}
+
+template <bool SYM, int GB, int NT>
 __global__ void __launch_bounds__(kTcThreads) qgemm_tc_kernel(const TcArgs a) {
+  constexpr int kCols = kTcHalves * NT < 32 ? 32 : kTcHalves * NT;  // tensor-memory columns: each half's NT fp32 tokens
+  constexpr uint32_t kIdesc = tc_idesc(NT);
   extern __shared__ __align__(1024) char smem[];
-  char* stA = smem;                                    // [stage][kTcA] dequantized weights
-  char* stB = smem + kTcStages * kTcA;                 // [slot][kTcB] activations (operand layout)
-  char* raw = stB + kTcSlots * kTcB;                   // [slot][kTcRaw] q4t words + scales
-  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + kTcSlots * kTcRaw);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kTcStages);
+  char* wring = smem;                                  // [slot][16 tiles][kTcSlotK k-blocks] q4t words
+  char* xring = wring + kTcWSlots * kTcWSlot;          // [slot][NT rows of an 8 KB block] activations
+  char* stA = xring + kTcXSlots * kTcXSlot;            // [stage][2 halves][kTcAHalf] dequantized weights
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(stA + kTcStages * kTcA);  // [slot] copies landed
+  uint64_t* wempty = wfull + kTcWSlots;                // [slot] dequantized by every warp
+  uint64_t* xfull = wempty + kTcWSlots;                // [slot] copies landed
+  uint64_t* xempty = xfull + kTcXSlots;                // [slot] its MMAs are done
+  uint64_t* afull = xempty + kTcXSlots;                // [stage] dequantized
+  uint64_t* aempty = afull + kTcStages;                // [stage] its MMAs are done
+  uint64_t* done = aempty + kTcStages;                 // every MMA is done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int tid = threadIdx.x, wid = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int KB = a.K / kTcKC, Nt = (a.N + 15) / 16;
   const int rb = blockIdx.x, S = gridDim.y, sp = blockIdx.y;
   const int kb0 = (int)((long long)sp * KB / S), kb1 = (int)((long long)(sp + 1) * KB / S);
   const int nch = kb1 - kb0;
-  constexpr int SB = SYM ? 32 : 64;  // scale bytes per (tile, group)
+  const int ntiles = min(kTcTiles, Nt - rb * kTcTiles);
 
-  if (wid == 0) {
+  if (wid == kTcWarpMma) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTcCols)
+                 "r"(kCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    for (int s = 0; s < kTcStages; ++s) mbar_init(bars + s, 1);
+    for (int s = 0; s < kTcWSlots; ++s) {
+      mbar_init(wfull + s, 1);
+      mbar_init(wempty + s, kTcDqWarps);
+    }
+    for (int s = 0; s < kTcXSlots; ++s) {
+      mbar_init(xfull + s, 1);
+      mbar_init(xempty + s, 1);
+    }
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(afull + s, kTcDqWarps);
+      mbar_init(aempty + s, 1);
+    }
+    mbar_init(done, 1);
+    *abort_s = 0;
     fence_mbar_init();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  bool ok = true;
 
-  // one chunk's asynchronous copies into slot `sl`: the 8 tiles' words
-  // (8 x 512 B) and scales, and the 64 x 64 activation tile straight into the
-  // operand layout (zeros beyond M); one commit group per chunk, empty past the end
-  auto issue = [&](int c) {
-    if (c < nch) {
-      const int kb = kb0 + c, sl = c % kTcSlots;
-      char* rw = raw + sl * kTcRaw;
-      char* bm = stB + sl * kTcB;
-      const int grp = (kb * kTcKC) / a.G;
-      for (int i = tid; i < 8 * 32; i += kTcThreads) {  // words: tile i / 32, 16-byte piece i % 32
-        const int tl = i >> 5, tile = rb * 8 + tl;
-        const bool v = tile < Nt;
-        const char* src = reinterpret_cast<const char*>(a.words) +
-                          (((size_t)(v ? tile : 0) * KB + kb) * 512 + (i & 31) * 16);
-        cp_async16(rw + i * 16, src, v ? 16u : 0u);
+  const int nfill = (nch + kTcSlotK - 1) / kTcSlotK;
+  if (wid == kTcWarpW || wid == kTcWarpX) {
+    // ---- producers: the weight warp streams the row tiles' words (a copy per
+    // tile and slot), the activation warp the NT-row activation blocks
+    const bool isw = wid == kTcWarpW;
+    const int nsl = isw ? kTcWSlots : kTcXSlots, nf = isw ? nfill : nch;
+    uint64_t* fullb = isw ? wfull : xfull;
+    uint64_t* emptyb = isw ? wempty : xempty;
+    int f = 0;
+    for (; f < nf; ++f) {
+      const int sl = f % nsl;
+      if (f >= nsl) {
+        // every lane that issues a copy into the slot observes its release
+        const bool got = __all_sync(0xffffffffu, mbar_wait(emptyb + sl, (uint32_t)((f / nsl - 1) & 1),
+                                                           kTcWaitLimit));
+        if (!got || *abort_s) {
+          if (lane == 0 && !got) {
+            *abort_s = 1;
+            atomicExch(a.err, AXB_ETIMEOUT);
+          }
+          break;
+        }
       }
-      for (int i = tid; i < 8 * (SB / 16); i += kTcThreads) {  // scales of the chunk's group
-        const int tl = i / (SB / 16), tile = rb * 8 + tl;
-        const bool v = tile < Nt;
-        const char* src = reinterpret_cast<const char*>(a.scales) +
-                          ((size_t)(v ? tile : 0) * (a.K / a.G) + grp) * SB + (i % (SB / 16)) * 16;
-        cp_async16(rw + kTcRawW + i * 16, src, v ? 16u : 0u);
+      const int kb = kb0 + (isw ? f * kTcSlotK : f), nk = isw ? min(kTcSlotK, kb1 - kb) : 1;
+      if (lane == 0) {
+        fence_proxy_async();
+        mbar_expect_tx(fullb + sl, (uint32_t)(isw ? nk * ntiles * 512 : NT * 128));
       }
-      for (int i = tid; i < kTcTok * (kTcKC / 8); i += kTcThreads) {
-        const int n = i >> 3, kc = i & 7;
-        const bool v = n < a.M;
-        cp_async16(bm + tc_off(n, kc * 8), a.x + (size_t)(v ? n : 0) * a.ldx + kb * kTcKC + kc * 8, v ? 16u : 0u);
+      __syncwarp();
+      if (isw && lane < ntiles) {
+        const int tile = rb * kTcTiles + lane;
+        bulk_g2s(wring + sl * kTcWSlot + lane * (kTcSlotK * 512),
+                 reinterpret_cast<const char*>(a.words) + ((size_t)tile * KB + kb) * 512, nk * 512, fullb + sl);
+      } else if (!isw && lane == 0) {
+        bulk_g2s(xring + sl * kTcXSlot, reinterpret_cast<const char*>(a.xl) + (size_t)kb * kTcX, NT * 128,
+                 fullb + sl);
       }
     }
-    cp_async_commit();
-  };
-  for (int c = 0; c < kTcAhead; ++c) issue(c);
-
-  for (int c = 0; c < nch; ++c) {
-    const int st = c & 1, sl = c % kTcSlots;
-    cp_async_wait<kTcAhead - 1>();  // this thread's copies of chunk c have landed
-    if (c >= kTcStages) {           // MMA c - 2 is done: A stage st and slot (c - 2) % kTcSlots are free
-      const bool got = mbar_wait(bars + st, (uint32_t)(((c - kTcStages) >> 1) & 1), kTcWaitLimit);
-      if (__syncthreads_or(!got)) {
-        ok = false;
+    // no copy may still be landing when the CTA exits: wait for the last fill of every slot
+    if (lane == 0)
+      for (int q = max(0, f - nsl); q < f; ++q)
+        if (!mbar_wait(fullb + q % nsl, (uint32_t)((q / nsl) & 1), kTcWaitLimit)) {
+          *abort_s = 1;
+          atomicExch(a.err, AXB_ETIMEOUT);
+        }
+  } else if (wid == kTcWarpMma) {
+    // ---- MMA issue (lane 0): both 128-row halves of one operand stage per k-block
+    if (lane == 0) {
+      for (int c = 0; c < nch; ++c) {
+        const int sl = c % kTcXSlots, st = c % kTcStages;
+        const bool got = mbar_wait(afull + st, (uint32_t)((c / kTcStages) & 1), kTcWaitLimit) &&
+                         mbar_wait(xfull + sl, (uint32_t)((c / kTcXSlots) & 1), kTcWaitLimit);
+        if (!got || *abort_s) {
+          if (!got) {
+            *abort_s = 1;
+            atomicExch(a.err, AXB_ETIMEOUT);
+          }
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sb = smem_u32(xring + sl * kTcXSlot);
+#pragma unroll
+        for (int h = 0; h < kTcHalves; ++h) {
+          const uint32_t sa = smem_u32(stA + st * kTcA + h * kTcAHalf);
+#pragma unroll
+          for (int ks = 0; ks < kTcKC / 16; ++ks)
+            tc_mma(tmem + (uint32_t)(h * NT), tc_desc(sa + 2 * kTcAK * ks, kTcAK, kTcAM),
+                   tc_desc(sb + 256 * ks, 128, 1024), kIdesc, (c > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc_commit(aempty + st);
+        tc_commit(xempty + sl);
+      }
+      tc_commit(done);  // covers every MMA issued above
+    }
+    __syncwarp();
+  } else {
+    // ---- dequantize: warp w takes row tile w; scales come straight from
+    // global memory, loaded one chunk ahead
+    const int ng = a.K / a.G;
+    const int tile = min(rb * kTcTiles + wid, Nt - 1);  // rows past N: any valid tile
+    auto load_sc = [&](int c) {
+      const int grp = ((kb0 + c) * kTcKC) / a.G;
+      uint2 sc;
+      if (SYM) {
+        sc.x = __ldg(reinterpret_cast<const uint32_t*>(a.scales) + ((size_t)tile * ng + grp) * 8 + g);
+        sc.y = 0;
+      } else {
+        sc = __ldg(reinterpret_cast<const uint2*>(a.scales) + ((size_t)tile * ng + grp) * 8 + g);
+      }
+      return sc;
+    };
+    uint2 sc_cur = nch > 0 ? load_sc(0) : make_uint2(0, 0);
+    for (int c = 0; c < nch; ++c) {
+      const int fl = c / kTcSlotK, sl = fl % kTcWSlots, st = c % kTcStages, hk = c % kTcSlotK;
+      const uint2 sc_nxt = c + 1 < nch ? load_sc(c + 1) : sc_cur;
+      // every lane reads the slot and writes the stage: each observes both barriers
+      bool mine = mbar_wait(wfull + sl, (uint32_t)((fl / kTcWSlots) & 1), kTcWaitLimit);
+      if (mine && c >= kTcStages) mine = mbar_wait(aempty + st, (uint32_t)((c / kTcStages - 1) & 1), kTcWaitLimit);
+      const bool got = __all_sync(0xffffffffu, mine);
+      if (!got || *abort_s) {
+        if (lane == 0 && !got) {
+          *abort_s = 1;
+          atomicExch(a.err, AXB_ETIMEOUT);
+        }
         break;
       }
-    } else {
-      __syncthreads();
-    }
-    issue(c + kTcAhead);  // slot (c + 3) % 5 == (c - 2) % 5: freed above
-    char* A = stA + st * kTcA;
-    const char* rw = raw + sl * kTcRaw;
-    // ---- dequantize: row tile wid, this lane's fragments
-    {
-      const int tl = wid;
-      const uint4 wv = *reinterpret_cast<const uint4*>(rw + tl * 512 + lane * 16);
-      uint2 sc;
-      if (SYM) sc.x = reinterpret_cast<const uint32_t*>(rw + kTcRawW + tl * SB)[g];
-      else sc = reinterpret_cast<const uint2*>(rw + kTcRawW + tl * SB)[g];
-      const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+      const char* slot = wring + sl * kTcWSlot;
+      char* A = stA + st * kTcA + (wid >> 3) * kTcAHalf;
+      {
+        const uint4 wv = *reinterpret_cast<const uint4*>(slot + wid * (kTcSlotK * 512) + hk * 512 + lane * 16);
+        const uint2 sc = sc_cur;
+        const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t rg[4][2], rg8[4][2];  // [word j][f0 / f2] rows g and g + 8
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t f[4];
-        if (SYM) {
-          unpack_word<8>(w4[j], f);  // exact (q - 8) as fp16
-          const __half2 s01 = u32_as_h2(sc.x);
-          const __half2 sg = __half2half2(__low2half(s01)), sg8 = __half2half2(__high2half(s01));
-          f[0] = h2_as_u32(__hmul2(u32_as_h2(f[0]), sg));
-          f[1] = h2_as_u32(__hmul2(u32_as_h2(f[1]), sg8));
-          f[2] = h2_as_u32(__hmul2(u32_as_h2(f[2]), sg));
-          f[3] = h2_as_u32(__hmul2(u32_as_h2(f[3]), sg8));
-        } else {
-          unpack_word<0>(w4[j], f);  // q as fp16
-          const __half2 p0 = u32_as_h2(sc.x), p1 = u32_as_h2(sc.y);  // (s[g], b[g]), (s[g+8], b[g+8])
-          const __half2 sg = __half2half2(__low2half(p0)), bg = __half2half2(__high2half(p0));
-          const __half2 sg8 = __half2half2(__low2half(p1)), bg8 = __half2half2(__high2half(p1));
-          f[0] = h2_as_u32(__hfma2(u32_as_h2(f[0]), sg, bg));
-          f[1] = h2_as_u32(__hfma2(u32_as_h2(f[1]), sg8, bg8));
-          f[2] = h2_as_u32(__hfma2(u32_as_h2(f[2]), sg, bg));
-          f[3] = h2_as_u32(__hfma2(u32_as_h2(f[3]), sg8, bg8));
+        for (int j = 0; j < 4; ++j) {
+          uint32_t fr[4];
+          if (SYM) {
+            unpack_word<8>(w4[j], fr);  // exact (q - 8) as fp16
+            const __half2 s01 = u32_as_h2(sc.x);
+            const __half2 sg = __half2half2(__low2half(s01)), sg8 = __half2half2(__high2half(s01));
+            fr[0] = h2_as_u32(__hmul2(u32_as_h2(fr[0]), sg));
+            fr[1] = h2_as_u32(__hmul2(u32_as_h2(fr[1]), sg8));
+            fr[2] = h2_as_u32(__hmul2(u32_as_h2(fr[2]), sg));
+            fr[3] = h2_as_u32(__hmul2(u32_as_h2(fr[3]), sg8));
+          } else {
+            unpack_word<0>(w4[j], fr);  // q as fp16
+            const __half2 p0 = u32_as_h2(sc.x), p1 = u32_as_h2(sc.y);  // (s[g], b[g]), (s[g+8], b[g+8])
+            const __half2 sg = __half2half2(__low2half(p0)), bg = __half2half2(__high2half(p0));
+            const __half2 sg8 = __half2half2(__low2half(p1)), bg8 = __half2half2(__high2half(p1));
+            fr[0] = h2_as_u32(__hfma2(u32_as_h2(fr[0]), sg, bg));
+            fr[1] = h2_as_u32(__hfma2(u32_as_h2(fr[1]), sg8, bg8));
+            fr[2] = h2_as_u32(__hfma2(u32_as_h2(fr[2]), sg, bg));
+            fr[3] = h2_as_u32(__hfma2(u32_as_h2(fr[3]), sg8, bg8));
+          }
+          // f0 / f2: row g, k = 16 t4 + 4 j + {0, 1} / {2, 3}; f1 / f3: row g + 8
+          rg[j][0] = fr[0];
+          rg[j][1] = fr[2];
+          rg8[j][0] = fr[1];
+          rg8[j][1] = fr[3];
         }
-        // f0 / f2: row g, k = 16 t4 + 4 j + {0, 1} / {2, 3}; f1 / f3: row g + 8
-        const int r = tl * 16 + g, k = 16 * t4 + 4 * j;
-        *reinterpret_cast<uint2*>(A + tc_off(r, k)) = make_uint2(f[0], f[2]);
-        *reinterpret_cast<uint2*>(A + tc_off(r + 8, k)) = make_uint2(f[1], f[3]);
+        const int r = (wid & 7) * 16 + g, k = 16 * t4;
+        *reinterpret_cast<uint4*>(A + tc_aoff(r, k)) = make_uint4(rg[0][0], rg[0][1], rg[1][0], rg[1][1]);
+        *reinterpret_cast<uint4*>(A + tc_aoff(r + 8, k)) = make_uint4(rg8[0][0], rg8[0][1], rg8[1][0], rg8[1][1]);
+        *reinterpret_cast<uint4*>(A + tc_aoff(r, k + 8)) = make_uint4(rg[2][0], rg[2][1], rg[3][0], rg[3][1]);
+        *reinterpret_cast<uint4*>(A + tc_aoff(r + 8, k + 8)) = make_uint4(rg8[2][0], rg8[2][1], rg8[3][0], rg8[3][1]);
+      }
+      fence_proxy_async();  // the tensor core reads the stage through the async proxy
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(afull + st);
+        if (hk == kTcSlotK - 1 || c == nch - 1) mbar_arrive(wempty + sl);  // the slot's words are consumed
+      }
+      sc_cur = sc_nxt;
+    }
+  }
+
+  // ---- every MMA of the CTA is done (or the CTA gave up): read the accumulators
+  if (wid < kTcDqWarps) {
+    const bool got = __all_sync(0xffffffffu, mbar_wait(done, 0u, kTcWaitLimit));
+    if (!got && lane == 0) {
+      *abort_s = 1;
+      atomicExch(a.err, AXB_ETIMEOUT);
+    }
+  }
+  __syncthreads();
+  const bool ok = *abort_s == 0 && nch > 0;
+  tc_fence_after();
+  // ---- epilogue (warps 0-15): warp w reads half w / 8, accumulator lanes 32 (w % 4) .. (its
+  // rows) and tokens (NT / 2) ((w / 4) % 2) ..; fp16 (+ bias), or the split's fp32 partial
+  if (wid < kTcDqWarps && ok) {
+    const int quarter = wid & 3, cpart = (wid >> 2) & 1, h = wid >> 3;
+    const int row = rb * kTcRows + h * kTcHalf + 32 * quarter + lane;
+    const bool live = row < a.N;
+    const float bsum = (S == 1 && a.bias && live) ? __half2float(a.bias[row]) : 0.f;
+#pragma unroll
+    for (int j = 0; j < NT / 32; ++j) {
+      const int n0 = cpart * (NT / 2) + 16 * j;
+      uint32_t r[16];
+      tc_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(h * NT + n0), r);
+      if (live) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int n = n0 + q;
+          if (n < a.M) {
+            if (S == 1)
+              a.y[(size_t)n * a.ldy + row] = __float2half_rn(__uint_as_float(r[q]) + bsum);
+            else
+              a.part[((size_t)sp * a.M + n) * a.N + row] = __uint_as_float(r[q]);
+          }
+        }
       }
     }
-    fence_proxy_async();  // the tensor core reads A (and the copied B) through the async proxy
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t sa = smem_u32(A), sb = smem_u32(stB + sl * kTcB);
-#pragma unroll
-      for (int ks = 0; ks < kTcKC / 16; ++ks)
-        tc_mma(tmem, tc_desc(sa + 256 * ks), tc_desc(sb + 256 * ks), (c > 0 || ks > 0) ? 1u : 0u);
-      tc_commit(bars + st);
-    }
-  }
-  cp_async_wait<0>();  // no copy may still be landing when the CTA exits
-
-  // ---- the last commit covers every MMA of this CTA
-  if (nch > 0) {
-    const int cl = nch - 1;
-    const bool got = mbar_wait(bars + (cl & 1), (uint32_t)((cl >> 1) & 1), kTcWaitLimit);
-    if (__syncthreads_or(!got)) ok = false;
-  }
-  if (!ok) {
-    if (tid == 0) atomicExch(a.err, AXB_ETIMEOUT);
-    // give the tensor core a last bounded chance to finish before the memory is freed
-    if (nch > 0) mbar_wait(bars + ((nch - 1) & 1), (uint32_t)(((nch - 1) >> 1) & 1), kTcWaitLimit);
-  }
-  tc_fence_after();
-  // warps w and w + 4 share accumulator lanes 32 (w % 4) ..: w < 4 reads tokens 0..31, w >= 4 tokens 32..63
-  constexpr int kHalf = kTcTok / 2;
-  const int quarter = wid & 3, n0 = (wid >> 2) * kHalf;
-  float v[kHalf];
-  if (ok && nch > 0) {
-    uint32_t r[kHalf];
-    const uint32_t taddr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)n0;
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int n = 0; n < kHalf; ++n) v[n] = __uint_as_float(r[n]);
-  } else {
-#pragma unroll
-    for (int n = 0; n < kHalf; ++n) v[n] = 0.f;
   }
   // ---- tensor memory is no longer needed
   tc_fence_before();
   __syncthreads();
-  if (wid == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
-  if (!ok) return;
-
-  // ---- epilogue: row = this thread's accumulator lane; fp16 (+ bias), or the split's fp32 partial
-  const int row = rb * kTcRows + 32 * quarter + lane;
-  if (row >= a.N) return;
-  if (S == 1) {
-    const float bsum = a.bias ? __half2float(a.bias[row]) : 0.f;
-#pragma unroll
-    for (int n = 0; n < kHalf; ++n)
-      if (n0 + n < a.M) a.y[(size_t)(n0 + n) * a.ldy + row] = __float2half_rn(v[n] + bsum);
-    return;
-  }
-#pragma unroll
-  for (int n = 0; n < kHalf; ++n)
-    if (n0 + n < a.M) a.part[((size_t)sp * a.M + n0 + n) * a.N + row] = v[n];
+  if (wid == kTcWarpMma)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
 }
 
 // split-K: y[m][n] = fp16(sum over splits in order + bias)
@@ -292,6 +410,7 @@ __global__ void tc_reduce_kernel(const float* __restrict__ part, int S, int M, i
   }
 }
 
+// splits of K so that the CTAs (two per SM) fill the GPU in about one wave
 int tc_splits(int N, int K) {
   const int rbs = (N + kTcRows - 1) / kTcRows, KB = K / kTcKC;
   int S = (2 * num_sms() + rbs - 1) / rbs;
@@ -305,12 +424,15 @@ using namespace axb;
 
 extern "C" {
 
+// workspace: error word | activations in the canonical layout | split-K partials
+static size_t tc_xl_bytes(int K) { return (size_t)(K / kTcKC) * kTcX; }
+
 size_t axb_qgemm_tc_workspace_bytes(int N, int K, int M) {
   (void)M;
   if (N <= 0 || K <= 0 || K % kTcKC) return 0;
   const int S = tc_splits(N, K);
   const size_t part = S > 1 ? (size_t)S * kTcTok * N * sizeof(float) : 0;
-  return 256 + part;  // error word, split-K partials
+  return 256 + tc_xl_bytes(K) + part;
 }
 
 int axb_qgemm_tc(const axb_qgemm_desc* d, void* stream) {
@@ -326,8 +448,10 @@ int axb_qgemm_tc(const axb_qgemm_desc* d, void* stream) {
   AXB_CHECK_ARG(d->words && d->scales && d->x && d->y && d->ldx >= d->K && d->ldy >= d->N,
                 "qgemm_tc: bad pointers / strides");
   AXB_CHECK_ARG((reinterpret_cast<uintptr_t>(d->x) & 15) == 0 && d->ldx % 8 == 0 &&
-                    (reinterpret_cast<uintptr_t>(d->words) & 15) == 0,
-                "qgemm_tc: x and words must be 16-byte aligned, ldx a multiple of 8");
+                    (reinterpret_cast<uintptr_t>(d->words) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(d->scales) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(d->workspace) & 255) == 0,
+                "qgemm_tc: x, words and scales must be 16-byte aligned (workspace 256), ldx a multiple of 8");
   const size_t need = axb_qgemm_tc_workspace_bytes(d->N, d->K, d->M);
   AXB_CHECK_ARG(d->workspace && d->workspace_bytes >= need, "qgemm_tc: workspace %zu < %zu bytes",
                 d->workspace_bytes, need);
@@ -335,10 +459,11 @@ int axb_qgemm_tc(const axb_qgemm_desc* d, void* stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(qgemm_tc_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kTcSmem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(qgemm_tc_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+    cudaError_t e = cudaSuccess;
+    const void* ks[4] = {(const void*)qgemm_tc_kernel<true, 2, 32>, (const void*)qgemm_tc_kernel<true, 2, 64>,
+                         (const void*)qgemm_tc_kernel<false, 1, 32>, (const void*)qgemm_tc_kernel<false, 1, 64>};
+    for (int i = 0; i < 4 && e == cudaSuccess; ++i)
+      e = cudaFuncSetAttribute(ks[i], cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
     if (e != cudaSuccess) return cuda_status(e, "qgemm_tc attribute");
     attr_dev = dev;
   }
@@ -348,22 +473,35 @@ int axb_qgemm_tc(const axb_qgemm_desc* d, void* stream) {
   TcArgs a;
   a.words = (const uint32_t*)d->words;
   a.scales = (const __half*)d->scales;
-  a.x = (const __half*)d->x;
+  a.xl = (const __half*)(ws + 256);
   a.bias = (const __half*)d->bias;
   a.y = (__half*)d->y;
   a.err = (int*)ws;
-  a.part = S > 1 ? (float*)(ws + 256) : nullptr;
+  a.part = S > 1 ? (float*)(ws + 256 + tc_xl_bytes(d->K)) : nullptr;
   a.N = d->N;
   a.K = d->K;
   a.M = d->M;
-  a.ldx = d->ldx;
   a.ldy = d->ldy;
   a.G = d->group;
+  {
+    const int pieces = (d->K / kTcKC) * kTcTok * 8;
+    tc_xlayout_kernel<<<std::min((pieces + 255) / 256, 8 * num_sms()), 256, 0, (cudaStream_t)stream>>>(
+        (const __half*)d->x, d->M, d->K, d->ldx, (__half*)(ws + 256));
+    if (int rc = launch_status("qgemm_tc layout")) return rc;
+  }
   dim3 grid(rbs, S);
-  if (d->fmt == AXB_W_Q4T_SYM)
-    qgemm_tc_kernel<true, 2><<<grid, kTcThreads, kTcSmem, (cudaStream_t)stream>>>(a);
-  else
-    qgemm_tc_kernel<false, 1><<<grid, kTcThreads, kTcSmem, (cudaStream_t)stream>>>(a);
+  const bool narrow = d->M <= 32;  // one 32-token MMA width: half the activation traffic
+  if (d->fmt == AXB_W_Q4T_SYM) {
+    if (narrow)
+      qgemm_tc_kernel<true, 2, 32><<<grid, kTcThreads, kTcSmem, (cudaStream_t)stream>>>(a);
+    else
+      qgemm_tc_kernel<true, 2, 64><<<grid, kTcThreads, kTcSmem, (cudaStream_t)stream>>>(a);
+  } else {
+    if (narrow)
+      qgemm_tc_kernel<false, 1, 32><<<grid, kTcThreads, kTcSmem, (cudaStream_t)stream>>>(a);
+    else
+      qgemm_tc_kernel<false, 1, 64><<<grid, kTcThreads, kTcSmem, (cudaStream_t)stream>>>(a);
+  }
   if (int rc = launch_status("qgemm_tc")) return rc;
   if (S > 1) {
     const size_t total = (size_t)d->M * d->N;

@@ -71,3 +71,11 @@ def test_matches_warp_level_gemv(ax):
 def test_more_than_64_tokens_chunked(ax):
     y, ref, _, _ = _case(ax, 512, 512, 100, True, seed=9)
     assert _rel(y, ref) < REL_TOL
+
+
+@pytest.mark.parametrize("N,K", [(256, 448), (2003, 320), (130, 64)])
+def test_odd_k_block_counts(ax, N, K):
+    """Splits whose k-block count is odd (a ring slot holding a single k-block),
+    a single k-block in all, and a row count that ends inside a tile."""
+    y, ref, _, _ = _case(ax, N, K, 40, False, bias=True, seed=N)
+    assert _rel(y, ref) < REL_TOL, f"{N}x{K}: rel {_rel(y, ref):.2e}"
