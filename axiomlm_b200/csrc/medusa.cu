@@ -146,12 +146,20 @@ __device__ __forceinline__ void for_tile8(const __half* row, int n, int base, bo
   for (int j = 0; j < 8; ++j) f(i0 + j, i0 + j < n, h_key(v[j]));
 }
 
-// Top-k (k <= AXB_TOPK_MAX) of each row by value, ties to the lower index:
-// the k-th largest key by a two-pass 8-bit radix select, then one ordered
-// pass collects the larger keys and the lowest-indexed ties, and one warp
-// sorts the k survivors.  One CTA per row.
+constexpr int kTopkCand = 2048;  // candidate capacity of the fast path
+
+// Top-k (k <= AXB_TOPK_MAX) of each row by value, ties to the lower index.
+// One CTA per row.  Fast path: the k-th largest of the threads' own maxima
+// bounds the row's k-th largest from below, so one more pass collecting the
+// keys at or above it (few, for logits) and a bitonic sort of those give the
+// answer.  When more than kTopkCand keys tie at the bound (flat rows), the
+// exact path runs instead: the k-th largest key by a two-pass 8-bit radix
+// select, then an ordered pass collects the larger keys and the
+// lowest-indexed ties, and one warp sorts the k survivors.
 __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const __half* __restrict__ x, int n, int ld, int k,
                                                                  int32_t* __restrict__ out_idx) {
+  __shared__ unsigned long long cand[kTopkCand];  // (key << 32) | ~index: larger is better
+  __shared__ uint32_t tmax_s[kTopkThreads];
   __shared__ int hist[256];
   __shared__ int red[kTopkWarps + 1];
   __shared__ uint32_t s_sel[2];
@@ -161,20 +169,81 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const __half* _
   const __half* row = x + (size_t)blockIdx.x * ld;
   const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
   const int tile = 8 * kTopkThreads;
+  const int tid = threadIdx.x;
+
+  // ---- fast path: per-thread maxima, their k-th largest as the bound
+  uint32_t tmax = 0;
+  for (int base = 0; base < n; base += tile)
+    for_tile8(row, n, base, vec, [&](int, bool ok, uint32_t key) {
+      if (ok) tmax = max(tmax, key);
+    });
+  tmax_s[tid] = tmax;
+  if (tid == 0) s_cnt = 0;
+  __syncthreads();
+  // bitonic sort of the maxima, descending: the k-th is the bound (k distinct
+  // elements are >= it)
+  for (int size = 2; size <= kTopkThreads; size <<= 1)
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (tid < kTopkThreads / 2) {
+        const int lo = 2 * tid - (tid & (stride - 1)), hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const uint32_t a = tmax_s[lo], b = tmax_s[hi];
+        if ((a < b) == desc) {
+          tmax_s[lo] = b;
+          tmax_s[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  const uint32_t bound = tmax_s[k - 1];
+  for (int base = 0; base < n; base += tile)
+    for_tile8(row, n, base, vec, [&](int i, bool ok, uint32_t key) {
+      if (ok && key >= bound) {
+        const int slot = atomicAdd(&s_cnt, 1);
+        if (slot < kTopkCand) cand[slot] = ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)i);
+      }
+    });
+  __syncthreads();
+  const int nc = s_cnt;
+  if (nc <= kTopkCand) {
+    int P = 64;
+    while (P < nc) P <<= 1;
+    for (int i = nc + tid; i < P; i += blockDim.x) cand[i] = 0ull;
+    __syncthreads();
+    // bitonic sort, descending
+    for (int size = 2; size <= P; size <<= 1)
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = tid; i < P / 2; i += blockDim.x) {
+          const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+          const bool desc = (lo & size) == 0;
+          const unsigned long long a = cand[lo], b = cand[hi];
+          if ((a < b) == desc) {
+            cand[lo] = b;
+            cand[hi] = a;
+          }
+        }
+        __syncthreads();
+      }
+    for (int j = tid; j < k; j += blockDim.x)
+      out_idx[(size_t)blockIdx.x * k + j] = (int32_t)(0xFFFFFFFFu - (uint32_t)(cand[j] & 0xFFFFFFFFull));
+    return;
+  }
+
+  // ---- exact path for flat rows
   uint32_t prefix = 0;  // selected high byte, then the whole key
   int want = k;         // rank still to find inside the selected bucket
   for (int pass = 0; pass < 2; ++pass) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     for (int base = 0; base < n; base += tile)
       for_tile8(row, n, base, vec, [&](int, bool ok, uint32_t key) {
         // lanes with the same bin add once (logits crowd into few bins)
         const uint32_t bin = !ok ? 0xFFFFu : pass == 0 ? key >> 8 : (key >> 8) == prefix ? (key & 0xFFu) : 0xFFFFu;
         const unsigned m = __match_any_sync(0xffffffffu, bin);
-        if (bin != 0xFFFFu && (threadIdx.x & 31) == __ffs(m) - 1) atomicAdd(&hist[bin], __popc(m));
+        if (bin != 0xFFFFu && (tid & 31) == __ffs(m) - 1) atomicAdd(&hist[bin], __popc(m));
       });
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
       int above = 0, b = 255;
       for (; b > 0; --b) {
         if (above + hist[b] >= want) break;
@@ -189,7 +258,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const __half* _
     __syncthreads();
   }
   const uint32_t thr = prefix;  // the k-th largest key; `want` ties of it are taken
-  if (threadIdx.x == 0) s_cnt = 0;
+  if (tid == 0) s_cnt = 0;
   __syncthreads();
   const int n_gt = k - want;
   int ties_before = 0;
@@ -220,8 +289,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const __half* _
   }
   __syncthreads();
   // rank sort of the k survivors: (key desc, index asc)
-  if (threadIdx.x < 32)
-    for (int a = threadIdx.x; a < k; a += 32) {
+  if (tid < 32)
+    for (int a = tid; a < k; a += 32) {
       const uint32_t ka = c_key[a];
       const int ia = c_idx[a];
       int pos = 0;

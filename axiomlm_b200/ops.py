@@ -53,7 +53,11 @@ class _Workspace:
         return b
 
 
+# One workspace per kernel family: each keeps its own fixed-offset layout (the
+# Q4 GEMV's tile counters must stay zero between calls), so two families must
+# never share one.
 _WS = _Workspace()
+_LB_WS = _Workspace()
 _ATTN_WS = _Workspace()
 
 # ---------------------------------------------------------------- formats
@@ -246,7 +250,7 @@ def lbgemm(x: torch.Tensor, W: Q2TWeight, bias: torch.Tensor | None = None,
         out = torch.empty((M, W.N), dtype=torch.float16, device=x.device)
     o2 = out.view(M, W.N)
     lib = L.load()
-    ws = _WS.get(lib.axb_lbgemv_workspace_bytes(W.fmt, W.N, K, 8), x.device)
+    ws = _LB_WS.get(lib.axb_lbgemv_workspace_bytes(W.fmt, W.N, K, 8), x.device)
     b = None if bias is None else _cuda(bias, "bias").to(torch.float16)
     for m0 in range(0, M, 8):
         m = min(8, M - m0)

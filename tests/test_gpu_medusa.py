@@ -201,7 +201,8 @@ def test_medusa_heads_match_reference(md):
 
 def test_medusa_heads_without_residual_stack(md):
     """Heads without residual blocks run as one stacked GEMV; the result
-    equals head-by-head GEMVs."""
+    matches head-by-head GEMVs (the two may split K differently, so the
+    comparison is at the GEMV tolerance, not bitwise)."""
     from axiomlm_b200 import ops
 
     g = torch.Generator(device="cuda").manual_seed(5)
@@ -211,8 +212,10 @@ def test_medusa_heads_without_residual_stack(md):
     x = torch.randn(2, 256, device="cuda", generator=g)
     out = heads(x)
     for k, w in enumerate(heads.head):
-        ref = ops.qgemm(x.half(), w)
-        assert torch.equal(out[k], ref), k
+        ref = x.half().float() @ w.dequant().float().t()
+        per_head = ops.qgemm(x.half(), w)
+        assert _rel(per_head, ref) < REL_TOL, ("per-head GEMV", k, _rel(per_head, ref))
+        assert _rel(out[k], ref) < REL_TOL, ("stacked GEMV", k, _rel(out[k], ref))
 
 
 # -------------------------------------------------------- whole generation
