@@ -431,12 +431,22 @@ struct TreeSmem {
   static constexpr int kQ = 0;                                  // [hi, lo][64 rows][LD] fp16
   static constexpr int kK = kQ + 2 * kTreeRows * LD * 2;        // [64 keys][LD] fp16 codes
   static constexpr int kV = kK + kTreeKeys * LD * 2;            // [64 keys][LD]
-  static constexpr int kKs = kV + kTreeKeys * LD * 2;           // [64 keys][8 groups] fp32 K scales
-  static constexpr int kVs = kKs + kTreeKeys * 8 * 4;           // [64 keys][8 groups] fp32 V scales
-  static constexpr int kVmax = kVs + kTreeKeys * 8 * 4;         // [8 groups] fp32
+  static constexpr int kKs = kV + kTreeKeys * LD * 2;           // [2 tiles][64 keys][8 groups] fp32 K scales
+  static constexpr int kVs = kKs + 2 * kTreeKeys * 8 * 4;       // [2 tiles][64 keys][8 groups] fp32 V scales
+  static constexpr int kVmax = kVs + 2 * kTreeKeys * 8 * 4;     // [8 groups] fp32
   static constexpr int kMask = kVmax + 8 * 4;                   // [64 rows] uint64
-  static constexpr int kBytes = kMask + kTreeRows * 8;
+  static constexpr int kRaw = kMask + kTreeRows * 8;            // [2 tiles][K, V][64 keys][row bytes] cache codes
+  // shared memory of a launch: the fixed part and the double-buffered raw codes
+  static constexpr int bytes(int row_bytes) { return kRaw + 2 * 2 * kTreeKeys * row_bytes; }
 };
+// 16-byte asynchronous copy global -> shared; src_bytes 0 writes zeros
+__device__ __forceinline__ void tree_cp16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void tree_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void tree_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -554,38 +564,81 @@ __global__ void __launch_bounds__(128) tree_attn_kernel(axb_attn_desc d, int nsp
 
   const int n_keys_all = d.prefix_len + d.T;
   const int k_begin = split * chunk, n_keys = min(n_keys_all, k_begin + chunk);
-  for (int kt = k_begin; kt < n_keys; kt += kTreeKeys) {
-    const int nk = min(kTreeKeys, n_keys - kt);
-    __syncthreads();  // the previous tile's K / V are no longer read
-    // ---- stage the tile: codes as fp16, scales as fp32 (keys past nk: zeros)
-    for (int i = tid; i < 2 * kTreeKeys * PPR; i += 128) {
-      const int isv = i / (kTreeKeys * PPR), j = (i / PPR) % kTreeKeys, p = i % PPR;
-      uint4 o[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-      if (j < nk) {
-        const int key = kt + j;
-        const int slot = key < d.prefix_len ? key : (d.write_pos + key - d.prefix_len) % d.max_seq;
-        tree_codes16((isv ? vc : kc) + (size_t)slot * rb + p * piece_bytes, d.kv_type, o);
+  // ---- K / V staging, double-buffered: the raw codes of the next tile are
+  // copied (cp.async) and its scales loaded into registers while the current
+  // tile is in the MMAs
+  char* raw = tsm + SM::kRaw;
+  const int p16 = rb / 16;  // 16-byte pieces per cached row
+  auto slot_of = [&](int key) { return key < d.prefix_len ? key : (d.write_pos + key - d.prefix_len) % d.max_seq; };
+  auto issue_tile = [&](int kt_i, int buf) {
+    const int nk_i = min(kTreeKeys, n_keys - kt_i);
+    char* rawb = raw + (size_t)buf * 2 * kTreeKeys * rb;
+    for (int i = tid; i < 2 * kTreeKeys * p16; i += 128) {
+      const int isv = i / (kTreeKeys * p16), j = (i / p16) % kTreeKeys, pc = i % p16;
+      const uint8_t* src = isv ? vc : kc;
+      uint32_t nb = 0;
+      if (j < nk_i) {
+        src += (size_t)slot_of(kt_i + j) * rb + pc * 16;
+        nb = 16;
       }
-      __half* dst = (isv ? v_s : k_s) + j * LD + 16 * p;
-      reinterpret_cast<uint4*>(dst)[0] = o[0];
-      reinterpret_cast<uint4*>(dst)[1] = o[1];
+      tree_cp16(rawb + ((size_t)(isv * kTreeKeys + j) * rb + pc * 16), src, nb);
     }
+  };
+  float sreg[8];  // this thread's scales of the next tile: element tid + 128 q, q < ng
+  auto load_sc = [&](int kt_i) {
+    const int nk_i = min(kTreeKeys, n_keys - kt_i);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q < ng) {
+        const int e = tid + 128 * q, isv = e / (kTreeKeys * ng), j = (e / ng) % kTreeKeys, gi = e % ng;
+        sreg[q] = j < nk_i ? __half2float((isv ? vsg : ksg)[(size_t)slot_of(kt_i + j) * ng + gi]) : 0.f;
+      }
+  };
+  auto store_sc = [&](int buf) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q < ng) {
+        const int e = tid + 128 * q, isv = e / (kTreeKeys * ng), j = (e / ng) % kTreeKeys, gi = e % ng;
+        (isv ? vs_s : ks_s)[buf * kTreeKeys * 8 + j * 8 + gi] = sreg[q];
+      }
+  };
+  if (k_begin < n_keys) {
+    issue_tile(k_begin, 0);
     if (quant) {
-      for (int i = tid; i < 2 * kTreeKeys * ng; i += 128) {
-        const int isv = i / (kTreeKeys * ng), j = (i / ng) % kTreeKeys, gi = i % ng;
-        float sc = 0.f;
-        if (j < nk) {
-          const int key = kt + j;
-          const int slot = key < d.prefix_len ? key : (d.write_pos + key - d.prefix_len) % d.max_seq;
-          sc = __half2float((isv ? vsg : ksg)[(size_t)slot * ng + gi]);
-        }
-        (isv ? vs_s : ks_s)[j * 8 + gi] = sc;
+      load_sc(k_begin);
+      store_sc(0);
+    }
+  }
+  tree_cp_commit();
+  int it = 0;
+  for (int kt = k_begin; kt < n_keys; kt += kTreeKeys, ++it) {
+    const int nk = min(kTreeKeys, n_keys - kt), buf = it & 1;
+    const bool has_next = kt + kTreeKeys < n_keys;
+    __syncthreads();  // the previous tile's K / V, raw codes and scales are no longer read
+    if (has_next) issue_tile(kt + kTreeKeys, buf ^ 1);
+    tree_cp_commit();
+    if (quant && has_next) load_sc(kt + kTreeKeys);
+    tree_cp_wait<1>();  // this thread's copies of the current tile have landed
+    __syncthreads();
+    // ---- codes as fp16 (keys past nk are zeros)
+    {
+      const char* rawb = raw + (size_t)buf * 2 * kTreeKeys * rb;
+      for (int i = tid; i < 2 * kTreeKeys * PPR; i += 128) {
+        const int isv = i / (kTreeKeys * PPR), j = (i / PPR) % kTreeKeys, pc = i % PPR;
+        uint4 o[2];
+        tree_codes16(reinterpret_cast<const uint8_t*>(rawb) + (size_t)(isv * kTreeKeys + j) * rb + pc * piece_bytes,
+                     d.kv_type, o);
+        __half* dst = (isv ? v_s : k_s) + j * LD + 16 * pc;
+        reinterpret_cast<uint4*>(dst)[0] = o[0];
+        reinterpret_cast<uint4*>(dst)[1] = o[1];
       }
     }
+    const float* ksb = ks_s + buf * kTreeKeys * 8;
+    const float* vsb = vs_s + buf * kTreeKeys * 8;
     __syncthreads();
     if (quant && w == 0) {  // the tile's largest V scale per group
       for (int gi = 0; gi < ng; ++gi) {
-        float mx = fmaxf(vs_s[lane * 8 + gi], vs_s[(lane + 32) * 8 + gi]);
+        float mx = fmaxf(vsb[lane * 8 + gi], vsb[(lane + 32) * 8 + gi]);
         mx = warp_max(mx);
         if (lane == 0) vmax_s[gi] = mx > 0.f ? mx : 1.f;
       }
@@ -627,7 +680,7 @@ __global__ void __launch_bounds__(128) tree_attn_kernel(axb_attn_desc d, int nsp
 #pragma unroll
           for (int nb = 0; nb < 8; ++nb) {
             const int j0 = 8 * nb + 2 * c;
-            const float s0 = quant ? ks_s[j0 * 8 + gi] : 1.f, s1 = quant ? ks_s[(j0 + 1) * 8 + gi] : 1.f;
+            const float s0 = quant ? ksb[j0 * 8 + gi] : 1.f, s1 = quant ? ksb[(j0 + 1) * 8 + gi] : 1.f;
             s[nb][0] = __fmaf_rn(gacc[nb][0], s0, s[nb][0]);
             s[nb][1] = __fmaf_rn(gacc[nb][1], s1, s[nb][1]);
             s[nb][2] = __fmaf_rn(gacc[nb][2], s0, s[nb][2]);
@@ -696,7 +749,7 @@ __global__ void __launch_bounds__(128) tree_attn_kernel(axb_attn_desc d, int nsp
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int j = 16 * kq + 8 * h + 2 * c + (q & 1);
-            pv[h][q] = quant ? s[2 * kq + h][q] * (vs_s[j * 8 + gi] * inv) : s[2 * kq + h][q];
+            pv[h][q] = quant ? s[2 * kq + h][q] * (vsb[j * 8 + gi] * inv) : s[2 * kq + h][q];
           }
         uint32_t phi[4], plo[4];
         tree_split_h2(pv[0][0], pv[0][1], phi[0], plo[0]);  // row g, keys 2c, 2c + 1
@@ -722,7 +775,9 @@ __global__ void __launch_bounds__(128) tree_attn_kernel(axb_attn_desc d, int nsp
 #pragma unroll
           for (int q = 0; q < 4; ++q) oacc[nb][q] *= vm;
     }
+    if (quant && has_next) store_sc(buf ^ 1);  // the next tile's scales (their loads have landed)
   }
+  tree_cp_wait<0>();  // no copy may still be landing when the CTA exits
   // ---- row sums across the quad; outputs
 #pragma unroll
   for (int hr = 0; hr < 2; ++hr) {
@@ -836,7 +891,7 @@ constexpr size_t kAttnHead = 256;  // error word
 int tree_splits(int B, int T, int n_head, int n_kv_head, int n_keys) {
   const int n_rep = n_head / n_kv_head;
   const int base = ((T * n_rep + kTreeRows - 1) / kTreeRows) * n_kv_head * B;
-  int S = (3 * num_sms() + base - 1) / base;  // about three 73 KB CTAs per SM
+  int S = (2 * num_sms() + base - 1) / base;  // about two CTAs per SM (registers)
   S = std::min(S, std::max(1, n_keys / (2 * kTreeKeys)));
   return std::max(1, std::min(S, 64));
 }
@@ -889,9 +944,10 @@ int attn_prepare() {
     e = cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tree_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             TreeSmem<128>::kBytes);
+                             TreeSmem<128>::bytes(kv_row_bytes(AXB_KV_F16, 128)));
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(tree_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, TreeSmem<64>::kBytes);
+    e = cudaFuncSetAttribute(tree_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             TreeSmem<64>::bytes(kv_row_bytes(AXB_KV_F16, 64)));
   if (e != cudaSuccess) return cuda_status(e, "attention attribute");
   done_dev = dev;
   return AXB_OK;
@@ -958,11 +1014,11 @@ int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s)
   dim3 grid(((d->T * n_rep + kTreeRows - 1) / kTreeRows) * S, d->n_kv_head, d->B);
   cudaError_t e;
   if (d->head_dim == 128)
-    e = launch_pdl(tree_attn_kernel<128>, grid, dim3(128), TreeSmem<128>::kBytes, s, d->pdl != 0, *d, S, chunk, po,
-                   pml);
+    e = launch_pdl(tree_attn_kernel<128>, grid, dim3(128),
+                   (size_t)TreeSmem<128>::bytes(kv_row_bytes(d->kv_type, 128)), s, d->pdl != 0, *d, S, chunk, po, pml);
   else
-    e = launch_pdl(tree_attn_kernel<64>, grid, dim3(128), TreeSmem<64>::kBytes, s, d->pdl != 0, *d, S, chunk, po,
-                   pml);
+    e = launch_pdl(tree_attn_kernel<64>, grid, dim3(128), (size_t)TreeSmem<64>::bytes(kv_row_bytes(d->kv_type, 64)),
+                   s, d->pdl != 0, *d, S, chunk, po, pml);
   if (e != cudaSuccess) return cuda_status(e, "tree attention launch");
   if (S > 1) {
     tree_combine_kernel<<<(unsigned)rows, 128, 0, s>>>(po, pml, S, d->head_dim, reinterpret_cast<__half*>(d->out));
