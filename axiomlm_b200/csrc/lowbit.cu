@@ -232,12 +232,14 @@ __global__ void __launch_bounds__(kLbWarps * 32) lbgemv_kernel(const uint4* __re
   const bool tok = g < M;  // B-fragment token of this lane
   const __half* xr = x + (size_t)(tok ? g : 0) * ldx + 8 * c;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int kb = kb0 + wid; kb < kb1; kb += kLbWarps) {
+  // the k-blocks of a warp are few (K / 128 / warps): issue the weight and
+  // metadata loads of up to kLbAhead of them before any math, so their latencies overlap
+  constexpr int kLbAhead = 4;
+  auto load_kb = [&](int kb, uint4& wv, uint4& mv, uint2& dmv) {
     const size_t tb = (size_t)t * KB + kb;
-    const uint4 wv = ldg_nc_v4(words + tb * 32 + lane);
-    const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
-    uint4 mv = make_uint4(0, 0, 0, 0);
-    uint2 dmv = make_uint2(0, 0);
+    wv = ldg_nc_v4(words + tb * 32 + lane);
+    mv = make_uint4(0, 0, 0, 0);
+    dmv = make_uint2(0, 0);
     if (FMT == AXB_W_TERNARY_G64) {
       const uint2 m2 = __ldg(reinterpret_cast<const uint2*>(meta) + tb * 8 + g);
       mv.x = m2.x;
@@ -250,6 +252,9 @@ __global__ void __launch_bounds__(kLbWarps * 32) lbgemv_kernel(const uint4* __re
       mv.y = s8.y;  // row g + 8
       dmv = __ldg(reinterpret_cast<const uint2*>(meta2) + ((size_t)t * (K / 256) + kb / 2) * 8 + g);
     }
+  };
+  auto compute_kb = [&](int kb, const uint4 wv, const uint4 mv, const uint2 dmv) {
+    const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
     float tmp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -296,6 +301,16 @@ __global__ void __launch_bounds__(kLbWarps * 32) lbgemv_kernel(const uint4* __re
         tmp[0] = tmp[1] = tmp[2] = tmp[3] = 0.f;
       }
     }
+    };
+  for (int kb = kb0 + wid; kb < kb1; kb += kLbAhead * kLbWarps) {
+    uint4 wv[kLbAhead], mv[kLbAhead];
+    uint2 dmv[kLbAhead];
+#pragma unroll
+    for (int u = 0; u < kLbAhead; ++u)
+      if (kb + u * kLbWarps < kb1) load_kb(kb + u * kLbWarps, wv[u], mv[u], dmv[u]);
+#pragma unroll
+    for (int u = 0; u < kLbAhead; ++u)
+      if (kb + u * kLbWarps < kb1) compute_kb(kb + u * kLbWarps, wv[u], mv[u], dmv[u]);
   }
   red[wid][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
   __syncthreads();
