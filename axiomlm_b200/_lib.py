@@ -19,6 +19,8 @@ AXB_EINVAL = -1
 AXB_ECUDA = -2
 AXB_EUNSUPPORTED = -3
 AXB_ETIMEOUT = -4
+DEBUG_HDUMP = 1  # AXB_DEBUG_HDUMP: per-layer hidden states into runner buffer 6
+DEBUG_TRACE = 2  # AXB_DEBUG_TRACE: step-kernel phase timeline into runner buffer 5
 
 W_Q4T_SYM = 1
 W_Q4T_AFFINE = 2
@@ -147,6 +149,7 @@ _SIGS = {
     "axb_qgemm_status": (i32, [vp, vp]),
     "axb_qgemm_noalloc": (i32, [C.POINTER(QGemmDesc), vp]),
     "axb_qgemm_noalloc_scratch_bytes": (sz, []),
+    "axb_qgemm_noalloc_status": (i32, [vp]),
     "axb_rmsnorm": (i32, [vp, vp, i32, i32, f32, vp, vp]),
     "axb_rope_kv_write": (i32, [C.POINTER(KvWriteDesc), vp]),
     "axb_kv_quantize": (i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp]),
@@ -167,6 +170,7 @@ _SIGS = {
     "axb_runner_buffer": (i32, [vp, i32, C.POINTER(sz), C.POINTER(sz)]),
     "axb_runner_step": (i32, [vp, i32, i32, i32, i32, i32, i32, vp, vp, i32, vp]),
     "axb_runner_uses_step_kernel": (i32, [vp]),
+    "axb_runner_set_debug": (i32, [vp, i32, C.c_uint32, C.c_uint32]),
     "axb_tp_unique_id": (i32, [vp]),
     "axb_tp_comm_create": (i32, [vp, i32, i32, C.POINTER(vp)]),
     "axb_tp_comm_destroy": (i32, [vp]),

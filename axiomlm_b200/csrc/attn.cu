@@ -935,10 +935,10 @@ int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s)
 // Raise the dynamic shared-memory limit of the decode kernels once per device
 // (outside any stream capture).
 int attn_prepare() {
-  static int done_dev = -1;
+  static DeviceOnce once;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (done_dev == dev) return AXB_OK;
+  if (once.done(dev)) return AXB_OK;
   cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
@@ -949,7 +949,7 @@ int attn_prepare() {
     e = cudaFuncSetAttribute(tree_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              TreeSmem<64>::bytes(kv_row_bytes(AXB_KV_F16, 64)));
   if (e != cudaSuccess) return cuda_status(e, "attention attribute");
-  done_dev = dev;
+  once.set(dev);
   return AXB_OK;
 }
 

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/axb.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
@@ -20,6 +22,19 @@ void set_error(const char* fmt, ...);
 int cuda_status(cudaError_t e, const char* what);
 int launch_status(const char* what);
 int num_sms();
+
+// Per-device "set-up done" flags: bit d is set once device d has been prepared
+// (function attributes raised, symbol addresses looked up).  Concurrent first
+// calls on one device may both run the set-up, which is idempotent.
+struct DeviceOnce {
+  std::atomic<unsigned long long> mask{0};
+  bool done(int dev) const {
+    return dev >= 0 && dev < 64 && ((mask.load(std::memory_order_acquire) >> dev) & 1ull) != 0;
+  }
+  void set(int dev) {
+    if (dev >= 0 && dev < 64) mask.fetch_or(1ull << dev, std::memory_order_acq_rel);
+  }
+};
 
 #define AXB_CHECK_ARG(cond, ...)            \
   do {                                      \
@@ -101,6 +116,38 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// L2 policy for data read once per pass (weights, cached K/V rows): evict
+// first, so the stream does not push out what is reused (the kernel's own
+// instructions, activations, counters).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// bulk copy as bulk_g2s, with an L2 cache policy
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Bring [src, src + bytes) into L2 without a destination (bulk prefetch):
+// src 16-byte aligned, bytes a multiple of 16
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// 16-byte global -> shared copy through L2 (Ampere-style async copy), for
+// scattered or padded destinations; completes per thread with cp_async_wait_all
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Bounded wait on an mbarrier phase: returns false if it did not complete
 // within `limit` polls (the caller records an error instead of hanging).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t limit) {

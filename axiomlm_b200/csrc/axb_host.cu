@@ -25,16 +25,16 @@ int cuda_status(cudaError_t e, const char* what) {
 int launch_status(const char* what) { return cuda_status(cudaGetLastError(), what); }
 
 int num_sms() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];  // zero-initialized (static storage)
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int n = 0;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cached[dev] = n;
+    cached[dev].store(n, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return n;
 }
 
 // modules.py:41-43 with an fp32 weight: rms = 1 / sqrt(mean(x^2) + eps),

@@ -40,14 +40,24 @@ __device__ __forceinline__ float group_max(float v, int lanes_per_group) {
 }
 
 // one warp quantizes one hd-vector held EPL = hd/32 elements per lane
+// (not inlined: it runs once per row written, and its FP8 rounding is long).
+// Returns this lane's bytes of the row (EPL fp16 values, EPL FP8 codes or
+// EPL/2 INT4 bytes, little-endian in .x then .y) and, in *scale_out, the fp16
+// scale of its group, so a caller can also place the row elsewhere.
 template <int EPL>
-__device__ __forceinline__ void store_kv_row(const float (&v)[EPL], int lane, int kv_type, int G, bool fp32_in,
-                                             uint8_t* row, __half* srow) {
+__device__ __noinline__ uint2 store_kv_row(const float (&v)[EPL], int lane, int kv_type, int G, bool fp32_in,
+                                           uint8_t* row, __half* srow, float* scale_out = nullptr) {
+  uint32_t pk[2] = {0u, 0u};
   if (kv_type == AXB_KV_F16) {
     __half* r = reinterpret_cast<__half*>(row);
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) r[lane * EPL + e] = __float2half_rn(v[e]);
-    return;
+    for (int e = 0; e < EPL; ++e) {
+      const __half h = __float2half_rn(v[e]);
+      r[lane * EPL + e] = h;
+      pk[e >> 1] |= (uint32_t)__half_as_ushort(h) << (16 * (e & 1));
+    }
+    if (scale_out) *scale_out = 1.f;
+    return make_uint2(pk[0], pk[1]);
   }
   float am = 0.f;
 #pragma unroll
@@ -57,16 +67,24 @@ __device__ __forceinline__ void store_kv_row(const float (&v)[EPL], int lane, in
   const float qmax = kv_type == AXB_KV_FP8 ? 448.f : 7.f;
   const float sc = kv_scale(am, qmax, fp32_in);
   if (srow && (lane % lpg) == 0) srow[(lane * EPL) / G] = __float2half_rn(sc);
+  if (scale_out) *scale_out = sc;
   if (kv_type == AXB_KV_FP8) {
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) row[lane * EPL + e] = fp8_code(v[e], sc, fp32_in);
+    for (int e = 0; e < EPL; ++e) {
+      const uint8_t b = fp8_code(v[e], sc, fp32_in);
+      row[lane * EPL + e] = b;
+      pk[e >> 2] |= (uint32_t)b << (8 * (e & 3));
+    }
   } else {
 #pragma unroll
     for (int e = 0; e < EPL; e += 2) {
       int lo = int4_code(v[e], sc, fp32_in), hi = int4_code(v[e + 1], sc, fp32_in);
-      row[(lane * EPL + e) >> 1] = (uint8_t)((lo & 0xF) | ((hi & 0xF) << 4));
+      const uint8_t b = (uint8_t)((lo & 0xF) | ((hi & 0xF) << 4));
+      row[(lane * EPL + e) >> 1] = b;
+      pk[0] |= (uint32_t)b << (8 * (e >> 1));
     }
   }
+  return make_uint2(pk[0], pk[1]);
 }
 
 __host__ __device__ __forceinline__ int kv_row_bytes(int kv_type, int hd) {

@@ -455,17 +455,17 @@ int axb_qgemm_tc(const axb_qgemm_desc* d, void* stream) {
   const size_t need = axb_qgemm_tc_workspace_bytes(d->N, d->K, d->M);
   AXB_CHECK_ARG(d->workspace && d->workspace_bytes >= need, "qgemm_tc: workspace %zu < %zu bytes",
                 d->workspace_bytes, need);
-  static int attr_dev = -1;
+  static DeviceOnce attr_once;  // per device: alternating between GPUs does not repeat the set-up
   int dev = 0;
   cudaGetDevice(&dev);
-  if (attr_dev != dev) {
+  if (!attr_once.done(dev)) {
     cudaError_t e = cudaSuccess;
     const void* ks[4] = {(const void*)qgemm_tc_kernel<true, 2, 32>, (const void*)qgemm_tc_kernel<true, 2, 64>,
                          (const void*)qgemm_tc_kernel<false, 1, 32>, (const void*)qgemm_tc_kernel<false, 1, 64>};
     for (int i = 0; i < 4 && e == cudaSuccess; ++i)
       e = cudaFuncSetAttribute(ks[i], cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
     if (e != cudaSuccess) return cuda_status(e, "qgemm_tc attribute");
-    attr_dev = dev;
+    attr_once.set(dev);
   }
   const int S = tc_splits(d->N, d->K);
   const int rbs = (d->N + kTcRows - 1) / kTcRows;

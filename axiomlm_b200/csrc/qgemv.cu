@@ -820,8 +820,8 @@ bool qgemm_can_fuse_norm(int M, int K) {
 int qgemm_prepare() {
   int dev = 0;
   cudaGetDevice(&dev);
-  static int done_dev = -1;
-  if (done_dev == dev) return AXB_OK;
+  static DeviceOnce once;
+  if (once.done(dev)) return AXB_OK;
 #define AXB_SET(NT, SYM, GB, XS)                                                                             \
   {                                                                                                         \
     cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<NT, SYM, GB, XS>,                                      \
@@ -833,7 +833,7 @@ int qgemm_prepare() {
   AXB_SET4(8, false)
 #undef AXB_SET4
 #undef AXB_SET
-  done_dev = dev;
+  once.set(dev);
   return AXB_OK;
 }
 
@@ -957,9 +957,10 @@ constexpr size_t kNoAllocBytes = kPartialsOff + 2 * kNoAllocMaxCtas * 32 * 4 * s
 static __device__ __align__(256) char g_noalloc_scratch[kNoAllocBytes];
 
 // Device address of g_noalloc_scratch, looked up once per device with that
-// device current (a host-side symbol is not a device address).
+// device current (a host-side symbol is not a device address).  Host threads
+// may race on a device's first call: both look the same address up.
 static void* noalloc_scratch(int* status) {
-  static void* addr[64] = {nullptr};
+  static std::atomic<void*> addr[64];  // null-initialized (static storage)
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) {
@@ -967,17 +968,17 @@ static void* noalloc_scratch(int* status) {
     if (*status == AXB_EINVAL) set_error("qgemm_noalloc: device index %d out of range", dev);
     return nullptr;
   }
-  if (!addr[dev]) {
-    void* p = nullptr;
+  void* p = addr[dev].load(std::memory_order_acquire);
+  if (!p) {
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) {
       *status = cuda_status(e, "qgemm_noalloc: cudaGetSymbolAddress");
       return nullptr;
     }
-    addr[dev] = p;
+    addr[dev].store(p, std::memory_order_release);
   }
   *status = AXB_OK;
-  return addr[dev];
+  return p;
 }
 
 int qgemm_noalloc(const axb_qgemm_desc* d, cudaStream_t stream) {
@@ -989,15 +990,23 @@ int qgemm_noalloc(const axb_qgemm_desc* d, cudaStream_t stream) {
   int rc = AXB_OK;
   char* ws = reinterpret_cast<char*>(noalloc_scratch(&rc));
   if (rc) return rc;
-  // the array keeps the previous call's contents: clear the error word and the
-  // tile counters this call uses (a call that ended early may leave them set)
-  cudaError_t e = cudaMemsetAsync(ws, 0, 4, stream);
-  if (e == cudaSuccess) e = cudaMemsetAsync(ws + kCountersOff, 0, (size_t)((d->N + 15) / 16) * 4, stream);
+  // the array keeps the previous call's contents: clear the tile counters this
+  // call uses (a call that ended early may leave them set).  The error word is
+  // left alone: it holds until axb_qgemm_noalloc_status reads and clears it.
+  cudaError_t e = cudaMemsetAsync(ws + kCountersOff, 0, (size_t)((d->N + 15) / 16) * 4, stream);
   if (e != cudaSuccess) return cuda_status(e, "qgemm_noalloc: clear scratch");
   axb_qgemm_desc dd = *d;
   dd.workspace = ws;
   dd.workspace_bytes = kNoAllocBytes;
   return qgemm(&dd, stream);
+}
+
+// The error word of the library-held scratch: same contract as qgemm_status.
+int qgemm_noalloc_status(cudaStream_t stream) {
+  int rc = AXB_OK;
+  void* ws = noalloc_scratch(&rc);
+  if (rc) return rc;
+  return qgemm_status(ws, stream);
 }
 
 }  // namespace axb
@@ -1095,6 +1104,8 @@ int axb_qgemm(const axb_qgemm_desc* d, void* stream) { return qgemm(d, (cudaStre
 int axb_qgemm_noalloc(const axb_qgemm_desc* d, void* stream) { return qgemm_noalloc(d, (cudaStream_t)stream); }
 
 size_t axb_qgemm_noalloc_scratch_bytes(void) { return kNoAllocBytes; }
+
+int axb_qgemm_noalloc_status(void* stream) { return qgemm_noalloc_status((cudaStream_t)stream); }
 
 int axb_qgemm_status(void* workspace, void* stream) {
   AXB_CHECK_ARG(workspace, "qgemm_status: null workspace");

@@ -212,8 +212,8 @@ struct Layout {
   size_t gu_tmp, tc_ws, tc_ws_bytes;  // tensor-core projections for many-token steps
   size_t gemm_ws_bytes, attn_ws_bytes;
   // persistent step kernel (decode, B <= 8)
-  size_t st_layers, st_done, st_tiles, st_part, st_po, st_pml, st_acnt, st_keys, st_exit, st_trace;
-  size_t st_trace_bytes;
+  size_t st_layers, st_done, st_tiles, st_part, st_po, st_pml, st_acnt, st_keys, st_exit, st_trace, st_hdump, st_maps;
+  size_t st_trace_bytes, st_hdump_bytes;
   int st_max_tiles;
 };
 
@@ -282,7 +282,7 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.st_layers = take((size_t)c.n_layer * sizeof(StepLayer));
   L.st_done = take((size_t)(2 + 5 * c.n_layer) * 4);
   L.st_tiles = take((size_t)L.st_max_tiles * 4);
-  L.st_part = take((size_t)num_sms() * step_num_warps() * 2 * 32 * 4 * sizeof(float));
+  L.st_part = take((size_t)num_sms() * step_num_warps() * 32 * 4 * sizeof(float));
   L.st_po = take((size_t)sb * c.n_head * kStepMaxSplits * c.head_dim * sizeof(float));
   L.st_pml = take((size_t)sb * c.n_head * kStepMaxSplits * 2 * sizeof(float));
   L.st_acnt = take((size_t)sb * c.n_kv_head * 4);
@@ -290,6 +290,9 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.st_exit = take(16);
   L.st_trace_bytes = (size_t)num_sms() * step_trace_slots(c.n_layer) * 8;
   L.st_trace = take(L.st_trace_bytes);
+  L.st_hdump_bytes = (size_t)c.n_layer * sb * c.d_model * 2;
+  L.st_hdump = take(L.st_hdump_bytes);
+  L.st_maps = take((size_t)c.n_layer * 2 * kStepMapBytes);  // 256-aligned (tensor maps need 64)
   L.total = off;
   return L;
 }
@@ -628,17 +631,30 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   }
   // persistent step kernel (env AXB_STEP=0 keeps decode on the per-kernel graph)
   const char* sv = getenv("AXB_STEP");
-  const int cap_tok = step_attn_cap(c.kv_type, c.head_dim, c.kv_group);
+  const StepPlan plan = step_plan(c.max_batch, c.d_model, c.ffn, c.n_head, c.n_kv_head, c.head_dim, c.kv_type,
+                                  c.kv_type == AXB_KV_F16 ? c.head_dim : c.kv_group, c.group, c.max_seq);
   r->step_ok = !(sv && atoi(sv) == 0) && c.tp_world <= 1 &&
                step_supported(c.wfmt, c.group, c.lm_fmt, c.lm_group, c.head_dim, c.n_head, c.n_kv_head, c.d_model,
                               c.kv_type, c.kv_group, c.max_seq) &&
-               c.ffn % 64 == 0;
+               c.ffn % 64 == 0 && plan.smem > 0;
   if (r->step_ok) {
     if (int rc = step_prepare()) {
       axb_runner_destroy(r);
       return rc;
     }
     std::vector<StepLayer> tab(c.n_layer);
+    // TMA tensor maps over every layer's K / V cache, stored in the workspace
+    std::vector<char> maps((size_t)c.n_layer * 2 * kStepMapBytes);
+    if (int rc = step_kv_maps(maps.data(), c.n_layer, p->k_cache, p->v_cache, c.max_batch * c.n_kv_head * c.max_seq,
+                              c.kv_type, c.head_dim)) {
+      axb_runner_destroy(r);
+      return rc;
+    }
+    e = cudaMemcpy(r->buf<void>(L.st_maps), maps.data(), maps.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      axb_runner_destroy(r);
+      return cuda_status(e, "step tensor maps");
+    }
     for (int l = 0; l < c.n_layer; ++l) {
       StepLayer& t = tab[l];
       t.w[0] = (const char*)p->qkv_w[l];
@@ -656,6 +672,8 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
       t.vc = (uint8_t*)p->v_cache[l];
       t.ks = p->k_scale ? (__half*)p->k_scale[l] : nullptr;
       t.vs = p->v_scale ? (__half*)p->v_scale[l] : nullptr;
+      t.kmap = r->buf<char>(L.st_maps) + (size_t)(2 * l) * kStepMapBytes;
+      t.vmap = r->buf<char>(L.st_maps) + (size_t)(2 * l + 1) * kStepMapBytes;
     }
     e = cudaMemcpy(r->buf<void>(L.st_layers), tab.data(), tab.size() * sizeof(StepLayer), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
@@ -702,7 +720,12 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
     a.keys = r->buf<unsigned long long>(L.st_keys);
     a.exit_cnt = r->buf<int>(L.st_exit);
     a.max_tiles = L.st_max_tiles;
-    a.attn_cap = cap_tok;
+    a.plan = plan;
+    a.pref_kb = 0;  // L2 prefetch past the rings: measured slower (the rings alone saturate HBM)
+    if (const char* pv = getenv("AXB_STEP_PREF")) a.pref_kb = atoi(pv);
+    a.spin_limit = kStepSpinLimit;
+    a.mbar_limit = kStepMbarLimit;
+    a.hdump = nullptr;
     const char* tr = getenv("AXB_STEP_TRACE");  // phase timeline into runner buffer 5
     a.trace = (tr && atoi(tr) != 0) ? r->buf<unsigned long long>(L.st_trace) : nullptr;
   }
@@ -730,7 +753,30 @@ int axb_runner_buffer(void* h, int which, size_t* off, size_t* bytes) {
     case 3: *off = r->L.xnorm; *bytes = rows * r->c.d_model * 4; break;
     case 4: *off = r->L.params + 16; *bytes = 4; break;
     case 5: *off = r->L.st_trace; *bytes = r->L.st_trace_bytes; break;
+    case 6: *off = r->L.st_hdump; *bytes = r->L.st_hdump_bytes; break;
     default: axb::set_error("runner_buffer: unknown buffer %d", which); return AXB_EINVAL;
+  }
+  return AXB_OK;
+}
+
+int axb_runner_set_debug(void* h, int flags, uint32_t spin_limit, uint32_t mbar_limit) {
+  Runner* r = reinterpret_cast<Runner*>(h);
+  AXB_CHECK_ARG(r, "runner_set_debug: null handle");
+  AXB_CHECK_ARG((flags & ~3) == 0, "runner_set_debug: unknown flags 0x%x", flags);
+  if (!r->step_ok) return AXB_OK;  // the per-kernel graph path has no step-kernel hooks
+  StepArgs& a = r->sa;
+  a.hdump = (flags & AXB_DEBUG_HDUMP) ? r->buf<__half>(r->L.st_hdump) : nullptr;
+  a.trace = (flags & AXB_DEBUG_TRACE) ? r->buf<unsigned long long>(r->L.st_trace) : nullptr;
+  a.spin_limit = spin_limit ? spin_limit : kStepSpinLimit;
+  a.mbar_limit = mbar_limit ? mbar_limit : kStepMbarLimit;
+  // captured step graphs hold the old arguments: drop them
+  for (auto it = r->graphs.begin(); it != r->graphs.end();) {
+    if (std::get<2>(it->first) == 2) {
+      cudaGraphExecDestroy(it->second);
+      it = r->graphs.erase(it);
+    } else {
+      ++it;
+    }
   }
   return AXB_OK;
 }

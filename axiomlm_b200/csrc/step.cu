@@ -11,20 +11,27 @@
 //
 // Design.
 //  * Every GEMV of the step is split "stream-K" over quantization groups with one
-//    rule: warp i of the grid owns units [i*U/W, (i+1)*U/W).  A warp's weight
-//    stream for the whole step is therefore known at launch.  Lane 0 streams it
-//    through a private ring of bulk copies (TMA, non-tensor form) and runs ahead
-//    across phase boundaries -- weights never depend on activations -- with an
-//    L2 prefetch further ahead, so HBM keeps streaming while the warp waits for
-//    the previous phase's activations.
-//  * Phases are ordered by completion counters in global memory (tiles finished,
-//    attention heads finished) instead of kernel boundaries.  Every wait is
-//    bounded; one that runs out records AXB_ETIMEOUT and the grid winds down.
-//  * A tile split between warps is finished by the last warp to arrive, which
-//    sums the partials in warp order: results are deterministic.
-//  * Attention runs on two groups of four warps per CTA over (sequence, kv head,
-//    split) items; the cached rows of an item are bulk-copied before the QKV
-//    phase has finished; RoPE and the new K/V row's quantized write are fused.
+//    rule: virtual warp i of the grid owns units [i*U/W, (i+1)*U/W).  A warp's
+//    weight stream for the whole step is therefore known at launch.  Lane 0
+//    streams it through a private ring of bulk copies (TMA, non-tensor form)
+//    that runs ahead across phase boundaries -- weights never depend on
+//    activations -- so HBM keeps streaming while the warp waits for the
+//    previous phase's activations.
+//  * 16 warps per SM, each under 128 registers.  The code of every phase is
+//    kept small (a one-group-per-iteration k loop read straight from the ring,
+//    no unrolled stage copies): the whole step's hot code has to stay in the
+//    SM's instruction cache, because each phase runs once per layer and a cold
+//    fetch of straight-line code costs microseconds.
+//  * Phases are ordered by completion counters in global memory (tiles
+//    finished, attention heads finished) instead of kernel boundaries.  Every
+//    wait is bounded (limits in StepArgs); one that runs out records
+//    AXB_ETIMEOUT and the grid winds down, waiting for its own copies first.
+//  * A tile split between warps is finished by the warp that owns its first
+//    unit, which sums the partials in warp order: results are deterministic.
+//  * Attention: one (sequence, kv head, split) item per CTA, on all 16 warps.
+//    The item's cached rows are bulk-copied before the QKV phase has finished;
+//    RoPE and the new K/V row's quantized write are fused.  The last split of a
+//    head to finish combines the head (no CTA waits for another's split).
 #include <algorithm>
 
 #include "kv.cuh"
@@ -33,53 +40,38 @@
 
 namespace axb {
 
-#ifndef AXB_STEP_CH
-#define AXB_STEP_CH 8
-#endif
-#ifndef AXB_STEP_WARPS
-#define AXB_STEP_WARPS 8
-#endif
-#ifndef AXB_STEP_STAGES
-#define AXB_STEP_STAGES (AXB_STEP_WARPS >= 16 ? 2 : 3)
-#endif
-#ifndef AXB_STEP_CHAINS
-#define AXB_STEP_CHAINS 2
-#endif
-// 1: the GEMV / attention / norm bodies are separate functions (smaller code, own register budgets)
-#ifndef AXB_STEP_OUTLINE
-#define AXB_STEP_OUTLINE 0
-#endif
-// 1: a stage is copied to registers and its ring slot re-armed before the math
-#ifndef AXB_STEP_REGSTAGE
-#define AXB_STEP_REGSTAGE 1
-#endif
-#if AXB_STEP_OUTLINE
-#define AXB_STEP_FN __noinline__
-#else
-#define AXB_STEP_FN __forceinline__
-#endif
-constexpr int kSW = AXB_STEP_WARPS;  // warps per CTA (one CTA per SM)
+constexpr int kSW = 16;  // warps per CTA (one CTA per SM)
 constexpr int kSThreads = kSW * 32;
-constexpr int kSCH = AXB_STEP_CH;          // k-blocks (512 B of weights each) per ring stage
-constexpr int kSStages = AXB_STEP_STAGES;  // ring stages per warp
-constexpr int kSChains = AXB_STEP_CHAINS;  // independent MMA accumulator chains per warp
-constexpr int kSStageW = kSCH * 512;
-constexpr int kSStageS = kSCH * 64;  // scale bytes per stage (max: affine, one group per k-block)
-constexpr int kSRing = (kSStages * (kSStageW + kSStageS) + kSStages * 8 + 127) / 128 * 128;
-// staged activations, or the two attention groups' working sets
-constexpr int kSUnion = (kSW >= 16 ? 72 : 96) * 1024;
-constexpr int kSMisc = 1024;  // reduction scratch [kSW][kStepMaxM] + attention mbarriers + flags
-constexpr size_t kSSmem = (size_t)kSW * kSRing + kSUnion + kSMisc;
-constexpr int kSGroups = 2;  // attention groups (4 warps each, warps 0-7) per CTA
-constexpr uint32_t kSpinLimit = 1u << 22;
-constexpr uint32_t kSMbarLimit = 1u << 22;
-constexpr int kMaxRepS = 4;  // q heads per kv head (GQA up to 4:1; larger ratios use the per-kernel runner)
-constexpr int kXsumLd = 16;  // tokens per group row of the staged-x sums
+constexpr int kSL = 4;                        // k-blocks (512 B of weights each) per ring slot
+constexpr int kSlotW = kSL * 512;             // weight bytes of a slot
+constexpr int kSlotS = kSL * 64;              // scale bytes of a slot (max: affine, one group per k-block)
+constexpr int kSlotB = kSlotW + kSlotS;       // 2304
+constexpr int kMaxSlots = 8;                  // ring slots per warp (upper bound; the plan picks 3-4)
+constexpr int kSBars = kSW * kMaxSlots * 8;   // ring mbarriers
+constexpr int kSMisc = 4096;                  // reduction scratch, attention mbarrier, flags, combine weights
+constexpr int kSmemMax = 227 * 1024;
+constexpr int kMaxRepS = 8;                   // q heads per kv head (the 8 rows of the score MMA)
+constexpr int kXsLd = kStepMaxM;              // tokens per group row of the staged-x sums
+constexpr uint32_t kDrainLimit = 1u << 22;    // polls for copies already in flight (not a runtime limit)
+// misc-region offsets
+constexpr int kMiscRed = 0;      // float [kSW][kStepMaxM]
+constexpr int kMiscBar = 512;    // uint64 attention mbarrier
+constexpr int kMiscFlag = 576;   // int flags
+constexpr int kMiscLs = 640;     // float [kMaxRepS] combined softmax sums
+constexpr int kMiscCoef = 1024;  // float [kMaxRepS][kStepMaxSplits] split weights
+constexpr int kMiscCur = 3072;   // per-warp producer cursors (lane 0), kept out of registers
+static_assert(kMiscCoef + kMaxRepS * kStepMaxSplits * 4 <= kMiscCur, "misc region");
+static_assert(kSW * kStepMaxM * 4 <= kMiscBar, "reduction scratch");
+static_assert(kSlotB % 128 == 0 && kSlotW % 16 == 0, "bulk-copy alignment");
+static_assert(kSW <= kStepTraceW, "trace slots per phase");
+
+__host__ __device__ constexpr int round_up_i(int v, int m) { return (v + m - 1) / m * m; }
 // the staged-x sums of a K-wide activation sit at the end of the union, the rows from its start
-__host__ __device__ constexpr int xsum_bytes(int K, int G) { return ((K / G) * kXsumLd * 4 + 127) / 128 * 128; }
-__host__ __device__ constexpr bool xs_fits(int M, int K, int G) {
-  return (long long)M * (K + 8) * 2 <= (long long)(kSUnion - xsum_bytes(K, G));
+__host__ __device__ constexpr int xsum_bytes(int K, int G) { return round_up_i((K / G) * kXsLd * 4, 128); }
+__host__ __device__ constexpr int stage_bytes(int M, int K, int G) {
+  return round_up_i(M * (K + 8) * 2, 128) + xsum_bytes(K, G);
 }
+
 // D = A * B with a zero accumulator (the first MMA of a chain)
 __device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -88,12 +80,6 @@ __device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t (&a)[4
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
 }
-static_assert(kSSmem <= 227 * 1024, "step kernel shared memory");
-static_assert(kSStageW % 16 == 0 && kSStageS % 16 == 0 && kSRing % 128 == 0, "bulk-copy alignment");
-static_assert((kSStages * (kSStageW + kSStageS)) % 8 == 0, "mbarrier alignment");
-static_assert(kSW >= 4 * kSGroups, "attention groups are 4 warps");
-static_assert(kSW * kStepMaxM * 4 <= 512, "reduction scratch");
-static_assert(kSW <= kStepTraceW, "trace slots per phase");
 
 // ------------------------------------------------------------------ helpers
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -102,9 +88,9 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   return v;
 }
 // Hand-offs between CTAs: the writers of a block of results meet at a warp /
-// group / CTA barrier, then one thread publishes with a release (or acq_rel)
-// atomic; the reader polls with an acquire load and meets its peers at a
-// barrier before they read.  No full fences.
+// CTA barrier, then one thread publishes with a release (or acq_rel) atomic;
+// the reader polls with an acquire load and meets its peers at a barrier
+// before they read.  No full fences.
 __device__ __forceinline__ void red_release_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -112,17 +98,6 @@ __device__ __forceinline__ int atom_acq_rel_add(int* p, int v) {
   int old;
   asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
-}
-__device__ __forceinline__ void group_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
-// barrier of one attention group that also ORs a predicate over its 128 threads
-__device__ __forceinline__ bool group_bar_or(int id, bool p) {
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred q, o;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred o, %2, 128, q;\n selp.u32 %0, 1, 0, o;\n}\n"
-      : "=r"(r)
-      : "r"((uint32_t)p), "r"(id)
-      : "memory");
-  return r != 0;
 }
 __device__ __forceinline__ int tiles_of(int n) { return (n + 15) >> 4; }
 
@@ -138,28 +113,27 @@ __device__ __forceinline__ void trace_mark(const StepArgs& a, int slot) {
   if (threadIdx.x == 0) trace_at(a, slot);
 }
 
-// Bounded wait for *ctr >= target.  Gives up early when another CTA has already
-// raised the abort flag; on running out it raises the flag and records
-// AXB_ETIMEOUT in the error word.
-__device__ bool wait_ge(const int* ctr, int target, const StepArgs& a) {
-  int* abort_flag = a.exit_cnt + 1;
-  for (uint32_t it = 0; it < kSpinLimit; ++it) {
-    if (ld_acquire(ctr) >= target) return true;
-    if ((it & 15) == 15 && *reinterpret_cast<volatile int*>(abort_flag) != 0) return false;
-    __nanosleep(it < 32 ? 20 : 200);
-  }
-  atomicExch(abort_flag, 1);
-  atomicExch(a.err, AXB_ETIMEOUT);
-  return false;
-}
-
-__device__ void raise_abort(const StepArgs& a) {
+__device__ __forceinline__ void raise_abort(const StepArgs& a) {
   atomicExch(a.exit_cnt + 1, 1);
   atomicExch(a.err, AXB_ETIMEOUT);
 }
 
+// Bounded wait for *ctr >= target (a.spin_limit polls).  Gives up early when
+// another CTA has already raised the abort flag; on running out it raises the
+// flag and records AXB_ETIMEOUT in the error word.
+__device__ __noinline__ bool wait_ge(const int* ctr, int target, const StepArgs& a) {
+  const int* abort_flag = a.exit_cnt + 1;
+  for (uint32_t it = 0; it < a.spin_limit; ++it) {
+    if (ld_acquire(ctr) >= target) return true;
+    if ((it & 15) == 15 && *reinterpret_cast<const volatile int*>(abort_flag) != 0) return false;
+    __nanosleep(32);
+  }
+  raise_abort(a);
+  return false;
+}
+
 // CTA-wide wait: thread 0 polls, the barrier publishes the outcome.
-__device__ bool cta_wait(const int* ctr, int target, const StepArgs& a, bool ok) {
+__device__ __forceinline__ bool cta_wait(const int* ctr, int target, const StepArgs& a, bool ok) {
   int good = 0;
   if (threadIdx.x == 0 && ok) good = wait_ge(ctr, target, a) ? 1 : 0;
   return __syncthreads_or(good) != 0;
@@ -170,15 +144,15 @@ __device__ bool cta_wait(const int* ctr, int target, const StepArgs& a, bool ok)
 struct GPh {
   const char* W;
   const char* S;
-  int N, K, upt, kind;
-  long long U;
+  int N, K, upt, kind, layer;
+  uint32_t U;  // units (tile, group); U * warps < 2^32 for every supported shape (host-checked)
 };
 
 // Warps that share a GEMV: min(warps, units), so every participating warp
 // owns at least one unit (the arrival count of a split tile relies on it).
 // Virtual warp v owns units [v*U/We, (v+1)*U/We); v = wid * C + cta spreads a
 // small GEMV over all CTAs.
-__device__ __forceinline__ long long eff_warps(long long U, int Wt) { return U < Wt ? U : (long long)Wt; }
+__device__ __forceinline__ uint32_t eff_warps(uint32_t U, int Wt) { return U < (uint32_t)Wt ? U : (uint32_t)Wt; }
 
 __device__ __forceinline__ GPh gph(const StepArgs& a, int ph) {
   GPh g;
@@ -188,12 +162,14 @@ __device__ __forceinline__ GPh gph(const StepArgs& a, int ph) {
     g.N = a.V;
     g.K = a.d;
     g.kind = 4;
+    g.layer = a.L;
   } else {
     const StepLayer* ly = a.layers + (ph >> 2);
     const int k = ph & 3;
     g.W = ly->w[k];
     g.S = ly->s[k];
     g.kind = k;
+    g.layer = ph >> 2;
     switch (k) {
       case 0: g.N = (a.Hq + 2 * a.Hkv) * a.hd; g.K = a.d; break;
       case 1: g.N = a.d; g.K = a.Hq * a.hd; break;
@@ -202,33 +178,35 @@ __device__ __forceinline__ GPh gph(const StepArgs& a, int ph) {
     }
   }
   g.upt = g.K / a.group;
-  g.U = (long long)tiles_of(g.N) * g.upt;
+  g.U = (uint32_t)tiles_of(g.N) * (uint32_t)g.upt;
   return g;
 }
 
 // Producer cursor over a warp's weight stream (lane 0 only).
 struct Cur {
   int ph, t, t_last, kb, kb_end, upt;
-  long long u0, u1;
+  uint32_t u0, u1;
   const char* W;
   const char* S;
 };
 
+static_assert(kMiscCur + kSW * sizeof(Cur) <= kSMisc, "producer cursors");
+
 template <int GB>
 __device__ __forceinline__ void cur_tile(Cur& c) {
-  c.kb = (int)max(c.u0, (long long)c.t * c.upt) * GB;
-  c.kb_end = (int)min(c.u1, (long long)(c.t + 1) * c.upt) * GB;
+  c.kb = (int)max(c.u0, (uint32_t)(c.t * c.upt)) * GB;
+  c.kb_end = (int)min(c.u1, (uint32_t)((c.t + 1) * c.upt)) * GB;
 }
 
 template <int GB>
-__device__ void cur_load(Cur& c, const StepArgs& a, int gw, int Wt) {
+__device__ __forceinline__ void cur_load(Cur& c, const StepArgs& a, int gw, int Wt) {
   const GPh g = gph(a, c.ph);
   c.W = g.W;
   c.S = g.S;
   c.upt = g.upt;
-  const long long We = eff_warps(g.U, Wt);
-  c.u0 = gw < We ? (long long)gw * g.U / We : 0;
-  c.u1 = gw < We ? (long long)(gw + 1) * g.U / We : 0;
+  const uint32_t We = eff_warps(g.U, Wt);
+  c.u0 = (uint32_t)gw < We ? (uint32_t)gw * g.U / We : 0u;
+  c.u1 = (uint32_t)gw < We ? ((uint32_t)gw + 1u) * g.U / We : 0u;
   if (c.u0 >= c.u1) {
     c.t = 0;
     c.t_last = -1;
@@ -242,7 +220,7 @@ __device__ void cur_load(Cur& c, const StepArgs& a, int gw, int Wt) {
 
 // advance past exhausted tiles / phases; false at the end of the step
 template <int GB>
-__device__ bool cur_fix(Cur& c, const StepArgs& a, int gw, int Wt) {
+__device__ __forceinline__ bool cur_fix(Cur& c, const StepArgs& a, int gw, int Wt) {
   while (c.kb >= c.kb_end) {
     if (c.t < c.t_last) {
       ++c.t;
@@ -256,20 +234,22 @@ __device__ bool cur_fix(Cur& c, const StepArgs& a, int gw, int Wt) {
   return true;
 }
 
-// Per-warp ring of kSStages slots.  Slot indices and mbarrier parities are
-// advanced incrementally (no divisions on the per-stage path).  A slot is
-// re-armed by the same warp after its stage has been computed: the generic
-// loads of the stage have returned by then, so no proxy fence is needed.
+// Per-warp ring of n slots.  Slot indices and mbarrier parities are advanced
+// incrementally.  A slot is re-armed by the same warp after its last read
+// (the warp's generic loads of the slot have returned by then), so no proxy
+// fence is needed.  A slot never spans two tiles: the consumer derives each
+// slot's k-block count from its own loop, in the producer's order.
 struct Ring {
   char* buf;
   uint64_t* bars;
+  int n;            // slots
   int cs, cpar;     // consumer: next slot and the parity its mbarrier completes with
   int ps;           // producer (lane 0): next slot to fill
-  int inflight;     // producer (lane 0): stages issued and not yet consumed
+  int inflight;     // producer (lane 0): slots issued and not yet consumed
 };
 
 __device__ __forceinline__ void ring_consumed(Ring& r) {
-  if (++r.cs == kSStages) {
+  if (++r.cs == r.n) {
     r.cs = 0;
     r.cpar ^= 1;
   }
@@ -282,90 +262,111 @@ __device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, const StepArgs& a, 
   constexpr int UB = SYM ? 32 : 64;  // scale bytes per group
   if (pc.kb >= pc.kb_end && !cur_fix<GB>(pc, a, gw, Wt)) return;
   const int st = r.ps;
-  r.ps = st + 1 == kSStages ? 0 : st + 1;
-  const int n = min(kSCH, pc.kb_end - pc.kb);
-  const uint32_t bw = n * 512, bs = (n / GB) * UB;
+  r.ps = st + 1 == r.n ? 0 : st + 1;
+  const int nk = min(kSL, pc.kb_end - pc.kb);
+  const uint32_t bw = nk * 512, bs = (nk / GB) * UB;
+  char* slot = r.buf + (size_t)st * kSlotB;
+  const uint64_t pol = l2_evict_first_policy();
   mbar_expect_tx(r.bars + st, bw + bs);
-  bulk_g2s(r.buf + st * kSStageW, pc.W + (size_t)pc.kb * 512, bw, r.bars + st);
-  bulk_g2s(r.buf + kSStages * kSStageW + st * kSStageS, pc.S + (size_t)(pc.kb / GB) * UB, bs, r.bars + st);
-  pc.kb += n;
+  bulk_g2s_hint(slot, pc.W + (size_t)pc.kb * 512, bw, r.bars + st, pol);
+  bulk_g2s_hint(slot + kSlotW, pc.S + (size_t)(pc.kb / GB) * UB, bs, r.bars + st, pol);
+  // keep the stream further ahead in flight through L2: the k-blocks a.pref_kb
+  // past this slot, while they stay in this warp's range of the phase (the
+  // range is one contiguous run of tiles)
+  if (a.pref_kb > 0) {
+    const int kp = pc.kb + a.pref_kb, kend = (int)pc.u1 * GB;
+    if (kp < kend) {
+      const int np = min(kSL, kend - kp);
+      bulk_prefetch_l2(pc.W + (size_t)kp * 512, np * 512);
+      if (np >= GB) bulk_prefetch_l2(pc.S + (size_t)(kp / GB) * UB, (np / GB) * UB);
+    }
+  }
+  pc.kb += nk;
   ++r.inflight;
 }
 
-__device__ __forceinline__ int warp_of_unit(long long u, long long U, long long Wt) {
-  return (int)(((u + 1) * Wt - 1) / U);
+__device__ __forceinline__ int warp_of_unit(uint32_t u, uint32_t U, uint32_t We) {
+  return (int)(((u + 1) * We - 1) / U);
 }
 
-// Tile epilogue: token n = 2*t4 + e, rows tile*16 + g (+8).
-__device__ void step_epilogue(const StepArgs& a, const GPh& g, int tile, const float (&acc)[4], int lane) {
+// Tile epilogue: token n = 2*t4 + e, rows tile*16 + g (+8).  The kind is
+// dispatched once, and the small loops stay rolled (the epilogue runs once
+// per tile; its code has to stay small, not fast).
+__device__ __forceinline__ void step_epilogue(const StepArgs& a, const GPh& g, int tile, float v00, float v01,
+                                           float v10, float v11, int lane) {
   const int gg = lane >> 2, t4 = lane & 3;
-  const int r0 = tile * 16 + gg, r1 = r0 + 8;
+  const int r0 = tile * 16 + gg;
   const int M = a.B;
-  unsigned long long best[2] = {0ull, 0ull};
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const int n = 2 * t4 + e;
-    if (n >= M) continue;
-    const float v0 = acc[e], v1 = acc[2 + e];
-    if (g.kind == 2) {  // SwiGLU: rows g (gate) and g + 8 (up) of the interleaved tile
-      const int j = tile * 8 + gg;
-      if (j < a.F) {
-        const float gv = __half2float(__float2half_rn(v0));
-        const float uv = __half2float(__float2half_rn(v1));
-        a.sw[(size_t)n * a.F + j] = __float2half_rn(__fmul_rn(silu_f(gv), uv));
-      }
-      continue;
+  const float acc[4] = {v00, v01, v10, v11};
+  if (g.kind == 2) {  // SwiGLU: rows g (gate) and g + 8 (up) of the interleaved tile
+    const int j = tile * 8 + gg;
+#pragma unroll 1
+    for (int e = 0; e < 2; ++e) {
+      const int n = 2 * t4 + e;
+      if (n >= M || j >= a.F) continue;
+      const float gv = __half2float(__float2half_rn(acc[e]));
+      const float uv = __half2float(__float2half_rn(acc[2 + e]));
+      a.sw[(size_t)n * a.F + j] = __float2half_rn(__fmul_rn(silu_f(gv), uv));
     }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int row = h ? r1 : r0;
-      if (row >= g.N) continue;
-      float v = h ? v1 : v0;
-      if (g.kind == 0) {
-        a.qkv[(size_t)n * g.N + row] = __float2half_rn(v);
-      } else if (g.kind == 4) {
-        const __half vh = __float2half_rn(v);
+    return;
+  }
+  if (g.kind == 4) {  // lm_head: logits + per-token argmax key
+#pragma unroll 1
+    for (int e = 0; e < 2; ++e) {
+      const int n = 2 * t4 + e;
+      unsigned long long best = 0ull;
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        const int row = r0 + 8 * hh;
+        if (n >= M || row >= g.N) continue;
+        const __half vh = __float2half_rn(acc[2 * hh + e]);
         a.logits[(size_t)n * a.V + row] = vh;
         // argmax key: ordered value bits, then the lowest row wins ties
         uint32_t bits = __float_as_uint(__half2float(vh));
+        if (bits == 0x80000000u) bits = 0u;  // -0 == +0: a tie, which the lower row wins
         bits = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
         const unsigned long long key = ((unsigned long long)bits << 32) | (0xFFFFFFFFu - (uint32_t)row);
-        best[e] = key > best[e] ? key : best[e];
-      } else {  // residual add into h (fp16 GEMV output, fp16 sum)
-        __half* hp = a.h + (size_t)n * a.d + row;
-        const float old = __half2float(__ldcg(hp));
-        *hp = __float2half_rn(__fadd_rn(old, __half2float(__float2half_rn(v))));
+        best = key > best ? key : best;
       }
-    }
-  }
-  if (g.kind == 4) {
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      unsigned long long k = best[e];
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) {
-        const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
-        k = ok > k ? ok : k;
+        const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best, o);
+        best = ok > best ? ok : best;
       }
-      const int n = 2 * t4 + e;
-      if (gg == 0 && n < M && k) atomicMax(a.keys + n, k);
+      if (gg == 0 && n < M && best) atomicMax(a.keys + n, best);
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int q = 0; q < 4; ++q) {
+    const int n = 2 * t4 + (q & 1), row = r0 + 8 * (q >> 1);
+    if (n >= M || row >= g.N) continue;
+    if (g.kind == 0) {
+      a.qkv[(size_t)n * g.N + row] = __float2half_rn(acc[q]);
+    } else {  // residual add into h (fp16 GEMV output, fp16 sum)
+      __half* hp = a.h + (size_t)n * a.d + row;
+      const float old = __half2float(__ldcg(hp));
+      const __half nv = __float2half_rn(__fadd_rn(old, __half2float(__float2half_rn(acc[q]))));
+      *hp = nv;
+      if (g.kind == 3 && a.hdump) a.hdump[((size_t)g.layer * M + n) * a.d + row] = nv;
     }
   }
 }
 
 // QKV bias (c_attn_bs) is folded in by the QKV tile finisher
-__device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const StepLayer* ly, const GPh& g, int tile,
-                                             float (&acc)[4], int lane) {
-  if (g.kind != 0 || ly == nullptr || ly->qkv_b == nullptr) return;
+__device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const GPh& g, int tile, float (&acc)[4], int lane) {
+  if (g.kind != 0) return;
+  const __half* qb = a.layers[g.layer].qkv_b;
+  if (qb == nullptr) return;
   const int gg = lane >> 2;
   const int r0 = tile * 16 + gg, r1 = r0 + 8;
   if (r0 < g.N) {
-    const float b0 = __half2float(ly->qkv_b[r0]);
+    const float b0 = __half2float(qb[r0]);
     acc[0] = __fadd_rn(acc[0], b0);
     acc[1] = __fadd_rn(acc[1], b0);
   }
   if (r1 < g.N) {
-    const float b1 = __half2float(ly->qkv_b[r1]);
+    const float b1 = __half2float(qb[r1]);
     acc[2] = __fadd_rn(acc[2], b1);
     acc[3] = __fadd_rn(acc[3], b1);
   }
@@ -373,15 +374,16 @@ __device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const StepLayer*
 
 // One GEMV phase for this warp.  x is staged in shared memory (XS: normalized
 // rows + per-group sums) or read from global memory (L2) one k-block ahead.
+// The k loop handles one quantization group (GB k-blocks) per iteration,
+// reading the weights straight from the ring slot.
 template <bool SYM, int GB, bool XS>
-__device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, const __half* xs, int xs_stride,
-                           const float* xsum, const __half* xg, int ldx, int gw, int Wt, int lane,
-                           bool ok, int* done_ctr) {
+__device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, const __half* xs,
+                                           int xs_stride, const float* xsum, const __half* xg, int ldx, int gw,
+                                           int Wt, int lane, bool ok, int* done_ctr) {
   const GPh g = gph(a, ph);
-  const long long We = eff_warps(g.U, Wt);
-  if (gw >= We || !ok) return ok;
-  const long long u0 = (long long)gw * g.U / We, u1 = (long long)(gw + 1) * g.U / We;
-  const StepLayer* ly = ph < 4 * a.L ? a.layers + (ph >> 2) : nullptr;
+  const uint32_t We = eff_warps(g.U, Wt);
+  if ((uint32_t)gw >= We || !ok) return ok;
+  const uint32_t u0 = (uint32_t)gw * g.U / We, u1 = ((uint32_t)gw + 1u) * g.U / We;
   const int gq = lane >> 2, t4 = lane & 3;
   const int KB = g.K / 64;
   const int t_first = (int)(u0 / g.upt), t_last = (int)((u1 - 1) / g.upt);
@@ -389,64 +391,37 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
   const uint4* xrow = reinterpret_cast<const uint4*>((XS ? xs + (size_t)nn * xs_stride : xg + (size_t)nn * ldx) +
                                                      16 * t4);
   int finished = 0;
-  constexpr int CH = kSChains;
   for (int t = t_first; t <= t_last && ok; ++t) {
-    const int kb_lo = (int)max(u0, (long long)t * g.upt) * GB;
-    const int kb_hi = (int)min(u1, (long long)(t + 1) * g.upt) * GB;
+    const int kb_lo = (int)max(u0, (uint32_t)(t * g.upt)) * GB;
+    const int kb_hi = (int)min(u1, (uint32_t)((t + 1) * g.upt)) * GB;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    // accumulators per MMA chain, in two sets used by alternate groups: the
-    // scale fold of one group overlaps the MMAs of the next
-    float tmp2[2][CH][4];
+    // two accumulator chains (alternate fragment words) so consecutive MMAs
+    // do not wait on each other; SYM restarts them per group, AFFINE (weights
+    // dequantized before the MMA) runs them over the tile
+    float c[2][4];
 #pragma unroll
-    for (int p2 = 0; p2 < 2; ++p2)
+    for (int q = 0; q < 2; ++q)
 #pragma unroll
-      for (int c2 = 0; c2 < CH; ++c2)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) tmp2[p2][c2][q] = 0.f;
+      for (int e = 0; e < 4; ++e) c[q][e] = 0.f;
     uint4 xn0 = make_uint4(0, 0, 0, 0), xn1 = xn0;
     if (!XS) {
       xn0 = __ldcg(xrow + (kb_lo - t * KB) * 8);
       xn1 = __ldcg(xrow + (kb_lo - t * KB) * 8 + 1);
     }
-    for (int kb0 = kb_lo; kb0 < kb_hi;) {
+    for (int kb = kb_lo; kb < kb_hi;) {
       const int st = r.cs;
-      const bool got = mbar_wait(r.bars + st, (uint32_t)r.cpar, kSMbarLimit);
-      if (!__all_sync(0xffffffffu, got)) {  // one decision for the whole warp
+      if (!__all_sync(0xffffffffu, mbar_wait(r.bars + st, (uint32_t)r.cpar, a.mbar_limit))) {
         if (lane == 0) raise_abort(a);
         ok = false;
         break;
       }
-      const int n = min(kSCH, kb_hi - kb0);
-      const uint4* wst = reinterpret_cast<const uint4*>(r.buf + st * kSStageW) + lane;
-      const char* sst = r.buf + kSStages * kSStageW + st * kSStageS;
-      const int kbt = kb0 - t * KB;
-      // copy the stage (this lane's words, the scales of its rows) into
-      // registers and hand the slot back at once: the next copy is in flight
-      // while this stage is computed
-      uint4 wreg[AXB_STEP_REGSTAGE ? kSCH : 1];
-      uint2 sreg[AXB_STEP_REGSTAGE ? kSCH : 1];  // SYM: .x = (s[g], s[g+8]); AFFINE: (s, b) pairs
-      if (AXB_STEP_REGSTAGE) {
-#pragma unroll
-        for (int j = 0; j < (AXB_STEP_REGSTAGE ? kSCH : 1); ++j) {
-          if (j < n) wreg[j] = wst[j * 32];
-          if (j < n / GB) {
-            if (SYM) sreg[j].x = reinterpret_cast<const uint32_t*>(sst)[j * 8 + gq];
-            else sreg[j] = reinterpret_cast<const uint2*>(sst)[j * 8 + gq];
-          }
-        }
-        __syncwarp();
-        ring_consumed(r);
-        ring_issue<SYM, GB>(r, pc, a, gw, Wt, lane);
-      }
-      auto wword = [&](const int j) -> uint4 { return AXB_STEP_REGSTAGE ? wreg[AXB_STEP_REGSTAGE ? j : 0] : wst[j * 32]; };
-      auto sword = [&](const int gi) -> uint2 {
-        if (AXB_STEP_REGSTAGE) return sreg[AXB_STEP_REGSTAGE ? gi : 0];
-        return SYM ? make_uint2(reinterpret_cast<const uint32_t*>(sst)[gi * 8 + gq], 0u)
-                   : reinterpret_cast<const uint2*>(sst)[gi * 8 + gq];
-      };
+      const int nk = min(kSL, kb_hi - kb);
+      const uint4* wsl = reinterpret_cast<const uint4*>(r.buf + (size_t)st * kSlotB) + lane;
+      const char* ssl = r.buf + (size_t)st * kSlotB + kSlotW;
+      const int kbt = kb - t * KB;
+      // one k-block of the slot; a group's scales are applied after its last k-block
       auto kblock = [&](const int j) {
-        float(&tmp)[CH][4] = tmp2[SYM ? ((j / GB) & 1) : 0];
-        const uint4 cur = wword(j);
+        const uint4 wv = wsl[j * 32];
         uint32_t bf[8];
         if (XS) {
           const uint4 v0 = xrow[(kbt + j) * 8], v1 = xrow[(kbt + j) * 8 + 1];
@@ -455,115 +430,79 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
         } else {
           bf[0] = xn0.x; bf[1] = xn0.y; bf[2] = xn0.z; bf[3] = xn0.w;
           bf[4] = xn1.x; bf[5] = xn1.y; bf[6] = xn1.z; bf[7] = xn1.w;
-          if (kb0 + j + 1 < kb_hi) {
+          if (kb + j + 1 < kb_hi) {
             xn0 = __ldcg(xrow + (kbt + j + 1) * 8);
             xn1 = __ldcg(xrow + (kbt + j + 1) * 8 + 1);
           }
         }
-        const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
-        if (SYM && XS) {
+        const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+        if (SYM) {
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
+          for (int q = 0; q < 4; ++q) {
             uint32_t af[4];
-            unpack_word_raw(words[jj], af);
-            // the first MMA of each chain in a group starts from zero
-            const bool fresh = (j % GB) == 0 && jj < CH;
-            if (fresh)
-              mma_16816_z(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1]);
-            else
-              mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
+            if (XS) unpack_word_raw(words[q], af);
+            else unpack_word<8>(words[q], af);
+            if ((j % GB) == 0 && q < 2) mma_16816_z(c[q & 1], af, bf[2 * q], bf[2 * q + 1]);
+            else mma_16816(c[q & 1], af, bf[2 * q], bf[2 * q + 1], c[q & 1]);
           }
-          if (GB == 1 || (j & 1)) {  // group complete: remove the offsets, apply the scales
-            const uint32_t sp = sword(j / GB).x;
-            const float2 sc = __half22float2(u32_as_h2(sp));
-            const int grp = (kbt + j) / GB;
-            const float2 xg2 = *reinterpret_cast<const float2*>(xsum + grp * kXsumLd + 2 * t4);
-            float s4[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float v = tmp[0][q];
-#pragma unroll
-              for (int c2 = 1; c2 < CH; ++c2) v += tmp[c2][q];
-              s4[q] = v;
-            }
-            acc[0] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.x, s4[0]), acc[0]);
-            acc[1] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.y, s4[1]), acc[1]);
-            acc[2] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[2], -72.f * xg2.x), acc[2]);
-            acc[3] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[3], -72.f * xg2.y), acc[3]);
-          }
-        } else if (SYM) {
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            uint32_t af[4];
-            unpack_word<8>(words[jj], af);
-            const bool fresh = (j % GB) == 0 && jj < CH;
-            if (fresh)
-              mma_16816_z(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1]);
-            else
-              mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
-          }
-          if (GB == 1 || (j & 1)) {
-            const uint32_t sp = sword(j / GB).x;
+          if ((j % GB) == GB - 1) {  // group complete: apply the scales (XS: remove the magic offsets first)
+            const uint32_t sp = reinterpret_cast<const uint32_t*>(ssl)[(j / GB) * 8 + gq];
             const float2 sc = __half22float2(u32_as_h2(sp));
             float s4[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float v = tmp[0][q];
-#pragma unroll
-              for (int c2 = 1; c2 < CH; ++c2) v += tmp[c2][q];
-              s4[q] = v;
+            for (int e = 0; e < 4; ++e) s4[e] = c[0][e] + c[1][e];
+            if (XS) {
+              const float2 xg2 = *reinterpret_cast<const float2*>(xsum + ((kbt + j) / GB) * kXsLd + 2 * t4);
+              acc[0] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.x, s4[0]), acc[0]);
+              acc[1] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.y, s4[1]), acc[1]);
+              acc[2] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[2], -72.f * xg2.x), acc[2]);
+              acc[3] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[3], -72.f * xg2.y), acc[3]);
+            } else {
+              acc[0] = __fmaf_rn(sc.x, s4[0], acc[0]);
+              acc[1] = __fmaf_rn(sc.x, s4[1], acc[1]);
+              acc[2] = __fmaf_rn(sc.y, s4[2], acc[2]);
+              acc[3] = __fmaf_rn(sc.y, s4[3], acc[3]);
             }
-            acc[0] = __fmaf_rn(sc.x, s4[0], acc[0]);
-            acc[1] = __fmaf_rn(sc.x, s4[1], acc[1]);
-            acc[2] = __fmaf_rn(sc.y, s4[2], acc[2]);
-            acc[3] = __fmaf_rn(sc.y, s4[3], acc[3]);
           }
         } else {
-          const uint2 sb = sword(j / GB);
+          const uint2 sb = reinterpret_cast<const uint2*>(ssl)[j * 8 + gq];
           const __half2 s01 = u32_as_h2(sb.x), s23 = u32_as_h2(sb.y);
           const __half2 sg = __half2half2(__low2half(s01)), bg = __half2half2(__high2half(s01));
           const __half2 sg8 = __half2half2(__low2half(s23)), bg8 = __half2half2(__high2half(s23));
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
+          for (int q = 0; q < 4; ++q) {
             uint32_t af[4];
-            unpack_word<0>(words[jj], af);
+            unpack_word<0>(words[q], af);
             af[0] = h2_as_u32(__hfma2(u32_as_h2(af[0]), sg, bg));
             af[1] = h2_as_u32(__hfma2(u32_as_h2(af[1]), sg8, bg8));
             af[2] = h2_as_u32(__hfma2(u32_as_h2(af[2]), sg, bg));
             af[3] = h2_as_u32(__hfma2(u32_as_h2(af[3]), sg8, bg8));
-            mma_16816(tmp[jj % CH], af, bf[2 * jj], bf[2 * jj + 1], tmp[jj % CH]);
+            mma_16816(c[q & 1], af, bf[2 * q], bf[2 * q + 1], c[q & 1]);
           }
         }
       };
-      if (n == kSCH) {
+      // one quantization group (GB k-blocks) per iteration: the loop body is
+      // the only copy of the GEMV math in the kernel (the step's code has to
+      // stay in the instruction cache)
+#pragma unroll 1
+      for (int j = 0; j < nk; j += GB) {
 #pragma unroll
-        for (int j = 0; j < kSCH; ++j) kblock(j);
-      } else {
-#pragma unroll
-        for (int j = 0; j < kSCH; ++j)
-          if (j < n) kblock(j);
+        for (int jj = 0; jj < GB; ++jj) kblock(j + jj);
       }
-      if (!AXB_STEP_REGSTAGE) {
-        __syncwarp();
-        ring_consumed(r);
-        ring_issue<SYM, GB>(r, pc, a, gw, Wt, lane);
-      }
-      kb0 += n;
+      __syncwarp();
+      ring_consumed(r);
+      ring_issue<SYM, GB>(r, pc, a, gw, Wt, lane);
+      kb += nk;
     }
     if (!ok) break;
     if (!SYM) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float v = tmp2[0][0][q];
-#pragma unroll
-        for (int c2 = 1; c2 < CH; ++c2) v += tmp2[0][c2][q];
-        acc[q] = v;
-      }
+      for (int e = 0; e < 4; ++e) acc[e] = c[0][e] + c[1][e];
     }
-    const bool complete = (long long)t * g.upt >= u0 && (long long)(t + 1) * g.upt <= u1;
+    const bool complete = (uint32_t)(t * g.upt) >= u0 && (uint32_t)((t + 1) * g.upt) <= u1;
     if (complete) {
-      qkv_bias_fix(a, ly, g, t, acc, lane);
-      step_epilogue(a, g, t, acc, lane);
+      qkv_bias_fix(a, g, t, acc, lane);
+      step_epilogue(a, g, t, acc[0], acc[1], acc[2], acc[3], lane);
       ++finished;
       continue;
     }
@@ -571,10 +510,10 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
     // is always that warp's last one (had its range run past the tile, it
     // would own the whole tile).  Every other warp of the tile has it as its
     // first tile: it publishes a partial and moves on without waiting.
-    const int wf = warp_of_unit((long long)t * g.upt, g.U, We);
-    const int wl = warp_of_unit((long long)(t + 1) * g.upt - 1, g.U, We);
+    const int wf = warp_of_unit((uint32_t)(t * g.upt), g.U, We);
+    const int wl = warp_of_unit((uint32_t)((t + 1) * g.upt - 1), g.U, We);
     if (gw != wf) {
-      float* p = a.partials + ((size_t)(gw * 2) * 32 + lane) * 4;
+      float* p = a.partials + ((size_t)gw * 32 + lane) * 4;
       *reinterpret_cast<float4*>(p) = make_float4(acc[0], acc[1], acc[2], acc[3]);
       __syncwarp();
       if (lane == 0) red_release_add(a.tile_cnt + t, 1);
@@ -592,7 +531,7 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
       float4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u)  // independent loads, all in flight
-        if (w0 + u <= wl) v[u] = __ldcg(reinterpret_cast<const float4*>(a.partials + ((size_t)((w0 + u) * 2) * 32 + lane) * 4));
+        if (w0 + u <= wl) v[u] = __ldcg(reinterpret_cast<const float4*>(a.partials + ((size_t)(w0 + u) * 32 + lane) * 4));
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         if (w0 + u > wl) continue;
@@ -602,8 +541,8 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
         tot[3] += v[u].w;
       }
     }
-    qkv_bias_fix(a, ly, g, t, tot, lane);
-    step_epilogue(a, g, t, tot, lane);
+    qkv_bias_fix(a, g, t, tot, lane);
+    step_epilogue(a, g, t, tot[0], tot[1], tot[2], tot[3], lane);
     if (lane == 0) a.tile_cnt[t] = 0;  // published by the done counter's release below
     ++finished;
   }
@@ -617,7 +556,7 @@ __device__ AXB_STEP_FN bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& 
 // ------------------------------------------------------------------ staging
 // Embedding rows (dequant_q8_rows, quant.py:132-163) into xs; CTA 0 also
 // stores them into h (the residual stream).
-__device__ void stage_embed(const StepArgs& a, __half* xs, int stride) {
+__device__ __noinline__ void stage_embed(const StepArgs& a, __half* xs, int stride) {
   const int K4 = a.d / 4;
   for (int i = threadIdx.x; i < a.B * K4; i += blockDim.x) {
     const int m = i / K4, k4 = i % K4;
@@ -643,19 +582,21 @@ __device__ void stage_embed(const StepArgs& a, __half* xs, int stride) {
 // from global memory (src), or the raw rows already in xs (src null).  With
 // an RMSNorm weight w (modules.py:30-43: rms = 1/sqrt(mean(x^2) + eps),
 // fp16((x * rms) * w)) the rows are normalized in place.  With sums (SYM
-// weights) the fp32 per-group sums of the staged rows follow.
+// weights) the fp32 per-group sums of the staged rows follow, reduced across
+// the G/8 consecutive lanes that hold a group.
 __device__ __noinline__ void stage_x(int B, int G, float eps, const __half* src, int K, const float* w, __half* xs,
                                      int stride, float* xsum, bool sums, float* red) {
   const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, wid = tid >> 5;
   const int K8 = K / 8;
+  // pass 1: copy (four 16-byte loads in flight per thread) + sums of squares
   for (int m = 0; m < B; ++m) {
-    float ss = 0.f;
     const uint4* srow = src ? reinterpret_cast<const uint4*>(src + (size_t)m * K) : nullptr;
     uint4* drow = reinterpret_cast<uint4*>(xs + (size_t)m * stride);
+    float ss = 0.f;
     for (int c0 = tid; c0 < K8; c0 += 4 * nth) {
       uint4 v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)  // all loads of the round in flight together
+      for (int u = 0; u < 4; ++u)
         if (c0 + u * nth < K8) v[u] = srow ? __ldcg(srow + c0 + u * nth) : drow[c0 + u * nth];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -678,102 +619,154 @@ __device__ __noinline__ void stage_x(int B, int G, float eps, const __half* src,
     }
   }
   __syncthreads();
-  if (w) {
-    for (int i = tid; i < B * K8; i += nth) {
-      const int m = i / K8, c = i % K8;
+  if (!w && !sums) return;
+  // pass 2: normalize in place, then the group sums (whole-warp trip counts:
+  // a group's G/8 lanes are consecutive and never straddle a warp, K8 being a
+  // multiple of 16)
+  const int lpg = G / 8;
+  for (int m = 0; m < B; ++m) {
+    float rms = 0.f;
+    if (w) {
       float tot = 0.f;
       for (int ww = 0; ww < (nth >> 5); ++ww) tot += red[ww * kStepMaxM + m];
-      const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), eps)));
-      uint4* sp = reinterpret_cast<uint4*>(xs + (size_t)m * stride) + c;
-      const uint4 v = *sp;
-      const __half2* hh = reinterpret_cast<const __half2*>(&v);
-      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c);
-      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c + 1);
-      const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      uint4 o;
-      __half2* oh = reinterpret_cast<__half2*>(&o);
+      rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), eps)));
+    }
+    uint4* drow = reinterpret_cast<uint4*>(xs + (size_t)m * stride);
+    for (int c0 = 0; c0 < K8; c0 += nth) {
+      const int cc = c0 + tid;
+      const bool act = cc < K8;
+      uint4 v = act ? drow[cc] : make_uint4(0, 0, 0, 0);
+      if (w && act) {
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * cc);
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * cc + 1);
+        const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const __half2* hh = reinterpret_cast<const __half2*>(&v);
+        uint4 o;
+        __half2* oh = reinterpret_cast<__half2*>(&o);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __half22float2(hh[q]);
-        oh[q] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, rms), ws[2 * q]),
-                                  __fmul_rn(__fmul_rn(f.y, rms), ws[2 * q + 1]));
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(hh[q]);
+          oh[q] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, rms), ws[2 * q]),
+                                    __fmul_rn(__fmul_rn(f.y, rms), ws[2 * q + 1]));
+        }
+        drow[cc] = o;
+        v = o;
       }
-      *sp = o;
-    }
-    __syncthreads();
-  }
-  if (sums) {
-    const int ngr = K / G, nw = nth >> 5;
-    for (int item = wid; item < ngr * B; item += nw) {
-      const int grp = item % ngr, m = item / ngr;
-      const __half* sx = xs + (size_t)m * stride + grp * G;
-      float v = 0.f;
-      for (int k = lane * 2; k < G; k += 64) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(sx + k));
-        v += f.x + f.y;
+      if (sums) {
+        const __half2* hh = reinterpret_cast<const __half2*>(&v);
+        float gs = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(hh[q]);
+          gs += f.x + f.y;
+        }
+        for (int o = 1; o < lpg; o <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
+        if (act && (cc & (lpg - 1)) == 0) xsum[(cc / lpg) * kXsLd + m] = gs;
       }
-      v = warp_sum(v);
-      if (lane == 0) xsum[grp * kXsumLd + m] = v;
     }
-    __syncthreads();
   }
+  __syncthreads();
 }
 
 // ------------------------------------------------------------------ attention
+// K/V rows are staged by TMA tensor copies in boxes of kBoxRows rows and at
+// most 128 bytes of a row (a "plane"; fp16 rows of 256 B take two planes),
+// with the copy engine's 16-byte-chunk swizzle (the XOR of the chunk index
+// with the row's position in the 1 KB swizzle atom): the eight rows one MMA
+// fragment reads then fall in different shared-memory banks.
+constexpr int kBoxRows = 32;
+
+__host__ __device__ constexpr int kv_box_bytes(int rb) { return rb < 128 ? rb : 128; }
+
+// byte b (< BX) of staged row r of one plane, swizzled as the copy engine
+// writes it (the plane starts on a 1 KB boundary)
+template <int BX>
+__device__ __forceinline__ int swz(int r, int b) {
+  return r * BX + ((((b >> 4) ^ ((r * BX >> 7) & (BX / 16 - 1)))) << 4) + (b & 15);
+}
+
 struct AttnLayout {
-  int rb, ng, kv, ksc, vsc, qh, p, ml, coef, bytes;
+  int rb, bx, np, ng, kv, ksc, vsc, qh, qs, p, ps, ml, bytes;
 };
 
-// Working set of one attention group: staged K and V rows, their fp16 scales
-// (bulk-copied with the rows), q as fp16 hi / lo parts (8 rows, the ones past
-// n_rep zero), the probabilities, the online-softmax state and the split
-// combine weights.
+// Working set of one attention item: the staged K and V planes (1 KB
+// aligned; the union start is aligned up at run time, hence the slack), their
+// fp16 scales, q as fp16 hi / lo parts (8 rows, the ones past n_rep zero;
+// rows HD/2 + 4 words apart), the probabilities (rows cap + 8 floats apart)
+// and the online-softmax state.  cap is a multiple of kBoxRows.
 __host__ __device__ inline AttnLayout attn_layout(int kv_type, int hd, int kv_group, int cap) {
   AttnLayout L;
   L.rb = kv_row_bytes(kv_type, hd);
+  L.bx = kv_box_bytes(L.rb);
+  L.np = L.rb / L.bx;
   L.ng = kv_type == AXB_KV_F16 ? 1 : hd / kv_group;
   int off = 0;
   L.kv = off;
   off += 2 * cap * L.rb;
-  off = (off + 15) / 16 * 16;
-  const int sb = (cap * L.ng * 2 + 15) / 16 * 16;
+  const int sb = round_up_i(cap * L.ng * 2, 16);
   L.ksc = off;
   off += sb;
   L.vsc = off;
   off += sb;
+  L.qs = hd / 2 + 4;
   L.qh = off;
-  off += 2 * 8 * hd * 2;
+  off += 2 * 8 * L.qs * 4;
+  L.ps = cap + 8;
   L.p = off;
-  off += kMaxRepS * cap * 4;
+  off += kMaxRepS * L.ps * 4;
   L.ml = off;
-  off += 32 * 4;  // m[8], l[8], alpha[8], flags
-  L.coef = off;
-  off += kMaxRepS * kStepMaxSplits * 4;
-  L.bytes = (off + 127) / 128 * 128;
+  off += 32 * 4;  // m[8], l[8], alpha[8]
+  L.bytes = round_up_i(off, 128) + 1024;  // + alignment slack
   return L;
 }
 
-__device__ __forceinline__ void attn_split_plan(int active, int units, int cap, int& nsplit, int& chunk) {
+// the 1 KB-aligned start of the attention working set inside the union
+__device__ __forceinline__ char* attn_base(char* uni) {
+  return uni + ((1024u - (smem_u32(uni) & 1023u)) & 1023u);
+}
+
+// Splits per (sequence, kv head): one item per CTA when the heads fit, and
+// chunks in kBoxRows multiples.
+__device__ __forceinline__ void attn_split_plan(int active, int units, int& nsplit, int& chunk) {
   int target = units;
   if (target > kStepMaxSplits) target = kStepMaxSplits;
   if (target < 1) target = 1;
   chunk = (active + target - 1) / target;
-  chunk = (chunk + 15) / 16 * 16;
-  if (chunk < 16) chunk = 16;
+  chunk = (chunk + kBoxRows - 1) / kBoxRows * kBoxRows;
+  if (chunk < kBoxRows) chunk = kBoxRows;
   nsplit = (active + chunk - 1) / chunk;
-  (void)cap;
 }
 
-// Issue the bulk copy of cached K/V rows [c0, c0 + nt) of one head and, for
-// quantized caches, their scales (rounded up to 8 tokens: 16-byte copies;
-// the cache length is a multiple of 8) (group thread 0).
-__device__ __forceinline__ void attn_copy(const StepLayer* ly, size_t head_base, int rb, int ng, bool quant, int c0,
-                                          int nt, char* gsm, const AttnLayout& Lo, int cap, uint64_t* bar) {
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Copy cached K/V rows [c0, c0 + nt) of one head (thread 0): whole boxes of
+// kBoxRows rows per plane through the layer's tensor maps (rows past the item
+// are staged but never read; rows past the cache are filled with zeros), and
+// for quantized caches the rows' scales (rounded up to 8 tokens: 16-byte
+// copies; the cache length is a multiple of 8) as plain bulk copies.
+__device__ __forceinline__ void attn_copy(const StepLayer* ly, size_t head_base, const AttnLayout& Lo, bool quant,
+                                          int c0, int nt, int cap, char* gsm, uint64_t* bar) {
+  const int nbox = (nt + kBoxRows - 1) / kBoxRows, ng = Lo.ng;
   const int nt8 = (nt + 7) & ~7;
   fence_proxy_async();
-  mbar_expect_tx(bar, 2u * nt * rb + (quant ? 2u * nt8 * ng * 2 : 0u));
-  bulk_g2s(gsm + Lo.kv, ly->kc + (head_base + c0) * rb, nt * rb, bar);
-  bulk_g2s(gsm + Lo.kv + (size_t)cap * rb, ly->vc + (head_base + c0) * rb, nt * rb, bar);
+  mbar_expect_tx(bar, 2u * Lo.np * nbox * kBoxRows * Lo.bx + (quant ? 2u * nt8 * ng * 2 : 0u));
+  char* kpl = gsm + Lo.kv;
+  char* vpl = kpl + (size_t)cap * Lo.rb;
+  const int y0 = (int)(head_base + c0);
+  const uint64_t pol = l2_evict_first_policy();  // cached rows are read once per step
+  for (int pl = 0; pl < Lo.np; ++pl)
+    for (int i = 0; i < nbox; ++i) {
+      const size_t off = (size_t)pl * cap * Lo.bx + (size_t)i * kBoxRows * Lo.bx;
+      tma_load_2d(kpl + off, ly->kmap, pl * Lo.bx, y0 + i * kBoxRows, bar, pol);
+      tma_load_2d(vpl + off, ly->vmap, pl * Lo.bx, y0 + i * kBoxRows, bar, pol);
+    }
   if (quant) {
     bulk_g2s(gsm + Lo.ksc, ly->ks + (head_base + c0) * ng, nt8 * ng * 2, bar);
     bulk_g2s(gsm + Lo.vsc, ly->vs + (head_base + c0) * ng, nt8 * ng * 2, bar);
@@ -795,33 +788,44 @@ __device__ __forceinline__ AttnItem attn_item_of(int item, int nsplit, int chunk
   return it;
 }
 
-// fp16 pair (elements e, e + 1) of a staged K/V row: an MMA fragment register
-// holding the cache's exact values (fp16, e4m3 codes, or int4 codes)
-__device__ __forceinline__ uint32_t kv_pair_h2(const uint8_t* row, int type, int e) {
-  if (type == AXB_KV_F16) return *reinterpret_cast<const uint32_t*>(row + e * 2);
+// Address of byte `byte` of staged row r (planes of BX bytes, cap rows each).
+template <int BX>
+__device__ __forceinline__ const uint8_t* kv_at(const char* planes, int cap, int r, int byte) {
+  const int pl = byte / BX;
+  return reinterpret_cast<const uint8_t*>(planes) + (size_t)pl * cap * BX + swz<BX>(r, byte - pl * BX);
+}
+
+// fp16 pair (elements e, e + 1; e even) of staged row r: an MMA fragment
+// register holding the cache's exact values (fp16, e4m3 codes, or int4 codes)
+template <int type, int BX>
+__device__ __forceinline__ uint32_t kv_pair_h2(const char* planes, int cap, int r, int e) {
+  if (type == AXB_KV_F16) return *reinterpret_cast<const uint32_t*>(kv_at<BX>(planes, cap, r, 2 * e));
   if (type == AXB_KV_FP8) {
-    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(*reinterpret_cast<const uint16_t*>(row + e), __NV_E4M3);
+    const __half2_raw h =
+        __nv_cvt_fp8x2_to_halfraw2(*reinterpret_cast<const uint16_t*>(kv_at<BX>(planes, cap, r, e)), __NV_E4M3);
     return (uint32_t)h.x | ((uint32_t)h.y << 16);
   }
-  const uint32_t cb = row[e >> 1];  // low nibble = element e, high = e + 1; value (n ^ 8) - 8
+  const uint32_t cb = *kv_at<BX>(planes, cap, r, e >> 1);  // low nibble = element e, high = e + 1; value (n ^ 8) - 8
   const uint32_t t = (((cb & 0xFu) | ((cb & 0xF0u) << 12)) ^ 0x00080008u) | 0x64006400u;
   return h2_as_u32(__hsub2(u32_as_h2(t), __float2half2_rn(1032.f)));
 }
-// element e of two staged rows as an fp16 pair (row0, row1); an absent row is 0
-__device__ __forceinline__ uint32_t kv_col_pair_h2(const uint8_t* r0, const uint8_t* r1, int type, int e) {
+// element e of staged rows r0, r1 as an fp16 pair (row0, row1); a row < 0 is 0
+template <int type, int BX>
+__device__ __forceinline__ uint32_t kv_col_pair_h2(const char* planes, int cap, int r0, int r1, int e) {
   if (type == AXB_KV_F16) {
-    const uint32_t lo = r0 ? reinterpret_cast<const uint16_t*>(r0)[e] : 0u;
-    const uint32_t hi = r1 ? reinterpret_cast<const uint16_t*>(r1)[e] : 0u;
+    const uint32_t lo = r0 >= 0 ? *reinterpret_cast<const uint16_t*>(kv_at<BX>(planes, cap, r0, 2 * e)) : 0u;
+    const uint32_t hi = r1 >= 0 ? *reinterpret_cast<const uint16_t*>(kv_at<BX>(planes, cap, r1, 2 * e)) : 0u;
     return lo | (hi << 16);
   }
   if (type == AXB_KV_FP8) {
-    const uint16_t two = (uint16_t)((r0 ? r0[e] : 0u) | ((r1 ? r1[e] : 0u) << 8));
-    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(two, __NV_E4M3);
+    const uint32_t b0 = r0 >= 0 ? *kv_at<BX>(planes, cap, r0, e) : 0u;
+    const uint32_t b1 = r1 >= 0 ? *kv_at<BX>(planes, cap, r1, e) : 0u;
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((uint16_t)(b0 | (b1 << 8)), __NV_E4M3);
     return (uint32_t)h.x | ((uint32_t)h.y << 16);
   }
   const uint32_t sh = (e & 1) * 4;
-  const uint32_t n0 = r0 ? ((r0[e >> 1] >> sh) & 0xFu) ^ 8u : 8u;  // 8 encodes 0 after the offset
-  const uint32_t n1 = r1 ? ((r1[e >> 1] >> sh) & 0xFu) ^ 8u : 8u;
+  const uint32_t n0 = r0 >= 0 ? ((*kv_at<BX>(planes, cap, r0, e >> 1) >> sh) & 0xFu) ^ 8u : 8u;  // 8 encodes 0
+  const uint32_t n1 = r1 >= 0 ? ((*kv_at<BX>(planes, cap, r1, e >> 1) >> sh) & 0xFu) ^ 8u : 8u;
   return h2_as_u32(__hsub2(u32_as_h2((n0 | (n1 << 16)) | 0x64006400u), __float2half2_rn(1032.f)));
 }
 // fp32 pair -> fp16 (hi, lo) pairs with hi + lo = the value to about 22 bits
@@ -832,39 +836,46 @@ __device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint3
   lo = h2_as_u32(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
 }
 
-// One attention item (sequence b, kv head, split) on a group of 4 warps, on
-// the tensor cores: S = q K^T with q as fp16 hi + lo (K codes are exact in
-// fp16; the per-token scales apply to the fp32 result), then O += P V with the
+// One attention item (sequence b, kv head, split) on the whole CTA, on the
+// tensor cores: S = q K^T with q as fp16 hi + lo (K codes are exact in fp16;
+// the per-token scales apply to the fp32 result), then O += P V with the
 // per-token V scale folded into P (normalized by the chunk's largest scale)
-// and P as hi + lo.  Warp w owns output dims [w HD / 4, (w + 1) HD / 4).
-// gt = thread index in the group, gwarp = warp index in the group.
-template <int HD>
-__device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, int layer, const AttnItem& it,
-                                      int nsplit, bool prefetched, char* gsm, uint64_t* bar, uint32_t& uses, int bar_id,
-                                      int gt, int* done_ctr, bool ok) {
-  constexpr int DPL = HD / 32, KS = HD / 16, NB = HD / 32;  // NB: n8 output blocks per warp
-  const int lane = gt & 31, gwarp = gt >> 5, g = lane >> 2, c = lane & 3;
-  const int cap = a.attn_cap;
-  const AttnLayout Lo = attn_layout(a.kv_type, HD, a.kv_group, cap);
-  const int rb = Lo.rb, ng = Lo.ng, G = a.kv_type == AXB_KV_F16 ? HD : a.kv_group;
-  const bool quant = a.kv_type != AXB_KV_F16;
+// and P as hi + lo.  Warp w owns output dims [8w, 8w + 8).  A split writes
+// its (O, m, l) partial; the head's last split to finish combines all of
+// them in split order and publishes the head.
+template <int HD, int KVT>
+__device__ __noinline__ bool attn_item(const StepArgs& a, const StepLayer* ly, int layer, const AttnItem& it,
+                                       int nsplit, bool prefetched, char* gsm, char* misc, uint32_t& uses,
+                                       int* done_ctr, bool ok) {
+  constexpr int BX = kv_box_bytes(KVT == AXB_KV_F16 ? HD * 2 : (KVT == AXB_KV_FP8 ? HD : HD / 2));
+  constexpr int DPL = HD / 32, KS = HD / 16;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, c = lane & 3;
+  const int cap = a.plan.attn_cap;
+  const AttnLayout Lo = attn_layout(KVT, HD, a.kv_group, cap);
+  const int ng = Lo.ng, G = KVT == AXB_KV_F16 ? HD : a.kv_group;
+  const int lgG = __ffs(G) - 1;  // scale groups are powers of two
+  const int qs = Lo.qs, ps = Lo.ps;
+  constexpr bool quant = KVT != AXB_KV_F16;
   const int n_rep = a.Hq / a.Hkv, hq0 = it.kvh * n_rep;
   const int rpos = a.params[0], wpos = a.params[1];
   const size_t head_base = ((size_t)it.b * a.Hkv + it.kvh) * a.S;
-  char* kst = gsm + Lo.kv;
-  char* vst = kst + (size_t)cap * rb;
+  int* flag = reinterpret_cast<int*>(misc + kMiscFlag) + 1;
+  float* Ls = reinterpret_cast<float*>(misc + kMiscLs);
+  float* coef = reinterpret_cast<float*>(misc + kMiscCoef);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(misc + kMiscBar);
+  char* kst = gsm + Lo.kv;  // K planes, then V planes
+  char* vst = kst + (size_t)cap * Lo.rb;
   __half* ksc_s = reinterpret_cast<__half*>(gsm + Lo.ksc);
   __half* vsc_s = reinterpret_cast<__half*>(gsm + Lo.vsc);
-  __half* qh_s = reinterpret_cast<__half*>(gsm + Lo.qh);  // [hi / lo][8 rows][HD]
+  uint32_t* qh32 = reinterpret_cast<uint32_t*>(gsm + Lo.qh);  // [hi / lo][8 rows][qs]
   float* p_s = reinterpret_cast<float*>(gsm + Lo.p);
-  float* ml_s = reinterpret_cast<float*>(gsm + Lo.ml);  // m[8] l[8] alpha[8] flag
-  float* coef = reinterpret_cast<float*>(gsm + Lo.coef);
+  float* ml_s = reinterpret_cast<float*>(gsm + Lo.ml);  // m[8] l[8] alpha[8]
 
   // ---- q with RoPE (fp32), as fp16 hi / lo rows; the new K/V row rotated, quantized and written
   const int qkv_dim = (a.Hq + 2 * a.Hkv) * HD;
   const __half* row = a.qkv + (size_t)it.b * qkv_dim;
   const float* fr = a.rope + (size_t)(rpos % a.rope_len) * HD;
-  for (int i = gt; i < 8 * HD / 2; i += 128) {
+  for (int i = tid; i < 8 * HD / 2; i += kSThreads) {
     const int rr = i / (HD / 2), pr = i % (HD / 2);
     float q0 = 0.f, q1 = 0.f;
     if (rr < n_rep) {
@@ -876,20 +887,22 @@ __device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, in
     }
     uint32_t hi, lo;
     split_h2(q0, q1, hi, lo);
-    reinterpret_cast<uint32_t*>(qh_s)[(rr * HD) / 2 + pr] = hi;
-    reinterpret_cast<uint32_t*>(qh_s)[(8 * HD + rr * HD) / 2 + pr] = lo;
+    qh32[rr * qs + pr] = hi;
+    qh32[(8 + rr) * qs + pr] = lo;
   }
-  if (gt < 8) {
-    ml_s[gt] = -INFINITY;
-    ml_s[8 + gt] = 0.f;
+  if (tid < 8) {
+    ml_s[tid] = -INFINITY;
+    ml_s[8 + tid] = 0.f;
   }
   float nkv[DPL];
+  uint2 ncode = make_uint2(0u, 0u);
+  float nscale = 0.f;
   const bool covers = wpos >= it.t0 && wpos < it.t1;
-  if (covers && gwarp < 2) {
-    const __half* src = row + (size_t)(a.Hq + (gwarp == 0 ? 0 : a.Hkv) + it.kvh) * HD;
+  if (covers && w < 2) {
+    const __half* src = row + (size_t)(a.Hq + (w == 0 ? 0 : a.Hkv) + it.kvh) * HD;
 #pragma unroll
     for (int e = 0; e < DPL; ++e) nkv[e] = __half2float(__ldcg(src + lane * DPL + e));
-    if (gwarp == 0) {  // RoPE on K, every product rounded (transformer.py:1105-1127)
+    if (w == 0) {  // RoPE on K, every product rounded (transformer.py:1105-1127)
 #pragma unroll
       for (int e = 0; e < DPL; e += 2) {
         const int pr = (lane * DPL + e) >> 1;
@@ -898,82 +911,98 @@ __device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, in
         nkv[e + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
       }
     }
-    uint8_t* crow = (gwarp == 0 ? ly->kc : ly->vc) + (head_base + wpos) * rb;
-    __half* srow = quant ? (gwarp == 0 ? ly->ks : ly->vs) + (head_base + wpos) * ng : nullptr;
-    store_kv_row<DPL>(nkv, lane, a.kv_type, G, true, crow, srow);
+    uint8_t* crow = (w == 0 ? ly->kc : ly->vc) + (head_base + wpos) * Lo.rb;
+    __half* srow = quant ? (w == 0 ? ly->ks : ly->vs) + (head_base + wpos) * ng : nullptr;
+    ncode = store_kv_row<DPL>(nkv, lane, KVT, G, true, crow, srow, &nscale);
   }
-  group_bar(bar_id);
+  __syncthreads();
 
+  // this thread's q fragments (rows g, hi and lo parts) for every 16-wide k step
+  uint32_t qa[KS][4];
+#pragma unroll
+  for (int s = 0; s < KS; ++s) {
+    qa[s][0] = qh32[g * qs + 8 * s + c];
+    qa[s][1] = qh32[g * qs + 8 * s + c + 4];
+    qa[s][2] = qh32[(8 + g) * qs + 8 * s + c];
+    qa[s][3] = qh32[(8 + g) * qs + 8 * s + c + 4];
+  }
   const float sm_scale = 1.0f / sqrtf((float)HD);
-  const int d0 = gwarp * (HD / 4);  // this warp's output dims (one V scale group: kv_group >= HD / 4)
-  const int vgrp = quant ? d0 / G : 0;
-  float oacc[NB][4];
-#pragma unroll
-  for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) oacc[nb][q] = 0.f;
+  const int d0 = w * 8;  // this warp's output dims (one V scale group: kv_group >= 8)
+  const bool pv_warp = d0 < HD;
+  const int vgrp = quant && pv_warp ? d0 >> lgG : 0;
+  float oacc[2] = {0.f, 0.f};
   bool first = true;
-  for (int c0 = it.t0; c0 < it.t1 && ok; c0 += cap) {
+  // Chunks of cap cached tokens.  The first chunk runs outside any loop: the
+  // chunk body entered through a loop was measured to stall about 14 us at
+  // the loop's entry on every item; later chunks (long splits only) loop.
+  auto chunk = [&](const int c0) {
     const int nt = min(cap, it.t1 - c0);
-    if (!(first && prefetched) && gt == 0) attn_copy(ly, head_base, rb, ng, quant, c0, nt, gsm, Lo, cap, bar);
+    if (!(first && prefetched) && tid == 0) attn_copy(ly, head_base, Lo, quant, c0, nt, cap, gsm, bar);
     first = false;
-    const bool got = mbar_wait(bar, uses & 1, kSMbarLimit);
+    const bool got = mbar_wait(bar, uses & 1, a.mbar_limit);
     ++uses;
-    if (group_bar_or(bar_id, !got)) {  // one decision for the whole group
-      if (gt == 0) raise_abort(a);
+    if (__syncthreads_or(!got)) {  // one decision for the whole CTA
+      if (tid == 0) {
+        raise_abort(a);
+        mbar_wait(bar, (uses - 1) & 1, kDrainLimit);  // the copies in flight land before the CTA moves on
+      }
       ok = false;
-      break;
+      return;
     }
-    if (covers && gwarp < 2 && wpos >= c0 && wpos < c0 + nt) {
-      // the copy may have read the slot (codes and scale) before this step wrote it
-      uint8_t* rowp = reinterpret_cast<uint8_t*>(gwarp == 0 ? kst : vst) + (size_t)(wpos - c0) * rb;
-      __half* sp = quant ? (gwarp == 0 ? ksc_s : vsc_s) + (size_t)(wpos - c0) * ng : nullptr;
-      store_kv_row<DPL>(nkv, lane, a.kv_type, G, true, rowp, sp);
+    if (covers && w < 2 && wpos >= c0 && wpos < c0 + nt) {
+      // the copy may have read the slot (codes and scale) before this step
+      // wrote it: place this step's row (this lane's bytes) and scale
+      constexpr int LB = KVT == AXB_KV_F16 ? 2 * DPL : (KVT == AXB_KV_FP8 ? DPL : DPL / 2);  // bytes per lane
+      uint8_t* dst = const_cast<uint8_t*>(kv_at<BX>(w == 0 ? kst : vst, cap, wpos - c0, lane * LB));
+      if (LB == 8) *reinterpret_cast<uint2*>(dst) = ncode;
+      else if (LB == 4) *reinterpret_cast<uint32_t*>(dst) = ncode.x;
+      else if (LB == 2) *reinterpret_cast<uint16_t*>(dst) = (uint16_t)ncode.x;
+      else *dst = (uint8_t)ncode.x;
+      const int lpg = G / DPL;
+      if (quant && (lane % lpg) == 0)
+        (w == 0 ? ksc_s : vsc_s)[(size_t)(wpos - c0) * ng + (lane * DPL) / G] = __float2half_rn(nscale);
     }
-    group_bar(bar_id);
-    // ---- scores: warp w takes 8-token blocks w, w + 4, ...; the fp32 result
-    // of each scale group is scaled by the token's K scale when the group ends
-    const uint32_t* qh32 = reinterpret_cast<const uint32_t*>(qh_s);
-    for (int blk = gwarp; blk * 8 < nt; blk += 4) {
+    __syncthreads();
+    // ---- scores: warp w takes 8-token blocks w, w + 16, ...  A quantized K
+    // row enters the MMA as the reference's dequantized fp16 values
+    // (fp16(code * scale), one HMUL2 per pair: the product of two fp16 values
+    // rounded once), so q . k sees the same K as the reference's SDPA.
+    for (int blk = w; blk * 8 < nt; blk += kSW) {
       const int tok = min(blk * 8 + g, nt - 1);  // B-fragment column; columns past nt are discarded
-      const uint8_t* krow = reinterpret_cast<const uint8_t*>(kst) + (size_t)tok * rb;
       const int t_a = blk * 8 + 2 * c, t_b = t_a + 1;  // this thread's C-fragment columns
-      float sc0 = 0.f, sc1 = 0.f, gacc[4] = {0.f, 0.f, 0.f, 0.f};
+      float gacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int s = 0; s < KS; ++s) {
-        const uint32_t b0 = kv_pair_h2(krow, a.kv_type, 16 * s + 2 * c);
-        const uint32_t b1 = kv_pair_h2(krow, a.kv_type, 16 * s + 2 * c + 8);
-        const uint32_t ahi[4] = {qh32[(g * HD + 16 * s + 2 * c) / 2], 0u, qh32[(g * HD + 16 * s + 2 * c + 8) / 2], 0u};
-        const uint32_t alo[4] = {qh32[(8 * HD + g * HD + 16 * s + 2 * c) / 2], 0u,
-                                 qh32[(8 * HD + g * HD + 16 * s + 2 * c + 8) / 2], 0u};
+        uint32_t b0 = kv_pair_h2<KVT, BX>(kst, cap, tok, 16 * s + 2 * c);
+        uint32_t b1 = kv_pair_h2<KVT, BX>(kst, cap, tok, 16 * s + 2 * c + 8);
+        if (quant) {
+          const __half2 sc2 = __half2half2(ksc_s[tok * ng + ((16 * s) >> lgG)]);
+          b0 = h2_as_u32(__hmul2(u32_as_h2(b0), sc2));
+          b1 = h2_as_u32(__hmul2(u32_as_h2(b1), sc2));
+        }
+        const uint32_t ahi[4] = {qa[s][0], 0u, qa[s][1], 0u};
+        const uint32_t alo[4] = {qa[s][2], 0u, qa[s][3], 0u};
         mma_16816(gacc, ahi, b0, b1, gacc);
         mma_16816(gacc, alo, b0, b1, gacc);
-        if ((16 * (s + 1)) % G == 0) {  // a K scale group is complete
-          const int grp = (16 * s) / G;
-          const float s0 = quant && t_a < nt ? __half2float(ksc_s[t_a * ng + grp]) : 1.f;
-          const float s1 = quant && t_b < nt ? __half2float(ksc_s[t_b * ng + grp]) : 1.f;
-          sc0 = __fmaf_rn(gacc[0], s0, sc0);
-          sc1 = __fmaf_rn(gacc[1], s1, sc1);
-          gacc[0] = gacc[1] = gacc[2] = gacc[3] = 0.f;
-        }
       }
       if (g < n_rep) {
-        if (t_a < nt) p_s[g * cap + t_a] = sc0 * sm_scale;
-        if (t_b < nt) p_s[g * cap + t_b] = sc1 * sm_scale;
+        if (t_a < nt) p_s[g * ps + t_a] = gacc[0] * sm_scale;
+        if (t_b < nt) p_s[g * ps + t_b] = gacc[1] * sm_scale;
       }
     }
-    group_bar(bar_id);
-    // ---- online softmax over the chunk: warp w handles heads w, w + 4
-    for (int r = gwarp; r < n_rep; r += 4) {
+    __syncthreads();
+    // ---- online softmax over the chunk: warp r handles head r
+    if (w < n_rep) {
+      const int r = w;
       float mx = -INFINITY;
-      for (int tk = lane; tk < nt; tk += 32) mx = fmaxf(mx, p_s[r * cap + tk]);
+      for (int tk = lane; tk < nt; tk += 32) mx = fmaxf(mx, p_s[r * ps + tk]);
       mx = warp_max(mx);
       const float m_old = ml_s[r];
       const float m_new = fmaxf(m_old, mx);
       float sum = 0.f;
       for (int tk = lane; tk < nt; tk += 32) {
-        const float e = __expf(p_s[r * cap + tk] - m_new);
-        p_s[r * cap + tk] = e;
+        const float e = __expf(p_s[r * ps + tk] - m_new);
+        p_s[r * ps + tk] = e;
         sum += e;
       }
       sum = warp_sum(sum);
@@ -985,106 +1014,81 @@ __device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, in
         ml_s[16 + r] = alpha;
       }
     }
-    group_bar(bar_id);
-    // ---- O = alpha O + vmax * (P' V), P' = p * vscale / vmax (vmax: the
-    // chunk's largest V scale of this warp's group, keeps P' in fp16 range)
-    float vmax = 1.f;
-    if (quant) {
-      float m = 0.f;
-      for (int tk = lane; tk < nt; tk += 32) m = fmaxf(m, __half2float(vsc_s[tk * ng + vgrp]));
-      m = warp_max(m);
-      vmax = m > 0.f ? m : 1.f;
-    }
-    const float inv_vmax = 1.f / vmax;
-    const float alpha = g < n_rep ? ml_s[16 + g] : 0.f;
-    float tacc[NB][4];
+    __syncthreads();
+    // ---- O = alpha O + P V, a quantized V row again as the reference's
+    // dequantized fp16 values, P as fp16 hi + lo
+    if (pv_warp) {
+      const float alpha = g < n_rep ? ml_s[16 + g] : 0.f;
+      float tacc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int t0 = 0; t0 < nt; t0 += 16) {
+        float pv[4];
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) tacc[nb][q] = 0.f;
-    for (int t0 = 0; t0 < nt; t0 += 16) {
-      float pv[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int t = t0 + 2 * c + (q & 1) + 8 * (q >> 1);
-        float v = 0.f;
-        if (g < n_rep && t < nt) {
-          v = p_s[g * cap + t];
-          if (quant) v *= __half2float(vsc_s[t * ng + vgrp]) * inv_vmax;
+        for (int q = 0; q < 4; ++q) {
+          const int t = t0 + 2 * c + (q & 1) + 8 * (q >> 1);
+          pv[q] = (g < n_rep && t < nt) ? p_s[g * ps + t] : 0.f;
         }
-        pv[q] = v;
+        uint32_t h01, l01, h23, l23;
+        split_h2(pv[0], pv[1], h01, l01);
+        split_h2(pv[2], pv[3], h23, l23);
+        const uint32_t ahi[4] = {h01, 0u, h23, 0u}, alo[4] = {l01, 0u, l23, 0u};
+        const int ta = t0 + 2 * c, tb = ta + 8;
+        const int r0 = ta < nt ? ta : -1, r1 = ta + 1 < nt ? ta + 1 : -1;
+        const int r2 = tb < nt ? tb : -1, r3 = tb + 1 < nt ? tb + 1 : -1;
+        const int d = d0 + g;  // B-fragment column
+        uint32_t b0 = kv_col_pair_h2<KVT, BX>(vst, cap, r0, r1, d);
+        uint32_t b1 = kv_col_pair_h2<KVT, BX>(vst, cap, r2, r3, d);
+        if (quant) {  // absent rows have zero codes; their scale is taken as 0 too
+          const __half z = __float2half_rn(0.f);
+          const __half2 s01 = __halves2half2(r0 >= 0 ? vsc_s[ta * ng + vgrp] : z, r1 >= 0 ? vsc_s[(ta + 1) * ng + vgrp] : z);
+          const __half2 s23 = __halves2half2(r2 >= 0 ? vsc_s[tb * ng + vgrp] : z, r3 >= 0 ? vsc_s[(tb + 1) * ng + vgrp] : z);
+          b0 = h2_as_u32(__hmul2(u32_as_h2(b0), s01));
+          b1 = h2_as_u32(__hmul2(u32_as_h2(b1), s23));
+        }
+        mma_16816(tacc, ahi, b0, b1, tacc);
+        mma_16816(tacc, alo, b0, b1, tacc);
       }
-      uint32_t h01, l01, h23, l23;
-      split_h2(pv[0], pv[1], h01, l01);
-      split_h2(pv[2], pv[3], h23, l23);
-      const uint32_t ahi[4] = {h01, 0u, h23, 0u}, alo[4] = {l01, 0u, l23, 0u};
-      const int ta = t0 + 2 * c, tb = ta + 8;
-      const uint8_t* r0 = ta < nt ? reinterpret_cast<const uint8_t*>(vst) + (size_t)ta * rb : nullptr;
-      const uint8_t* r1 = ta + 1 < nt ? reinterpret_cast<const uint8_t*>(vst) + (size_t)(ta + 1) * rb : nullptr;
-      const uint8_t* r2 = tb < nt ? reinterpret_cast<const uint8_t*>(vst) + (size_t)tb * rb : nullptr;
-      const uint8_t* r3 = tb + 1 < nt ? reinterpret_cast<const uint8_t*>(vst) + (size_t)(tb + 1) * rb : nullptr;
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-        const int d = d0 + nb * 8 + g;  // B-fragment column
-        const uint32_t b0 = kv_col_pair_h2(r0, r1, a.kv_type, d);
-        const uint32_t b1 = kv_col_pair_h2(r2, r3, a.kv_type, d);
-        mma_16816(tacc[nb], ahi, b0, b1, tacc[nb]);
-        mma_16816(tacc[nb], alo, b0, b1, tacc[nb]);
-      }
+      oacc[0] = __fmaf_rn(oacc[0], alpha, tacc[0]);
+      oacc[1] = __fmaf_rn(oacc[1], alpha, tacc[1]);
     }
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      oacc[nb][0] = __fmaf_rn(vmax, tacc[nb][0], oacc[nb][0] * alpha);
-      oacc[nb][1] = __fmaf_rn(vmax, tacc[nb][1], oacc[nb][1] * alpha);
-    }
-    group_bar(bar_id);  // staged rows and p_s are free for the next chunk
-  }
+    __syncthreads();  // staged rows and p_s are free for the next chunk
+  };
+  chunk(it.t0);
+  for (int c0 = it.t0 + cap; c0 < it.t1 && ok; c0 += cap) chunk(c0);
   if (!ok) return false;
-  // ---- this thread's outputs: head g, dims d0 + 8 nb + 2c + {0, 1}
+  // ---- this thread's outputs: head g, dims d0 + 2c + {0, 1}
   const size_t pidx = (size_t)it.b * a.Hq + hq0;
-  if (g < n_rep) {
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      const int d = d0 + nb * 8 + 2 * c;
-      if (nsplit == 1) {
-        a.attn[(pidx + g) * HD + d] = __float2half_rn(__fdiv_rn(oacc[nb][0], ml_s[8 + g]));
-        a.attn[(pidx + g) * HD + d + 1] = __float2half_rn(__fdiv_rn(oacc[nb][1], ml_s[8 + g]));
-      } else {
-        *reinterpret_cast<float2*>(a.part_o + ((pidx + g) * kStepMaxSplits + it.split) * HD + d) =
-            make_float2(oacc[nb][0], oacc[nb][1]);
-      }
+  if (pv_warp && g < n_rep) {
+    const int d = d0 + 2 * c;
+    if (nsplit == 1) {
+      __half* op = a.attn + (pidx + g) * HD + d;
+      op[0] = __float2half_rn(__fdiv_rn(oacc[0], ml_s[8 + g]));
+      op[1] = __float2half_rn(__fdiv_rn(oacc[1], ml_s[8 + g]));
+    } else {
+      *reinterpret_cast<float2*>(a.part_o + ((pidx + g) * kStepMaxSplits + it.split) * HD + d) =
+          make_float2(oacc[0], oacc[1]);
     }
   }
+  if (nsplit > 1 && tid < n_rep)
+    *reinterpret_cast<float2*>(a.part_ml + ((pidx + tid) * kStepMaxSplits + it.split) * 2) =
+        make_float2(ml_s[tid], ml_s[8 + tid]);
+  __syncthreads();
   if (nsplit == 1) {
-    group_bar(bar_id);
-    if (gt == 0) red_release_add(done_ctr, 1);
+    if (tid == 0) red_release_add(done_ctr, 1);
     return true;
   }
-  if (gt < n_rep) {
-    a.part_ml[((pidx + gt) * kStepMaxSplits + it.split) * 2 + 0] = ml_s[gt];
-    a.part_ml[((pidx + gt) * kStepMaxSplits + it.split) * 2 + 1] = ml_s[8 + gt];
+  // ---- the head's last split to arrive combines it.  The per-head counter
+  // only grows during a step (layer l completes at (l + 1) * nsplit arrivals);
+  // the step's last CTA clears it.
+  if (tid == 0) {
+    const int old = atom_acq_rel_add(a.attn_cnt + it.b * a.Hkv + it.kvh, 1);
+    *flag = old == (layer + 1) * nsplit - 1 ? 1 : 0;
   }
-  group_bar(bar_id);
-  // ---- combine, shared by all the head's split groups.  Every split of the
-  // head runs at once (n_items <= attention groups in the grid), so each group
-  // waits for all of them and then combines its own slice of the head's
-  // n_rep * HD outputs.  The per-head counter only grows during a step (layer l
-  // completes at (l + 1) * nsplit arrivals); the step's last CTA clears it.
-  int* cnt = a.attn_cnt + it.b * a.Hkv + it.kvh;
-  int* flag = reinterpret_cast<int*>(ml_s + 24);
-  if (gt == 0) {
-    red_release_add(cnt, 1);
-    *flag = wait_ge(cnt, (layer + 1) * nsplit, a) ? 1 : 0;
-  }
-  group_bar(bar_id);
-  if (!*flag) return false;
-  const int nout = n_rep * HD;
-  const int i0 = it.split * nout / nsplit, i1 = (it.split + 1) * nout / nsplit;
-  const int r_lo = i0 / HD, r_hi = (i1 - 1) / HD;  // heads touched by the slice
+  __syncthreads();
+  if (!*flag) return true;
   // per-head split weights: each lane loads the (m, l) of splits lane and lane + 32
   static_assert(kStepMaxSplits <= 64, "two splits per lane");
-  for (int r = r_lo + gwarp; r <= r_hi; r += 4) {
-    const size_t hb = (pidx + r) * kStepMaxSplits;
+  if (w < n_rep) {
+    const size_t hb = (pidx + w) * kStepMaxSplits;
     float2 ml[2];
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
@@ -1092,49 +1096,85 @@ __device__ AXB_STEP_FN bool attn_item(const StepArgs& a, const StepLayer* ly, in
       ml[q] = sp < nsplit ? __ldcg(reinterpret_cast<const float2*>(a.part_ml) + hb + sp) : make_float2(-INFINITY, 0.f);
     }
     const float Mx = warp_max(fmaxf(ml[0].x, ml[1].x));
-    float Ls = 0.f;
+    float Lsum = 0.f;
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const int sp = lane + 32 * q;
       if (sp < nsplit) {
         const float cw = (ml[q].x == -INFINITY) ? 0.f : __expf(ml[q].x - Mx);
-        coef[(r - r_lo) * kStepMaxSplits + sp] = cw;
-        Ls += ml[q].y * cw;
+        coef[w * kStepMaxSplits + sp] = cw;
+        Lsum += ml[q].y * cw;
       }
     }
-    Ls = warp_sum(Ls);
-    if (lane == 0) ml_s[8 + (r - r_lo)] = Ls;
+    Lsum = warp_sum(Lsum);
+    if (lane == 0) Ls[w] = Lsum;
   }
-  group_bar(bar_id);
-  // 8 lanes per output (splits j, j + 8, ...), 16 outputs per pass; the
-  // lanes' partial sums meet in a fixed shuffle order
-  const int j8 = gt & 7, npass = (i1 - i0 + 15) / 16;  // the same trip count in every lane
-  for (int pass = 0; pass < npass; ++pass) {
-    const int i = i0 + 16 * pass + (gt >> 3);
-    const bool act = i < i1;
-    const int ii = act ? i : i0;
-    const int r = ii / HD, e = ii % HD;
-    const size_t hb = (pidx + r) * kStepMaxSplits;
-    float v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int sp = j8 + 8 * u;
-      v[u] = (act && sp < nsplit) ? __ldcg(a.part_o + (hb + sp) * HD + e) : 0.f;
-    }
+  __syncthreads();
+  // one output per thread, the splits summed in order (eight loads in flight)
+  for (int i = tid; i < n_rep * HD; i += kSThreads) {
+    const int r = i / HD, e = i % HD;
+    const float* po = a.part_o + (pidx + r) * kStepMaxSplits * HD + e;
     float O = 0.f;
+    for (int s0 = 0; s0 < nsplit; s0 += 8) {
+      float v[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int sp = j8 + 8 * u;
-      if (act && sp < nsplit) O = __fmaf_rn(v[u], coef[(r - r_lo) * kStepMaxSplits + sp], O);
+      for (int u = 0; u < 8; ++u) v[u] = s0 + u < nsplit ? __ldcg(po + (size_t)(s0 + u) * HD) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < nsplit) O = __fmaf_rn(v[u], coef[r * kStepMaxSplits + s0 + u], O);
     }
-    O += __shfl_xor_sync(0xffffffffu, O, 1);
-    O += __shfl_xor_sync(0xffffffffu, O, 2);
-    O += __shfl_xor_sync(0xffffffffu, O, 4);
-    if (act && j8 == 0) a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, ml_s[8 + (r - r_lo)]));
+    a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, Ls[r]));
   }
-  group_bar(bar_id);
-  if (gt == 0) red_release_add(done_ctr, 1);
+  __syncthreads();
+  if (tid == 0) red_release_add(done_ctr, 1);
   return true;
+}
+
+// The attention phase of layer l on this CTA: its first item's cached rows
+// are copied before the layer's QKV phase has finished (they do not depend on
+// it), then the CTA takes items blockIdx.x, + gridDim.x, ...
+template <int HD>
+__device__ __noinline__ bool attn_phase(const StepArgs& a, int l, char* uni, char* misc, uint32_t& uses, bool ok) {
+  const int tid = threadIdx.x, C = gridDim.x;
+  const StepLayer* ly = a.layers + l;
+  int* dn = a.done + 1 + 5 * l;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(misc + kMiscBar);
+  const int qkv_dim = (a.Hq + 2 * a.Hkv) * a.hd;
+  const int active = a.params[2];
+  int nsplit, chunk;
+  attn_split_plan(active, C / (a.B * a.Hkv), nsplit, chunk);
+  const int n_items = a.B * a.Hkv * nsplit;
+  const AttnLayout Lo = attn_layout(a.kv_type, HD, a.kv_group, a.plan.attn_cap);
+  char* gsm = attn_base(uni);
+  int item = blockIdx.x;
+  const bool pre = ok && item < n_items;
+  if (pre && tid == 0) {  // cached rows do not depend on this step's QKV
+    const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
+    const size_t hb = ((size_t)it.b * a.Hkv + it.kvh) * a.S;
+    attn_copy(ly, hb, Lo, a.kv_type != AXB_KV_F16, it.t0, min(a.plan.attn_cap, it.t1 - it.t0), a.plan.attn_cap,
+              gsm, bar);
+  }
+  ok = cta_wait(dn + 0, tiles_of(qkv_dim), a, ok);
+  trace_mark(a, 1 + 10 * l + 2);
+  bool first = true;
+  for (; item < n_items; item += C) {
+    if (!ok) {
+      // the copies issued above land before the union is reused
+      if (first && pre && tid == 0) mbar_wait(bar, uses & 1, kDrainLimit);
+      if (first && pre) ++uses;
+      break;
+    }
+    const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
+    if (a.kv_type == AXB_KV_FP8)
+      ok = attn_item<HD, AXB_KV_FP8>(a, ly, l, it, nsplit, first, gsm, misc, uses, dn + 1, ok);
+    else if (a.kv_type == AXB_KV_INT4)
+      ok = attn_item<HD, AXB_KV_INT4>(a, ly, l, it, nsplit, first, gsm, misc, uses, dn + 1, ok);
+    else
+      ok = attn_item<HD, AXB_KV_F16>(a, ly, l, it, nsplit, first, gsm, misc, uses, dn + 1, ok);
+    first = false;
+  }
+  if (tid == 0) trace_at(a, 4 + 10 * a.L + (4 * a.L + 1) * kStepTraceW + 2 * l);
+  return ok;
 }
 
 // ------------------------------------------------------------------ kernel
@@ -1143,40 +1183,42 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   extern __shared__ __align__(128) char smem[];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int C = gridDim.x, Wt = C * kSW, gw = wid * C + blockIdx.x;  // virtual warp id
-  char* uni = smem + kSW * kSRing;
-  float* red = reinterpret_cast<float*>(uni + kSUnion);  // [kSW][kStepMaxM]
-  uint64_t* abar = reinterpret_cast<uint64_t*>(uni + kSUnion + 512);  // one per attention group
-  int* s_last = reinterpret_cast<int*>(uni + kSUnion + 512 + 64);
+  const int nsl = a.plan.nslots;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kSW * nsl * kSlotB);
+  char* uni = smem + (size_t)kSW * nsl * kSlotB + kSBars;
+  char* misc = uni + a.plan.union_bytes;
+  float* red = reinterpret_cast<float*>(misc + kMiscRed);
+  int* s_last = reinterpret_cast<int*>(misc + kMiscFlag);
 
   // staged activations: M rows of K + 8 halves from the union's start, their
   // per-(group, token) sums at its end
   __half* xs = reinterpret_cast<__half*>(uni);
-  auto xsum_of = [&](int K) { return reinterpret_cast<float*>(uni + kSUnion - xsum_bytes(K, a.group)); };
+  const int ub = a.plan.union_bytes;
+  auto xsum_of = [&](int K) { return reinterpret_cast<float*>(uni + ub - xsum_bytes(K, a.group)); };
   const int xs_stride = a.d + 8;
 
   Ring ring;
-  ring.buf = smem + wid * kSRing;
-  ring.bars = reinterpret_cast<uint64_t*>(ring.buf + kSStages * (kSStageW + kSStageS));
+  ring.buf = smem + (size_t)wid * nsl * kSlotB;
+  ring.bars = bars + wid * kMaxSlots;
+  ring.n = nsl;
   ring.cs = 0;
   ring.cpar = 0;
   ring.ps = 0;
   ring.inflight = 0;
-  Cur pc;
+  Cur& pc = reinterpret_cast<Cur*>(misc + kMiscCur)[wid];
   if (lane == 0) {
-    for (int s = 0; s < kSStages; ++s) mbar_init(ring.bars + s, 1);
-    if (wid < kSGroups) mbar_init(abar + wid, 1);
+    for (int s = 0; s < nsl; ++s) mbar_init(ring.bars + s, 1);
+    if (wid == 0) mbar_init(reinterpret_cast<uint64_t*>(misc + kMiscBar), 1);
     fence_mbar_init();
     pc.ph = 0;
     cur_load<GB>(pc, a, gw, Wt);
-    for (int s = 0; s < kSStages; ++s) ring_issue<SYM, GB>(ring, pc, a, gw, Wt, lane);
+    for (int s = 0; s < nsl; ++s) ring_issue<SYM, GB>(ring, pc, a, gw, Wt, lane);
   }
   __syncthreads();
 
   bool ok = true;
-  const int qkv_dim = (a.Hq + 2 * a.Hkv) * a.hd;
   const int t_d = tiles_of(a.d);
-  const int grp = wid >> 2, gt = tid & 127;
-  uint32_t abar_uses = 0;
+  uint32_t abar_uses = 0;  // completed phases of the attention mbarrier
 
   trace_mark(a, 0);
   // embedding rows for the first layer's QKV (every CTA stages its own copy)
@@ -1204,11 +1246,7 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
       nw = ly->ln1;
       done_ctr = dn;
     } else if (kind == 1) {  // o: attention output (+ residual)
-      {
-        int nsplit, chunk;
-        attn_split_plan(a.params[2], (kSGroups * C) / (a.B * a.Hkv), a.attn_cap, nsplit, chunk);
-        ok = cta_wait(dn + 1, a.B * a.Hkv * nsplit, a, ok);  // every attention item (and its combine slice)
-      }
+      ok = cta_wait(dn + 1, a.B * a.Hkv, a, ok);     // every head combined
       if (l == 0) ok = cta_wait(a.done, 1, a, ok);  // h holds the embedding rows
       trace_mark(a, ts + 4);
       src = a.attn;
@@ -1237,11 +1275,11 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     }
     // ---- the GEMV: activations staged in shared memory when they fit (always
     // for the normalized inputs), else read from L2 one k-block ahead
-    const bool staged = xs_fits(a.B, K, a.group);
+    const bool staged = stage_bytes(a.B, K, a.group) <= ub;
     if (!staged && (nw != nullptr || src == nullptr)) {
       // normalized inputs (and layer 0's embedding rows) exist only as staged
-      // rows; the host guarantees they fit (xs_fits for d_model), so this is a
-      // contract violation: report it rather than read an absent source
+      // rows; the host guarantees they fit, so this is a contract violation:
+      // report it rather than read an absent source
       if (tid == 0) atomicExch(a.err, AXB_EINVAL);
       ok = false;
     }
@@ -1257,45 +1295,15 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     if (kind != 0) continue;
     // ---- attention of layer l (RoPE + KV write fused)
     ok = __syncthreads_and(ok) != 0;  // the staged rows are dead: the union holds attention next
-    {
-      const int active = a.params[2];
-      int nsplit, chunk;
-      attn_split_plan(active, (kSGroups * C) / (a.B * a.Hkv), a.attn_cap, nsplit, chunk);
-      const int n_items = a.B * a.Hkv * nsplit;
-      char* gsm = uni + (grp < kSGroups ? grp : 0) * (kSUnion / kSGroups);
-      const AttnLayout Lo = attn_layout(a.kv_type, HD, a.kv_group, a.attn_cap);
-      // warps beyond the attention groups take no items
-      int item = grp < kSGroups ? blockIdx.x * kSGroups + grp : n_items;
-      if (ok && item < n_items && gt == 0) {  // cached rows do not depend on this step's QKV
-        const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
-        const size_t hb = ((size_t)it.b * a.Hkv + it.kvh) * a.S;
-        attn_copy(ly, hb, Lo.rb, Lo.ng, a.kv_type != AXB_KV_F16, it.t0, min(a.attn_cap, it.t1 - it.t0), gsm, Lo,
-                  a.attn_cap, abar + grp);
-      }
-      const bool pre_ok = ok;
-      ok = cta_wait(dn + 0, tiles_of(qkv_dim), a, ok);
-      trace_mark(a, ts + 2);
-      bool first = true;
-      for (; item < n_items; item += kSGroups * C) {
-        if (!ok) {
-          // a copy issued above is still owed to this group's mbarrier
-          if (first && pre_ok) mbar_wait(abar + grp, abar_uses & 1, kSMbarLimit);
-          break;
-        }
-        const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
-        ok = attn_item<HD>(a, ly, l, it, nsplit, first, gsm, abar + grp, abar_uses, 1 + grp, gt, dn + 1, ok);
-        first = false;
-      }
-      if (gt == 0 && grp < kSGroups) trace_at(a, 4 + 10 * a.L + (4 * a.L + 1) * kStepTraceW + 2 * l + grp);
-    }
+    ok = attn_phase<HD>(a, l, uni, misc, abar_uses, ok);
     trace_mark(a, ts + 3);
   }
 
-  // ---- wind down: copies still in flight (only after an abort) get a bounded wait
+  // ---- wind down: copies still in flight (only after an abort) are waited for
   if (lane == 0)
     for (int i = 0; i < ring.inflight; ++i) {
-      mbar_wait(ring.bars + ring.cs, (uint32_t)ring.cpar, kSMbarLimit);
-      if (++ring.cs == kSStages) {
+      mbar_wait(ring.bars + ring.cs, (uint32_t)ring.cpar, kDrainLimit);
+      if (++ring.cs == ring.n) {
         ring.cs = 0;
         ring.cpar ^= 1;
       }
@@ -1326,12 +1334,70 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
 // ------------------------------------------------------------------ host
 int step_num_warps() { return kSW; }
 
-int step_attn_cap(int kv_type, int hd, int kv_group) {
-  for (int cap = 256; cap >= 16; cap -= 16) {
-    const AttnLayout L = attn_layout(kv_type, hd, kv_group, cap);
-    if (L.bytes <= kSUnion / kSGroups) return cap;
+int step_kv_maps(void* maps_host, int L, void* const* kc, void* const* vc, int rows, int kv_type, int hd) {
+  static_assert(sizeof(CUtensorMap) == kStepMapBytes, "tensor map size");
+  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+      set_error("step: cuTensorMapEncodeTiled is not available from the driver");
+      return AXB_ECUDA;
+    }
+    encode = reinterpret_cast<EncodeFn>(fn);
   }
-  return 0;
+  const int rb = kv_row_bytes(kv_type, hd), bx = kv_box_bytes(rb);
+  const CUtensorMapSwizzle sw = bx == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                          : (bx == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  CUtensorMap* maps = reinterpret_cast<CUtensorMap*>(maps_host);
+  const cuuint64_t dims[2] = {(cuuint64_t)rb, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)rb};
+  const cuuint32_t box[2] = {(cuuint32_t)bx, (cuuint32_t)kBoxRows};
+  const cuuint32_t estr[2] = {1, 1};
+  for (int l = 0; l < L; ++l)
+    for (int kv = 0; kv < 2; ++kv) {
+      CUresult r = encode(maps + 2 * l + kv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, kv ? vc[l] : kc[l], dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) {
+        set_error("step: tensor map of layer %d (%s) failed (%d)", l, kv ? "V" : "K", (int)r);
+        return AXB_ECUDA;
+      }
+    }
+  return AXB_OK;
+}
+
+StepPlan step_plan(int max_batch, int d, int F, int Hq, int Hkv, int hd, int kv_type, int kv_group, int group,
+                   int max_seq) {
+  (void)F;
+  (void)Hq;
+  (void)Hkv;
+  (void)max_seq;
+  StepPlan p = {0, 0, 0, 0};
+  const int B = std::min(max_batch, kStepMaxM);
+  const int need = stage_bytes(B, d, group);  // normalized inputs are always staged
+  for (int ns : {4, 3}) {
+    const int fixed = kSW * ns * kSlotB + kSBars + kSMisc;
+    const int avail = (kSmemMax - fixed) / 128 * 128;
+    if (avail < need) continue;
+    int cap = 0;
+    for (int c = 256; c >= kBoxRows; c -= kBoxRows)
+      if (attn_layout(kv_type, hd, kv_group, c).bytes <= avail) {
+        cap = c;
+        break;
+      }
+    if (cap == 0) continue;
+    p.nslots = ns;
+    p.union_bytes = avail;
+    p.attn_cap = cap;
+    p.smem = fixed + avail;
+    return p;
+  }
+  return p;
 }
 
 bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n_head, int n_kv_head, int d_model,
@@ -1342,11 +1408,10 @@ bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n
   if (hd != 64 && hd != 128) return false;
   if (n_kv_head <= 0 || n_head % n_kv_head != 0 || n_head / n_kv_head > kMaxRepS) return false;
   if (d_model % 128 != 0) return false;
-  if (!xs_fits(kStepMaxM, d_model, group)) return false;
-  // a K scale group spans whole 16-wide MMA steps, a V scale group a warp's output dims
-  if (kv_type != AXB_KV_F16 && (kv_group < 16 || kv_group < hd / 4 || hd % kv_group != 0)) return false;
+  // a K scale group spans whole 16-wide MMA steps, a V scale group a warp's 8 output dims
+  if (kv_type != AXB_KV_F16 && (kv_group < 16 || hd % kv_group != 0)) return false;
   if (max_seq % 8) return false;  // scales are bulk-copied in 8-token (16-byte) runs
-  return step_attn_cap(kv_type, hd, kv_group) > 0;
+  return true;
 }
 
 #define AXB_STEP_KERNELS(X) \
@@ -1355,17 +1420,17 @@ bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n
 int step_prepare() {
   int dev = 0;
   cudaGetDevice(&dev);
-  static int done_dev = -1;
-  if (done_dev == dev) return AXB_OK;
+  static DeviceOnce once;
+  if (once.done(dev)) return AXB_OK;
 #define AXB_SET(SYM, GB, HD)                                                                                 \
   {                                                                                                         \
     cudaError_t e = cudaFuncSetAttribute(step_kernel<SYM, GB, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                         (int)kSSmem);                                                      \
+                                         kSmemMax);                                                         \
     if (e != cudaSuccess) return cuda_status(e, "step kernel attribute");                                   \
   }
   AXB_STEP_KERNELS(AXB_SET)
 #undef AXB_SET
-  done_dev = dev;
+  once.set(dev);
   return AXB_OK;
 }
 
@@ -1376,9 +1441,15 @@ int step_launch(const StepArgs& a, cudaStream_t s) {
   AXB_CHECK_ARG(a.d > 0 && a.d % 128 == 0 && a.F % 64 == 0 && a.V > 0, "step: bad dims (%d, %d, %d)", a.d, a.F, a.V);
   AXB_CHECK_ARG((a.hd == 64 || a.hd == 128) && a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kMaxRepS,
                 "step: bad heads (%d, %d, %d)", a.Hq, a.Hkv, a.hd);
-  AXB_CHECK_ARG(xs_fits(kStepMaxM, a.d, a.group), "step: d_model %d too large for the staged activations", a.d);
-  AXB_CHECK_ARG(a.attn_cap >= 16 && attn_layout(a.kv_type, a.hd, a.kv_group, a.attn_cap).bytes <= kSUnion / kSGroups,
-                "step: attention chunk %d does not fit", a.attn_cap);
+  AXB_CHECK_ARG(a.plan.smem > 0 && a.plan.smem <= kSmemMax && a.plan.nslots >= 2 && a.plan.nslots <= kMaxSlots &&
+                    a.plan.union_bytes % 128 == 0,
+                "step: no shared-memory plan for this model");
+  AXB_CHECK_ARG(stage_bytes(a.B, a.d, a.group) <= a.plan.union_bytes,
+                "step: d_model %d too large for the staged activations at batch %d", a.d, a.B);
+  AXB_CHECK_ARG(a.plan.attn_cap >= kBoxRows && a.plan.attn_cap % kBoxRows == 0 &&
+                    attn_layout(a.kv_type, a.hd, a.kv_group, a.plan.attn_cap).bytes <= a.plan.union_bytes,
+                "step: attention chunk %d does not fit", a.plan.attn_cap);
+  AXB_CHECK_ARG(a.spin_limit > 0 && a.mbar_limit > 0, "step: wait limits must be positive");
   AXB_CHECK_ARG(a.lm_w && a.lm_s && a.ln_f && a.emb_w && a.emb_s && a.rope && a.tokens && a.params && a.err && a.h &&
                     a.logits && a.amax && a.done && a.tile_cnt && a.partials && a.keys && a.exit_cnt &&
                     (a.L == 0 || (a.layers && a.qkv && a.attn && a.sw && a.part_o && a.part_ml && a.attn_cnt)),
@@ -1389,7 +1460,7 @@ int step_launch(const StepArgs& a, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_sms());
   cfg.blockDim = dim3(kSThreads);
-  cfg.dynamicSmemBytes = kSSmem;
+  cfg.dynamicSmemBytes = a.plan.smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the phases wait on one another

@@ -17,6 +17,19 @@ struct StepLayer {
   uint8_t* vc;
   __half* ks;
   __half* vs;
+  const void* kmap;  // TMA tensor maps (CUtensorMap, device memory) over kc / vc as
+  const void* vmap;  // (rows = max_batch * Hkv * S, row bytes) tables
+};
+
+// Shared-memory plan of one step-kernel configuration (host-computed once per
+// runner): per-warp weight rings of `nslots` slots, a union region that holds
+// the staged activations of a GEMV phase or the attention working set, and a
+// fixed scratch area.
+struct StepPlan {
+  int nslots;       // ring slots per warp
+  int union_bytes;  // staged activations / attention working set
+  int attn_cap;     // cached tokens per attention sub-chunk
+  int smem;         // dynamic shared memory of the launch
 };
 
 struct StepArgs {
@@ -25,7 +38,7 @@ struct StepArgs {
   int d, Hq, Hkv, hd, F, V, S, kv_type, kv_group, group;
   int sym;  // 1: AXB_W_Q4T_SYM, 0: AXB_W_Q4T_AFFINE (all projections and the lm_head)
   float eps;
-  int B;  // sequences this step (one token each), <= 8
+  int B;  // sequences this step (one token each), <= kStepMaxM
   const uint32_t* emb_w;
   const __half* emb_s;
   const char* lm_w;
@@ -46,35 +59,49 @@ struct StepArgs {
   // scratch (zeroed once; every counter returns to zero by the end of a step)
   int* done;          // per-phase completion counters
   int* tile_cnt;      // per-tile arrival counters
-  float* partials;    // per warp: 2 x 32 lanes x 4 floats
+  float* partials;    // per virtual warp: 32 lanes x 4 floats
   float* part_o;      // attention split partials (B, Hq, kStepMaxSplits, hd)
   float* part_ml;     // (B, Hq, kStepMaxSplits, 2)
-  int* attn_cnt;      // (B, Hkv)
+  int* attn_cnt;      // (B, Hkv) split arrivals, grow through a step
   unsigned long long* keys;  // per-token argmax keys
   int* exit_cnt;
   int max_tiles;      // size of tile_cnt
-  int attn_cap;       // tokens per attention sub-chunk
+  StepPlan plan;
+  // bounded waits: polls of a cross-CTA counter and of a copy's mbarrier
+  // before the step gives up with AXB_ETIMEOUT (copies already issued are
+  // still waited for, with a fixed limit, before a CTA exits)
+  uint32_t spin_limit;
+  uint32_t mbar_limit;
+  int pref_kb;        // k-blocks ahead of a warp's ring that it also prefetches into L2 (0: off)
+  __half* hdump;      // optional (L, B, d): the residual stream after each layer
   unsigned long long* trace;  // optional phase timeline: [CTA][step_trace_slots(L)] globaltimer stamps
 };
 
 // Phase timeline slots per CTA: start, 10 per layer, then lm_head wait,
 // lm_head done, exit (thread 0); then, per GEMV phase, the time each of the
-// CTA's warps finished its share; then, per layer, the time each of the two
-// attention groups finished its items.
-constexpr int kStepTraceW = 16;  // warp slots per GEMV phase (at least the warps per CTA)
+// CTA's warps finished its share; then, per layer, the time the CTA finished
+// its attention items.
+constexpr int kStepTraceW = 16;  // warp slots per GEMV phase (the warps per CTA)
 __host__ __device__ inline int step_trace_slots(int L) { return 4 + 10 * L + (4 * L + 1) * kStepTraceW + 2 * L; }
 
 constexpr int kStepMaxSplits = 64;
 constexpr int kStepMaxM = 8;
+constexpr uint32_t kStepSpinLimit = 1u << 22;  // default polls of a cross-CTA counter
+constexpr uint32_t kStepMbarLimit = 1u << 22;  // default polls of a copy's mbarrier
 
 // host side
 int step_prepare();
-// Tokens per attention sub-chunk for this cache format, or 0 when the
-// attention working set does not fit the kernel's shared memory.
-int step_attn_cap(int kv_type, int hd, int kv_group);
+// Shared-memory plan for a model (batch up to max_batch); plan.smem == 0 when
+// the configuration does not fit the kernel.
+StepPlan step_plan(int max_batch, int d, int F, int Hq, int Hkv, int hd, int kv_type, int kv_group, int group,
+                   int max_seq);
 bool step_supported(int wfmt, int group, int lm_fmt, int lm_group, int hd, int n_head, int n_kv_head, int d_model,
                     int kv_type, int kv_group, int max_seq);
 int step_num_warps();  // warps per CTA of the step kernel (partials are sized per warp)
 int step_launch(const StepArgs& a, cudaStream_t s);
+// Encode the tensor maps of every layer's K and V cache into maps_host
+// (2 * L CUtensorMap, K then V per layer) for the attention staging.
+int step_kv_maps(void* maps_host, int L, void* const* kc, void* const* vc, int rows, int kv_type, int hd);
+constexpr int kStepMapBytes = 128;  // sizeof(CUtensorMap)
 
 }  // namespace axb

@@ -88,6 +88,7 @@ __global__ void tp_key_kernel(const __half* __restrict__ logits, int ld, const i
   if (r >= rows) return;
   const int li = local_idx[r];
   uint32_t bits = __float_as_uint(__half2float(logits[(size_t)r * ld + li]));
+  if (bits == 0x80000000u) bits = 0u;  // -0 == +0: a tie, which the lower index wins
   bits = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
   keys[r] = ((unsigned long long)bits << 32) | (0xFFFFFFFFu - (uint32_t)(base + li));
 }

@@ -65,7 +65,8 @@ _ATTN_WS = _Workspace()
 
 @dataclass
 class Q4TWeight:
-    """A projection in the q4t layout ("Weight layout")."""
+    """A projection in the q4t layout: 16-row tiles, each tile's K range stored
+    contiguously as 64-wide k-blocks of 512 B of mma A-fragment words."""
 
     words: torch.Tensor  # int32, (tiles * K/64 * 128,)
     scales: torch.Tensor  # fp16

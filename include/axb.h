@@ -33,7 +33,10 @@ extern "C" {
 
 /* ---- formats ----------------------------------------------------------------- */
 /* Projection weights: q4t = 16-row tiles of mma A-fragments, 64207531 nibble
- * interleave.  SYM: w = (q - 8) * s; AFFINE: w = q * s + b. */
+ * interleave.  A tile (16 rows) stores its K range contiguously as 64-wide
+ * k-blocks of 512 B; lane l = 4g + t of a warp owns, in 32-bit word j, rows
+ * {g, g + 8} x columns 64b + 16t + 4j + {0..3}.  SYM: w = (q - 8) * s;
+ * AFFINE: w = q * s + b. */
 #define AXB_W_Q4T_SYM 1
 #define AXB_W_Q4T_AFFINE 2
 #define AXB_W_Q8_G64 3 /* reference Q8_G64 row-major (quant.py:72) */
@@ -181,10 +184,15 @@ int axb_qgemm(const axb_qgemm_desc* d, void* stream);
  * call on a device looks the array's device address up (make that call before
  * any stream capture).  All calls share the array: two calls that may run at
  * the same time on the GPU (different streams without ordering) race.  Each
- * call clears the parts of the array that must start at zero.  This entry
- * point has no counterpart in the reference. */
+ * call clears the tile counters, which must start at zero; the error word
+ * holds until axb_qgemm_noalloc_status reads it.  This entry point has no
+ * counterpart in the reference. */
 int axb_qgemm_noalloc(const axb_qgemm_desc* d, void* stream);
 size_t axb_qgemm_noalloc_scratch_bytes(void);
+/* Synchronizes `stream`; returns AXB_ETIMEOUT (and clears the flag) if a
+ * bounded weight-stream wait of an earlier axb_qgemm_noalloc on this device
+ * ran out, so its y may be incomplete.  No counterpart in the reference. */
+int axb_qgemm_noalloc_status(void* stream);
 /* Synchronizes `stream`; returns AXB_ETIMEOUT (and clears the flag) if a
  * bounded weight-stream wait in an earlier axb_qgemm on this workspace ran out. */
 int axb_qgemm_status(void* workspace, void* stream);
@@ -340,9 +348,20 @@ int axb_runner_destroy(void* handle);
  * 2 argmax int32 (rows), 3 final-norm hidden fp32 (rows, d), 4 error word int32
  * (non-zero after a step that met an out-of-vocabulary token id or a bounded
  * device wait that ran out), 5 step-kernel phase timeline uint64 (SMs,
- * 4 + 10 * n_layer) globaltimer stamps, written when AXB_STEP_TRACE=1 was set
- * at creation */
+ * slots per SM) globaltimer stamps, written when AXB_STEP_TRACE=1 was set at
+ * creation or AXB_DEBUG_TRACE is on, 6 step-kernel residual stream after each
+ * layer fp16 (n_layer, B, d), written when AXB_DEBUG_HDUMP is on */
 int axb_runner_buffer(void* handle, int which, size_t* offset_out, size_t* bytes_out);
+/* Test and diagnosis hooks of the persistent step kernel (no counterpart in
+ * the reference): flags AXB_DEBUG_HDUMP (per-layer hidden states into buffer
+ * 6) and AXB_DEBUG_TRACE (phase timeline into buffer 5); spin_limit /
+ * mbar_limit: polls of a cross-CTA counter / of a copy's mbarrier before a
+ * step gives up with AXB_ETIMEOUT (0 = the defaults, 2^22).  A step that gives
+ * up still waits for its own copies in flight and leaves the runner usable.
+ * A no-op for runners on the per-kernel graph path. */
+#define AXB_DEBUG_HDUMP 1
+#define AXB_DEBUG_TRACE 2
+int axb_runner_set_debug(void* handle, int flags, uint32_t spin_limit, uint32_t mbar_limit);
 /* One forward step over B sequences x T new tokens already placed in the
  * token buffer.  T == 1 and masks == NULL: decode (all active slots visible).
  * Otherwise tree/chunk mode: masks[t] / depths[t] host arrays of length T. */
