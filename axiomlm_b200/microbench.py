@@ -16,9 +16,7 @@ from __future__ import annotations
 
 import argparse
 import ctypes as C
-import os
 import random
-import sys
 
 import torch
 
@@ -110,14 +108,11 @@ def random_tree(nodes: int, max_depth: int = 6, max_children: int = 4, seed: int
 
 
 def bench_tree(ctx: int, nodes: int, layers: int) -> str:
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    sys.path.insert(0, root)
-    import bench  # the bench's 8B-shape weights and packing
-
+    from . import synth
     from .model import QuantizedDecoder
 
-    cfg = dict(bench.CFG_8B, n_layer=layers)
-    tmp = bench.build_decoder(cfg, 1, 64, ("fp8", 128))
+    cfg = dict(synth.CFG_8B, n_layer=layers)
+    tmp = synth.build_decoder(cfg, 1, 64, ("fp8", 128))
     packed = tmp.packed
     tmp.close()
     dec = QuantizedDecoder(cfg, packed, kv_dtype="fp8", kv_group=128, max_batch=1, max_seq=ctx + 128,
@@ -153,12 +148,10 @@ def bench_medusa(heads: int, residual: bool) -> str:
     from .medusa import DEFAULT_MEDUSA_TREE_CHOICES, DeviceTree, MedusaHeads, compile_medusa_tree, draft_tokens
     from .model import QuantizedDecoder
 
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    sys.path.insert(0, root)
-    import bench
+    from . import synth
 
-    cfg = dict(bench.CFG_8B, n_layer=1)
-    tmp = bench.build_decoder(cfg, 1, 64, ("fp8", 128))
+    cfg = dict(synth.CFG_8B, n_layer=1)
+    tmp = synth.build_decoder(cfg, 1, 64, ("fp8", 128))
     packed = tmp.packed
     tmp.close()
     dec = QuantizedDecoder(cfg, packed, kv_dtype="fp8", kv_group=128, max_batch=1, max_seq=4096, max_tokens=64,

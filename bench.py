@@ -34,13 +34,13 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CFG_8B = dict(n_layer=32, d_model=4096, n_head=32, n_kv_head=8, ffn=14336, vocab=128256, eps=1e-5, theta=10000.0,
-              block_size=8192)
+from axiomlm_b200.synth import CFG_8B  # noqa: E402  (after the path insert)
+
 METRIC = "decode tokens/s (Q4 8B-shape, FP8 KV, ctx 4096)"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # DRAM bytes (read + write) per algorithmic byte of the step kernel, from one
-# ncu capture of a smaller case (profiles/step_kernel_8b_q4g128_fp8.md); the
-# traffic of a full launch is this ratio times its algorithmic bytes.
+# ncu capture of a smaller case (the 8B layer shapes, 2 layers); the traffic of
+# a full launch is this ratio times its algorithmic bytes.
 STEP_TRAFFIC_RATIO = 1.015
 
 
@@ -152,50 +152,15 @@ class ClockSampler:
 # ------------------------------------------------------------------ our arm
 
 def build_decoder(cfg, batch, ctx, kv, seed=0, tp=None):
-    """Random N(0, 0.02) weights packed on the GPU.  With ``tp`` (tensor
-    parallel) this rank packs only its shard: H / N query heads, Hkv / N KV
-    heads, F / N FFN rows, V / N vocab rows; the embedding and the norms,
-    replicated, come from the same seed on every rank."""
-    from axiomlm_b200 import ops
-    from axiomlm_b200.model import QuantizedDecoder
+    from axiomlm_b200.synth import build_decoder as bd
 
-    world = tp.world if tp is not None else 1
-    g = torch.Generator(device="cuda").manual_seed(seed + (tp.rank if tp is not None else 0))
-    dev = torch.device("cuda")
-
-    def rn(*shape):
-        return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * 0.02
-
-    d, H, Hkv, F, V = cfg["d_model"], cfg["n_head"], cfg["n_kv_head"], cfg["ffn"], cfg["vocab"]
-    hd = d // H
-    H, Hkv, F, V_l = H // world, Hkv // world, F // world, V // world
-    layers = []
-    for _ in range(cfg["n_layer"]):
-        layers.append(dict(
-            qkv=ops.pack_q4t(rn((H + 2 * Hkv) * hd, d), 128, True), o=ops.pack_q4t(rn(d, H * hd), 128, True),
-            gu=ops.pack_q4t(rn(2 * F, d), 128, True, gate_up=True), down=ops.pack_q4t(rn(d, F), 128, True),
-            ln_1=torch.ones(d, device=dev), ln_2=torch.ones(d, device=dev), qkv_b=None))
-        torch.cuda.synchronize()
-    gr = torch.Generator(device="cuda").manual_seed(seed + 7919)  # replicated tensors: same on every rank
-    wte = torch.randn(V, d, generator=gr, device=dev, dtype=torch.float32) * 0.02
-    emb_w, emb_s = ops.pack_q8_g64(wte)
-    del wte
-    lm = ops.pack_q4t(rn(V_l, d), 128, True)
-    packed = dict(layers=layers, emb_w=emb_w, emb_s=emb_s, lm_head=lm, ln_f=torch.ones(d, device=dev))
-    torch.cuda.synchronize()
-    kv_dtype, kv_group = kv
-    dec = QuantizedDecoder(cfg, packed, kv_dtype=kv_dtype, kv_group=kv_group, max_batch=batch,
-                           max_seq=ctx + 1024, max_tokens=1, rope_len=cfg["block_size"], tp=tp)
-    return dec
+    return bd(cfg, batch, ctx, kv, seed=seed, tp=tp)
 
 
 def fill_context(dec, batch, ctx, seed=1):
-    """ctx random token ids per sequence, run through the decode graph."""
-    g = torch.Generator(device="cuda").manual_seed(seed)
-    toks = torch.randint(0, dec.cfg["vocab"], (batch, ctx), generator=g, device="cuda")
-    for t in range(ctx):
-        dec.decode_step(toks[:, t:t + 1])
-    torch.cuda.synchronize()
+    from axiomlm_b200.synth import fill_context as fc
+
+    fc(dec, batch, ctx, seed=seed)
 
 
 def step_bytes(dec, batch):
@@ -392,7 +357,7 @@ def run_ours(args, rank, world):
             "clocks": clk.summary(), "gpu_launches": launches_per_step * args.steps,
         }
         if world == 1 and not args.no_cpu_baseline:
-            out["cpu_baseline"] = cpu_baseline(cfg, B, args.ctx, kv, reps=1)
+            out["cpu_baseline"] = cpu_baseline(cfg, B, args.ctx, kv, args)
     dec.close()
     if tp is not None:
         tp.close()
@@ -439,48 +404,176 @@ def _cpu_sample_fns(cfg, B, ctx, kv):
         o = linear("o", y, H * hd, d)
         gu = linear("gu", o, d, 2 * F).float()
         sw = torch.nn.functional.silu(gu[..., :F]) * gu[..., F:]
-        linear("down", sw, F, d)
-        linear("lm", o, d, V // cfg["n_layer"])
+        dn = linear("down", sw, F, d)
+        linear("lm", dn, d, V // cfg["n_layer"])
 
     return sample
 
 
-def cpu_baseline(cfg, B, ctx, kv, reps=1):
+def cpu_baseline(cfg, B, ctx, kv, args):
+    """The reported CPU baseline beside our arm: one full decode step of the
+    reference's own CPU path (reference_cpu), or, when the reference is not
+    installed, the oracle restatement on a bounded sample."""
+    import copy
+
+    a = copy.copy(args)
+    a.steps, a.warmup = 1, 1
+    res = reference_cpu(a)
+    if res is not None:
+        t = sum(res["step_s"]) / res["steps"]
+        return {"value": round(B / t, 4), "unit": "tokens/s", "cores": res["cores"], "kind": "reference",
+                "sample": f"1 full {res['layers']}-layer decode step of {res['module']} after 1 warm-up step "
+                          f"({t:.1f} s; one packed layer serving every layer slot; FP8 G64 cache, ctx {ctx})"}
     torch.set_num_threads(os.cpu_count() or 1)
     sample = _cpu_sample_fns(cfg, B, ctx, kv)
     sample()  # warm
-    ts = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        sample()
-        ts.append(time.perf_counter() - t0)
-    tok_s = B / (min(ts) * cfg["n_layer"])
-    return {"value": round(tok_s, 4), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+    t0 = time.perf_counter()
+    sample()
+    t = time.perf_counter() - t0
+    return {"value": round(B / (t * cfg["n_layer"]), 4), "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port",
             "sample": f"1 of {cfg['n_layer']} layers + 1/{cfg['n_layer']} of lm_head rows per step "
-                      f"(per-call dequant + F.linear, SDPA over the dequantized FP8 cache, ctx {ctx}), x{cfg['n_layer']}"}
+                      f"(oracle restatement: per-call dequant + F.linear, SDPA over the dequantized FP8 cache, "
+                      f"ctx {ctx}), x{cfg['n_layer']}"}
+
+
+REF_ROOT = os.path.join(ROOT, "baseline", "_ref")  # the reference, installed offline (pip --target)
+
+
+def _ref_step_worker(args):
+    """The reference's own CPU decode path, timed on the host cores (run in a
+    fresh process: no CUDA context, every core to torch's CPU kernels).
+
+    A step is one greedy decode token at the bench config through
+    ``Transformer.forward`` -> ``_forward_quantized_sequence``
+    (axiomlm/models/transformer.py:1036-1200) after ``quantize("q4_rtn")``:
+    every layer's ``qmv_q4_marlin`` (quant.py:637-661, which dequantizes the
+    whole matrix on every call), RMSNorm, RoPE, ``StaticKVCache.update``
+    (paged_cache.py:218-361, re-quantizing and dequantizing the FP8 window) and
+    SDPA, then the lm_head.  To keep the set-up within seconds, one decoder
+    layer is packed by the reference and its packed tensors serve all 32
+    layer slots (the cost of a layer does not depend on the weight values);
+    the 4096-token context is written straight into the reference's cache
+    buffers as FP8 codes made by its own quantize_kv_fp8.  The reference's FP8
+    cache has a scale per 64 elements (its only FP8 format)."""
+    if not os.path.isdir(os.path.join(REF_ROOT, "axiomlm")):
+        return None
+    sys.path.insert(0, REF_ROOT)
+    torch.set_num_threads(os.cpu_count() or 1)
+    from axiomlm.engine.paged_cache import StaticKVCache
+    from axiomlm.kernels.quant import quantize_kv_fp8
+    from axiomlm.models.transformer import ModelConfig, Transformer
+
+    cfg = dict(CFG_8B)
+    if args.layers:
+        cfg["n_layer"] = args.layers
+    L, B, ctx = cfg["n_layer"], args.batch, args.ctx
+    d, H, Hkv, F, V = cfg["d_model"], cfg["n_head"], cfg["n_kv_head"], cfg["ffn"], cfg["vocab"]
+    hd = d // H
+    n_steps, n_warm = max(1, min(args.steps, 2)), max(1, min(args.warmup, 1))
+    t_setup = time.perf_counter()
+    mc = ModelConfig(block_size=ctx + n_steps + n_warm + 8, vocab_size=V, n_layer=1, n_head=H, n_embd=d,
+                     n_kv_head=Hkv, intermediate_size=F, rms_norm_eps=cfg["eps"], rope_theta=cfg["theta"],
+                     tie_word_embeddings=False)
+    g = torch.Generator().manual_seed(0)
+    with torch.no_grad():
+        m = Transformer(mc, init_weights=False)
+        for name, p in m.named_parameters():
+            if p.dim() == 1:
+                p.fill_(1.0)
+            else:
+                p.normal_(0.0, 0.02, generator=g)
+        m.eval()
+        m.quantize("q4_rtn")
+        qw = m._ensure_quant_weights(torch.device("cpu"))
+        for key in ("c_attn_p", "c_attn_s", "c_attn_b", "c_proj_p", "c_proj_s", "gu_p", "gu_s", "wd_p", "wd_s"):
+            qw[key] = [qw[key][0]] * L
+        m.transformer.h = torch.nn.ModuleList([m.transformer.h[0]] * L)
+        m.config.n_layer = L
+        cache = StaticKVCache(B, mc.block_size, L, Hkv, hd, dtype=torch.float16, device="cpu", cache_dtype="fp8")
+        k = torch.randn(B, Hkv, ctx, hd, generator=g).half()
+        v = torch.randn(B, Hkv, ctx, hd, generator=g).half()
+        kq, ks, vq, vs = quantize_kv_fp8(k, v)
+        for i in range(L):
+            cache.k_caches[i][:, :, :ctx] = kq
+            cache.v_caches[i][:, :, :ctx] = vq
+            cache.k_scales[i][:, :, :ctx] = ks
+            cache.v_scales[i][:, :, :ctx] = vs
+        cache.total_seen_tokens = [ctx] * L
+        cache.layer_seq_lens = [ctx] * L
+        t_setup = time.perf_counter() - t_setup
+        idx = torch.randint(0, V, (B, 1), generator=g)
+        for _ in range(n_warm):
+            logits, _, _ = m(idx, kv_caches=cache)
+            idx = logits[:, -1].argmax(-1, keepdim=True)
+        times = []
+        for _ in range(n_steps):
+            t0 = time.perf_counter()
+            logits, _, _ = m(idx, kv_caches=cache)
+            idx = logits[:, -1].argmax(-1, keepdim=True)
+            times.append(time.perf_counter() - t0)
+    return {"step_s": times, "setup_s": t_setup, "cores": torch.get_num_threads(), "layers": L, "batch": B,
+            "steps": n_steps, "warmup": n_warm, "module": "axiomlm.models.transformer.Transformer (q4_rtn)"}
+
+
+def reference_cpu(args):
+    """Time the reference's CPU step in a child process (spawned fresh: no
+    CUDA context is inherited); None when the reference is not installed."""
+    import subprocess
+
+    cmd = [sys.executable, os.path.abspath(__file__), "--ref-worker", "--batch", str(args.batch), "--ctx",
+           str(args.ctx), "--steps", str(args.steps), "--warmup", str(args.warmup)]
+    if args.layers:
+        cmd += ["--layers", str(args.layers)]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
+    if r.returncode != 0 or not lines:
+        sys.stderr.write(r.stderr[-2000:])
+        return None
+    return json.loads(lines[-1])
 
 
 def run_reference(args, rank, world):
+    """``--impl reference``: the reference's own CPU decode path, rank 0 only
+    (other ranks exit without work).  Falls back to the oracle restatement
+    only when the reference is not installed."""
     if rank != 0:
         return None
     cfg = dict(CFG_8B)
-    kv = {"fp8_head": ("fp8", 128), "fp8_g64": ("fp8", 64), "fp16": ("fp16", 64), "int4_g32": ("int4", 32)}[args.kv]
-    torch.set_num_threads(os.cpu_count() or 1)
-    sample = _cpu_sample_fns(cfg, args.batch, args.ctx, kv)
-    for _ in range(args.warmup):
-        sample()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        sample()
-    t = (time.perf_counter() - t0) * cfg["n_layer"]
-    v = args.batch * args.steps / t
-    cb = {"value": round(v, 4), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-          "sample": f"per step: 1 of {cfg['n_layer']} layers + 1/{cfg['n_layer']} of lm_head rows, x{cfg['n_layer']}"}
+    if args.layers:
+        cfg["n_layer"] = args.layers
+    res = reference_cpu(args)
+    if res is None:
+        kv = {"fp8_head": ("fp8", 128), "fp8_g64": ("fp8", 64), "fp16": ("fp16", 64), "int4_g32": ("int4", 32)}[args.kv]
+        torch.set_num_threads(os.cpu_count() or 1)
+        sample = _cpu_sample_fns(cfg, args.batch, args.ctx, kv)
+        for _ in range(args.warmup):
+            sample()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            sample()
+        t = (time.perf_counter() - t0) * cfg["n_layer"]
+        steps, warm, ms = args.steps, args.warmup, t / args.steps * 1e3
+        kind, sample_txt, cores = "port", (f"per step: 1 of {cfg['n_layer']} layers + 1/{cfg['n_layer']} of lm_head "
+                                           f"rows, x{cfg['n_layer']} (oracle restatement; reference not installed)"), \
+            torch.get_num_threads()
+    else:
+        steps, warm, cores = res["steps"], res["warmup"], res["cores"]
+        t = sum(res["step_s"])
+        ms = t / steps * 1e3
+        kind = "reference"
+        sample_txt = (f"{steps} full {res['layers']}-layer decode steps of {res['module']} on the host cores "
+                      f"(one packed layer serving every layer slot; FP8 G64 cache, ctx {args.ctx}); "
+                      f"per-step s: {', '.join('%.2f' % x for x in res['step_s'])}; set-up {res['setup_s']:.0f} s")
+    v = args.batch * steps / t
+    cb = {"value": round(v, 4), "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample_txt}
     return {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 2),
+            "steps": steps, "warmup": warm, "ms_per_step": round(ms, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (CPU)",
-            "data": "synthetic", "config": {"workload": f"Llama-3-8B-shape decode, Q4 (reference MARLIN layout), "
-                                                        f"KV {args.kv}, ctx {args.ctx}, batch {args.batch}",
+            "data": "synthetic", "config": {"workload": f"Llama-3-8B-shape decode ({cfg['n_layer']} layers), Q4 "
+                                                        f"(reference MARLIN RTN layout), KV fp8 G64, ctx {args.ctx}, "
+                                                        f"batch {args.batch}",
                                             "global_batch": args.batch, "seq_len": args.ctx,
                                             "parallelism": "CPU, rank 0 only"},
             "cpu_baseline": cb, "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -499,7 +592,13 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (debug only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (all ranks share one batch)")
+    ap.add_argument("--ref-worker", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.ref_worker:  # child process of reference_cpu: CPU only
+        res = _ref_step_worker(args)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
     if args.steps is None:
         args.steps = 200 if args.impl == "ours" else 5
     if args.warmup is None:

@@ -506,14 +506,25 @@ def _q4t_word_coords():
 _Q4T_ROWS, _Q4T_KS = _q4t_word_coords()
 
 
+_Q4T_FLAT = (_Q4T_ROWS * 64 + _Q4T_KS).reshape(-1)  # (32*4*8,) offsets into a 16 x 64 block
+
+
 def _q4t_pack_codes(q: np.ndarray) -> np.ndarray:
-    """q (Npad, K) int codes 0..15 -> words uint32 (tiles, K/64, 32, 4)."""
+    """q (Npad, K) int codes 0..15 -> words uint32 (tiles, K/64, 32, 4).
+    Processed in tile chunks: (tile, k-block) blocks made contiguous, the
+    fragment positions gathered by one flat index, 8 nibbles per word."""
     npad, K = q.shape
     nt, kb = npad // 16, K // 64
-    qb = q.reshape(nt, 16, kb, 64).transpose(0, 2, 1, 3)  # (nt, kb, 16, 64)
-    vals = qb[:, :, _Q4T_ROWS, _Q4T_KS].astype(np.uint32)  # (nt, kb, 32, 4, 8)
+    out = np.empty((nt, kb, 32, 4), np.uint32)
+    step = max(1, (1 << 22) // (16 * K))  # about 4M codes per chunk
     sh = (np.arange(8, dtype=np.uint32) * 4)
-    return ((vals & 0xF) << sh).sum(-1, dtype=np.uint32)
+    for t0 in range(0, nt, step):
+        t1 = min(nt, t0 + step)
+        qb = np.ascontiguousarray(q[t0 * 16:t1 * 16].astype(np.uint8).reshape(t1 - t0, 16, kb, 64)
+                                  .transpose(0, 2, 1, 3)).reshape(t1 - t0, kb, 1024)
+        vals = np.take(qb, _Q4T_FLAT, axis=2).reshape(t1 - t0, kb, 32, 4, 8).astype(np.uint32)
+        out[t0:t1] = ((vals & 0xF) << sh).sum(-1, dtype=np.uint32)
+    return out
 
 
 def _q4t_unpack_codes(words: np.ndarray) -> np.ndarray:
@@ -551,22 +562,29 @@ def q4t_pack(w, group: int = 128, symmetric: bool = True, gate_up: bool = False)
     assert K % 64 == 0 and K % group == 0
     nt = (N + 15) // 16
     src = _gu_rows(nt * 16, N, gate_up)
-    wp = np.concatenate([w, np.zeros((1, K), np.float32)], 0)[src]
-    wg = wp.reshape(nt * 16, K // group, group)
-    if symmetric:
-        amax = np.abs(wg).max(-1)
-        s = (np.maximum(amax, np.float32(1e-8)) / np.float32(7.0)).astype(np.float16)
-        sf = s[..., None].astype(np.float32)
-        with np.errstate(divide="ignore", invalid="ignore"):
-            q = np.clip(np.rint(wg / sf), -8, 7)
-        q = np.where(sf == 0, 0, q).astype(np.int32) + 8
-        sc = s.reshape(nt, 2, 8, K // group).transpose(0, 3, 2, 1)  # (nt, grp, 8, [g, g+8])
-    else:
-        q, s, b = _rtn_affine(wg, 15.0)
-        sb = np.stack([s, b], -1).reshape(nt, 2, 8, K // group, 2)  # (nt, h, g, grp, 2)
-        sc = sb.transpose(0, 3, 2, 1, 4).reshape(nt, K // group, 8, 4)
-    words = _q4t_pack_codes(q.reshape(nt * 16, K))
-    return words.view(np.int32), np.ascontiguousarray(sc.astype(np.float16))
+    words = np.empty((nt, K // 64, 32, 4), np.uint32)
+    sc = np.empty((nt, K // group, 8, 2 if symmetric else 4), np.float16)
+    step = max(1, (1 << 22) // (16 * K))  # tiles per chunk: about 4M weights (rows are independent)
+    zero = np.zeros((1, K), np.float32)
+    for t0 in range(0, nt, step):
+        t1 = min(nt, t0 + step)
+        rows = src[t0 * 16:t1 * 16]
+        wp = np.where((rows < N)[:, None], w[np.minimum(rows, N - 1)], zero)
+        wg = wp.reshape((t1 - t0) * 16, K // group, group)
+        if symmetric:
+            amax = np.abs(wg).max(-1)
+            s16 = (np.maximum(amax, np.float32(1e-8)) / np.float32(7.0)).astype(np.float16)
+            sf = s16[..., None].astype(np.float32)
+            with np.errstate(divide="ignore", invalid="ignore"):
+                q = np.clip(np.rint(wg / sf), -8, 7)
+            q = np.where(sf == 0, 0, q).astype(np.int32) + 8
+            sc[t0:t1] = s16.reshape(t1 - t0, 2, 8, K // group).transpose(0, 3, 2, 1)  # (nt, grp, 8, [g, g+8])
+        else:
+            q, s16, b16 = _rtn_affine(wg, 15.0)
+            sb = np.stack([s16, b16], -1).reshape(t1 - t0, 2, 8, K // group, 2)  # (nt, h, g, grp, 2)
+            sc[t0:t1] = sb.transpose(0, 3, 2, 1, 4).reshape(t1 - t0, K // group, 8, 4)
+        words[t0:t1] = _q4t_pack_codes(q.reshape((t1 - t0) * 16, K))
+    return words.view(np.int32), sc
 
 
 def q4t_dequant(words, scales, K: int, group: int, symmetric: bool, out_features: int | None = None,
@@ -806,6 +824,7 @@ class OracleCache:
     head_dim: int
     cache_dtype: str = "fp16"  # fp16 | fp8 | int4
     ring_buffer: bool = False
+    kv_group: int = 64  # 64: the reference; head_dim: one FP8 scale per (token, head); 32: INT4 G32
     seen: int = 0
     k: list = field(default_factory=list)
     v: list = field(default_factory=list)
@@ -814,7 +833,7 @@ class OracleCache:
 
     def __post_init__(self):
         L, B, H, S, D = self.n_layer, self.max_batch, self.n_kv_head, self.max_seq, self.head_dim
-        G = max(1, D // 64)
+        G = max(1, D // self.kv_group)
         for _ in range(L):
             if self.cache_dtype == "fp16":
                 self.k.append(np.zeros((B, H, S, D), np.float16))
@@ -843,8 +862,8 @@ class OracleCache:
             self.v[layer][:B, :, slots] = v16
             return
         qf = quant_kv_fp8 if self.cache_dtype == "fp8" else quant_kv_int4
-        kq, ks = qf(k16)
-        vq, vs = qf(v16)
+        kq, ks = qf(k16, self.kv_group)
+        vq, vs = qf(v16, self.kv_group)
         self.k[layer][:B, :, slots] = kq
         self.v[layer][:B, :, slots] = vq
         self.ks[layer][:B, :, slots] = ks
@@ -855,11 +874,11 @@ class OracleCache:
         if self.cache_dtype == "fp16":
             k, v = self.k[layer][:B, :, :n], self.v[layer][:B, :, :n]
         elif self.cache_dtype == "fp8":
-            k = dequant_kv_fp8(self.k[layer][:B, :, :n], self.ks[layer][:B, :, :n])
-            v = dequant_kv_fp8(self.v[layer][:B, :, :n], self.vs[layer][:B, :, :n])
+            k = dequant_kv_fp8(self.k[layer][:B, :, :n], self.ks[layer][:B, :, :n], self.kv_group)
+            v = dequant_kv_fp8(self.v[layer][:B, :, :n], self.vs[layer][:B, :, :n], self.kv_group)
         else:
-            k = dequant_kv_int4(self.k[layer][:B, :, :n], self.ks[layer][:B, :, :n])
-            v = dequant_kv_int4(self.v[layer][:B, :, :n], self.vs[layer][:B, :, :n])
+            k = dequant_kv_int4(self.k[layer][:B, :, :n], self.ks[layer][:B, :, :n], self.kv_group)
+            v = dequant_kv_int4(self.v[layer][:B, :, :n], self.vs[layer][:B, :, :n], self.kv_group)
         return torch.from_numpy(np.ascontiguousarray(k)), torch.from_numpy(np.ascontiguousarray(v))
 
     def compact(self, write_pos: int, accepted: list[int], new_seen: int):
@@ -891,9 +910,15 @@ class OracleModel:
     projections and lm_head (Q8_G64 when tied), Q8_G64 token embeddings.
     RMSNorm weights stay fp32 (the reference model's parameter dtype), so the
     norms are evaluated in fp32 and cast to fp16 by ``_qlin``.
+
+    ``weight_format="q4_g128_sym"`` is the BASELINE variant (parity
+    unpinned): the projections and an untied lm_head are quantized by
+    ``q4t_pack`` (symmetric, group 128, fp16 scales) and dequantized by
+    ``q4t_dequant``; everything else -- embeddings, norms, the forward -- is the
+    reference's ``q4_rtn`` path unchanged.
     """
 
-    def __init__(self, cfg: dict, weights: dict, rope_len: int):
+    def __init__(self, cfg: dict, weights: dict, rope_len: int, weight_format: str = "q4_rtn"):
         self.cfg = cfg
         d, H, Hkv = cfg["d_model"], cfg["n_head"], cfg["n_kv_head"]
         self.hd = d // H
@@ -901,22 +926,26 @@ class OracleModel:
         self.eps = cfg["eps"]
         self.V = cfg["vocab"]
         self.F = cfg["ffn"]
+        if weight_format not in ("q4_rtn", "q4_g128_sym"):
+            raise ValueError(f"unknown weight format {weight_format}")
+        self.sym = weight_format == "q4_g128_sym"
+        pack = (lambda w: q4t_pack(w, 128, True)) if self.sym else pack_q4_marlin_rtn
         tied = weights.get("lm_head") is None
         if tied:
             self.lmh = ("q8",) + pack_q8_g64(weights["wte"])
             self.wte = self.lmh[1:]
         else:
-            self.lmh = ("q4",) + pack_q4_marlin_rtn(weights["lm_head"])
+            self.lmh = ("q4",) + pack(weights["lm_head"])
             self.wte = pack_q8_g64(weights["wte"])
         self.layers = []
         for lw in weights["layers"]:
             gu = np.concatenate([_f32(_to_np(lw["w_gate"])), _f32(_to_np(lw["w_up"]))], 0)
             self.layers.append(
                 dict(
-                    c_attn=pack_q4_marlin_rtn(lw["c_attn"]),
-                    c_proj=pack_q4_marlin_rtn(lw["c_proj"]),
-                    gu=pack_q4_marlin_rtn(gu),
-                    wd=pack_q4_marlin_rtn(lw["w_down"]),
+                    c_attn=pack(lw["c_attn"]),
+                    c_proj=pack(lw["c_proj"]),
+                    gu=pack(gu),
+                    wd=pack(lw["w_down"]),
                     ln_1=torch.as_tensor(_to_np(lw["ln_1"])).float(),
                     ln_2=torch.as_tensor(_to_np(lw["ln_2"])).float(),
                 )
@@ -927,7 +956,10 @@ class OracleModel:
 
     def _w(self, key, packed, K, n):
         if key not in self._dq:
-            self._dq[key] = torch.from_numpy(dequant_q4_marlin(packed[0], packed[1], K, n))
+            if self.sym:
+                self._dq[key] = torch.from_numpy(q4t_dequant(packed[0], packed[1], K, 128, True, n))
+            else:
+                self._dq[key] = torch.from_numpy(dequant_q4_marlin(packed[0], packed[1], K, n))
         return self._dq[key]
 
     def qlin(self, x: torch.Tensor, key, packed, n_out: int) -> torch.Tensor:
@@ -945,9 +977,11 @@ class OracleModel:
             return F.linear(xn.to(torch.float16), w).to(xn.dtype)
         return self.qlin(xn, "lmh", self.lmh[1:], self.V)
 
-    def forward(self, idx: np.ndarray, cache: OracleCache, return_all: bool = False):
+    def forward(self, idx: np.ndarray, cache: OracleCache, return_all: bool = False, hidden: list | None = None):
         """One ``_forward_quantized_sequence`` call (transformer.py:1036-1200).
-        idx (B, T) ints.  Returns (logits fp16, x_norm)."""
+        idx (B, T) ints.  Returns (logits fp16, x_norm).  With ``hidden`` (a
+        list) the residual stream after each layer, (B, T, d) fp16, is
+        appended to it."""
         idx = np.asarray(idx)
         B, T = idx.shape
         H, Hkv, hd = self.cfg["n_head"], self.cfg["n_kv_head"], self.hd
@@ -986,6 +1020,8 @@ class OracleModel:
             g, u = gu.chunk(2, dim=-1)
             sw = F.silu(g) * u
             x = x + self.qlin(sw, (i, "down"), L["wd"], self.q_dim).to(x.dtype)
+            if hidden is not None:
+                hidden.append(x.clone())
         cache.seen = new_seen
         xt = x if (return_all or T == 1) else x[:, -1:, :]
         xn = rmsnorm(xt, self.ln_f, self.eps)

@@ -246,21 +246,33 @@ def test_decode_attention_matches_reference_fixture(ax):
 
 @pytest.mark.parametrize("hd,Hq,Hkv,S,active", [(128, 32, 8, 4096, 4096), (64, 12, 12, 300, 257),
                                                  (128, 28, 4, 1000, 999), (64, 9, 3, 100, 1)])
-@pytest.mark.parametrize("kv", ["fp16", "fp8", "int4"])
+@pytest.mark.parametrize("kv", ["fp16", "fp8", "int4", "fp8_head", "int4_g32"])
 def test_decode_attention_vs_oracle(ax, hd, Hq, Hkv, S, active, kv):
+    """Split-K decode attention against the oracle's SDPA over the cache the
+    oracle's own quantizer produced: the reference formats (group 64) and the
+    BASELINE variants (one FP8 scale per (token, head); INT4 groups of 32)."""
     torch.manual_seed(hd + S)
     B = 2
     k = torch.randn(B, Hkv, S, hd, device="cuda").half()
     v = torch.randn(B, Hkv, S, hd, device="cuda").half()
     q = torch.randn(B, Hq, 1, hd, device="cuda")
-    if kv == "fp16":
+    kvt, group = {"fp16": ("fp16", 64), "fp8": ("fp8", 64), "int4": ("int4", 64), "fp8_head": ("fp8", hd),
+                  "int4_g32": ("int4", 32)}[kv]
+    if kvt == "fp16":
         kc, vc, ks, vs = k, v, None, None
-        kd, vd = k, v
+        kd, vd = k.float().cpu(), v.float().cpu()
     else:
-        kc, ks = ax.quantize_kv(k, kv)
-        vc, vs = ax.quantize_kv(v, kv)
-        kd, vd = ax.dequantize_kv(kc, ks, kv, hd), ax.dequantize_kv(vc, vs, kv, hd)
-    ref = O.attention_decode(q.cpu(), kd.float().cpu(), vd.float().cpu(), active)
+        qf, dqf = (O.quant_kv_fp8, O.dequant_kv_fp8) if kvt == "fp8" else (O.quant_kv_int4, O.dequant_kv_int4)
+        kq, ksc = qf(k.cpu().numpy(), group)
+        vq, vsc = qf(v.cpu().numpy(), group)
+        kc, ks, vc, vs = (torch.from_numpy(t).cuda() for t in (kq, ksc, vq, vsc))
+        # the device quantizer writes the same codes and scales
+        kc2, ks2 = ax.quantize_kv(k, kvt, group)
+        assert torch.equal(kc2, kc) and torch.equal(ks2, ks), kv
+        kd = torch.from_numpy(dqf(kq, ksc, group)).float()
+        vd = torch.from_numpy(dqf(vq, vsc, group)).float()
+        kv = kvt
+    ref = O.attention_decode(q.cpu(), kd, vd, active)
     for splits in (0, 1, 7):
         out = ax._attention(q, kc, vc, ks, vs, kv, active_len=active, num_splits=splits)
         assert _rel(out.view(B, Hq, hd).cpu(), ref.view(B, Hq, hd)) < REL_TOL

@@ -1,0 +1,185 @@
+"""The benchmarked configuration against the oracle, end to end.
+
+The bench times the persistent step kernel on the BASELINE formats: Q4
+group-128 symmetric weights, an FP8 KV cache with one fp16 scale per
+(token, head), head_dim 128 and GQA 4:1.  Here that kernel runs on the same
+seeded weights and the same teacher-forced tokens as the oracle's restatement
+of the reference forward (oracle.OracleModel, the reference's own
+``_forward_quantized_sequence`` rounding points over the BASELINE layouts),
+and is checked:
+
+* per layer: the residual stream after every layer, within rel 2e-3 of the
+  oracle's (north_star's layer-level bound; relative to the largest |h|);
+* logits within rel 2e-3;
+* the greedy token identical at every step, except where the oracle's own
+  top-2 margin is a near-tie.
+
+With a quantized cache the two sides must attend over the same cached codes
+for that bound to be meaningful: a last-ulp difference in one K value (fp32
+GEMV summation order) can move the group's amax, hence its fp16 scale, hence
+every FP8/INT4 code of the group.  So before each step the oracle's cache is
+copied into the device cache (teacher-forced cache), and only the new token's
+row is quantized by each side on its own.  The free-running variant (each
+side keeps its own cache) is checked too, at a looser bound, with the
+fraction of cached codes that differ reported.
+
+Cases: a 2-layer model with the 8B layer ratios scaled down (d 1024, 8/2
+heads of 128) for every KV format at batch 1 and 3, and a 2-layer slice of
+the real Llama-3-8B shape (d 4096, 32/8 heads, FFN 14336, vocab 128256).
+"""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from model_weights import make_weights
+
+pytestmark = pytest.mark.gpu
+
+MID = dict(n_layer=2, d_model=1024, n_head=8, n_kv_head=2, ffn=2048, vocab=4096, eps=1e-5, theta=10000.0,
+           block_size=2048)
+SLICE_8B = dict(n_layer=2, d_model=4096, n_head=32, n_kv_head=8, ffn=14336, vocab=128256, eps=1e-5, theta=500000.0,
+                block_size=2048)
+
+LAYER_TOL = 2e-3
+LOGIT_TOL = 2e-3
+# free-running quantized caches: codes of whole groups move with their scale
+FREE_TOL = {"fp16": 2e-3, "fp8": 1e-2, "int4": 1e-2}
+TIE = 2e-3
+
+
+def _rel(a, b):
+    a = torch.as_tensor(a).float().cpu()
+    b = torch.as_tensor(b).float().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp(min=1e-6))
+
+
+def _hdump(dec, B):
+    from axiomlm_b200 import _lib as L
+
+    off, nb = C.c_size_t(), C.c_size_t()
+    L.call("axb_runner_buffer", dec._h, 6, C.byref(off), C.byref(nb))
+    nl, d = dec.cfg["n_layer"], dec.cfg["d_model"]
+    return dec.workspace[off.value: off.value + nl * B * d * 2].view(torch.float16).view(nl, B, d).clone()
+
+
+def _sync_cache(dec, ocache, B, n):
+    """Copy the oracle's cached codes and scales for slots [0, n) into the
+    device cache."""
+    c = dec.cache
+    for layer in range(len(ocache.k)):
+        c.cache[layer, 0, :B, :, :n] = torch.from_numpy(ocache.k[layer][:B, :, :n]).to(c.cache.device)
+        c.cache[layer, 1, :B, :, :n] = torch.from_numpy(ocache.v[layer][:B, :, :n]).to(c.cache.device)
+        if c.scales is not None:
+            c.scales[layer, 0, :B, :, :n] = torch.from_numpy(ocache.ks[layer][:B, :, :n]).to(c.cache.device)
+            c.scales[layer, 1, :B, :, :n] = torch.from_numpy(ocache.vs[layer][:B, :, :n]).to(c.cache.device)
+
+
+def _run(cfg, kv, kv_group, B, prompt_len, steps, seed, sync_cache=True):
+    from axiomlm_b200 import _lib as L
+    from axiomlm_b200.model import QuantizedDecoder
+
+    W = make_weights(cfg, seed, ln_random=True)
+    hd = cfg["d_model"] // cfg["n_head"]
+    max_seq = 512
+    oracle = O.OracleModel(cfg, W, max_seq, weight_format="q4_g128_sym")
+    ocache = O.OracleCache(cfg["n_layer"], B, cfg["n_kv_head"], max_seq, hd, kv, kv_group=kv_group)
+    dec = QuantizedDecoder.from_weights(cfg, W, "q4_g128_sym", kv_dtype=kv, kv_group=kv_group, max_batch=B,
+                                        max_seq=max_seq, rope_len=max_seq)
+    assert dec.uses_step_kernel, "the benchmarked path is the persistent step kernel"
+    L.call("axb_runner_set_debug", dec._h, L.DEBUG_HDUMP, 0, 0)
+    g = torch.Generator().manual_seed(seed + 1)
+    prompt = torch.randint(0, cfg["vocab"], (B, prompt_len), generator=g)
+    forced = torch.randint(0, cfg["vocab"], (steps, B), generator=g)
+    oracle.forward(prompt.numpy(), ocache)
+    dec.prefill(prompt.cuda())
+    worst = {"layer": 0.0, "logits": 0.0}
+    errs = []
+    for i in range(steps):
+        tok = forced[i].view(B, 1)
+        if sync_cache:
+            _sync_cache(dec, ocache, B, prompt_len + i)
+        hidden = []
+        ref_logits, _ = oracle.forward(tok.numpy(), ocache, hidden=hidden)
+        lg = dec.decode_step(tok.cuda()).float().cpu()
+        assert dec.status() == 0, f"step {i}: runner status {dec.status()}"
+        hd_gpu = _hdump(dec, B)
+        for layer, h_ref in enumerate(hidden):
+            r = _rel(hd_gpu[layer], h_ref[:, 0, :])
+            worst["layer"] = max(worst["layer"], r)
+            errs.append(("h", i, layer, r))
+        r = _rel(lg[:, 0], ref_logits[:, 0])
+        worst["logits"] = max(worst["logits"], r)
+        errs.append(("logits", i, -1, r))
+        am = dec.argmax(B).long().cpu()
+        for b in range(B):
+            ref_row = ref_logits[b, 0].float()
+            ref_tok = int(torch.argmax(ref_row))
+            if int(am[b]) != ref_tok:
+                top = ref_row.topk(2).values
+                margin = float(top[0] - top[1]) / float(ref_row.abs().max())
+                assert margin < TIE, f"step {i} row {b}: ours {int(am[b])} oracle {ref_tok}, margin {margin:.2e}"
+    # the cached K/V codes: the fraction that differs from the oracle's cache
+    flips = 0.0
+    if kv != "fp16":
+        tot = dif = 0
+        for layer in range(cfg["n_layer"]):
+            gk = dec.cache.k_caches[layer][:B].cpu().numpy()
+            ok_ = ocache.k[layer][:B]
+            n = prompt_len + steps
+            tot += gk[:, :, :n].size
+            dif += int((gk[:, :, :n] != ok_[:, :, :n]).sum())
+        flips = dif / max(tot, 1)
+    dec.close()
+    print(f"{kv}/{kv_group} B={B} cache {'synced' if sync_cache else 'free'}: worst hidden rel "
+          f"{worst['layer']:.2e}, logits rel {worst['logits']:.2e}, K codes differing {flips:.2e}")
+    for name, i, layer, r in errs:
+        tol = (LAYER_TOL if name == "h" else LOGIT_TOL) if sync_cache else FREE_TOL[kv]
+        assert r < tol, f"step {i} {'layer %d' % layer if name == 'h' else 'logits'}: rel {r:.2e} (tol {tol})"
+    return worst
+
+
+@pytest.mark.parametrize("kv,kv_group", [("fp8", 128), ("int4", 32), ("fp16", 64), ("fp8", 64), ("int4", 64)])
+@pytest.mark.parametrize("B", [1, 3])
+def test_step_kernel_vs_oracle_mid(kv, kv_group, B):
+    _run(MID, kv, kv_group, B, prompt_len=40, steps=6, seed=3)
+
+
+@pytest.mark.parametrize("kv,kv_group", [("fp8", 128), ("int4", 32)])
+def test_step_kernel_vs_oracle_mid_free_cache(kv, kv_group):
+    _run(MID, kv, kv_group, 2, prompt_len=40, steps=6, seed=4, sync_cache=False)
+
+
+def test_step_kernel_vs_oracle_8b_slice():
+    _run(SLICE_8B, "fp8", 128, 1, prompt_len=24, steps=3, seed=8)
+
+
+def test_greedy_tokens_vs_oracle_mid():
+    """Free-running greedy decode: the step kernel's tokens equal the oracle's
+    for every step before the oracle's first near-tie (top-2 margin < 2e-3)."""
+    from axiomlm_b200.model import QuantizedDecoder
+
+    cfg, n_new, seed = MID, 48, 5
+    W = make_weights(cfg, seed, ln_random=True)
+    hd = cfg["d_model"] // cfg["n_head"]
+    oracle = O.OracleModel(cfg, W, 512, weight_format="q4_g128_sym")
+    prompt = torch.randint(0, cfg["vocab"], (1, 32), generator=torch.Generator().manual_seed(seed))
+    ocache = O.OracleCache(cfg["n_layer"], 1, cfg["n_kv_head"], 512, hd, "fp8", kv_group=hd)
+    logits, _ = oracle.forward(prompt.numpy(), ocache)
+    ref, margins = [], []
+    for _ in range(n_new):
+        row = logits[0, -1].float()
+        top = row.topk(2).values
+        margins.append(float(top[0] - top[1]) / float(row.abs().max()))
+        ref.append(int(torch.argmax(row)))
+        logits, _ = oracle.forward(np.array([[ref[-1]]]), ocache)
+    dec = QuantizedDecoder.from_weights(cfg, W, "q4_g128_sym", kv_dtype="fp8", kv_group=hd, max_seq=512,
+                                        rope_len=512)
+    toks = dec.generate_greedy(prompt, n_new)
+    dec.close()
+    first_tie = next((i for i, m in enumerate(margins) if m < TIE), n_new)
+    assert toks[:first_tie] == ref[:first_tie], (toks, ref, first_tie)
+    print(f"greedy tokens identical for {first_tie} of {n_new} steps (first near-tie at {first_tie})")
