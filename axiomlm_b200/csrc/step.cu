@@ -48,7 +48,7 @@ constexpr int kSlotS = kSL * 64;              // scale bytes of a slot (max: aff
 constexpr int kSlotB = kSlotW + kSlotS;       // 2304
 constexpr int kMaxSlots = 8;                  // ring slots per warp (upper bound; the plan picks 3-4)
 constexpr int kSBars = kSW * kMaxSlots * 8;   // ring mbarriers
-constexpr int kSMisc = 4096;                  // reduction scratch, attention mbarrier, flags, combine weights
+constexpr int kSMisc = 4096;                  // reduction scratch, attention mbarrier, flags, producer cursors
 constexpr int kSmemMax = 227 * 1024;
 constexpr int kMaxRepS = 8;                   // q heads per kv head (the 8 rows of the score MMA)
 constexpr int kXsLd = kStepMaxM;              // tokens per group row of the staged-x sums
@@ -57,10 +57,7 @@ constexpr uint32_t kDrainLimit = 1u << 22;    // polls for copies already in fli
 constexpr int kMiscRed = 0;      // float [kSW][kStepMaxM]
 constexpr int kMiscBar = 512;    // uint64 attention mbarrier
 constexpr int kMiscFlag = 576;   // int flags
-constexpr int kMiscLs = 640;     // float [kMaxRepS] combined softmax sums
-constexpr int kMiscCoef = 1024;  // float [kMaxRepS][kStepMaxSplits] split weights
 constexpr int kMiscCur = 3072;   // per-warp producer cursors (lane 0), kept out of registers
-static_assert(kMiscCoef + kMaxRepS * kStepMaxSplits * 4 <= kMiscCur, "misc region");
 static_assert(kSW * kStepMaxM * 4 <= kMiscBar, "reduction scratch");
 static_assert(kSlotB % 128 == 0 && kSlotW % 16 == 0, "bulk-copy alignment");
 static_assert(kSW <= kStepTraceW, "trace slots per phase");
@@ -556,7 +553,7 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
 // ------------------------------------------------------------------ staging
 // Embedding rows (dequant_q8_rows, quant.py:132-163) into xs; CTA 0 also
 // stores them into h (the residual stream).
-__device__ __noinline__ void stage_embed(const StepArgs& a, __half* xs, int stride) {
+__device__ __forceinline__ void stage_embed(const StepArgs& a, __half* xs, int stride) {
   const int K4 = a.d / 4;
   for (int i = threadIdx.x; i < a.B * K4; i += blockDim.x) {
     const int m = i / K4, k4 = i % K4;
@@ -584,7 +581,7 @@ __device__ __noinline__ void stage_embed(const StepArgs& a, __half* xs, int stri
 // fp16((x * rms) * w)) the rows are normalized in place.  With sums (SYM
 // weights) the fp32 per-group sums of the staged rows follow, reduced across
 // the G/8 consecutive lanes that hold a group.
-__device__ __noinline__ void stage_x(int B, int G, float eps, const __half* src, int K, const float* w, __half* xs,
+__device__ __forceinline__ void stage_x(int B, int G, float eps, const __half* src, int K, const float* w, __half* xs,
                                      int stride, float* xsum, bool sums, float* red) {
   const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, wid = tid >> 5;
   const int K8 = K / 8;
@@ -686,23 +683,25 @@ __device__ __forceinline__ int swz(int r, int b) {
 }
 
 struct AttnLayout {
-  int rb, bx, np, ng, kv, ksc, vsc, qh, qs, p, ps, ml, bytes;
+  int rb, bx, np, ng, kv, ksc, vsc, qh, qs, bytes;
 };
 
 // Working set of one attention item: the staged K and V planes (1 KB
-// aligned; the union start is aligned up at run time, hence the slack), their
-// fp16 scales, q as fp16 hi / lo parts (8 rows, the ones past n_rep zero;
-// rows HD/2 + 4 words apart), the probabilities (rows cap + 8 floats apart)
-// and the online-softmax state.  cap is a multiple of kBoxRows.
-__host__ __device__ inline AttnLayout attn_layout(int kv_type, int hd, int kv_group, int cap) {
+// aligned; the union start is aligned up at run time, hence the slack), which
+// after the last chunk hold the warps' partial results (per warp: m[8], l[8],
+// O[n_rep][hd + 4] in fp32), their rows' fp16 scales, and q as fp16 hi / lo parts
+// (8 rows, the ones past n_rep zero; rows hd/2 + 4 words apart).  cap is a
+// multiple of kBoxRows.
+__host__ __device__ inline AttnLayout attn_layout(int kv_type, int hd, int kv_group, int cap, int n_rep) {
   AttnLayout L;
   L.rb = kv_row_bytes(kv_type, hd);
   L.bx = kv_box_bytes(L.rb);
   L.np = L.rb / L.bx;
   L.ng = kv_type == AXB_KV_F16 ? 1 : hd / kv_group;
-  int off = 0;
-  L.kv = off;
-  off += 2 * cap * L.rb;
+  L.kv = 0;
+  const int stage = 2 * cap * L.rb;
+  const int merge = kSW * 16 * 4 + kSW * n_rep * (hd + 4) * 4;
+  int off = round_up_i(stage > merge ? stage : merge, 128);
   const int sb = round_up_i(cap * L.ng * 2, 16);
   L.ksc = off;
   off += sb;
@@ -711,11 +710,6 @@ __host__ __device__ inline AttnLayout attn_layout(int kv_type, int hd, int kv_gr
   L.qs = hd / 2 + 4;
   L.qh = off;
   off += 2 * 8 * L.qs * 4;
-  L.ps = cap + 8;
-  L.p = off;
-  off += kMaxRepS * L.ps * 4;
-  L.ml = off;
-  off += 32 * 4;  // m[8], l[8], alpha[8]
   L.bytes = round_up_i(off, 128) + 1024;  // + alignment slack
   return L;
 }
@@ -751,25 +745,25 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int x, i
 // are staged but never read; rows past the cache are filled with zeros), and
 // for quantized caches the rows' scales (rounded up to 8 tokens: 16-byte
 // copies; the cache length is a multiple of 8) as plain bulk copies.
-__device__ __forceinline__ void attn_copy(const StepLayer* ly, size_t head_base, const AttnLayout& Lo, bool quant,
-                                          int c0, int nt, int cap, char* gsm, uint64_t* bar) {
-  const int nbox = (nt + kBoxRows - 1) / kBoxRows, ng = Lo.ng;
+__device__ __noinline__ void attn_copy(const StepLayer* ly, size_t head_base, int np, int bx, int ng, int rb,
+                                       bool quant, int c0, int nt, int cap, char* kpl, char* ksc, char* vsc,
+                                       uint64_t* bar) {
+  const int nbox = (nt + kBoxRows - 1) / kBoxRows;
   const int nt8 = (nt + 7) & ~7;
   fence_proxy_async();
-  mbar_expect_tx(bar, 2u * Lo.np * nbox * kBoxRows * Lo.bx + (quant ? 2u * nt8 * ng * 2 : 0u));
-  char* kpl = gsm + Lo.kv;
-  char* vpl = kpl + (size_t)cap * Lo.rb;
+  mbar_expect_tx(bar, 2u * np * nbox * kBoxRows * bx + (quant ? 2u * nt8 * ng * 2 : 0u));
+  char* vpl = kpl + (size_t)cap * rb;
   const int y0 = (int)(head_base + c0);
   const uint64_t pol = l2_evict_first_policy();  // cached rows are read once per step
-  for (int pl = 0; pl < Lo.np; ++pl)
+  for (int pl = 0; pl < np; ++pl)
     for (int i = 0; i < nbox; ++i) {
-      const size_t off = (size_t)pl * cap * Lo.bx + (size_t)i * kBoxRows * Lo.bx;
-      tma_load_2d(kpl + off, ly->kmap, pl * Lo.bx, y0 + i * kBoxRows, bar, pol);
-      tma_load_2d(vpl + off, ly->vmap, pl * Lo.bx, y0 + i * kBoxRows, bar, pol);
+      const size_t off = (size_t)pl * cap * bx + (size_t)i * kBoxRows * bx;
+      tma_load_2d(kpl + off, ly->kmap, pl * bx, y0 + i * kBoxRows, bar, pol);
+      tma_load_2d(vpl + off, ly->vmap, pl * bx, y0 + i * kBoxRows, bar, pol);
     }
   if (quant) {
-    bulk_g2s(gsm + Lo.ksc, ly->ks + (head_base + c0) * ng, nt8 * ng * 2, bar);
-    bulk_g2s(gsm + Lo.vsc, ly->vs + (head_base + c0) * ng, nt8 * ng * 2, bar);
+    bulk_g2s(ksc, ly->ks + (head_base + c0) * ng, nt8 * ng * 2, bar);
+    bulk_g2s(vsc, ly->vs + (head_base + c0) * ng, nt8 * ng * 2, bar);
   }
 }
 
@@ -828,6 +822,78 @@ __device__ __forceinline__ uint32_t kv_col_pair_h2(const char* planes, int cap, 
   const uint32_t n1 = r1 >= 0 ? ((*kv_at<BX>(planes, cap, r1, e >> 1) >> sh) & 0xFu) ^ 8u : 8u;
   return h2_as_u32(__hsub2(u32_as_h2((n0 | (n1 << 16)) | 0x64006400u), __float2half2_rn(1032.f)));
 }
+// fp16 pair (row A, row B) of element 16 MS + 8 H + g of two staged rows,
+// given the rows' byte offsets in a plane (rb = r * BX) and swizzle keys
+// (key = (rb >> 7) & (BX / 16 - 1)): the element's 16-byte chunk is a
+// compile-time constant, so an access is one XOR, one add and the load.
+template <int KVT, int BX>
+__device__ __forceinline__ int kv_key(int rb) {
+  return (rb >> 7) & (BX / 16 - 1);
+}
+template <int KVT, int BX, int MS, int H>
+__device__ __forceinline__ uint32_t kv_rows_pair(const char* planes, int capBX, int rbA, int keyA, int rbB, int keyB,
+                                                 int g) {
+  if constexpr (KVT == AXB_KV_FP8) {  // byte 16 MS + 8 H + g
+    constexpr int byte0 = 16 * MS, pl = byte0 / BX, ch = (byte0 % BX) >> 4;
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(planes) + pl * capBX + 8 * H + g;
+    const uint32_t b0 = p[rbA + ((ch ^ keyA) << 4)], b1 = p[rbB + ((ch ^ keyB) << 4)];
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((uint16_t)(b0 | (b1 << 8)), __NV_E4M3);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
+  } else if constexpr (KVT == AXB_KV_F16) {  // bytes 32 MS + 16 H + 2 g, + 1
+    constexpr int byte0 = 32 * MS + 16 * H, pl = byte0 / BX, ch = (byte0 % BX) >> 4;
+    const char* p = planes + pl * capBX + 2 * g;
+    const uint32_t lo = *reinterpret_cast<const uint16_t*>(p + rbA + ((ch ^ keyA) << 4));
+    const uint32_t hi = *reinterpret_cast<const uint16_t*>(p + rbB + ((ch ^ keyB) << 4));
+    return lo | (hi << 16);
+  } else {  // INT4: byte 8 MS + 4 H + g / 2, nibble g & 1 (value (n ^ 8) - 8)
+    constexpr int byte0 = 8 * MS + 4 * H, pl = byte0 / BX, ch = (byte0 % BX) >> 4;
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(planes) + pl * capBX + (byte0 & 15) + (g >> 1);
+    const int sh = (g & 1) * 4;
+    const uint32_t n0 = ((p[rbA + ((ch ^ keyA) << 4)] >> sh) & 0xFu) ^ 8u;
+    const uint32_t n1 = ((p[rbB + ((ch ^ keyB) << 4)] >> sh) & 0xFu) ^ 8u;
+    return h2_as_u32(__hsub2(u32_as_h2((n0 | (n1 << 16)) | 0x64006400u), __float2half2_rn(1032.f)));
+  }
+}
+template <int KVT, int BX, int MS>
+__device__ __forceinline__ void kv_v_frag(const char* planes, int capBX, const int (&rb)[4], const int (&key)[4], int g,
+                                          uint32_t (&va)[4]) {
+  va[0] = kv_rows_pair<KVT, BX, MS, 0>(planes, capBX, rb[0], key[0], rb[1], key[1], g);
+  va[1] = kv_rows_pair<KVT, BX, MS, 1>(planes, capBX, rb[0], key[0], rb[1], key[1], g);
+  va[2] = kv_rows_pair<KVT, BX, MS, 0>(planes, capBX, rb[2], key[2], rb[3], key[3], g);
+  va[3] = kv_rows_pair<KVT, BX, MS, 1>(planes, capBX, rb[2], key[2], rb[3], key[3], g);
+}
+template <int KVT, int BX, int MS, int NMS>
+__device__ __forceinline__ void pv_steps(const char* vst, int capBX, const int (&rb)[4], const int (&key)[4],
+                                         const int (&rr)[4], const __half* vsc_s, int ng, int G, int lgG, int g,
+                                         uint32_t h01, uint32_t h23, uint32_t l01, uint32_t l23, float al0, float al1,
+                                         __half2& s01, __half2& s23, float (&o)[NMS][4]) {
+  if constexpr (MS < NMS) {
+    constexpr bool quant = KVT != AXB_KV_F16;
+    if (quant && (MS == 0 || ((16 * MS) & (G - 1)) == 0)) {  // a new V scale group (groups span 16 dims or more)
+      const int gi = (16 * MS) >> lgG;
+      s01 = __halves2half2(vsc_s[rr[0] * ng + gi], vsc_s[rr[1] * ng + gi]);
+      s23 = __halves2half2(vsc_s[rr[2] * ng + gi], vsc_s[rr[3] * ng + gi]);
+    }
+    uint32_t va[4];
+    kv_v_frag<KVT, BX, MS>(vst, capBX, rb, key, g, va);
+    if (quant) {
+      va[0] = h2_as_u32(__hmul2(u32_as_h2(va[0]), s01));
+      va[1] = h2_as_u32(__hmul2(u32_as_h2(va[1]), s01));
+      va[2] = h2_as_u32(__hmul2(u32_as_h2(va[2]), s23));
+      va[3] = h2_as_u32(__hmul2(u32_as_h2(va[3]), s23));
+    }
+    float t[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_16816(t, va, h01, h23, t);
+    mma_16816(t, va, l01, l23, t);
+    o[MS][0] = __fmaf_rn(o[MS][0], al0, t[0]);
+    o[MS][1] = __fmaf_rn(o[MS][1], al1, t[1]);
+    o[MS][2] = __fmaf_rn(o[MS][2], al0, t[2]);
+    o[MS][3] = __fmaf_rn(o[MS][3], al1, t[3]);
+    pv_steps<KVT, BX, MS + 1, NMS>(vst, capBX, rb, key, rr, vsc_s, ng, G, lgG, g, h01, h23, l01, l23, al0, al1, s01,
+                                   s23, o);
+  }
+}
+
 // fp32 pair -> fp16 (hi, lo) pairs with hi + lo = the value to about 22 bits
 __device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
   const __half2 h = __floats2half2_rn(x0, x1);
@@ -837,39 +903,42 @@ __device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint3
 }
 
 // One attention item (sequence b, kv head, split) on the whole CTA, on the
-// tensor cores: S = q K^T with q as fp16 hi + lo (K codes are exact in fp16;
-// the per-token scales apply to the fp32 result), then O += P V with the
-// per-token V scale folded into P (normalized by the chunk's largest scale)
-// and P as hi + lo.  Warp w owns output dims [8w, 8w + 8).  A split writes
-// its (O, m, l) partial; the head's last split to finish combines all of
-// them in split order and publishes the head.
+// tensor cores.  Warp w takes the 16-token blocks w, w + 16, ... of each
+// staged chunk and keeps its own online-softmax state for the (up to 8) q
+// heads of the kv head: S = q K^T for the block with q as fp16 hi + lo (a
+// quantized K row enters as the reference's dequantized fp16 values,
+// fp16(code * scale): one HMUL2 per pair, the product of two fp16 values
+// rounded once, so q . k sees the same K as the reference's SDPA); the block's
+// probabilities stay in registers (the score MMA's output fragment is the PV
+// MMA's input fragment); O += P V with P as hi + lo and V again as its
+// dequantized fp16 values.  After the last chunk the warps' states are merged
+// in warp order.  A split writes its (O, m, l) partial; the head's last split
+// to finish combines all of them in split order and publishes the head.
+// Every loop here runs once per block or per output: the code is kept small
+// (one copy of the chunk loop, a rolled score loop).
 template <int HD, int KVT>
-__device__ __noinline__ bool attn_item(const StepArgs& a, const StepLayer* ly, int layer, const AttnItem& it,
+__device__ __forceinline__ bool attn_item(const StepArgs& a, const StepLayer* ly, int layer, const AttnItem& it,
                                        int nsplit, bool prefetched, char* gsm, char* misc, uint32_t& uses,
                                        int* done_ctr, bool ok) {
   constexpr int BX = kv_box_bytes(KVT == AXB_KV_F16 ? HD * 2 : (KVT == AXB_KV_FP8 ? HD : HD / 2));
-  constexpr int DPL = HD / 32, KS = HD / 16;
+  constexpr int DPL = HD / 32, KS = HD / 16, OS = HD + 4;  // OS: row stride of the merged O
+  constexpr bool quant = KVT != AXB_KV_F16;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, c = lane & 3;
   const int cap = a.plan.attn_cap;
-  const AttnLayout Lo = attn_layout(KVT, HD, a.kv_group, cap);
+  const int n_rep = a.Hq / a.Hkv, hq0 = it.kvh * n_rep;
+  const AttnLayout Lo = attn_layout(KVT, HD, a.kv_group, cap, n_rep);
   const int ng = Lo.ng, G = KVT == AXB_KV_F16 ? HD : a.kv_group;
   const int lgG = __ffs(G) - 1;  // scale groups are powers of two
-  const int qs = Lo.qs, ps = Lo.ps;
-  constexpr bool quant = KVT != AXB_KV_F16;
-  const int n_rep = a.Hq / a.Hkv, hq0 = it.kvh * n_rep;
+  const int qs = Lo.qs;
   const int rpos = a.params[0], wpos = a.params[1];
   const size_t head_base = ((size_t)it.b * a.Hkv + it.kvh) * a.S;
   int* flag = reinterpret_cast<int*>(misc + kMiscFlag) + 1;
-  float* Ls = reinterpret_cast<float*>(misc + kMiscLs);
-  float* coef = reinterpret_cast<float*>(misc + kMiscCoef);
   uint64_t* bar = reinterpret_cast<uint64_t*>(misc + kMiscBar);
   char* kst = gsm + Lo.kv;  // K planes, then V planes
   char* vst = kst + (size_t)cap * Lo.rb;
-  __half* ksc_s = reinterpret_cast<__half*>(gsm + Lo.ksc);
-  __half* vsc_s = reinterpret_cast<__half*>(gsm + Lo.vsc);
+  const __half* ksc_s = reinterpret_cast<const __half*>(gsm + Lo.ksc);
+  const __half* vsc_s = reinterpret_cast<const __half*>(gsm + Lo.vsc);
   uint32_t* qh32 = reinterpret_cast<uint32_t*>(gsm + Lo.qh);  // [hi / lo][8 rows][qs]
-  float* p_s = reinterpret_cast<float*>(gsm + Lo.p);
-  float* ml_s = reinterpret_cast<float*>(gsm + Lo.ml);  // m[8] l[8] alpha[8]
 
   // ---- q with RoPE (fp32), as fp16 hi / lo rows; the new K/V row rotated, quantized and written
   const int qkv_dim = (a.Hq + 2 * a.Hkv) * HD;
@@ -890,15 +959,11 @@ __device__ __noinline__ bool attn_item(const StepArgs& a, const StepLayer* ly, i
     qh32[rr * qs + pr] = hi;
     qh32[(8 + rr) * qs + pr] = lo;
   }
-  if (tid < 8) {
-    ml_s[tid] = -INFINITY;
-    ml_s[8 + tid] = 0.f;
-  }
-  float nkv[DPL];
   uint2 ncode = make_uint2(0u, 0u);
   float nscale = 0.f;
   const bool covers = wpos >= it.t0 && wpos < it.t1;
   if (covers && w < 2) {
+    float nkv[DPL];
     const __half* src = row + (size_t)(a.Hq + (w == 0 ? 0 : a.Hkv) + it.kvh) * HD;
 #pragma unroll
     for (int e = 0; e < DPL; ++e) nkv[e] = __half2float(__ldcg(src + lane * DPL + e));
@@ -917,28 +982,14 @@ __device__ __noinline__ bool attn_item(const StepArgs& a, const StepLayer* ly, i
   }
   __syncthreads();
 
-  // this thread's q fragments (rows g, hi and lo parts) for every 16-wide k step
-  uint32_t qa[KS][4];
-#pragma unroll
-  for (int s = 0; s < KS; ++s) {
-    qa[s][0] = qh32[g * qs + 8 * s + c];
-    qa[s][1] = qh32[g * qs + 8 * s + c + 4];
-    qa[s][2] = qh32[(8 + g) * qs + 8 * s + c];
-    qa[s][3] = qh32[(8 + g) * qs + 8 * s + c + 4];
-  }
   const float sm_scale = 1.0f / sqrtf((float)HD);
-  const int d0 = w * 8;  // this warp's output dims (one V scale group: kv_group >= 8)
-  const bool pv_warp = d0 < HD;
-  const int vgrp = quant && pv_warp ? d0 >> lgG : 0;
-  float oacc[2] = {0.f, 0.f};
-  bool first = true;
-  // Chunks of cap cached tokens.  The first chunk runs outside any loop: the
-  // chunk body entered through a loop was measured to stall about 14 us at
-  // the loop's entry on every item; later chunks (long splits only) loop.
-  auto chunk = [&](const int c0) {
+  float m_run = -INFINITY, l_run = 0.f;  // head g (the same in the four lanes of a row)
+  float o[HD / 16][4];  // dims 16 ms + g (+ 8) x heads 2c, 2c + 1
+#pragma unroll
+  for (int ms = 0; ms < HD / 16; ++ms) o[ms][0] = o[ms][1] = o[ms][2] = o[ms][3] = 0.f;
+  for (int c0 = it.t0; c0 < it.t1; c0 += cap) {
     const int nt = min(cap, it.t1 - c0);
-    if (!(first && prefetched) && tid == 0) attn_copy(ly, head_base, Lo, quant, c0, nt, cap, gsm, bar);
-    first = false;
+    if (!(c0 == it.t0 && prefetched) && tid == 0) attn_copy(ly, head_base, Lo.np, Lo.bx, Lo.ng, Lo.rb, quant, c0, nt, cap, gsm + Lo.kv, gsm + Lo.ksc, gsm + Lo.vsc, bar);
     const bool got = mbar_wait(bar, uses & 1, a.mbar_limit);
     ++uses;
     if (__syncthreads_or(!got)) {  // one decision for the whole CTA
@@ -947,7 +998,7 @@ __device__ __noinline__ bool attn_item(const StepArgs& a, const StepLayer* ly, i
         mbar_wait(bar, (uses - 1) & 1, kDrainLimit);  // the copies in flight land before the CTA moves on
       }
       ok = false;
-      return;
+      break;
     }
     if (covers && w < 2 && wpos >= c0 && wpos < c0 + nt) {
       // the copy may have read the slot (codes and scale) before this step
@@ -960,117 +1011,118 @@ __device__ __noinline__ bool attn_item(const StepArgs& a, const StepLayer* ly, i
       else *dst = (uint8_t)ncode.x;
       const int lpg = G / DPL;
       if (quant && (lane % lpg) == 0)
-        (w == 0 ? ksc_s : vsc_s)[(size_t)(wpos - c0) * ng + (lane * DPL) / G] = __float2half_rn(nscale);
+        const_cast<__half*>(w == 0 ? ksc_s : vsc_s)[(size_t)(wpos - c0) * ng + (lane * DPL) / G] =
+            __float2half_rn(nscale);
     }
     __syncthreads();
-    // ---- scores: warp w takes 8-token blocks w, w + 16, ...  A quantized K
-    // row enters the MMA as the reference's dequantized fp16 values
-    // (fp16(code * scale), one HMUL2 per pair: the product of two fp16 values
-    // rounded once), so q . k sees the same K as the reference's SDPA.
-    for (int blk = w; blk * 8 < nt; blk += kSW) {
-      const int tok = min(blk * 8 + g, nt - 1);  // B-fragment column; columns past nt are discarded
-      const int t_a = blk * 8 + 2 * c, t_b = t_a + 1;  // this thread's C-fragment columns
-      float gacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
+    for (int tb = 16 * w; tb < nt; tb += 16 * kSW) {
+      // ---- scores of the block's two 8-token halves (B-fragment columns tb + g, tb + 8 + g;
+      // columns past the chunk read its last row and are masked below)
+      const int k0 = min(tb + g, nt - 1), k1 = min(tb + 8 + g, nt - 1);
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
       for (int s = 0; s < KS; ++s) {
-        uint32_t b0 = kv_pair_h2<KVT, BX>(kst, cap, tok, 16 * s + 2 * c);
-        uint32_t b1 = kv_pair_h2<KVT, BX>(kst, cap, tok, 16 * s + 2 * c + 8);
+        const uint32_t* qp = qh32 + g * qs + 8 * s + c;
+        const uint32_t ahi[4] = {qp[0], 0u, qp[4], 0u};
+        const uint32_t alo[4] = {qp[8 * qs], 0u, qp[8 * qs + 4], 0u};
+        const int e0 = 16 * s + 2 * c;
+        uint32_t b00 = kv_pair_h2<KVT, BX>(kst, cap, k0, e0), b01 = kv_pair_h2<KVT, BX>(kst, cap, k0, e0 + 8);
+        uint32_t b10 = kv_pair_h2<KVT, BX>(kst, cap, k1, e0), b11 = kv_pair_h2<KVT, BX>(kst, cap, k1, e0 + 8);
         if (quant) {
-          const __half2 sc2 = __half2half2(ksc_s[tok * ng + ((16 * s) >> lgG)]);
-          b0 = h2_as_u32(__hmul2(u32_as_h2(b0), sc2));
-          b1 = h2_as_u32(__hmul2(u32_as_h2(b1), sc2));
+          const int gi = (16 * s) >> lgG;
+          const __half2 sc0 = __half2half2(ksc_s[k0 * ng + gi]), sc1 = __half2half2(ksc_s[k1 * ng + gi]);
+          b00 = h2_as_u32(__hmul2(u32_as_h2(b00), sc0));
+          b01 = h2_as_u32(__hmul2(u32_as_h2(b01), sc0));
+          b10 = h2_as_u32(__hmul2(u32_as_h2(b10), sc1));
+          b11 = h2_as_u32(__hmul2(u32_as_h2(b11), sc1));
         }
-        const uint32_t ahi[4] = {qa[s][0], 0u, qa[s][1], 0u};
-        const uint32_t alo[4] = {qa[s][2], 0u, qa[s][3], 0u};
-        mma_16816(gacc, ahi, b0, b1, gacc);
-        mma_16816(gacc, alo, b0, b1, gacc);
+        mma_16816(s0, ahi, b00, b01, s0);
+        mma_16816(s0, alo, b00, b01, s0);
+        mma_16816(s1, ahi, b10, b11, s1);
+        mma_16816(s1, alo, b10, b11, s1);
       }
-      if (g < n_rep) {
-        if (t_a < nt) p_s[g * ps + t_a] = gacc[0] * sm_scale;
-        if (t_b < nt) p_s[g * ps + t_b] = gacc[1] * sm_scale;
-      }
-    }
-    __syncthreads();
-    // ---- online softmax over the chunk: warp r handles head r
-    if (w < n_rep) {
-      const int r = w;
-      float mx = -INFINITY;
-      for (int tk = lane; tk < nt; tk += 32) mx = fmaxf(mx, p_s[r * ps + tk]);
-      mx = warp_max(mx);
-      const float m_old = ml_s[r];
-      const float m_new = fmaxf(m_old, mx);
-      float sum = 0.f;
-      for (int tk = lane; tk < nt; tk += 32) {
-        const float e = __expf(p_s[r * ps + tk] - m_new);
-        p_s[r * ps + tk] = e;
-        sum += e;
-      }
-      sum = warp_sum(sum);
-      __syncwarp();
-      if (lane == 0) {
-        const float alpha = m_old == -INFINITY ? 0.f : __expf(m_old - m_new);
-        ml_s[r] = m_new;
-        ml_s[8 + r] = ml_s[8 + r] * alpha + sum;
-        ml_s[16 + r] = alpha;
-      }
-    }
-    __syncthreads();
-    // ---- O = alpha O + P V, a quantized V row again as the reference's
-    // dequantized fp16 values, P as fp16 hi + lo
-    if (pv_warp) {
-      const float alpha = g < n_rep ? ml_s[16 + g] : 0.f;
-      float tacc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int t0 = 0; t0 < nt; t0 += 16) {
-        float pv[4];
+      // ---- online softmax: this thread holds head g at tokens ta, ta + 1, tc, tc + 1
+      const int ta = tb + 2 * c, tc = ta + 8;
+      const float sv[4] = {ta < nt ? s0[0] * sm_scale : -INFINITY, ta + 1 < nt ? s0[1] * sm_scale : -INFINITY,
+                           tc < nt ? s1[0] * sm_scale : -INFINITY, tc + 1 < nt ? s1[1] * sm_scale : -INFINITY};
+      float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);  // finite: token tb is in the chunk
+      const float alpha = m_run == -INFINITY ? 0.f : __expf(m_run - m_new);
+      float p[4], ps = 0.f;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int t = t0 + 2 * c + (q & 1) + 8 * (q >> 1);
-          pv[q] = (g < n_rep && t < nt) ? p_s[g * ps + t] : 0.f;
-        }
-        uint32_t h01, l01, h23, l23;
-        split_h2(pv[0], pv[1], h01, l01);
-        split_h2(pv[2], pv[3], h23, l23);
-        const uint32_t ahi[4] = {h01, 0u, h23, 0u}, alo[4] = {l01, 0u, l23, 0u};
-        const int ta = t0 + 2 * c, tb = ta + 8;
-        const int r0 = ta < nt ? ta : -1, r1 = ta + 1 < nt ? ta + 1 : -1;
-        const int r2 = tb < nt ? tb : -1, r3 = tb + 1 < nt ? tb + 1 : -1;
-        const int d = d0 + g;  // B-fragment column
-        uint32_t b0 = kv_col_pair_h2<KVT, BX>(vst, cap, r0, r1, d);
-        uint32_t b1 = kv_col_pair_h2<KVT, BX>(vst, cap, r2, r3, d);
-        if (quant) {  // absent rows have zero codes; their scale is taken as 0 too
-          const __half z = __float2half_rn(0.f);
-          const __half2 s01 = __halves2half2(r0 >= 0 ? vsc_s[ta * ng + vgrp] : z, r1 >= 0 ? vsc_s[(ta + 1) * ng + vgrp] : z);
-          const __half2 s23 = __halves2half2(r2 >= 0 ? vsc_s[tb * ng + vgrp] : z, r3 >= 0 ? vsc_s[(tb + 1) * ng + vgrp] : z);
-          b0 = h2_as_u32(__hmul2(u32_as_h2(b0), s01));
-          b1 = h2_as_u32(__hmul2(u32_as_h2(b1), s23));
-        }
-        mma_16816(tacc, ahi, b0, b1, tacc);
-        mma_16816(tacc, alo, b0, b1, tacc);
+      for (int q = 0; q < 4; ++q) {
+        p[q] = sv[q] == -INFINITY ? 0.f : __expf(sv[q] - m_new);
+        ps += p[q];
       }
-      oacc[0] = __fmaf_rn(oacc[0], alpha, tacc[0]);
-      oacc[1] = __fmaf_rn(oacc[1], alpha, tacc[1]);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+      l_run = __fmaf_rn(l_run, alpha, ps);
+      m_run = m_new;
+      // ---- O^T = alpha O^T + V^T P^T (dims x heads): the A operand is V^T
+      // (16 dims x the block's 16 tokens), the B operand this thread's
+      // probabilities as the score MMA left them (head g at tokens ta, ta + 1
+      // and tc, tc + 1), as fp16 hi + lo
+      uint32_t h01, l01, h23, l23;
+      split_h2(p[0], p[1], h01, l01);
+      split_h2(p[2], p[3], h23, l23);
+      // the rescale of this thread's output heads 2c, 2c + 1 (rows 2c, 2c + 1 of the score layout)
+      const float al0 = __shfl_sync(0xffffffffu, alpha, 8 * c), al1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
+      // this thread's four tokens' rows, clamped into the chunk: an absent
+      // token has p = 0 and reads a finite cached row, so it adds exactly 0
+      const int rr[4] = {min(ta, nt - 1), min(ta + 1, nt - 1), min(tc, nt - 1), min(tc + 1, nt - 1)};
+      int rb[4], key[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        rb[q] = rr[q] * BX;
+        key[q] = kv_key<KVT, BX>(rb[q]);
+      }
+      __half2 s01, s23;
+      pv_steps<KVT, BX, 0, HD / 16>(vst, cap * BX, rb, key, rr, vsc_s, ng, G, lgG, g, h01, h23, l01, l23, al0, al1, s01,
+                                    s23, o);
     }
-    __syncthreads();  // staged rows and p_s are free for the next chunk
-  };
-  chunk(it.t0);
-  for (int c0 = it.t0 + cap; c0 < it.t1 && ok; c0 += cap) chunk(c0);
+    __syncthreads();  // the staged rows are free for the next chunk
+  }
   if (!ok) return false;
-  // ---- this thread's outputs: head g, dims d0 + 2c + {0, 1}
+
+  // ---- merge the warps' states in warp order (the staged rows are dead)
+  float* wm = reinterpret_cast<float*>(gsm + Lo.kv);  // [kSW][8] m, then [kSW][8] l
+  float* wo = wm + 2 * kSW * 8;                        // [kSW][n_rep][OS]
+  if (c == 0) {
+    wm[w * 8 + g] = m_run;
+    wm[kSW * 8 + w * 8 + g] = l_run;
+  }
+#pragma unroll
+  for (int ms = 0; ms < HD / 16; ++ms)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int h = 2 * c + (q & 1), dd = 16 * ms + g + 8 * (q >> 1);
+      if (h < n_rep) wo[((size_t)w * n_rep + h) * OS + dd] = o[ms][q];
+    }
+  __syncthreads();
   const size_t pidx = (size_t)it.b * a.Hq + hq0;
-  if (pv_warp && g < n_rep) {
-    const int d = d0 + 2 * c;
+  for (int i = tid; i < n_rep * HD; i += kSThreads) {
+    const int r = i / HD, e = i % HD;
+    float M = -INFINITY;
+#pragma unroll 4
+    for (int v = 0; v < kSW; ++v) M = fmaxf(M, wm[v * 8 + r]);
+    float Ls = 0.f, O = 0.f;
+#pragma unroll 4
+    for (int v = 0; v < kSW; ++v) {
+      const float mv = wm[v * 8 + r];
+      const float cw = mv == -INFINITY ? 0.f : __expf(mv - M);
+      Ls = __fmaf_rn(wm[kSW * 8 + v * 8 + r], cw, Ls);
+      O = __fmaf_rn(wo[((size_t)v * n_rep + r) * OS + e], cw, O);
+    }
     if (nsplit == 1) {
-      __half* op = a.attn + (pidx + g) * HD + d;
-      op[0] = __float2half_rn(__fdiv_rn(oacc[0], ml_s[8 + g]));
-      op[1] = __float2half_rn(__fdiv_rn(oacc[1], ml_s[8 + g]));
+      a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, Ls));
     } else {
-      *reinterpret_cast<float2*>(a.part_o + ((pidx + g) * kStepMaxSplits + it.split) * HD + d) =
-          make_float2(oacc[0], oacc[1]);
+      a.part_o[((pidx + r) * kStepMaxSplits + it.split) * HD + e] = O;
+      if (e == 0)
+        *reinterpret_cast<float2*>(a.part_ml + ((pidx + r) * kStepMaxSplits + it.split) * 2) = make_float2(M, Ls);
     }
   }
-  if (nsplit > 1 && tid < n_rep)
-    *reinterpret_cast<float2*>(a.part_ml + ((pidx + tid) * kStepMaxSplits + it.split) * 2) =
-        make_float2(ml_s[tid], ml_s[8 + tid]);
   __syncthreads();
   if (nsplit == 1) {
     if (tid == 0) red_release_add(done_ctr, 1);
@@ -1085,45 +1137,23 @@ __device__ __noinline__ bool attn_item(const StepArgs& a, const StepLayer* ly, i
   }
   __syncthreads();
   if (!*flag) return true;
-  // per-head split weights: each lane loads the (m, l) of splits lane and lane + 32
-  static_assert(kStepMaxSplits <= 64, "two splits per lane");
-  if (w < n_rep) {
-    const size_t hb = (pidx + w) * kStepMaxSplits;
-    float2 ml[2];
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int sp = lane + 32 * q;
-      ml[q] = sp < nsplit ? __ldcg(reinterpret_cast<const float2*>(a.part_ml) + hb + sp) : make_float2(-INFINITY, 0.f);
-    }
-    const float Mx = warp_max(fmaxf(ml[0].x, ml[1].x));
-    float Lsum = 0.f;
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int sp = lane + 32 * q;
-      if (sp < nsplit) {
-        const float cw = (ml[q].x == -INFINITY) ? 0.f : __expf(ml[q].x - Mx);
-        coef[w * kStepMaxSplits + sp] = cw;
-        Lsum += ml[q].y * cw;
-      }
-    }
-    Lsum = warp_sum(Lsum);
-    if (lane == 0) Ls[w] = Lsum;
-  }
-  __syncthreads();
-  // one output per thread, the splits summed in order (eight loads in flight)
   for (int i = tid; i < n_rep * HD; i += kSThreads) {
     const int r = i / HD, e = i % HD;
-    const float* po = a.part_o + (pidx + r) * kStepMaxSplits * HD + e;
-    float O = 0.f;
-    for (int s0 = 0; s0 < nsplit; s0 += 8) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = s0 + u < nsplit ? __ldcg(po + (size_t)(s0 + u) * HD) : 0.f;
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (s0 + u < nsplit) O = __fmaf_rn(v[u], coef[r * kStepMaxSplits + s0 + u], O);
+    const size_t hb = (pidx + r) * kStepMaxSplits;
+    const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + hb;
+    const float* po = a.part_o + hb * HD + e;
+    float M = -INFINITY;
+#pragma unroll 4
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(&ml[sp].x));
+    float Ls = 0.f, O = 0.f;
+#pragma unroll 4
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float2 v = __ldcg(ml + sp);
+      const float cw = v.x == -INFINITY ? 0.f : __expf(v.x - M);
+      Ls = __fmaf_rn(v.y, cw, Ls);
+      O = __fmaf_rn(__ldcg(po + (size_t)sp * HD), cw, O);
     }
-    a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, Ls[r]));
+    a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, Ls));
   }
   __syncthreads();
   if (tid == 0) red_release_add(done_ctr, 1);
@@ -1134,7 +1164,7 @@ __device__ __noinline__ bool attn_item(const StepArgs& a, const StepLayer* ly, i
 // are copied before the layer's QKV phase has finished (they do not depend on
 // it), then the CTA takes items blockIdx.x, + gridDim.x, ...
 template <int HD>
-__device__ __noinline__ bool attn_phase(const StepArgs& a, int l, char* uni, char* misc, uint32_t& uses, bool ok) {
+__device__ __forceinline__ bool attn_phase(const StepArgs& a, int l, char* uni, char* misc, uint32_t& uses, bool ok) {
   const int tid = threadIdx.x, C = gridDim.x;
   const StepLayer* ly = a.layers + l;
   int* dn = a.done + 1 + 5 * l;
@@ -1144,15 +1174,15 @@ __device__ __noinline__ bool attn_phase(const StepArgs& a, int l, char* uni, cha
   int nsplit, chunk;
   attn_split_plan(active, C / (a.B * a.Hkv), nsplit, chunk);
   const int n_items = a.B * a.Hkv * nsplit;
-  const AttnLayout Lo = attn_layout(a.kv_type, HD, a.kv_group, a.plan.attn_cap);
+  const AttnLayout Lo = attn_layout(a.kv_type, HD, a.kv_group, a.plan.attn_cap, a.Hq / a.Hkv);
   char* gsm = attn_base(uni);
   int item = blockIdx.x;
   const bool pre = ok && item < n_items;
   if (pre && tid == 0) {  // cached rows do not depend on this step's QKV
     const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
     const size_t hb = ((size_t)it.b * a.Hkv + it.kvh) * a.S;
-    attn_copy(ly, hb, Lo, a.kv_type != AXB_KV_F16, it.t0, min(a.plan.attn_cap, it.t1 - it.t0), a.plan.attn_cap,
-              gsm, bar);
+    attn_copy(ly, hb, Lo.np, Lo.bx, Lo.ng, Lo.rb, a.kv_type != AXB_KV_F16, it.t0, min(a.plan.attn_cap, it.t1 - it.t0),
+              a.plan.attn_cap, gsm + Lo.kv, gsm + Lo.ksc, gsm + Lo.vsc, bar);
   }
   ok = cta_wait(dn + 0, tiles_of(qkv_dim), a, ok);
   trace_mark(a, 1 + 10 * l + 2);
@@ -1374,8 +1404,6 @@ int step_kv_maps(void* maps_host, int L, void* const* kc, void* const* vc, int r
 StepPlan step_plan(int max_batch, int d, int F, int Hq, int Hkv, int hd, int kv_type, int kv_group, int group,
                    int max_seq) {
   (void)F;
-  (void)Hq;
-  (void)Hkv;
   (void)max_seq;
   StepPlan p = {0, 0, 0, 0};
   const int B = std::min(max_batch, kStepMaxM);
@@ -1386,7 +1414,7 @@ StepPlan step_plan(int max_batch, int d, int F, int Hq, int Hkv, int hd, int kv_
     if (avail < need) continue;
     int cap = 0;
     for (int c = 256; c >= kBoxRows; c -= kBoxRows)
-      if (attn_layout(kv_type, hd, kv_group, c).bytes <= avail) {
+      if (attn_layout(kv_type, hd, kv_group, c, Hq / Hkv).bytes <= avail) {
         cap = c;
         break;
       }
@@ -1447,7 +1475,7 @@ int step_launch(const StepArgs& a, cudaStream_t s) {
   AXB_CHECK_ARG(stage_bytes(a.B, a.d, a.group) <= a.plan.union_bytes,
                 "step: d_model %d too large for the staged activations at batch %d", a.d, a.B);
   AXB_CHECK_ARG(a.plan.attn_cap >= kBoxRows && a.plan.attn_cap % kBoxRows == 0 &&
-                    attn_layout(a.kv_type, a.hd, a.kv_group, a.plan.attn_cap).bytes <= a.plan.union_bytes,
+                    attn_layout(a.kv_type, a.hd, a.kv_group, a.plan.attn_cap, a.Hq / a.Hkv).bytes <= a.plan.union_bytes,
                 "step: attention chunk %d does not fit", a.plan.attn_cap);
   AXB_CHECK_ARG(a.spin_limit > 0 && a.mbar_limit > 0, "step: wait limits must be positive");
   AXB_CHECK_ARG(a.lm_w && a.lm_s && a.ln_f && a.emb_w && a.emb_s && a.rope && a.tokens && a.params && a.err && a.h &&
