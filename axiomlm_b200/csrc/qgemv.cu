@@ -305,8 +305,6 @@ struct GemmArgs {
   int xs_stride;  // smem row stride (halves); 0 = read x from global
   int xs_bytes;   // bytes of the staged-x region at the start of shared memory
   int early_trigger;  // release the dependent launch right after staging x
-  int xsum_off;       // byte offset of the per-(group, token) x sums in shared memory (SYM + XS)
-  int xsum_ld;        // tokens per group row of the x sums (>= M rounded to 8)
 };
 
 #ifndef AXB_GEMV_WARPS
@@ -443,23 +441,6 @@ __device__ void stage_x(const GemmArgs& a, __half* xs, float* red) {
   }
 }
 
-// Per-(group, token) sums of the staged fp16 x, in fp32: X[g][m].
-__device__ void stage_xsum(const GemmArgs& a, const __half* xs, float* X, int G) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int ngr = a.K / G;
-  for (int item = wid; item < ngr * a.M; item += nw) {
-    const int grp = item % ngr, m = item / ngr;
-    const __half* src = xs + (size_t)m * a.xs_stride + grp * G;
-    float v = 0.f;
-    for (int k = lane * 2; k < G; k += 64) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(src + k));
-      v += f.x + f.y;
-    }
-    v = warp_sum(v);
-    if (lane == 0) X[grp * a.xsum_ld + m] = v;
-  }
-}
-
 // chunk of tile t handled by warp w: global k-block range [lo, hi)
 __device__ __forceinline__ void warp_chunk(int upt, int GB, int U0, int U1, int t, int w, int& lo, int& hi) {
   const int s0 = max(U0, t * upt), s1 = min(U1, (t + 1) * upt);
@@ -516,10 +497,6 @@ __global__ void __launch_bounds__(kWarps * 32, (NT == 1 ? 28 : (NT == 2 ? 20 : 1
   if (XS) {
     stage_x(a, xs, nred);
     __syncthreads();
-    if (SYM) {
-      stage_xsum(a, xs, reinterpret_cast<float*>(smem + a.xsum_off), GB * 64);
-      __syncthreads();
-    }
   }
   if (a.early_trigger) pdl_trigger();
 
@@ -599,40 +576,7 @@ __global__ void __launch_bounds__(kWarps * 32, (NT == 1 ? 28 : (NT == 2 ? 20 : 1
             }
           }
           const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
-          if (SYM && XS) {
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              uint32_t af[4];
-              unpack_word_raw(words[jj], af);
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt)
-                mma_16816(tmp[jj % CH][nt], af, bf[nt][2 * jj], bf[nt][2 * jj + 1], tmp[jj % CH][nt]);
-            }
-            if (GB == 1 || (j & 1)) {  // group complete: remove the offsets, apply the scales
-              const uint32_t sp = reinterpret_cast<const uint32_t*>(sst)[(j / GB) * 8 + g];
-              const float2 sc = __half22float2(u32_as_h2(sp));
-              const int grp = (kbt + j) / GB;
-              const float* Xg = reinterpret_cast<const float*>(smem + a.xsum_off) + grp * a.xsum_ld;
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) {
-                const float2 xg = *reinterpret_cast<const float2*>(Xg + nt * 8 + 2 * t4);
-                float s4[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  float v = tmp[0][nt][q];
-#pragma unroll
-                  for (int c2 = 1; c2 < CH; ++c2) v += tmp[c2][nt][q];
-                  s4[q] = v;
-#pragma unroll
-                  for (int c2 = 0; c2 < CH; ++c2) tmp[c2][nt][q] = 0.f;
-                }
-                acc[nt][0] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg.x, s4[0]), acc[nt][0]);
-                acc[nt][1] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg.y, s4[1]), acc[nt][1]);
-                acc[nt][2] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[2], -72.f * xg.x), acc[nt][2]);
-                acc[nt][3] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[3], -72.f * xg.y), acc[nt][3]);
-              }
-            }
-          } else if (SYM) {
+          if (SYM) {
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
               uint32_t af[4];
@@ -900,11 +844,7 @@ int qgemm(const axb_qgemm_desc* d, cudaStream_t stream) {
   const bool xs = nt <= 4 && (d->norm_w != nullptr || xsb <= 32 * 1024) && xsb <= kXsLimit;
   AXB_CHECK_ARG(xs || !d->norm_w, "qgemm: fused RMSNorm needs M <= 32 and M*K*2 <= %zu bytes", kXsLimit);
   ga.xs_stride = xs ? d->K + 8 : 0;
-  ga.xsum_ld = (d->M + 7) / 8 * 8 + 8;
-  size_t xsum_b = 0;
-  if (xs && d->fmt == AXB_W_Q4T_SYM) xsum_b = round_up((size_t)(d->K / d->group) * ga.xsum_ld * 4, 128);
-  ga.xs_bytes = xs ? (int)(xsb + xsum_b) : 0;
-  ga.xsum_off = (int)xsb;
+  ga.xs_bytes = xs ? (int)xsb : 0;
   const size_t smem = (size_t)ga.xs_bytes + kRingBytes + red_bytes(nt);
   // persistent grid: every CTA resident at once (up to kCtasPerSm per SM, fewer
   // when the staged activations make CTAs larger) and owning >= 1 group

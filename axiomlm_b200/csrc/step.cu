@@ -51,7 +51,6 @@ constexpr int kSBars = kSW * kMaxSlots * 8;   // ring mbarriers
 constexpr int kSMisc = 4096;                  // reduction scratch, attention mbarrier, flags, producer cursors
 constexpr int kSmemMax = 227 * 1024;
 constexpr int kMaxRepS = 8;                   // q heads per kv head (the 8 rows of the score MMA)
-constexpr int kXsLd = kStepMaxM;              // tokens per group row of the staged-x sums
 constexpr uint32_t kDrainLimit = 1u << 22;    // polls for copies already in flight (not a runtime limit)
 // misc-region offsets
 constexpr int kMiscRed = 0;      // float [kSW][kStepMaxM]
@@ -63,11 +62,8 @@ static_assert(kSlotB % 128 == 0 && kSlotW % 16 == 0, "bulk-copy alignment");
 static_assert(kSW <= kStepTraceW, "trace slots per phase");
 
 __host__ __device__ constexpr int round_up_i(int v, int m) { return (v + m - 1) / m * m; }
-// the staged-x sums of a K-wide activation sit at the end of the union, the rows from its start
-__host__ __device__ constexpr int xsum_bytes(int K, int G) { return round_up_i((K / G) * kXsLd * 4, 128); }
-__host__ __device__ constexpr int stage_bytes(int M, int K, int G) {
-  return round_up_i(M * (K + 8) * 2, 128) + xsum_bytes(K, G);
-}
+// staged activations: M rows of K + 8 halves from the union's start
+__host__ __device__ constexpr int stage_bytes(int M, int K) { return round_up_i(M * (K + 8) * 2, 128); }
 
 // D = A * B with a zero accumulator (the first MMA of a chain)
 __device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -369,13 +365,14 @@ __device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const GPh& g, in
   }
 }
 
-// One GEMV phase for this warp.  x is staged in shared memory (XS: normalized
-// rows + per-group sums) or read from global memory (L2) one k-block ahead.
+// One GEMV phase for this warp.  x is staged in shared memory (XS: the rows,
+// normalized where the phase has an RMSNorm) or read from global memory (L2)
+// one k-block ahead.  The nibbles enter the MMA as exact fp16 (q - 8).
 // The k loop handles one quantization group (GB k-blocks) per iteration,
 // reading the weights straight from the ring slot.
 template <bool SYM, int GB, bool XS>
 __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, const __half* xs,
-                                           int xs_stride, const float* xsum, const __half* xg, int ldx, int gw,
+                                           int xs_stride, const __half* xg, int ldx, int gw,
                                            int Wt, int lane, bool ok, int* done_ctr) {
   const GPh g = gph(a, ph);
   const uint32_t We = eff_warps(g.U, Wt);
@@ -437,29 +434,17 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t af[4];
-            if (XS) unpack_word_raw(words[q], af);
-            else unpack_word<8>(words[q], af);
+            unpack_word<8>(words[q], af);
             if ((j % GB) == 0 && q < 2) mma_16816_z(c[q & 1], af, bf[2 * q], bf[2 * q + 1]);
             else mma_16816(c[q & 1], af, bf[2 * q], bf[2 * q + 1], c[q & 1]);
           }
-          if ((j % GB) == GB - 1) {  // group complete: apply the scales (XS: remove the magic offsets first)
+          if ((j % GB) == GB - 1) {  // group complete: apply the scales
             const uint32_t sp = reinterpret_cast<const uint32_t*>(ssl)[(j / GB) * 8 + gq];
             const float2 sc = __half22float2(u32_as_h2(sp));
-            float s4[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) s4[e] = c[0][e] + c[1][e];
-            if (XS) {
-              const float2 xg2 = *reinterpret_cast<const float2*>(xsum + ((kbt + j) / GB) * kXsLd + 2 * t4);
-              acc[0] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.x, s4[0]), acc[0]);
-              acc[1] = __fmaf_rn(sc.x, __fmaf_rn(-1032.f, xg2.y, s4[1]), acc[1]);
-              acc[2] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[2], -72.f * xg2.x), acc[2]);
-              acc[3] = __fmaf_rn(sc.y, __fmaf_rn(0.0625f, s4[3], -72.f * xg2.y), acc[3]);
-            } else {
-              acc[0] = __fmaf_rn(sc.x, s4[0], acc[0]);
-              acc[1] = __fmaf_rn(sc.x, s4[1], acc[1]);
-              acc[2] = __fmaf_rn(sc.y, s4[2], acc[2]);
-              acc[3] = __fmaf_rn(sc.y, s4[3], acc[3]);
-            }
+            acc[0] = __fmaf_rn(sc.x, c[0][0] + c[1][0], acc[0]);
+            acc[1] = __fmaf_rn(sc.x, c[0][1] + c[1][1], acc[1]);
+            acc[2] = __fmaf_rn(sc.y, c[0][2] + c[1][2], acc[2]);
+            acc[3] = __fmaf_rn(sc.y, c[0][3] + c[1][3], acc[3]);
           }
         } else {
           const uint2 sb = reinterpret_cast<const uint2*>(ssl)[j * 8 + gq];
@@ -578,11 +563,9 @@ __device__ __forceinline__ void stage_embed(const StepArgs& a, __half* xs, int s
 // Stage M rows of K activations into shared memory (row stride K + 8 halves):
 // from global memory (src), or the raw rows already in xs (src null).  With
 // an RMSNorm weight w (modules.py:30-43: rms = 1/sqrt(mean(x^2) + eps),
-// fp16((x * rms) * w)) the rows are normalized in place.  With sums (SYM
-// weights) the fp32 per-group sums of the staged rows follow, reduced across
-// the G/8 consecutive lanes that hold a group.
-__device__ __forceinline__ void stage_x(int B, int G, float eps, const __half* src, int K, const float* w, __half* xs,
-                                     int stride, float* xsum, bool sums, float* red) {
+// fp16((x * rms) * w)) the rows are normalized in place.
+__device__ __forceinline__ void stage_x(int B, float eps, const __half* src, int K, const float* w, __half* xs,
+                                        int stride, float* red) {
   const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, wid = tid >> 5;
   const int K8 = K / 8;
   // pass 1: copy (four 16-byte loads in flight per thread) + sums of squares
@@ -599,67 +582,41 @@ __device__ __forceinline__ void stage_x(int B, int G, float eps, const __half* s
       for (int u = 0; u < 4; ++u) {
         if (c0 + u * nth >= K8) continue;
         if (srow) drow[c0 + u * nth] = v[u];
-        if (w) {
-          const __half2* hh = reinterpret_cast<const __half2*>(&v[u]);
+        const __half2* hh = reinterpret_cast<const __half2*>(&v[u]);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f = __half22float2(hh[q]);
-            ss = __fmaf_rn(f.x, f.x, ss);
-            ss = __fmaf_rn(f.y, f.y, ss);
-          }
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(hh[q]);
+          ss = __fmaf_rn(f.x, f.x, ss);
+          ss = __fmaf_rn(f.y, f.y, ss);
         }
       }
     }
-    if (w) {
-      ss = warp_sum(ss);
-      if (lane == 0) red[wid * kStepMaxM + m] = ss;
-    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[wid * kStepMaxM + m] = ss;
   }
   __syncthreads();
-  if (!w && !sums) return;
-  // pass 2: normalize in place, then the group sums (whole-warp trip counts:
-  // a group's G/8 lanes are consecutive and never straddle a warp, K8 being a
-  // multiple of 16)
-  const int lpg = G / 8;
+  if (!w) return;
+  // pass 2: normalize in place
   for (int m = 0; m < B; ++m) {
-    float rms = 0.f;
-    if (w) {
-      float tot = 0.f;
-      for (int ww = 0; ww < (nth >> 5); ++ww) tot += red[ww * kStepMaxM + m];
-      rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), eps)));
-    }
+    float tot = 0.f;
+    for (int ww = 0; ww < (nth >> 5); ++ww) tot += red[ww * kStepMaxM + m];
+    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), eps)));
     uint4* drow = reinterpret_cast<uint4*>(xs + (size_t)m * stride);
-    for (int c0 = 0; c0 < K8; c0 += nth) {
-      const int cc = c0 + tid;
-      const bool act = cc < K8;
-      uint4 v = act ? drow[cc] : make_uint4(0, 0, 0, 0);
-      if (w && act) {
-        const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * cc);
-        const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * cc + 1);
-        const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        const __half2* hh = reinterpret_cast<const __half2*>(&v);
-        uint4 o;
-        __half2* oh = reinterpret_cast<__half2*>(&o);
+    for (int cc = tid; cc < K8; cc += nth) {
+      const uint4 v = drow[cc];
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * cc);
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * cc + 1);
+      const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      const __half2* hh = reinterpret_cast<const __half2*>(&v);
+      uint4 o;
+      __half2* oh = reinterpret_cast<__half2*>(&o);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 f = __half22float2(hh[q]);
-          oh[q] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, rms), ws[2 * q]),
-                                    __fmul_rn(__fmul_rn(f.y, rms), ws[2 * q + 1]));
-        }
-        drow[cc] = o;
-        v = o;
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __half22float2(hh[q]);
+        oh[q] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, rms), ws[2 * q]),
+                                  __fmul_rn(__fmul_rn(f.y, rms), ws[2 * q + 1]));
       }
-      if (sums) {
-        const __half2* hh = reinterpret_cast<const __half2*>(&v);
-        float gs = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 f = __half22float2(hh[q]);
-          gs += f.x + f.y;
-        }
-        for (int o = 1; o < lpg; o <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
-        if (act && (cc & (lpg - 1)) == 0) xsum[(cc / lpg) * kXsLd + m] = gs;
-      }
+      drow[cc] = o;
     }
   }
   __syncthreads();
@@ -1220,11 +1177,9 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   float* red = reinterpret_cast<float*>(misc + kMiscRed);
   int* s_last = reinterpret_cast<int*>(misc + kMiscFlag);
 
-  // staged activations: M rows of K + 8 halves from the union's start, their
-  // per-(group, token) sums at its end
+  // staged activations: M rows of K + 8 halves from the union's start
   __half* xs = reinterpret_cast<__half*>(uni);
   const int ub = a.plan.union_bytes;
-  auto xsum_of = [&](int K) { return reinterpret_cast<float*>(uni + ub - xsum_bytes(K, a.group)); };
   const int xs_stride = a.d + 8;
 
   Ring ring;
@@ -1305,7 +1260,7 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     }
     // ---- the GEMV: activations staged in shared memory when they fit (always
     // for the normalized inputs), else read from L2 one k-block ahead
-    const bool staged = stage_bytes(a.B, K, a.group) <= ub;
+    const bool staged = stage_bytes(a.B, K) <= ub;
     if (!staged && (nw != nullptr || src == nullptr)) {
       // normalized inputs (and layer 0's embedding rows) exist only as staged
       // rows; the host guarantees they fit, so this is a contract violation:
@@ -1314,11 +1269,11 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
       ok = false;
     }
     if (staged) {
-      if (ok) stage_x(a.B, a.group, a.eps, src, K, nw, xs, K + 8, xsum_of(K), SYM, red);
-      ok = gemv_phase<SYM, GB, true>(a, ph, ring, pc, xs, K + 8, xsum_of(K), nullptr, 0, gw, Wt, lane, ok,
+      if (ok) stage_x(a.B, a.eps, src, K, nw, xs, K + 8, red);
+      ok = gemv_phase<SYM, GB, true>(a, ph, ring, pc, xs, K + 8, nullptr, 0, gw, Wt, lane, ok,
                                      done_ctr);
     } else {
-      ok = gemv_phase<SYM, GB, false>(a, ph, ring, pc, nullptr, 0, nullptr, src, K, gw, Wt, lane, ok, done_ctr);
+      ok = gemv_phase<SYM, GB, false>(a, ph, ring, pc, nullptr, 0, src, K, gw, Wt, lane, ok, done_ctr);
     }
     if (lane == 0) trace_at(a, 4 + 10 * a.L + ph * kStepTraceW + wid);  // this warp's share done
     trace_mark(a, kind == 4 ? 2 + 10 * a.L : ts + (kind == 0 ? 1 : 2 * kind + 3));  // QKV, o, gate_up, down done
@@ -1407,7 +1362,7 @@ StepPlan step_plan(int max_batch, int d, int F, int Hq, int Hkv, int hd, int kv_
   (void)max_seq;
   StepPlan p = {0, 0, 0, 0};
   const int B = std::min(max_batch, kStepMaxM);
-  const int need = stage_bytes(B, d, group);  // normalized inputs are always staged
+  const int need = stage_bytes(B, d);  // normalized inputs are always staged
   for (int ns : {4, 3}) {
     const int fixed = kSW * ns * kSlotB + kSBars + kSMisc;
     const int avail = (kSmemMax - fixed) / 128 * 128;
@@ -1472,7 +1427,7 @@ int step_launch(const StepArgs& a, cudaStream_t s) {
   AXB_CHECK_ARG(a.plan.smem > 0 && a.plan.smem <= kSmemMax && a.plan.nslots >= 2 && a.plan.nslots <= kMaxSlots &&
                     a.plan.union_bytes % 128 == 0,
                 "step: no shared-memory plan for this model");
-  AXB_CHECK_ARG(stage_bytes(a.B, a.d, a.group) <= a.plan.union_bytes,
+  AXB_CHECK_ARG(stage_bytes(a.B, a.d) <= a.plan.union_bytes,
                 "step: d_model %d too large for the staged activations at batch %d", a.d, a.B);
   AXB_CHECK_ARG(a.plan.attn_cap >= kBoxRows && a.plan.attn_cap % kBoxRows == 0 &&
                     attn_layout(a.kv_type, a.hd, a.kv_group, a.plan.attn_cap, a.Hq / a.Hkv).bytes <= a.plan.union_bytes,

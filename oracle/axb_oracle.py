@@ -830,6 +830,11 @@ class OracleCache:
     v: list = field(default_factory=list)
     ks: list = field(default_factory=list)
     vs: list = field(default_factory=list)
+    # Test hook for quantized caches: {layer: (k codes, v codes, k scales,
+    # v scales)}, each (B, H, T, .), stored by write() in place of what it
+    # computed; what it computed goes to ``written`` for comparison.
+    pinned: dict | None = None
+    written: dict = field(default_factory=dict)
 
     def __post_init__(self):
         L, B, H, S, D = self.n_layer, self.max_batch, self.n_kv_head, self.max_seq, self.head_dim
@@ -864,6 +869,9 @@ class OracleCache:
         qf = quant_kv_fp8 if self.cache_dtype == "fp8" else quant_kv_int4
         kq, ks = qf(k16, self.kv_group)
         vq, vs = qf(v16, self.kv_group)
+        if self.pinned is not None and layer in self.pinned:
+            self.written[layer] = (kq, vq, ks, vs)
+            kq, vq, ks, vs = self.pinned[layer]
         self.k[layer][:B, :, slots] = kq
         self.v[layer][:B, :, slots] = vq
         self.ks[layer][:B, :, slots] = ks

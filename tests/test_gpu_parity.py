@@ -17,11 +17,17 @@ and is checked:
 With a quantized cache the two sides must attend over the same cached codes
 for that bound to be meaningful: a last-ulp difference in one K value (fp32
 GEMV summation order) can move the group's amax, hence its fp16 scale, hence
-every FP8/INT4 code of the group.  So before each step the oracle's cache is
-copied into the device cache (teacher-forced cache), and only the new token's
-row is quantized by each side on its own.  The free-running variant (each
-side keeps its own cache) is checked too, at a looser bound, with the
-fraction of cached codes that differ reported.
+every FP8/INT4 code of the group, and a single flipped FP8 code moves its
+element by 1/8.  So before each step the oracle's cache is copied into the
+device cache (teacher-forced cache); after the step the row the kernel
+quantized and wrote for the new token is read back and the oracle stores it in
+place of its own (``OracleCache.pinned``), so both sides attend over identical
+codes.  The kernel's new rows are themselves checked against the oracle's:
+scales within 4 fp16 ulps and at most 8% of codes different (a code differs
+only where a last-ulp input difference crosses a rounding boundary).  The
+free-running variant (each side keeps its own cache, nothing pinned) is
+checked too, at a looser bound, with the fraction of cached codes that differ
+reported.
 
 Cases: a 2-layer model with the 8B layer ratios scaled down (d 1024, 8/2
 heads of 128) for every KV format at batch 1 and 3, and a 2-layer slice of
@@ -49,6 +55,13 @@ LOGIT_TOL = 2e-3
 # free-running quantized caches: codes of whole groups move with their scale
 FREE_TOL = {"fp16": 2e-3, "fp8": 1e-2, "int4": 1e-2}
 TIE = 2e-3
+# The kernel's quantized new K/V rows against the oracle's quantization of its
+# own K/V: the inputs differ by the last ulps of the GEMV (fp32 summation
+# order) -- more after the first layer, whose input already differs -- so a
+# scale moves by a few fp16 ulps at most and a code flips only where its value
+# sits at a rounding boundary.
+NEW_ROW_SCALE = 2.0 ** -8
+NEW_ROW_FLIPS = 0.08
 
 
 def _rel(a, b):
@@ -78,6 +91,35 @@ def _sync_cache(dec, ocache, B, n):
             c.scales[layer, 1, :B, :, :n] = torch.from_numpy(ocache.vs[layer][:B, :, :n]).to(c.cache.device)
 
 
+def _device_rows(dec, n_layer, B, slot):
+    """The kernel's cache row at ``slot`` for every layer: {layer: (k, v, ks, vs)}, each (B, H, 1, .)."""
+    c = dec.cache
+    rows = {}
+    for layer in range(n_layer):
+        k = c.cache[layer, 0, :B, :, slot:slot + 1].cpu().numpy()
+        v = c.cache[layer, 1, :B, :, slot:slot + 1].cpu().numpy()
+        ks = c.scales[layer, 0, :B, :, slot:slot + 1].cpu().numpy()
+        vs = c.scales[layer, 1, :B, :, slot:slot + 1].cpu().numpy()
+        rows[layer] = (k, v, ks, vs)
+    return rows
+
+
+def _check_new_rows(ocache, rows):
+    """The kernel's quantized new rows against the oracle's own.  Returns the
+    largest scale difference (relative) and the fraction of codes that differ."""
+    tot = dif = 0
+    worst_scale = 0.0
+    for layer, (k, v, ks, vs) in rows.items():
+        ok_, ov, oks, ovs = ocache.written[layer]
+        for mine, ref in ((ks, oks), (vs, ovs)):
+            m, r = mine.astype(np.float32), ref.astype(np.float32)
+            worst_scale = max(worst_scale, float((np.abs(m - r) / np.maximum(np.abs(r), 1e-8)).max()))
+        for mine, ref in ((k, ok_), (v, ov)):
+            tot += mine.size
+            dif += int((mine != ref).sum())
+    return worst_scale, dif / max(tot, 1)
+
+
 def _run(cfg, kv, kv_group, B, prompt_len, steps, seed, sync_cache=True):
     from axiomlm_b200 import _lib as L
     from axiomlm_b200.model import QuantizedDecoder
@@ -96,17 +138,26 @@ def _run(cfg, kv, kv_group, B, prompt_len, steps, seed, sync_cache=True):
     forced = torch.randint(0, cfg["vocab"], (steps, B), generator=g)
     oracle.forward(prompt.numpy(), ocache)
     dec.prefill(prompt.cuda())
-    worst = {"layer": 0.0, "logits": 0.0}
+    worst = {"layer": 0.0, "logits": 0.0, "new_row_scale": 0.0, "new_row_flips": 0.0}
     errs = []
     for i in range(steps):
         tok = forced[i].view(B, 1)
         if sync_cache:
             _sync_cache(dec, ocache, B, prompt_len + i)
-        hidden = []
-        ref_logits, _ = oracle.forward(tok.numpy(), ocache, hidden=hidden)
         lg = dec.decode_step(tok.cuda()).float().cpu()
         assert dec.status() == 0, f"step {i}: runner status {dec.status()}"
         hd_gpu = _hdump(dec, B)
+        am = dec.argmax(B).long().cpu()
+        pin = sync_cache and kv != "fp16"
+        if pin:
+            ocache.pinned = _device_rows(dec, cfg["n_layer"], B, prompt_len + i)
+        hidden = []
+        ref_logits, _ = oracle.forward(tok.numpy(), ocache, hidden=hidden)
+        if pin:
+            sc, fl = _check_new_rows(ocache, ocache.pinned)
+            worst["new_row_scale"] = max(worst["new_row_scale"], sc)
+            worst["new_row_flips"] = max(worst["new_row_flips"], fl)
+            ocache.pinned = None
         for layer, h_ref in enumerate(hidden):
             r = _rel(hd_gpu[layer], h_ref[:, 0, :])
             worst["layer"] = max(worst["layer"], r)
@@ -114,7 +165,6 @@ def _run(cfg, kv, kv_group, B, prompt_len, steps, seed, sync_cache=True):
         r = _rel(lg[:, 0], ref_logits[:, 0])
         worst["logits"] = max(worst["logits"], r)
         errs.append(("logits", i, -1, r))
-        am = dec.argmax(B).long().cpu()
         for b in range(B):
             ref_row = ref_logits[b, 0].float()
             ref_tok = int(torch.argmax(ref_row))
@@ -135,7 +185,11 @@ def _run(cfg, kv, kv_group, B, prompt_len, steps, seed, sync_cache=True):
         flips = dif / max(tot, 1)
     dec.close()
     print(f"{kv}/{kv_group} B={B} cache {'synced' if sync_cache else 'free'}: worst hidden rel "
-          f"{worst['layer']:.2e}, logits rel {worst['logits']:.2e}, K codes differing {flips:.2e}")
+          f"{worst['layer']:.2e}, logits rel {worst['logits']:.2e}, new rows: scales rel {worst['new_row_scale']:.1e}, "
+          f"codes differing {worst['new_row_flips']:.2e}; cached K codes differing {flips:.2e}")
+    # the new rows: scales within NEW_ROW_SCALE, codes within NEW_ROW_FLIPS
+    assert worst["new_row_scale"] <= NEW_ROW_SCALE, worst
+    assert worst["new_row_flips"] <= NEW_ROW_FLIPS, worst
     for name, i, layer, r in errs:
         tol = (LAYER_TOL if name == "h" else LOGIT_TOL) if sync_cache else FREE_TOL[kv]
         assert r < tol, f"step {i} {'layer %d' % layer if name == 'h' else 'logits'}: rel {r:.2e} (tol {tol})"
