@@ -282,7 +282,7 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.st_layers = take((size_t)c.n_layer * sizeof(StepLayer));
   L.st_done = take((size_t)(2 + 5 * c.n_layer) * 4);
   L.st_tiles = take((size_t)L.st_max_tiles * 4);
-  L.st_part = take((size_t)num_sms() * step_num_warps() * 32 * 4 * sizeof(float));
+  L.st_part = take((size_t)num_sms() * step_num_warps() * 32 * 8 * sizeof(float));  // (value, flag) pairs
   L.st_po = take((size_t)sb * c.n_head * kStepMaxSplits * c.head_dim * sizeof(float));
   L.st_pml = take((size_t)sb * c.n_head * kStepMaxSplits * 2 * sizeof(float));
   L.st_acnt = take((size_t)sb * c.n_kv_head * 4);

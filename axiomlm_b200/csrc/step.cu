@@ -27,7 +27,9 @@
 //    wait is bounded (limits in StepArgs); one that runs out records
 //    AXB_ETIMEOUT and the grid winds down, waiting for its own copies first.
 //  * A tile split between warps is finished by the warp that owns its first
-//    unit, which sums the partials in warp order: results are deterministic.
+//    unit, which sums the partials in warp order (deterministic results).  The
+//    partials carry their own flags (value, flag pairs in one vector store),
+//    so no fence or counter sits between a partial and its reader.
 //  * Attention: one (sequence, kv head, split) item per CTA, on all 16 warps.
 //    The item's cached rows are bulk-copied before the QKV phase has finished;
 //    RoPE and the new K/V row's quantized write are fused.  The last split of a
@@ -52,6 +54,7 @@ constexpr int kSMisc = 4096;                  // reduction scratch, attention mb
 constexpr int kSmemMax = 227 * 1024;
 constexpr int kMaxRepS = 8;                   // q heads per kv head (the 8 rows of the score MMA)
 constexpr uint32_t kDrainLimit = 1u << 22;    // polls for copies already in flight (not a runtime limit)
+constexpr int kSPartBytes = kSW * 2 * 32 * 16;  // split-tile pieces: two per warp, 32 lanes x 4 floats
 // misc-region offsets
 constexpr int kMiscRed = 0;      // float [kSW][kStepMaxM]
 constexpr int kMiscBar = 512;    // uint64 attention mbarrier
@@ -93,6 +96,25 @@ __device__ __forceinline__ int atom_acq_rel_add(int* p, int v) {
   return old;
 }
 __device__ __forceinline__ int tiles_of(int n) { return (n + 15) >> 4; }
+
+// Split-tile partials travel with their flag: each 16-byte word holds two
+// (value, flag) pairs, written by one vector store and read by one vector
+// load, and a reader takes a word once both flags carry the current phase's
+// value (a per-launch epoch and the phase).  The data is its own signal: no
+// fence, counter or atomic on the way.
+__device__ __forceinline__ void st_ll(uint4* p, float v0, float v1, uint32_t fl) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(__float_as_uint(v0)), "r"(fl),
+               "r"(__float_as_uint(v1)), "r"(fl)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_ll(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
 
 // phase timeline stamp, only when a trace buffer is set: thread 0 of each CTA
 // (trace_mark), or the calling thread (trace_at)
@@ -141,11 +163,29 @@ struct GPh {
   uint32_t U;  // units (tile, group); U * warps < 2^32 for every supported shape (host-checked)
 };
 
-// Warps that share a GEMV: min(warps, units), so every participating warp
-// owns at least one unit (the arrival count of a split tile relies on it).
-// Virtual warp v owns units [v*U/We, (v+1)*U/We); v = wid * C + cta spreads a
-// small GEMV over all CTAs.
-__device__ __forceinline__ uint32_t eff_warps(uint32_t U, int Wt) { return U < (uint32_t)Wt ? U : (uint32_t)Wt; }
+// Units of a GEMV phase: CTA c owns the contiguous run [c U / C, (c + 1) U / C),
+// and inside it warp w of its min(16, units) participating warps an equal
+// contiguous share.  A tile is therefore split between warps of one CTA
+// (reduced through shared memory) and between at most a few CTAs (one
+// partial per CTA through global memory).  The producer cursor uses the same
+// ranges.
+struct URange {
+  uint32_t u0, u1;
+};
+__device__ __forceinline__ uint32_t cta_u0(uint32_t U, int c, int C) {
+  return (uint32_t)(((unsigned long long)U * (unsigned)c) / (unsigned)C);
+}
+__device__ __forceinline__ uint32_t cta_warps(uint32_t n) { return n < (uint32_t)kSW ? n : (uint32_t)kSW; }
+__device__ __forceinline__ URange warp_range(uint32_t U, int c, int C, int w) {
+  const uint32_t c0 = cta_u0(U, c, C), n = cta_u0(U, c + 1, C) - c0, we = cta_warps(n);
+  if ((uint32_t)w >= we) return {0u, 0u};
+  return {c0 + (uint32_t)(((unsigned long long)n * (unsigned)w) / we),
+          c0 + (uint32_t)(((unsigned long long)n * (unsigned)(w + 1)) / we)};
+}
+// the owner of unit u among n units split as above (warps of a CTA from c0, or CTAs from 0)
+__device__ __forceinline__ int owner_of(uint32_t u, uint32_t c0, uint32_t n, uint32_t parts) {
+  return (int)(((unsigned long long)(u - c0 + 1) * parts - 1) / n);
+}
 
 __device__ __forceinline__ GPh gph(const StepArgs& a, int ph) {
   GPh g;
@@ -192,14 +232,14 @@ __device__ __forceinline__ void cur_tile(Cur& c) {
 }
 
 template <int GB>
-__device__ __forceinline__ void cur_load(Cur& c, const StepArgs& a, int gw, int Wt) {
+__device__ __forceinline__ void cur_load(Cur& c, const StepArgs& a, int wid) {
   const GPh g = gph(a, c.ph);
   c.W = g.W;
   c.S = g.S;
   c.upt = g.upt;
-  const uint32_t We = eff_warps(g.U, Wt);
-  c.u0 = (uint32_t)gw < We ? (uint32_t)gw * g.U / We : 0u;
-  c.u1 = (uint32_t)gw < We ? ((uint32_t)gw + 1u) * g.U / We : 0u;
+  const URange r = warp_range(g.U, blockIdx.x, gridDim.x, wid);
+  c.u0 = r.u0;
+  c.u1 = r.u1;
   if (c.u0 >= c.u1) {
     c.t = 0;
     c.t_last = -1;
@@ -213,7 +253,7 @@ __device__ __forceinline__ void cur_load(Cur& c, const StepArgs& a, int gw, int 
 
 // advance past exhausted tiles / phases; false at the end of the step
 template <int GB>
-__device__ __forceinline__ bool cur_fix(Cur& c, const StepArgs& a, int gw, int Wt) {
+__device__ __forceinline__ bool cur_fix(Cur& c, const StepArgs& a, int wid) {
   while (c.kb >= c.kb_end) {
     if (c.t < c.t_last) {
       ++c.t;
@@ -222,7 +262,7 @@ __device__ __forceinline__ bool cur_fix(Cur& c, const StepArgs& a, int gw, int W
     }
     if (c.ph >= 4 * a.L) return false;
     ++c.ph;
-    cur_load<GB>(c, a, gw, Wt);
+    cur_load<GB>(c, a, wid);
   }
   return true;
 }
@@ -250,10 +290,10 @@ __device__ __forceinline__ void ring_consumed(Ring& r) {
 }
 
 template <bool SYM, int GB>
-__device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, const StepArgs& a, int gw, int Wt, int lane) {
+__device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, const StepArgs& a, int wid, int lane) {
   if (lane != 0) return;
   constexpr int UB = SYM ? 32 : 64;  // scale bytes per group
-  if (pc.kb >= pc.kb_end && !cur_fix<GB>(pc, a, gw, Wt)) return;
+  if (pc.kb >= pc.kb_end && !cur_fix<GB>(pc, a, wid)) return;
   const int st = r.ps;
   r.ps = st + 1 == r.n ? 0 : st + 1;
   const int nk = min(kSL, pc.kb_end - pc.kb);
@@ -278,15 +318,11 @@ __device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, const StepArgs& a, 
   ++r.inflight;
 }
 
-__device__ __forceinline__ int warp_of_unit(uint32_t u, uint32_t U, uint32_t We) {
-  return (int)(((u + 1) * We - 1) / U);
-}
-
 // Tile epilogue: token n = 2*t4 + e, rows tile*16 + g (+8).  The kind is
 // dispatched once, and the small loops stay rolled (the epilogue runs once
 // per tile; its code has to stay small, not fast).
 __device__ __forceinline__ void step_epilogue(const StepArgs& a, const GPh& g, int tile, float v00, float v01,
-                                           float v10, float v11, int lane) {
+                                           float v10, float v11, const uint2& hres, int lane) {
   const int gg = lane >> 2, t4 = lane & 3;
   const int r0 = tile * 16 + gg;
   const int M = a.B;
@@ -330,20 +366,34 @@ __device__ __forceinline__ void step_epilogue(const StepArgs& a, const GPh& g, i
     }
     return;
   }
-#pragma unroll 1
+  const __half2 hr01 = u32_as_h2(hres.x), hr23 = u32_as_h2(hres.y);
+  const float hrv[4] = {__low2float(hr01), __high2float(hr01), __low2float(hr23), __high2float(hr23)};
+#pragma unroll
   for (int q = 0; q < 4; ++q) {
     const int n = 2 * t4 + (q & 1), row = r0 + 8 * (q >> 1);
     if (n >= M || row >= g.N) continue;
     if (g.kind == 0) {
       a.qkv[(size_t)n * g.N + row] = __float2half_rn(acc[q]);
-    } else {  // residual add into h (fp16 GEMV output, fp16 sum)
-      __half* hp = a.h + (size_t)n * a.d + row;
-      const float old = __half2float(__ldcg(hp));
-      const __half nv = __float2half_rn(__fadd_rn(old, __half2float(__float2half_rn(acc[q]))));
-      *hp = nv;
+    } else {  // residual add into h (fp16 GEMV output, fp16 sum); h was read at the tile's start
+      const __half nv = __float2half_rn(__fadd_rn(hrv[q], __half2float(__float2half_rn(acc[q]))));
+      a.h[(size_t)n * a.d + row] = nv;
       if (g.kind == 3 && a.hdump) a.hdump[((size_t)g.layer * M + n) * a.d + row] = nv;
     }
   }
+}
+
+// The residual values a tile's epilogue adds to (o and down phases): read at
+// the tile's start so the load's latency hides under the tile's k loop.
+__device__ __forceinline__ uint2 residual_of(const StepArgs& a, const GPh& g, int tile, int lane) {
+  if (g.kind != 1 && g.kind != 3) return make_uint2(0u, 0u);
+  const int gg = lane >> 2, t4 = lane & 3, r0 = tile * 16 + gg;
+  __half h[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int n = 2 * t4 + (q & 1), row = r0 + 8 * (q >> 1);
+    h[q] = (n < a.B && row < g.N) ? __ldcg(a.h + (size_t)n * a.d + row) : __ushort_as_half((unsigned short)0);
+  }
+  return make_uint2(h2_as_u32(__halves2half2(h[0], h[1])), h2_as_u32(__halves2half2(h[2], h[3])));
 }
 
 // QKV bias (c_attn_bs) is folded in by the QKV tile finisher
@@ -369,18 +419,23 @@ __device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const GPh& g, in
 // normalized where the phase has an RMSNorm) or read from global memory (L2)
 // one k-block ahead.  The nibbles enter the MMA as exact fp16 (q - 8).
 // The k loop handles one quantization group (GB k-blocks) per iteration,
-// reading the weights straight from the ring slot.
+// reading the weights straight from the ring slot.  A tile that lies whole in
+// the warp's range is finished at once; a piece of a split tile goes to the
+// warp's shared-memory slot (0: its first tile, 1: its last), and after a CTA
+// barrier the CTA sums each split tile's pieces in warp order.  A tile that
+// began in an earlier CTA is published as this CTA's partial; the CTA that
+// owns a tile's first unit adds the later CTAs' partials in CTA order and
+// finishes it (deterministic sums).
 template <bool SYM, int GB, bool XS>
 __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, const __half* xs,
-                                           int xs_stride, const __half* xg, int ldx, int gw,
-                                           int Wt, int lane, bool ok, int* done_ctr) {
+                                           int xs_stride, const __half* xg, int ldx, float* spart, int wid,
+                                           int lane, bool ok, int* done_ctr, uint32_t fl) {
   const GPh g = gph(a, ph);
-  const uint32_t We = eff_warps(g.U, Wt);
-  if ((uint32_t)gw >= We || !ok) return ok;
-  const uint32_t u0 = (uint32_t)gw * g.U / We, u1 = ((uint32_t)gw + 1u) * g.U / We;
+  const URange wr = warp_range(g.U, blockIdx.x, gridDim.x, wid);
+  const uint32_t u0 = wr.u0, u1 = wr.u1;
   const int gq = lane >> 2, t4 = lane & 3;
   const int KB = g.K / 64;
-  const int t_first = (int)(u0 / g.upt), t_last = (int)((u1 - 1) / g.upt);
+  const int t_first = (int)(u0 / g.upt), t_last = u1 > u0 ? (int)((u1 - 1) / g.upt) : t_first - 1;
   const int nn = min(gq, a.B - 1);
   const uint4* xrow = reinterpret_cast<const uint4*>((XS ? xs + (size_t)nn * xs_stride : xg + (size_t)nn * ldx) +
                                                      16 * t4);
@@ -388,6 +443,8 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
   for (int t = t_first; t <= t_last && ok; ++t) {
     const int kb_lo = (int)max(u0, (uint32_t)(t * g.upt)) * GB;
     const int kb_hi = (int)min(u1, (uint32_t)((t + 1) * g.upt)) * GB;
+    const bool complete = (uint32_t)(t * g.upt) >= u0 && (uint32_t)((t + 1) * g.upt) <= u1;
+    const uint2 hres = complete ? residual_of(a, g, t, lane) : make_uint2(0u, 0u);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     // two accumulator chains (alternate fragment words) so consecutive MMAs
     // do not wait on each other; SYM restarts them per group, AFFINE (weights
@@ -473,7 +530,7 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
       }
       __syncwarp();
       ring_consumed(r);
-      ring_issue<SYM, GB>(r, pc, a, gw, Wt, lane);
+      ring_issue<SYM, GB>(r, pc, a, wid, lane);
       kb += nk;
     }
     if (!ok) break;
@@ -481,52 +538,76 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[e] = c[0][e] + c[1][e];
     }
-    const bool complete = (uint32_t)(t * g.upt) >= u0 && (uint32_t)((t + 1) * g.upt) <= u1;
     if (complete) {
       qkv_bias_fix(a, g, t, acc, lane);
-      step_epilogue(a, g, t, acc[0], acc[1], acc[2], acc[3], lane);
+      step_epilogue(a, g, t, acc[0], acc[1], acc[2], acc[3], hres, lane);
       ++finished;
       continue;
     }
-    // A split tile is finished by the warp that owns its first unit: the tile
-    // is always that warp's last one (had its range run past the tile, it
-    // would own the whole tile).  Every other warp of the tile has it as its
-    // first tile: it publishes a partial and moves on without waiting.
-    const int wf = warp_of_unit((uint32_t)(t * g.upt), g.U, We);
-    const int wl = warp_of_unit((uint32_t)((t + 1) * g.upt - 1), g.U, We);
-    if (gw != wf) {
-      float* p = a.partials + ((size_t)gw * 32 + lane) * 4;
-      *reinterpret_cast<float4*>(p) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      __syncwarp();
-      if (lane == 0) red_release_add(a.tile_cnt + t, 1);
-      continue;
-    }
-    int arrived = 1;
-    if (lane == 0) arrived = wait_ge(a.tile_cnt + t, wl - wf, a) ? 1 : 0;
-    if (__shfl_sync(0xffffffffu, arrived, 0) == 0) {
-      ok = false;
-      break;
-    }
-    // the partials in warp order, this warp's own first
-    float tot[4] = {acc[0], acc[1], acc[2], acc[3]};
-    for (int w0 = wf + 1; w0 <= wl; w0 += 4) {
-      float4 v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)  // independent loads, all in flight
-        if (w0 + u <= wl) v[u] = __ldcg(reinterpret_cast<const float4*>(a.partials + ((size_t)(w0 + u) * 32 + lane) * 4));
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (w0 + u > wl) continue;
-        tot[0] += v[u].x;
-        tot[1] += v[u].y;
-        tot[2] += v[u].z;
-        tot[3] += v[u].w;
+    *reinterpret_cast<float4*>(spart + ((wid * 2 + (t == t_first ? 0 : 1)) * 32 + lane) * 4) =
+        make_float4(acc[0], acc[1], acc[2], acc[3]);
+  }
+  // ---- the CTA's split tiles (tile ct0 + i is taken by warp i % 16)
+  ok = __syncthreads_and(ok) != 0;
+  const int C = gridDim.x, cta = blockIdx.x;
+  const uint32_t c0 = cta_u0(g.U, cta, C), n = cta_u0(g.U, cta + 1, C) - c0, we = cta_warps(n);
+  const uint32_t upt = (uint32_t)g.upt;
+  if (ok && n > 0) {
+    const int ct0 = (int)(c0 / upt), ct1 = (int)((c0 + n - 1) / upt);
+    for (int t = ct0 + wid; t <= ct1 && ok; t += kSW) {
+      const uint32_t ts = (uint32_t)t * upt, te = ts + upt;
+      const uint32_t p0 = max(c0, ts), p1 = min(c0 + n, te);
+      const int wa = owner_of(p0, c0, n, we), wb = owner_of(p1 - 1, c0, n, we);
+      const uint32_t ra0 = c0 + (uint32_t)(((unsigned long long)n * (unsigned)wa) / we);
+      const uint32_t ra1 = c0 + (uint32_t)(((unsigned long long)n * (unsigned)(wa + 1)) / we);
+      if (wa == wb && ra0 <= ts && ra1 >= te) continue;  // whole in one warp: already finished
+      const bool first_cta = p0 == ts;
+      const uint2 hres = first_cta ? residual_of(a, g, t, lane) : make_uint2(0u, 0u);
+      float tot[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int w0 = wa; w0 <= wb; ++w0) {
+        const uint32_t r0 = c0 + (uint32_t)(((unsigned long long)n * (unsigned)w0) / we);
+        const float4 v =
+            *reinterpret_cast<const float4*>(spart + ((w0 * 2 + ((uint32_t)t == r0 / upt ? 0 : 1)) * 32 + lane) * 4);
+        tot[0] += v.x;
+        tot[1] += v.y;
+        tot[2] += v.z;
+        tot[3] += v.w;
       }
+      if (!first_cta) {  // the tile began in an earlier CTA: publish this CTA's piece (one per CTA)
+        uint4* p = reinterpret_cast<uint4*>(a.partials) + ((size_t)cta * 32 + lane) * 2;
+        st_ll(p, tot[0], tot[1], fl);
+        st_ll(p + 1, tot[2], tot[3], fl);
+        continue;
+      }
+      if (p1 != te) {  // the tile runs on into later CTAs: their pieces, in CTA order
+        const int cb = owner_of(te - 1, 0u, g.U, (uint32_t)C);
+        for (int cc = cta + 1; cc <= cb; ++cc) {
+          if (cta_u0(g.U, cc + 1, C) == cta_u0(g.U, cc, C)) continue;  // a CTA with no units (U < C)
+          const uint4* p = reinterpret_cast<const uint4*>(a.partials) + ((size_t)cc * 32 + lane) * 2;
+          uint4 v0 = ld_ll(p), v1 = ld_ll(p + 1);
+          uint32_t it = 0;
+          while (v0.y != fl || v0.w != fl || v1.y != fl || v1.w != fl) {
+            if (++it >= a.spin_limit) break;
+            __nanosleep(32);
+            v0 = ld_ll(p);
+            v1 = ld_ll(p + 1);
+          }
+          if (__any_sync(0xffffffffu, it >= a.spin_limit)) {
+            if (lane == 0) raise_abort(a);
+            ok = false;
+            break;
+          }
+          tot[0] += __uint_as_float(v0.x);
+          tot[1] += __uint_as_float(v0.z);
+          tot[2] += __uint_as_float(v1.x);
+          tot[3] += __uint_as_float(v1.z);
+        }
+        if (!ok) break;
+      }
+      qkv_bias_fix(a, g, t, tot, lane);
+      step_epilogue(a, g, t, tot[0], tot[1], tot[2], tot[3], hres, lane);
+      ++finished;
     }
-    qkv_bias_fix(a, g, t, tot, lane);
-    step_epilogue(a, g, t, tot[0], tot[1], tot[2], tot[3], lane);
-    if (lane == 0) a.tile_cnt[t] = 0;  // published by the done counter's release below
-    ++finished;
   }
   if (finished) {
     __syncwarp();
@@ -1169,7 +1250,7 @@ template <bool SYM, int GB, int HD>
 __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   extern __shared__ __align__(128) char smem[];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const int C = gridDim.x, Wt = C * kSW, gw = wid * C + blockIdx.x;  // virtual warp id
+  const int C = gridDim.x;
   const int nsl = a.plan.nslots;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kSW * nsl * kSlotB);
   char* uni = smem + (size_t)kSW * nsl * kSlotB + kSBars;
@@ -1181,6 +1262,7 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   __half* xs = reinterpret_cast<__half*>(uni);
   const int ub = a.plan.union_bytes;
   const int xs_stride = a.d + 8;
+  float* spart = reinterpret_cast<float*>(uni + ub - kSPartBytes);  // split-tile pieces, at the union's end
 
   Ring ring;
   ring.buf = smem + (size_t)wid * nsl * kSlotB;
@@ -1196,13 +1278,17 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     if (wid == 0) mbar_init(reinterpret_cast<uint64_t*>(misc + kMiscBar), 1);
     fence_mbar_init();
     pc.ph = 0;
-    cur_load<GB>(pc, a, gw, Wt);
-    for (int s = 0; s < nsl; ++s) ring_issue<SYM, GB>(ring, pc, a, gw, Wt, lane);
+    cur_load<GB>(pc, a, wid);
+    for (int s = 0; s < nsl; ++s) ring_issue<SYM, GB>(ring, pc, a, wid, lane);
   }
   __syncthreads();
 
   bool ok = true;
   const int t_d = tiles_of(a.d);
+  // launch epoch (advanced by the step's last CTA): split-tile partials of
+  // GEMV phase ph carry the flag epoch * 512 + ph + 1 (never 0, the value of
+  // an unwritten slot)
+  const uint32_t epoch = *reinterpret_cast<volatile const uint32_t*>(a.exit_cnt + 2);
   uint32_t abar_uses = 0;  // completed phases of the attention mbarrier
 
   trace_mark(a, 0);
@@ -1260,7 +1346,7 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     }
     // ---- the GEMV: activations staged in shared memory when they fit (always
     // for the normalized inputs), else read from L2 one k-block ahead
-    const bool staged = stage_bytes(a.B, K) <= ub;
+    const bool staged = stage_bytes(a.B, K) + kSPartBytes <= ub;
     if (!staged && (nw != nullptr || src == nullptr)) {
       // normalized inputs (and layer 0's embedding rows) exist only as staged
       // rows; the host guarantees they fit, so this is a contract violation:
@@ -1270,10 +1356,11 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     }
     if (staged) {
       if (ok) stage_x(a.B, a.eps, src, K, nw, xs, K + 8, red);
-      ok = gemv_phase<SYM, GB, true>(a, ph, ring, pc, xs, K + 8, nullptr, 0, gw, Wt, lane, ok,
-                                     done_ctr);
+      ok = gemv_phase<SYM, GB, true>(a, ph, ring, pc, xs, K + 8, nullptr, 0, spart, wid, lane, ok, done_ctr,
+                                     epoch * 512u + (uint32_t)ph + 1u);
     } else {
-      ok = gemv_phase<SYM, GB, false>(a, ph, ring, pc, nullptr, 0, src, K, gw, Wt, lane, ok, done_ctr);
+      ok = gemv_phase<SYM, GB, false>(a, ph, ring, pc, nullptr, 0, src, K, spart, wid, lane, ok, done_ctr,
+                                      epoch * 512u + (uint32_t)ph + 1u);
     }
     if (lane == 0) trace_at(a, 4 + 10 * a.L + ph * kStepTraceW + wid);  // this warp's share done
     trace_mark(a, kind == 4 ? 2 + 10 * a.L : ts + (kind == 0 ? 1 : 2 * kind + 3));  // QKV, o, gate_up, down done
@@ -1311,6 +1398,7 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   }
   __syncthreads();
   if (tid == 0) {
+    a.exit_cnt[2] += 1;  // the next launch's epoch (every CTA read this one at its start)
     a.exit_cnt[1] = 0;
     a.exit_cnt[0] = 0;
   }
@@ -1362,7 +1450,7 @@ StepPlan step_plan(int max_batch, int d, int F, int Hq, int Hkv, int hd, int kv_
   (void)max_seq;
   StepPlan p = {0, 0, 0, 0};
   const int B = std::min(max_batch, kStepMaxM);
-  const int need = stage_bytes(B, d);  // normalized inputs are always staged
+  const int need = stage_bytes(B, d) + kSPartBytes;  // normalized inputs are always staged
   for (int ns : {4, 3}) {
     const int fixed = kSW * ns * kSlotB + kSBars + kSMisc;
     const int avail = (kSmemMax - fixed) / 128 * 128;
@@ -1427,12 +1515,13 @@ int step_launch(const StepArgs& a, cudaStream_t s) {
   AXB_CHECK_ARG(a.plan.smem > 0 && a.plan.smem <= kSmemMax && a.plan.nslots >= 2 && a.plan.nslots <= kMaxSlots &&
                     a.plan.union_bytes % 128 == 0,
                 "step: no shared-memory plan for this model");
-  AXB_CHECK_ARG(stage_bytes(a.B, a.d) <= a.plan.union_bytes,
+  AXB_CHECK_ARG(stage_bytes(a.B, a.d) + kSPartBytes <= a.plan.union_bytes,
                 "step: d_model %d too large for the staged activations at batch %d", a.d, a.B);
   AXB_CHECK_ARG(a.plan.attn_cap >= kBoxRows && a.plan.attn_cap % kBoxRows == 0 &&
                     attn_layout(a.kv_type, a.hd, a.kv_group, a.plan.attn_cap, a.Hq / a.Hkv).bytes <= a.plan.union_bytes,
                 "step: attention chunk %d does not fit", a.plan.attn_cap);
   AXB_CHECK_ARG(a.spin_limit > 0 && a.mbar_limit > 0, "step: wait limits must be positive");
+  AXB_CHECK_ARG(a.L >= 0 && 4 * a.L + 1 < 511, "step: %d layers (the phase flags allow 127)", a.L);
   AXB_CHECK_ARG(a.lm_w && a.lm_s && a.ln_f && a.emb_w && a.emb_s && a.rope && a.tokens && a.params && a.err && a.h &&
                     a.logits && a.amax && a.done && a.tile_cnt && a.partials && a.keys && a.exit_cnt &&
                     (a.L == 0 || (a.layers && a.qkv && a.attn && a.sw && a.part_o && a.part_ml && a.attn_cnt)),

@@ -59,12 +59,12 @@ struct StepArgs {
   // scratch (zeroed once; every counter returns to zero by the end of a step)
   int* done;          // per-phase completion counters
   int* tile_cnt;      // per-tile arrival counters
-  float* partials;    // per virtual warp: 32 lanes x 4 floats
+  float* partials;    // per virtual warp: 32 lanes x 4 (value, flag) pairs
   float* part_o;      // attention split partials (B, Hq, kStepMaxSplits, hd)
   float* part_ml;     // (B, Hq, kStepMaxSplits, 2)
   int* attn_cnt;      // (B, Hkv) split arrivals, grow through a step
   unsigned long long* keys;  // per-token argmax keys
-  int* exit_cnt;
+  int* exit_cnt;      // [0] CTAs done, [1] abort flag, [2] launch epoch
   int max_tiles;      // size of tile_cnt
   StepPlan plan;
   // bounded waits: polls of a cross-CTA counter and of a copy's mbarrier
