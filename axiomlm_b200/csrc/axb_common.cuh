@@ -159,6 +159,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_
         : "r"(smem_u32(bar)), "r"(phase)
         : "memory");
     if (done) return true;
+    __nanosleep(64);  // a waiting warp yields its issue slots to the SM's working warps
   }
   return false;
 }

@@ -44,11 +44,10 @@ namespace axb {
 
 constexpr int kSW = 16;  // warps per CTA (one CTA per SM)
 constexpr int kSThreads = kSW * 32;
-constexpr int kSL = 4;                        // k-blocks (512 B of weights each) per ring slot
-constexpr int kSlotW = kSL * 512;             // weight bytes of a slot
-constexpr int kSlotS = kSL * 64;              // scale bytes of a slot (max: affine, one group per k-block)
-constexpr int kSlotB = kSlotW + kSlotS;       // 2304
-constexpr int kMaxSlots = 8;                  // ring slots per warp (upper bound; the plan picks 3-4)
+// A ring slot holds plan.slot_kb k-blocks (512 B of weights each) and their
+// scales (at most 64 B per k-block: affine, one group per k-block).
+constexpr int kSlotPerKb = 512 + 64;
+constexpr int kMaxSlots = 8;                  // ring slots per warp (upper bound; the plan picks 2-3)
 constexpr int kSBars = kSW * kMaxSlots * 8;   // ring mbarriers
 constexpr int kSMisc = 4096;                  // reduction scratch, attention mbarrier, flags, producer cursors
 constexpr int kSmemMax = 227 * 1024;
@@ -61,7 +60,7 @@ constexpr int kMiscBar = 512;    // uint64 attention mbarrier
 constexpr int kMiscFlag = 576;   // int flags
 constexpr int kMiscCur = 3072;   // per-warp producer cursors (lane 0), kept out of registers
 static_assert(kSW * kStepMaxM * 4 <= kMiscBar, "reduction scratch");
-static_assert(kSlotB % 128 == 0 && kSlotW % 16 == 0, "bulk-copy alignment");
+static_assert((4 * kSlotPerKb) % 128 == 0, "bulk-copy alignment of every slot size (a multiple of 4 k-blocks)");
 static_assert(kSW <= kStepTraceW, "trace slots per phase");
 
 __host__ __device__ constexpr int round_up_i(int v, int m) { return (v + m - 1) / m * m; }
@@ -296,20 +295,21 @@ __device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, const StepArgs& a, 
   if (pc.kb >= pc.kb_end && !cur_fix<GB>(pc, a, wid)) return;
   const int st = r.ps;
   r.ps = st + 1 == r.n ? 0 : st + 1;
-  const int nk = min(kSL, pc.kb_end - pc.kb);
+  const int sl = a.plan.slot_kb;
+  const int nk = min(sl, pc.kb_end - pc.kb);
   const uint32_t bw = nk * 512, bs = (nk / GB) * UB;
-  char* slot = r.buf + (size_t)st * kSlotB;
+  char* slot = r.buf + (size_t)st * sl * kSlotPerKb;
   const uint64_t pol = l2_evict_first_policy();
   mbar_expect_tx(r.bars + st, bw + bs);
   bulk_g2s_hint(slot, pc.W + (size_t)pc.kb * 512, bw, r.bars + st, pol);
-  bulk_g2s_hint(slot + kSlotW, pc.S + (size_t)(pc.kb / GB) * UB, bs, r.bars + st, pol);
+  bulk_g2s_hint(slot + sl * 512, pc.S + (size_t)(pc.kb / GB) * UB, bs, r.bars + st, pol);
   // keep the stream further ahead in flight through L2: the k-blocks a.pref_kb
   // past this slot, while they stay in this warp's range of the phase (the
   // range is one contiguous run of tiles)
   if (a.pref_kb > 0) {
     const int kp = pc.kb + a.pref_kb, kend = (int)pc.u1 * GB;
     if (kp < kend) {
-      const int np = min(kSL, kend - kp);
+      const int np = min(sl, kend - kp);
       bulk_prefetch_l2(pc.W + (size_t)kp * 512, np * 512);
       if (np >= GB) bulk_prefetch_l2(pc.S + (size_t)(kp / GB) * UB, (np / GB) * UB);
     }
@@ -466,9 +466,10 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
         ok = false;
         break;
       }
-      const int nk = min(kSL, kb_hi - kb);
-      const uint4* wsl = reinterpret_cast<const uint4*>(r.buf + (size_t)st * kSlotB) + lane;
-      const char* ssl = r.buf + (size_t)st * kSlotB + kSlotW;
+      const int sl = a.plan.slot_kb;
+      const int nk = min(sl, kb_hi - kb);
+      const uint4* wsl = reinterpret_cast<const uint4*>(r.buf + (size_t)st * sl * kSlotPerKb) + lane;
+      const char* ssl = r.buf + (size_t)st * sl * kSlotPerKb + sl * 512;
       const int kbt = kb - t * KB;
       // one k-block of the slot; a group's scales are applied after its last k-block
       auto kblock = [&](const int j) {
@@ -1251,9 +1252,9 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   extern __shared__ __align__(128) char smem[];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int C = gridDim.x;
-  const int nsl = a.plan.nslots;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kSW * nsl * kSlotB);
-  char* uni = smem + (size_t)kSW * nsl * kSlotB + kSBars;
+  const int nsl = a.plan.nslots, slot_b = a.plan.slot_kb * kSlotPerKb;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kSW * nsl * slot_b);
+  char* uni = smem + (size_t)kSW * nsl * slot_b + kSBars;
   char* misc = uni + a.plan.union_bytes;
   float* red = reinterpret_cast<float*>(misc + kMiscRed);
   int* s_last = reinterpret_cast<int*>(misc + kMiscFlag);
@@ -1265,7 +1266,7 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   float* spart = reinterpret_cast<float*>(uni + ub - kSPartBytes);  // split-tile pieces, at the union's end
 
   Ring ring;
-  ring.buf = smem + (size_t)wid * nsl * kSlotB;
+  ring.buf = smem + (size_t)wid * nsl * slot_b;
   ring.bars = bars + wid * kMaxSlots;
   ring.n = nsl;
   ring.cs = 0;
@@ -1448,11 +1449,15 @@ StepPlan step_plan(int max_batch, int d, int F, int Hq, int Hkv, int hd, int kv_
                    int max_seq) {
   (void)F;
   (void)max_seq;
-  StepPlan p = {0, 0, 0, 0};
+  StepPlan p = {0, 0, 0, 0, 0};
   const int B = std::min(max_batch, kStepMaxM);
   const int need = stage_bytes(B, d) + kSPartBytes;  // normalized inputs are always staged
-  for (int ns : {4, 3}) {
-    const int fixed = kSW * ns * kSlotB + kSBars + kSMisc;
+  // ring shapes, best first: 2 slots of 8 k-blocks, then 3 or 2 slots of 4
+  // (the same bytes in flight in fewer, larger copies, as long as the union fits)
+  const int shapes[3][2] = {{8, 2}, {4, 3}, {4, 2}};
+  for (const auto& sh : shapes) {
+    const int sl = sh[0], ns = sh[1];
+    const int fixed = kSW * ns * sl * kSlotPerKb + kSBars + kSMisc;
     const int avail = (kSmemMax - fixed) / 128 * 128;
     if (avail < need) continue;
     int cap = 0;
@@ -1463,6 +1468,7 @@ StepPlan step_plan(int max_batch, int d, int F, int Hq, int Hkv, int hd, int kv_
       }
     if (cap == 0) continue;
     p.nslots = ns;
+    p.slot_kb = sl;
     p.union_bytes = avail;
     p.attn_cap = cap;
     p.smem = fixed + avail;
@@ -1513,6 +1519,7 @@ int step_launch(const StepArgs& a, cudaStream_t s) {
   AXB_CHECK_ARG((a.hd == 64 || a.hd == 128) && a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kMaxRepS,
                 "step: bad heads (%d, %d, %d)", a.Hq, a.Hkv, a.hd);
   AXB_CHECK_ARG(a.plan.smem > 0 && a.plan.smem <= kSmemMax && a.plan.nslots >= 2 && a.plan.nslots <= kMaxSlots &&
+                    a.plan.slot_kb >= 4 && a.plan.slot_kb % 4 == 0 &&
                     a.plan.union_bytes % 128 == 0,
                 "step: no shared-memory plan for this model");
   AXB_CHECK_ARG(stage_bytes(a.B, a.d) + kSPartBytes <= a.plan.union_bytes,

@@ -27,6 +27,7 @@ struct StepLayer {
 // fixed scratch area.
 struct StepPlan {
   int nslots;       // ring slots per warp
+  int slot_kb;      // k-blocks (512 B of weights) per slot
   int union_bytes;  // staged activations / attention working set
   int attn_cap;     // cached tokens per attention sub-chunk
   int smem;         // dynamic shared memory of the launch
