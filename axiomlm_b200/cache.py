@@ -6,8 +6,9 @@ Same constructor, buffers and bookkeeping fields as the reference
 ``total_seen_tokens``, ``layer_seq_lens``, ``ring_buffer``), plus one B200
 extension: ``kv_group`` (elements per fp16 scale; 64 = the reference,
 ``head_dim`` = one scale per (token, head), 32 = group-32 INT4).
-The cache is written by the CUDA decode runner; ``compact_tree_path`` runs
-the compaction kernel.
+The cache is written by the CUDA decode runner, or through ``update`` (the
+reference's per-layer write that returns the active window);
+``compact_tree_path`` runs the compaction kernel.
 """
 
 from __future__ import annotations
@@ -80,6 +81,56 @@ class StaticKVCache:
         active = min(new_seen, self.max_seq_len)
         self.total_seen_tokens[:] = [new_seen] * self.n_layer
         self.layer_seq_lens[:] = [active] * self.n_layer
+
+    def update(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """paged_cache.py:218-361: write K and V of shape (B, n_kv_head, T,
+        head_dim) at the layer's next positions and return the active window.
+
+        Positions follow the reference: a monotonic write while the tokens fit
+        (and the cache is not a ring); otherwise a ring write at seen % max_seq_len
+        (wrapping to slot 0), or the last max_seq_len tokens when T alone fills
+        the cache.  Each layer keeps its own ``total_seen_tokens`` and
+        ``layer_seq_lens``.  FP8 / INT4 caches quantize the new rows with the
+        CUDA kernels (fp16 inputs by the fp16 rule, fp32 by the fp32 rule) and
+        return dequantized fp16 copies of the window, as the reference returns
+        high-precision views for SDPA; an fp16 cache returns views of its
+        buffers."""
+        B, _, T, _ = k.shape
+        seen = self.total_seen_tokens[layer_idx]
+        S = self.max_seq_len
+        kb, vb = self.k_caches[layer_idx], self.v_caches[layer_idx]
+        quant = self.cache_dtype != "fp16"
+        if quant:
+            kq, ks = ops.quantize_kv(k, self.cache_dtype, self.kv_group)
+            vq, vs = ops.quantize_kv(v, self.cache_dtype, self.kv_group)
+            pairs = ((kb, kq), (vb, vq), (self.k_scales[layer_idx], ks), (self.v_scales[layer_idx], vs))
+        else:
+            pairs = ((kb, k), (vb, v))
+
+        def put(dst0: int, src0: int, n: int):
+            for dst, src in pairs:
+                dst[:B, :, dst0:dst0 + n] = src[:, :, src0:src0 + n]
+
+        new_seen = seen + T
+        if not self.ring_buffer and new_seen <= S:
+            put(seen, 0, T)
+        elif T >= S:
+            put(0, T - S, S)
+        else:
+            wp = seen % S
+            first = min(T, S - wp)
+            put(wp, 0, first)
+            if T > first:
+                put(0, first, T - first)
+        active = min(new_seen, S)
+        self.layer_seq_lens[layer_idx] = active
+        self.total_seen_tokens[layer_idx] = new_seen
+        if quant:
+            return (ops.dequantize_kv(kb[:B, :, :active], self.k_scales[layer_idx][:B, :, :active], self.cache_dtype,
+                                      self.head_dim),
+                    ops.dequantize_kv(vb[:B, :, :active], self.v_scales[layer_idx][:B, :, :active], self.cache_dtype,
+                                      self.head_dim))
+        return kb[:B, :, :active], vb[:B, :, :active]
 
     def get_quantized_views(self, layer_idx: int):
         k_s = self.k_scales[layer_idx] if self.scales is not None else None

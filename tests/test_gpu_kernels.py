@@ -188,7 +188,8 @@ def test_gemv_sweep(ax, M, fmt):
 
 def test_gemv_big_shapes_and_determinism(ax):
     torch.manual_seed(0)
-    for N, K in [(4096, 4096), (6144, 4096), (4096, 14336), (512, 14336)]:
+    # every 8B decode shape at M = 1: QKV, o, down, gate_up and the lm_head
+    for N, K in [(4096, 4096), (6144, 4096), (4096, 14336), (512, 14336), (28672, 4096), (128256, 4096)]:
         w = torch.randn(N, K, device="cuda") * 0.02
         W = ax.pack_q4t(w, 128, True)
         x = torch.randn(1, K, device="cuda").half()
