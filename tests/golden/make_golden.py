@@ -201,20 +201,7 @@ def gen_model(cfg, seed, prompt_len, n_new, kv, ln_random, tied=False, with_tree
     return out
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("AXIOMLM_REFERENCE", ""))
-    ap.add_argument("--skip-tiny", action="store_true")
-    args = ap.parse_args()
-    if not args.reference or not os.path.isdir(args.reference):
-        raise SystemExit("pass --reference <path to the AxiomLM checkout>")
-    sys.path.insert(0, args.reference)
-    torch.set_num_threads(os.cpu_count() or 1)
-    import axiomlm.kernels.ops as ops
-    import axiomlm.kernels.quant as q
-    import axiomlm.models.modules as modules
-    from axiomlm.engine.medusa import DEFAULT_MEDUSA_TREE_CHOICES, compile_medusa_tree
-
+def _gen_small(q, ops, modules, compile_medusa_tree, DEFAULT_MEDUSA_TREE_CHOICES):
     np.savez_compressed(os.path.join(HERE, "quant.npz"), **gen_quant(q))
     np.savez_compressed(os.path.join(HERE, "kv.npz"), **gen_kv(q))
     np.savez_compressed(os.path.join(HERE, "rope.npz"), **gen_rope(modules))
@@ -237,11 +224,40 @@ def main():
     np.savez_compressed(os.path.join(HERE, "small_fp8_ring.npz"), **o)
     o = gen_model(SMALL, 31, 10, 16, "fp16", ln_random=True, tied=True)
     np.savez_compressed(os.path.join(HERE, "small_tied.npz"), **o)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("AXIOMLM_REFERENCE", ""))
+    ap.add_argument("--skip-tiny", action="store_true")
+    ap.add_argument("--tiny-only", action="store_true", help="regenerate only the BASELINE config-1 fixtures")
+    args = ap.parse_args()
+    if not args.reference or not os.path.isdir(args.reference):
+        raise SystemExit("pass --reference <path to the AxiomLM checkout>")
+    sys.path.insert(0, args.reference)
+    torch.set_num_threads(os.cpu_count() or 1)
+    import axiomlm.kernels.ops as ops
+    import axiomlm.kernels.quant as q
+    import axiomlm.models.modules as modules
+    from axiomlm.engine.medusa import DEFAULT_MEDUSA_TREE_CHOICES, compile_medusa_tree
+
+    if not args.tiny_only:
+        _gen_small(q, ops, modules, compile_medusa_tree, DEFAULT_MEDUSA_TREE_CHOICES)
     if not args.skip_tiny:
         for kv in ("fp16", "fp8"):
             t0 = time.time()
             o = gen_model(TINY, 5, 128, 128, kv, ln_random=False)
-            o.pop("logits")
+            # the full (128, 32000) logits are too large for a fixture: keep,
+            # per step, the top-32 entries, a fixed sample of 256 columns and
+            # the largest |logit| (the scale of the per-step tolerance)
+            lg = torch.from_numpy(o.pop("logits")).float()
+            top = torch.topk(lg, 32, dim=-1)
+            cols = torch.randperm(lg.shape[1], generator=torch.Generator().manual_seed(77))[:256].sort().values
+            o["logit_top_idx"] = _np(top.indices.to(torch.int32))
+            o["logit_top_val"] = _np(top.values.to(torch.float16))
+            o["logit_cols"] = _np(cols.to(torch.int32))
+            o["logit_col_val"] = _np(lg[:, cols].to(torch.float16))
+            o["logit_absmax"] = _np(lg.abs().amax(-1))
             np.savez_compressed(os.path.join(HERE, f"tiny_{kv}.npz"), **o)
             print(f"tiny {kv}: {time.time() - t0:.1f}s min-margin={o['margin'].min():.2e}")
 

@@ -94,7 +94,11 @@ def test_small_model_greedy_parity(name, kv, graph):
 
 @pytest.mark.parametrize("kv", ["fp16", "fp8"])
 def test_tiny_config_128_greedy_tokens(kv):
-    """12L/768d/12H, vocab 32000, prompt 128, 128 greedy tokens."""
+    """12L/768d/12H, vocab 32000, prompt 128, 128 greedy tokens.
+
+    Free-running tokens match up to the reference's first near-tie (the step
+    is reported on failure); teacher-forced, all 128 steps' tokens and logits
+    are checked."""
     fx = _fx(f"tiny_{kv}")
     dec = _decoder(TINY, fx, kv)
     # free-running greedy: identical to the reference up to its first near-tie
@@ -106,8 +110,21 @@ def test_tiny_config_128_greedy_tokens(kv):
         pytest.fail(f"first divergence at step {i}: ours {toks[i]} ref {ref[i]}; reference top-2 margin "
                     f"there {fx['margin'][i]:.2e}")
     dec.close()
-    # teacher-forced: every step agrees except at near-ties
+    # teacher-forced: every step agrees except at near-ties, and every step's
+    # logits match the reference's at its top-32 entries and at 256 fixed
+    # columns, relative to that step's largest |logit|
     dec = _decoder(TINY, fx, kv)
-    toks, _ = _greedy_with_logits(dec, fx["prompt"], len(fx["tokens"]), forced=fx["tokens"])
+    toks, logits = _greedy_with_logits(dec, fx["prompt"], len(fx["tokens"]), forced=fx["tokens"])
     _check_tokens(toks, fx)
     dec.close()
+    cols = torch.as_tensor(fx["logit_cols"]).long()
+    worst = 0.0
+    for i in range(len(toks)):
+        top = torch.as_tensor(fx["logit_top_idx"][i]).long()
+        ours = torch.cat([logits[i][top], logits[i][cols]])
+        ref = torch.cat([torch.as_tensor(fx["logit_top_val"][i]).float(),
+                         torch.as_tensor(fx["logit_col_val"][i]).float()])
+        rel = float((ours - ref).abs().max()) / float(fx["logit_absmax"][i])
+        worst = max(worst, rel)
+        assert rel < REL_TOL[kv], f"step {i}: logits rel {rel:.2e} (tol {REL_TOL[kv]})"
+    print(f"tiny {kv}: 128 teacher-forced steps, worst logit rel {worst:.2e}")
