@@ -33,6 +33,8 @@ struct DecodeFuse {
 };
 int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s);
 int attn_prepare();
+int q8_gemv(const __half* x, int ldx, int M, int K, const uint32_t* w, const __half2* sb, int N, __half* y, int ldy,
+            cudaStream_t st);
 size_t attn_workspace(int B, int n_head, int head_dim, int max_splits);
 int tree_splits(int B, int T, int n_head, int n_kv_head, int n_keys);
 size_t tree_workspace(int B, int T, int n_head, int head_dim, int nsplit);
@@ -175,8 +177,9 @@ __global__ void argmax_part_kernel(const __half* __restrict__ x, int n, int ld, 
 }
 
 // final-norm hidden state in fp32 (the reference's x_norm / get_last_norm)
-__global__ void rmsnorm_f32_kernel(const __half* __restrict__ x, const float* __restrict__ w, int K, float eps,
-                                   float* __restrict__ out) {
+template <typename OutT>
+__global__ void rmsnorm_kernel(const __half* __restrict__ x, const float* __restrict__ w, int K, float eps,
+                               OutT* __restrict__ out) {
   pdl_wait();
   const int row = blockIdx.x;
   const __half* xr = x + (size_t)row * K;
@@ -196,8 +199,11 @@ __global__ void rmsnorm_f32_kernel(const __half* __restrict__ x, const float* __
   }
   __syncthreads();
   const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)K), eps)));
-  for (int k = threadIdx.x; k < K; k += blockDim.x)
-    out[(size_t)row * K + k] = __fmul_rn(__fmul_rn(__half2float(xr[k]), rms), w[k]);
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = __fmul_rn(__fmul_rn(__half2float(xr[k]), rms), w[k]);
+    if constexpr (sizeof(OutT) == 2) out[(size_t)row * K + k] = __float2half_rn(v);
+    else out[(size_t)row * K + k] = v;
+  }
 }
 
 static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
@@ -526,13 +532,24 @@ struct Runner {
       rc = row_parallel(dn_w[l], dn_s[l], c.ffn, rows, buf<__half>(L.sw), st);
       if (rc) return rc;
     }
-    int rc = use_tc(rows) ? norm_tc(ln_f, lm_w, lm_s, c.lm_fmt, c.lm_group, c.vocab, d, rows, buf<__half>(L.logits),
-                                    c.vocab, nullptr, st)
-                          : norm_gemv(ln_f, lm_w, lm_s, c.vocab, d, rows, buf<void>(L.logits), c.vocab, nullptr,
-                                      AXB_EPI_STORE, 0, c.lm_fmt, c.lm_group, st);
+    int rc;
+    if (c.lm_fmt == AXB_W_Q8_G64) {
+      // tied lm_head: the Q8_G64 embedding matrix, on the final-norm rows
+      // (fp16, the reference's qlin cast) staged in the attention buffer
+      e = launch_pdl(rmsnorm_kernel<__half>, dim3(rows), dim3(256), 0, st, pdl, (const __half*)buf<__half>(L.x), ln_f,
+                     d, c.eps, buf<__half>(L.attn));
+      if (e != cudaSuccess) return cuda_status(e, "lm_head norm launch");
+      rc = q8_gemv(buf<__half>(L.attn), d, rows, d, static_cast<const uint32_t*>(lm_w),
+                   static_cast<const __half2*>(lm_s), c.vocab, buf<__half>(L.logits), c.vocab, st);
+    } else {
+      rc = use_tc(rows) ? norm_tc(ln_f, lm_w, lm_s, c.lm_fmt, c.lm_group, c.vocab, d, rows, buf<__half>(L.logits),
+                                  c.vocab, nullptr, st)
+                        : norm_gemv(ln_f, lm_w, lm_s, c.vocab, d, rows, buf<void>(L.logits), c.vocab, nullptr,
+                                    AXB_EPI_STORE, 0, c.lm_fmt, c.lm_group, st);
+    }
     if (rc) return rc;
     if (want_norm) {
-      e = launch_pdl(rmsnorm_f32_kernel, dim3(rows), dim3(256), 0, st, pdl, (const __half*)buf<__half>(L.x), ln_f,
+      e = launch_pdl(rmsnorm_kernel<float>, dim3(rows), dim3(256), 0, st, pdl, (const __half*)buf<__half>(L.x), ln_f,
                      d, c.eps, buf<float>(L.xnorm));
       if (e != cudaSuccess) return cuda_status(e, "final norm launch");
     }
@@ -571,7 +588,8 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   AXB_CHECK_ARG(c.n_head * c.head_dim * tpw == c.d_model,
                 "runner_create: n_head * head_dim * tp_world must equal d_model");
   AXB_CHECK_ARG(c.wfmt == AXB_W_Q4T_SYM || c.wfmt == AXB_W_Q4T_AFFINE, "runner_create: unsupported weight format");
-  AXB_CHECK_ARG(c.lm_fmt == AXB_W_Q4T_SYM || c.lm_fmt == AXB_W_Q4T_AFFINE,
+  AXB_CHECK_ARG(c.lm_fmt == AXB_W_Q4T_SYM || c.lm_fmt == AXB_W_Q4T_AFFINE ||
+                    (c.lm_fmt == AXB_W_Q8_G64 && c.lm_group == 64 && c.tp_world <= 1),
                 "runner_create: lm_head format %d not supported by the runner", c.lm_fmt);
   AXB_CHECK_ARG(c.max_tokens >= 1 && c.max_tokens <= 64 && c.max_batch >= 1, "runner_create: bad max_tokens/batch");
   AXB_CHECK_ARG(c.ffn % 8 == 0, "runner_create: ffn must be a multiple of 8");

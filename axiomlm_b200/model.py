@@ -127,12 +127,12 @@ class QuantizedDecoder:
         """Pack fp32 master weights (``tests/golden/model_weights.make_weights``
         layout) on the GPU, following ``_ensure_quant_weights`` in q4_rtn
         mode (transformer.py:822-1008): projections and an untied lm_head in
-        Q4, token embeddings in Q8_G64, RMSNorm weights kept fp32."""
+        Q4, token embeddings in Q8_G64 (also the lm_head when the embeddings are
+        tied), RMSNorm weights kept fp32."""
         dev = torch.device(kw.get("device", "cuda"))
         fmt, group = WEIGHT_FORMATS[weight_format]
         sym = fmt == L.W_Q4T_SYM
-        if weights.get("lm_head") is None:
-            raise NotImplementedError("tied embeddings need the Q8_G64 lm_head GEMV, which the runner lacks")
+        tied = weights.get("lm_head") is None
 
         def g(t):
             return t.to(dev, torch.float32)
@@ -146,8 +146,10 @@ class QuantizedDecoder:
                 ln_1=g(lw["ln_1"]).contiguous(), ln_2=g(lw["ln_2"]).contiguous(), qkv_b=None))
             del gu
         emb_w, emb_s = ops.pack_q8_g64(g(weights["wte"]))
-        packed = dict(layers=layers, emb_w=emb_w, emb_s=emb_s, lm_head=ops.pack_q4t(g(weights["lm_head"]), group, sym),
-                      ln_f=g(weights["ln_f"]).contiguous())
+        # tied embeddings (transformer.py:842-847): the Q8_G64 embedding matrix is the lm_head
+        lm = (ops.Q8Weight(emb_w, emb_s, emb_w.shape[0], emb_w.shape[1] * 4) if tied
+              else ops.pack_q4t(g(weights["lm_head"]), group, sym))
+        packed = dict(layers=layers, emb_w=emb_w, emb_s=emb_s, lm_head=lm, ln_f=g(weights["ln_f"]).contiguous())
         dec = cls(cfg, packed, **kw)
         if weights.get("medusa"):
             from .medusa import MedusaHeads
@@ -162,8 +164,6 @@ class QuantizedDecoder:
         dev = torch.device(kw.get("device", "cuda"))
         mc = model.config
         qw = model._ensure_quant_weights(torch.device("cpu"))
-        if qw["lmh_p"].ndim != 4:
-            raise NotImplementedError("Q8_G64 lm_head (tied / q4_k_m) is not supported by the runner")
         H = mc.n_head
         Hkv = mc.n_kv_head or H
         hd = mc.n_embd // H
@@ -184,7 +184,10 @@ class QuantizedDecoder:
                 ln_2=b.ln_2.weight.detach().to(dev, torch.float32).contiguous(),
                 qkv_b=cb.to(dev, torch.float16) if cb.numel() > 0 else None))
         packed = dict(layers=layers, emb_w=qw["wte_p"].to(dev), emb_s=qw["wte_sb"].to(dev),
-                      lm_head=ops.q4t_from_marlin(qw["lmh_p"].to(dev), qw["lmh_sb"].to(dev), mc.vocab_size),
+                      lm_head=(ops.q4t_from_marlin(qw["lmh_p"].to(dev), qw["lmh_sb"].to(dev), mc.vocab_size)
+                               if qw["lmh_p"].ndim == 4 else  # Q8_G64 lm_head: tied embeddings (the default)
+                               ops.Q8Weight(qw["lmh_p"].to(dev).contiguous(), qw["lmh_sb"].to(dev).contiguous(),
+                                            mc.vocab_size, mc.n_embd)),
                       ln_f=model.transformer.ln_f.weight.detach().to(dev, torch.float32).contiguous())
         dec = cls(cfg, packed, **kw)
         if qw.get("medusa_packs"):

@@ -120,6 +120,40 @@ def q4t_from_marlin(w_marlin: torch.Tensor, sb_marlin: torch.Tensor, n_out: int 
     return Q4TWeight(words, scales, N, K, 64, L.W_Q4T_AFFINE, gate_up)
 
 
+@dataclass
+class Q8Weight:
+    """A projection in the reference's own Q8_G64 layout (quant.py:72-129):
+    ``words`` (N, K/4) int32, ``scales`` (N, K/64, 2) fp16 scale and bias."""
+
+    words: torch.Tensor
+    scales: torch.Tensor
+    N: int
+    K: int
+    group: int = 64
+    fmt: int = L.W_Q8_G64
+
+    @property
+    def nbytes(self) -> int:
+        return self.words.numel() * 4 + self.scales.numel() * 2
+
+
+def qmv_q8_g64(x: torch.Tensor, w_packed: torch.Tensor, scales_biases: torch.Tensor) -> torch.Tensor:
+    """qmv_q8_g64 / qmm_q8_g64 (quant.py:201-233): y = x . dequant(W)^T, fp16,
+    with the weights dequantized as dequantize_q8_g64 does."""
+    x = _cuda(x, "x").half()
+    w = _cuda(w_packed, "w_packed")
+    sb = _cuda(scales_biases, "scales_biases").half()
+    K = x.shape[-1]
+    N = w.shape[0]
+    M = x.numel() // K
+    y = torch.empty((*x.shape[:-1], N), dtype=torch.float16, device=x.device)
+    L.call("axb_q8g64_gemv", _p(x), K, M, K, _p(w), _p(sb), N, _p(y), N, _stream())
+    return y
+
+
+qmm_q8_g64 = qmv_q8_g64
+
+
 def pack_q8_g64(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """pack_linear_q8_g64 (quant.py:72-129) on the GPU."""
     w = _cuda(w, "w").float()

@@ -148,6 +148,16 @@ typedef struct {
 size_t axb_lbgemv_workspace_bytes(int fmt, int N, int K, int M);
 int axb_lbgemv(const axb_lbgemv_desc* d, void* stream);
 
+/* ---- Q8_G64 GEMV / small-M GEMM (qmv_q8_g64 / qmm_q8_g64, quant.py:201-233;
+ *      Metal qmv_q8_g64_half_kernel :1941) ------------------------------------
+ * y (M, ldy) fp16 = x (M, ldx) fp16 . dequant(W)^T with W in the reference's
+ * own Q8_G64 layout: w_packed (N, K/4) int32, scales_biases (N, K/64, 2) fp16,
+ * dequantized as dequantize_q8_g64 does (fp16(q * scale + bias) in fp32).
+ * K % 64 == 0, ldx % 8 == 0, x and w 16-byte aligned. The tied lm_head (the
+ * reference default) runs on it. No workspace. */
+int axb_q8g64_gemv(const void* x, int ldx, int M, int K, const int32_t* w_packed, const uint16_t* scales_biases,
+                   int N, void* y, int ldy, void* stream);
+
 /* ---- quantized GEMV / small-M GEMM (qmv_q4_marlin / qmm_q4_marlin,
  *      quant.py:637-684; Metal qmv_q4_marlin_apple_kernel) ------------------- */
 typedef struct {

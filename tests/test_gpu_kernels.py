@@ -199,6 +199,28 @@ def test_gemv_big_shapes_and_determinism(ax):
         assert _rel(y1, _torch_ref_gemv(x, W.dequant())) < REL_TOL
 
 
+@pytest.mark.parametrize("N,K,M", [(40, 256, 3), (32000, 768, 1), (32000, 768, 5), (1000, 4096, 12)])
+def test_q8_g64_gemv(ax, N, K, M):
+    """qmv_q8_g64 (quant.py:201-233): the reference fixture's Q8 pack at its
+    own size, then larger seeded packs (the tied lm_head of the BASELINE
+    config-1 shape among them), against an fp32 matmul of the oracle's
+    dequantized weights (dequantize_q8_g64 values, pinned to the fixture)."""
+    g = np.load(os.path.join(GOLDEN, "quant.npz"))
+    if (N, K) == (40, 256):
+        wp, sb = g["q8_w"], g["q8_sb"]
+        assert np.array_equal(O.dequant_q8_g64(wp, sb, K), g["q8_dq"])
+        x = torch.from_numpy(g["x"]).cuda().half()
+    else:
+        torch.manual_seed(N + K + M)
+        wp, sb = O.pack_q8_g64(np.random.default_rng(N + M).standard_normal((N, K), dtype=np.float32) * 0.02)
+        x = torch.randn(M, K, device="cuda").half()
+    y = ax.qmv_q8_g64(x, torch.from_numpy(np.ascontiguousarray(wp)).cuda(), torch.from_numpy(sb).cuda())
+    dq = torch.from_numpy(O.dequant_q8_g64(wp, sb, K)).cuda().float()
+    ref = x.float() @ dq.t()
+    assert y.shape == (M, N)
+    assert _rel(y, ref) < REL_TOL
+
+
 def test_gemv_epilogues(ax):
     torch.manual_seed(1)
     F, K = 512, 256

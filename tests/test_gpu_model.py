@@ -72,7 +72,7 @@ def _check_tokens(toks, fx, logits=None):
 
 
 @pytest.mark.parametrize("name,kv", [("small_fp16", "fp16"), ("small_fp8", "fp8"), ("small_int4", "int4"),
-                                     ("small_fp8_ring", "fp8")])
+                                     ("small_fp8_ring", "fp8"), ("small_tied", "fp16")])
 @pytest.mark.parametrize("graph", [True, False])
 def test_small_model_greedy_parity(name, kv, graph):
     fx = _fx(name)
