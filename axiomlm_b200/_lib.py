@@ -151,6 +151,7 @@ _SIGS = {
     "axb_qgemm_noalloc_scratch_bytes": (sz, []),
     "axb_qgemm_noalloc_status": (i32, [vp]),
     "axb_q8g64_gemv": (i32, [vp, i32, i32, i32, vp, vp, i32, vp, i32, vp]),
+    "axb_q4t_from_q4g64": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
     "axb_rmsnorm": (i32, [vp, vp, i32, i32, f32, vp, vp]),
     "axb_rope_kv_write": (i32, [C.POINTER(KvWriteDesc), vp]),
     "axb_kv_quantize": (i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp]),

@@ -167,6 +167,48 @@ __global__ void q4t_from_marlin_kernel(const uint32_t* __restrict__ wm, const __
   }
 }
 
+// ---- relayout of the reference's legacy Q4_G64 format --------------------
+// pack_linear_q4_g64 (quant.py:17-69): code k of row n in bits 4 (k % 8) of
+// word n * K/8 + k / 8; scale and bias per (row, 64-wide group).  The same
+// affine values as q4t AFFINE G64, in a different order.
+__global__ void q4t_from_q4g64_kernel(const uint32_t* __restrict__ wl, const __half* __restrict__ sb, int N, int K,
+                                      int gu, uint32_t* __restrict__ words, __half* __restrict__ scales) {
+  const int KB = K / 64, tile = blockIdx.y, kb = blockIdx.x;
+  const int t = threadIdx.x;
+  if (t < 128) {
+    const int lane = t >> 2, j = t & 3;
+    uint32_t word = 0;
+#pragma unroll
+    for (int nib = 0; nib < 8; ++nib) {
+      int row, kk;
+      q4t_word_coords(lane, j, nib, row, kk);
+      const int src = gu_src_row(tile * 16 + row, N, gu);
+      uint32_t q = 0;
+      if (src < N) {
+        const int k = kb * 64 + kk;
+        q = (wl[(size_t)src * (K / 8) + (k >> 3)] >> (4 * (k & 7))) & 0xFu;
+      }
+      word |= q << (4 * nib);
+    }
+    words[((size_t)tile * KB + kb) * 128 + lane * 4 + j] = word;
+  } else if (t < 136) {
+    const int g = t - 128;
+    const size_t base = ((size_t)tile * KB + kb) * 8 + g;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int src = gu_src_row(tile * 16 + g + 8 * h, N, gu);
+      __half sc = __float2half_rn(0.f), bi = __float2half_rn(0.f);
+      if (src < N) {
+        const __half* p = sb + ((size_t)src * KB + kb) * 2;
+        sc = p[0];
+        bi = p[1];
+      }
+      scales[base * 4 + 2 * h + 0] = sc;
+      scales[base * 4 + 2 * h + 1] = bi;
+    }
+  }
+}
+
 // ---- dequant (bit-exact statements of the reference formulas) --------------
 __global__ void q4t_dequant_kernel(const uint32_t* __restrict__ words, const __half* __restrict__ scales, int N,
                                    int K, int G, int sym, int gu, __half* __restrict__ out) {
@@ -969,6 +1011,17 @@ int axb_q4t_pack(const float* w, int N, int K, int group, int fmt, int gu, void*
   q4t_pack_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(w, N, K, group, fmt == AXB_W_Q4T_SYM, gu,
                                                           (uint32_t*)words, (__half*)scales);
   return launch_status("q4t_pack");
+}
+
+int axb_q4t_from_q4g64(const int32_t* w_packed, const uint16_t* sb, int N, int K, int gu, void* words, void* scales,
+                       void* stream) {
+  AXB_CHECK_ARG(w_packed && sb && words && scales, "q4t_from_q4g64: null pointer");
+  AXB_CHECK_ARG(N > 0 && K > 0 && K % 64 == 0, "q4t_from_q4g64: bad shape (%d, %d)", N, K);
+  AXB_CHECK_ARG(!gu || N % 16 == 0, "q4t_from_q4g64: gate/up interleave needs N %% 16 == 0");
+  dim3 grid(K / 64, (N + 15) / 16);
+  q4t_from_q4g64_kernel<<<grid, 160, 0, (cudaStream_t)stream>>>((const uint32_t*)w_packed, (const __half*)sb, N, K, gu,
+                                                                 (uint32_t*)words, (__half*)scales);
+  return launch_status("q4t_from_q4g64");
 }
 
 int axb_q4t_from_marlin(const int32_t* wm, const uint16_t* sb, int n_tiles8, int K, int n_out, int gu, void* words,

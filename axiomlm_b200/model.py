@@ -160,7 +160,9 @@ class QuantizedDecoder:
     @classmethod
     def from_reference(cls, model: Any, **kw) -> "QuantizedDecoder":
         """Serve a reference ``Transformer`` after ``model.quantize("q4" |
-        "q4_rtn")``: its packed MARLIN tensors are relaid out bit-exactly."""
+        "q4_rtn" | "q4_legacy")``: its packed MARLIN or legacy Q4_G64 tensors
+        are relaid out bit-exactly; a Q8_G64 lm_head (tied embeddings) runs on
+        the Q8 GEMV."""
         dev = torch.device(kw.get("device", "cuda"))
         mc = model.config
         qw = model._ensure_quant_weights(torch.device("cpu"))
@@ -174,7 +176,11 @@ class QuantizedDecoder:
         layers = []
         for i, b in enumerate(model.transformer.h):
             def rl(p, s, n, gu=False):
-                return ops.q4t_from_marlin(p.to(dev), s.to(dev), n, gate_up=gu)
+                if p.ndim == 4:  # MARLIN ladder ("q4", "q4_rtn")
+                    return ops.q4t_from_marlin(p.to(dev), s.to(dev), n, gate_up=gu)
+                if p.shape[1] * 8 == s.shape[1] * 64:  # legacy Q4_G64 ("q4_legacy")
+                    return ops.q4t_from_q4g64(p.to(dev).contiguous(), s.to(dev).contiguous(), n, gate_up=gu)
+                raise NotImplementedError("Q8_G64 projections (the q8 / q4_k_m modes) are not served by the runner")
             cb = qw["c_attn_b"][i]
             layers.append(dict(
                 qkv=rl(qw["c_attn_p"][i], qw["c_attn_s"][i], qkv_dim), o=rl(qw["c_proj_p"][i], qw["c_proj_s"][i], mc.n_embd),
@@ -184,10 +190,10 @@ class QuantizedDecoder:
                 ln_2=b.ln_2.weight.detach().to(dev, torch.float32).contiguous(),
                 qkv_b=cb.to(dev, torch.float16) if cb.numel() > 0 else None))
         packed = dict(layers=layers, emb_w=qw["wte_p"].to(dev), emb_s=qw["wte_sb"].to(dev),
-                      lm_head=(ops.q4t_from_marlin(qw["lmh_p"].to(dev), qw["lmh_sb"].to(dev), mc.vocab_size)
-                               if qw["lmh_p"].ndim == 4 else  # Q8_G64 lm_head: tied embeddings (the default)
-                               ops.Q8Weight(qw["lmh_p"].to(dev).contiguous(), qw["lmh_sb"].to(dev).contiguous(),
-                                            mc.vocab_size, mc.n_embd)),
+                      lm_head=(ops.Q8Weight(qw["lmh_p"].to(dev).contiguous(), qw["lmh_sb"].to(dev).contiguous(),
+                                            mc.vocab_size, mc.n_embd)
+                               if qw["lmh_p"].ndim == 2 and qw["lmh_p"].shape[1] * 4 == mc.n_embd  # tied: Q8_G64
+                               else rl(qw["lmh_p"], qw["lmh_sb"], mc.vocab_size)),
                       ln_f=model.transformer.ln_f.weight.detach().to(dev, torch.float32).contiguous())
         dec = cls(cfg, packed, **kw)
         if qw.get("medusa_packs"):

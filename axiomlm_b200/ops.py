@@ -120,6 +120,40 @@ def q4t_from_marlin(w_marlin: torch.Tensor, sb_marlin: torch.Tensor, n_out: int 
     return Q4TWeight(words, scales, N, K, 64, L.W_Q4T_AFFINE, gate_up)
 
 
+def q4t_from_q4g64(w_packed: torch.Tensor, scales_biases: torch.Tensor, n_out: int | None = None,
+                   gate_up: bool = False) -> Q4TWeight:
+    """Relayout the reference's legacy Q4_G64 pack (pack_linear_q4_g64,
+    quant.py:17-69) into q4t affine G64 (bit-identical codes, scales, biases)."""
+    wp = _cuda(w_packed, "w_packed")
+    sb = _cuda(scales_biases, "scales_biases")
+    N, K = wp.shape[0], wp.shape[1] * 8
+    if n_out is not None and n_out != N:
+        raise ValueError(f"legacy pack has {N} rows, expected {n_out}")
+    words, scales = _alloc_q4t(N, K, 64, L.W_Q4T_AFFINE, wp.device)
+    L.call("axb_q4t_from_q4g64", _p(wp), _p(sb), N, K, int(gate_up), _p(words), _p(scales), _stream())
+    return Q4TWeight(words, scales, N, K, 64, L.W_Q4T_AFFINE, gate_up)
+
+
+def qmv_q4_g64(x: torch.Tensor, w_packed: torch.Tensor, scales_biases: torch.Tensor) -> torch.Tensor:
+    """qmv_q4_g64 / qmm_q4_g64 (quant.py:166-198) through the q4t GEMV (the
+    relayout is cached per weight tensor)."""
+    key = (w_packed.data_ptr(), w_packed._version, scales_biases.data_ptr(), scales_biases._version,
+           tuple(w_packed.shape))
+    W = _LEGACY_CACHE.get(key)
+    if W is None:
+        if len(_LEGACY_CACHE) > 256:
+            _LEGACY_CACHE.clear()
+        W = q4t_from_q4g64(w_packed, scales_biases)
+        _LEGACY_CACHE[key] = W
+    K = x.shape[-1]
+    y = qgemm(x.reshape(-1, K).half(), W)
+    return y.view(*x.shape[:-1], W.N)
+
+
+_LEGACY_CACHE: dict = {}
+qmm_q4_g64 = qmv_q4_g64
+
+
 @dataclass
 class Q8Weight:
     """A projection in the reference's own Q8_G64 layout (quant.py:72-129):

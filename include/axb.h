@@ -91,6 +91,12 @@ int axb_q4t_pack(const float* w_dev, int N, int K, int group, int fmt, int gate_
 int axb_q4t_from_marlin(const int32_t* w_marlin_dev, const uint16_t* sb_marlin_dev, int n_tiles8, int K,
                         int n_out, int gate_up_interleave, void* words_dev, void* scales_dev, void* stream);
 
+/* Relayout the reference's legacy Q4_G64 (w_packed int32 (N, K/8), sb fp16
+ * (N, K/64, 2); pack_linear_q4_g64, quant.py:17-69, the "q4_legacy" mode) into
+ * q4t affine G64: bit-identical codes, scales and biases. */
+int axb_q4t_from_q4g64(const int32_t* w_packed_dev, const uint16_t* sb_dev, int N, int K, int gate_up_interleave,
+                       void* words_dev, void* scales_dev, void* stream);
+
 /* fp16 (N, K) dequant of q4t (replaces dequantize_q4_marlin, quant.py:597,
  * on the relaid-out form: identical values). */
 int axb_q4t_dequant(const void* words_dev, const void* scales_dev, int N, int K, int group, int fmt,

@@ -68,6 +68,26 @@ def test_relayout_from_marlin_bit_exact(ax, gate_up):
         assert np.array_equal(_bits(W.dequant()), g["q4m_clip_dq"].view(np.uint16))
 
 
+def test_relayout_from_legacy_q4g64_bit_exact(ax):
+    """q4_legacy packs (pack_linear_q4_g64, quant.py:17-69): the relayout keeps
+    the reference's codes, scales and biases, so the q4t dequant equals
+    dequantize_q4_g64 bit for bit; the GEMV (qmv_q4_g64) agrees with an fp32
+    matmul of those values, and the gate/up interleave keeps every row."""
+    g = _g("quant.npz")
+    W = ax.q4t_from_q4g64(_cu(g["q4g_w"]), _cu(g["q4g_sb"]))
+    assert np.array_equal(_bits(W.dequant()), g["q4g_dq"].view(np.uint16))
+    x = _cu(g["x"]).half()
+    ref = x.float() @ torch.from_numpy(g["q4g_dq"]).cuda().float().t()
+    assert _rel(ax.qmv_q4_g64(x, _cu(g["q4g_w"]), _cu(g["q4g_sb"])), ref) < REL_TOL
+    # gate/up interleave of a seeded 2F x K legacy pack (rows g of a tile = gate j, g + 8 = up j)
+    rng = np.random.default_rng(5)
+    wp, sb = O.pack_q4_g64(rng.standard_normal((64, 256), dtype=np.float32) * 0.02)
+    Wg = ax.q4t_from_q4g64(_cu(wp), _cu(sb), gate_up=True)
+    Wp = ax.q4t_from_q4g64(_cu(wp), _cu(sb))
+    dq_g, dq_p = Wg.dequant().float().cpu(), Wp.dequant().float().cpu()
+    assert torch.equal(torch.sort(dq_g, 0).values, torch.sort(dq_p, 0).values)
+
+
 @pytest.mark.parametrize("group,sym,gu", [(64, False, False), (128, True, False), (128, True, True), (64, True, True),
                                           (128, False, False)])
 def test_q4t_pack_matches_oracle(ax, group, sym, gu):
