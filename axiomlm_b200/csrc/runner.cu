@@ -219,6 +219,7 @@ struct Layout {
   size_t gemm_ws_bytes, attn_ws_bytes;
   // persistent step kernel (decode, B <= 8)
   size_t st_layers, st_done, st_tiles, st_part, st_po, st_pml, st_acnt, st_keys, st_exit, st_trace, st_hdump, st_maps;
+  size_t st_h, st_qkv, st_attn, st_sw;  // the step kernel's flagged activations: one 8-byte word per 2 halves
   size_t st_trace_bytes, st_hdump_bytes;
   int st_max_tiles;
 };
@@ -299,6 +300,10 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.st_hdump_bytes = (size_t)c.n_layer * sb * c.d_model * 2;
   L.st_hdump = take(L.st_hdump_bytes);
   L.st_maps = take((size_t)c.n_layer * 2 * kStepMapBytes);  // 256-aligned (tensor maps need 64)
+  L.st_h = take((size_t)sb * c.d_model * 4);
+  L.st_qkv = take((size_t)sb * qkv_dim * 4);
+  L.st_attn = take((size_t)sb * c.n_head * c.head_dim * 4);
+  L.st_sw = take((size_t)sb * c.ffn * 4);
   L.total = off;
   return L;
 }
@@ -723,10 +728,10 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
     a.tokens = r->buf<int32_t>(L.tokens);
     a.params = r->buf<int32_t>(L.params);
     a.err = r->buf<int>(L.params) + 4;
-    a.h = r->buf<__half>(L.x);
-    a.qkv = r->buf<__half>(L.qkv);
-    a.attn = r->buf<__half>(L.attn);
-    a.sw = r->buf<__half>(L.sw);
+    a.h = r->buf<uint2>(L.st_h);
+    a.qkv = r->buf<uint2>(L.st_qkv);
+    a.attn = r->buf<uint2>(L.st_attn);
+    a.sw = r->buf<uint2>(L.st_sw);
     a.logits = r->buf<__half>(L.logits);
     a.amax = r->buf<int32_t>(L.amax);
     a.done = r->buf<int>(L.st_done);

@@ -115,6 +115,22 @@ __device__ __forceinline__ uint4 ld_ll(const uint4* p) {
   return v;
 }
 
+// Activations move the same way: word i of a row holds halves 2i, 2i + 1
+// and the flag of the phase that wrote them, in one 8-byte store, so a phase
+// starts when the words it reads carry the flag it expects; no counter,
+// release or acquire sits between a producer's store and its reader.  The
+// flag of phase p (-1: the embedding rows) of launch e is e * 512 + p + 2,
+// never 0, the value of a word nobody wrote.
+__device__ __forceinline__ uint32_t act_flag(uint32_t epoch, int p) { return epoch * 512u + (uint32_t)(p + 2); }
+__device__ __forceinline__ void st_act(uint2* p, uint32_t h2, uint32_t fl) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(h2), "r"(fl) : "memory");
+}
+__device__ __forceinline__ uint2 ld_act(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
 // phase timeline stamp, only when a trace buffer is set: thread 0 of each CTA
 // (trace_mark), or the calling thread (trace_at)
 __device__ __forceinline__ void trace_at(const StepArgs& a, int slot) {
@@ -130,6 +146,41 @@ __device__ __forceinline__ void trace_mark(const StepArgs& a, int slot) {
 __device__ __forceinline__ void raise_abort(const StepArgs& a) {
   atomicExch(a.exit_cnt + 1, 1);
   atomicExch(a.err, AXB_ETIMEOUT);
+}
+
+// The halves of a flagged activation word once it carries flag fl.  The wait
+// is bounded: it gives up after a.spin_limit polls (raising the abort) or as
+// soon as another CTA has raised it; the step's outputs are then not valid.
+__device__ __forceinline__ bool act_giveup(uint32_t it, const StepArgs& a) {
+  if (it >= a.spin_limit) {
+    raise_abort(a);
+    return true;
+  }
+  return (it & 15) == 0 && *reinterpret_cast<const volatile int*>(a.exit_cnt + 1) != 0;
+}
+__device__ __forceinline__ uint32_t act_get(const uint2* p, uint32_t fl, const StepArgs& a) {
+  uint2 v = ld_act(p);
+  for (uint32_t it = 1; v.y != fl && !act_giveup(it, a); ++it) {
+    __nanosleep(32);
+    v = ld_act(p);
+  }
+  return v.x;
+}
+// Loads are issued first (all in flight) and only then waited on: v holds
+// what the first load saw; these reload until the flag(s) match.
+__device__ __forceinline__ void act_wait1(const uint2* p, uint2& v, uint32_t fl, const StepArgs& a) {
+  for (uint32_t it = 1; v.y != fl && !act_giveup(it, a); ++it) {
+    __nanosleep(32);
+    v = ld_act(p);
+  }
+}
+// two consecutive flagged words in one 16-byte load: halves 4i .. 4i + 3
+__device__ __forceinline__ void act_wait2(const uint2* p, uint4& v, uint32_t fl, const StepArgs& a) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+  for (uint32_t it = 1; (v.y != fl || v.w != fl) && !act_giveup(it, a); ++it) {
+    __nanosleep(32);
+    v = ld_ll(q);
+  }
 }
 
 // Bounded wait for *ctr >= target (a.spin_limit polls).  Gives up early when
@@ -322,20 +373,24 @@ __device__ __forceinline__ void ring_issue(Ring& r, Cur& pc, const StepArgs& a, 
 // dispatched once, and the small loops stay rolled (the epilogue runs once
 // per tile; its code has to stay small, not fast).
 __device__ __forceinline__ void step_epilogue(const StepArgs& a, const GPh& g, int tile, float v00, float v01,
-                                           float v10, float v11, const uint2& hres, int lane) {
+                                           float v10, float v11, const uint2& hres, int lane, uint32_t efl) {
   const int gg = lane >> 2, t4 = lane & 3;
   const int r0 = tile * 16 + gg;
   const int M = a.B;
   const float acc[4] = {v00, v01, v10, v11};
+  // outputs go out as flagged words of two halves: rows r and r + 1 live in
+  // lanes g and g + 1 (four lanes apart), so the even row's lane takes its
+  // neighbour's half and stores the pair
   if (g.kind == 2) {  // SwiGLU: rows g (gate) and g + 8 (up) of the interleaved tile
     const int j = tile * 8 + gg;
-#pragma unroll 1
+#pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int n = 2 * t4 + e;
-      if (n >= M || j >= a.F) continue;
       const float gv = __half2float(__float2half_rn(acc[e]));
       const float uv = __half2float(__float2half_rn(acc[2 + e]));
-      a.sw[(size_t)n * a.F + j] = __float2half_rn(__fmul_rn(silu_f(gv), uv));
+      const uint32_t sv = __half_as_ushort(__float2half_rn(__fmul_rn(silu_f(gv), uv)));
+      const uint32_t nb = __shfl_down_sync(0xffffffffu, sv, 4);
+      if ((gg & 1) == 0 && n < M && j < a.F) st_act(a.sw + ((size_t)n * a.F + j) / 2, sv | (nb << 16), efl);
     }
     return;
   }
@@ -371,29 +426,41 @@ __device__ __forceinline__ void step_epilogue(const StepArgs& a, const GPh& g, i
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const int n = 2 * t4 + (q & 1), row = r0 + 8 * (q >> 1);
-    if (n >= M || row >= g.N) continue;
+    __half nv;
     if (g.kind == 0) {
-      a.qkv[(size_t)n * g.N + row] = __float2half_rn(acc[q]);
+      nv = __float2half_rn(acc[q]);
     } else {  // residual add into h (fp16 GEMV output, fp16 sum); h was read at the tile's start
-      const __half nv = __float2half_rn(__fadd_rn(hrv[q], __half2float(__float2half_rn(acc[q]))));
-      a.h[(size_t)n * a.d + row] = nv;
-      if (g.kind == 3 && a.hdump) a.hdump[((size_t)g.layer * M + n) * a.d + row] = nv;
+      nv = __float2half_rn(__fadd_rn(hrv[q], __half2float(__float2half_rn(acc[q]))));
+      if (g.kind == 3 && a.hdump && n < M && row < g.N) a.hdump[((size_t)g.layer * M + n) * a.d + row] = nv;
+    }
+    const uint32_t sv = __half_as_ushort(nv);
+    const uint32_t nb = __shfl_down_sync(0xffffffffu, sv, 4);
+    if ((gg & 1) == 0 && n < M && row < g.N) {
+      uint2* dst = g.kind == 0 ? a.qkv + ((size_t)n * g.N + row) / 2 : a.h + ((size_t)n * a.d + row) / 2;
+      st_act(dst, sv | (nb << 16), efl);
     }
   }
 }
 
 // The residual values a tile's epilogue adds to (o and down phases): read at
 // the tile's start so the load's latency hides under the tile's k loop.
-__device__ __forceinline__ uint2 residual_of(const StepArgs& a, const GPh& g, int tile, int lane) {
+__device__ __forceinline__ uint2 residual_of(const StepArgs& a, const GPh& g, int tile, int lane, uint32_t rfl) {
   if (g.kind != 1 && g.kind != 3) return make_uint2(0u, 0u);
   const int gg = lane >> 2, t4 = lane & 3, r0 = tile * 16 + gg;
-  __half h[4];
+  uint2 w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {  // all four loads in flight, then the flag checks
+    const int n = 2 * t4 + (q & 1), row = r0 + 8 * (q >> 1);
+    w[q] = (n < a.B && row < g.N) ? ld_act(a.h + ((size_t)n * a.d + row) / 2) : make_uint2(0u, rfl);
+  }
+  uint32_t h[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const int n = 2 * t4 + (q & 1), row = r0 + 8 * (q >> 1);
-    h[q] = (n < a.B && row < g.N) ? __ldcg(a.h + (size_t)n * a.d + row) : __ushort_as_half((unsigned short)0);
+    if (n < a.B && row < g.N) act_wait1(a.h + ((size_t)n * a.d + row) / 2, w[q], rfl, a);
+    h[q] = (w[q].x >> (16 * (row & 1))) & 0xFFFFu;
   }
-  return make_uint2(h2_as_u32(__halves2half2(h[0], h[1])), h2_as_u32(__halves2half2(h[2], h[3])));
+  return make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
 }
 
 // QKV bias (c_attn_bs) is folded in by the QKV tile finisher
@@ -428,23 +495,29 @@ __device__ __forceinline__ void qkv_bias_fix(const StepArgs& a, const GPh& g, in
 // finishes it (deterministic sums).
 template <bool SYM, int GB, bool XS>
 __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, Cur& pc, const __half* xs,
-                                           int xs_stride, const __half* xg, int ldx, float* spart, int wid,
-                                           int lane, bool ok, int* done_ctr, uint32_t fl) {
+                                           int xs_stride, const uint2* xg, int ldx, float* spart, int wid,
+                                           int lane, bool ok, uint32_t epoch) {
   const GPh g = gph(a, ph);
+  const uint32_t fl = epoch * 512u + (uint32_t)ph + 1u;  // split-tile partials (never 0)
+  const uint32_t efl = act_flag(epoch, ph);              // this phase's outputs
+  const uint32_t rfl = act_flag(epoch, ph - 2);          // the residual: h as the phase two back wrote it
+  const uint32_t sfl = act_flag(epoch, ph - 1);          // x read from global memory: the previous phase's output
   const URange wr = warp_range(g.U, blockIdx.x, gridDim.x, wid);
   const uint32_t u0 = wr.u0, u1 = wr.u1;
   const int gq = lane >> 2, t4 = lane & 3;
   const int KB = g.K / 64;
   const int t_first = (int)(u0 / g.upt), t_last = u1 > u0 ? (int)((u1 - 1) / g.upt) : t_first - 1;
   const int nn = min(gq, a.B - 1);
-  const uint4* xrow = reinterpret_cast<const uint4*>((XS ? xs + (size_t)nn * xs_stride : xg + (size_t)nn * ldx) +
-                                                     16 * t4);
-  int finished = 0;
+  // staged x: this lane's 16 halves of a k-block as two 16-byte loads; x in
+  // global memory: the same halves as 8 flagged words (four 16-byte loads,
+  // issued one k-block ahead and checked when used)
+  const uint4* xrow = XS ? reinterpret_cast<const uint4*>(xs + (size_t)nn * xs_stride + 16 * t4) : nullptr;
+  const uint2* xw = XS ? nullptr : xg + (size_t)nn * (ldx / 2) + 8 * t4;
   for (int t = t_first; t <= t_last && ok; ++t) {
     const int kb_lo = (int)max(u0, (uint32_t)(t * g.upt)) * GB;
     const int kb_hi = (int)min(u1, (uint32_t)((t + 1) * g.upt)) * GB;
     const bool complete = (uint32_t)(t * g.upt) >= u0 && (uint32_t)((t + 1) * g.upt) <= u1;
-    const uint2 hres = complete ? residual_of(a, g, t, lane) : make_uint2(0u, 0u);
+    const uint2 hres = complete ? residual_of(a, g, t, lane, rfl) : make_uint2(0u, 0u);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     // two accumulator chains (alternate fragment words) so consecutive MMAs
     // do not wait on each other; SYM restarts them per group, AFFINE (weights
@@ -454,10 +527,10 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
     for (int q = 0; q < 2; ++q)
 #pragma unroll
       for (int e = 0; e < 4; ++e) c[q][e] = 0.f;
-    uint4 xn0 = make_uint4(0, 0, 0, 0), xn1 = xn0;
+    uint4 xn[4];
     if (!XS) {
-      xn0 = __ldcg(xrow + (kb_lo - t * KB) * 8);
-      xn1 = __ldcg(xrow + (kb_lo - t * KB) * 8 + 1);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) xn[i] = ld_ll(reinterpret_cast<const uint4*>(xw + 32 * (kb_lo - t * KB)) + i);
     }
     for (int kb = kb_lo; kb < kb_hi;) {
       const int st = r.cs;
@@ -480,11 +553,15 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
           bf[0] = v0.x; bf[1] = v0.y; bf[2] = v0.z; bf[3] = v0.w;
           bf[4] = v1.x; bf[5] = v1.y; bf[6] = v1.z; bf[7] = v1.w;
         } else {
-          bf[0] = xn0.x; bf[1] = xn0.y; bf[2] = xn0.z; bf[3] = xn0.w;
-          bf[4] = xn1.x; bf[5] = xn1.y; bf[6] = xn1.z; bf[7] = xn1.w;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            act_wait2(xw + 32 * (kbt + j) + 2 * i, xn[i], sfl, a);
+            bf[2 * i] = xn[i].x;
+            bf[2 * i + 1] = xn[i].z;
+          }
           if (kb + j + 1 < kb_hi) {
-            xn0 = __ldcg(xrow + (kbt + j + 1) * 8);
-            xn1 = __ldcg(xrow + (kbt + j + 1) * 8 + 1);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xn[i] = ld_ll(reinterpret_cast<const uint4*>(xw + 32 * (kbt + j + 1)) + i);
           }
         }
         const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
@@ -541,8 +618,7 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
     }
     if (complete) {
       qkv_bias_fix(a, g, t, acc, lane);
-      step_epilogue(a, g, t, acc[0], acc[1], acc[2], acc[3], hres, lane);
-      ++finished;
+      step_epilogue(a, g, t, acc[0], acc[1], acc[2], acc[3], hres, lane, efl);
       continue;
     }
     *reinterpret_cast<float4*>(spart + ((wid * 2 + (t == t_first ? 0 : 1)) * 32 + lane) * 4) =
@@ -563,7 +639,7 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
       const uint32_t ra1 = c0 + (uint32_t)(((unsigned long long)n * (unsigned)(wa + 1)) / we);
       if (wa == wb && ra0 <= ts && ra1 >= te) continue;  // whole in one warp: already finished
       const bool first_cta = p0 == ts;
-      const uint2 hres = first_cta ? residual_of(a, g, t, lane) : make_uint2(0u, 0u);
+      const uint2 hres = first_cta ? residual_of(a, g, t, lane, rfl) : make_uint2(0u, 0u);
       float tot[4] = {0.f, 0.f, 0.f, 0.f};
       for (int w0 = wa; w0 <= wb; ++w0) {
         const uint32_t r0 = c0 + (uint32_t)(((unsigned long long)n * (unsigned)w0) / we);
@@ -606,13 +682,8 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
         if (!ok) break;
       }
       qkv_bias_fix(a, g, t, tot, lane);
-      step_epilogue(a, g, t, tot[0], tot[1], tot[2], tot[3], hres, lane);
-      ++finished;
+      step_epilogue(a, g, t, tot[0], tot[1], tot[2], tot[3], hres, lane, efl);
     }
-  }
-  if (finished) {
-    __syncwarp();
-    if (lane == 0) red_release_add(done_ctr, finished);
   }
   return ok;
 }
@@ -620,7 +691,7 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
 // ------------------------------------------------------------------ staging
 // Embedding rows (dequant_q8_rows, quant.py:132-163) into xs; CTA 0 also
 // stores them into h (the residual stream).
-__device__ __forceinline__ void stage_embed(const StepArgs& a, __half* xs, int stride) {
+__device__ __forceinline__ void stage_embed(const StepArgs& a, __half* xs, int stride, uint32_t efl) {
   const int K4 = a.d / 4;
   for (int i = threadIdx.x; i < a.B * K4; i += blockDim.x) {
     const int m = i / K4, k4 = i % K4;
@@ -638,7 +709,11 @@ __device__ __forceinline__ void stage_embed(const StepArgs& a, __half* xs, int s
     __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
     uint2 pk = make_uint2(h2_as_u32(h01), h2_as_u32(h23));
     *reinterpret_cast<uint2*>(xs + (size_t)m * stride + 4 * k4) = pk;
-    if (blockIdx.x == 0) *reinterpret_cast<uint2*>(a.h + (size_t)m * a.d + 4 * k4) = pk;
+    if (blockIdx.x == 0) {
+      uint2* hp = a.h + ((size_t)m * a.d + 4 * k4) / 2;
+      st_act(hp, pk.x, efl);
+      st_act(hp + 1, pk.y, efl);
+    }
   }
 }
 
@@ -646,22 +721,46 @@ __device__ __forceinline__ void stage_embed(const StepArgs& a, __half* xs, int s
 // from global memory (src), or the raw rows already in xs (src null).  With
 // an RMSNorm weight w (modules.py:30-43: rms = 1/sqrt(mean(x^2) + eps),
 // fp16((x * rms) * w)) the rows are normalized in place.
-__device__ __forceinline__ void stage_x(int B, float eps, const __half* src, int K, const float* w, __half* xs,
-                                        int stride, float* red) {
+//
+// Every warp of the CTA calls it, whatever its own ok (an abort can leave ok
+// different in different warps): the barriers are the same for all, the
+// first one makes ok the CTA's, and the copy is skipped where ok is false.
+__device__ __forceinline__ bool stage_x(const StepArgs& a, int B, float eps, const uint2* src, uint32_t sfl, int K,
+                                        const float* w, __half* xs, int stride, float* red, bool ok) {
   const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, wid = tid >> 5;
-  const int K8 = K / 8;
-  // pass 1: copy (four 16-byte loads in flight per thread) + sums of squares
+  const int K8 = ok ? K / 8 : 0;
+  // pass 1: copy (two 8-half chunks in flight per thread, each two 16-byte
+  // flagged loads, waited for until they carry the producer's flag) + sums
+  // of squares
   for (int m = 0; m < B; ++m) {
-    const uint4* srow = src ? reinterpret_cast<const uint4*>(src + (size_t)m * K) : nullptr;
+    const uint2* srow = src ? src + (size_t)m * (K / 2) : nullptr;
     uint4* drow = reinterpret_cast<uint4*>(xs + (size_t)m * stride);
     float ss = 0.f;
-    for (int c0 = tid; c0 < K8; c0 += 4 * nth) {
-      uint4 v[4];
+    for (int c0 = tid; c0 < K8; c0 += 2 * nth) {
+      uint4 v[2];
+      if (srow) {
+        uint4 raw[2][2];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (c0 + u * nth < K8) v[u] = srow ? __ldcg(srow + c0 + u * nth) : drow[c0 + u * nth];
+        for (int u = 0; u < 2; ++u)  // all four loads in flight, then the flag checks
+          if (c0 + u * nth < K8) {
+            const uint4* q = reinterpret_cast<const uint4*>(srow + 4 * (c0 + u * nth));
+            raw[u][0] = ld_ll(q);
+            raw[u][1] = ld_ll(q + 1);
+          }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 2; ++u)
+          if (c0 + u * nth < K8) {
+            act_wait2(srow + 4 * (c0 + u * nth), raw[u][0], sfl, a);
+            act_wait2(srow + 4 * (c0 + u * nth) + 2, raw[u][1], sfl, a);
+            v[u] = make_uint4(raw[u][0].x, raw[u][0].z, raw[u][1].x, raw[u][1].z);
+          }
+      } else {
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          if (c0 + u * nth < K8) v[u] = drow[c0 + u * nth];
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
         if (c0 + u * nth >= K8) continue;
         if (srow) drow[c0 + u * nth] = v[u];
         const __half2* hh = reinterpret_cast<const __half2*>(&v[u]);
@@ -676,8 +775,8 @@ __device__ __forceinline__ void stage_x(int B, float eps, const __half* src, int
     ss = warp_sum(ss);
     if (lane == 0) red[wid * kStepMaxM + m] = ss;
   }
-  __syncthreads();
-  if (!w) return;
+  ok = __syncthreads_and(ok) != 0;
+  if (!w || !ok) return ok;
   // pass 2: normalize in place
   for (int m = 0; m < B; ++m) {
     float tot = 0.f;
@@ -702,6 +801,7 @@ __device__ __forceinline__ void stage_x(int B, float eps, const __half* src, int
     }
   }
   __syncthreads();
+  return ok;
 }
 
 // ------------------------------------------------------------------ attention
@@ -958,7 +1058,7 @@ __device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint3
 template <int HD, int KVT>
 __device__ __forceinline__ bool attn_item(const StepArgs& a, const StepLayer* ly, int layer, const AttnItem& it,
                                        int nsplit, bool prefetched, char* gsm, char* misc, uint32_t& uses,
-                                       int* done_ctr, bool ok) {
+                                       uint32_t afl, bool ok) {
   constexpr int BX = kv_box_bytes(KVT == AXB_KV_F16 ? HD * 2 : (KVT == AXB_KV_FP8 ? HD : HD / 2));
   constexpr int DPL = HD / 32, KS = HD / 16, OS = HD + 4;  // OS: row stride of the merged O
   constexpr bool quant = KVT != AXB_KV_F16;
@@ -981,13 +1081,13 @@ __device__ __forceinline__ bool attn_item(const StepArgs& a, const StepLayer* ly
 
   // ---- q with RoPE (fp32), as fp16 hi / lo rows; the new K/V row rotated, quantized and written
   const int qkv_dim = (a.Hq + 2 * a.Hkv) * HD;
-  const __half* row = a.qkv + (size_t)it.b * qkv_dim;
+  const uint2* row = a.qkv + (size_t)it.b * qkv_dim / 2;  // flagged words of this token's q, k, v
   const float* fr = a.rope + (size_t)(rpos % a.rope_len) * HD;
   for (int i = tid; i < 8 * HD / 2; i += kSThreads) {
     const int rr = i / (HD / 2), pr = i % (HD / 2);
     float q0 = 0.f, q1 = 0.f;
     if (rr < n_rep) {
-      const __half2 x2 = __ldcg(reinterpret_cast<const __half2*>(row + (hq0 + rr) * HD) + pr);
+      const __half2 x2 = u32_as_h2(act_get(row + (hq0 + rr) * HD / 2 + pr, afl, a));
       const float a0 = __low2float(x2), a1 = __high2float(x2);
       const float cs = fr[2 * pr], sn = fr[2 * pr + 1];
       q0 = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
@@ -1003,9 +1103,13 @@ __device__ __forceinline__ bool attn_item(const StepArgs& a, const StepLayer* ly
   const bool covers = wpos >= it.t0 && wpos < it.t1;
   if (covers && w < 2) {
     float nkv[DPL];
-    const __half* src = row + (size_t)(a.Hq + (w == 0 ? 0 : a.Hkv) + it.kvh) * HD;
+    const uint2* src = row + (size_t)(a.Hq + (w == 0 ? 0 : a.Hkv) + it.kvh) * HD / 2;
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) nkv[e] = __half2float(__ldcg(src + lane * DPL + e));
+    for (int e = 0; e < DPL; e += 2) {
+      const __half2 v2 = u32_as_h2(act_get(src + (lane * DPL + e) / 2, afl, a));
+      nkv[e] = __low2float(v2);
+      nkv[e + 1] = __high2float(v2);
+    }
     if (w == 0) {  // RoPE on K, every product rounded (transformer.py:1105-1127)
 #pragma unroll
       for (int e = 0; e < DPL; e += 2) {
@@ -1154,8 +1258,10 @@ __device__ __forceinline__ bool attn_item(const StepArgs& a, const StepLayer* ly
       Ls = __fmaf_rn(wm[kSW * 8 + v * 8 + r], cw, Ls);
       O = __fmaf_rn(wo[((size_t)v * n_rep + r) * OS + e], cw, O);
     }
-    if (nsplit == 1) {
-      a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, Ls));
+    if (nsplit == 1) {  // adjacent outputs e, e + 1 sit in adjacent lanes: one flagged word
+      const uint32_t hv = __half_as_ushort(__float2half_rn(__fdiv_rn(O, Ls)));
+      const uint32_t nb = __shfl_down_sync(0xffffffffu, hv, 1);
+      if ((e & 1) == 0) st_act(a.attn + ((pidx + r) * HD + e) / 2, hv | (nb << 16), afl);
     } else {
       a.part_o[((pidx + r) * kStepMaxSplits + it.split) * HD + e] = O;
       if (e == 0)
@@ -1163,10 +1269,7 @@ __device__ __forceinline__ bool attn_item(const StepArgs& a, const StepLayer* ly
     }
   }
   __syncthreads();
-  if (nsplit == 1) {
-    if (tid == 0) red_release_add(done_ctr, 1);
-    return true;
-  }
+  if (nsplit == 1) return true;
   // ---- the head's last split to arrive combines it.  The per-head counter
   // only grows during a step (layer l completes at (l + 1) * nsplit arrivals);
   // the step's last CTA clears it.
@@ -1192,10 +1295,11 @@ __device__ __forceinline__ bool attn_item(const StepArgs& a, const StepLayer* ly
       Ls = __fmaf_rn(v.y, cw, Ls);
       O = __fmaf_rn(__ldcg(po + (size_t)sp * HD), cw, O);
     }
-    a.attn[(pidx + r) * HD + e] = __float2half_rn(__fdiv_rn(O, Ls));
+    const uint32_t hv = __half_as_ushort(__float2half_rn(__fdiv_rn(O, Ls)));
+    const uint32_t nb = __shfl_down_sync(0xffffffffu, hv, 1);
+    if ((e & 1) == 0) st_act(a.attn + ((pidx + r) * HD + e) / 2, hv | (nb << 16), afl);
   }
   __syncthreads();
-  if (tid == 0) red_release_add(done_ctr, 1);
   return true;
 }
 
@@ -1203,12 +1307,12 @@ __device__ __forceinline__ bool attn_item(const StepArgs& a, const StepLayer* ly
 // are copied before the layer's QKV phase has finished (they do not depend on
 // it), then the CTA takes items blockIdx.x, + gridDim.x, ...
 template <int HD>
-__device__ __forceinline__ bool attn_phase(const StepArgs& a, int l, char* uni, char* misc, uint32_t& uses, bool ok) {
+__device__ __forceinline__ bool attn_phase(const StepArgs& a, int l, char* uni, char* misc, uint32_t& uses, bool ok,
+                                           uint32_t epoch) {
   const int tid = threadIdx.x, C = gridDim.x;
   const StepLayer* ly = a.layers + l;
-  int* dn = a.done + 1 + 5 * l;
   uint64_t* bar = reinterpret_cast<uint64_t*>(misc + kMiscBar);
-  const int qkv_dim = (a.Hq + 2 * a.Hkv) * a.hd;
+  const uint32_t afl = act_flag(epoch, 4 * l);  // the layer's QKV outputs, and this phase's outputs
   const int active = a.params[2];
   int nsplit, chunk;
   attn_split_plan(active, C / (a.B * a.Hkv), nsplit, chunk);
@@ -1223,8 +1327,7 @@ __device__ __forceinline__ bool attn_phase(const StepArgs& a, int l, char* uni, 
     attn_copy(ly, hb, Lo.np, Lo.bx, Lo.ng, Lo.rb, a.kv_type != AXB_KV_F16, it.t0, min(a.plan.attn_cap, it.t1 - it.t0),
               a.plan.attn_cap, gsm + Lo.kv, gsm + Lo.ksc, gsm + Lo.vsc, bar);
   }
-  ok = cta_wait(dn + 0, tiles_of(qkv_dim), a, ok);
-  trace_mark(a, 1 + 10 * l + 2);
+  trace_mark(a, 1 + 10 * l + 2);  // an item waits for its own head's q, k, v words
   bool first = true;
   for (; item < n_items; item += C) {
     if (!ok) {
@@ -1235,11 +1338,11 @@ __device__ __forceinline__ bool attn_phase(const StepArgs& a, int l, char* uni, 
     }
     const AttnItem it = attn_item_of(item, nsplit, chunk, a.Hkv, active);
     if (a.kv_type == AXB_KV_FP8)
-      ok = attn_item<HD, AXB_KV_FP8>(a, ly, l, it, nsplit, first, gsm, misc, uses, dn + 1, ok);
+      ok = attn_item<HD, AXB_KV_FP8>(a, ly, l, it, nsplit, first, gsm, misc, uses, afl, ok);
     else if (a.kv_type == AXB_KV_INT4)
-      ok = attn_item<HD, AXB_KV_INT4>(a, ly, l, it, nsplit, first, gsm, misc, uses, dn + 1, ok);
+      ok = attn_item<HD, AXB_KV_INT4>(a, ly, l, it, nsplit, first, gsm, misc, uses, afl, ok);
     else
-      ok = attn_item<HD, AXB_KV_F16>(a, ly, l, it, nsplit, first, gsm, misc, uses, dn + 1, ok);
+      ok = attn_item<HD, AXB_KV_F16>(a, ly, l, it, nsplit, first, gsm, misc, uses, afl, ok);
     first = false;
   }
   if (tid == 0) trace_at(a, 4 + 10 * a.L + (4 * a.L + 1) * kStepTraceW + 2 * l);
@@ -1285,7 +1388,6 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   __syncthreads();
 
   bool ok = true;
-  const int t_d = tiles_of(a.d);
   // launch epoch (advanced by the step's last CTA): split-tile partials of
   // GEMV phase ph carry the flag epoch * 512 + ph + 1 (never 0, the value of
   // an unwritten slot)
@@ -1294,9 +1396,8 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
 
   trace_mark(a, 0);
   // embedding rows for the first layer's QKV (every CTA stages its own copy)
-  stage_embed(a, xs, xs_stride);
+  stage_embed(a, xs, xs_stride, act_flag(epoch, -1));
   __syncthreads();
-  if (blockIdx.x == 0 && tid == 0) red_release_add(a.done, 1);
 
   // GEMV phases in order: p = 4 l + {0 QKV, 1 o, 2 gate_up, 3 down}, 4 L = lm_head;
   // attention runs between a layer's QKV and o phases.  One loop, so every
@@ -1306,44 +1407,35 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     const StepLayer* ly = a.layers + (kind == 4 ? 0 : l);
     int* dn = a.done + 1 + 5 * l;  // QKV, attention, o, gate_up, down counters of layer l
     const int ts = 1 + 10 * l;
-    // ---- wait for the phase's input; its source, width and RMSNorm weight
-    const __half* src;
+    // ---- the phase's input: its source, width and RMSNorm weight.  There is
+    // no wait here: the staging (or the GEMV's own x loads) waits for the
+    // words of the previous phase's output to carry that phase's flag.
+    const uint2* src;
     const float* nw = nullptr;
-    int K, *done_ctr;
+    int K;
     if (kind == 0) {  // QKV: RMSNorm(h) (the embedding rows already in xs for layer 0)
-      if (l > 0) ok = cta_wait(dn - 1, t_d, a, ok);
       trace_mark(a, ts + 0);
       src = l > 0 ? a.h : nullptr;
       K = a.d;
       nw = ly->ln1;
-      done_ctr = dn;
     } else if (kind == 1) {  // o: attention output (+ residual)
-      ok = cta_wait(dn + 1, a.B * a.Hkv, a, ok);     // every head combined
-      if (l == 0) ok = cta_wait(a.done, 1, a, ok);  // h holds the embedding rows
       trace_mark(a, ts + 4);
       src = a.attn;
       K = a.Hq * a.hd;
-      done_ctr = dn + 2;
     } else if (kind == 2) {  // gate_up: RMSNorm(h), SwiGLU epilogue
-      ok = cta_wait(dn + 2, t_d, a, ok);
       trace_mark(a, ts + 6);
       src = a.h;
       K = a.d;
       nw = ly->ln2;
-      done_ctr = dn + 3;
     } else if (kind == 3) {  // down: SwiGLU output (+ residual)
-      ok = cta_wait(dn + 3, tiles_of(2 * a.F), a, ok);
       trace_mark(a, ts + 8);
       src = a.sw;
       K = a.F;
-      done_ctr = dn + 4;
     } else {  // lm_head: final RMSNorm(h); with no layers h holds CTA 0's embedding rows
-      ok = a.L > 0 ? cta_wait(a.done + 5 * a.L, t_d, a, ok) : cta_wait(a.done, 1, a, ok);
       trace_mark(a, 1 + 10 * a.L);
       src = a.h;
       K = a.d;
       nw = a.ln_f;
-      done_ctr = a.done + 1 + 5 * a.L;
     }
     // ---- the GEMV: activations staged in shared memory when they fit (always
     // for the normalized inputs), else read from L2 one k-block ahead
@@ -1356,19 +1448,17 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
       ok = false;
     }
     if (staged) {
-      if (ok) stage_x(a.B, a.eps, src, K, nw, xs, K + 8, red);
-      ok = gemv_phase<SYM, GB, true>(a, ph, ring, pc, xs, K + 8, nullptr, 0, spart, wid, lane, ok, done_ctr,
-                                     epoch * 512u + (uint32_t)ph + 1u);
+      ok = stage_x(a, a.B, a.eps, src, act_flag(epoch, ph - 1), K, nw, xs, K + 8, red, ok);
+      ok = gemv_phase<SYM, GB, true>(a, ph, ring, pc, xs, K + 8, nullptr, 0, spart, wid, lane, ok, epoch);
     } else {
-      ok = gemv_phase<SYM, GB, false>(a, ph, ring, pc, nullptr, 0, src, K, spart, wid, lane, ok, done_ctr,
-                                      epoch * 512u + (uint32_t)ph + 1u);
+      ok = gemv_phase<SYM, GB, false>(a, ph, ring, pc, nullptr, 0, src, K, spart, wid, lane, ok, epoch);
     }
     if (lane == 0) trace_at(a, 4 + 10 * a.L + ph * kStepTraceW + wid);  // this warp's share done
     trace_mark(a, kind == 4 ? 2 + 10 * a.L : ts + (kind == 0 ? 1 : 2 * kind + 3));  // QKV, o, gate_up, down done
     if (kind != 0) continue;
     // ---- attention of layer l (RoPE + KV write fused)
     ok = __syncthreads_and(ok) != 0;  // the staged rows are dead: the union holds attention next
-    ok = attn_phase<HD>(a, l, uni, misc, abar_uses, ok);
+    ok = attn_phase<HD>(a, l, uni, misc, abar_uses, ok, epoch);
     trace_mark(a, ts + 3);
   }
 

@@ -50,11 +50,12 @@ struct StepArgs {
   const int32_t* tokens;
   const int32_t* params;  // rope_pos, write_pos, active_len, prefix_len
   int* err;
-  // activations
-  __half* h;       // (B, d) residual stream
-  __half* qkv;     // (B, (Hq + 2 Hkv) hd)
-  __half* attn;    // (B, Hq hd)
-  __half* sw;      // (B, F)
+  // activations, as flagged words: word i of a row holds halves 2i, 2i + 1 and
+  // the flag of the phase that wrote them (the reader waits for the flag)
+  uint2* h;        // (B, d / 2) residual stream
+  uint2* qkv;      // (B, (Hq + 2 Hkv) hd / 2)
+  uint2* attn;     // (B, Hq hd / 2)
+  uint2* sw;       // (B, F / 2)
   __half* logits;  // (B, V)
   int32_t* amax;   // (B,)
   // scratch (zeroed once; every counter returns to zero by the end of a step)
