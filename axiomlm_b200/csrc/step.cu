@@ -1279,27 +1279,55 @@ __device__ __forceinline__ bool attn_item(const StepArgs& a, const StepLayer* ly
   }
   __syncthreads();
   if (!*flag) return true;
-  for (int i = tid; i < n_rep * HD; i += kSThreads) {
-    const int r = i / HD, e = i % HD;
-    const size_t hb = (pidx + r) * kStepMaxSplits;
-    const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + hb;
-    const float* po = a.part_o + hb * HD + e;
-    float M = -INFINITY;
-#pragma unroll 4
-    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(&ml[sp].x));
-    float Ls = 0.f, O = 0.f;
-#pragma unroll 4
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float2 v = __ldcg(ml + sp);
-      const float cw = v.x == -INFINITY ? 0.f : __expf(v.x - M);
-      Ls = __fmaf_rn(v.y, cw, Ls);
-      O = __fmaf_rn(__ldcg(po + (size_t)sp * HD), cw, O);
+  // The splits' partials are staged in shared memory first, all loads of a
+  // batch in flight at once: every (m, l), then the head group's O rows in
+  // groups of gs splits (all of them when they fit, the usual case).  The
+  // sums are the same as reading the partials one by one: M over all splits,
+  // then l and O accumulated in split order.  One output per thread
+  // (n_rep <= 4, HD <= 128).
+  static_assert(4 * HD <= kSThreads, "one combined output per thread");
+  const int mlb = round_up_i(n_rep * nsplit * 8, 16);
+  float2* sml = reinterpret_cast<float2*>(gsm + Lo.kv);  // [n_rep][nsplit]
+  float4* so4 = reinterpret_cast<float4*>(gsm + Lo.kv + mlb);  // [n_rep][gs][HD / 4]
+  const int gs = min(nsplit, (Lo.ksc - Lo.kv - mlb) / (n_rep * HD * 4));
+  for (int i = tid; i < n_rep * nsplit; i += kSThreads) {
+    const int hr = i / nsplit, sp = i - hr * nsplit;
+    sml[i] = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + (pidx + hr) * kStepMaxSplits + sp);
+  }
+  const bool mine = tid < n_rep * HD;
+  const int r = tid / HD, e = tid % HD;
+  float M = -INFINITY, Ls = 0.f, O = 0.f;
+  for (int s0 = 0; s0 < nsplit; s0 += gs) {
+    const int ns = min(gs, nsplit - s0), per = ns * (HD / 4), n4 = n_rep * per;
+    for (int i = tid; i < n4; i += kSThreads) {  // 16-byte async copies through L2: no registers held
+      const int hr = i / per;
+      cp_async16(so4 + hr * gs * (HD / 4) + (i - hr * per),
+                 reinterpret_cast<const float4*>(a.part_o + ((pidx + hr) * kStepMaxSplits + s0) * HD) + (i - hr * per));
     }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    if (mine) {
+      if (s0 == 0) {
+#pragma unroll 4
+        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, sml[r * nsplit + sp].x);
+      }
+      const float* so = reinterpret_cast<const float*>(so4) + (size_t)r * gs * HD + e;
+#pragma unroll 4
+      for (int sp = 0; sp < ns; ++sp) {
+        const float2 v = sml[r * nsplit + s0 + sp];
+        const float cw = v.x == -INFINITY ? 0.f : __expf(v.x - M);
+        Ls = __fmaf_rn(v.y, cw, Ls);
+        O = __fmaf_rn(so[sp * HD], cw, O);
+      }
+    }
+    __syncthreads();
+  }
+  if (mine) {  // n_rep * HD is a multiple of 32: whole warps
     const uint32_t hv = __half_as_ushort(__float2half_rn(__fdiv_rn(O, Ls)));
     const uint32_t nb = __shfl_down_sync(0xffffffffu, hv, 1);
     if ((e & 1) == 0) st_act(a.attn + ((pidx + r) * HD + e) / 2, hv | (nb << 16), afl);
   }
-  __syncthreads();
   return true;
 }
 
