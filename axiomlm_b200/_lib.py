@@ -105,6 +105,7 @@ class ModelCfg(C.Structure):
         ("ffn", i32), ("vocab", i32), ("eps", f32), ("wfmt", i32), ("group", i32), ("lm_fmt", i32),
         ("lm_group", i32), ("kv_type", i32), ("kv_group", i32), ("max_batch", i32), ("max_seq", i32),
         ("max_tokens", i32), ("rope_len", i32), ("has_qkv_bias", i32), ("tp_world", i32), ("tp_rank", i32),
+        ("dn_fmt", i32), ("dn_group", i32),
     ]
 
 

@@ -10,7 +10,9 @@
 // as dequantize_q8_g64 does (quant.py:132-147): fp16(fp32(q) * fp32(s) +
 // fp32(b)), the product exact in fp32 and the sum rounded to fp32, then to
 // fp16; the products with the fp16 activations accumulate in fp32 and the
-// output is rounded to fp16 once, as F.linear in fp16 does.
+// output is rounded to fp16 once, as F.linear in fp16 does.  An optional
+// bias is added to that fp16 output and rounded again, as _qlin does for Q8
+// projections (transformer.py:1026-1029: y = qmv_q8_g64(x) + bias, in fp16).
 //
 // One warp per output row at a time: lane l reads 16 codes (one 16-byte load)
 // at k = 16 (l + 32 i), the four lanes of a 64-wide group share its scale and
@@ -31,11 +33,13 @@ __device__ __forceinline__ float q8_weight(uint32_t word, int byte, float s, flo
   return __half2float(__float2half_rn(__fadd_rn(__fmul_rn(q, s), b)));
 }
 
-// x: (M, ldx) fp16 rows, w: (N, K/4) int32, sb: (N, K/64) half2, y: (M, ldy) fp16
+// x: (M, ldx) fp16 rows, w: (N, K/4) int32, sb: (N, K/64) half2, y: (M, ldy) fp16,
+// bias: (N) fp16 or null
 __global__ void __launch_bounds__(kQ8Warps * 32) q8_gemv_kernel(const __half* __restrict__ x, int ldx, int m0,
                                                                    int Mb, int K, const uint32_t* __restrict__ w,
                                                                    const __half2* __restrict__ sb, int N,
-                                                                   __half* __restrict__ y, int ldy) {
+                                                                   __half* __restrict__ y, int ldy,
+                                                                   const __half* __restrict__ bias) {
   extern __shared__ __align__(16) __half xs[];  // (Mb, K)
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < Mb * K / 8; i += blockDim.x) {
@@ -79,13 +83,17 @@ __global__ void __launch_bounds__(kQ8Warps * 32) q8_gemv_kernel(const __half* __
     for (int m = 0; m < kQ8MaxMb; ++m) {
       if (m >= Mb) break;
       const float v = warp_sum(acc[m]);
-      if (lane == 0) y[(size_t)(m0 + m) * ldy + row] = __float2half_rn(v);
+      if (lane == 0) {
+        __half o = __float2half_rn(v);
+        if (bias) o = __float2half_rn(__fadd_rn(__half2float(o), __half2float(bias[row])));
+        y[(size_t)(m0 + m) * ldy + row] = o;
+      }
     }
   }
 }
 
 int q8_gemv(const __half* x, int ldx, int M, int K, const uint32_t* w, const __half2* sb, int N, __half* y, int ldy,
-            cudaStream_t st) {
+            cudaStream_t st, const __half* bias) {
   AXB_CHECK_ARG(x && w && sb && y, "q8_gemv: null pointer");
   AXB_CHECK_ARG(M >= 1 && N >= 1 && K >= 64 && K % 64 == 0 && ldx >= K && ldy >= N && ldx % 8 == 0,
                 "q8_gemv: bad shape (M %d, N %d, K %d, ldx %d, ldy %d)", M, N, K, ldx, ldy);
@@ -105,7 +113,7 @@ int q8_gemv(const __half* x, int ldx, int M, int K, const uint32_t* w, const __h
   for (int m0 = 0; m0 < M; m0 += kQ8MaxMb) {
     const int Mb = std::min(kQ8MaxMb, M - m0);
     q8_gemv_kernel<<<blocks, kQ8Warps * 32, (size_t)Mb * K * sizeof(__half), st>>>(x, ldx, m0, Mb, K, w, sb, N, y,
-                                                                                     ldy);
+                                                                                     ldy, bias);
     if (int rc = cuda_status(cudaGetLastError(), "q8_gemv launch")) return rc;
   }
   return AXB_OK;
@@ -117,5 +125,5 @@ extern "C" int axb_q8g64_gemv(const void* x, int ldx, int M, int K, const int32_
                               const uint16_t* scales_biases, int N, void* y, int ldy, void* stream) {
   return axb::q8_gemv(static_cast<const __half*>(x), ldx, M, K, reinterpret_cast<const uint32_t*>(w_packed),
                       reinterpret_cast<const __half2*>(scales_biases), N, static_cast<__half*>(y), ldy,
-                      static_cast<cudaStream_t>(stream));
+                      static_cast<cudaStream_t>(stream), nullptr);
 }

@@ -34,7 +34,7 @@ struct DecodeFuse {
 int attention_fused(const axb_attn_desc* d, const DecodeFuse& f, cudaStream_t s);
 int attn_prepare();
 int q8_gemv(const __half* x, int ldx, int M, int K, const uint32_t* w, const __half2* sb, int N, __half* y, int ldy,
-            cudaStream_t st);
+            cudaStream_t st, const __half* bias = nullptr);
 size_t attn_workspace(int B, int n_head, int head_dim, int max_splits);
 int tree_splits(int B, int T, int n_head, int n_kv_head, int n_keys);
 size_t tree_workspace(int B, int T, int n_head, int head_dim, int nsplit);
@@ -55,6 +55,16 @@ __global__ void swiglu_packed_kernel(const __half* __restrict__ gu, int ld, int 
     const int m = (int)(i / F), j = (int)(i % F);
     const int p = (j >> 3) * 16 + (j & 7);
     const float g = __half2float(gu[(size_t)m * ld + p]), u = __half2float(gu[(size_t)m * ld + p + 8]);
+    sw[(size_t)m * F + j] = __float2half_rn(__fmul_rn(silu_f(g), u));
+  }
+}
+// gate rows first, then up rows (the reference's gate_up = cat(w_gate, w_up),
+// transformer.py:959-964, as Q8 projections keep it): sw[m][j] = fp16(silu(g) * u)
+__global__ void swiglu_split_kernel(const __half* __restrict__ gu, int ld, int F, int rows, __half* __restrict__ sw) {
+  const size_t total = (size_t)rows * F;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / F), j = (int)(i % F);
+    const float g = __half2float(gu[(size_t)m * ld + j]), u = __half2float(gu[(size_t)m * ld + F + j]);
     sw[(size_t)m * F + j] = __float2half_rn(__fmul_rn(silu_f(g), u));
   }
 }
@@ -254,7 +264,8 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.tp_part = take(c.tp_world > 1 ? rows * c.d_model * 4 : 0);
   // tensor-core path (rows > 16): gate_up output in packed order, tcgen05 workspace
   const bool tc = rows > kTcMinRows && c.tp_world <= 1;
-  L.gu_tmp = take(tc ? rows * 2 * (size_t)c.ffn * 2 : 0);
+  // (Q8 gate_up projections also leave their product there before the SwiGLU pass)
+  L.gu_tmp = take(tc || c.wfmt == AXB_W_Q8_G64 ? rows * 2 * (size_t)c.ffn * 2 : 0);
   size_t tcw = 0;
   if (tc) {
     const int qd_ = c.n_head * c.head_dim;
@@ -334,6 +345,7 @@ struct Runner {
 
   int gemv(const void* w, const void* s, int fmt, int group, int N, int K, int M, const __half* x, int ldx,
            void* y, int ldy, const void* bias, const float* norm_w, int epi, int gu, cudaStream_t st) const {
+    if (fmt == AXB_W_Q8_G64) return q8_proj(w, s, N, K, M, x, ldx, y, ldy, bias, norm_w, epi, st);
     // rows beyond 64 are processed in 64-row chunks (one weight pass each)
     for (int m0 = 0; m0 < M; m0 += 64) {
       axb_qgemm_desc d = {};
@@ -363,11 +375,40 @@ struct Runner {
     return AXB_OK;
   }
 
+  // Q8_G64 projections (the reference's q8 and q4_k_m modes, transformer.py:847-858):
+  // the GEMV rounds its product to fp16 (then adds the bias and rounds again,
+  // as _qlin does), and the residual add or SwiGLU runs as its own pass with
+  // the rounding of the fused Q4 epilogues.  The product lands in h (free
+  // during the o / down projections) or gu_tmp (gate_up).
+  int q8_proj(const void* w, const void* s, int N, int K, int M, const __half* x, int ldx, void* y, int ldy,
+              const void* bias, const float* norm_w, int epi, cudaStream_t st) const {
+    const uint32_t* w8 = static_cast<const uint32_t*>(w);
+    const __half2* s8 = static_cast<const __half2*>(s);
+    const __half* b = static_cast<const __half*>(bias);
+    AXB_CHECK_ARG(norm_w == nullptr, "runner: Q8 projections take normalized rows");
+    if (epi == AXB_EPI_STORE) return q8_gemv(x, ldx, M, K, w8, s8, N, static_cast<__half*>(y), ldy, st, b);
+    const int grid = std::min((M * N + 255) / 256, 4 * num_sms());
+    if (epi == AXB_EPI_RESIDUAL) {
+      AXB_CHECK_ARG(ldy == N && N == c.d_model, "runner: Q8 residual projection shape");
+      if (int rc = q8_gemv(x, ldx, M, K, w8, s8, N, buf<__half>(L.h), N, st, b)) return rc;
+      residual_add_kernel<<<grid, 256, 0, st>>>(static_cast<__half*>(y), buf<__half>(L.h), M * N);
+      return launch_status("q8 residual add");
+    }
+    if (epi == AXB_EPI_SWIGLU) {
+      AXB_CHECK_ARG(N == 2 * c.ffn && ldy == c.ffn && L.gu_tmp, "runner: Q8 gate_up projection shape");
+      if (int rc = q8_gemv(x, ldx, M, K, w8, s8, N, buf<__half>(L.gu_tmp), N, st, b)) return rc;
+      swiglu_split_kernel<<<grid, 256, 0, st>>>(buf<__half>(L.gu_tmp), N, c.ffn, M, static_cast<__half*>(y));
+      return launch_status("q8 swiglu");
+    }
+    set_error("runner: epilogue %d is not available for Q8 projections", epi);
+    return AXB_EINVAL;
+  }
+
   // norm + GEMV: fused prologue when the normalized rows fit in shared memory
   int norm_gemv(const float* nw, const void* w, const void* s, int N, int K, int M, void* y, int ldy,
                 const void* bias, int epi, int gu, int fmt, int group, cudaStream_t st) const {
     const __half* x = buf<__half>(L.x);
-    if (qgemm_can_fuse_norm(M, K))
+    if (fmt != AXB_W_Q8_G64 && qgemm_can_fuse_norm(M, K))
       return gemv(w, s, fmt, group, N, K, M, x, K, y, ldy, bias, nw, epi, gu, st);
     int rc = rmsnorm(x, nw, M, K, c.eps, buf<__half>(L.h), st);
     if (rc) return rc;
@@ -381,6 +422,7 @@ struct Runner {
   bool tc_ok = true;  // env AXB_TC=0 keeps many-token steps on the warp-level GEMV
   bool use_tc(int rows) const {
     return tc_ok && rows > kTcMinRows && c.tp_world <= 1 && L.tc_ws_bytes > 0 && tc_fmt(c.wfmt, c.group) &&
+           tc_fmt(c.dn_fmt, c.dn_group) &&
            tc_fmt(c.lm_fmt, c.lm_group);
   }
 
@@ -420,10 +462,11 @@ struct Runner {
   // x += W a for the o / down projections.  Tensor parallel: this rank's
   // K-slice gives an fp32 partial, the ranks' partials meet in one allreduce,
   // then the residual add rounds as the single-GPU path does.
-  int row_parallel(const void* w, const void* s, int K, int rows, const __half* act, cudaStream_t st) const {
+  int row_parallel(const void* w, const void* s, int fmt, int group, int K, int rows, const __half* act,
+                   cudaStream_t st) const {
     const int d = c.d_model;
     if (use_tc(rows)) {  // h is free here: the product lands there, then the residual add
-      int rc = tc_gemm(w, s, c.wfmt, c.group, d, K, rows, act, K, buf<__half>(L.h), d, nullptr, st);
+      int rc = tc_gemm(w, s, fmt, group, d, K, rows, act, K, buf<__half>(L.h), d, nullptr, st);
       if (rc) return rc;
       const int n = rows * d;
       residual_add_kernel<<<std::min((n + 255) / 256, 4 * num_sms()), 256, 0, st>>>(buf<__half>(L.x),
@@ -431,9 +474,8 @@ struct Runner {
       return launch_status("residual add");
     }
     if (c.tp_world <= 1)
-      return gemv(w, s, c.wfmt, c.group, d, K, rows, act, K, buf<void>(L.x), d, nullptr, nullptr, AXB_EPI_RESIDUAL, 0,
-                  st);
-    int rc = gemv(w, s, c.wfmt, c.group, d, K, rows, act, K, buf<void>(L.tp_part), d, nullptr, nullptr,
+      return gemv(w, s, fmt, group, d, K, rows, act, K, buf<void>(L.x), d, nullptr, nullptr, AXB_EPI_RESIDUAL, 0, st);
+    int rc = gemv(w, s, fmt, group, d, K, rows, act, K, buf<void>(L.tp_part), d, nullptr, nullptr,
                   AXB_EPI_F32_ACC, 0, st);
     if (rc) return rc;
     rc = tp_allreduce(tp_comm, buf<void>(L.tp_part), (size_t)rows * d, AXB_TP_SUM_F32, st);
@@ -519,7 +561,7 @@ struct Runner {
         rc = attention_fused(&ad, f, st);
       }
       if (rc) return rc;
-      rc = row_parallel(o_w[l], o_s[l], qd, rows, buf<__half>(L.attn), st);
+      rc = row_parallel(o_w[l], o_s[l], c.wfmt, c.group, qd, rows, buf<__half>(L.attn), st);
       if (rc) return rc;
       if (use_tc(rows)) {
         rc = norm_tc(ln2[l], gu_w[l], gu_s[l], c.wfmt, c.group, 2 * c.ffn, d, rows, buf<__half>(L.gu_tmp), 2 * c.ffn,
@@ -534,7 +576,7 @@ struct Runner {
                        1, c.wfmt, c.group, st);
       }
       if (rc) return rc;
-      rc = row_parallel(dn_w[l], dn_s[l], c.ffn, rows, buf<__half>(L.sw), st);
+      rc = row_parallel(dn_w[l], dn_s[l], c.dn_fmt, c.dn_group, c.ffn, rows, buf<__half>(L.sw), st);
       if (rc) return rc;
     }
     int rc;
@@ -592,7 +634,14 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
                 "runner_create: tensor parallel needs a rank in [0, tp_world) and a communicator");
   AXB_CHECK_ARG(c.n_head * c.head_dim * tpw == c.d_model,
                 "runner_create: n_head * head_dim * tp_world must equal d_model");
-  AXB_CHECK_ARG(c.wfmt == AXB_W_Q4T_SYM || c.wfmt == AXB_W_Q4T_AFFINE, "runner_create: unsupported weight format");
+  AXB_CHECK_ARG(c.wfmt == AXB_W_Q4T_SYM || c.wfmt == AXB_W_Q4T_AFFINE ||
+                    (c.wfmt == AXB_W_Q8_G64 && c.group == 64 && c.tp_world <= 1),
+                "runner_create: unsupported weight format %d", c.wfmt);
+  // the down projection: the projections' format, or Q8_G64 (the q4_k_m mode)
+  const int dn_fmt = c.dn_fmt ? c.dn_fmt : c.wfmt, dn_group = c.dn_fmt ? c.dn_group : c.group;
+  AXB_CHECK_ARG((dn_fmt == c.wfmt && dn_group == c.group) ||
+                    (dn_fmt == AXB_W_Q8_G64 && dn_group == 64 && c.tp_world <= 1),
+                "runner_create: down projection format %d (group %d) not supported", dn_fmt, dn_group);
   AXB_CHECK_ARG(c.lm_fmt == AXB_W_Q4T_SYM || c.lm_fmt == AXB_W_Q4T_AFFINE ||
                     (c.lm_fmt == AXB_W_Q8_G64 && c.lm_group == 64 && c.tp_world <= 1),
                 "runner_create: lm_head format %d not supported by the runner", c.lm_fmt);
@@ -612,6 +661,8 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   if (int rc = attn_prepare()) return rc;
   Runner* r = new Runner();
   r->c = c;
+  r->c.dn_fmt = dn_fmt;
+  r->c.dn_group = dn_group;
   if (c.tp_world <= 1) {
     r->c.tp_world = 1;
     r->c.tp_rank = 0;
@@ -656,7 +707,7 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   const char* sv = getenv("AXB_STEP");
   const StepPlan plan = step_plan(c.max_batch, c.d_model, c.ffn, c.n_head, c.n_kv_head, c.head_dim, c.kv_type,
                                   c.kv_type == AXB_KV_F16 ? c.head_dim : c.kv_group, c.group, c.max_seq);
-  r->step_ok = !(sv && atoi(sv) == 0) && c.tp_world <= 1 &&
+  r->step_ok = !(sv && atoi(sv) == 0) && c.tp_world <= 1 && dn_fmt == c.wfmt &&
                step_supported(c.wfmt, c.group, c.lm_fmt, c.lm_group, c.head_dim, c.n_head, c.n_kv_head, c.d_model,
                               c.kv_type, c.kv_group, c.max_seq) &&
                c.ffn % 64 == 0 && plan.smem > 0;

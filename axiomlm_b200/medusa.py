@@ -208,6 +208,8 @@ class MedusaHeads:
         from .model import WEIGHT_FORMATS
 
         fmt, group = WEIGHT_FORMATS[weight_format]
+        if fmt not in (L.W_Q4T_SYM, L.W_Q4T_AFFINE):
+            raise NotImplementedError(f"Medusa heads are served in the Q4 formats, not {weight_format!r}")
         sym = fmt == L.W_Q4T_SYM
         dev = torch.device(kw.pop("device", "cuda"))
         packed = []

@@ -24,6 +24,9 @@ WEIGHT_FORMATS = {
     "q4_rtn": (L.W_Q4T_AFFINE, 64),
     # BASELINE config: symmetric, group 128, fp16 scales (4.125 bits/weight)
     "q4_g128_sym": (L.W_Q4T_SYM, 128),
+    # reference q8: every projection and the lm_head Q8_G64 in its own layout
+    # (transformer.py:847-855), gate_up as cat(w_gate, w_up)
+    "q8": (L.W_Q8_G64, 64),
 }
 
 
@@ -72,7 +75,8 @@ class QuantizedDecoder:
                        group=wq.group, tp_world=world, tp_rank=tp.rank if tp is not None else 0,
                        lm_fmt=lm.fmt, lm_group=lm.group, kv_type=L.KV_TYPES[self.cache.cache_dtype],
                        kv_group=self.cache.kv_group, max_batch=max_batch, max_seq=max_seq, max_tokens=max_tokens,
-                       rope_len=self.rope_len, has_qkv_bias=int(lay[0].get("qkv_b") is not None))
+                       rope_len=self.rope_len, has_qkv_bias=int(lay[0].get("qkv_b") is not None),
+                       dn_fmt=lay[0]["down"].fmt, dn_group=lay[0]["down"].group)
         self._cfg_c = c
         lib = L.load()
         nbytes = lib.axb_runner_workspace_bytes(C.byref(c))
@@ -128,7 +132,8 @@ class QuantizedDecoder:
         layout) on the GPU, following ``_ensure_quant_weights`` in q4_rtn
         mode (transformer.py:822-1008): projections and an untied lm_head in
         Q4, token embeddings in Q8_G64 (also the lm_head when the embeddings are
-        tied), RMSNorm weights kept fp32."""
+        tied), RMSNorm weights kept fp32.  ``weight_format="q8"`` packs every
+        projection and the lm_head Q8_G64 (the reference's q8 mode)."""
         dev = torch.device(kw.get("device", "cuda"))
         fmt, group = WEIGHT_FORMATS[weight_format]
         sym = fmt == L.W_Q4T_SYM
@@ -137,18 +142,23 @@ class QuantizedDecoder:
         def g(t):
             return t.to(dev, torch.float32)
 
+        def pack(w, gate_up=False):
+            if fmt == L.W_Q8_G64:
+                return ops.Q8Weight(*ops.pack_q8_g64(w), w.shape[0], w.shape[1])
+            return ops.pack_q4t(w, group, sym, gate_up=gate_up)
+
         layers = []
         for lw in weights["layers"]:
             gu = torch.cat([g(lw["w_gate"]), g(lw["w_up"])], 0)
             layers.append(dict(
-                qkv=ops.pack_q4t(g(lw["c_attn"]), group, sym), o=ops.pack_q4t(g(lw["c_proj"]), group, sym),
-                gu=ops.pack_q4t(gu, group, sym, gate_up=True), down=ops.pack_q4t(g(lw["w_down"]), group, sym),
-                ln_1=g(lw["ln_1"]).contiguous(), ln_2=g(lw["ln_2"]).contiguous(), qkv_b=None))
+                qkv=pack(g(lw["c_attn"])), o=pack(g(lw["c_proj"])), gu=pack(gu, gate_up=True),
+                down=pack(g(lw["w_down"])), ln_1=g(lw["ln_1"]).contiguous(), ln_2=g(lw["ln_2"]).contiguous(),
+                qkv_b=None))
             del gu
         emb_w, emb_s = ops.pack_q8_g64(g(weights["wte"]))
         # tied embeddings (transformer.py:842-847): the Q8_G64 embedding matrix is the lm_head
         lm = (ops.Q8Weight(emb_w, emb_s, emb_w.shape[0], emb_w.shape[1] * 4) if tied
-              else ops.pack_q4t(g(weights["lm_head"]), group, sym))
+              else pack(g(weights["lm_head"])))
         packed = dict(layers=layers, emb_w=emb_w, emb_s=emb_s, lm_head=lm, ln_f=g(weights["ln_f"]).contiguous())
         dec = cls(cfg, packed, **kw)
         if weights.get("medusa"):
@@ -160,46 +170,65 @@ class QuantizedDecoder:
     @classmethod
     def from_reference(cls, model: Any, **kw) -> "QuantizedDecoder":
         """Serve a reference ``Transformer`` after ``model.quantize("q4" |
-        "q4_rtn" | "q4_legacy")``: its packed MARLIN or legacy Q4_G64 tensors
-        are relaid out bit-exactly; a Q8_G64 lm_head (tied embeddings) runs on
-        the Q8 GEMV."""
-        dev = torch.device(kw.get("device", "cuda"))
+        "q4_k_m" | "q4_rtn" | "q4_legacy" | "q8")``, the modes its quantized
+        forward and decode runner take (transformer.py:797-799, 1227-1236):
+        its own packed tensors (``_ensure_quant_weights``) are served by
+        ``from_packed``."""
         mc = model.config
         qw = model._ensure_quant_weights(torch.device("cpu"))
         H = mc.n_head
-        Hkv = mc.n_kv_head or H
-        hd = mc.n_embd // H
-        cfg = dict(n_layer=mc.n_layer, d_model=mc.n_embd, n_head=H, n_kv_head=Hkv, ffn=qw["hidden_dim"],
-                   vocab=mc.vocab_size, eps=mc.rms_norm_eps, theta=mc.rope_theta, rope_scaling=mc.rope_scaling,
-                   block_size=mc.block_size)
+        cfg = dict(n_layer=mc.n_layer, d_model=mc.n_embd, n_head=H, n_kv_head=mc.n_kv_head or H,
+                   ffn=qw["hidden_dim"], vocab=mc.vocab_size, eps=mc.rms_norm_eps, theta=mc.rope_theta,
+                   rope_scaling=mc.rope_scaling, block_size=mc.block_size)
+        return cls.from_packed(cfg, qw, [b.ln_1.weight for b in model.transformer.h],
+                               [b.ln_2.weight for b in model.transformer.h], model.transformer.ln_f.weight, **kw)
+
+    @classmethod
+    def from_packed(cls, cfg: dict, qw: dict, ln_1: list, ln_2: list, ln_f, **kw) -> "QuantizedDecoder":
+        """Serve the reference's packed tensors (the dict of
+        ``_ensure_quant_weights``, transformer.py:822-1008) with its RMSNorm
+        weights.  Per projection, by shape: MARLIN Q4 ("q4", "q4_k_m",
+        "q4_rtn") and legacy Q4_G64 ("q4_legacy") are relaid out bit-exactly
+        into q4t; Q8_G64 ("q8"; w_down in "q4_k_m") and a Q8_G64 lm_head (tied
+        embeddings, "q8", "q4_k_m") run on the Q8 GEMV in the reference's own
+        layout."""
+        dev = torch.device(kw.get("device", "cuda"))
+        H, Hkv, d = cfg["n_head"], cfg["n_kv_head"], cfg["d_model"]
+        hd = d // H
         qkv_dim = (H + 2 * Hkv) * hd
+
+        def rl(p, s, n, gu=False):
+            p = torch.as_tensor(p)
+            s = torch.as_tensor(s)
+            if p.ndim == 4:  # MARLIN ladder
+                return ops.q4t_from_marlin(p.to(dev), s.to(dev), n, gate_up=gu)
+            if p.shape[1] * 4 == s.shape[1] * 64:  # Q8_G64 (N, K/4) words: kept as packed
+                return ops.Q8Weight(p.to(dev).contiguous(), s.to(dev).contiguous(), n, p.shape[1] * 4)
+            if p.shape[1] * 8 == s.shape[1] * 64:  # legacy Q4_G64 (N, K/8) words
+                return ops.q4t_from_q4g64(p.to(dev).contiguous(), s.to(dev).contiguous(), n, gate_up=gu)
+            raise NotImplementedError(f"packed weight of shape {tuple(p.shape)} / {tuple(s.shape)}")
+
+        def f32(w):
+            return torch.as_tensor(w).detach().to(dev, torch.float32).contiguous()
+
         layers = []
-        for i, b in enumerate(model.transformer.h):
-            def rl(p, s, n, gu=False):
-                if p.ndim == 4:  # MARLIN ladder ("q4", "q4_rtn")
-                    return ops.q4t_from_marlin(p.to(dev), s.to(dev), n, gate_up=gu)
-                if p.shape[1] * 8 == s.shape[1] * 64:  # legacy Q4_G64 ("q4_legacy")
-                    return ops.q4t_from_q4g64(p.to(dev).contiguous(), s.to(dev).contiguous(), n, gate_up=gu)
-                raise NotImplementedError("Q8_G64 projections (the q8 / q4_k_m modes) are not served by the runner")
-            cb = qw["c_attn_b"][i]
+        for i in range(cfg["n_layer"]):
+            cb = torch.as_tensor(qw["c_attn_b"][i]) if qw.get("c_attn_b") is not None else torch.empty(0)
             layers.append(dict(
-                qkv=rl(qw["c_attn_p"][i], qw["c_attn_s"][i], qkv_dim), o=rl(qw["c_proj_p"][i], qw["c_proj_s"][i], mc.n_embd),
-                gu=rl(qw["gu_p"][i], qw["gu_s"][i], 2 * qw["hidden_dim"], True),
-                down=rl(qw["wd_p"][i], qw["wd_s"][i], mc.n_embd),
-                ln_1=b.ln_1.weight.detach().to(dev, torch.float32).contiguous(),
-                ln_2=b.ln_2.weight.detach().to(dev, torch.float32).contiguous(),
+                qkv=rl(qw["c_attn_p"][i], qw["c_attn_s"][i], qkv_dim), o=rl(qw["c_proj_p"][i], qw["c_proj_s"][i], d),
+                gu=rl(qw["gu_p"][i], qw["gu_s"][i], 2 * cfg["ffn"], True),
+                down=rl(qw["wd_p"][i], qw["wd_s"][i], d),
+                ln_1=f32(ln_1[i]), ln_2=f32(ln_2[i]),
                 qkv_b=cb.to(dev, torch.float16) if cb.numel() > 0 else None))
-        packed = dict(layers=layers, emb_w=qw["wte_p"].to(dev), emb_s=qw["wte_sb"].to(dev),
-                      lm_head=(ops.Q8Weight(qw["lmh_p"].to(dev).contiguous(), qw["lmh_sb"].to(dev).contiguous(),
-                                            mc.vocab_size, mc.n_embd)
-                               if qw["lmh_p"].ndim == 2 and qw["lmh_p"].shape[1] * 4 == mc.n_embd  # tied: Q8_G64
-                               else rl(qw["lmh_p"], qw["lmh_sb"], mc.vocab_size)),
-                      ln_f=model.transformer.ln_f.weight.detach().to(dev, torch.float32).contiguous())
+        lmh_p = torch.as_tensor(qw["lmh_p"])
+        packed = dict(layers=layers, emb_w=torch.as_tensor(qw["wte_p"]).to(dev),
+                      emb_s=torch.as_tensor(qw["wte_sb"]).to(dev),
+                      lm_head=rl(lmh_p, qw["lmh_sb"], cfg["vocab"]), ln_f=f32(ln_f))
         dec = cls(cfg, packed, **kw)
         if qw.get("medusa_packs"):
             from .medusa import MedusaHeads
 
-            dec.add_medusa_heads(MedusaHeads.from_packs(qw["medusa_packs"], mc.n_embd, mc.vocab_size, device=dev))
+            dec.add_medusa_heads(MedusaHeads.from_packs(qw["medusa_packs"], d, cfg["vocab"], device=dev))
         return dec
 
     # ------------------------------------------------------------ steps

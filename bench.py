@@ -40,9 +40,9 @@ METRIC = "decode tokens/s (Q4 8B-shape, FP8 KV, ctx 4096)"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # DRAM bytes (read + write) per algorithmic byte of the step kernel, from one
 # ncu capture of a smaller case (the 8B layer shapes, 4 layers, ctx 4096:
-# 766.0 MB for 754.8 MB); the traffic of a full launch is this ratio times its
+# 768.5 MB for 754.8 MB); the traffic of a full launch is this ratio times its
 # algorithmic bytes.
-STEP_TRAFFIC_RATIO = 1.015
+STEP_TRAFFIC_RATIO = 1.018
 
 
 def peaks():

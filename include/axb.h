@@ -317,8 +317,8 @@ int axb_argmax(const uint16_t* x_dev, int rows, int n, int ld, int32_t* out_dev,
 typedef struct {
   int n_layer, d_model, n_head, n_kv_head, head_dim, ffn, vocab;
   float eps;
-  int wfmt, group;       /* projection format (AXB_W_Q4T_*) */
-  int lm_fmt, lm_group;  /* lm_head: AXB_W_Q4T_* or AXB_W_Q8_G64 (tied) */
+  int wfmt, group;       /* projection format (AXB_W_Q4T_*, or AXB_W_Q8_G64 group 64: the q8 mode) */
+  int lm_fmt, lm_group;  /* lm_head: AXB_W_Q4T_* or AXB_W_Q8_G64 (tied, q8, q4_k_m) */
   int kv_type, kv_group; /* cache format */
   int max_batch, max_seq, max_tokens; /* max_tokens = tokens per sequence per step (<= 64) */
   int rope_len;
@@ -327,6 +327,11 @@ typedef struct {
    * ffn and vocab are this rank's shard (heads tp_rank * n_head .., FFN rows
    * tp_rank * ffn .., vocab rows tp_rank * vocab ..); d_model is replicated. */
   int tp_world, tp_rank;
+  /* down projection format: 0 = the projections' (wfmt, group), or
+   * AXB_W_Q8_G64 group 64 (the q4_k_m mode: Q4 projections, Q8 w_down,
+   * transformer.py:847).  Q8 projections keep the reference's own layout,
+   * gate_up as cat(w_gate, w_up); they run on the per-kernel graph path. */
+  int dn_fmt, dn_group;
 } axb_model_cfg;
 
 typedef struct {

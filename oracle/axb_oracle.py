@@ -924,9 +924,16 @@ class OracleModel:
     ``q4t_pack`` (symmetric, group 128, fp16 scales) and dequantized by
     ``q4t_dequant``; everything else -- embeddings, norms, the forward -- is the
     reference's ``q4_rtn`` path unchanged.
+
+    The reference's other quantized-forward modes (transformer.py:840-858):
+    ``"q8"`` packs every projection and the lm_head Q8_G64; ``"q4_k_m"`` takes
+    the MSE-clipped MARLIN packs of c_attn, c_proj and gate_up as the
+    reference made them (``packs``: {"c_attn"|"c_proj"|"gu": [(p, s) per
+    layer]}, no clip search is restated here) with Q8_G64 w_down and lm_head.
     """
 
-    def __init__(self, cfg: dict, weights: dict, rope_len: int, weight_format: str = "q4_rtn"):
+    def __init__(self, cfg: dict, weights: dict, rope_len: int, weight_format: str = "q4_rtn",
+                 packs: dict | None = None):
         self.cfg = cfg
         d, H, Hkv = cfg["d_model"], cfg["n_head"], cfg["n_kv_head"]
         self.hd = d // H
@@ -934,45 +941,57 @@ class OracleModel:
         self.eps = cfg["eps"]
         self.V = cfg["vocab"]
         self.F = cfg["ffn"]
-        if weight_format not in ("q4_rtn", "q4_g128_sym"):
+        if weight_format not in ("q4_rtn", "q4_g128_sym", "q8", "q4_k_m"):
             raise ValueError(f"unknown weight format {weight_format}")
         self.sym = weight_format == "q4_g128_sym"
-        pack = (lambda w: q4t_pack(w, 128, True)) if self.sym else pack_q4_marlin_rtn
-        tied = weights.get("lm_head") is None
-        if tied:
-            self.lmh = ("q8",) + pack_q8_g64(weights["wte"])
-            self.wte = self.lmh[1:]
+        # every packed tensor carries its format: "marlin" (MARLIN Q4), "q4t"
+        # (symmetric G128), "q8" (Q8_G64)
+        q8 = lambda w: ("q8",) + pack_q8_g64(w)  # noqa: E731
+        if weight_format == "q8":  # transformer.py:852-854: every projection Q8_G64
+            pack = q8
+        elif self.sym:
+            pack = lambda w: ("q4t",) + q4t_pack(w, 128, True)  # noqa: E731
         else:
-            self.lmh = ("q4",) + pack(weights["lm_head"])
-            self.wte = pack_q8_g64(weights["wte"])
+            pack = lambda w: ("marlin",) + pack_q4_marlin_rtn(w)  # noqa: E731
+        tied = weights.get("lm_head") is None
+        self.wte = pack_q8_g64(weights["wte"])
+        if tied:
+            self.lmh = ("q8",) + self.wte
+        else:  # q8 / q4_k_m: a Q8_G64 lm_head (transformer.py:842-846)
+            self.lmh = q8(weights["lm_head"]) if weight_format in ("q8", "q4_k_m") else pack(weights["lm_head"])
         self.layers = []
-        for lw in weights["layers"]:
+        for i, lw in enumerate(weights["layers"]):
             gu = np.concatenate([_f32(_to_np(lw["w_gate"])), _f32(_to_np(lw["w_up"]))], 0)
-            self.layers.append(
-                dict(
-                    c_attn=pack(lw["c_attn"]),
-                    c_proj=pack(lw["c_proj"]),
-                    gu=pack(gu),
-                    wd=pack(lw["w_down"]),
-                    ln_1=torch.as_tensor(_to_np(lw["ln_1"])).float(),
-                    ln_2=torch.as_tensor(_to_np(lw["ln_2"])).float(),
-                )
-            )
+            if weight_format == "q4_k_m":
+                # MSE-clipped MARLIN packs (quant.py:495-571) as the reference
+                # made them, passed in ``packs``; w_down Q8_G64 (transformer.py:847)
+                ent = dict(c_attn=("marlin",) + tuple(packs["c_attn"][i]), c_proj=("marlin",) + tuple(packs["c_proj"][i]),
+                           gu=("marlin",) + tuple(packs["gu"][i]), wd=q8(lw["w_down"]))
+            else:
+                ent = dict(c_attn=pack(lw["c_attn"]), c_proj=pack(lw["c_proj"]), gu=pack(gu), wd=pack(lw["w_down"]))
+            ent.update(ln_1=torch.as_tensor(_to_np(lw["ln_1"])).float(),
+                       ln_2=torch.as_tensor(_to_np(lw["ln_2"])).float())
+            self.layers.append(ent)
         self.ln_f = torch.as_tensor(_to_np(weights["ln_f"])).float()
         self.freqs = rope_freqs(self.hd, rope_len, cfg.get("theta", 10000.0), cfg.get("rope_scaling"))
         self._dq = {}
 
     def _w(self, key, packed, K, n):
         if key not in self._dq:
-            if self.sym:
-                self._dq[key] = torch.from_numpy(q4t_dequant(packed[0], packed[1], K, 128, True, n))
+            tag, p, s = packed
+            if tag == "q4t":
+                w = q4t_dequant(p, s, K, 128, True, n)
+            elif tag == "q8":  # quant.py:132-147
+                w = dequant_q8_g64(p, s, K)
             else:
-                self._dq[key] = torch.from_numpy(dequant_q4_marlin(packed[0], packed[1], K, n))
+                w = dequant_q4_marlin(p, s, K, n)
+            self._dq[key] = torch.from_numpy(w)
         return self._dq[key]
 
     def qlin(self, x: torch.Tensor, key, packed, n_out: int) -> torch.Tensor:
-        """transformer.py:1010-1034 -> quant.py:656-661: dequant + F.linear in
-        fp16, result cast back to ``x``'s dtype (fp32 after an fp32 norm)."""
+        """transformer.py:1010-1034 -> quant.py:656-661 / 201-233: dequant +
+        F.linear in fp16, result cast back to ``x``'s dtype (fp32 after an
+        fp32 norm)."""
         x16 = x.to(torch.float16)
         return F.linear(x16, self._w(key, packed, x16.size(-1), n_out)).to(x.dtype)
 
@@ -980,10 +999,7 @@ class OracleModel:
         return torch.from_numpy(dequant_q8_rows(idx, self.wte[0], self.wte[1]))
 
     def lm_head(self, xn: torch.Tensor) -> torch.Tensor:
-        if self.lmh[0] == "q8":
-            w = torch.from_numpy(dequant_q8_g64(self.lmh[1], self.lmh[2], xn.size(-1)))
-            return F.linear(xn.to(torch.float16), w).to(xn.dtype)
-        return self.qlin(xn, "lmh", self.lmh[1:], self.V)
+        return self.qlin(xn, "lmh", self.lmh, self.V)
 
     def forward(self, idx: np.ndarray, cache: OracleCache, return_all: bool = False, hidden: list | None = None):
         """One ``_forward_quantized_sequence`` call (transformer.py:1036-1200).

@@ -132,7 +132,7 @@ def gen_attn(q, ops):
     return out
 
 
-def _ref_model(cfg, W, tied):
+def _ref_model(cfg, W, tied, mode="q4_rtn"):
     from axiomlm.models.transformer import ModelConfig, Transformer
 
     mc = ModelConfig(block_size=cfg["block_size"], vocab_size=cfg["vocab"], n_layer=cfg["n_layer"],
@@ -154,21 +154,41 @@ def _ref_model(cfg, W, tied):
             b.ln_2.weight.copy_(lw["ln_2"])
         m.transformer.ln_f.weight.copy_(W["ln_f"])
     m.eval()
-    m.quantize("q4_rtn")
+    m.quantize(mode)
     return m
 
 
-def gen_model(cfg, seed, prompt_len, n_new, kv, ln_random, tied=False, with_tree=False, ring=None):
+# The reference's MSE-clipped MARLIN packs of a q4_k_m model
+# (_ensure_quant_weights, quant.py:495-571), per layer.  No packer here
+# repeats the clip search, so the GPU test serves these tensors as packed; the
+# model's Q8_G64 tensors (w_down, lm_head, embeddings) are plain RTN and are
+# packed again on the GPU.
+_PACKED_Q4 = ("c_attn_p", "c_attn_s", "c_proj_p", "c_proj_s", "gu_p", "gu_s")
+
+
+def _packed_arrays(m):
+    qw = m._ensure_quant_weights(torch.device("cpu"))
+    out = {}
+    for k in _PACKED_Q4:
+        for i, t in enumerate(qw[k]):
+            out[f"pk_{k}_{i}"] = _np(t)
+    return out
+
+
+def gen_model(cfg, seed, prompt_len, n_new, kv, ln_random, tied=False, with_tree=False, ring=None, mode="q4_rtn"):
     from axiomlm.engine.medusa import DEFAULT_MEDUSA_TREE_CHOICES, compile_medusa_tree
     from axiomlm.engine.paged_cache import StaticKVCache
 
     W = make_weights(cfg, seed, ln_random=ln_random, tied=tied)
-    m = _ref_model(cfg, W, tied)
+    m = _ref_model(cfg, W, tied, mode)
     hd = cfg["d_model"] // cfg["n_head"]
     max_seq = ring if ring else cfg["block_size"]
     prompt = make_prompt(prompt_len, cfg["vocab"], seed + 1)
     out = {"prompt": _np(prompt), "seed": np.array(seed), "ln_random": np.array(int(ln_random)),
-           "tied": np.array(int(tied)), "max_seq": np.array(max_seq), "ring": np.array(int(bool(ring)))}
+           "tied": np.array(int(tied)), "max_seq": np.array(max_seq), "ring": np.array(int(bool(ring))),
+           "mode": np.array(mode)}
+    if mode == "q4_k_m":
+        out.update(_packed_arrays(m))
     with torch.no_grad():
         cache = StaticKVCache(1, max_seq, cfg["n_layer"], cfg["n_kv_head"], hd, dtype=torch.float16,
                               device="cpu", ring_buffer=bool(ring), cache_dtype=kv)
@@ -231,6 +251,8 @@ def main():
     ap.add_argument("--reference", default=os.environ.get("AXIOMLM_REFERENCE", ""))
     ap.add_argument("--skip-tiny", action="store_true")
     ap.add_argument("--tiny-only", action="store_true", help="regenerate only the BASELINE config-1 fixtures")
+    ap.add_argument("--modes-only", action="store_true",
+                    help="regenerate only the q8 / q4_k_m model fixtures (small_q8, small_q4km)")
     args = ap.parse_args()
     if not args.reference or not os.path.isdir(args.reference):
         raise SystemExit("pass --reference <path to the AxiomLM checkout>")
@@ -241,6 +263,16 @@ def main():
     import axiomlm.models.modules as modules
     from axiomlm.engine.medusa import DEFAULT_MEDUSA_TREE_CHOICES, compile_medusa_tree
 
+    if args.modes_only or not args.tiny_only:
+        # the reference's other quantized-forward modes (transformer.py:797-799):
+        # Q8_G64 everywhere ("q8"), MSE-clipped Q4 with Q8 w_down and lm_head ("q4_k_m")
+        for mode, name, seed in (("q8", "small_q8", 41), ("q4_k_m", "small_q4km", 55)):
+            t0 = time.time()
+            o = gen_model(SMALL, seed, 12, 16, "fp16", ln_random=True, mode=mode)
+            np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **o)
+            print(f"{name}: {time.time() - t0:.1f}s tokens={o['tokens'][:8]}")
+        if args.modes_only:
+            return
     if not args.tiny_only:
         _gen_small(q, ops, modules, compile_medusa_tree, DEFAULT_MEDUSA_TREE_CHOICES)
     if not args.skip_tiny:

@@ -128,3 +128,42 @@ def test_tiny_config_128_greedy_tokens(kv):
         worst = max(worst, rel)
         assert rel < REL_TOL[kv], f"step {i}: logits rel {rel:.2e} (tol {REL_TOL[kv]})"
     print(f"tiny {kv}: 128 teacher-forced steps, worst logit rel {worst:.2e}")
+
+
+def _mode_decoder(cfg, fx, **kw):
+    from axiomlm_b200 import ops
+    from axiomlm_b200.model import QuantizedDecoder
+
+    W = make_weights(cfg, int(fx["seed"]), ln_random=bool(fx["ln_random"]))
+    kw = dict(kv_dtype="fp16", max_seq=int(fx["max_seq"]), rope_len=cfg["block_size"], **kw)
+    if str(fx["mode"]) == "q8":
+        return QuantizedDecoder.from_weights(cfg, W, "q8", **kw)
+    # q4_k_m: the reference's MSE-clipped MARLIN packs as it packed them; its
+    # Q8_G64 tensors (w_down, lm_head, embeddings) are RTN, packed here
+    n = cfg["n_layer"]
+    qw = {k: [torch.from_numpy(fx[f"pk_{k}_{i}"]) for i in range(n)]
+          for k in ("c_attn_p", "c_attn_s", "c_proj_p", "c_proj_s", "gu_p", "gu_s")}
+    wd = [ops.pack_q8_g64(W["layers"][i]["w_down"].cuda()) for i in range(n)]
+    qw["wd_p"], qw["wd_s"] = [p for p, _ in wd], [s for _, s in wd]
+    qw["wte_p"], qw["wte_sb"] = ops.pack_q8_g64(W["wte"].cuda())
+    qw["lmh_p"], qw["lmh_sb"] = ops.pack_q8_g64(W["lm_head"].cuda())
+    return QuantizedDecoder.from_packed(cfg, qw, [lw["ln_1"] for lw in W["layers"]],
+                                        [lw["ln_2"] for lw in W["layers"]], W["ln_f"], **kw)
+
+
+@pytest.mark.parametrize("name", ["small_q8", "small_q4km"])
+@pytest.mark.parametrize("graph", [True, False])
+def test_small_model_q8_modes_greedy_parity(name, graph):
+    """The reference's other quantized-forward modes (transformer.py:797-799,
+    847-858): "q8" (every projection and the lm_head Q8_G64) and "q4_k_m"
+    (MSE-clipped Q4 projections, Q8_G64 w_down and lm_head), served by the
+    runner's per-kernel path with the Q8 GEMV."""
+    fx = _fx(name)
+    dec = _mode_decoder(SMALL, fx, use_graph=graph)
+    assert not dec.uses_step_kernel
+    toks, logits = _greedy_with_logits(dec, fx["prompt"], len(fx["tokens"]), forced=fx["tokens"])
+    _check_tokens(toks, fx)
+    for i in range(len(toks)):
+        assert _rel(logits[i], fx["logits"][i]) < REL_TOL["fp16"], i
+    assert int(dec.argmax(1)[0]) == toks[-1]
+    dec.close()

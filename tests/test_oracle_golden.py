@@ -199,3 +199,31 @@ def test_oracle_model_greedy_matches_reference(name):
     if "tree_logits" in fx.files:
         tl, _ = m.forward_tree(fx["tree_tokens"], cache, fx["tree_depths"].tolist(), fx["tree_mask"].tolist())
         assert np.array_equal(tl[0].float().numpy(), fx["tree_logits"].astype(np.float32))
+
+
+@pytest.mark.parametrize("name", ["small_q8", "small_q4km"])
+def test_oracle_model_q8_modes_match_reference(name):
+    """The oracle in the reference's "q8" and "q4_k_m" modes against the
+    reference's own greedy decode of the same model (tests/golden/make_golden.py
+    --modes-only): tokens and logits bit-identical."""
+    from model_weights import SMALL, make_weights
+
+    fx = _load(f"{name}.npz")
+    mode = str(fx["mode"])
+    W = make_weights(SMALL, int(fx["seed"]), ln_random=bool(fx["ln_random"]))
+    packs = None
+    if mode == "q4_k_m":
+        packs = {k: [(fx[f"pk_{src}_p_{i}"], fx[f"pk_{src}_s_{i}"]) for i in range(SMALL["n_layer"])]
+                 for k, src in (("c_attn", "c_attn"), ("c_proj", "c_proj"), ("gu", "gu"))}
+    m = O.OracleModel(SMALL, W, rope_len=SMALL["block_size"], weight_format=mode, packs=packs)
+    hd = SMALL["d_model"] // SMALL["n_head"]
+    cache = O.OracleCache(SMALL["n_layer"], 1, SMALL["n_kv_head"], int(fx["max_seq"]), hd, "fp16", False)
+    logits, _ = m.forward(fx["prompt"], cache)
+    steps = [logits[0, -1]]
+    toks = [int(torch.argmax(logits[0, -1]))]
+    for _ in range(len(fx["tokens"]) - 1):
+        logits, _ = m.forward(np.array([[toks[-1]]]), cache)
+        steps.append(logits[0, -1])
+        toks.append(int(torch.argmax(logits[0, -1])))
+    assert toks == fx["tokens"].tolist()
+    assert np.array_equal(torch.stack(steps).to(torch.float16).numpy().view(np.uint16), fx["logits"].view(np.uint16))
