@@ -81,6 +81,12 @@ class KvWriteDesc(C.Structure):
     ]
 
 
+class Q2TMeta(C.Structure):
+    """axb_q2t_meta: a 2-bit projection's metadata, passed to the runner in
+    place of a scale pointer."""
+    _fields_ = [("meta", vp), ("meta2", vp), ("pt_scale", vp)]
+
+
 class LbGemvDesc(C.Structure):
     _fields_ = [
         ("fmt", i32), ("words", vp), ("meta", vp), ("meta2", vp), ("pt_scale", vp),
@@ -173,6 +179,7 @@ _SIGS = {
     "axb_runner_buffer": (i32, [vp, i32, C.POINTER(sz), C.POINTER(sz)]),
     "axb_runner_step": (i32, [vp, i32, i32, i32, i32, i32, i32, vp, vp, i32, vp]),
     "axb_runner_uses_step_kernel": (i32, [vp]),
+    "axb_runner_step_launches": (i32, [vp, i32, i32, i32]),
     "axb_runner_set_debug": (i32, [vp, i32, C.c_uint32, C.c_uint32]),
     "axb_tp_unique_id": (i32, [vp]),
     "axb_tp_comm_create": (i32, [vp, i32, i32, C.POINTER(vp)]),

@@ -218,11 +218,21 @@ __global__ void rmsnorm_kernel(const __half* __restrict__ x, const float* __rest
 
 static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
+// 2-bit projections (q2t; axb_lbgemv)
+static bool is_q2t(int f) {
+  return f == AXB_W_TERNARY_G64 || f == AXB_W_TERNARY_PT || f == AXB_W_Q2_G64 || f == AXB_W_Q2K_SB256;
+}
+// formats served by their own GEMV followed by separate residual-add / SwiGLU
+// passes, with gate_up in the reference's row order, cat(w_gate, w_up)
+static bool ext_fmt(int f) { return f == AXB_W_Q8_G64 || is_q2t(f); }
+constexpr int kLbMaxM = 8;  // rows per axb_lbgemv launch
+
 constexpr int kArgmaxParts = 256;
 constexpr int kTcMinRows = 16;  // tree / prefill steps above this many rows use the tcgen05 GEMM
 
 struct Layout {
   size_t tokens, params, masks, depths, x, h, qkv, q, attn, sw, logits, amax, xnorm, gemm_ws, attn_ws, total;
+  size_t lb_ws, lb_ws_bytes;  // 2-bit GEMV workspace
   size_t am_v, am_i, am_cnt;
   size_t tp_part, tp_keys;  // tensor parallel: row-parallel partial sums (fp32), argmax keys
   size_t gu_tmp, tc_ws, tc_ws_bytes;  // tensor-core projections for many-token steps
@@ -264,8 +274,19 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.tp_part = take(c.tp_world > 1 ? rows * c.d_model * 4 : 0);
   // tensor-core path (rows > 16): gate_up output in packed order, tcgen05 workspace
   const bool tc = rows > kTcMinRows && c.tp_world <= 1;
-  // (Q8 gate_up projections also leave their product there before the SwiGLU pass)
-  L.gu_tmp = take(tc || c.wfmt == AXB_W_Q8_G64 ? rows * 2 * (size_t)c.ffn * 2 : 0);
+  // (Q8 / 2-bit gate_up projections also leave their product there before the SwiGLU pass)
+  L.gu_tmp = take(tc || ext_fmt(c.wfmt) ? rows * 2 * (size_t)c.ffn * 2 : 0);
+  {
+    const int dn = c.dn_fmt ? c.dn_fmt : c.wfmt;
+    const int qd_ = c.n_head * c.head_dim;
+    const int FNK[5][3] = {{c.wfmt, (int)qkv_dim, c.d_model}, {c.wfmt, c.d_model, qd_}, {c.wfmt, 2 * c.ffn, c.d_model},
+                           {dn, c.d_model, c.ffn}, {c.lm_fmt, c.vocab, c.d_model}};
+    size_t lb = 0;
+    for (auto& f : FNK)
+      if (is_q2t(f[0])) lb = std::max(lb, axb_lbgemv_workspace_bytes(f[0], f[1], f[2], kLbMaxM));
+    L.lb_ws_bytes = lb;
+    L.lb_ws = take(lb);
+  }
   size_t tcw = 0;
   if (tc) {
     const int qd_ = c.n_head * c.head_dim;
@@ -328,11 +349,13 @@ struct Runner {
   const void *emb_w, *emb_s, *lm_w, *lm_s;
   const float *ln_f, *rope;
   std::vector<const void*> qkv_w, qkv_s, qkv_b, o_w, o_s, gu_w, gu_s, dn_w, dn_s;
+  std::vector<axb_q2t_meta> q2m;  // copies of the 2-bit projections' metadata (the *_s pointers point here)
   std::vector<const float*> ln1, ln2;
   std::vector<void*> kc, vc, ks, vs;
   void* tp_comm = nullptr;  // tensor parallel communicator (tp_world > 1)
   cudaStream_t cap = nullptr;
   std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;
+  std::map<std::tuple<int, int, int>, int> graph_kernels;  // kernel nodes per captured step
   // persistent step kernel: decode steps of B <= 8 sequences run as one launch
   bool step_ok = false;
   bool step_graph_ok = true;  // cleared if the cooperative launch cannot be captured
@@ -345,7 +368,7 @@ struct Runner {
 
   int gemv(const void* w, const void* s, int fmt, int group, int N, int K, int M, const __half* x, int ldx,
            void* y, int ldy, const void* bias, const float* norm_w, int epi, int gu, cudaStream_t st) const {
-    if (fmt == AXB_W_Q8_G64) return q8_proj(w, s, N, K, M, x, ldx, y, ldy, bias, norm_w, epi, st);
+    if (ext_fmt(fmt)) return ext_proj(fmt, w, s, N, K, M, x, ldx, y, ldy, bias, norm_w, epi, st);
     // rows beyond 64 are processed in 64-row chunks (one weight pass each)
     for (int m0 = 0; m0 < M; m0 += 64) {
       axb_qgemm_desc d = {};
@@ -375,32 +398,58 @@ struct Runner {
     return AXB_OK;
   }
 
-  // Q8_G64 projections (the reference's q8 and q4_k_m modes, transformer.py:847-858):
-  // the GEMV rounds its product to fp16 (then adds the bias and rounds again,
-  // as _qlin does), and the residual add or SwiGLU runs as its own pass with
-  // the rounding of the fused Q4 epilogues.  The product lands in h (free
-  // during the o / down projections) or gu_tmp (gate_up).
-  int q8_proj(const void* w, const void* s, int N, int K, int M, const __half* x, int ldx, void* y, int ldy,
-              const void* bias, const float* norm_w, int epi, cudaStream_t st) const {
-    const uint32_t* w8 = static_cast<const uint32_t*>(w);
-    const __half2* s8 = static_cast<const __half2*>(s);
+  // y = x W^T (+ bias) for a Q8_G64 or 2-bit projection, fp16 out
+  int ext_gemv(int fmt, const void* w, const void* s, int N, int K, int M, const __half* x, int ldx, __half* y,
+               int ldy, const __half* b, cudaStream_t st) const {
+    if (fmt == AXB_W_Q8_G64)
+      return q8_gemv(x, ldx, M, K, static_cast<const uint32_t*>(w), static_cast<const __half2*>(s), N, y, ldy, st, b);
+    const axb_q2t_meta* m = static_cast<const axb_q2t_meta*>(s);
+    for (int m0 = 0; m0 < M; m0 += kLbMaxM) {
+      axb_lbgemv_desc d = {};
+      d.fmt = fmt;
+      d.words = w;
+      d.meta = m->meta;
+      d.meta2 = m->meta2;
+      d.pt_scale = m->pt_scale;
+      d.N = N;
+      d.K = K;
+      d.M = std::min(kLbMaxM, M - m0);
+      d.x = x + (size_t)m0 * ldx;
+      d.ldx = ldx;
+      d.y = y + (size_t)m0 * ldy;
+      d.ldy = ldy;
+      d.bias = b;
+      d.workspace = buf<void>(L.lb_ws);
+      d.workspace_bytes = L.lb_ws_bytes;
+      if (int rc = axb_lbgemv(&d, st)) return rc;
+    }
+    return AXB_OK;
+  }
+
+  // Q8_G64 projections (the reference's q8 and q4_k_m modes, transformer.py:847-858)
+  // and 2-bit ones: the GEMV rounds its product to fp16 (for Q8, then adds the
+  // bias and rounds again, as _qlin does), and the residual add or SwiGLU runs
+  // as its own pass with the rounding of the fused Q4 epilogues.  The product
+  // lands in h (free during the o / down projections) or gu_tmp (gate_up).
+  int ext_proj(int fmt, const void* w, const void* s, int N, int K, int M, const __half* x, int ldx, void* y, int ldy,
+               const void* bias, const float* norm_w, int epi, cudaStream_t st) const {
     const __half* b = static_cast<const __half*>(bias);
-    AXB_CHECK_ARG(norm_w == nullptr, "runner: Q8 projections take normalized rows");
-    if (epi == AXB_EPI_STORE) return q8_gemv(x, ldx, M, K, w8, s8, N, static_cast<__half*>(y), ldy, st, b);
+    AXB_CHECK_ARG(norm_w == nullptr, "runner: Q8 / 2-bit projections take normalized rows");
+    if (epi == AXB_EPI_STORE) return ext_gemv(fmt, w, s, N, K, M, x, ldx, static_cast<__half*>(y), ldy, b, st);
     const int grid = std::min((M * N + 255) / 256, 4 * num_sms());
     if (epi == AXB_EPI_RESIDUAL) {
-      AXB_CHECK_ARG(ldy == N && N == c.d_model, "runner: Q8 residual projection shape");
-      if (int rc = q8_gemv(x, ldx, M, K, w8, s8, N, buf<__half>(L.h), N, st, b)) return rc;
+      AXB_CHECK_ARG(ldy == N && N == c.d_model, "runner: residual projection shape");
+      if (int rc = ext_gemv(fmt, w, s, N, K, M, x, ldx, buf<__half>(L.h), N, b, st)) return rc;
       residual_add_kernel<<<grid, 256, 0, st>>>(static_cast<__half*>(y), buf<__half>(L.h), M * N);
-      return launch_status("q8 residual add");
+      return launch_status("residual add");
     }
     if (epi == AXB_EPI_SWIGLU) {
-      AXB_CHECK_ARG(N == 2 * c.ffn && ldy == c.ffn && L.gu_tmp, "runner: Q8 gate_up projection shape");
-      if (int rc = q8_gemv(x, ldx, M, K, w8, s8, N, buf<__half>(L.gu_tmp), N, st, b)) return rc;
+      AXB_CHECK_ARG(N == 2 * c.ffn && ldy == c.ffn && L.gu_tmp, "runner: gate_up projection shape");
+      if (int rc = ext_gemv(fmt, w, s, N, K, M, x, ldx, buf<__half>(L.gu_tmp), N, b, st)) return rc;
       swiglu_split_kernel<<<grid, 256, 0, st>>>(buf<__half>(L.gu_tmp), N, c.ffn, M, static_cast<__half*>(y));
-      return launch_status("q8 swiglu");
+      return launch_status("swiglu");
     }
-    set_error("runner: epilogue %d is not available for Q8 projections", epi);
+    set_error("runner: epilogue %d is not available for Q8 / 2-bit projections", epi);
     return AXB_EINVAL;
   }
 
@@ -408,7 +457,7 @@ struct Runner {
   int norm_gemv(const float* nw, const void* w, const void* s, int N, int K, int M, void* y, int ldy,
                 const void* bias, int epi, int gu, int fmt, int group, cudaStream_t st) const {
     const __half* x = buf<__half>(L.x);
-    if (fmt != AXB_W_Q8_G64 && qgemm_can_fuse_norm(M, K))
+    if (!ext_fmt(fmt) && qgemm_can_fuse_norm(M, K))
       return gemv(w, s, fmt, group, N, K, M, x, K, y, ldy, bias, nw, epi, gu, st);
     int rc = rmsnorm(x, nw, M, K, c.eps, buf<__half>(L.h), st);
     if (rc) return rc;
@@ -635,7 +684,8 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   AXB_CHECK_ARG(c.n_head * c.head_dim * tpw == c.d_model,
                 "runner_create: n_head * head_dim * tp_world must equal d_model");
   AXB_CHECK_ARG(c.wfmt == AXB_W_Q4T_SYM || c.wfmt == AXB_W_Q4T_AFFINE ||
-                    (c.wfmt == AXB_W_Q8_G64 && c.group == 64 && c.tp_world <= 1),
+                    (c.wfmt == AXB_W_Q8_G64 && c.group == 64 && c.tp_world <= 1) ||
+                    (is_q2t(c.wfmt) && c.tp_world <= 1),
                 "runner_create: unsupported weight format %d", c.wfmt);
   // the down projection: the projections' format, or Q8_G64 (the q4_k_m mode)
   const int dn_fmt = c.dn_fmt ? c.dn_fmt : c.wfmt, dn_group = c.dn_fmt ? c.dn_group : c.group;
@@ -643,8 +693,12 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
                     (dn_fmt == AXB_W_Q8_G64 && dn_group == 64 && c.tp_world <= 1),
                 "runner_create: down projection format %d (group %d) not supported", dn_fmt, dn_group);
   AXB_CHECK_ARG(c.lm_fmt == AXB_W_Q4T_SYM || c.lm_fmt == AXB_W_Q4T_AFFINE ||
-                    (c.lm_fmt == AXB_W_Q8_G64 && c.lm_group == 64 && c.tp_world <= 1),
+                    (c.lm_fmt == AXB_W_Q8_G64 && c.lm_group == 64 && c.tp_world <= 1) ||
+                    (is_q2t(c.lm_fmt) && c.tp_world <= 1),
                 "runner_create: lm_head format %d not supported by the runner", c.lm_fmt);
+  if (is_q2t(c.wfmt) || is_q2t(c.lm_fmt))  // 2-bit k-blocks are 128 wide
+    AXB_CHECK_ARG(c.d_model % 128 == 0 && (c.n_head * c.head_dim) % 128 == 0 && c.ffn % 128 == 0,
+                  "runner_create: 2-bit projections need d_model, n_head * head_dim and ffn multiples of 128");
   AXB_CHECK_ARG(c.max_tokens >= 1 && c.max_tokens <= 64 && c.max_batch >= 1, "runner_create: bad max_tokens/batch");
   AXB_CHECK_ARG(c.ffn % 8 == 0, "runner_create: ffn must be a multiple of 8");
   Layout L = make_layout(c);
@@ -698,6 +752,21 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
     r->ks.push_back(p->k_scale ? p->k_scale[l] : nullptr);
     r->vs.push_back(p->v_scale ? p->v_scale[l] : nullptr);
   }
+  // 2-bit projections: the scale pointers address host metadata structs, copied
+  // here (reserved up front, so the pointers into q2m stay valid)
+  r->q2m.reserve(4 * (size_t)c.n_layer + 1);
+  auto own_meta = [&](int fmt, const void*& sp) {
+    if (!is_q2t(fmt)) return;
+    r->q2m.push_back(*static_cast<const axb_q2t_meta*>(sp));
+    sp = &r->q2m.back();
+  };
+  for (int l = 0; l < c.n_layer; ++l) {
+    own_meta(c.wfmt, r->qkv_s[l]);
+    own_meta(c.wfmt, r->o_s[l]);
+    own_meta(c.wfmt, r->gu_s[l]);
+    own_meta(dn_fmt, r->dn_s[l]);
+  }
+  own_meta(c.lm_fmt, r->lm_s);
   cudaError_t e = cudaStreamCreateWithFlags(&r->cap, cudaStreamNonBlocking);
   if (e != cudaSuccess) {
     delete r;
@@ -855,6 +924,14 @@ int axb_runner_set_debug(void* h, int flags, uint32_t spin_limit, uint32_t mbar_
   return AXB_OK;
 }
 
+int axb_runner_step_launches(void* h, int B, int T, int tree) {
+  Runner* r = static_cast<Runner*>(h);
+  if (!r) return -1;
+  const bool step_mode = !tree && T == 1 && B <= kStepMaxM && r->step_ok;
+  auto it = r->graph_kernels.find(std::make_tuple(B, T, step_mode ? 2 : (tree ? 1 : 0)));
+  return it == r->graph_kernels.end() ? -1 : it->second + 1;  // + the parameter kernel launched beside the graph
+}
+
 int axb_runner_uses_step_kernel(void* h) {
   Runner* r = reinterpret_cast<Runner*>(h);
   return r && r->step_ok ? 1 : 0;
@@ -908,6 +985,19 @@ int axb_runner_step(void* h, int B, int T, int rope_pos, int write_pos, int acti
     e = cudaStreamEndCapture(r->cap, &g);
     cudaGraphExec_t ex = nullptr;
     if (!rc && e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
+    if (g && ex) {  // count the step's kernel launches
+      size_t n = 0;
+      if (cudaGraphGetNodes(g, nullptr, &n) == cudaSuccess && n) {
+        std::vector<cudaGraphNode_t> nodes(n);
+        int k = 0;
+        if (cudaGraphGetNodes(g, nodes.data(), &n) == cudaSuccess)
+          for (size_t i = 0; i < n; ++i) {
+            cudaGraphNodeType t;
+            if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++k;
+          }
+        r->graph_kernels[key] = k;
+      }
+    }
     if (g) cudaGraphDestroy(g);
     if (step_mode && (rc || e != cudaSuccess)) {
       // the cooperative step launch could not go into a graph: launch it directly from now on

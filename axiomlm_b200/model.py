@@ -33,8 +33,19 @@ WEIGHT_FORMATS = {
 def _vp_array(items):
     arr = (C.c_void_p * len(items))()
     for i, t in enumerate(items):
-        arr[i] = None if t is None else t.data_ptr()
+        arr[i] = None if t is None else (t if isinstance(t, int) else t.data_ptr())
     return arr
+
+
+def _scale_ref(w, keep: list):
+    """What the runner takes as a projection's scale pointer: the scales
+    tensor, or for a 2-bit projection the address of its axb_q2t_meta (kept
+    alive in ``keep`` until the runner has copied it)."""
+    if isinstance(w, ops.Q2TWeight):
+        m = w.runner_meta()
+        keep.append(m)
+        return C.addressof(m)
+    return w.scales
 
 
 class QuantizedDecoder:
@@ -85,20 +96,24 @@ class QuantizedDecoder:
         vc = self.cache.v_caches
         ks = self.cache.k_scales or [None] * cfg["n_layer"]
         vs = self.cache.v_scales or [None] * cfg["n_layer"]
+        metas: list = []
+        sr = lambda w: _scale_ref(w, metas)  # noqa: E731
         self._arrays = dict(
-            qkv_w=_vp_array([x["qkv"].words for x in lay]), qkv_s=_vp_array([x["qkv"].scales for x in lay]),
+            qkv_w=_vp_array([x["qkv"].words for x in lay]), qkv_s=_vp_array([sr(x["qkv"]) for x in lay]),
             qkv_b=_vp_array([x.get("qkv_b") for x in lay]),
-            o_w=_vp_array([x["o"].words for x in lay]), o_s=_vp_array([x["o"].scales for x in lay]),
-            gu_w=_vp_array([x["gu"].words for x in lay]), gu_s=_vp_array([x["gu"].scales for x in lay]),
-            dn_w=_vp_array([x["down"].words for x in lay]), dn_s=_vp_array([x["down"].scales for x in lay]),
+            o_w=_vp_array([x["o"].words for x in lay]), o_s=_vp_array([sr(x["o"]) for x in lay]),
+            gu_w=_vp_array([x["gu"].words for x in lay]), gu_s=_vp_array([sr(x["gu"]) for x in lay]),
+            dn_w=_vp_array([x["down"].words for x in lay]), dn_s=_vp_array([sr(x["down"]) for x in lay]),
             ln1=_vp_array([x["ln_1"] for x in lay]), ln2=_vp_array([x["ln_2"] for x in lay]),
             k_cache=_vp_array(kc), v_cache=_vp_array(vc), k_scale=_vp_array(ks), v_scale=_vp_array(vs))
+        lm_s = sr(lm)
         p = L.ModelPtrs(emb_w=packed["emb_w"].data_ptr(), emb_s=packed["emb_s"].data_ptr(), lm_w=lm.words.data_ptr(),
-                        lm_s=lm.scales.data_ptr(), ln_f=packed["ln_f"].data_ptr(), rope=self.rope.data_ptr(),
+                        lm_s=lm_s if isinstance(lm_s, int) else lm_s.data_ptr(), ln_f=packed["ln_f"].data_ptr(), rope=self.rope.data_ptr(),
                         tp_comm=tp.comm if tp is not None else None,
                         **{k: C.cast(v, C.POINTER(C.c_void_p)) for k, v in self._arrays.items()})
         h = C.c_void_p()
         L.call("axb_runner_create", C.byref(c), C.byref(p), C.c_void_p(self.workspace.data_ptr()), nbytes, C.byref(h))
+        del metas  # copied by the runner
         self._h = h
 
         def view(which, dtype, shape):
@@ -202,7 +217,12 @@ class QuantizedDecoder:
             s = torch.as_tensor(s)
             if p.ndim == 4:  # MARLIN ladder
                 return ops.q4t_from_marlin(p.to(dev), s.to(dev), n, gate_up=gu)
-            if p.shape[1] * 4 == s.shape[1] * 64:  # Q8_G64 (N, K/4) words: kept as packed
+            if p.dtype == torch.uint8 and p.shape[1] * 4 == s.shape[1] * 64:
+                # 2-bit codes (N, K/4): ternary with group-64 scales (quant.py:236-274)
+                # or "Q2_K" G64 (scale, bias) pairs (quant.py:339-381)
+                fmt = L.W_Q2_G64 if s.ndim == 3 else L.W_TERNARY_G64
+                return ops.q2t_from_ref(fmt, p.to(dev).contiguous(), s.to(dev).contiguous(), None, p.shape[1] * 4)
+            if p.shape[1] * 4 == s.shape[1] * 64:  # Q8_G64 (N, K/4) int32 words: kept as packed
                 return ops.Q8Weight(p.to(dev).contiguous(), s.to(dev).contiguous(), n, p.shape[1] * 4)
             if p.shape[1] * 8 == s.shape[1] * 64:  # legacy Q4_G64 (N, K/8) words
                 return ops.q4t_from_q4g64(p.to(dev).contiguous(), s.to(dev).contiguous(), n, gate_up=gu)

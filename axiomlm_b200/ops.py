@@ -260,6 +260,13 @@ class Q2TWeight:
     N: int
     K: int
     fmt: int
+    group: int = 0  # unused: the format fixes its grouping
+
+    def runner_meta(self) -> "L.Q2TMeta":
+        """The axb_q2t_meta the decode runner takes in place of a scale pointer."""
+        return L.Q2TMeta(meta=None if self.meta is None else self.meta.data_ptr(),
+                         meta2=None if self.meta2 is None else self.meta2.data_ptr(),
+                         pt_scale=None if self.pt_scale is None else self.pt_scale.data_ptr())
 
     @property
     def nbytes(self) -> int:

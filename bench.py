@@ -152,10 +152,10 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ our arm
 
-def build_decoder(cfg, batch, ctx, kv, seed=0, tp=None):
+def build_decoder(cfg, batch, ctx, kv, seed=0, tp=None, weights="q4_g128", ring=0):
     from axiomlm_b200.synth import build_decoder as bd
 
-    return bd(cfg, batch, ctx, kv, seed=seed, tp=tp)
+    return bd(cfg, batch, ctx, kv, seed=seed, tp=tp, weights=weights, ring=ring)
 
 
 def fill_context(dec, batch, ctx, seed=1):
@@ -200,17 +200,28 @@ def gemv_roofline(dec, batch, reps=3):
                      (lay["gu"], act(lay["gu"].K), L.EPI_SWIGLU), (lay["down"], act(lay["down"].K), L.EPI_STORE)]
     launches.append((dec.packed["lm_head"], act(dec.packed["lm_head"].K), L.EPI_STORE))
     tot_bytes = sum(W.nbytes + batch * W.K * 2 + batch * W.N * 2 for W, _, _ in launches)
-    outs = [torch.empty(batch, W.N // 2 if e == L.EPI_SWIGLU else W.N, dtype=torch.float16, device="cuda")
-            for W, _, e in launches]
+
+    def lowbit(W):  # 2-bit projections: the 2-bit GEMV, its product stored (the runner's next pass applies SwiGLU)
+        return isinstance(W, ops.Q2TWeight)
+
+    outs = [torch.empty(batch, W.N // 2 if e == L.EPI_SWIGLU and not lowbit(W) else W.N, dtype=torch.float16,
+                        device="cuda") for W, _, e in launches]
+
+    def run(W, x, e, o):
+        if lowbit(W):
+            ops.lbgemm(x, W, out=o)
+        else:
+            ops.qgemm(x, W, epilogue=e, out=o)
+
     for (W, x, e), o in zip(launches[:8], outs):  # warm-up (allocates the workspace)
-        ops.qgemm(x, W, epilogue=e, out=o)
+        run(W, x, e, o)
     torch.cuda.synchronize()
     # the launch sequence is captured once and replayed, so host launch cost
     # does not leak into the kernel time; same kernels and grids as the runner
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         for (W, x, e), o in zip(launches, outs):
-            ops.qgemm(x, W, epilogue=e, out=o)
+            run(W, x, e, o)
     g.replay()
     times = []
     for _ in range(reps):
@@ -270,7 +281,8 @@ def run_ours(args, rank, world):
         if args.tp != world:
             raise SystemExit(f"--tp {args.tp} needs {args.tp} ranks under torchrun (got {world})")
         tp = TensorParallel.from_process_group()
-    dec = build_decoder(cfg, B, args.ctx, kv, seed=1000 + (0 if tp else rank), tp=tp)
+    dec = build_decoder(cfg, B, args.ctx, kv, seed=1000 + (0 if tp else rank), tp=tp, weights=args.weights,
+                        ring=args.ring)
     fill_context(dec, B, args.ctx, seed=2000 + (0 if tp else rank))
     st = torch.cuda.current_stream()
     tok = dec.argmax(B).view(B, 1).long()
@@ -321,7 +333,11 @@ def run_ours(args, rank, world):
     # launch per step), or the Q4 GEMV when the per-kernel graph runs the step
     pk, pk_kind = peaks()
     step_kernel = dec.uses_step_kernel and B <= 8  # the persistent kernel takes decode batches of up to 8
-    if step_kernel:
+    lowbit = args.weights != "q4_g128"
+    if lowbit:  # 2-bit projections on the per-kernel graph: the 2-bit GEMV dominates
+        bpl, spl, nl = gemv_roofline(dec, B)
+        kname = f"lbgemv_kernel ({args.weights} GEMV, split-K) + its x-sum / reduce kernels"
+    elif step_kernel:
         bpl, spl, nl = step_roofline(dec, B)
         kname = "step_kernel<SYM, GB=2, HD=128> (whole decode step, one persistent launch)"
     elif B > 16:  # many-token decode: the graph path with the tcgen05 projections; whole step timed
@@ -333,17 +349,25 @@ def run_ours(args, rank, world):
     achieved = bpl / spl / 1e9
     out = None
     if rank == 0:
-        # set_params + the step kernel; per-kernel graph: set_params, embed, 5/layer, lm_head, argmax
-        launches_per_step = 2 if step_kernel else 2 + cfg["n_layer"] * 5 + 2
+        # the runner counts the kernel nodes of the step's CUDA graph (+ its parameter kernel)
+        launches_per_step = L.load().axb_runner_step_launches(dec._h, B, 1, 0)
+        if launches_per_step < 0:  # no graph captured (cooperative launch outside a graph)
+            launches_per_step = 2
         out = {
-            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "metric": METRIC if not (lowbit or args.ring) else
+            f"decode tokens/s ({args.weights} 8B-shape, KV {args.kv}, ctx {args.ctx}"
+            + (f", ring {args.ring})" if args.ring else ")"),
+            "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
             "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
-            "dtype": "w4a16 (fp32 accumulate)",
+            "dtype": "w2a16 (fp32 accumulate)" if lowbit else "w4a16 (fp32 accumulate)",
             "data": "synthetic (seeded N(0,0.02) weights, uniform-random token ids)",
-            "config": {"workload": f"Llama-3-8B-shape decode ({cfg['n_layer']} layers), Q4 G128 sym, "
-                                   f"KV {args.kv}, ctx {args.ctx}, batch {B}" + (f" tensor-parallel x{world}" if tp
-                                                                                 else "/GPU"),
+            "config": {"workload": f"Llama-3-8B-shape decode ({cfg['n_layer']} layers), "
+                                   + {"q4_g128": "Q4 G128 sym", "ternary_pt": "BitNet ternary per-tensor",
+                                      "q2k": "Q2_K 256 super-blocks"}[args.weights]
+                                   + f", KV {args.kv}, ctx {args.ctx}"
+                                   + (f" (ring window {args.ring})" if args.ring else "") + f", batch {B}"
+                                   + (f" tensor-parallel x{world}" if tp else "/GPU"),
                        "global_batch": seqs, "seq_len": args.ctx,
                        "parallelism": f"tp{world}" if tp else f"replicas x{world}",
                        "l2": "inputs larger than L2 (weights %.2f GB per step)" % (dec.weight_bytes / 1e9)},
@@ -357,7 +381,7 @@ def run_ours(args, rank, world):
             "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},
             "clocks": clk.summary(), "gpu_launches": launches_per_step * args.steps,
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not lowbit and not args.ring:
             out["cpu_baseline"] = cpu_baseline(cfg, B, args.ctx, kv, args)
     dec.close()
     if tp is not None:
@@ -593,6 +617,9 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (debug only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (all ranks share one batch)")
+    ap.add_argument("--weights", default="q4_g128", choices=["q4_g128", "ternary_pt", "q2k"],
+                    help="projection and lm_head format (2-bit: the long-context low-bit configuration)")
+    ap.add_argument("--ring", type=int, default=0, help="ring cache of this many slots (the sliding window)")
     ap.add_argument("--ref-worker", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.ref_worker:  # child process of reference_cpu: CPU only

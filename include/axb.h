@@ -317,7 +317,8 @@ int axb_argmax(const uint16_t* x_dev, int rows, int n, int ld, int32_t* out_dev,
 typedef struct {
   int n_layer, d_model, n_head, n_kv_head, head_dim, ffn, vocab;
   float eps;
-  int wfmt, group;       /* projection format (AXB_W_Q4T_*, or AXB_W_Q8_G64 group 64: the q8 mode) */
+  int wfmt, group;       /* projection format: AXB_W_Q4T_*, AXB_W_Q8_G64 group 64 (the q8 mode),
+                            or a 2-bit AXB_W_TERNARY_* / AXB_W_Q2_* format (group unused) */
   int lm_fmt, lm_group;  /* lm_head: AXB_W_Q4T_* or AXB_W_Q8_G64 (tied, q8, q4_k_m) */
   int kv_type, kv_group; /* cache format */
   int max_batch, max_seq, max_tokens; /* max_tokens = tokens per sequence per step (<= 64) */
@@ -333,6 +334,17 @@ typedef struct {
    * gate_up as cat(w_gate, w_up); they run on the per-kernel graph path. */
   int dn_fmt, dn_group;
 } axb_model_cfg;
+
+/* Metadata of a 2-bit projection (q2t, from axb_q2t_from_ref) served by the
+ * runner.  For the AXB_W_TERNARY_* / AXB_W_Q2_* formats, a projection's scale
+ * pointer (qkv_s[l], o_s[l], gu_s[l], dn_s[l], lm_s) points to one of these
+ * in host memory; axb_runner_create copies them.  2-bit gate_up projections
+ * keep the reference's row order, cat(w_gate, w_up). */
+typedef struct {
+  const void* meta;         /* q2t per-group metadata, or NULL (TERNARY_PT) */
+  const void* meta2;        /* Q2K_SB256 (d, dmin), else NULL */
+  const uint16_t* pt_scale; /* TERNARY_PT fp16 scale (device), else NULL */
+} axb_q2t_meta;
 
 typedef struct {
   const void* emb_w;  /* Q8_G64 (V, d/4) int32 */
@@ -392,6 +404,10 @@ int axb_runner_step(void* handle, int B, int T, int rope_pos, int write_pos, int
  * kernel launch, 0 when they run as the per-kernel CUDA graph (unsupported
  * format, or AXB_STEP=0 in the environment at creation). */
 int axb_runner_uses_step_kernel(void* handle);
+/* Kernel launches of one step of shape (B, T, tree) once its CUDA graph has
+ * been captured (the graph's kernel nodes + the parameter kernel launched
+ * beside it); -1 if no such step has run through a graph yet. */
+int axb_runner_step_launches(void* handle, int B, int T, int tree);
 
 /* ---- Medusa speculative decoding on the device (engine/medusa.py:48-116,
  *      :231-330, models/medusa.py:20-54, transformer.py:414-445) ----------- */

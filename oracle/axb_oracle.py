@@ -925,6 +925,12 @@ class OracleModel:
     ``q4t_dequant``; everything else -- embeddings, norms, the forward -- is the
     reference's ``q4_rtn`` path unchanged.
 
+    2-bit models: ``"ternary_g64"`` and ``"q2_g64"`` pack projections and an
+    untied lm_head with the reference's ``pack_linear_ternary`` /
+    ``pack_linear_q2_k`` (its ``quantize("ternary" | "q2_k")``,
+    transformer.py:857-862); ``"ternary_pt"`` and ``"q2k"`` use the BASELINE
+    layouts (parity unpinned, as above).
+
     The reference's other quantized-forward modes (transformer.py:840-858):
     ``"q8"`` packs every projection and the lm_head Q8_G64; ``"q4_k_m"`` takes
     the MSE-clipped MARLIN packs of c_attn, c_proj and gate_up as the
@@ -941,7 +947,11 @@ class OracleModel:
         self.eps = cfg["eps"]
         self.V = cfg["vocab"]
         self.F = cfg["ffn"]
-        if weight_format not in ("q4_rtn", "q4_g128_sym", "q8", "q4_k_m"):
+        lowbit = {"ternary_g64": lambda w: ("tern",) + pack_ternary(w),
+                  "q2_g64": lambda w: ("q2",) + pack_q2(w),
+                  "ternary_pt": lambda w: ("tpt",) + ternary_pt_pack(w),
+                  "q2k": lambda w: ("q2k",) + q2k_pack(w)}
+        if weight_format not in ("q4_rtn", "q4_g128_sym", "q8", "q4_k_m", *lowbit):
             raise ValueError(f"unknown weight format {weight_format}")
         self.sym = weight_format == "q4_g128_sym"
         # every packed tensor carries its format: "marlin" (MARLIN Q4), "q4t"
@@ -949,6 +959,8 @@ class OracleModel:
         q8 = lambda w: ("q8",) + pack_q8_g64(w)  # noqa: E731
         if weight_format == "q8":  # transformer.py:852-854: every projection Q8_G64
             pack = q8
+        elif weight_format in lowbit:  # 2-bit projections and lm_head (transformer.py:857-862)
+            pack = lowbit[weight_format]
         elif self.sym:
             pack = lambda w: ("q4t",) + q4t_pack(w, 128, True)  # noqa: E731
         else:
@@ -978,11 +990,19 @@ class OracleModel:
 
     def _w(self, key, packed, K, n):
         if key not in self._dq:
-            tag, p, s = packed
+            tag, p, s = packed[:3]
             if tag == "q4t":
                 w = q4t_dequant(p, s, K, 128, True, n)
             elif tag == "q8":  # quant.py:132-147
                 w = dequant_q8_g64(p, s, K)
+            elif tag == "tern":  # quant.py:277-295
+                w = dequant_ternary(p, s, K)
+            elif tag == "q2":  # quant.py:383-403
+                w = dequant_q2(p, s, K)
+            elif tag == "tpt":
+                w = ternary_pt_dequant(p, s)
+            elif tag == "q2k":
+                w = q2k_dequant(p, s, packed[3])
             else:
                 w = dequant_q4_marlin(p, s, K, n)
             self._dq[key] = torch.from_numpy(w)

@@ -167,3 +167,67 @@ def test_small_model_q8_modes_greedy_parity(name, graph):
         assert _rel(logits[i], fx["logits"][i]) < REL_TOL["fp16"], i
     assert int(dec.argmax(1)[0]) == toks[-1]
     dec.close()
+
+
+_LOWBIT = {"ternary_g64": "W_TERNARY_G64", "q2_g64": "W_Q2_G64", "ternary_pt": "W_TERNARY_PT", "q2k": "W_Q2K_SB256"}
+
+
+@pytest.mark.parametrize("fmt", list(_LOWBIT))
+def test_small_model_lowbit_matches_oracle(fmt):
+    """2-bit models on the runner (the 2-bit GEMV, per-kernel path) against
+    the oracle's forward with the same packs.  "ternary_g64" / "q2_g64" are the
+    reference's quantize("ternary" | "q2_k") packings (transformer.py:857-862),
+    served through from_packed as a reference model's tensors would be;
+    "ternary_pt" / "q2k" are the BASELINE layouts."""
+    from oracle import axb_oracle as O
+
+    from axiomlm_b200 import _lib as L
+    from axiomlm_b200 import ops
+    from axiomlm_b200.model import QuantizedDecoder
+
+    cfg, n_new = SMALL, 12
+    W = make_weights(cfg, 61, ln_random=True)
+    m = O.OracleModel(cfg, W, rope_len=cfg["block_size"], weight_format=fmt)
+    hd = cfg["d_model"] // cfg["n_head"]
+    prompt = np.random.default_rng(62).integers(0, cfg["vocab"], (1, 12))
+    cache = O.OracleCache(cfg["n_layer"], 1, cfg["n_kv_head"], 128, hd, "fp16", False)
+    lg, _ = m.forward(prompt, cache)
+    ref = [lg[0, -1].float()]
+    toks = [int(torch.argmax(ref[-1]))]
+    for _ in range(n_new - 1):
+        lg, _ = m.forward(np.array([[toks[-1]]]), cache)
+        ref.append(lg[0, -1].float())
+        toks.append(int(torch.argmax(ref[-1])))
+    kw = dict(kv_dtype="fp16", max_seq=128, rope_len=cfg["block_size"])
+    ln1 = [lw["ln_1"] for lw in W["layers"]]
+    ln2 = [lw["ln_2"] for lw in W["layers"]]
+    if fmt in ("ternary_g64", "q2_g64"):
+        qw = {"hidden_dim": cfg["ffn"], "c_attn_b": None}
+        for key, src in (("c_attn", "c_attn"), ("c_proj", "c_proj"), ("gu", "gu"), ("wd", "wd")):
+            qw[f"{key}_p"] = [torch.from_numpy(ly[src][1]) for ly in m.layers]
+            qw[f"{key}_s"] = [torch.from_numpy(ly[src][2]) for ly in m.layers]
+        qw["wte_p"], qw["wte_sb"] = (torch.from_numpy(t) for t in m.wte)
+        qw["lmh_p"], qw["lmh_sb"] = torch.from_numpy(m.lmh[1]), torch.from_numpy(m.lmh[2])
+        dec = QuantizedDecoder.from_packed(cfg, qw, ln1, ln2, W["ln_f"], **kw)
+    else:
+        code = getattr(L, _LOWBIT[fmt])
+
+        def q2t(pk, K):
+            t = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in pk[1:]]
+            return ops.q2t_from_ref(code, t[0], t[1], t[2] if len(t) > 2 else None, K)
+
+        d, F = cfg["d_model"], cfg["ffn"]
+        layers = [dict(qkv=q2t(ly["c_attn"], d), o=q2t(ly["c_proj"], d), gu=q2t(ly["gu"], d), down=q2t(ly["wd"], F),
+                       ln_1=lw["ln_1"].cuda(), ln_2=lw["ln_2"].cuda(), qkv_b=None)
+                  for ly, lw in zip(m.layers, W["layers"])]
+        packed = dict(layers=layers, emb_w=torch.from_numpy(m.wte[0]).cuda(), emb_s=torch.from_numpy(m.wte[1]).cuda(),
+                      lm_head=q2t(m.lmh, d), ln_f=W["ln_f"].cuda())
+        dec = QuantizedDecoder(cfg, packed, **kw)
+    assert not dec.uses_step_kernel
+    ours, logits = _greedy_with_logits(dec, prompt, n_new, forced=toks)
+    for i in range(n_new):
+        assert _rel(logits[i], ref[i]) < REL_TOL["fp16"], (i, _rel(logits[i], ref[i]))
+        if ours[i] != toks[i]:  # only at a near-tie of the oracle's own logits
+            top2 = torch.topk(ref[i], 2).values
+            assert float((top2[0] - top2[1]) / top2[0].abs()) < TIE, i
+    dec.close()
