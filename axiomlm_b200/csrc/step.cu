@@ -22,14 +22,18 @@
 //    no unrolled stage copies): the whole step's hot code has to stay in the
 //    SM's instruction cache, because each phase runs once per layer and a cold
 //    fetch of straight-line code costs microseconds.
-//  * Phases are ordered by completion counters in global memory (tiles
-//    finished, attention heads finished) instead of kernel boundaries.  Every
-//    wait is bounded (limits in StepArgs); one that runs out records
-//    AXB_ETIMEOUT and the grid winds down, waiting for its own copies first.
-//  * A tile split between warps is finished by the warp that owns its first
-//    unit, which sums the partials in warp order (deterministic results).  The
-//    partials carry their own flags (value, flag pairs in one vector store),
-//    so no fence or counter sits between a partial and its reader.
+//  * Phases hand off through flagged activation words instead of kernel
+//    boundaries or counters: each 8-byte word holds two fp16 values and the
+//    flag of the phase that wrote it (one vector store), and a reader reloads
+//    the words it needs until they carry that flag.  Every wait is bounded
+//    (limits in StepArgs); one that runs out records AXB_ETIMEOUT and the grid
+//    winds down, waiting for its own copies first.
+//  * A tile split between the warps of a CTA is summed in shared memory, in
+//    warp order, after one CTA barrier; a tile that continues into later CTAs
+//    is finished by the CTA that owns its first unit, which adds their pieces
+//    in CTA order (deterministic results).  Those pieces carry their own flags
+//    (value, flag pairs), so no fence or counter sits between a piece and its
+//    reader.
 //  * Attention: one (sequence, kv head, split) item per CTA, on all 16 warps.
 //    The item's cached rows are bulk-copied before the QKV phase has finished;
 //    RoPE and the new K/V row's quantized write are fused.  The last split of a
