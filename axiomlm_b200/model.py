@@ -11,6 +11,8 @@ runner (replacing MPSQuantizedDecodeRunner, mps_kernels.mm:2982-3737).
 from __future__ import annotations
 
 import ctypes as C
+import dataclasses
+import json
 from typing import Any
 
 import torch
@@ -46,6 +48,81 @@ def _scale_ref(w, keep: list):
         keep.append(m)
         return C.addressof(m)
     return w.scales
+
+
+_WEIGHT_TYPES = {c.__name__: c for c in (ops.Q4TWeight, ops.Q8Weight, ops.Q2TWeight)}
+
+
+def packed_to_tensors(packed: dict) -> tuple[dict, dict]:
+    """A packed-weight dict as flat named tensors (on the host) and string
+    metadata: each weight object's type and scalar fields, and which optional
+    tensors are absent."""
+    tensors: dict = {}
+    meta: dict = {"n_layer": str(len(packed["layers"]))}
+
+    def put(name, v):
+        if v is None:
+            meta[name] = "none"
+        elif isinstance(v, torch.Tensor):
+            # a host copy per name (a tied lm_head shares the embedding's storage)
+            tensors[name] = v.detach().to("cpu", copy=True).contiguous()
+        else:
+            fields = {}
+            for f in dataclasses.fields(v):
+                x = getattr(v, f.name)
+                if isinstance(x, torch.Tensor) or x is None:
+                    put(f"{name}.{f.name}", x)
+                else:
+                    fields[f.name] = x
+            meta[name] = json.dumps({"type": type(v).__name__, **fields})
+
+    for i, ly in enumerate(packed["layers"]):
+        for k in ("qkv", "o", "gu", "down", "ln_1", "ln_2", "qkv_b"):
+            put(f"layers.{i}.{k}", ly.get(k))
+    lm = packed["lm_head"]
+    tied = isinstance(lm, ops.Q8Weight) and lm.words.data_ptr() == packed["emb_w"].data_ptr()
+    for k in ("emb_w", "emb_s", "ln_f") + (() if tied else ("lm_head",)):
+        put(k, packed[k])
+    if tied:  # the embedding matrix is the lm_head: stored once, shared again on load
+        meta["lm_head"] = json.dumps({"tied": True, "N": lm.N, "K": lm.K})
+    return tensors, meta
+
+
+def read_packed(path, device="cuda") -> tuple[dict, dict]:
+    """(cfg, packed dict) from a file ``QuantizedDecoder.save_packed`` wrote,
+    tensors on ``device``."""
+    from safetensors import safe_open
+
+    with safe_open(str(path), framework="pt", device="cpu") as f:
+        meta = f.metadata() or {}
+        if meta.get("format") != QuantizedDecoder._PACKED_FORMAT:
+            raise ValueError(f"{path} is not a packed-weight file of this library")
+        names = set(f.keys())
+        dev = torch.device(device)
+
+        def get(name):
+            if name in names:
+                return f.get_tensor(name).to(dev)
+            m = meta.get(name)
+            if m is None or m == "none":
+                return None
+            d = json.loads(m)
+            if d.get("tied"):
+                return ops.Q8Weight(get("emb_w"), get("emb_s"), d["N"], d["K"])
+            cls = _WEIGHT_TYPES[d.pop("type")]
+            for fld in dataclasses.fields(cls):
+                if fld.name not in d:
+                    d[fld.name] = get(f"{name}.{fld.name}")
+            return cls(**d)
+
+        layers = [{k: get(f"layers.{i}.{k}") for k in ("qkv", "o", "gu", "down", "ln_1", "ln_2", "qkv_b")}
+                  for i in range(int(meta["n_layer"]))]
+        packed = dict(layers=layers, **{k: get(k) for k in ("emb_w", "emb_s", "ln_f")})
+        packed["lm_head"] = get("lm_head")
+        if isinstance(packed["lm_head"], ops.Q8Weight) and json.loads(meta["lm_head"]).get("tied"):
+            packed["lm_head"] = ops.Q8Weight(packed["emb_w"], packed["emb_s"], packed["lm_head"].N,
+                                             packed["lm_head"].K)
+    return json.loads(meta["cfg"]), packed
 
 
 class QuantizedDecoder:
@@ -165,10 +242,11 @@ class QuantizedDecoder:
         layers = []
         for lw in weights["layers"]:
             gu = torch.cat([g(lw["w_gate"]), g(lw["w_up"])], 0)
+            b = lw.get("c_attn_b")
             layers.append(dict(
                 qkv=pack(g(lw["c_attn"])), o=pack(g(lw["c_proj"])), gu=pack(gu, gate_up=True),
                 down=pack(g(lw["w_down"])), ln_1=g(lw["ln_1"]).contiguous(), ln_2=g(lw["ln_2"]).contiguous(),
-                qkv_b=None))
+                qkv_b=None if b is None else b.to(dev, torch.float16).contiguous()))
             del gu
         emb_w, emb_s = ops.pack_q8_g64(g(weights["wte"]))
         # tied embeddings (transformer.py:842-847): the Q8_G64 embedding matrix is the lm_head
@@ -181,6 +259,38 @@ class QuantizedDecoder:
 
             dec.add_medusa_heads(MedusaHeads.from_weights(weights["medusa"], weight_format, device=dev))
         return dec
+
+    @classmethod
+    def from_hf(cls, model_dir, weight_format: str = "q4_rtn", max_seq_len: int | None = None,
+                dtype: torch.dtype = torch.float16, **kw) -> "QuantizedDecoder":
+        """A local Hugging Face checkpoint (Llama-3 / SmolLM2 / Qwen2.5; the
+        reference's load_hf_safetensors, hf_importer.py:199-305), packed on
+        the GPU in ``weight_format``.  ``dtype`` is the load dtype the
+        reference quantizes from (fp16 by default)."""
+        from .hf_import import read_hf_checkpoint
+
+        cfg, w = read_hf_checkpoint(model_dir, dtype=dtype, max_seq_len=max_seq_len)
+        return cls.from_weights(cfg, w, weight_format, **kw)
+
+    # ------------------------------------------------------------ packed-weight cache
+    _PACKED_FORMAT = "axiomlm_b200.packed/1"
+
+    def save_packed(self, path) -> None:
+        """Write the packed weights (every format, as packed) and the model
+        config to one safetensors file, so a large model is packed once;
+        ``load_packed`` serves it again.  Medusa heads are not included."""
+        from safetensors.torch import save_file
+
+        tensors, meta = packed_to_tensors(self.packed)
+        meta["cfg"] = json.dumps(self.cfg)
+        meta["format"] = self._PACKED_FORMAT
+        save_file(tensors, str(path), metadata=meta)
+
+    @classmethod
+    def load_packed(cls, path, **kw) -> "QuantizedDecoder":
+        """A decoder over the weights ``save_packed`` wrote (no packing)."""
+        cfg, packed = read_packed(path, kw.get("device", "cuda"))
+        return cls(cfg, packed, **kw)
 
     @classmethod
     def from_reference(cls, model: Any, **kw) -> "QuantizedDecoder":

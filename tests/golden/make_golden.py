@@ -24,7 +24,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
-from model_weights import SMALL, TINY, make_prompt, make_weights  # noqa: E402
+from model_weights import SMALL, TINY, make_hf_checkpoint, make_prompt, make_weights  # noqa: E402
 
 
 def _np(t):
@@ -246,11 +246,45 @@ def _gen_small(q, ops, modules, compile_medusa_tree, DEFAULT_MEDUSA_TREE_CHOICES
     np.savez_compressed(os.path.join(HERE, "small_tied.npz"), **o)
 
 
+def gen_hf():
+    """The reference's load_hf_safetensors (hf_importer.py:199-305) on seeded
+    tiny checkpoints: its fp16 parameters, which the importer here must
+    reproduce from the same checkpoint files."""
+    import tempfile
+
+    from axiomlm.utils.hf_importer import load_hf_safetensors
+
+    out = {}
+    for tag, seed, bias, tied, shards in (("llama", 71, False, False, 1), ("qwen", 72, True, True, 2)):
+        with tempfile.TemporaryDirectory() as d:
+            make_hf_checkpoint(d, seed, bias=bias, tied=tied, shards=shards)
+            m = load_hf_safetensors(d, device="cpu", dtype=torch.float16)
+        out[f"{tag}_wte"] = _np(m.transformer.wte.weight)
+        out[f"{tag}_ln_f"] = _np(m.transformer.ln_f.weight)
+        out[f"{tag}_lm_head"] = _np(m.lm_head.weight)
+        out[f"{tag}_block_size"] = np.array(m.config.block_size)
+        out[f"{tag}_theta"] = np.array(m.config.rope_theta)
+        for i, b in enumerate(m.transformer.h):
+            out[f"{tag}_{i}_c_attn"] = _np(b.attn.c_attn.weight)
+            if b.attn.c_attn.bias is not None:
+                out[f"{tag}_{i}_c_attn_b"] = _np(b.attn.c_attn.bias)
+            out[f"{tag}_{i}_c_proj"] = _np(b.attn.c_proj.weight)
+            out[f"{tag}_{i}_w_gate"] = _np(b.mlp.w_gate.weight)
+            out[f"{tag}_{i}_w_up"] = _np(b.mlp.w_up.weight)
+            out[f"{tag}_{i}_w_down"] = _np(b.mlp.w_down.weight)
+            out[f"{tag}_{i}_ln_1"] = _np(b.ln_1.weight)
+            out[f"{tag}_{i}_ln_2"] = _np(b.ln_2.weight)
+    np.savez_compressed(os.path.join(HERE, "hf_import.npz"), **out)
+    print("hf_import:", len(out), "arrays")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("AXIOMLM_REFERENCE", ""))
     ap.add_argument("--skip-tiny", action="store_true")
     ap.add_argument("--tiny-only", action="store_true", help="regenerate only the BASELINE config-1 fixtures")
+    ap.add_argument("--hf-only", action="store_true",
+                    help="regenerate only the Hugging Face importer fixture (hf_import.npz)")
     ap.add_argument("--modes-only", action="store_true",
                     help="regenerate only the q8 / q4_k_m model fixtures (small_q8, small_q4km)")
     args = ap.parse_args()
@@ -263,6 +297,10 @@ def main():
     import axiomlm.models.modules as modules
     from axiomlm.engine.medusa import DEFAULT_MEDUSA_TREE_CHOICES, compile_medusa_tree
 
+    if args.hf_only or not args.tiny_only:
+        gen_hf()
+        if args.hf_only:
+            return
     if args.modes_only or not args.tiny_only:
         # the reference's other quantized-forward modes (transformer.py:797-799):
         # Q8_G64 everywhere ("q8"), MSE-clipped Q4 with Q8 w_down and lm_head ("q4_k_m")
