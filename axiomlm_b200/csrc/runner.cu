@@ -776,7 +776,8 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
   const char* sv = getenv("AXB_STEP");
   const StepPlan plan = step_plan(c.max_batch, c.d_model, c.ffn, c.n_head, c.n_kv_head, c.head_dim, c.kv_type,
                                   c.kv_type == AXB_KV_F16 ? c.head_dim : c.kv_group, c.group, c.max_seq);
-  r->step_ok = !(sv && atoi(sv) == 0) && c.tp_world <= 1 && dn_fmt == c.wfmt &&
+  // (the step kernel's phase flags allow 127 layers; deeper models take the graph path)
+  r->step_ok = !(sv && atoi(sv) == 0) && c.tp_world <= 1 && dn_fmt == c.wfmt && c.n_layer <= 127 &&
                step_supported(c.wfmt, c.group, c.lm_fmt, c.lm_group, c.head_dim, c.n_head, c.n_kv_head, c.d_model,
                               c.kv_type, c.kv_group, c.max_seq) &&
                c.ffn % 64 == 0 && plan.smem > 0;
