@@ -204,5 +204,11 @@ __device__ __forceinline__ uint8_t float_to_e4m3(float f) {
 
 // Reference SiLU on fp32: x / (1 + exp(-x)).
 __device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+// SwiGLU of fp16 gate / up values as the reference's fp16 tensors compute
+// F.silu(g) * u (transformer.py:1187-1188): the silu rounded to fp16, then the
+// product rounded to fp16
+__device__ __forceinline__ __half swiglu_h(float g, float u) {
+  return __float2half_rn(__fmul_rn(__half2float(__float2half_rn(silu_f(g))), u));
+}
 
 }  // namespace axb

@@ -393,11 +393,10 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, int tile, const floa
       if (a.epi == AXB_EPI_SWIGLU) {
         const int j = tile * 8 + g;
         if (j < (a.N >> 1)) {
-          // gate and up are fp16-rounded GEMV outputs; silu(g) * u in fp32
-          float gg = __half2float(__float2half_rn(v0));
-          float uu = __half2float(__float2half_rn(v1));
-          float sw = __fmul_rn(silu_f(gg), uu);
-          reinterpret_cast<__half*>(a.y)[(size_t)n * a.ldy + j] = __float2half_rn(sw);
+          // gate and up are fp16-rounded GEMV outputs
+          const float gg = __half2float(__float2half_rn(v0));
+          const float uu = __half2float(__float2half_rn(v1));
+          reinterpret_cast<__half*>(a.y)[(size_t)n * a.ldy + j] = swiglu_h(gg, uu);
         }
         continue;
       }

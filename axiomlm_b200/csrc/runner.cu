@@ -48,24 +48,24 @@ __global__ void residual_add_kernel(__half* __restrict__ x, const __half* __rest
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     x[i] = __float2half_rn(__fadd_rn(__half2float(x[i]), __half2float(y[i])));
 }
-// gate / up rows interleaved by 8 (tile = 8 gate + 8 up rows): sw[m][j] = fp16(silu(g) * u)
+// gate / up rows interleaved by 8 (tile = 8 gate + 8 up rows): sw[m][j] = swiglu_h(g, u)
 __global__ void swiglu_packed_kernel(const __half* __restrict__ gu, int ld, int F, int rows, __half* __restrict__ sw) {
   const size_t total = (size_t)rows * F;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int m = (int)(i / F), j = (int)(i % F);
     const int p = (j >> 3) * 16 + (j & 7);
     const float g = __half2float(gu[(size_t)m * ld + p]), u = __half2float(gu[(size_t)m * ld + p + 8]);
-    sw[(size_t)m * F + j] = __float2half_rn(__fmul_rn(silu_f(g), u));
+    sw[(size_t)m * F + j] = swiglu_h(g, u);
   }
 }
 // gate rows first, then up rows (the reference's gate_up = cat(w_gate, w_up),
-// transformer.py:959-964, as Q8 projections keep it): sw[m][j] = fp16(silu(g) * u)
+// transformer.py:959-964, as Q8 projections keep it): sw[m][j] = swiglu_h(g, u)
 __global__ void swiglu_split_kernel(const __half* __restrict__ gu, int ld, int F, int rows, __half* __restrict__ sw) {
   const size_t total = (size_t)rows * F;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int m = (int)(i / F), j = (int)(i % F);
     const float g = __half2float(gu[(size_t)m * ld + j]), u = __half2float(gu[(size_t)m * ld + F + j]);
-    sw[(size_t)m * F + j] = __float2half_rn(__fmul_rn(silu_f(g), u));
+    sw[(size_t)m * F + j] = swiglu_h(g, u);
   }
 }
 int argmax(const __half* x, int rows, int n, int ld, int32_t* out, cudaStream_t s);

@@ -392,7 +392,7 @@ __device__ __forceinline__ void step_epilogue(const StepArgs& a, const GPh& g, i
       const int n = 2 * t4 + e;
       const float gv = __half2float(__float2half_rn(acc[e]));
       const float uv = __half2float(__float2half_rn(acc[2 + e]));
-      const uint32_t sv = __half_as_ushort(__float2half_rn(__fmul_rn(silu_f(gv), uv)));
+      const uint32_t sv = __half_as_ushort(swiglu_h(gv, uv));
       const uint32_t nb = __shfl_down_sync(0xffffffffu, sv, 4);
       if ((gg & 1) == 0 && n < M && j < a.F) st_act(a.sw + ((size_t)n * a.F + j) / 2, sv | (nb << 16), efl);
     }
