@@ -29,6 +29,11 @@ WEIGHT_FORMATS = {
     # reference q8: every projection and the lm_head Q8_G64 in its own layout
     # (transformer.py:847-855), gate_up as cat(w_gate, w_up)
     "q8": (L.W_Q8_G64, 64),
+    # reference q4 / q4_k_m: affine G64 with the clip search (ops.pack_q4_mse),
+    # importance-weighted as _ensure_quant_weights weighs it (transformer.py:
+    # 880-884, 931-941); q4_k_m keeps w_down and the lm_head Q8_G64
+    "q4": (L.W_Q4T_AFFINE, 64),
+    "q4_k_m": (L.W_Q4T_AFFINE, 64),
 }
 
 
@@ -225,7 +230,11 @@ class QuantizedDecoder:
         mode (transformer.py:822-1008): projections and an untied lm_head in
         Q4, token embeddings in Q8_G64 (also the lm_head when the embeddings are
         tied), RMSNorm weights kept fp32.  ``weight_format="q8"`` packs every
-        projection and the lm_head Q8_G64 (the reference's q8 mode)."""
+        projection and the lm_head Q8_G64 (the reference's q8 mode); "q4" and
+        "q4_k_m" pack with the reference's clip search, c_attn weighted by
+        |ln_1|, gate_up by |ln_2|, w_down by |w_gate row| * |w_up row| and the
+        lm_head by |ln_f| ("q4"), or w_down and the lm_head in Q8_G64
+        ("q4_k_m")."""
         dev = torch.device(kw.get("device", "cuda"))
         fmt, group = WEIGHT_FORMATS[weight_format]
         sym = fmt == L.W_Q4T_SYM
@@ -234,24 +243,41 @@ class QuantizedDecoder:
         def g(t):
             return t.to(dev, torch.float32)
 
-        def pack(w, gate_up=False):
+        mse = weight_format in ("q4", "q4_k_m")
+
+        def q8(w):
+            return ops.Q8Weight(*ops.pack_q8_g64(w), w.shape[0], w.shape[1])
+
+        def pack(w, gate_up=False, imp=None):
             if fmt == L.W_Q8_G64:
-                return ops.Q8Weight(*ops.pack_q8_g64(w), w.shape[0], w.shape[1])
+                return q8(w)
+            if mse:
+                return ops.pack_q4_mse(w, imp, gate_up=gate_up)
             return ops.pack_q4t(w, group, sym, gate_up=gate_up)
 
         layers = []
         for lw in weights["layers"]:
-            gu = torch.cat([g(lw["w_gate"]), g(lw["w_up"])], 0)
+            wg_, wu_ = g(lw["w_gate"]), g(lw["w_up"])
+            gu = torch.cat([wg_, wu_], 0)
             b = lw.get("c_attn_b")
+            ln1, ln2 = g(lw["ln_1"]).contiguous(), g(lw["ln_2"]).contiguous()
+            if weight_format == "q4_k_m":
+                down = q8(g(lw["w_down"]))
+            else:
+                down = pack(g(lw["w_down"]), imp=wg_.norm(dim=1) * wu_.norm(dim=1) if mse else None)
             layers.append(dict(
-                qkv=pack(g(lw["c_attn"])), o=pack(g(lw["c_proj"])), gu=pack(gu, gate_up=True),
-                down=pack(g(lw["w_down"])), ln_1=g(lw["ln_1"]).contiguous(), ln_2=g(lw["ln_2"]).contiguous(),
+                qkv=pack(g(lw["c_attn"]), imp=ln1.abs() if mse else None), o=pack(g(lw["c_proj"])),
+                gu=pack(gu, gate_up=True, imp=ln2.abs() if mse else None), down=down, ln_1=ln1, ln_2=ln2,
                 qkv_b=None if b is None else b.to(dev, torch.float16).contiguous()))
-            del gu
+            del gu, wg_, wu_
         emb_w, emb_s = ops.pack_q8_g64(g(weights["wte"]))
         # tied embeddings (transformer.py:842-847): the Q8_G64 embedding matrix is the lm_head
-        lm = (ops.Q8Weight(emb_w, emb_s, emb_w.shape[0], emb_w.shape[1] * 4) if tied
-              else pack(g(weights["lm_head"])))
+        if tied:
+            lm = ops.Q8Weight(emb_w, emb_s, emb_w.shape[0], emb_w.shape[1] * 4)
+        elif weight_format == "q4_k_m":
+            lm = q8(g(weights["lm_head"]))
+        else:
+            lm = pack(g(weights["lm_head"]), imp=g(weights["ln_f"]).abs() if mse else None)
         packed = dict(layers=layers, emb_w=emb_w, emb_s=emb_s, lm_head=lm, ln_f=g(weights["ln_f"]).contiguous())
         dec = cls(cfg, packed, **kw)
         if weights.get("medusa"):

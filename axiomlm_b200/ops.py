@@ -134,6 +134,79 @@ def q4t_from_q4g64(w_packed: torch.Tensor, scales_biases: torch.Tensor, n_out: i
     return Q4TWeight(words, scales, N, K, 64, L.W_Q4T_AFFINE, gate_up)
 
 
+def q4_mse_codes(w: torch.Tensor, importance: torch.Tensor | None = None, steps: int = 13,
+                 min_shrink: float = 0.72) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The reference's clip search for affine Q4 G64 (pack_linear_q4_marlin
+    with clip_search=True, quant.py:495-571), on ``w``'s device: per 64-wide
+    group, shrink the low end towards the group's (importance-weighted) mean
+    by each of ``steps`` factors from 1 to ``min_shrink`` and keep the one
+    with the least importance-weighted squared error, then the high end the
+    same way at that low end.  Scale and bias are evaluated as the fp16 values
+    they are stored as.  ``importance`` (K,) is squared and normalized to a
+    unit mean per group.  The steps and their fp32 / fp16 rounding points are
+    the reference's, so the packs are identical.  Returns codes (N, K) int32
+    in 0..15, scales and biases (N, K/64) fp16."""
+    w = w.float()
+    N, K = w.shape
+    if K % 64:
+        raise ValueError(f"K ({K}) must be a multiple of 64")
+    wg = w.reshape(N, K // 64, 64)
+    imp = None
+    if importance is not None:
+        if importance.numel() != K:
+            raise ValueError(f"importance has {importance.numel()} entries, expected {K}")
+        imp = importance.to(w.device, torch.float32).reshape(1, K // 64, 64)
+        imp = imp * imp
+        imp = imp / imp.mean(dim=-1, keepdim=True).clamp(min=1e-8)
+    lo0 = wg.amin(dim=-1, keepdim=True)
+    hi0 = wg.amax(dim=-1, keepdim=True)
+    mu = (wg * imp).mean(dim=-1, keepdim=True) if imp is not None else wg.mean(dim=-1, keepdim=True)
+    shrink = torch.linspace(1.0, min_shrink, steps=max(2, steps)).tolist()
+
+    def err(scale_h, bias_h):
+        sc, bi = scale_h.float(), bias_h.float()
+        q = ((wg - bi) / sc.clamp(min=1e-8)).round().clamp(0.0, 15.0)
+        d = wg - (q * sc + bi)
+        return (imp * (d * d)).sum(dim=-1) if imp is not None else (d * d).sum(dim=-1)
+
+    # the low end, with the group's maximum
+    best = torch.full(wg.shape[:2], float("inf"), dtype=torch.float32, device=w.device)
+    lo = lo0.clone()
+    for a in shrink:
+        cand = mu + a * (lo0 - mu)
+        e = err(((hi0 - cand).clamp(min=1e-8) / 15.0).to(torch.float16), cand.to(torch.float16))
+        better = e < best
+        best = torch.where(better, e, best)
+        lo = torch.where(better.unsqueeze(-1), cand, lo)
+    # the high end, at that low end
+    best.fill_(float("inf"))
+    bias = lo.to(torch.float16)
+    scale = ((hi0 - lo).clamp(min=1e-8) / 15.0).to(torch.float16)
+    for a in shrink:
+        cand = mu + a * (hi0 - mu)
+        sc_h = ((cand - lo).clamp(min=1e-8) / 15.0).to(torch.float16)
+        e = err(sc_h, bias)
+        better = e < best
+        best = torch.where(better, e, best)
+        scale = torch.where(better.unsqueeze(-1), sc_h, scale)
+    q = ((wg - bias.float()) / scale.float().clamp(min=1e-8)).round().clamp(0.0, 15.0).to(torch.int32)
+    return q.reshape(N, K), scale.reshape(N, K // 64), bias.reshape(N, K // 64)
+
+
+def pack_q4_mse(w: torch.Tensor, importance: torch.Tensor | None = None, gate_up: bool = False) -> Q4TWeight:
+    """The reference's default Q4 packing ("q4" / "q4_k_m": the clip search
+    of ``q4_mse_codes``) as q4t affine G64: the codes go through the legacy
+    Q4_G64 word layout (8 sequential nibbles per int32, quant.py:42-46) into
+    the q4t relayout."""
+    q, sc, bi = q4_mse_codes(w, importance)
+    N, K = q.shape
+    qv = q.reshape(N, K // 8, 8)
+    words = torch.zeros((N, K // 8), dtype=torch.int32, device=q.device)
+    for j in range(8):  # nibble j of a word holds k = 8 * word + j
+        words |= (qv[:, :, j] & 0xF) << (4 * j)
+    return q4t_from_q4g64(words, torch.stack([sc, bi], dim=-1), N, gate_up=gate_up)
+
+
 def qmv_q4_g64(x: torch.Tensor, w_packed: torch.Tensor, scales_biases: torch.Tensor) -> torch.Tensor:
     """qmv_q4_g64 / qmm_q4_g64 (quant.py:166-198) through the q4t GEMV (the
     relayout is cached per weight tensor)."""

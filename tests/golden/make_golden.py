@@ -246,6 +246,26 @@ def _gen_small(q, ops, modules, compile_medusa_tree, DEFAULT_MEDUSA_TREE_CHOICES
     np.savez_compressed(os.path.join(HERE, "small_tied.npz"), **o)
 
 
+def gen_mse(q):
+    """pack_linear_q4_marlin's clip search (quant.py:495-571) with column
+    importance, on fp32 and fp16 inputs (the model's parameters can be
+    either): the packs the clip-search restatement must reproduce."""
+    g = torch.Generator().manual_seed(4321)
+    W = torch.randn(40, 256, generator=g) * 0.02
+    W[5, 100] = 0.4  # outlier
+    W[9, 64:128] = 0.01  # constant group
+    imp_ln = (1.0 + 0.1 * torch.randn(256, generator=g)).abs()  # |ln weight| (c_attn, gate_up, lm_head)
+    a = torch.randn(256, 256, generator=g) * 0.02
+    b = torch.randn(256, 256, generator=g) * 0.02
+    imp_sw = a.norm(dim=1) * b.norm(dim=1)  # |w_gate row| * |w_up row| (w_down)
+    out = {"W": _np(W), "imp_ln": _np(imp_ln), "imp_sw": _np(imp_sw)}
+    for tag, w, imp in (("f32_ln", W, imp_ln), ("f16_none", W.half(), None), ("f16_sw", W.half(), imp_sw)):
+        wm, sb = q.pack_linear_q4_marlin(w, clip_search=True, col_importance=imp)
+        out[f"{tag}_w"], out[f"{tag}_sb"] = _np(wm), _np(sb)
+    np.savez_compressed(os.path.join(HERE, "quant_mse.npz"), **out)
+    print("quant_mse:", len(out), "arrays")
+
+
 def gen_hf():
     """The reference's load_hf_safetensors (hf_importer.py:199-305) on seeded
     tiny checkpoints: its fp16 parameters, which the importer here must
@@ -283,6 +303,8 @@ def main():
     ap.add_argument("--reference", default=os.environ.get("AXIOMLM_REFERENCE", ""))
     ap.add_argument("--skip-tiny", action="store_true")
     ap.add_argument("--tiny-only", action="store_true", help="regenerate only the BASELINE config-1 fixtures")
+    ap.add_argument("--mse-only", action="store_true",
+                    help="regenerate only the clip-search packing fixture (quant_mse.npz)")
     ap.add_argument("--hf-only", action="store_true",
                     help="regenerate only the Hugging Face importer fixture (hf_import.npz)")
     ap.add_argument("--modes-only", action="store_true",
@@ -297,6 +319,10 @@ def main():
     import axiomlm.models.modules as modules
     from axiomlm.engine.medusa import DEFAULT_MEDUSA_TREE_CHOICES, compile_medusa_tree
 
+    if args.mse_only or not args.tiny_only:
+        gen_mse(q)
+        if args.mse_only:
+            return
     if args.hf_only or not args.tiny_only:
         gen_hf()
         if args.hf_only:
