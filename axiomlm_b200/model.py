@@ -58,6 +58,27 @@ def _scale_ref(w, keep: list):
 _WEIGHT_TYPES = {c.__name__: c for c in (ops.Q4TWeight, ops.Q8Weight, ops.Q2TWeight)}
 
 
+def packed_kind(p: torch.Tensor, s: torch.Tensor) -> str:
+    """Which of the reference's packings a (words, scales) pair is, by shape
+    and dtype (_ensure_quant_weights, transformer.py:849-876):
+    "marlin" ((N/8, K/64, 32, 2) int32 MARLIN ladder: q4, q4_k_m, q4_rtn),
+    "ternary_g64" / "q2_g64" ((N, K/4) uint8 codes with (N, K/64) scales or
+    (N, K/64, 2) scale / bias pairs: ternary, q2_k), "q8_g64" ((N, K/4)
+    int32: q8, and w_down / lm_head in q4_k_m), "q4_g64" ((N, K/8) int32:
+    q4_legacy)."""
+    if p.ndim == 4:
+        return "marlin"
+    if p.ndim == 2 and s.ndim >= 2:
+        k64 = s.shape[1] * 64
+        if p.dtype == torch.uint8 and p.shape[1] * 4 == k64:
+            return "q2_g64" if s.ndim == 3 else "ternary_g64"
+        if p.dtype == torch.int32 and p.shape[1] * 4 == k64:
+            return "q8_g64"
+        if p.dtype == torch.int32 and p.shape[1] * 8 == k64:
+            return "q4_g64"
+    raise NotImplementedError(f"packed weight of {p.dtype} {tuple(p.shape)} / {tuple(s.shape)}")
+
+
 def packed_to_tensors(packed: dict) -> tuple[dict, dict]:
     """A packed-weight dict as flat named tensors (on the host) and string
     metadata: each weight object's type and scalar fields, and which optional
@@ -351,18 +372,15 @@ class QuantizedDecoder:
         def rl(p, s, n, gu=False):
             p = torch.as_tensor(p)
             s = torch.as_tensor(s)
-            if p.ndim == 4:  # MARLIN ladder
+            kind = packed_kind(p, s)
+            if kind == "marlin":
                 return ops.q4t_from_marlin(p.to(dev), s.to(dev), n, gate_up=gu)
-            if p.dtype == torch.uint8 and p.shape[1] * 4 == s.shape[1] * 64:
-                # 2-bit codes (N, K/4): ternary with group-64 scales (quant.py:236-274)
-                # or "Q2_K" G64 (scale, bias) pairs (quant.py:339-381)
-                fmt = L.W_Q2_G64 if s.ndim == 3 else L.W_TERNARY_G64
+            if kind in ("ternary_g64", "q2_g64"):
+                fmt = L.W_Q2_G64 if kind == "q2_g64" else L.W_TERNARY_G64
                 return ops.q2t_from_ref(fmt, p.to(dev).contiguous(), s.to(dev).contiguous(), None, p.shape[1] * 4)
-            if p.shape[1] * 4 == s.shape[1] * 64:  # Q8_G64 (N, K/4) int32 words: kept as packed
+            if kind == "q8_g64":  # kept as packed
                 return ops.Q8Weight(p.to(dev).contiguous(), s.to(dev).contiguous(), n, p.shape[1] * 4)
-            if p.shape[1] * 8 == s.shape[1] * 64:  # legacy Q4_G64 (N, K/8) words
-                return ops.q4t_from_q4g64(p.to(dev).contiguous(), s.to(dev).contiguous(), n, gate_up=gu)
-            raise NotImplementedError(f"packed weight of shape {tuple(p.shape)} / {tuple(s.shape)}")
+            return ops.q4t_from_q4g64(p.to(dev).contiguous(), s.to(dev).contiguous(), n, gate_up=gu)
 
         def f32(w):
             return torch.as_tensor(w).detach().to(dev, torch.float32).contiguous()
