@@ -225,6 +225,8 @@ def qmv_q4_g64(x: torch.Tensor, w_packed: torch.Tensor, scales_biases: torch.Ten
 
 _LEGACY_CACHE: dict = {}
 qmm_q4_g64 = qmv_q4_g64
+# the Metal entry points' names (quant.py:177-178, 194)
+qmv_q4_g64_mps = qmm_q4_g64_mps = qmv_q4_g64
 
 
 @dataclass
@@ -259,6 +261,8 @@ def qmv_q8_g64(x: torch.Tensor, w_packed: torch.Tensor, scales_biases: torch.Ten
 
 
 qmm_q8_g64 = qmv_q8_g64
+# the Metal entry points' names (quant.py:212-213, 229)
+qmv_q8_g64_mps = qmm_q8_g64_mps = qmv_q8_g64
 
 
 def pack_q8_g64(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -714,6 +718,22 @@ def gqa_tree_verify_mps(q, k_cache, v_cache, tree_mask, prefix_len: int, write_p
         q_tok = q.reshape(1, T, -1)
     return _attention(q_tok, k_cache, v_cache, k_scales, v_scales, kv_dtype.lower(), masks=masks,
                       prefix_len=prefix_len, write_pos=write_pos, T=T)
+
+
+def gqa_tree_verify_fp8_mps(q, k_cache, v_cache, k_scales, v_scales, tree_mask, prefix_len: int, write_pos: int,
+                            n_head: int, num_splits: int = 0):
+    """The FP8-cache tree verify in the argument order of the Metal entry
+    point (ops.py:697-708)."""
+    return gqa_tree_verify_mps(q, k_cache, v_cache, tree_mask, prefix_len, write_pos, n_head, num_splits, k_scales,
+                               v_scales, "fp8")
+
+
+def gqa_tree_verify_int4_mps(q, k_cache, v_cache, k_scales, v_scales, tree_mask, prefix_len: int, write_pos: int,
+                             n_head: int, num_splits: int = 0):
+    """The INT4-cache tree verify in the argument order of the Metal entry
+    point (ops.py:715-726)."""
+    return gqa_tree_verify_mps(q, k_cache, v_cache, tree_mask, prefix_len, write_pos, n_head, num_splits, k_scales,
+                               v_scales, "int4")
 
 
 def compact_tree_kv(cache: torch.Tensor, scales: torch.Tensor | None, write_pos: int, accepted: list[int],
