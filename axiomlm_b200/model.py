@@ -511,6 +511,33 @@ class QuantizedDecoder:
         self.medusa_heads = heads
         return self
 
+    def forward_with_medusa(self, idx: torch.Tensor, kv_caches: Any = None, return_all_logits: bool = False,
+                            return_medusa: bool = True):
+        """transformer.py:447-520 (its decode-runner branch): the T tokens of
+        one sequence as a causal chain, the cache counters moved past them,
+        and the Medusa heads on the final-norm rows.  Returns (logits (1, T or
+        1, V), per-head logits, ``kv_caches``); with T > 1 only the last
+        position unless ``return_all_logits``."""
+        idx = idx if idx.dim() == 2 else idx.view(1, -1)
+        B, T = idx.shape
+        if B != 1:
+            raise ValueError("forward_with_medusa serves one sequence (as the reference's runner does)")
+        seen = self.cache.total_seen_tokens[0]
+        logits = self.forward_tree_verify(idx, list(range(T)), [(1 << (i + 1)) - 1 for i in range(T)])
+        self.cache.advance(seen + T)
+        x_norm = self.get_last_norm(T)
+        if T > 1 and not return_all_logits:
+            logits, x_norm = logits[:, -1:], x_norm[:, -1:]
+        med = self.eval_medusa_heads(x_norm) if return_medusa and self.medusa_heads is not None else []
+        return logits, med, kv_caches
+
+    def get_decode_runner(self, cache: Any = None) -> "QuantizedDecoder":
+        """transformer.py:1202: the decode runner bound to the cache; here the
+        decoder is its own runner (bound to ``self.cache``)."""
+        if cache is not None and cache is not self.cache:
+            raise ValueError("this decoder's runner is bound to its own cache (dec.cache)")
+        return self
+
     def eval_medusa_heads(self, x_norm: torch.Tensor) -> list[torch.Tensor]:
         """transformer.py:414-445: the heads' logits on final-norm rows."""
         if self.medusa_heads is None:
