@@ -4,7 +4,7 @@
 // Replaces qmv_ternary / qmm_ternary (axiomlm/kernels/quant.py:298-336, Metal
 // qmv_ternary_half_kernel :3990 / qmm_ternary_half_kernel :4074) and
 // qmv_q2_k / qmm_q2_k (quant.py:406-444, Metal :4167 / :4246), plus the
-// BASELINE-only layouts (per-tensor ternary scale; K-quant-style 256-element
+// benchmark-only layouts (no reference implementation) (per-tensor ternary scale; K-quant-style 256-element
 // super-blocks with 4-bit sub-scales and sub-mins).
 //
 // Layout q2t.  The reference's row-major codes (4 per byte, element i of a

@@ -24,7 +24,7 @@ from .cache import StaticKVCache
 WEIGHT_FORMATS = {
     # reference q4_rtn: MARLIN RTN values, affine (scale, bias), group 64
     "q4_rtn": (L.W_Q4T_AFFINE, 64),
-    # BASELINE config: symmetric, group 128, fp16 scales (4.125 bits/weight)
+    # the benchmark format: symmetric, group 128, fp16 scales (4.125 bits/weight)
     "q4_g128_sym": (L.W_Q4T_SYM, 128),
     # reference q8: every projection and the lm_head Q8_G64 in its own layout
     # (transformer.py:847-855), gate_up as cat(w_gate, w_up)

@@ -298,7 +298,7 @@ def dequant_q8_rows(indices: torch.Tensor, w_packed: torch.Tensor, scales_biases
 
 
 def dequantize_ternary(w_packed, scales, K: int | None = None) -> torch.Tensor:
-    """quant.py:277-295 (per-group scales) or the per-tensor BASELINE form
+    """quant.py:277-295 (per-group scales) or the per-tensor benchmark form
     when ``scales`` has one element."""
     w = _cuda(w_packed, "w_packed")
     s = _cuda(scales, "scales")

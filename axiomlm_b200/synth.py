@@ -1,4 +1,4 @@
-"""Seeded synthetic models at the BASELINE shapes (random N(0, 0.02) weights
+"""Seeded synthetic models at the benchmark shapes (random N(0, 0.02) weights
 packed on the GPU, uniform-random token ids), shared by the benchmark and the
 op micro-benchmarks.  There are no checkpoints or datasets on this path: the
 weights only have to have the right shapes, formats and value distribution."""
@@ -7,13 +7,13 @@ from __future__ import annotations
 
 import torch
 
-# Llama-3-8B shape
+# Llama-3-8B shape (the decode, tree-verification and long-context benchmarks)
 CFG_8B = dict(n_layer=32, d_model=4096, n_head=32, n_kv_head=8, ffn=14336, vocab=128256, eps=1e-5, theta=10000.0,
               block_size=8192)
 
 
 def _q2t_random(fmt, N, K, g):
-    """A 2-bit projection with random codes at the BASELINE value
+    """A 2-bit projection with random codes at the benchmark's value
     distribution: uniform bytes give each 2-bit ternary field +1 and -1 with
     p = .25 and 0 with p = .5; the scales are those of N(0, 0.02) weights
     (per-tensor absmean 0.016; K-quant d, dmin about range / 15)."""
@@ -38,7 +38,7 @@ def build_decoder(cfg, batch, ctx, kv, seed=0, tp=None, max_tokens=1, extra_slot
     norms, replicated, come from the same seed on every rank.
 
     ``weights="ternary_pt" | "q2k"``: the projections and the lm_head in that
-    2-bit BASELINE layout (random codes, ``_q2t_random``).  ``ring``: a ring
+    2-bit benchmark-only layout (random codes, ``_q2t_random``).  ``ring``: a ring
     cache of that many slots (the sliding window) instead of ``ctx +
     extra_slots``; positions run on to ``ctx + extra_slots``."""
     from . import _lib as L

@@ -1,9 +1,9 @@
-"""Decode throughput of the quantized hot path (BASELINE.json metric).
+"""Decode throughput of the quantized hot path (the headline benchmark's metric).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
                     [--batch B] [--ctx C] [--layers L]
 
-Workload (one GPU): Llama-3-8B-shaped decoder (32 layers,
+Workload (the 8B decode benchmark, one GPU): Llama-3-8B-shaped decoder (32 layers,
 d 4096, 32/8 heads, head_dim 128, FFN 14336, vocab 128256), random N(0, 0.02)
 weights quantized Q4 group-128 symmetric (4.125 bits/weight), FP8-e4m3 KV
 cache with one fp16 scale per (token, head), a 4096-token context of random

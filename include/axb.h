@@ -43,10 +43,10 @@ extern "C" {
 /* 2-bit formats (q2t layout on the device, relaid out from these reference packings):
  * TERNARY_G64: pack_linear_ternary (quant.py:236-274): codes (N, K/4) u8 (0 -> 0,
  *   1 -> +1, 2 -> -1), scales (N, K/64) fp16, w = q * s.
- * TERNARY_PT:  same codes, one per-tensor fp16 absmean scale.
+ * TERNARY_PT:  same codes, one per-tensor fp16 absmean scale (the format of the GEMV sweep's ternary case).
  * Q2_G64:      pack_linear_q2_k (quant.py:339-381): codes (N, K/4) u8 (u in 0..3),
  *   (scale, bias) (N, K/64, 2) fp16, w = fp16(fp16(u * s) + b).
- * Q2K_SB256:   K-quant-style super-blocks: codes (N, K/4) u8,
+ * Q2K_SB256:   K-quant-style super-blocks (the long-context low-bit configuration's format): codes (N, K/4) u8,
  *   sub (N, K/16) u8 = sc | mn << 4, (d, dmin) (N, K/256, 2) fp16,
  *   w = d * sc * u - dmin * mn. */
 #define AXB_W_TERNARY_G64 4
@@ -79,8 +79,8 @@ size_t axb_q4t_scales_bytes(int N, int K, int group, int fmt);
 
 /* Round-to-nearest pack of fp32 (N, K) row-major weights into q4t.
  * fmt AXB_W_Q4T_AFFINE reproduces pack_linear_q4_marlin(clip_search=False)
- * values (quant.py:475-486) at any group; AXB_W_Q4T_SYM is the BASELINE
- * group-128 symmetric form.  `gate_up_interleave`: rows are [gate(F); up(F)]
+ * values (quant.py:475-486) at any group; AXB_W_Q4T_SYM is the
+ * benchmark's group-128 symmetric form.  `gate_up_interleave`: rows are [gate(F); up(F)]
  * and are stored interleaved by 8 for the SwiGLU epilogue. */
 int axb_q4t_pack(const float* w_dev, int N, int K, int group, int fmt, int gate_up_interleave,
                  void* words_dev, void* scales_dev, void* stream);

@@ -422,7 +422,7 @@ def _as_kv_input(x) -> np.ndarray:
 def quant_kv_fp8(x, group: int = 64) -> tuple[np.ndarray, np.ndarray]:
     """quant.py:692-724: ``q = e4m3fn(x / scale)`` with ``scale = amax/448``
     (rounding points per ``_kv_scale_and_ratio``).  ``group`` = 64 is the
-    reference; ``group`` = head_dim is the per-(token, head) BASELINE variant."""
+    reference; ``group`` = head_dim is the per-(token, head) benchmark variant."""
     a = _as_kv_input(x)
     xg = a.reshape(*a.shape[:-1], -1, group)
     scale, r = _kv_scale_and_ratio(xg, 448.0)
@@ -442,8 +442,8 @@ def dequant_kv_fp8(q, scales, group: int = 64) -> np.ndarray:
 def quant_kv_int4(x, group: int = 64) -> tuple[np.ndarray, np.ndarray]:
     """quant.py:771-807: ``q = clip(rint(x / scale), -8, 7)``, ``scale =
     amax/7``, low nibble = even element.  A zero scale gives the reference's
-    x/0 path: +inf -> 7, -inf -> -8, NaN -> 0.  ``group`` = 32 is the BASELINE
-    variant."""
+    x/0 path: +inf -> 7, -inf -> -8, NaN -> 0.  ``group`` = 32 is the
+    long-context benchmark's variant."""
     a = _as_kv_input(x)
     hd = a.shape[-1]
     xg = a.reshape(*a.shape[:-1], -1, group)
@@ -631,7 +631,7 @@ def q4t_from_marlin(w_marlin, sb_marlin, n_out: int | None = None, gate_up: bool
 
 
 def ternary_pt_pack(w):
-    """BitNet b1.58 with one per-tensor absmean fp16 scale.
+    """BitNet b1.58 with one per-tensor absmean fp16 scale (the format of the GEMV sweep's ternary case).
 
     Same 2-bit codes and byte order as the reference (quant.py:264-274);
     ``scale = fp16(max(mean|w|, 1e-5))`` over the whole matrix (float64 sum).
@@ -653,7 +653,7 @@ def ternary_pt_dequant(packed, scale) -> np.ndarray:
 
 
 def q2k_pack(w):
-    """K-quant-style 2-bit super-blocks (no reference impl).
+    """K-quant-style 2-bit super-blocks (the long-context low-bit format; no reference implementation).
 
     Per 256-element super-block: fp16 ``d`` (scale of sub-scales) and fp16
     ``dmin`` (scale of sub-mins); per 16-element sub-block a 4-bit sub-scale
@@ -705,7 +705,7 @@ def q2k_dequant(codes, sub, dm) -> np.ndarray:
 
 
 def quant_kv_fp8_head(x):
-    """FP8 KV with one fp16 scale per (token, head): the
+    """FP8 KV with one fp16 scale per (token, head) (the 8B decode benchmark's cache format): the
     reference rule at group size = head_dim."""
     a = _as_kv_input(x)
     q, s = quant_kv_fp8(a, group=a.shape[-1])
@@ -718,7 +718,7 @@ def dequant_kv_fp8_head(q, scale):
 
 
 def quant_kv_int4_g32(x):
-    """INT4 KV with 32-element groups."""
+    """INT4 KV with 32-element groups (the long-context low-bit configuration's format)."""
     return quant_kv_int4(x, group=32)
 
 
@@ -919,7 +919,7 @@ class OracleModel:
     RMSNorm weights stay fp32 (the reference model's parameter dtype), so the
     norms are evaluated in fp32 and cast to fp16 by ``_qlin``.
 
-    ``weight_format="q4_g128_sym"`` is the BASELINE variant (parity
+    ``weight_format="q4_g128_sym"`` is the benchmark variant (parity
     unpinned): the projections and an untied lm_head are quantized by
     ``q4t_pack`` (symmetric, group 128, fp16 scales) and dequantized by
     ``q4t_dequant``; everything else -- embeddings, norms, the forward -- is the
@@ -928,8 +928,8 @@ class OracleModel:
     2-bit models: ``"ternary_g64"`` and ``"q2_g64"`` pack projections and an
     untied lm_head with the reference's ``pack_linear_ternary`` /
     ``pack_linear_q2_k`` (its ``quantize("ternary" | "q2_k")``,
-    transformer.py:857-862); ``"ternary_pt"`` and ``"q2k"`` use the BASELINE
-    layouts (parity unpinned, as above).
+    transformer.py:857-862); ``"ternary_pt"`` and ``"q2k"`` use the
+    benchmark-only layouts (parity unpinned, as above).
 
     The reference's other quantized-forward modes (transformer.py:840-858):
     ``"q8"`` packs every projection and the lm_head Q8_G64; ``"q4_k_m"`` takes

@@ -302,7 +302,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("AXIOMLM_REFERENCE", ""))
     ap.add_argument("--skip-tiny", action="store_true")
-    ap.add_argument("--tiny-only", action="store_true", help="regenerate only the BASELINE config-1 fixtures")
+    ap.add_argument("--tiny-only", action="store_true", help="regenerate only the tiny-model fixtures")
     ap.add_argument("--mse-only", action="store_true",
                     help="regenerate only the clip-search packing fixture (quant_mse.npz)")
     ap.add_argument("--hf-only", action="store_true",

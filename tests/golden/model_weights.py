@@ -12,7 +12,7 @@ import torch
 
 SMALL = dict(n_layer=2, d_model=256, n_head=4, n_kv_head=2, ffn=512, vocab=1024,
              eps=1e-5, theta=10000.0, block_size=256)
-# BASELINE config 1 (the reference's CPU-runnable case).
+# The reference's CPU-runnable tiny model.
 TINY = dict(n_layer=12, d_model=768, n_head=12, n_kv_head=12, ffn=2048, vocab=32000,
             eps=1e-5, theta=10000.0, block_size=512)
 

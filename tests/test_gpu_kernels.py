@@ -122,7 +122,7 @@ def test_ternary_and_q2_dequant_bit_exact(ax):
     assert np.array_equal(_bits(t), g["ter_dq"].view(np.uint16))
     q = ax.dequantize_q2_k(_cu(g["q2_w"]), _cu(g["q2_sb"]), 256)
     assert np.array_equal(_bits(q), g["q2_dq"].view(np.uint16))
-    # per-tensor ternary
+    # per-tensor ternary (the format of the GEMV sweep's ternary case)
     w = (np.random.default_rng(3).standard_normal((16, 128)) * 0.02).astype(np.float32)
     pw, ps = O.ternary_pt_pack(w)
     t = ax.dequantize_ternary(_cu(pw), _cu(ps), 128)
@@ -222,8 +222,8 @@ def test_gemv_big_shapes_and_determinism(ax):
 @pytest.mark.parametrize("N,K,M", [(40, 256, 3), (32000, 768, 1), (32000, 768, 5), (1000, 4096, 12)])
 def test_q8_g64_gemv(ax, N, K, M):
     """qmv_q8_g64 (quant.py:201-233): the reference fixture's Q8 pack at its
-    own size, then larger seeded packs (the tied lm_head of the BASELINE
-    config-1 shape among them), against an fp32 matmul of the oracle's
+    own size, then larger seeded packs (the tied lm_head of the reference's
+    CPU-runnable tiny model among them), against an fp32 matmul of the oracle's
     dequantized weights (dequantize_q8_g64 values, pinned to the fixture)."""
     g = np.load(os.path.join(GOLDEN, "quant.npz"))
     if (N, K) == (40, 256):
@@ -293,7 +293,7 @@ def test_decode_attention_matches_reference_fixture(ax):
 def test_decode_attention_vs_oracle(ax, hd, Hq, Hkv, S, active, kv):
     """Split-K decode attention against the oracle's SDPA over the cache the
     oracle's own quantizer produced: the reference formats (group 64) and the
-    BASELINE variants (one FP8 scale per (token, head); INT4 groups of 32)."""
+    benchmark variants (one FP8 scale per (token, head); INT4 groups of 32)."""
     torch.manual_seed(hd + S)
     B = 2
     k = torch.randn(B, Hkv, S, hd, device="cuda").half()

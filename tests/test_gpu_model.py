@@ -94,7 +94,7 @@ def test_small_model_greedy_parity(name, kv, graph):
 
 @pytest.mark.parametrize("kv", ["fp16", "fp8"])
 def test_tiny_config_128_greedy_tokens(kv):
-    """12L/768d/12H, vocab 32000, prompt 128, 128 greedy tokens.
+    """The reference's CPU-runnable tiny model: 12L/768d/12H, vocab 32000, prompt 128, 128 greedy tokens.
 
     Free-running tokens match up to the reference's first near-tie (the step
     is reported on failure); teacher-forced, all 128 steps' tokens and logits
@@ -178,7 +178,7 @@ def test_small_model_lowbit_matches_oracle(fmt):
     the oracle's forward with the same packs.  "ternary_g64" / "q2_g64" are the
     reference's quantize("ternary" | "q2_k") packings (transformer.py:857-862),
     served through from_packed as a reference model's tensors would be;
-    "ternary_pt" / "q2k" are the BASELINE layouts."""
+    "ternary_pt" / "q2k" are the benchmark-only layouts."""
     from oracle import axb_oracle as O
 
     from axiomlm_b200 import _lib as L

@@ -1,11 +1,11 @@
 """The benchmarked configuration against the oracle, end to end.
 
-The bench times the persistent step kernel on the BASELINE formats: Q4
+The bench times the persistent step kernel on the benchmark formats: Q4
 group-128 symmetric weights, an FP8 KV cache with one fp16 scale per
 (token, head), head_dim 128 and GQA 4:1.  Here that kernel runs on the same
 seeded weights and the same teacher-forced tokens as the oracle's restatement
 of the reference forward (oracle.OracleModel, the reference's own
-``_forward_quantized_sequence`` rounding points over the BASELINE layouts),
+``_forward_quantized_sequence`` rounding points over the benchmark-only layouts),
 and is checked:
 
 * per layer: the residual stream after every layer, within rel 2e-3 of the

@@ -4,7 +4,7 @@ runner, on the same weights and the same (teacher-forced) inputs.
 Both paths are checked against the reference elsewhere (test_gpu_model.py runs
 decode through whichever path the runner picks; the GEMV and attention unit
 tests pin the per-kernel path).  Here the two are compared with each other over
-the cases the model fixtures do not reach: the BASELINE weight format
+the cases the model fixtures do not reach: the benchmark weight format
 (symmetric Q4, group 128), head_dim 128, batch > 1, a wrapped ring buffer and
 contexts long enough that an attention split spans several shared-memory
 chunks.
