@@ -58,6 +58,23 @@ def _scale_ref(w, keep: list):
 _WEIGHT_TYPES = {c.__name__: c for c in (ops.Q4TWeight, ops.Q8Weight, ops.Q2TWeight)}
 
 
+def clip_importance(layer: dict | None, which: str, ln_f: torch.Tensor | None = None) -> torch.Tensor | None:
+    """The column importance the reference's clip search gets for a
+    projection in its "q4" / "q4_k_m" modes (_ensure_quant_weights,
+    transformer.py:880-884, 931-941): |ln_1| for c_attn ("qkv"), none for
+    c_proj ("o"), |ln_2| for gate_up ("gu"), |w_gate row| * |w_up row| for
+    w_down ("down"), |ln_f| for the lm_head ("lm")."""
+    if which == "lm":
+        return ln_f.float().abs()
+    if which == "qkv":
+        return layer["ln_1"].float().abs()
+    if which == "gu":
+        return layer["ln_2"].float().abs()
+    if which == "down":
+        return layer["w_gate"].float().norm(dim=1) * layer["w_up"].float().norm(dim=1)
+    return None
+
+
 def packed_kind(p: torch.Tensor, s: torch.Tensor) -> str:
     """Which of the reference's packings a (words, scales) pair is, by shape
     and dtype (_ensure_quant_weights, transformer.py:849-876):
@@ -278,19 +295,19 @@ class QuantizedDecoder:
 
         layers = []
         for lw in weights["layers"]:
-            wg_, wu_ = g(lw["w_gate"]), g(lw["w_up"])
-            gu = torch.cat([wg_, wu_], 0)
+            dl = {k: g(lw[k]) for k in ("w_gate", "w_up", "ln_1", "ln_2")}
+            gu = torch.cat([dl["w_gate"], dl["w_up"]], 0)
             b = lw.get("c_attn_b")
-            ln1, ln2 = g(lw["ln_1"]).contiguous(), g(lw["ln_2"]).contiguous()
-            if weight_format == "q4_k_m":
-                down = q8(g(lw["w_down"]))
-            else:
-                down = pack(g(lw["w_down"]), imp=wg_.norm(dim=1) * wu_.norm(dim=1) if mse else None)
+
+            def imp(which):
+                return clip_importance(dl, which) if mse else None
+
+            down = q8(g(lw["w_down"])) if weight_format == "q4_k_m" else pack(g(lw["w_down"]), imp=imp("down"))
             layers.append(dict(
-                qkv=pack(g(lw["c_attn"]), imp=ln1.abs() if mse else None), o=pack(g(lw["c_proj"])),
-                gu=pack(gu, gate_up=True, imp=ln2.abs() if mse else None), down=down, ln_1=ln1, ln_2=ln2,
-                qkv_b=None if b is None else b.to(dev, torch.float16).contiguous()))
-            del gu, wg_, wu_
+                qkv=pack(g(lw["c_attn"]), imp=imp("qkv")), o=pack(g(lw["c_proj"]), imp=imp("o")),
+                gu=pack(gu, gate_up=True, imp=imp("gu")), down=down, ln_1=dl["ln_1"].contiguous(),
+                ln_2=dl["ln_2"].contiguous(), qkv_b=None if b is None else b.to(dev, torch.float16).contiguous()))
+            del gu, dl
         emb_w, emb_s = ops.pack_q8_g64(g(weights["wte"]))
         # tied embeddings (transformer.py:842-847): the Q8_G64 embedding matrix is the lm_head
         if tied:
@@ -298,7 +315,7 @@ class QuantizedDecoder:
         elif weight_format == "q4_k_m":
             lm = q8(g(weights["lm_head"]))
         else:
-            lm = pack(g(weights["lm_head"]), imp=g(weights["ln_f"]).abs() if mse else None)
+            lm = pack(g(weights["lm_head"]), imp=clip_importance(None, "lm", g(weights["ln_f"])) if mse else None)
         packed = dict(layers=layers, emb_w=emb_w, emb_s=emb_s, lm_head=lm, ln_f=g(weights["ln_f"]).contiguous())
         dec = cls(cfg, packed, **kw)
         if weights.get("medusa"):

@@ -935,7 +935,9 @@ class OracleModel:
     ``"q8"`` packs every projection and the lm_head Q8_G64; ``"q4_k_m"`` takes
     the MSE-clipped MARLIN packs of c_attn, c_proj and gate_up as the
     reference made them (``packs``: {"c_attn"|"c_proj"|"gu": [(p, s) per
-    layer]}, no clip search is restated here) with Q8_G64 w_down and lm_head.
+    layer]}, no clip search is restated here) with Q8_G64 w_down and lm_head;
+    ``"q4"`` takes every projection's and the lm_head's clip-searched packs
+    (also "wd" per layer and "lmh").
     """
 
     def __init__(self, cfg: dict, weights: dict, rope_len: int, weight_format: str = "q4_rtn",
@@ -951,7 +953,7 @@ class OracleModel:
                   "q2_g64": lambda w: ("q2",) + pack_q2(w),
                   "ternary_pt": lambda w: ("tpt",) + ternary_pt_pack(w),
                   "q2k": lambda w: ("q2k",) + q2k_pack(w)}
-        if weight_format not in ("q4_rtn", "q4_g128_sym", "q8", "q4_k_m", *lowbit):
+        if weight_format not in ("q4_rtn", "q4_g128_sym", "q8", "q4_k_m", "q4", *lowbit):
             raise ValueError(f"unknown weight format {weight_format}")
         self.sym = weight_format == "q4_g128_sym"
         # every packed tensor carries its format: "marlin" (MARLIN Q4), "q4t"
@@ -969,16 +971,20 @@ class OracleModel:
         self.wte = pack_q8_g64(weights["wte"])
         if tied:
             self.lmh = ("q8",) + self.wte
+        elif weight_format == "q4":  # the reference's clip-searched lm_head, from ``packs``
+            self.lmh = ("marlin",) + tuple(packs["lmh"])
         else:  # q8 / q4_k_m: a Q8_G64 lm_head (transformer.py:842-846)
             self.lmh = q8(weights["lm_head"]) if weight_format in ("q8", "q4_k_m") else pack(weights["lm_head"])
         self.layers = []
         for i, lw in enumerate(weights["layers"]):
             gu = np.concatenate([_f32(_to_np(lw["w_gate"])), _f32(_to_np(lw["w_up"]))], 0)
-            if weight_format == "q4_k_m":
+            if weight_format in ("q4_k_m", "q4"):
                 # MSE-clipped MARLIN packs (quant.py:495-571) as the reference
-                # made them, passed in ``packs``; w_down Q8_G64 (transformer.py:847)
+                # made them, passed in ``packs``; w_down Q8_G64 in q4_k_m
+                # (transformer.py:847), clip-searched too in q4
                 ent = dict(c_attn=("marlin",) + tuple(packs["c_attn"][i]), c_proj=("marlin",) + tuple(packs["c_proj"][i]),
-                           gu=("marlin",) + tuple(packs["gu"][i]), wd=q8(lw["w_down"]))
+                           gu=("marlin",) + tuple(packs["gu"][i]),
+                           wd=("marlin",) + tuple(packs["wd"][i]) if weight_format == "q4" else q8(lw["w_down"]))
             else:
                 ent = dict(c_attn=pack(lw["c_attn"]), c_proj=pack(lw["c_proj"]), gu=pack(gu), wd=pack(lw["w_down"]))
             ent.update(ln_1=torch.as_tensor(_to_np(lw["ln_1"])).float(),

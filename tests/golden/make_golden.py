@@ -166,12 +166,14 @@ def _ref_model(cfg, W, tied, mode="q4_rtn"):
 _PACKED_Q4 = ("c_attn_p", "c_attn_s", "c_proj_p", "c_proj_s", "gu_p", "gu_s")
 
 
-def _packed_arrays(m):
+def _packed_arrays(m, keys=_PACKED_Q4, single=()):
     qw = m._ensure_quant_weights(torch.device("cpu"))
     out = {}
-    for k in _PACKED_Q4:
+    for k in keys:
         for i, t in enumerate(qw[k]):
             out[f"pk_{k}_{i}"] = _np(t)
+    for k in single:
+        out[f"pk_{k}"] = _np(qw[k])
     return out
 
 
@@ -189,6 +191,8 @@ def gen_model(cfg, seed, prompt_len, n_new, kv, ln_random, tied=False, with_tree
            "mode": np.array(mode)}
     if mode == "q4_k_m":
         out.update(_packed_arrays(m))
+    elif mode == "q4":  # every projection and the lm_head clip-searched: the packer under test
+        out.update(_packed_arrays(m, _PACKED_Q4 + ("wd_p", "wd_s"), ("lmh_p", "lmh_sb")))
     with torch.no_grad():
         cache = StaticKVCache(1, max_seq, cfg["n_layer"], cfg["n_kv_head"], hd, dtype=torch.float16,
                               device="cpu", ring_buffer=bool(ring), cache_dtype=kv)
@@ -308,7 +312,7 @@ def main():
     ap.add_argument("--hf-only", action="store_true",
                     help="regenerate only the Hugging Face importer fixture (hf_import.npz)")
     ap.add_argument("--modes-only", action="store_true",
-                    help="regenerate only the q8 / q4_k_m model fixtures (small_q8, small_q4km)")
+                    help="regenerate only the q8 / q4_k_m / q4 model fixtures (small_q8, small_q4km, small_q4)")
     args = ap.parse_args()
     if not args.reference or not os.path.isdir(args.reference):
         raise SystemExit("pass --reference <path to the AxiomLM checkout>")
@@ -319,27 +323,28 @@ def main():
     import axiomlm.models.modules as modules
     from axiomlm.engine.medusa import DEFAULT_MEDUSA_TREE_CHOICES, compile_medusa_tree
 
-    if args.mse_only or not args.tiny_only:
+    # with one of the --*-only flags, only that part; with none, everything
+    only = [k for k in ("tiny", "mse", "hf", "modes") if getattr(args, f"{k}_only")]
+
+    def part(name):
+        return not only or name in only
+
+    if part("mse"):
         gen_mse(q)
-        if args.mse_only:
-            return
-    if args.hf_only or not args.tiny_only:
+    if part("hf"):
         gen_hf()
-        if args.hf_only:
-            return
-    if args.modes_only or not args.tiny_only:
+    if part("modes"):
         # the reference's other quantized-forward modes (transformer.py:797-799):
-        # Q8_G64 everywhere ("q8"), MSE-clipped Q4 with Q8 w_down and lm_head ("q4_k_m")
-        for mode, name, seed in (("q8", "small_q8", 41), ("q4_k_m", "small_q4km", 55)):
+        # Q8_G64 everywhere ("q8"), MSE-clipped Q4 with Q8 w_down and lm_head
+        # ("q4_k_m"), MSE-clipped Q4 everywhere ("q4")
+        for mode, name, seed in (("q8", "small_q8", 41), ("q4_k_m", "small_q4km", 55), ("q4", "small_q4", 84)):
             t0 = time.time()
             o = gen_model(SMALL, seed, 12, 16, "fp16", ln_random=True, mode=mode)
             np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **o)
             print(f"{name}: {time.time() - t0:.1f}s tokens={o['tokens'][:8]}")
-        if args.modes_only:
-            return
-    if not args.tiny_only:
+    if not only:
         _gen_small(q, ops, modules, compile_medusa_tree, DEFAULT_MEDUSA_TREE_CHOICES)
-    if not args.skip_tiny:
+    if part("tiny") and not args.skip_tiny:
         for kv in ("fp16", "fp8"):
             t0 = time.time()
             o = gen_model(TINY, 5, 128, 128, kv, ln_random=False)

@@ -201,7 +201,7 @@ def test_oracle_model_greedy_matches_reference(name):
         assert np.array_equal(tl[0].float().numpy(), fx["tree_logits"].astype(np.float32))
 
 
-@pytest.mark.parametrize("name", ["small_q8", "small_q4km"])
+@pytest.mark.parametrize("name", ["small_q8", "small_q4km", "small_q4"])
 def test_oracle_model_q8_modes_match_reference(name):
     """The oracle in the reference's "q8" and "q4_k_m" modes against the
     reference's own greedy decode of the same model (tests/golden/make_golden.py
@@ -212,9 +212,11 @@ def test_oracle_model_q8_modes_match_reference(name):
     mode = str(fx["mode"])
     W = make_weights(SMALL, int(fx["seed"]), ln_random=bool(fx["ln_random"]))
     packs = None
-    if mode == "q4_k_m":
-        packs = {k: [(fx[f"pk_{src}_p_{i}"], fx[f"pk_{src}_s_{i}"]) for i in range(SMALL["n_layer"])]
-                 for k, src in (("c_attn", "c_attn"), ("c_proj", "c_proj"), ("gu", "gu"))}
+    if mode in ("q4_k_m", "q4"):
+        packs = {k: [(fx[f"pk_{k}_p_{i}"], fx[f"pk_{k}_s_{i}"]) for i in range(SMALL["n_layer"])]
+                 for k in ("c_attn", "c_proj", "gu") + (("wd",) if mode == "q4" else ())}
+        if mode == "q4":
+            packs["lmh"] = (fx["pk_lmh_p"], fx["pk_lmh_sb"])
     m = O.OracleModel(SMALL, W, rope_len=SMALL["block_size"], weight_format=mode, packs=packs)
     hd = SMALL["d_model"] // SMALL["n_head"]
     cache = O.OracleCache(SMALL["n_layer"], 1, SMALL["n_kv_head"], int(fx["max_seq"]), hd, "fp16", False)

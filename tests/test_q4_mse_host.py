@@ -54,3 +54,32 @@ def test_clip_search_never_worse_than_round_to_nearest():
     e_mse = ((wg - deq) ** 2).sum(-1)
     assert bool((e_mse <= e_rtn + 1e-12).all())
     assert bool((e_mse < e_rtn).any())
+
+
+def test_q4_model_packs_match_reference_quantize():
+    """Every projection of a model in the reference's "q4" mode (its own
+    quantize("q4") packs in small_q4.npz) from ``q4_mse_codes`` with the
+    importance ``clip_importance`` picks per projection: the packing rule of
+    from_weights(..., "q4"), bit-identical on the host."""
+    from model_weights import SMALL, make_weights
+
+    from axiomlm_b200.model import clip_importance
+    from axiomlm_b200.ops import q4_mse_codes
+
+    fx = np.load(os.path.join(GOLDEN, "small_q4.npz"))
+    W = make_weights(SMALL, int(fx["seed"]), ln_random=bool(fx["ln_random"]))
+
+    def check(w, imp, p, s):
+        q, sc, bi = q4_mse_codes(w, imp)
+        N, K = w.shape
+        assert np.array_equal(q.numpy(), O._marlin_unlayout(p).reshape(-1, K)[:N])
+        sb = s.transpose(0, 2, 1, 3).reshape(-1, K // 64, 2)[:N]
+        assert np.array_equal(sc.numpy().view(np.uint16), sb[..., 0].view(np.uint16))
+        assert np.array_equal(bi.numpy().view(np.uint16), sb[..., 1].view(np.uint16))
+
+    for i, lw in enumerate(W["layers"]):
+        gu = torch.cat([lw["w_gate"], lw["w_up"]], 0)
+        for key, w, which in (("c_attn", lw["c_attn"], "qkv"), ("c_proj", lw["c_proj"], "o"), ("gu", gu, "gu"),
+                              ("wd", lw["w_down"], "down")):
+            check(w, clip_importance(lw, which), fx[f"pk_{key}_p_{i}"], fx[f"pk_{key}_s_{i}"])
+    check(W["lm_head"], clip_importance(None, "lm", W["ln_f"]), fx["pk_lmh_p"], fx["pk_lmh_sb"])
