@@ -34,7 +34,15 @@ WEIGHT_FORMATS = {
     # 880-884, 931-941); q4_k_m keeps w_down and the lm_head Q8_G64
     "q4": (L.W_Q4T_AFFINE, 64),
     "q4_k_m": (L.W_Q4T_AFFINE, 64),
+    # 2-bit: the reference's ternary / q2_k packings (group 64, quant.py:236-381)
+    # and the benchmark-only per-tensor ternary and K-quant super-blocks; every
+    # projection and an untied lm_head, gate_up as cat(w_gate, w_up)
+    "ternary": (L.W_TERNARY_G64, 64),
+    "q2_k": (L.W_Q2_G64, 64),
+    "ternary_pt": (L.W_TERNARY_PT, 0),
+    "q2k": (L.W_Q2K_SB256, 256),
 }
+_LOWBIT_FORMATS = (L.W_TERNARY_G64, L.W_Q2_G64, L.W_TERNARY_PT, L.W_Q2K_SB256)
 
 
 def _vp_array(items):
@@ -268,7 +276,8 @@ class QuantizedDecoder:
         mode (transformer.py:822-1008): projections and an untied lm_head in
         Q4, token embeddings in Q8_G64 (also the lm_head when the embeddings are
         tied), RMSNorm weights kept fp32.  ``weight_format="q8"`` packs every
-        projection and the lm_head Q8_G64 (the reference's q8 mode); "q4" and
+        projection and the lm_head Q8_G64 (the reference's q8 mode); "ternary",
+        "q2_k", "ternary_pt" and "q2k" pack them in a 2-bit format; "q4" and
         "q4_k_m" pack with the reference's clip search, c_attn weighted by
         |ln_1|, gate_up by |ln_2|, w_down by |w_gate row| * |w_up row| and the
         lm_head by |ln_f| ("q4"), or w_down and the lm_head in Q8_G64
@@ -289,6 +298,8 @@ class QuantizedDecoder:
         def pack(w, gate_up=False, imp=None):
             if fmt == L.W_Q8_G64:
                 return q8(w)
+            if fmt in _LOWBIT_FORMATS:
+                return ops.pack_q2t(w, fmt)
             if mse:
                 return ops.pack_q4_mse(w, imp, gate_up=gate_up)
             return ops.pack_q4t(w, group, sym, gate_up=gate_up)

@@ -386,6 +386,102 @@ def q2t_from_ref(fmt: int, codes: torch.Tensor, s1: torch.Tensor | None = None, 
     return Q2TWeight(words, meta, meta2, pt, N, K, fmt)
 
 
+def _pack4_2bit(c: torch.Tensor) -> torch.Tensor:
+    """Four 2-bit codes per byte, element 4i + j at bits 2j (quant.py:266-273)."""
+    N, K = c.shape
+    c = c.to(torch.uint8).reshape(N, K // 4, 4)
+    return (c[..., 0] | (c[..., 1] << 2) | (c[..., 2] << 4) | (c[..., 3] << 6)).contiguous()
+
+
+def ternary_g64_codes(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """pack_linear_ternary (quant.py:236-274) on ``w``'s device: per group of
+    64 the absmean scale (in ``w``'s dtype, clamped to 1e-5, as fp16), codes
+    round(w / scale) clamped to -1..1 as 0 -> 0, +1 -> 1, -1 -> 2.  Returns
+    codes (N, K/4) uint8 and scales (N, K/64) fp16."""
+    N, K = w.shape
+    wg = w.reshape(N, K // 64, 64)
+    scale = wg.abs().mean(dim=-1, keepdim=True).clamp(min=1e-5).to(torch.float16)
+    q = torch.clamp(torch.round(wg.float() / scale.float().clamp(min=1e-5)), -1.0, 1.0)
+    code = torch.where(q == 1, 1, torch.where(q == -1, 2, 0))
+    return _pack4_2bit(code.reshape(N, K)), scale.reshape(N, K // 64)
+
+
+def q2_g64_codes(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """pack_linear_q2_k (quant.py:339-381; 2-bit affine per group of 64) on
+    ``w``'s device: scale fp16((max - min) / 3), bias fp16(min) (the range in
+    ``w``'s dtype), codes round((w - bias) / scale) in 0..3.  Returns codes
+    (N, K/4) uint8 and (scale, bias) pairs (N, K/64, 2) fp16."""
+    N, K = w.shape
+    wg = w.reshape(N, K // 64, 64)
+    lo = wg.amin(dim=-1, keepdim=True)
+    hi = wg.amax(dim=-1, keepdim=True)
+    scale = (torch.clamp(hi - lo, min=1e-8) / 3.0).to(torch.float16)
+    bias = lo.to(torch.float16)
+    q = torch.clamp(torch.round((wg.float() - bias.float()) / torch.clamp(scale.float(), min=1e-8)), 0.0, 3.0)
+    return _pack4_2bit(q.reshape(N, K)), torch.stack([scale.squeeze(-1), bias.squeeze(-1)], dim=-1).contiguous()
+
+
+def ternary_pt_codes(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """BitNet b1.58 with one per-tensor absmean scale (the benchmark-only
+    layout; the reference packs per group of 64): scale fp16(max(mean |w|,
+    1e-5)) with the mean in float64, codes round(w / scale) clamped to -1..1
+    in the reference's 2-bit code and byte order.  Returns codes (N, K/4)
+    uint8 and the scale (1,) fp16."""
+    N, K = w.shape
+    s16 = torch.clamp(w.double().abs().mean(), min=1e-5).to(torch.float16)
+    q = torch.clamp(torch.round(w.float() / s16.float()), -1.0, 1.0)
+    code = torch.where(q == 1, 1, torch.where(q == -1, 2, 0))
+    return _pack4_2bit(code), s16.reshape(1)
+
+
+def q2k_sb256_codes(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """K-quant-style 2-bit super-blocks (the benchmark-only layout): per 256
+    weights fp16 ``d`` and ``dmin`` (the largest 16-element sub-block scale
+    and sub-min over 15), per 16 weights a 4-bit sub-scale and sub-min, codes
+    round((w + dmin * mn) / (d * sc)) in 0..3, all in fp32.  Returns codes
+    (N, K/4) uint8, sub-bytes (N, K/16) uint8 (scale | min << 4) and (d, dmin)
+    (N, K/256, 2) fp16."""
+    w = w.float()
+    N, K = w.shape
+    if K % 256:
+        raise ValueError(f"K ({K}) must be a multiple of 256")
+    sb = w.reshape(N, K // 256, 16, 16)
+    mn = torch.clamp(sb.amin(dim=-1), max=0.0)
+    sub_scale = torch.clamp(sb.amax(dim=-1) - mn, min=1e-8) / 3.0
+    sub_min = -mn
+    d = (sub_scale.amax(dim=-1) / 15.0).to(torch.float16)
+    dmin = (sub_min.amax(dim=-1) / 15.0).to(torch.float16)
+    df = torch.clamp(d.float(), min=1e-8)[..., None]
+    mf = torch.clamp(dmin.float(), min=1e-8)[..., None]
+    sc = torch.clamp(torch.round(sub_scale / df), 0, 15)
+    mi = torch.clamp(torch.round(sub_min / mf), 0, 15)
+    eff_s = d.float()[..., None] * sc
+    eff_m = dmin.float()[..., None] * mi
+    q = torch.clamp(torch.round((sb + eff_m[..., None]) / torch.clamp(eff_s, min=1e-12)[..., None]), 0, 3)
+    sub = (sc.to(torch.uint8) | (mi.to(torch.uint8) << 4)).reshape(N, K // 16).contiguous()
+    return _pack4_2bit(q.reshape(N, K)), sub, torch.stack([d, dmin], dim=-1).contiguous()
+
+
+def pack_q2t(w: torch.Tensor, fmt: int) -> Q2TWeight:
+    """fp32 / fp16 weights packed in a 2-bit format on their device, then
+    relaid out into q2t: ``L.W_TERNARY_G64`` / ``L.W_Q2_G64`` (the reference's
+    ternary / q2_k packings), ``L.W_TERNARY_PT`` / ``L.W_Q2K_SB256``."""
+    N, K = w.shape
+    if fmt == L.W_TERNARY_G64:
+        c, s1 = ternary_g64_codes(w)
+        return q2t_from_ref(fmt, c, s1, None, K)
+    if fmt == L.W_Q2_G64:
+        c, s1 = q2_g64_codes(w)
+        return q2t_from_ref(fmt, c, s1, None, K)
+    if fmt == L.W_TERNARY_PT:
+        c, s1 = ternary_pt_codes(w)
+        return q2t_from_ref(fmt, c, s1, None, K)
+    if fmt == L.W_Q2K_SB256:
+        c, s1, s2 = q2k_sb256_codes(w)
+        return q2t_from_ref(fmt, c, s1, s2, K)
+    raise ValueError(f"format {fmt} is not a 2-bit format")
+
+
 def lbgemm(x: torch.Tensor, W: Q2TWeight, bias: torch.Tensor | None = None,
            out: torch.Tensor | None = None) -> torch.Tensor:
     """y[M, N] = x[M, K] W^T (+ bias) on the 2-bit tensor-core kernel (M <= 8
