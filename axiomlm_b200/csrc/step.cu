@@ -654,8 +654,12 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
         tot[2] += v.z;
         tot[3] += v.w;
       }
+      // A CTA's pieces alternate between two slots by phase parity: its next
+      // phase's piece never lands on one a slower CTA has yet to read (writing
+      // the piece of phase ph + 2 needs phase ph + 1 outputs, hence every
+      // phase-ph tile, this one included, finished).
       if (!first_cta) {  // the tile began in an earlier CTA: publish this CTA's piece (one per CTA)
-        uint4* p = reinterpret_cast<uint4*>(a.partials) + ((size_t)cta * 32 + lane) * 2;
+        uint4* p = reinterpret_cast<uint4*>(a.partials) + (((size_t)cta * 2 + (ph & 1)) * 32 + lane) * 2;
         st_ll(p, tot[0], tot[1], fl);
         st_ll(p + 1, tot[2], tot[3], fl);
         continue;
@@ -664,7 +668,7 @@ __device__ __forceinline__ bool gemv_phase(const StepArgs& a, int ph, Ring& r, C
         const int cb = owner_of(te - 1, 0u, g.U, (uint32_t)C);
         for (int cc = cta + 1; cc <= cb; ++cc) {
           if (cta_u0(g.U, cc + 1, C) == cta_u0(g.U, cc, C)) continue;  // a CTA with no units (U < C)
-          const uint4* p = reinterpret_cast<const uint4*>(a.partials) + ((size_t)cc * 32 + lane) * 2;
+          const uint4* p = reinterpret_cast<const uint4*>(a.partials) + (((size_t)cc * 2 + (ph & 1)) * 32 + lane) * 2;
           uint4 v0 = ld_ll(p), v1 = ld_ll(p + 1);
           uint32_t it = 0;
           while (v0.y != fl || v0.w != fl || v1.y != fl || v1.w != fl) {
