@@ -61,7 +61,7 @@ struct StepArgs {
   // scratch (zeroed once; every counter returns to zero by the end of a step)
   int* done;          // per-phase completion counters
   int* tile_cnt;      // per-tile arrival counters
-  float* partials;    // per virtual warp: 32 lanes x 4 (value, flag) pairs
+  float* partials;    // split-tile pieces: per CTA two slots (phase parity) of 32 lanes x 4 (value, flag) pairs
   float* part_o;      // attention split partials (B, Hq, kStepMaxSplits, hd)
   float* part_ml;     // (B, Hq, kStepMaxSplits, 2)
   int* attn_cnt;      // (B, Hkv) split arrivals, grow through a step
