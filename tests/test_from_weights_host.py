@@ -1,0 +1,75 @@
+"""``QuantizedDecoder.from_weights`` packing, run on the host up to the GPU
+relayout: the relayout (``ops.q4t_from_q4g64``, tested on the GPU against
+the oracle) and the decoder constructor are replaced by stand-ins that keep
+what they are given.  In the reference's "q4" mode every projection and the
+lm_head then dequantize to exactly what the reference's own quantize("q4")
+packs of the same model dequantize to (tests/golden/small_q4.npz); in
+"q4_k_m" the Q4 projections do (small_q4km.npz), and w_down and the lm_head
+go to the Q8 packer."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from model_weights import SMALL, make_weights
+from oracle import axb_oracle as O
+
+
+@pytest.fixture
+def captured(monkeypatch):
+    from axiomlm_b200 import model as M
+    from axiomlm_b200 import ops
+
+    cap = {}
+
+    def relayout(words, sb, n_out=None, gate_up=False):
+        return ("q4g64", words.clone(), sb.clone(), gate_up)
+
+    def q8(w):  # the Q8_G64 packer is round-to-nearest; its CUDA kernel is tested against the oracle
+        p, s = O.pack_q8_g64(w.numpy())
+        return torch.from_numpy(p), torch.from_numpy(s)
+
+    def init(self, cfg, packed, **kw):
+        cap["cfg"], cap["packed"] = cfg, packed
+
+    monkeypatch.setattr(ops, "q4t_from_q4g64", relayout)
+    monkeypatch.setattr(ops, "pack_q8_g64", q8)
+    monkeypatch.setattr(M.QuantizedDecoder, "__init__", init)
+    return cap
+
+
+def _same_values(ours, ref_p, ref_s, K, N):
+    kind, words, sb, _ = ours
+    assert kind == "q4g64"
+    a = O.dequant_q4_g64(words.numpy(), sb.numpy(), K)
+    b = O.dequant_q4_marlin(ref_p, ref_s, K, N)
+    assert np.array_equal(a.view(np.uint16), b.view(np.uint16))
+
+
+@pytest.mark.parametrize("name,mode", [("small_q4", "q4"), ("small_q4km", "q4_k_m")])
+def test_from_weights_packs_like_the_reference(captured, name, mode):
+    from axiomlm_b200 import ops
+    from axiomlm_b200.model import QuantizedDecoder
+
+    fx = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+    W = make_weights(SMALL, int(fx["seed"]), ln_random=bool(fx["ln_random"]))
+    QuantizedDecoder.from_weights(SMALL, W, mode, device="cpu")
+    packed = captured["packed"]
+    d, F = SMALL["d_model"], SMALL["ffn"]
+    qkv_dim = (SMALL["n_head"] + 2 * SMALL["n_kv_head"]) * (d // SMALL["n_head"])
+    for i, ly in enumerate(packed["layers"]):
+        _same_values(ly["qkv"], fx[f"pk_c_attn_p_{i}"], fx[f"pk_c_attn_s_{i}"], d, qkv_dim)
+        _same_values(ly["o"], fx[f"pk_c_proj_p_{i}"], fx[f"pk_c_proj_s_{i}"], d, d)
+        _same_values(ly["gu"], fx[f"pk_gu_p_{i}"], fx[f"pk_gu_s_{i}"], d, 2 * F)
+        assert ly["gu"][3] is True  # gate_up rows are interleaved for the SwiGLU epilogue
+        if mode == "q4":
+            _same_values(ly["down"], fx[f"pk_wd_p_{i}"], fx[f"pk_wd_s_{i}"], F, d)
+        else:
+            assert isinstance(ly["down"], ops.Q8Weight) and ly["down"].K == F
+    if mode == "q4":
+        _same_values(packed["lm_head"], fx["pk_lmh_p"], fx["pk_lmh_sb"], d, SMALL["vocab"])
+    else:
+        assert isinstance(packed["lm_head"], ops.Q8Weight) and packed["lm_head"].N == SMALL["vocab"]
