@@ -73,3 +73,32 @@ def test_from_weights_packs_like_the_reference(captured, name, mode):
         _same_values(packed["lm_head"], fx["pk_lmh_p"], fx["pk_lmh_sb"], d, SMALL["vocab"])
     else:
         assert isinstance(packed["lm_head"], ops.Q8Weight) and packed["lm_head"].N == SMALL["vocab"]
+
+
+@pytest.mark.parametrize("fmt,oracle_pack", [("ternary", "pack_ternary"), ("q2_k", "pack_q2"),
+                                             ("ternary_pt", "ternary_pt_pack"), ("q2k", "q2k_pack")])
+def test_from_weights_lowbit_packs(monkeypatch, captured, fmt, oracle_pack):
+    """The 2-bit formats: every projection (gate_up as cat(w_gate, w_up), the
+    reference's row order) and the untied lm_head reach the q2t relayout as
+    the oracle packs them (the oracle's ternary / Q2 G64 packers are pinned to
+    the reference's)."""
+    from axiomlm_b200 import ops
+    from axiomlm_b200.model import QuantizedDecoder
+
+    seen = []
+    monkeypatch.setattr(ops, "q2t_from_ref", lambda f, c, s1, s2=None, K=None: seen.append((f, c, s1, s2, K)) or
+                        ops.Q2TWeight(c, None, None, None, c.shape[0], K, f))
+    W = make_weights(SMALL, 7, ln_random=True)
+    QuantizedDecoder.from_weights(SMALL, W, fmt, device="cpu")
+    mats = []
+    for lw in W["layers"]:
+        # from_weights packs a layer's w_down first, then c_attn, c_proj and gate_up
+        mats += [lw["w_down"], lw["c_attn"], lw["c_proj"], torch.cat([lw["w_gate"], lw["w_up"]], 0)]
+    mats.append(W["lm_head"])
+    assert len(seen) == len(mats)
+    for (f, c, s1, s2, K), w in zip(seen, mats):
+        ref = getattr(O, oracle_pack)(w.numpy())
+        assert K == w.shape[1] and np.array_equal(c.numpy(), ref[0])
+        assert np.array_equal(s1.numpy().view(np.uint8), np.asarray(ref[1]).view(np.uint8))
+        if s2 is not None:
+            assert np.array_equal(s2.numpy().view(np.uint8), np.asarray(ref[2]).view(np.uint8))
