@@ -102,3 +102,25 @@ def test_from_weights_lowbit_packs(monkeypatch, captured, fmt, oracle_pack):
         assert np.array_equal(s1.numpy().view(np.uint8), np.asarray(ref[1]).view(np.uint8))
         if s2 is not None:
             assert np.array_equal(s2.numpy().view(np.uint8), np.asarray(ref[2]).view(np.uint8))
+
+
+def test_from_hf_carries_bias_and_config(tmp_path, captured):
+    """from_hf on a Qwen2-style checkpoint (q / k / v biases, tied
+    embeddings): the fused, RoPE-interleaved bias reaches the packed layers in
+    fp16 as the reference's importer builds it, the embedding is the Q8
+    lm_head, and the model config comes through."""
+    from model_weights import make_hf_checkpoint
+
+    from axiomlm_b200 import ops
+    from axiomlm_b200.model import QuantizedDecoder
+
+    make_hf_checkpoint(str(tmp_path), 72, bias=True, tied=True, shards=2)
+    QuantizedDecoder.from_hf(tmp_path, weight_format="q4", device="cpu")
+    fx = np.load(os.path.join(GOLDEN, "hf_import.npz"))
+    cfg, packed = captured["cfg"], captured["packed"]
+    assert cfg["theta"] == float(fx["qwen_theta"]) and cfg["tied"]
+    for i, ly in enumerate(packed["layers"]):
+        assert ly["qkv_b"].dtype == torch.float16
+        assert np.array_equal(ly["qkv_b"].numpy().view(np.uint16), fx[f"qwen_{i}_c_attn_b"].view(np.uint16))
+    lm = packed["lm_head"]
+    assert isinstance(lm, ops.Q8Weight) and lm.words is packed["emb_w"]
