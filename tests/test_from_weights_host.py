@@ -124,3 +124,38 @@ def test_from_hf_carries_bias_and_config(tmp_path, captured):
         assert np.array_equal(ly["qkv_b"].numpy().view(np.uint16), fx[f"qwen_{i}_c_attn_b"].view(np.uint16))
     lm = packed["lm_head"]
     assert isinstance(lm, ops.Q8Weight) and lm.words is packed["emb_w"]
+
+
+@pytest.mark.parametrize("fmt", ["q4_rtn", "q4_g128_sym", "q8", "q4", "q4_k_m", "ternary", "q2_k", "ternary_pt",
+                                 "q2k"])
+def test_from_weights_every_format_on_host(monkeypatch, captured, fmt):
+    """Every weight format builds its packed model on the host (GPU calls
+    replaced by stand-ins): each projection and the lm_head in the format's
+    kind, with the right (N, K); gate_up as one (2F, d) matrix."""
+    from axiomlm_b200 import model as M
+    from axiomlm_b200 import ops
+
+    monkeypatch.setattr(ops, "pack_q4t", lambda w, group=128, symmetric=True, gate_up=False:
+                        ops.Q4TWeight(torch.zeros(1, dtype=torch.int32), torch.zeros(1).half(), w.shape[0], w.shape[1],
+                                      group, 1 if symmetric else 2, gate_up))
+    monkeypatch.setattr(ops, "q2t_from_ref", lambda f, c, s1, s2=None, K=None:
+                        ops.Q2TWeight(c, None, None, None, c.shape[0], K, f))
+    W = make_weights(SMALL, 9, ln_random=True)
+    M.QuantizedDecoder.from_weights(SMALL, W, fmt, device="cpu")
+    packed = captured["packed"]
+    d, F, V = SMALL["d_model"], SMALL["ffn"], SMALL["vocab"]
+    qkv = (SMALL["n_head"] + 2 * SMALL["n_kv_head"]) * (d // SMALL["n_head"])
+
+    def nk(w):
+        if isinstance(w, tuple):  # the q4g64 relayout stand-in: (kind, words (N, K/8), ...)
+            return w[1].shape[0], w[1].shape[1] * 8
+        return w.N, w.K
+
+    q8_down = fmt in ("q8", "q4_k_m")
+    for ly in packed["layers"]:
+        assert [nk(ly[k]) for k in ("qkv", "o", "gu", "down")] == [(qkv, d), (d, d), (2 * F, d), (d, F)]
+        assert isinstance(ly["down"], ops.Q8Weight) == q8_down
+        assert isinstance(ly["qkv"], ops.Q8Weight) == (fmt == "q8")
+        assert isinstance(ly["qkv"], ops.Q2TWeight) == (fmt in ("ternary", "q2_k", "ternary_pt", "q2k"))
+    assert nk(packed["lm_head"]) == (V, d)
+    assert isinstance(packed["lm_head"], ops.Q8Weight) == q8_down
