@@ -24,6 +24,9 @@ from .cache import StaticKVCache
 WEIGHT_FORMATS = {
     # reference q4_rtn: MARLIN RTN values, affine (scale, bias), group 64
     "q4_rtn": (L.W_Q4T_AFFINE, 64),
+    # reference q4_legacy: the same round-to-nearest G64 values in another
+    # layout (pack_linear_q4_g64, quant.py:17-69), so the same q4t packs
+    "q4_legacy": (L.W_Q4T_AFFINE, 64),
     # the benchmark format: symmetric, group 128, fp16 scales (4.125 bits/weight)
     "q4_g128_sym": (L.W_Q4T_SYM, 128),
     # reference q8: every projection and the lm_head Q8_G64 in its own layout

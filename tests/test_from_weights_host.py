@@ -126,8 +126,8 @@ def test_from_hf_carries_bias_and_config(tmp_path, captured):
     assert isinstance(lm, ops.Q8Weight) and lm.words is packed["emb_w"]
 
 
-@pytest.mark.parametrize("fmt", ["q4_rtn", "q4_g128_sym", "q8", "q4", "q4_k_m", "ternary", "q2_k", "ternary_pt",
-                                 "q2k"])
+@pytest.mark.parametrize("fmt", ["q4_rtn", "q4_legacy", "q4_g128_sym", "q8", "q4", "q4_k_m", "ternary", "q2_k",
+                                 "ternary_pt", "q2k"])
 def test_from_weights_every_format_on_host(monkeypatch, captured, fmt):
     """Every weight format builds its packed model on the host (GPU calls
     replaced by stand-ins): each projection and the lm_head in the format's
