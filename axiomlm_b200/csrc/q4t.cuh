@@ -34,17 +34,4 @@ __device__ __forceinline__ void unpack_word(uint32_t w, uint32_t (&a)[4]) {
   a[3] = h2_as_u32(__hfma2(u32_as_h2(hi1), mul, add));
 }
 
-// nibble pairs of one word -> four A-fragment registers holding fp16
-// (1024 + q) for rows g (registers 0, 2) and (1024 + 16 q) for rows g + 8
-// (registers 1, 3); the offsets are removed per group with the group sums of
-// x: sum (q - 8) x = C_lo - 1032 X  and  C_hi / 16 - 72 X.
-__device__ __forceinline__ void unpack_word_raw(uint32_t w, uint32_t (&a)[4]) {
-  const uint32_t MAGIC = 0x64006400u;
-  a[0] = lop3_and_or(w, 0x000F000Fu, MAGIC);
-  a[1] = lop3_and_or(w, 0x00F000F0u, MAGIC);
-  const uint32_t w8 = w >> 8;
-  a[2] = lop3_and_or(w8, 0x000F000Fu, MAGIC);
-  a[3] = lop3_and_or(w8, 0x00F000F0u, MAGIC);
-}
-
 }  // namespace axb
