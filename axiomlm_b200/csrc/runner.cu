@@ -238,10 +238,9 @@ struct Layout {
   size_t gu_tmp, tc_ws, tc_ws_bytes;  // tensor-core projections for many-token steps
   size_t gemm_ws_bytes, attn_ws_bytes;
   // persistent step kernel (decode, B <= 8)
-  size_t st_layers, st_done, st_tiles, st_part, st_po, st_pml, st_acnt, st_keys, st_exit, st_trace, st_hdump, st_maps;
+  size_t st_layers, st_part, st_po, st_pml, st_acnt, st_keys, st_exit, st_trace, st_hdump, st_maps;
   size_t st_h, st_qkv, st_attn, st_sw;  // the step kernel's flagged activations: one 8-byte word per 2 halves
   size_t st_trace_bytes, st_hdump_bytes;
-  int st_max_tiles;
 };
 
 static Layout make_layout(const axb_model_cfg& c) {
@@ -316,11 +315,7 @@ static Layout make_layout(const axb_model_cfg& c) {
   L.attn_ws_bytes = a;
   L.attn_ws = take(a);
   const int sb = std::min(c.max_batch, kStepMaxM);
-  L.st_max_tiles = 0;
-  for (int n : {(int)qkv_dim, c.d_model, 2 * c.ffn, c.vocab}) L.st_max_tiles = std::max(L.st_max_tiles, (n + 15) / 16);
   L.st_layers = take((size_t)c.n_layer * sizeof(StepLayer));
-  L.st_done = take((size_t)(2 + 5 * c.n_layer) * 4);
-  L.st_tiles = take((size_t)L.st_max_tiles * 4);
   L.st_part = take((size_t)num_sms() * step_num_warps() * 32 * 8 * sizeof(float));  // (value, flag) pairs
   L.st_po = take((size_t)sb * c.n_head * kStepMaxSplits * c.head_dim * sizeof(float));
   L.st_pml = take((size_t)sb * c.n_head * kStepMaxSplits * 2 * sizeof(float));
@@ -855,15 +850,12 @@ int axb_runner_create(const axb_model_cfg* cfg, const axb_model_ptrs* p, void* w
     a.sw = r->buf<uint2>(L.st_sw);
     a.logits = r->buf<__half>(L.logits);
     a.amax = r->buf<int32_t>(L.amax);
-    a.done = r->buf<int>(L.st_done);
-    a.tile_cnt = r->buf<int>(L.st_tiles);
     a.partials = r->buf<float>(L.st_part);
     a.part_o = r->buf<float>(L.st_po);
     a.part_ml = r->buf<float>(L.st_pml);
     a.attn_cnt = r->buf<int>(L.st_acnt);
     a.keys = r->buf<unsigned long long>(L.st_keys);
     a.exit_cnt = r->buf<int>(L.st_exit);
-    a.max_tiles = L.st_max_tiles;
     a.plan = plan;
     a.pref_kb = 0;  // L2 prefetch past the rings: measured slower (the rings alone saturate HBM)
     if (const char* pv = getenv("AXB_STEP_PREF")) a.pref_kb = atoi(pv);

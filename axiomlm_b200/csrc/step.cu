@@ -81,18 +81,8 @@ __device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t (&a)[4
 }
 
 // ------------------------------------------------------------------ helpers
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-// Hand-offs between CTAs: the writers of a block of results meet at a warp /
-// CTA barrier, then one thread publishes with a release (or acq_rel) atomic;
-// the reader polls with an acquire load and meets its peers at a barrier
-// before they read.  No full fences.
-__device__ __forceinline__ void red_release_add(int* p, int v) {
-  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
+// The attention split count and the CTA exit count: one thread's acq_rel
+// atomic after its CTA's barrier (the CTA's writes before it are released).
 __device__ __forceinline__ int atom_acq_rel_add(int* p, int v) {
   int old;
   asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
@@ -185,27 +175,6 @@ __device__ __forceinline__ void act_wait2(const uint2* p, uint4& v, uint32_t fl,
     __nanosleep(32);
     v = ld_ll(q);
   }
-}
-
-// Bounded wait for *ctr >= target (a.spin_limit polls).  Gives up early when
-// another CTA has already raised the abort flag; on running out it raises the
-// flag and records AXB_ETIMEOUT in the error word.
-__device__ __noinline__ bool wait_ge(const int* ctr, int target, const StepArgs& a) {
-  const int* abort_flag = a.exit_cnt + 1;
-  for (uint32_t it = 0; it < a.spin_limit; ++it) {
-    if (ld_acquire(ctr) >= target) return true;
-    if ((it & 15) == 15 && *reinterpret_cast<const volatile int*>(abort_flag) != 0) return false;
-    __nanosleep(32);
-  }
-  raise_abort(a);
-  return false;
-}
-
-// CTA-wide wait: thread 0 polls, the barrier publishes the outcome.
-__device__ __forceinline__ bool cta_wait(const int* ctr, int target, const StepArgs& a, bool ok) {
-  int good = 0;
-  if (threadIdx.x == 0 && ok) good = wait_ge(ctr, target, a) ? 1 : 0;
-  return __syncthreads_or(good) != 0;
 }
 
 // ------------------------------------------------------------------ GEMV phases
@@ -1441,7 +1410,6 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
   for (int ph = 0; ph <= 4 * a.L; ++ph) {
     const int l = ph >> 2, kind = ph < 4 * a.L ? (ph & 3) : 4;
     const StepLayer* ly = a.layers + (kind == 4 ? 0 : l);
-    int* dn = a.done + 1 + 5 * l;  // QKV, attention, o, gate_up, down counters of layer l
     const int ts = 1 + 10 * l;
     // ---- the phase's input: its source, width and RMSNorm weight.  There is
     // no wait here: the staging (or the GEMV's own x loads) waits for the
@@ -1518,11 +1486,7 @@ __global__ void __launch_bounds__(kSThreads, 1) step_kernel(const StepArgs a) {
     a.amax[tid] = k ? (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
     a.keys[tid] = 0ull;
   }
-  for (int i = tid; i < 2 + 5 * a.L; i += blockDim.x) a.done[i] = 0;
   for (int i = tid; i < a.B * a.Hkv; i += blockDim.x) a.attn_cnt[i] = 0;  // grow through the step
-  if (*reinterpret_cast<volatile int*>(a.exit_cnt + 1) != 0) {  // an aborted step may leave arrivals behind
-    for (int i = tid; i < a.max_tiles; i += blockDim.x) a.tile_cnt[i] = 0;
-  }
   __syncthreads();
   if (tid == 0) {
     a.exit_cnt[2] += 1;  // the next launch's epoch (every CTA read this one at its start)
@@ -1656,7 +1620,7 @@ int step_launch(const StepArgs& a, cudaStream_t s) {
   AXB_CHECK_ARG(a.spin_limit > 0 && a.mbar_limit > 0, "step: wait limits must be positive");
   AXB_CHECK_ARG(a.L >= 0 && 4 * a.L + 1 < 511, "step: %d layers (the phase flags allow 127)", a.L);
   AXB_CHECK_ARG(a.lm_w && a.lm_s && a.ln_f && a.emb_w && a.emb_s && a.rope && a.tokens && a.params && a.err && a.h &&
-                    a.logits && a.amax && a.done && a.tile_cnt && a.partials && a.keys && a.exit_cnt &&
+                    a.logits && a.amax && a.partials && a.keys && a.exit_cnt &&
                     (a.L == 0 || (a.layers && a.qkv && a.attn && a.sw && a.part_o && a.part_ml && a.attn_cnt)),
                 "step: null pointer in the step arguments");
   AXB_CHECK_ARG((reinterpret_cast<uintptr_t>(a.lm_w) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.lm_s) & 15) == 0,

@@ -59,17 +59,15 @@ struct StepArgs {
   __half* logits;  // (B, V)
   int32_t* amax;   // (B,)
   // scratch (zeroed once; every counter returns to zero by the end of a step)
-  int* done;          // per-phase completion counters
-  int* tile_cnt;      // per-tile arrival counters
   float* partials;    // split-tile pieces: per CTA two slots (phase parity) of 32 lanes x 4 (value, flag) pairs
   float* part_o;      // attention split partials (B, Hq, kStepMaxSplits, hd)
   float* part_ml;     // (B, Hq, kStepMaxSplits, 2)
   int* attn_cnt;      // (B, Hkv) split arrivals, grow through a step
   unsigned long long* keys;  // per-token argmax keys
   int* exit_cnt;      // [0] CTAs done, [1] abort flag, [2] launch epoch
-  int max_tiles;      // size of tile_cnt
   StepPlan plan;
-  // bounded waits: polls of a cross-CTA counter and of a copy's mbarrier
+  // bounded waits: polls of a flagged word (activations, split-tile pieces)
+  // and of a copy's mbarrier
   // before the step gives up with AXB_ETIMEOUT (copies already issued are
   // still waited for, with a fixed limit, before a CTA exits)
   uint32_t spin_limit;
@@ -88,7 +86,7 @@ __host__ __device__ inline int step_trace_slots(int L) { return 4 + 10 * L + (4 
 
 constexpr int kStepMaxSplits = 64;
 constexpr int kStepMaxM = 8;
-constexpr uint32_t kStepSpinLimit = 1u << 22;  // default polls of a cross-CTA counter
+constexpr uint32_t kStepSpinLimit = 1u << 22;  // default polls of a flagged word
 constexpr uint32_t kStepMbarLimit = 1u << 22;  // default polls of a copy's mbarrier
 
 // host side
