@@ -1,10 +1,10 @@
 """A device-side wait that runs out.
 
-Every wait of the persistent step kernel is bounded (polls of a cross-CTA
-counter, of a copy's mbarrier, of a split-tile partial's flags).
+Every wait of the persistent step kernel is bounded (polls of a flagged
+activation word, of a split-tile piece's flags, of a copy's mbarrier).
 ``axb_runner_set_debug`` lowers those limits to a single poll, so waits give
 up long before what they wait for can arrive: the host-side stand-in for a
-counter that never arrives (nothing is made to fault or hang).  The step must
+word that never arrives (nothing is made to fault or hang).  The step must
 then wind down by itself, waiting for its own copies in flight, report
 AXB_ETIMEOUT in the error word, and leave the context usable: the same
 decoder runs clean steps once the limits are restored, and a fresh decoder
